@@ -1,0 +1,492 @@
+"""Benchmark of the gated delta-rule hot path on B200.
+
+Headline line (one JSON object on rank 0): recurrent decode tokens/s on the
+decode workload -- B=64, H=16, dk=dv=128, bf16 q/k/v, fp32 state ~N(0,0.02),
+one bench step = 512 consecutive single-token decode steps with the state
+updated in place (512 kernel launches, replayed as one CUDA graph).  The
+``prefill`` object in the same line reports chunked prefill tokens/s on B=4,
+T=4096, H=16, dk=dv=128, chunk=64, bf16 in / fp32 state (one launch per step).
+
+Multi-GPU (torchrun, one rank per GPU): batch x head work is independent, so
+every rank runs its own full workload (weak scaling, no collective on the
+data path); NCCL is used only for the barrier and the max-over-ranks time.
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(NumPy, all host cores) on a bounded sample of the same decode workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+DEC = dict(B=64, H=16, dk=128, dv=128, tokens=512)
+PRE = dict(B=4, T=4096, H=16, dk=128, dv=128, chunk=64)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end legs")
+    p.add_argument("--no-prefill", action="store_true", help="skip the prefill leg")
+    return p.parse_args()
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _profile_traffic(name):
+    """Per-launch DRAM bytes recorded from ncu in profiles/<name>.txt, or None."""
+    path = os.path.join(REPO, "profiles", name + ".txt")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*=\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.path = os.path.join("/tmp", f"gdn_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.close()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9 or (self.uuid and self.uuid not in parts[0]):
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for _, _, flags in rows for n, f in zip(names, flags)
+                          if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the oracle restatement; never the measured product)
+# ---------------------------------------------------------------------------
+
+def _cpu_decode_inputs(seed=0):
+    import numpy as np
+    from oracle import gdn_oracle as orc
+    B, H, dk, dv = DEC["B"], DEC["H"], DEC["dk"], DEC["dv"]
+    q, k, v, g, beta, h0 = orc.make_inputs(B, 8, H, dk, dv, seed=seed, h0_std=0.02)
+    cast = lambda x: np.ascontiguousarray(x, np.float32)  # noqa: E731
+    return [cast(x) for x in (q, k, v, g, beta)], cast(h0)
+
+
+def _cpu_decode_tokens(inputs, state, ntok, pool, nthreads):
+    """Decode `ntok` tokens of the B=64 batch with the float32 NumPy recurrence,
+    the batch split over `nthreads` host threads; returns the new state."""
+    import numpy as np
+    from oracle import gdn_oracle as orc
+    q, k, v, g, beta = inputs
+    B = q.shape[0]
+    parts = np.array_split(np.arange(B), nthreads)
+
+    def run(idx, s):
+        sl = slice(idx[0], idx[-1] + 1)
+        out = None
+        for t in range(ntok):
+            tt = t % q.shape[1]
+            ts = slice(tt, tt + 1)
+            out, s = orc.recurrent_ref(q[sl, ts], k[sl, ts], v[sl, ts], g[sl, ts], beta[sl, ts],
+                                       s, dtype=np.float32)
+        return s
+
+    futs = [pool.submit(run, idx, state[idx[0]:idx[-1] + 1]) for idx in parts]
+    return np.concatenate([f.result() for f in futs], 0)
+
+
+def cpu_decode_baseline(budget_s=10.0):
+    import concurrent.futures as cf
+    nthreads = os.cpu_count() or 1
+    inputs, state = _cpu_decode_inputs()
+    with cf.ThreadPoolExecutor(nthreads) as pool:
+        _cpu_decode_tokens(inputs, state, 1, pool, nthreads)  # warm-up
+        ntok, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or ntok < 2:
+            state = _cpu_decode_tokens(inputs, state, 1, pool, nthreads)
+            ntok += 1
+        el = time.perf_counter() - t0
+    return {"value": DEC["B"] * ntok / el, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+            "sample": f"{ntok} decode steps of the B=64 H=16 dk=dv=128 batch (float32 NumPy "
+                      f"restatement of the reference recurrence, batch split over {nthreads} "
+                      f"threads), {el:.1f} s"}
+
+
+def cpu_prefill_baseline(budget_s=10.0):
+    import numpy as np
+    from oracle import gdn_oracle as orc
+    T, H, dk, dv, C = PRE["T"], PRE["H"], PRE["dk"], PRE["dv"], PRE["chunk"]
+    q, k, v, g, beta, _ = orc.make_inputs(1, T, H, dk, dv, seed=0)
+    f32 = lambda x: np.ascontiguousarray(x, np.float32)  # noqa: E731
+    q, k, v, g, beta = (f32(x) for x in (q, k, v, g, beta))
+    ntok, t0, h = 0, time.perf_counter(), None
+    seg = 512
+    while time.perf_counter() - t0 < budget_s or ntok < seg:
+        s = slice(ntok % T, ntok % T + seg)
+        _, h = orc.chunk_exact(q[:, s], k[:, s], v[:, s], g[:, s], beta[:, s], h, C, np.float32)
+        ntok += seg
+    el = time.perf_counter() - t0
+    return {"value": ntok / el, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{ntok} tokens of B=1 sequences, H=16 dk=dv=128 chunk=64 (float32 "
+                      f"NumPy restatement of the chunked recurrence, BLAS threads), {el:.1f} s"}
+
+
+def run_reference_arm(a):
+    """--impl reference: the CPU restatement, rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import concurrent.futures as cf
+    nthreads = os.cpu_count() or 1
+    inputs, state = _cpu_decode_inputs()
+    ntok_step = 4
+    with cf.ThreadPoolExecutor(nthreads) as pool:
+        for _ in range(a.warmup):
+            state = _cpu_decode_tokens(inputs, state, ntok_step, pool, nthreads)
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            state = _cpu_decode_tokens(inputs, state, ntok_step, pool, nthreads)
+        el = time.perf_counter() - t0
+    value = DEC["B"] * ntok_step * a.steps / el
+    print(json.dumps({
+        "impl": "reference", "metric": "recurrent decode tokens/s", "value": value,
+        "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": el / a.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode B=64 H=16 dk=dv=128, fp32 state ~N(0,0.02); each step a "
+                               f"sample of {ntok_step} decode tokens of the batch",
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                         "sample": f"{ntok_step} decode tokens x B=64 per step, float32 NumPy "
+                                   "restatement of the reference recurrence (JAX is not "
+                                   "installable here, so the reference itself cannot run)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU legs
+# ---------------------------------------------------------------------------
+
+class Dist:
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.dist = dist
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=self.dev)
+
+    def barrier(self):
+        import torch
+        torch.cuda.synchronize(self.dev)
+        if self.world > 1:
+            self.dist.barrier()
+        torch.cuda.synchronize(self.dev)
+
+    def max(self, x):
+        import torch
+        if self.world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+def _timed(d, fn, steps, sampler=None):
+    """Time exactly `steps` calls of fn on the current stream; max over ranks (ms/step)."""
+    import torch
+    st = torch.cuda.current_stream(d.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d.barrier()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    e0.record(st)
+    for _ in range(steps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize(d.dev)
+    clocks = sampler.stop() if sampler else None
+    d.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    return d.max(ms), clocks
+
+
+def decode_leg(d, a, lib, uuid):
+    import torch
+    from gated_deltanet_jax_b200 import _lib, ops
+    from oracle import gdn_oracle as orc
+    B, H, dk, dv, TOK = DEC["B"], DEC["H"], DEC["dk"], DEC["dv"], DEC["tokens"]
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(1234 + d.rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(TOK, B, 1, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    k = nrm(torch.randn(TOK, B, 1, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(TOK, B, 1, H, dv, device=d.dev, generator=gen).bfloat16()
+    g = torch.nn.functional.logsigmoid(torch.randn(TOK, B, 1, H, device=d.dev, generator=gen))
+    beta = torch.sigmoid(torch.randn(TOK, B, 1, H, device=d.dev, generator=gen))
+    S = torch.randn(B, H, dk, dv, device=d.dev, generator=gen) * 0.02
+    o = torch.empty(TOK, B, 1, H, dv, device=d.dev, dtype=torch.bfloat16)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def one_step(stream):
+        for t in range(TOK):
+            rc = lib.gdn_recurrent_fwd(ptr(q[t]), ptr(k[t]), ptr(v[t]), ptr(g[t]), ptr(beta[t]),
+                                       ptr(S), ptr(o[t]), ptr(S), B, 1, H, dk, dv,
+                                       _lib.GDN_DTYPE_BF16, ctypes.c_void_p(stream))
+            if rc:
+                _lib.check(rc, "gdn_recurrent_fwd")
+
+    one_step(torch.cuda.current_stream(d.dev).cuda_stream)  # load modules before capture
+    torch.cuda.synchronize(d.dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        one_step(torch.cuda.current_stream(d.dev).cuda_stream)
+    for _ in range(a.warmup):
+        graph.replay()
+    sampler = ClockSampler(uuid) if d.rank == 0 else None
+    ms, clocks = _timed(d, graph.replay, a.steps, sampler)
+    del graph
+    value = d.world * B * TOK / (ms / 1e3)
+    bytes_launch = B * H * orc.bytes_recurrent_per_head_step(dk, dv, 2)
+    launch_s = ms / 1e3 / TOK
+    res = {"ms": ms, "value": value, "clocks": clocks, "launch_s": launch_s,
+           "bytes_launch": bytes_launch, "launches": a.steps * TOK}
+
+    if not a.no_e2e:
+        # Public API, host buffers: per token H2D of q/k/v/g/beta, op call, D2H of o.
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hg, hb = g.cpu().pin_memory(), beta.cpu().pin_memory()
+        ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+        dq, dk_, dv_ = torch.empty_like(q[0]), torch.empty_like(k[0]), torch.empty_like(v[0])
+        dg, db = torch.empty_like(g[0]), torch.empty_like(beta[0])
+
+        def e2e_step():
+            for t in range(TOK):
+                dq.copy_(hq[t], non_blocking=True)
+                dk_.copy_(hk[t], non_blocking=True)
+                dv_.copy_(hv[t], non_blocking=True)
+                dg.copy_(hg[t], non_blocking=True)
+                db.copy_(hb[t], non_blocking=True)
+                ot, _ = ops.fused_recurrent_gated_delta_rule(dq, dk_, dv_, dg, db,
+                                                             initial_state=S, final_state_out=S)
+                ho[t].copy_(ot, non_blocking=True)
+
+        for _ in range(min(a.warmup, 2)):
+            e2e_step()
+        e2e_steps = max(1, min(a.steps, 10))
+        ms_e2e, _ = _timed(d, e2e_step, e2e_steps)
+        h2d = TOK * (q[0].nbytes + k[0].nbytes + v[0].nbytes + g[0].nbytes + beta[0].nbytes)
+        res["e2e"] = {"value": d.world * B * TOK / (ms_e2e / 1e3), "unit": "tokens/s",
+                      "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(TOK * o[0].nbytes),
+                      "steps": e2e_steps,
+                      "path": "ops.fused_recurrent_gated_delta_rule per token, pinned host "
+                              "buffers, state resident on the device"}
+    return res
+
+
+def prefill_leg(d, a, lib):
+    import torch
+    from gated_deltanet_jax_b200 import _lib, ops
+    from oracle import gdn_oracle as orc
+    B, T, H, dk, dv, C = (PRE[x] for x in ("B", "T", "H", "dk", "dv", "chunk"))
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(99 + d.rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    k = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, device=d.dev, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, T, H, device=d.dev, generator=gen))
+    o = torch.empty(B, T, H, dv, device=d.dev, dtype=torch.bfloat16)
+    hT = torch.empty(B, H, dk, dv, device=d.dev, dtype=torch.float32)
+    ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, dk, dv, C, _lib.GDN_DTYPE_BF16, 0)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=d.dev)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        rc = lib.gdn_chunk_fwd(ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), None, ptr(o), ptr(hT),
+                               B, T, H, dk, dv, C, _lib.GDN_DTYPE_BF16, 0, ptr(ws), ws_bytes,
+                               ctypes.c_void_p(torch.cuda.current_stream(d.dev).cuda_stream))
+        if rc:
+            _lib.check(rc, "gdn_chunk_fwd")
+
+    for _ in range(a.warmup):
+        step()
+    ms, _ = _timed(d, step, a.steps)
+    flops = B * T * H * orc.flops_chunk_per_token_head(dk, dv, C)
+    res = {"ms": ms, "value": d.world * B * T / (ms / 1e3), "flops_launch": flops,
+           "launch_s": ms / 1e3, "launches": a.steps,
+           "bytes_launch": B * T * H * orc.bytes_chunk_per_token_head(dk, dv) + B * H * dk * dv * 4}
+    if not a.no_e2e:
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hg, hb = g.cpu().pin_memory(), beta.cpu().pin_memory()
+        ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+        hh = torch.empty(hT.shape, dtype=hT.dtype).pin_memory()
+
+        def e2e_step():
+            dq, dk_, dv_ = (t.to(d.dev, non_blocking=True) for t in (hq, hk, hv))
+            dg, db = hg.to(d.dev, non_blocking=True), hb.to(d.dev, non_blocking=True)
+            ot, ht = ops.chunk_gated_delta_rule(dq, dk_, dv_, dg, db, output_final_state=True)
+            ho.copy_(ot, non_blocking=True)
+            hh.copy_(ht, non_blocking=True)
+
+        for _ in range(min(a.warmup, 2)):
+            e2e_step()
+        e2e_steps = max(1, min(a.steps, 20))
+        ms_e2e, _ = _timed(d, e2e_step, e2e_steps)
+        res["e2e"] = {"value": d.world * B * T / (ms_e2e / 1e3), "unit": "tokens/s",
+                      "h2d_bytes_per_step": int(q.nbytes + k.nbytes + v.nbytes + g.nbytes
+                                                + beta.nbytes),
+                      "d2h_bytes_per_step": int(o.nbytes + hT.nbytes), "steps": e2e_steps,
+                      "path": "ops.chunk_gated_delta_rule, pinned host buffers"}
+    return res
+
+
+def main():
+    a = _args()
+    if a.impl == "reference":
+        run_reference_arm(a)
+        return
+    if a.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    import torch
+    from gated_deltanet_jax_b200 import _lib
+    lib = _lib.load()
+    d = Dist()
+    peaks, peak_src = _peaks()
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(d.dev).uuid)
+    except Exception:
+        pass
+
+    dec = decode_leg(d, a, lib, uuid)
+    pre = None if a.no_prefill else prefill_leg(d, a, lib)
+
+    cpu = None
+    if d.rank == 0 and d.world == 1 and not a.no_cpu:
+        cpu = cpu_decode_baseline()
+        cpu_pre = None if a.no_prefill else cpu_prefill_baseline()
+
+    if d.rank == 0:
+        hbm = float(peaks["hbm_gbs"])
+        ach = dec["bytes_launch"] / dec["launch_s"] / 1e9
+        traffic = _profile_traffic("recurrent_decode_b64_h16_d128")
+        line = {
+            "metric": "recurrent decode tokens/s", "value": dec["value"], "unit": "tokens/s",
+            "n_gpus": d.world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dec["ms"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "fused recurrent decode: B=64 H=16 dk=dv=128, bf16 q/k/v, "
+                                   "fp32 state ~N(0,0.02) updated in place; one step = 512 "
+                                   "consecutive decode tokens (512 launches, one CUDA graph)",
+                       "global_batch": DEC["B"] * d.world, "seq_len": DEC["tokens"],
+                       "parallelism": f"batch x head over {d.world} GPU(s), no collective",
+                       "l2": "inputs larger than L2 (512 MB fp32 state per GPU)"},
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": ach / hbm, "peak_source": f"{peak_src} hbm_gbs",
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": dec["bytes_launch"]},
+            "gpu_launches": dec["launches"] + (pre["launches"] if pre else 0),
+            "clocks": dec["clocks"],
+        }
+        if "e2e" in dec:
+            line["e2e"] = dec["e2e"]
+        if cpu:
+            line["cpu_baseline"] = cpu
+        if pre:
+            tf = pre["flops_launch"] / pre["launch_s"] / 1e12
+            bf16 = float(peaks["bf16_tflops"])
+            pre_line = {
+                "metric": "chunk prefill tokens/s", "value": pre["value"], "unit": "tokens/s",
+                "ms_per_step": pre["ms"],
+                "config": {"workload": "chunked prefill B=4 T=4096 H=16 dk=dv=128 chunk=64, "
+                                       "bf16 in, fp32 state, final state out",
+                           "l2": "inputs larger than L2 (201 MB q/k/v per GPU)"},
+                "roofline": {"bound": "tensor", "achieved": tf, "peak": bf16, "unit": "TFLOP/s",
+                             "frac": tf / bf16, "peak_source": f"{peak_src} bf16_tflops (burst)",
+                             "traffic": _profile_traffic("chunk_prefill_b4_t4096_h16_d128"),
+                             "algorithmic_flops_per_launch": pre["flops_launch"],
+                             "hbm_achieved_gbs": pre["bytes_launch"] / pre["launch_s"] / 1e9},
+            }
+            if "e2e" in pre:
+                pre_line["e2e"] = pre["e2e"]
+            if cpu and cpu_pre:
+                pre_line["cpu_baseline"] = cpu_pre
+            line["prefill"] = pre_line
+        print(json.dumps(line), flush=True)
+    d.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,23 @@
+"""B200 (sm_100a) gated delta-rule core with the reference package's op API.
+
+Public names follow reference ``src/gated_deltanet_jax/__init__.py`` for the
+parts on the op path: the config class and the two ops.
+"""
+
+from .configuration import GatedDeltaNetConfig
+from .dispatch import delta_rule
+from .ops import (
+    chunk_gated_delta_rule,
+    chunk_gated_delta_rule_fwd,
+    fused_recurrent_gated_delta_rule,
+    fused_recurrent_gated_delta_rule_fwd,
+)
+
+__all__ = [
+    "GatedDeltaNetConfig",
+    "chunk_gated_delta_rule",
+    "chunk_gated_delta_rule_fwd",
+    "fused_recurrent_gated_delta_rule",
+    "fused_recurrent_gated_delta_rule_fwd",
+    "delta_rule",
+]

@@ -1,0 +1,84 @@
+"""ctypes binding of ``libgdn_b200.so`` (the C ABI in ``include/gdn.h``).
+
+Loading fails loudly: there is no CPU fallback anywhere in this package.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libgdn_b200.so")
+
+GDN_OK = 0
+GDN_ERR_INVALID = 1
+GDN_ERR_UNSUPPORTED = 2
+GDN_ERR_CUDA = 3
+
+GDN_DTYPE_FP32 = 0
+GDN_DTYPE_BF16 = 1
+
+GDN_SEMANTICS_EXACT = 0
+GDN_SEMANTICS_REFERENCE = 1
+
+#: Every symbol ``include/gdn.h`` declares.
+EXPORTED_SYMBOLS = (
+    "gdn_recurrent_fwd",
+    "gdn_chunk_fwd",
+    "gdn_chunk_workspace_bytes",
+    "gdn_last_error",
+    "gdn_abi_version",
+)
+
+_lock = threading.Lock()
+_lib = None
+
+_vp, _i, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+
+
+class GDNError(RuntimeError):
+    """A non-OK status from the C ABI, with the library's message."""
+
+    def __init__(self, code: int, func: str, message: str):
+        self.code = code
+        kind = {GDN_ERR_INVALID: "invalid argument", GDN_ERR_UNSUPPORTED: "unsupported",
+                GDN_ERR_CUDA: "CUDA error"}.get(code, f"status {code}")
+        super().__init__(f"{func}: {kind}: {message}")
+
+
+def _declare(lib):
+    lib.gdn_recurrent_fwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                      _i, _i, _i, _i, _i, _i, _vp]
+    lib.gdn_recurrent_fwd.restype = _i
+    lib.gdn_chunk_fwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                  _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.gdn_chunk_fwd.restype = _i
+    lib.gdn_chunk_workspace_bytes.argtypes = [_i] * 8
+    lib.gdn_chunk_workspace_bytes.restype = _sz
+    lib.gdn_last_error.argtypes = []
+    lib.gdn_last_error.restype = ctypes.c_char_p
+    lib.gdn_abi_version.argtypes = []
+    lib.gdn_abi_version.restype = _i
+
+
+def load(path: str = LIB_PATH):
+    """Load (once) and return the library; raise if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(path):
+                raise RuntimeError(
+                    f"{path} is missing: build it with `python -m gated_deltanet_jax_b200._build` "
+                    "(there is no CPU fallback)")
+            lib = ctypes.CDLL(path)
+            _declare(lib)
+            _lib = lib
+        return _lib
+
+
+def check(rc: int, func: str) -> None:
+    if rc != GDN_OK:
+        msg = load().gdn_last_error().decode(errors="replace")
+        raise GDNError(rc, func, msg)

@@ -1,0 +1,117 @@
+// C ABI of libgdn_b200.so (declared in include/gdn.h): argument checks on the
+// host, then dispatch to the kernels.  No allocation, no CPU fallback.
+#include <cstdint>
+#include <cstdio>
+#include <cstdarg>
+
+#include "gdn.h"
+#include "gdn_internal.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool dk_supported(int dk) { return dk == 16 || dk == 32 || dk == 64 || dk == 128 || dk == 256; }
+
+int check_common(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                 const float* h0, const void* o, const float* hT, int B, int T, int H, int dk,
+                 int dv, int dtype) {
+  if (B < 0 || T < 0 || H < 0) return fail(GDN_ERR_INVALID, "negative size B=%d T=%d H=%d", B, T, H);
+  if (dtype != GDN_DTYPE_FP32 && dtype != GDN_DTYPE_BF16)
+    return fail(GDN_ERR_INVALID, "dtype %d is neither GDN_DTYPE_FP32 nor GDN_DTYPE_BF16", dtype);
+  if (!dk_supported(dk))
+    return fail(GDN_ERR_UNSUPPORTED, "dk=%d not supported (16, 32, 64, 128 or 256)", dk);
+  if (dv < 16 || dv > 512 || dv % 16)
+    return fail(GDN_ERR_UNSUPPORTED, "dv=%d not supported (multiple of 16 in [16, 512])", dv);
+  const long long elems = (long long)B * T * H;
+  if (elems * (dk > dv ? dk : dv) > (1LL << 40))
+    return fail(GDN_ERR_INVALID, "tensor too large (B*T*H*dim > 2^40)");
+  if (elems > 0) {
+    if (!q || !k || !v || !g || !beta || !o)
+      return fail(GDN_ERR_INVALID, "q, k, v, g, beta and o must be non-NULL");
+    const void* ptrs[6] = {q, k, v, g, beta, o};
+    const char* names[6] = {"q", "k", "v", "g", "beta", "o"};
+    for (int i = 0; i < 6; ++i)
+      if (!aligned16(ptrs[i])) return fail(GDN_ERR_INVALID, "%s is not 16-byte aligned", names[i]);
+  }
+  if (h0 && !aligned16(h0)) return fail(GDN_ERR_INVALID, "h0 is not 16-byte aligned");
+  if (hT && !aligned16(hT)) return fail(GDN_ERR_INVALID, "hT is not 16-byte aligned");
+  return GDN_OK;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return GDN_OK;
+  return fail(GDN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_recurrent_fwd(const void* q, const void* k, const void* v, const float* g,
+                      const float* beta, const float* h0, void* o, float* hT, int B, int T,
+                      int H, int dk, int dv, int dtype, void* stream) {
+  g_err[0] = '\0';
+  int rc = check_common(q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype);
+  if (rc) return rc;
+  if (T == 0 && (B * H) > 0 && h0 != hT && hT) {
+    // Nothing to run but the state must still be carried through.
+    cudaError_t e = h0 ? cudaMemcpyAsync(hT, h0, sizeof(float) * (size_t)B * H * dk * dv,
+                                         cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
+                       : cudaMemsetAsync(hT, 0, sizeof(float) * (size_t)B * H * dk * dv,
+                                         (cudaStream_t)stream);
+    return cuda_status(e, "gdn_recurrent_fwd (T=0 state copy)");
+  }
+  gdn::RecurrentArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype};
+  return cuda_status(gdn::launch_recurrent(a, (cudaStream_t)stream), "gdn_recurrent_fwd");
+}
+
+size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int dtype,
+                                 int semantics) {
+  (void)B; (void)T; (void)H; (void)dk; (void)dv; (void)chunk; (void)dtype; (void)semantics;
+  return 0;
+}
+
+int gdn_chunk_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                  const float* h0, void* o, float* hT, int B, int T, int H, int dk, int dv,
+                  int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
+                  void* stream) {
+  g_err[0] = '\0';
+  int rc = check_common(q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype);
+  if (rc) return rc;
+  if (chunk != 16 && chunk != 32 && chunk != 64)
+    return fail(GDN_ERR_UNSUPPORTED, "chunk=%d not supported (16, 32 or 64)", chunk);
+  if (semantics != GDN_SEMANTICS_EXACT && semantics != GDN_SEMANTICS_REFERENCE)
+    return fail(GDN_ERR_INVALID, "semantics %d unknown", semantics);
+  const size_t need = gdn_chunk_workspace_bytes(B, T, H, dk, dv, chunk, dtype, semantics);
+  if (ws_bytes < need || (need && !workspace))
+    return fail(GDN_ERR_INVALID, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  if (T == 0 && (B * H) > 0 && hT && h0 != hT) {
+    cudaError_t e = h0 ? cudaMemcpyAsync(hT, h0, sizeof(float) * (size_t)B * H * dk * dv,
+                                         cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
+                       : cudaMemsetAsync(hT, 0, sizeof(float) * (size_t)B * H * dk * dv,
+                                         (cudaStream_t)stream);
+    return cuda_status(e, "gdn_chunk_fwd (T=0 state copy)");
+  }
+  gdn::ChunkArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, chunk, dtype, semantics,
+                   workspace, ws_bytes};
+  if (gdn::chunk_simt_smem_bytes(a) == 0)
+    return fail(GDN_ERR_UNSUPPORTED, "no chunk kernel fits dk=%d dv=%d chunk=%d", dk, dv, chunk);
+  return cuda_status(gdn::launch_chunk_simt(a, (cudaStream_t)stream), "gdn_chunk_fwd");
+}
+
+const char* gdn_last_error(void) { return g_err; }
+
+int gdn_abi_version(void) { return (1 << 16) | 0; }
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// Internal launch interface shared by the kernels and the C ABI (gdn_capi.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace gdn {
+
+enum DType : int { kFP32 = 0, kBF16 = 1 };
+enum Semantics : int { kExact = 0, kReference = 1 };
+
+struct RecurrentArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* beta;
+  const float* h0;
+  void* o;
+  float* hT;
+  int B, T, H, dk, dv, dtype;
+};
+
+struct ChunkArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* beta;
+  const float* h0;
+  void* o;
+  float* hT;
+  int B, T, H, dk, dv, chunk, dtype, semantics;
+  void* workspace;
+  size_t ws_bytes;
+};
+
+cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);
+
+// Portable CUDA-core chunk kernel (any supported shape, fp32 or bf16 inputs).
+cudaError_t launch_chunk_simt(const ChunkArgs& a, cudaStream_t st);
+// Shared-memory bytes launch_chunk_simt needs for this shape (0 = unsupported).
+size_t chunk_simt_smem_bytes(const ChunkArgs& a);
+
+}  // namespace gdn

@@ -1,0 +1,151 @@
+"""Gated delta-rule ops with the reference package's names and signatures.
+
+Mirrors ``gated_deltanet_jax.ops`` (reference ``src/gated_deltanet_jax/ops.py``):
+
+* :func:`chunk_gated_delta_rule_fwd` / :func:`chunk_gated_delta_rule`
+  -- ops.py:299 and its alias at ops.py:352;
+* :func:`fused_recurrent_gated_delta_rule` / :func:`fused_recurrent_gated_delta_rule_fwd`
+  -- the Pallas wrapper ops.py:187 and its aliases at ops.py:350-351.
+
+Arrays are CUDA ``torch.Tensor`` s in the reference layout (q, k ``[B,T,H,dk]``,
+v ``[B,T,H,dv]``, g, beta ``[B,T,H]``, states ``[B,H,dk,dv]``).  Every call
+goes through the C ABI of ``libgdn_b200.so`` on the tensor's current CUDA
+stream; there is no CPU path.  Both ops compute the delta-rule recurrence
+(the reference's recurrent kernel, ops.py:170-184) with an fp32 state and
+return ``o`` in v's dtype.
+
+Differences from the reference, all additive:
+
+* ``fused_recurrent_gated_delta_rule`` also accepts ``initial_state`` and
+  ``output_final_state`` (the reference always starts from zeros and returns
+  ``(o, None)``, ops.py:168/219); without them it behaves the same.
+* ``final_state_out=`` writes the final state into a given fp32 tensor, which
+  may be ``initial_state`` itself (in-place decode).
+* ``semantics="reference"`` on the chunk op reproduces ops.py:238-346 as
+  written, including its deviations from the recurrence.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.GDN_DTYPE_FP32, torch.bfloat16: _lib.GDN_DTYPE_BF16}
+_SEMANTICS = {"exact": _lib.GDN_SEMANTICS_EXACT, "reference": _lib.GDN_SEMANTICS_REFERENCE}
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_state):
+    for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path)")
+    if q.dim() != 4 or k.shape != q.shape:
+        raise ValueError(f"q and k must both be [B,T,H,dk]; got {tuple(q.shape)}, {tuple(k.shape)}")
+    B, T, H, dk = q.shape
+    if v.dim() != 4 or tuple(v.shape[:3]) != (B, T, H):
+        raise ValueError(f"v must be [B,T,H,dv] with B,T,H={B},{T},{H}; got {tuple(v.shape)}")
+    dv = v.shape[3]
+    for name, t in (("g", g), ("beta", beta)):
+        if tuple(t.shape) != (B, T, H):
+            raise ValueError(f"{name} must be [B,T,H]=({B},{T},{H}); got {tuple(t.shape)}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError(f"q, k, v must share one dtype; got {q.dtype}, {k.dtype}, {v.dtype}")
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"dtype {q.dtype} not supported (bfloat16 or float32)")
+    dev = q.device
+    for name, t in (("k", k), ("v", v), ("g", g), ("beta", beta)):
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, q on {dev}")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    g = g.to(torch.float32).contiguous()
+    beta = beta.to(torch.float32).contiguous()
+    h0 = None
+    if initial_state is not None:
+        if tuple(initial_state.shape) != (B, H, dk, dv):
+            raise ValueError(f"initial_state must be [B,H,dk,dv]=({B},{H},{dk},{dv}); "
+                             f"got {tuple(initial_state.shape)}")
+        if initial_state.device != dev:
+            raise ValueError(f"initial_state is on {initial_state.device}, q on {dev}")
+        h0 = initial_state
+        if h0.dtype != torch.float32 or not h0.is_contiguous():
+            h0 = h0.to(torch.float32).contiguous()
+    hT = None
+    if final_state_out is not None:
+        if (tuple(final_state_out.shape) != (B, H, dk, dv) or final_state_out.dtype != torch.float32
+                or not final_state_out.is_contiguous() or final_state_out.device != dev):
+            raise ValueError("final_state_out must be a contiguous float32 [B,H,dk,dv] tensor "
+                             "on the inputs' device")
+        hT = final_state_out
+    elif output_final_state:
+        hT = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
+    o = torch.empty((B, T, H, dv), dtype=v.dtype, device=dev)
+    return q, k, v, g, beta, h0, hT, o, (B, T, H, dk, dv)
+
+
+def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_final_state=False,
+                               chunk_size=64, *, semantics: str = "exact",
+                               final_state_out: Optional[torch.Tensor] = None
+                               ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Chunked gated delta rule (reference ``chunk_gated_delta_rule_fwd``, ops.py:299).
+
+    Returns ``(o, final_state)`` when ``output_final_state`` (or
+    ``final_state_out``) is given, else ``(o, None)`` (ops.py:344-346).
+    ``chunk_size`` is 16, 32 or 64.  ``semantics="exact"`` (default) equals the
+    recurrence; ``"reference"`` reproduces the reference chunk code as written.
+    """
+    if semantics not in _SEMANTICS:
+        raise ValueError(f"semantics must be one of {sorted(_SEMANTICS)}; got {semantics!r}")
+    q, k, v, g, beta, h0, hT, o, (B, T, H, dk, dv) = _prepare(
+        q, k, v, g, beta, initial_state, final_state_out, output_final_state)
+    lib = _lib.load()
+    dtype = _DTYPES[q.dtype]
+    sem = _SEMANTICS[semantics]
+    with torch.cuda.device(q.device):
+        ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, dk, dv, int(chunk_size), dtype, sem)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = lib.gdn_chunk_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0), _ptr(o),
+                               _ptr(hT), B, T, H, dk, dv, int(chunk_size), dtype, sem, _ptr(ws),
+                               ws_bytes, stream)
+    _lib.check(rc, "gdn_chunk_fwd")
+    return o, hT
+
+
+def fused_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None,
+                                     output_final_state=False, *,
+                                     final_state_out: Optional[torch.Tensor] = None
+                                     ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Fused recurrent gated delta rule (reference Pallas wrapper, ops.py:187-219).
+
+    With neither ``initial_state`` nor ``output_final_state`` this is the
+    reference call: zero initial state, returns ``(o, None)``.  For decode pass
+    ``initial_state=S, final_state_out=S`` to update the state in place.
+    """
+    q, k, v, g, beta, h0, hT, o, (B, T, H, dk, dv) = _prepare(
+        q, k, v, g, beta, initial_state, final_state_out, output_final_state)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = lib.gdn_recurrent_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
+                                   _ptr(o), _ptr(hT), B, T, H, dk, dv, _DTYPES[q.dtype], stream)
+    _lib.check(rc, "gdn_recurrent_fwd")
+    return o, hT
+
+
+# Aliases with the reference's public names (ops.py:350-352).
+fused_recurrent_gated_delta_rule_fwd = fused_recurrent_gated_delta_rule
+fused_recurrent_gated_delta_rule_pallas = fused_recurrent_gated_delta_rule
+chunk_gated_delta_rule = chunk_gated_delta_rule_fwd
+
+__all__ = [
+    "chunk_gated_delta_rule", "chunk_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule",
+    "fused_recurrent_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule_pallas",
+]

@@ -1,0 +1,94 @@
+/*
+ * gdn.h -- C ABI of the B200 (sm_100a) gated delta-rule library (libgdn_b200.so).
+ *
+ * Plain pointers, sizes and an opaque CUDA stream; no framework types.  Every
+ * pointer argument is a DEVICE pointer unless stated otherwise.  Tensors are
+ * dense row-major in the reference package's layout:
+ *
+ *   q, k   [B, T, H, dk]     dtype = `dtype` (GDN_DTYPE_BF16 or GDN_DTYPE_FP32)
+ *   v, o   [B, T, H, dv]     dtype = `dtype`
+ *   g,beta [B, T, H]         float32 (g = log-decay, <= 0 in practice)
+ *   h0,hT  [B, H, dk, dv]    float32 (recurrent state; may be NULL; may alias)
+ *
+ * Supported head dims: dk in {16, 32, 64, 128, 256}; dv a multiple of 16 in
+ * [16, 512].  Every pointer must be 16-byte aligned.  Calls are asynchronous
+ * on `stream` (a cudaStream_t; NULL = legacy default stream), allocate no
+ * memory, and are reentrant: the only global state is a one-time per-device
+ * kernel attribute set-up and the thread-local error message.
+ *
+ * Return value: GDN_OK or one of the GDN_ERR_* codes; gdn_last_error() then
+ * returns a message for the calling thread.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_OK 0
+#define GDN_ERR_INVALID 1     /* bad shape, pointer, alignment or flag */
+#define GDN_ERR_UNSUPPORTED 2 /* valid request outside the built kernels */
+#define GDN_ERR_CUDA 3        /* CUDA launch or runtime error */
+
+#define GDN_DTYPE_FP32 0
+#define GDN_DTYPE_BF16 1
+
+/* Chunk-path semantics. */
+#define GDN_SEMANTICS_EXACT 0     /* the delta-rule recurrence (default) */
+#define GDN_SEMANTICS_REFERENCE 1 /* the reference chunk code as written */
+
+/*
+ * Fused recurrent gated delta rule over T tokens (T = 1 is one decode step).
+ *
+ * Replaces the Pallas call of the reference, ops.py:187-219
+ * (fused_recurrent_gated_delta_rule_pallas -> fused_recurrent_kernel_simple,
+ * ops.py:162-184).  Per (b, h) and token t, with an fp32 state S [dk, dv]:
+ *     S <- e^{g_t} S;  u = beta_t (v_t - k_t^T S);  S <- S + k_t u^T;
+ *     o_t = S^T q_t
+ * h0 == NULL starts from zeros (the reference's only mode, ops.py:168);
+ * hT == NULL drops the final state (the reference returns None, ops.py:219).
+ * h0 == hT updates the state in place (decode).
+ */
+int gdn_recurrent_fwd(const void* q, const void* k, const void* v,
+                      const float* g, const float* beta,
+                      const float* h0, void* o, float* hT,
+                      int B, int T, int H, int dk, int dv, int dtype,
+                      void* stream);
+
+/*
+ * Chunked gated delta-rule forward.
+ *
+ * Replaces chunk_gated_delta_rule_fwd, ops.py:299-346 (with its helpers
+ * chunk_local_cumsum :238, chunk_scaled_dot_kkt :249, solve_inv_I_minus_A
+ * :271, recompute_w_u :276 and the lax.scan body :322-340).  With
+ * GDN_SEMANTICS_EXACT the result equals gdn_recurrent_fwd on the same inputs
+ * (to rounding).  `chunk` is the chunk length C (16, 32 or 64).  h0 == NULL
+ * starts from zeros (ops.py:318-319); hT == NULL skips the final state
+ * (output_final_state=False, ops.py:344-346).  `workspace` / `ws_bytes` may be
+ * NULL / 0 when gdn_chunk_workspace_bytes() returns 0.
+ */
+int gdn_chunk_fwd(const void* q, const void* k, const void* v,
+                  const float* g, const float* beta,
+                  const float* h0, void* o, float* hT,
+                  int B, int T, int H, int dk, int dv, int chunk,
+                  int dtype, int semantics,
+                  void* workspace, size_t ws_bytes, void* stream);
+
+/* Device scratch bytes gdn_chunk_fwd needs for these sizes (0 = none). */
+size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
+                                 int dtype, int semantics);
+
+/* Message for the last non-OK return on the calling thread ("" if none). */
+const char* gdn_last_error(void);
+
+/* ABI version of this header: (major << 16) | minor. */
+int gdn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

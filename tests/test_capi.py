@@ -1,0 +1,156 @@
+"""CPU tests of the C ABI boundary and the host-side argument checks.
+
+No GPU is needed: the library must load, export every symbol include/gdn.h
+declares, and reject bad arguments on the host before any CUDA call.
+"""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+
+from gated_deltanet_jax_b200 import _lib, ops
+from gated_deltanet_jax_b200 import _build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "gdn.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gdn_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(_lib.LIB_PATH):
+        _build.build()
+    return _lib.load()
+
+
+def test_header_and_binding_agree():
+    assert _declared_functions() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH],
+                         capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\sT\s(gdn_\w+)", out))
+    assert set(_declared_functions()) <= exported
+
+
+def test_library_targets_sm100a():
+    out = subprocess.run(["cuobjdump", "--list-elf", _lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    assert "sm_100a" in out
+
+
+def test_abi_version(lib):
+    assert lib.gdn_abi_version() >> 16 == 1
+
+
+def _call_recurrent(lib, ptr=16, B=1, T=1, H=1, dk=16, dv=16, dtype=_lib.GDN_DTYPE_BF16):
+    p = ctypes.c_void_p(ptr)
+    return lib.gdn_recurrent_fwd(p, p, p, p, p, None, p, None, B, T, H, dk, dv, dtype, None)
+
+
+def _call_chunk(lib, ptr=16, B=1, T=1, H=1, dk=16, dv=16, chunk=64, dtype=_lib.GDN_DTYPE_BF16,
+                semantics=_lib.GDN_SEMANTICS_EXACT):
+    p = ctypes.c_void_p(ptr)
+    return lib.gdn_chunk_fwd(p, p, p, p, p, None, p, None, B, T, H, dk, dv, chunk, dtype,
+                             semantics, None, 0, None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(dk=48), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(dk=512), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(dv=8), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(dv=24), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(dv=1024), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(dtype=7), _lib.GDN_ERR_INVALID),
+    (dict(B=-1), _lib.GDN_ERR_INVALID),
+    (dict(ptr=0), _lib.GDN_ERR_INVALID),
+    (dict(ptr=18), _lib.GDN_ERR_INVALID),
+])
+def test_recurrent_rejects_bad_arguments(lib, kw, code):
+    assert _call_recurrent(lib, **kw) == code
+    assert lib.gdn_last_error()
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(chunk=48), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(chunk=128), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(semantics=5), _lib.GDN_ERR_INVALID),
+    (dict(dk=100), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(ptr=8), _lib.GDN_ERR_INVALID),
+])
+def test_chunk_rejects_bad_arguments(lib, kw, code):
+    assert _call_chunk(lib, **kw) == code
+    msg = lib.gdn_last_error().decode()
+    assert msg
+
+
+def test_empty_problem_is_a_no_op(lib):
+    # B*H == 0: nothing to launch, no CUDA call, OK.
+    assert _call_recurrent(lib, B=0) == _lib.GDN_OK
+    assert _call_chunk(lib, H=0) == _lib.GDN_OK
+
+
+def test_workspace_query(lib):
+    assert lib.gdn_chunk_workspace_bytes(4, 4096, 16, 128, 128, 64, 1, 0) >= 0
+
+
+def test_error_raises_with_message(lib):
+    rc = _call_chunk(lib, chunk=48)
+    with pytest.raises(_lib.GDNError, match="chunk=48"):
+        _lib.check(rc, "gdn_chunk_fwd")
+
+
+def _cpu_inputs(B=1, T=4, H=2, dk=16, dv=16, dtype=torch.float32):
+    q = torch.zeros(B, T, H, dk, dtype=dtype)
+    return q, q.clone(), torch.zeros(B, T, H, dv, dtype=dtype), torch.zeros(B, T, H), \
+        torch.zeros(B, T, H)
+
+
+def test_ops_reject_cpu_tensors():
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.chunk_gated_delta_rule(*_cpu_inputs())
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.fused_recurrent_gated_delta_rule(*_cpu_inputs())
+
+
+def test_ops_reject_bad_semantics():
+    with pytest.raises(ValueError, match="semantics"):
+        ops.chunk_gated_delta_rule(*_cpu_inputs(), semantics="fast")
+
+
+def test_reference_names_exported():
+    import gated_deltanet_jax_b200 as pkg
+    for name in ("chunk_gated_delta_rule", "fused_recurrent_gated_delta_rule",
+                 "chunk_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule_fwd",
+                 "GatedDeltaNetConfig"):
+        assert hasattr(pkg, name)
+    assert ops.chunk_gated_delta_rule is ops.chunk_gated_delta_rule_fwd
+    assert ops.fused_recurrent_gated_delta_rule_fwd is ops.fused_recurrent_gated_delta_rule
+
+
+def test_mode_switch_rejects_unknown_mode():
+    from gated_deltanet_jax_b200 import GatedDeltaNetConfig, delta_rule
+    cfg = GatedDeltaNetConfig(attn_mode="parallel")
+    with pytest.raises(ValueError, match="Unknown mode parallel"):
+        delta_rule(cfg, *_cpu_inputs())
+
+
+def test_config_defaults_match_reference():
+    from gated_deltanet_jax_b200 import GatedDeltaNetConfig
+    c = GatedDeltaNetConfig()
+    assert (c.attn_mode, c.hidden_size, c.head_dim, c.num_heads, c.expand_v, c.conv_size,
+            c.num_hidden_layers, c.norm_eps, c.vocab_size) == \
+        ("chunk", 2048, 256, 6, 2.0, 4, 21, 1e-6, 32000)
+    assert c.num_v_heads is None and c.use_gate and c.use_short_conv

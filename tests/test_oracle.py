@@ -1,0 +1,127 @@
+"""CPU tests of the oracle: pinned to the reference's own outputs (golden.npz),
+and self-consistent across its chunked, recurrent and two-pass forms."""
+
+import numpy as np
+import pytest
+
+from oracle import gdn_oracle as orc
+
+
+def _f64(case, key):
+    return case[key].astype(np.float64)
+
+
+def test_golden_cases_present(golden):
+    assert set(golden) >= {"c0", "h0", "tail", "layer", "lm", "h1"}
+    B, T, H, dk, dv, C = golden["c0"]["shape"]
+    assert (B, T, H, dk, dv, C) == (1, 256, 2, 64, 64, 64)
+
+
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+def test_recurrent_matches_reference_kernel(golden, name):
+    """recurrent_ref == the reference Pallas kernel (ops.py:162-184), zero state."""
+    c = golden[name]
+    o, _ = orc.recurrent_ref(*(_f64(c, x) for x in ("q", "k", "v", "g", "beta")))
+    assert orc.rel_err(o, c["o_recurrent"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+def test_literal_chunk_matches_reference_chunk(golden, name):
+    """chunk_reference_literal == the reference chunk path (ops.py:299-346)."""
+    c = golden[name]
+    C = int(c["shape"][5])
+    h0 = _f64(c, "h0") if "h0" in c else None
+    o, h = orc.chunk_reference_literal(*(_f64(c, x) for x in ("q", "k", "v", "g", "beta")),
+                                       initial_state=h0, output_final_state=True, chunk_size=C)
+    assert orc.rel_err(o, c["o_chunk"]) < 1e-6
+    assert orc.rel_err(h, c["h_chunk"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+def test_exact_chunk_matches_reference_recurrence(golden, name):
+    """The exact chunked form reproduces the reference recurrent kernel."""
+    c = golden[name]
+    C = int(c["shape"][5])
+    o, _ = orc.chunk_exact(*(_f64(c, x) for x in ("q", "k", "v", "g", "beta")), chunk_size=C)
+    assert orc.rel_err(o, c["o_recurrent"]) < 1e-6
+
+
+def test_reference_chunk_deviates_from_recurrence(golden):
+    """Documented deviation: the reference chunk path is not the recurrence."""
+    c = golden["c0"]
+    assert orc.rel_err(c["o_chunk"], c["o_recurrent"]) > 0.5
+
+
+def test_literal_output_permutation(golden):
+    """The reference output reshape (ops.py:342) is a pure (token, head)
+    permutation of per-position outputs: undoing it on a deviation-free
+    input (H=1 identity, else a permuted comparison) is consistent."""
+    for name in ("c0", "layer", "tail"):
+        c = golden[name]
+        B, T, H, dk, dv, C = (int(x) for x in c["shape"])
+        src_t, src_h = orc.literal_output_permutation(T, H, C)
+        # a bijection onto the valid and padded (token, head) positions
+        pairs = set(zip(src_t.ravel().tolist(), src_h.ravel().tolist()))
+        assert len(pairs) == T * H
+        if H == 1:
+            assert np.array_equal(src_t[:, 0], np.arange(T))
+
+
+@pytest.mark.parametrize("shape", [(2, 130, 3, 16, 32, 32), (1, 64, 2, 32, 16, 16),
+                                   (1, 200, 2, 64, 64, 64), (1, 1, 1, 16, 16, 64)])
+def test_chunk_exact_equals_recurrent(shape):
+    B, T, H, dk, dv, C = shape
+    q, k, v, g, beta, h0 = orc.make_inputs(B, T, H, dk, dv, seed=7, h0_std=0.02)
+    o1, h1 = orc.recurrent_ref(q, k, v, g, beta, h0)
+    o2, h2 = orc.chunk_exact(q, k, v, g, beta, h0, C)
+    assert orc.max_abs_err(o1, o2) < 1e-12
+    assert orc.max_abs_err(h1, h2) < 1e-12
+
+
+@pytest.mark.parametrize("parts", [1, 2, 3, 5])
+def test_two_pass_split_equals_recurrent(parts):
+    q, k, v, g, beta, h0 = orc.make_inputs(1, 300, 2, 16, 32, seed=11, h0_std=0.02)
+    o1, h1 = orc.recurrent_ref(q, k, v, g, beta, h0)
+    o2, h2 = orc.two_pass_sp(q, k, v, g, beta, h0, parts=parts, chunk_size=32)
+    assert orc.max_abs_err(o1, o2) < 1e-12
+    assert orc.max_abs_err(h1, h2) < 1e-12
+
+
+def test_segment_transition_is_affine_map():
+    q, k, v, g, beta, h0 = orc.make_inputs(2, 40, 2, 16, 24, seed=3, h0_std=0.1)
+    _, S = orc.recurrent_ref(q, k, v, g, beta, None)
+    M = orc.segment_transition(k, g, beta)
+    _, hT = orc.recurrent_ref(q, k, v, g, beta, h0)
+    assert orc.max_abs_err(hT, M @ h0 + S) < 1e-12
+
+
+def test_split_resume_equals_one_shot():
+    q, k, v, g, beta, h0 = orc.make_inputs(1, 150, 2, 32, 32, seed=5, h0_std=0.02)
+    o, h = orc.chunk_exact(q, k, v, g, beta, h0, 64)
+    oa, ha = orc.chunk_exact(q[:, :77], k[:, :77], v[:, :77], g[:, :77], beta[:, :77], h0, 64)
+    ob, hb = orc.chunk_exact(q[:, 77:], k[:, 77:], v[:, 77:], g[:, 77:], beta[:, 77:], ha, 64)
+    assert orc.max_abs_err(np.concatenate([oa, ob], 1), o) < 1e-12
+    assert orc.max_abs_err(hb, h) < 1e-12
+
+
+def test_round_bf16():
+    x = np.array([1.0, 1.00390625, 1.01171875, -3.3e-3, 0.0, 65504.0])
+    r = orc.round_bf16(x)
+    assert r[0] == 1.0 and r[1] == 1.0  # tie to even
+    assert r[2] == 1.015625              # tie rounds up to even mantissa
+    assert abs(r[3] - x[3]) / abs(x[3]) < 2 ** -8
+    assert r[4] == 0.0
+
+
+def test_tolerance_rules():
+    ref = np.array([1.0, -2.0, 3.0])
+    assert orc.within_tolerance(ref + 1e-3, ref, "fp32")[0]
+    assert not orc.within_tolerance(ref + 3e-3, ref, "fp32")[0]
+    assert orc.within_tolerance(ref + 0.05, ref, "bf16")[0]     # 0.05 / 3 < 2e-2
+    assert not orc.within_tolerance(ref + 0.07, ref, "bf16")[0]
+
+
+def test_work_accounting():
+    assert orc.flops_chunk_per_token_head(128, 128, 64) == 180224
+    assert orc.bytes_chunk_per_token_head(128, 128) == 1032
+    assert orc.bytes_recurrent_per_head_step(128, 128) == 132104

@@ -1,0 +1,109 @@
+"""GPU parity of the fused recurrent kernel (gdn_recurrent_fwd) against the
+oracle, the reference's own outputs (golden.npz) and a PyTorch fp32 step."""
+
+import numpy as np
+import pytest
+import torch
+
+from gated_deltanet_jax_b200 import ops
+from oracle import gdn_oracle as orc
+from helpers import (assert_close, device_inputs, device_inputs_fast, f64, to_dev,
+                     torch_recurrent_step_fp32)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+def test_matches_reference_kernel_outputs(golden, cuda, name):
+    """Zero initial state, no final state: the reference call form (ops.py:187)."""
+    c = golden[name]
+    args = [to_dev(c[x], torch.float32, cuda) for x in ("q", "k", "v", "g", "beta")]
+    o, hT = ops.fused_recurrent_gated_delta_rule(*args)
+    assert hT is None
+    assert o.dtype == torch.float32
+    assert_close(f64(o), c["o_recurrent"], "fp32", name)
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("dk,dv", [(16, 16), (16, 32), (32, 64), (64, 64), (64, 48),
+                                   (128, 128), (128, 256), (256, 512), (256, 16)])
+@pytest.mark.parametrize("T", [1, 5, 40])
+def test_against_oracle(cuda, dtype, dk, dv, T):
+    (q, k, v, g, b, h0), host = device_inputs(2, T, 3, dk, dv, seed=dk + dv + T, dtype=dtype,
+                                              dev=cuda, h0_std=0.02)
+    o, hT = ops.fused_recurrent_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                                 output_final_state=True)
+    ro, rh = orc.recurrent_ref(*host)
+    assert o.dtype == q.dtype
+    assert_close(f64(o), ro, dtype, "o")
+    assert_close(f64(hT), rh, dtype, "state")
+
+
+def test_in_place_state(cuda):
+    (q, k, v, g, b, h0), host = device_inputs(3, 4, 2, 64, 64, seed=1, dtype="bf16",
+                                              dev=cuda, h0_std=0.05)
+    S = h0.clone()
+    o, hT = ops.fused_recurrent_gated_delta_rule(q, k, v, g, b, initial_state=S,
+                                                 final_state_out=S)
+    assert hT.data_ptr() == S.data_ptr()
+    ro, rh = orc.recurrent_ref(*host)
+    assert_close(f64(o), ro, "bf16", "o")
+    assert_close(f64(S), rh, "bf16", "state")
+
+
+def test_multi_token_call_equals_single_steps(cuda):
+    (q, k, v, g, b, h0), _ = device_inputs(2, 9, 4, 128, 128, seed=2, dtype="bf16",
+                                           dev=cuda, h0_std=0.02)
+    o_all, h_all = ops.fused_recurrent_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                                        output_final_state=True)
+    S = h0.clone()
+    outs = []
+    for t in range(9):
+        sl = slice(t, t + 1)
+        o_t, _ = ops.fused_recurrent_gated_delta_rule(q[:, sl], k[:, sl], v[:, sl], g[:, sl],
+                                                      b[:, sl], initial_state=S,
+                                                      final_state_out=S)
+        outs.append(o_t)
+    torch.testing.assert_close(torch.cat(outs, 1).float(), o_all.float(), rtol=0, atol=1e-2)
+    torch.testing.assert_close(S, h_all, rtol=1e-5, atol=1e-6)
+
+
+def test_empty_sequence_carries_state(cuda):
+    (q, k, v, g, b, h0), _ = device_inputs(1, 0, 2, 32, 32, seed=0, dtype="fp32", dev=cuda,
+                                           h0_std=0.1)
+    o, hT = ops.fused_recurrent_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                                 output_final_state=True)
+    assert o.shape == (1, 0, 2, 32)
+    torch.testing.assert_close(hT, h0)
+
+
+def test_decode_config_full_size(cuda):
+    """B=64, H=16, dk=dv=128, bf16 q/k/v, fp32 state ~N(0,0.02), 8 in-place steps.
+
+    Every head against a PyTorch fp32 step; sampled heads against the float64
+    oracle over all 8 steps."""
+    B, H, dk, dv, steps = 64, 16, 128, 128, 8
+    q, k, v, g, b, S = device_inputs_fast(B, steps, H, dk, dv, seed=1, dtype="bf16",
+                                          dev=cuda, h0_std=0.02)
+    S0 = S.clone()
+    S_ref = S.clone()
+    outs = []
+    for t in range(steps):
+        sl = slice(t, t + 1)
+        o, _ = ops.fused_recurrent_gated_delta_rule(q[:, sl], k[:, sl], v[:, sl], g[:, sl],
+                                                    b[:, sl], initial_state=S, final_state_out=S)
+        o_ref, S_ref = torch_recurrent_step_fp32(q[:, t], k[:, t], v[:, t], g[:, t], b[:, t],
+                                                 S_ref)
+        assert_close(f64(o[:, 0]), f64(o_ref), "bf16", f"step {t} o")
+        outs.append(o)
+    assert_close(f64(S), f64(S_ref), "bf16", "state")
+    picks = [(0, 0), (5, 3), (31, 15), (63, 7)]
+    bi = [p[0] for p in picks]
+    hi = [p[1] for p in picks]
+    o_all = torch.cat(outs, 1)
+    ro, rh = orc.recurrent_ref(f64(q[bi, :, hi][:, :, None]), f64(k[bi, :, hi][:, :, None]),
+                               f64(v[bi, :, hi][:, :, None]), f64(g[bi, :, hi][:, :, None]),
+                               f64(b[bi, :, hi][:, :, None]), f64(S0[bi, hi][:, None]))
+    assert_close(f64(o_all[bi, :, hi]), ro[:, :, 0], "bf16", "sampled o vs oracle")
+    assert_close(f64(S[bi, hi]), rh[:, 0], "bf16", "sampled state vs oracle")
+    assert np.isfinite(f64(S)).all()
