@@ -29,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_fwd",
     "gdn_chunk_workspace_bytes",
     "gdn_last_error",
+    "gdn_device_error",
     "gdn_abi_version",
 )
 
@@ -59,6 +60,8 @@ def _declare(lib):
     lib.gdn_chunk_workspace_bytes.restype = _sz
     lib.gdn_last_error.argtypes = []
     lib.gdn_last_error.restype = ctypes.c_char_p
+    lib.gdn_device_error.argtypes = [_i]
+    lib.gdn_device_error.restype = _i
     lib.gdn_abi_version.argtypes = []
     lib.gdn_abi_version.restype = _i
 

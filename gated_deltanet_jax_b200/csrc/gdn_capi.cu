@@ -3,6 +3,8 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdarg>
+#include <cstdlib>
+#include <cstring>
 
 #include "gdn.h"
 #include "gdn_internal.h"
@@ -105,12 +107,24 @@ int gdn_chunk_fwd(const void* q, const void* k, const void* v, const float* g, c
   }
   gdn::ChunkArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, chunk, dtype, semantics,
                    workspace, ws_bytes};
+  // GDN_CHUNK_KERNEL=simt forces the CUDA-core kernel (kernel cross-checks).
+  const char* force = getenv("GDN_CHUNK_KERNEL");
+  const bool simt_only = force && strcmp(force, "simt") == 0;
+  if (!simt_only && gdn::chunk_tc_supported(a))
+    return cuda_status(gdn::launch_chunk_tc(a, (cudaStream_t)stream), "gdn_chunk_fwd");
   if (gdn::chunk_simt_smem_bytes(a) == 0)
     return fail(GDN_ERR_UNSUPPORTED, "no chunk kernel fits dk=%d dv=%d chunk=%d", dk, dv, chunk);
   return cuda_status(gdn::launch_chunk_simt(a, (cudaStream_t)stream), "gdn_chunk_fwd");
 }
 
 const char* gdn_last_error(void) { return g_err; }
+
+int gdn_device_error(int clear) {
+  // Synchronous: waits for the current device's outstanding work.
+  const int a = gdn::device_error_recurrent_bulk(clear != 0);
+  const int b = gdn::device_error_chunk_tc(clear != 0);
+  return a ? a : b;
+}
 
 int gdn_abi_version(void) { return (1 << 16) | 0; }
 

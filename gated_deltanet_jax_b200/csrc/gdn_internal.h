@@ -37,6 +37,18 @@ struct ChunkArgs {
 
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);
 
+// Decode step (T == 1) with the state streamed by bulk copies (dk = dv = 128).
+bool recurrent_bulk_supported(const RecurrentArgs& a);
+cudaError_t launch_recurrent_bulk(const RecurrentArgs& a, cudaStream_t st);
+
+// Device error words of the kernel files with bounded waits (0 = none).
+int device_error_recurrent_bulk(bool clear);
+int device_error_chunk_tc(bool clear);
+
+// Tensor-core chunk kernel: bf16, dk = 128, dv % 64 == 0, chunk = 64, exact.
+bool chunk_tc_supported(const ChunkArgs& a);
+cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
+
 // Portable CUDA-core chunk kernel (any supported shape, fp32 or bf16 inputs).
 cudaError_t launch_chunk_simt(const ChunkArgs& a, cudaStream_t st);
 // Shared-memory bytes launch_chunk_simt needs for this shape (0 = unsupported).

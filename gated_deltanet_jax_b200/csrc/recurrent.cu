@@ -172,6 +172,7 @@ cudaError_t launch_t(const RecurrentArgs& a, cudaStream_t st) {
 
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (recurrent_bulk_supported(a)) return launch_recurrent_bulk(a, st);
   return a.dtype == kBF16 ? launch_t<__nv_bfloat16>(a, st) : launch_t<float>(a, st);
 }
 

@@ -81,6 +81,16 @@ int gdn_chunk_fwd(const void* q, const void* k, const void* v,
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
                                  int dtype, int semantics);
 
+/*
+ * Device-side error word of the current device (0 = none; 1 = a bounded wait
+ * inside a kernel gave up, so that launch's results are invalid).  Kernels
+ * with pipelined copies never spin without limit: a wait that runs out
+ * records the error and the kernel returns.  Synchronous (it waits for the
+ * device's outstanding work); clear != 0 resets the word.  Diagnostics only;
+ * no counterpart in the reference, which has no device-side waits.
+ */
+int gdn_device_error(int clear);
+
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 

@@ -108,3 +108,50 @@ def test_prefill_config_full_size(cuda):
     assert_close(f64(o[bi, :, hi]), ro[:, :, 0], "bf16", "o")
     assert_close(f64(hT[bi, hi]), rh[:, 0], "bf16", "state")
     assert np.isfinite(ro).all()
+
+
+def _with_kernel(kind, fn):
+    import os
+    old = os.environ.get("GDN_CHUNK_KERNEL")
+    os.environ["GDN_CHUNK_KERNEL"] = kind
+    try:
+        return fn()
+    finally:
+        if old is None:
+            del os.environ["GDN_CHUNK_KERNEL"]
+        else:
+            os.environ["GDN_CHUNK_KERNEL"] = old
+
+
+@pytest.mark.parametrize("dv", [64, 128, 256])
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 300])
+@pytest.mark.parametrize("with_h0", [False, True])
+def test_tensor_core_path_against_oracle(cuda, dv, T, with_h0):
+    """bf16, dk=128, chunk=64: the tcgen05 kernel's shapes, partial chunks included."""
+    (q, k, v, g, b, h0), host = device_inputs(2, T, 3, 128, dv, seed=dv + T, dtype="bf16",
+                                              dev=cuda, h0_std=0.05)
+    o, hT = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0 if with_h0 else None,
+                                       output_final_state=True)
+    ro, rh = orc.chunk_exact(*host[:5], host[5] if with_h0 else None, 64)
+    assert_close(f64(o), ro, "bf16", "o")
+    assert_close(f64(hT), rh, "bf16", "state")
+
+
+@pytest.mark.parametrize("B,T,H,dv", [(1, 640, 2, 128), (3, 257, 5, 64), (2, 129, 1, 512)])
+def test_tensor_core_matches_cuda_core_kernel(cuda, B, T, H, dv):
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, dv, seed=T, dtype="bf16", dev=cuda,
+                                           h0_std=0.02)
+
+    def run():
+        return ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                          output_final_state=True)
+
+    o_tc, h_tc = run()
+    o_cc, h_cc = _with_kernel("simt", run)
+    assert_close(f64(o_tc), f64(o_cc), "bf16", "o")
+    assert_close(f64(h_tc), f64(h_cc), "bf16", "state")
+
+
+def test_no_device_error_recorded_chunk(cuda):
+    from gated_deltanet_jax_b200 import _lib
+    assert _lib.load().gdn_device_error(1) == 0

@@ -107,3 +107,27 @@ def test_decode_config_full_size(cuda):
     assert_close(f64(o_all[bi, :, hi]), ro[:, :, 0], "bf16", "sampled o vs oracle")
     assert_close(f64(S[bi, hi]), rh[:, 0], "bf16", "sampled state vs oracle")
     assert np.isfinite(f64(S)).all()
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("with_h0,with_hT", [(True, True), (False, True), (True, False),
+                                             (False, False)])
+@pytest.mark.parametrize("B,H", [(1, 3), (7, 11), (37, 16)])
+def test_decode_step_state_modes(cuda, dtype, with_h0, with_hT, B, H):
+    """Single-token steps at dk=dv=128 (the bulk-copy decode kernel): every
+    combination of initial / final state, fewer and more heads than SMs."""
+    (q, k, v, g, b, h0), host = device_inputs(B, 1, H, 128, 128, seed=B * H, dtype=dtype,
+                                              dev=cuda, h0_std=0.05)
+    o, hT = ops.fused_recurrent_gated_delta_rule(
+        q, k, v, g, b, initial_state=h0 if with_h0 else None, output_final_state=with_hT)
+    ro, rh = orc.recurrent_ref(*host[:5], host[5] if with_h0 else None)
+    assert_close(f64(o), ro, dtype, "o")
+    if with_hT:
+        assert_close(f64(hT), rh, dtype, "state")
+    else:
+        assert hT is None
+
+
+def test_no_device_error_recorded(cuda):
+    from gated_deltanet_jax_b200 import _lib
+    assert _lib.load().gdn_device_error(1) == 0
