@@ -12,7 +12,8 @@
 //   prep (independent of the state; runs one chunk ahead):
 //     D_pre = [K;Q] K^T                      (M=128: rows K K^T, then Q K^T)
 //     A = tril_{-1}(beta_i e^{G_i-G_j} K K^T),  P = tril_0(e^{G_i-G_j} Q K^T)
-//     T = (I + A)^{-1}                       (fp32 blocked substitution, CUDA cores)
+//     T = (I + A)^{-1}                       (16x16 diagonal blocks by fp32 substitution,
+//                                             off-diagonal blocks on tf32 warp MMAs)
 //     tile TP = [T; P] (bf16, 128 x 64)
 //   chain (sequential over chunks, state S [128 x 64] fp32 in registers):
 //     D1 = [K;Q] S_bf16                      rows 0-63: K S, rows 64-127: Q S
@@ -46,6 +47,7 @@ constexpr int DVT = 64;
 constexpr int NSTAGE = 2;
 constexpr int kThreads = 384;
 constexpr int LDF = 68;  // fp32 row stride of the A / T matrices (16-byte aligned rows)
+constexpr int LDY = 20;  // fp32 row stride of the per-warp 16x16 scratch
 
 // Shared-memory byte offsets from a 1024-byte aligned base.
 constexpr int SM_KQ = 0;                        // NSTAGE x [2 kblk][128 rows][128 B]
@@ -57,10 +59,12 @@ constexpr int SM_VP = SM_VPP + 8192;            // V'
 constexpr int SM_TP = SM_VP + 8192;             // 2 x [128 rows][128 B]: rows 0-63 T, 64-127 P
 constexpr int SM_AF = SM_TP + 2 * 16384;        // fp32 A [64][LDF]
 constexpr int SM_TF = SM_AF + 64 * LDF * 4;     // fp32 T [64][LDF]
-constexpr int SM_Y = SM_TF + 64 * LDF * 4;      // fp32 [3][16][16]
-constexpr int SM_VEC = SM_Y + 3 * 256 * 4;      // 2 x VecBuf
+constexpr int SM_Y = SM_TF + 64 * LDF * 4;      // fp32 [3 warps][16][LDY]
+constexpr int SM_VEC = SM_Y + 3 * 16 * LDY * 4; // 2 x VecBuf
 struct VecBuf {
   float G[C], eG[C], dec[C], beta[C];
+  float F[C][4];  // e^{G_i - G_{16k}} for k <= i / 16 (gate factors, row part)
+  float E[C];     // e^{G_{16 floor(j/16)} - G_j}      (gate factors, column part)
   float eGC, pad[3];
 };
 constexpr int SM_BAR = SM_VEC + 2 * (int)sizeof(VecBuf);
@@ -119,11 +123,41 @@ __device__ __forceinline__ void unpack_bf16x8(uint4 u, float* f) {
   }
 }
 
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// D(16x8) += A(16x8, row) * B(8x8, col), tf32 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// OR of `pred` over the 128 threads of the prep warpgroup (named barrier 1).
+__device__ __forceinline__ int __syncthreads_or_named(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return (int)r;
+}
+
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Bounded wait that every lane of a warp performs; returns false on timeout.
+// Bounded wait by a single thread (the elected lane of a one-thread role).
 __device__ __forceinline__ bool wait_bar(uint64_t* bars, int idx, uint32_t parity) {
   return mbar_wait(&bars[idx], parity);
 }
@@ -133,9 +167,11 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
                 const float* __restrict__ beta, const float* __restrict__ h0,
                 __nv_bfloat16* __restrict__ o, float* __restrict__ hT, int T, int H, int dv) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* sm = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // Round up to 1024 bytes by offsetting the shared array itself, so that the
+  // compiler keeps every access below in the shared address space.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SM_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + SM_TMEM);
   VecBuf* vecs = reinterpret_cast<VecBuf*>(sm + SM_VEC);
@@ -296,10 +332,10 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     auto fetch = [&](int n) {
       if (p < 32) {
         const int t = n * C + 2 * p;
-        gn0 = t < T ? g[gb + (size_t)t * H] : 0.f;
-        gn1 = t + 1 < T ? g[gb + (size_t)(t + 1) * H] : 0.f;
-        bn0 = t < T ? beta[gb + (size_t)t * H] : 0.f;
-        bn1 = t + 1 < T ? beta[gb + (size_t)(t + 1) * H] : 0.f;
+        gn0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
+        gn1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
+        bn0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
+        bn1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
       }
     };
     fetch(0);
@@ -328,14 +364,37 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         vb.G[2 * p + 1] = G1;
         vb.beta[2 * p] = bn0;
         vb.beta[2 * p + 1] = bn1;
-        vb.eG[2 * p] = __expf(G0);
-        vb.eG[2 * p + 1] = __expf(G1);
-        vb.dec[2 * p] = __expf(GC - G0);
-        vb.dec[2 * p + 1] = __expf(GC - G1);
-        if (p == 0) vb.eGC = __expf(GC);
+        vb.eG[2 * p] = gate_exp(G0);
+        vb.eG[2 * p + 1] = gate_exp(G1);
+        vb.dec[2 * p] = gate_exp(GC - G0);
+        vb.dec[2 * p + 1] = gate_exp(GC - G1);
+        if (p == 0) vb.eGC = gate_exp(GC);
         if (n + 1 < N) fetch(n + 1);
       }
       named_sync(1, 128);
+      // Separable gate factors: e^{G_i - G_j} = F[i][j/16] * E[j] for j <= i.
+      // Every exponent lies in one 16-token block or spans from a block start
+      // to a later row; if any exceeds 40 (a factor could then overflow, or
+      // hide a non-negligible product behind an underflowed partner) the
+      // chunk forms e^{G_i - G_j} directly instead.
+      bool direct;
+      {
+        const int i = p & 63, k0 = (p >> 6) * 2;
+        float big = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const int k = k0 + kk;
+          const float x = (16 * k <= i) ? vb.G[i] - vb.G[16 * k] : 0.f;
+          vb.F[i][k] = gate_exp(x);
+          big = fmaxf(big, x);
+        }
+        if (p < 64) {
+          const float x = vb.G[p & ~15] - vb.G[p];
+          vb.E[p] = gate_exp(x);
+          big = fmaxf(big, x);
+        }
+        direct = __syncthreads_or_named(big > 40.f) != 0;
+      }
       // A (rows 0-63) and P (rows 64-127) from D_pre
       ok = wait_bar(bars, B_PRE_FULL + pb, (uint32_t)(n >> 1) & 1u);
       if (!ok) break;
@@ -345,20 +404,24 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         const float Gi = vb.G[i], bi = vb.beta[i];
         const uint32_t ta = tmem + TM_PRE + (uint32_t)pb * 64 + ((uint32_t)(wq * 32) << 16);
 #pragma unroll
+        const int jmax = p < 64 ? i - 1 : i;  // A is strictly lower, P includes the diagonal
+        const float rs = p < 64 ? bi : 1.f;
         for (int q4 = 0; q4 < 4; ++q4) {
           float v[16];
           tmem_ld16(ta + q4 * 16, v);
-          tmem_ld_wait();
           float out[16];
+          const float fq = rs * vb.F[i][q4];
+          if (!direct) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int j = q4 * 16 + e;
-            if (p < 64) {
-              const float d = (j < i) ? Gi - vb.G[j] : -INFINITY;
-              out[e] = bi * __expf(d) * v[e];
-            } else {
-              const float d = (j <= i) ? Gi - vb.G[j] : -INFINITY;
-              out[e] = __expf(d) * v[e];
+            for (int e = 0; e < 16; ++e) {
+              const int j = q4 * 16 + e;
+              out[e] = (j <= jmax) ? fq * vb.E[j] * v[e] : 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int j = q4 * 16 + e;
+              out[e] = (j <= jmax) ? rs * gate_exp(Gi - vb.G[j]) * v[e] : 0.f;
             }
           }
           if (p < 64) {
@@ -393,47 +456,65 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         for (int r = 0; r < 16; ++r) Tb[r * LDF + c] = t[r];
       }
       named_sync(1, 128);
-      // ---- off-diagonal blocks, one block diagonal at a time ----
-      for (int L = 1; L < 4; ++L) {
-        const int nstrip = (4 - L) * 64;
-        for (int sidx = p; sidx < nstrip; sidx += 128) {
-          const int jb = sidx >> 6, rr = (sidx >> 2) & 15, c4 = (sidx & 3) * 4;
-          const int ib = jb + L;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int kb = jb; kb < ib; ++kb) {
-            const float* arow = AF + (ib * 16 + rr) * LDF + kb * 16;
-            const float* tcol = TF + (kb * 16) * LDF + jb * 16 + c4;
+      // ---- off-diagonal blocks, one block diagonal at a time:
+      //      T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj  (warp w: block j = w),
+      //      16x16 products on warp-level tf32 MMAs (m16n8k8), fp32 accumulate ----
+      {
+        const int gq = lane >> 2, tq = lane & 3;
+        float* Yw = Y + wq * 16 * LDY;
+        for (int L = 1; L < 4; ++L) {
+          if (wq < 4 - L) {
+            const int jb = wq, ib = jb + L;
+            float acc[2][4] = {};
+            for (int kb = jb; kb < ib; ++kb) {
 #pragma unroll
-            for (int x = 0; x < 16; ++x) {
-              const float a = arow[x];
-              const float4 tv = *reinterpret_cast<const float4*>(tcol + x * LDF);
-              acc.x = fmaf(a, tv.x, acc.x);
-              acc.y = fmaf(a, tv.y, acc.y);
-              acc.z = fmaf(a, tv.z, acc.z);
-              acc.w = fmaf(a, tv.w, acc.w);
+              for (int kk = 0; kk < 16; kk += 8) {
+                const float* Ar = AF + (ib * 16) * LDF + kb * 16 + kk;
+                const uint32_t a[4] = {to_tf32(Ar[gq * LDF + tq]), to_tf32(Ar[(gq + 8) * LDF + tq]),
+                                       to_tf32(Ar[gq * LDF + tq + 4]),
+                                       to_tf32(Ar[(gq + 8) * LDF + tq + 4])};
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                  const float* Tr = TF + (kb * 16 + kk) * LDF + jb * 16 + nt * 8;
+                  const uint32_t bb[2] = {to_tf32(Tr[tq * LDF + gq]), to_tf32(Tr[(tq + 4) * LDF + gq])};
+                  mma_tf32(acc[nt], a, bb);
+                }
+              }
             }
-          }
-          *reinterpret_cast<float4*>(Y + jb * 256 + rr * 16 + c4) = acc;
-        }
-        named_sync(1, 128);
-        for (int sidx = p; sidx < nstrip; sidx += 128) {
-          const int jb = sidx >> 6, rr = (sidx >> 2) & 15, c4 = (sidx & 3) * 4;
-          const int ib = jb + L;
-          const float* trow = TF + (ib * 16 + rr) * LDF + ib * 16;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int x = 0; x < 16; ++x) {
-            const float a = trow[x];
-            const float4 yv = *reinterpret_cast<const float4*>(Y + jb * 256 + x * 16 + c4);
-            acc.x = fmaf(a, yv.x, acc.x);
-            acc.y = fmaf(a, yv.y, acc.y);
-            acc.z = fmaf(a, yv.z, acc.z);
-            acc.w = fmaf(a, yv.w, acc.w);
+            for (int nt = 0; nt < 2; ++nt) {
+              Yw[gq * LDY + nt * 8 + 2 * tq] = acc[nt][0];
+              Yw[gq * LDY + nt * 8 + 2 * tq + 1] = acc[nt][1];
+              Yw[(gq + 8) * LDY + nt * 8 + 2 * tq] = acc[nt][2];
+              Yw[(gq + 8) * LDY + nt * 8 + 2 * tq + 1] = acc[nt][3];
+            }
+            __syncwarp();
+            float acc2[2][4] = {};
+#pragma unroll
+            for (int kk = 0; kk < 16; kk += 8) {
+              const float* Tr = TF + (ib * 16) * LDF + ib * 16 + kk;
+              const uint32_t a[4] = {to_tf32(Tr[gq * LDF + tq]), to_tf32(Tr[(gq + 8) * LDF + tq]),
+                                     to_tf32(Tr[gq * LDF + tq + 4]),
+                                     to_tf32(Tr[(gq + 8) * LDF + tq + 4])};
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) {
+                const uint32_t bb[2] = {to_tf32(Yw[(kk + tq) * LDY + nt * 8 + gq]),
+                                        to_tf32(Yw[(kk + tq + 4) * LDY + nt * 8 + gq])};
+                mma_tf32(acc2[nt], a, bb);
+              }
+            }
+            float* Td = TF + (ib * 16) * LDF + jb * 16;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              Td[gq * LDF + nt * 8 + 2 * tq] = -acc2[nt][0];
+              Td[gq * LDF + nt * 8 + 2 * tq + 1] = -acc2[nt][1];
+              Td[(gq + 8) * LDF + nt * 8 + 2 * tq] = -acc2[nt][2];
+              Td[(gq + 8) * LDF + nt * 8 + 2 * tq + 1] = -acc2[nt][3];
+            }
+            __syncwarp();
           }
-          *reinterpret_cast<float4*>(TF + (ib * 16 + rr) * LDF + jb * 16 + c4) =
-              make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
+          named_sync(1, 128);
         }
-        named_sync(1, 128);
       }
       // ---- T -> bf16 rows 0-63 of the TP tile (zero above the diagonal) ----
       if (p < 64) {
@@ -496,7 +577,6 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           tmem_ld16(d1 + q4 * 16, ks);
           unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4)), vv);
           unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4 + 1)), vv + 8);
-          tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 16; ++e) x[e] = bi * (vv[e] - egi * ks[e]);
           *reinterpret_cast<uint4*>(sm + SM_X + sw128(i, 2 * q4)) = pack_bf16x8(x);
@@ -515,7 +595,6 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         for (int q4 = 0; q4 < 4; ++q4) {
           float vp[16], vpp[16];
           tmem_ld16(tmem + TM_D2 + lane_off + q4 * 16, vp);
-          tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 16; ++e) vpp[e] = di * vp[e];
           *reinterpret_cast<uint4*>(sm + SM_VPP + sw128(i, 2 * q4)) = pack_bf16x8(vpp);
@@ -538,7 +617,6 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         for (int q4 = 0; q4 < 4; ++q4) {
           float ds[16];
           tmem_ld16(tmem + TM_D3 + lane_off + q4 * 16, ds);
-          tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 16; ++e) S[q4 * 16 + e] = fmaf(egc, S[q4 * 16 + e], ds[e]);
           *reinterpret_cast<uint4*>(Stile + sw128(r, 2 * q4)) = pack_bf16x8(S + q4 * 16);
@@ -563,7 +641,6 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           float qs[16], pv[16], out[16];
           tmem_ld16(d1 + q4 * 16, qs);
           tmem_ld16(tmem + TM_D4 + lane_off + q4 * 16, pv);
-          tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 16; ++e) out[e] = fmaf(egi, qs[e], pv[e]);
           if (t < T) {

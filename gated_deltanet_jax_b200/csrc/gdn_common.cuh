@@ -56,4 +56,14 @@ __device__ __forceinline__ float4 scale4(float a, float4 x) {
   return make_float4(a * x.x, a * x.y, a * x.z, a * x.w);
 }
 
+// e^x for gate factors, from e^x = 2^(x log2 e) and the PTX instruction
+// ex2.approx.ftz.f32 (documented maximum relative error 2^-22 for normal
+// results).  Results below the smallest normal float flush to zero, which is
+// below any gate factor that contributes to an output.
+__device__ __forceinline__ float gate_exp(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
+}
+
 }  // namespace gdn

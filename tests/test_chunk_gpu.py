@@ -155,3 +155,18 @@ def test_tensor_core_matches_cuda_core_kernel(cuda, B, T, H, dv):
 def test_no_device_error_recorded_chunk(cuda):
     from gated_deltanet_jax_b200 import _lib
     assert _lib.load().gdn_device_error(1) == 0
+
+
+@pytest.mark.parametrize("gscale,gshift", [(8.0, 0.0), (0.3, 0.25), (0.0, 0.0)])
+def test_tensor_core_gate_ranges(cuda, gscale, gshift):
+    """Steep decays (spans > 40 inside 16 tokens, the kernel's direct-exponent
+    path), gates of both signs, and no decay at all, against the oracle."""
+    (q, k, v, g, b, h0), host = device_inputs(2, 200, 2, 128, 128, seed=17, dtype="bf16",
+                                              dev=cuda, h0_std=0.05)
+    g = (g * gscale + gshift).contiguous()
+    host[3] = f64(g)
+    o, hT = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    ro, rh = orc.chunk_exact(*host[:5], host[5], 64)
+    assert np.isfinite(ro).all()
+    assert_close(f64(o), ro, "bf16", "o")
+    assert_close(f64(hT), rh, "bf16", "state")
