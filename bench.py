@@ -34,6 +34,7 @@ sys.path.insert(0, REPO)
 DEC = dict(B=64, H=16, dk=128, dv=128, tokens=512)
 NBUF = 4  # decode states used round robin per bench step
 PRE = dict(B=4, T=4096, H=16, dk=128, dv=128, chunk=64)
+LONG = dict(B=1, T=65536, H=16, dk=128, dv=128, chunk=64, parts=4)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -46,6 +47,7 @@ def _args():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end legs")
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill leg")
+    p.add_argument("--no-long", action="store_true", help="skip the long-context leg")
     return p.parse_args()
 
 
@@ -430,6 +432,53 @@ def prefill_leg(d, a, lib):
     return res
 
 
+def long_context_leg(d, a):
+    """B=1, T=65536, H=16 over all ranks (strong scaling: the sequence is split
+    evenly across ranks, the state handed off by an NCCL all-gather), each rank's
+    segment split again into parts on its GPU."""
+    import torch
+    from gated_deltanet_jax_b200 import ops, sequence_parallel as sp
+    from oracle import gdn_oracle as orc
+    B, T, H, dk, dv, C = (LONG[x] for x in ("B", "T", "H", "dk", "dv", "chunk"))
+    seg = T // d.world
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(7 + d.rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(B, seg, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    k = nrm(torch.randn(B, seg, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(B, seg, H, dv, device=d.dev, generator=gen).bfloat16()
+    g = torch.nn.functional.logsigmoid(torch.randn(B, seg, H, device=d.dev, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, seg, H, device=d.dev, generator=gen))
+    local_parts = max(1, LONG["parts"] // d.world)
+    if d.world == 1:
+        def step():
+            sp.chunk_gated_delta_rule_split(q, k, v, g, beta, output_final_state=True,
+                                            parts=local_parts)
+    else:
+        def step():
+            sp.chunk_gated_delta_rule_sp(q, k, v, g, beta, output_final_state=True,
+                                         local_parts=local_parts)
+    for _ in range(a.warmup):
+        step()
+    steps = max(1, min(a.steps, 20))
+    ms, _ = _timed(d, step, steps)
+    flops = T * H * orc.flops_chunk_per_token_head(dk, dv, C)
+    res = {"metric": "long-context chunk prefill tokens/s", "value": B * T / (ms / 1e3),
+           "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
+           "config": {"workload": f"B=1 T={T} H=16 dk=dv=128 chunk=64 bf16, sequence split over "
+                                  f"{d.world} GPU(s) x {local_parts} segment(s) per GPU, "
+                                  "final state out", "parallelism": f"sequence split sp{d.world}"},
+           "algorithmic_tflops": flops / (ms / 1e3) / 1e12}
+    if d.world == 1:
+        def direct():
+            ops.chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True)
+        for _ in range(2):
+            direct()
+        ms_d, _ = _timed(d, direct, max(1, min(a.steps, 5)))
+        res["unsplit_ms_per_step"] = ms_d
+    return res
+
+
 def main():
     a = _args()
     if a.impl == "reference":
@@ -450,6 +499,7 @@ def main():
 
     dec = decode_leg(d, a, lib, uuid)
     pre = None if a.no_prefill else prefill_leg(d, a, lib)
+    lng = None if a.no_long else long_context_leg(d, a)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not a.no_cpu:
@@ -505,6 +555,8 @@ def main():
             if cpu and cpu_pre:
                 pre_line["cpu_baseline"] = cpu_pre
             line["prefill"] = pre_line
+        if lng:
+            line["long_context"] = lng
         print(json.dumps(line), flush=True)
     d.close()
 

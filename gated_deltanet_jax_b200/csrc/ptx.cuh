@@ -103,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bulk copy global -> shared, completing `bytes` of transaction on `bar`.
-// dst, src 16-byte aligned; bytes a multiple of 16.  No multicast.
+// dst, src 16-byte aligned; bytes a multiple of 16; this CTA's shared memory only.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(
@@ -171,7 +171,7 @@ __device__ __forceinline__ bool elect_one() {
 namespace gdn {
 
 // ---------------------------------------------------------------------------
-// TMA tensor loads (tile mode, no multicast)
+// TMA tensor loads (tile mode, into this CTA's shared memory only)
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0, int c1, int c2,

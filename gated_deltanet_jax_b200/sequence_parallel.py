@@ -1,0 +1,156 @@
+"""Sequence-split chunked forward: one long sequence over several segments.
+
+The delta-rule state evolves affinely over a segment of tokens,
+
+    h_end = M h_start + S,     M = prod_t e^{g_t} (I - beta_t k_t k_t^T),
+
+where S is the end state from a zero start and M the end state of the same
+recurrence started from the identity with v = 0.  A long sequence is therefore
+processed in two passes over contiguous segments:
+
+1. per segment, in parallel: (S_p, M_p) from ONE chunked call on the extended
+   value / state  v' = [v | 0],  h0' = [0 | I]  (its final state is [S_p | M_p]);
+2. hand-off: S_in(0) = h0,  S_in(p+1) = M_p S_in(p) + S_p;
+3. per segment, in parallel: the chunked forward from S_in(p), giving o.
+
+Two placements of the segments:
+
+* :func:`chunk_gated_delta_rule_sp` -- one segment per rank of a
+  ``torch.distributed`` group (each rank holds its tokens); the hand-off is one
+  all-gather of the (S_p, M_p) pairs, after which every rank folds the prefix
+  locally (no sequential chain of sends).
+* :func:`chunk_gated_delta_rule_split` -- several segments of one sequence on
+  one GPU, laid side by side in the batch dimension so both passes run as single
+  wide launches.
+
+Both are exact (same math as the unsplit op, up to rounding).  The per-segment
+work runs through ``segment_fn`` -- by default the CUDA chunked op.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional, Tuple
+
+import torch
+
+from . import ops
+
+SegmentFn = Callable[..., Tuple[torch.Tensor, torch.Tensor]]
+
+
+def _default_segment_fn(chunk_size: int) -> SegmentFn:
+    def fn(q, k, v, g, beta, h0):
+        return ops.chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=h0,
+                                              output_final_state=True, chunk_size=chunk_size)
+    return fn
+
+
+def segment_summary(q, k, v, g, beta, segment_fn: SegmentFn):
+    """(S, M) of a segment: end state from zero and the transition matrix.
+
+    One call on v' = [v | 0] with h0' = [0 | I]; the returned state is [S | M]
+    with S [B,H,dk,dv] and M [B,H,dk,dk].
+    """
+    B, T, H, dk = k.shape
+    dv = v.shape[-1]
+    v_ext = torch.cat([v, torch.zeros(B, T, H, dk, dtype=v.dtype, device=v.device)], dim=-1)
+    h_ext = torch.zeros(B, H, dk, dv + dk, dtype=torch.float32, device=v.device)
+    h_ext[..., dv:] = torch.eye(dk, dtype=torch.float32, device=v.device)
+    _, ext = segment_fn(q, k, v_ext.contiguous(), g, beta, h_ext)
+    return ext[..., :dv].contiguous(), ext[..., dv:].contiguous()
+
+
+def fold_states(h0: torch.Tensor, pairs) -> list:
+    """States entering each segment: S_in(0) = h0, S_in(p+1) = M_p S_in(p) + S_p.
+
+    ``pairs`` is a sequence of (S_p, M_p); returns [S_in(0), ..., S_in(P)]
+    (the last entry is the state after the final segment).
+    """
+    states = [h0]
+    s = h0
+    for S_p, M_p in pairs:
+        s = torch.matmul(M_p, s) + S_p
+        states.append(s)
+    return states
+
+
+def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final_state=False,
+                              chunk_size=64, group=None, segment_fn: Optional[SegmentFn] = None,
+                              local_parts: int = 1):
+    """Chunked forward with the sequence split across the ranks of ``group``.
+
+    Every rank passes its own contiguous segment ``[B, T_p, H, D]`` (rank order =
+    token order; every segment but the last should hold whole chunks).
+    ``initial_state`` is the state before rank 0's segment and must be the same
+    on every rank (or None).  ``local_parts > 1`` also splits each rank's segment
+    on its GPU (:func:`chunk_gated_delta_rule_split`).  Returns
+    ``(o_segment, final_state or None)``; ``final_state`` is the state after the
+    LAST segment, on every rank.
+    """
+    import torch.distributed as dist
+
+    fn = segment_fn or _default_segment_fn(chunk_size)
+    if local_parts > 1:
+        inner = fn
+
+        def fn(q_, k_, v_, g_, b_, h_):  # noqa: F811
+            return chunk_gated_delta_rule_split(q_, k_, v_, g_, b_, initial_state=h_,
+                                                output_final_state=True, chunk_size=chunk_size,
+                                                parts=local_parts, segment_fn=inner)
+    B, T, H, dk = k.shape
+    dv = v.shape[-1]
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    S_p, M_p = segment_summary(q, k, v, g, beta, fn)
+    packed = torch.cat([S_p, M_p], dim=-1).contiguous()                # [B,H,dk,dv+dk]
+    gathered = [torch.empty_like(packed) for _ in range(world)]
+    dist.all_gather(gathered, packed, group=group)
+    pairs = [(x[..., :dv], x[..., dv:]) for x in gathered]
+    h0 = (torch.zeros(B, H, dk, dv, dtype=packed.dtype, device=v.device)
+          if initial_state is None else initial_state.to(packed.dtype))
+    states = fold_states(h0, pairs)
+    o, _ = fn(q, k, v, g, beta, states[rank].contiguous())
+    return (o, states[world]) if output_final_state else (o, None)
+
+
+def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_final_state=False,
+                                 chunk_size=64, parts: int = 4,
+                                 segment_fn: Optional[SegmentFn] = None):
+    """Chunked forward of B long sequences, each split into ``parts`` segments
+    that run side by side in the batch dimension of two wide launches.
+
+    The sequence is zero-padded (g = 0, beta = 0, k = v = 0) up to a multiple of
+    ``parts * chunk_size``; padded tokens leave the state unchanged.  Returns
+    ``(o, final_state or None)`` like the unsplit op.
+    """
+    fn = segment_fn or _default_segment_fn(chunk_size)
+    B, T, H, dk = k.shape
+    dv = v.shape[-1]
+    if parts <= 1 or T <= chunk_size:
+        o, hT = fn(q, k, v, g, beta, initial_state)
+        return (o, hT) if output_final_state else (o, None)
+    seg = -(-T // (parts * chunk_size)) * chunk_size          # tokens per segment
+    Tp = seg * parts
+    pad = Tp - T
+
+    def to_segments(x):
+        if pad:
+            x = torch.cat([x, torch.zeros((B, pad) + tuple(x.shape[2:]), dtype=x.dtype,
+                                          device=x.device)], dim=1)
+        return x.reshape((B * parts, seg) + tuple(x.shape[2:])).contiguous()
+
+    qs, ks, vs, gs, bs = (to_segments(x) for x in (q, k, v, g, beta))
+    S, M = segment_summary(qs, ks, vs, gs, bs, fn)                      # [B*parts, H, ...]
+    S = S.view(B, parts, H, dk, dv)
+    M = M.view(B, parts, H, dk, dk)
+    h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
+          if initial_state is None else initial_state.to(S.dtype))
+    states = fold_states(h0, [(S[:, p], M[:, p]) for p in range(parts)])
+    s_in = torch.stack(states[:parts], dim=1).reshape(B * parts, H, dk, dv).contiguous()
+    o, _ = fn(qs, ks, vs, gs, bs, s_in)
+    o = o.reshape(B, Tp, H, dv)[:, :T]
+    return (o, states[parts]) if output_final_state else (o, None)
+
+
+__all__ = ["chunk_gated_delta_rule_sp", "chunk_gated_delta_rule_split", "segment_summary",
+           "fold_states"]

@@ -1,0 +1,139 @@
+"""Sequence-split forward: host logic on CPU (oracle as the per-segment
+function, gloo ranks for the distributed hand-off) and the CUDA path on GPU."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gated_deltanet_jax_b200 import sequence_parallel as sp
+from oracle import gdn_oracle as orc
+
+
+def oracle_segment_fn(chunk_size=16):
+    """Per-segment chunked forward by the float64 oracle on CPU tensors."""
+    def fn(q, k, v, g, beta, h0):
+        arrs = [x.detach().cpu().numpy().astype(np.float64) for x in (q, k, v, g, beta)]
+        h = None if h0 is None else h0.detach().cpu().numpy().astype(np.float64)
+        o, hT = orc.chunk_exact(*arrs, h, chunk_size)
+        return torch.from_numpy(o), torch.from_numpy(hT)
+    return fn
+
+
+def _t(x):
+    return torch.from_numpy(np.asarray(x, np.float64))
+
+
+@pytest.mark.parametrize("B,T,parts", [(1, 200, 4), (2, 96, 3), (1, 50, 2), (1, 16, 4)])
+def test_split_on_one_device_matches_oracle(B, T, parts):
+    q, k, v, g, beta, h0 = orc.make_inputs(B, T, 2, 16, 24, seed=T, h0_std=0.05)
+    o, hT = sp.chunk_gated_delta_rule_split(*(_t(x) for x in (q, k, v, g, beta)),
+                                            initial_state=_t(h0), output_final_state=True,
+                                            chunk_size=16, parts=parts,
+                                            segment_fn=oracle_segment_fn(16))
+    ro, rh = orc.recurrent_ref(q, k, v, g, beta, h0)
+    assert orc.max_abs_err(o.numpy(), ro) < 1e-10
+    assert orc.max_abs_err(hT.numpy(), rh) < 1e-10
+
+
+def test_segment_summary_is_affine_map():
+    q, k, v, g, beta, h0 = orc.make_inputs(1, 40, 2, 16, 16, seed=1, h0_std=0.1)
+    S, M = sp.segment_summary(*(_t(x) for x in (q, k, v, g, beta)), oracle_segment_fn(16))
+    _, hT = orc.recurrent_ref(q, k, v, g, beta, h0)
+    assert orc.max_abs_err((M @ _t(h0) + S).numpy(), hT) < 1e-10
+
+
+def _sp_worker(rank, world, port, T, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, v, g, beta, h0 = orc.make_inputs(1, T, 2, 16, 16, seed=5, h0_std=0.05)
+        seg = T // world
+        sl = slice(rank * seg, (rank + 1) * seg if rank < world - 1 else T)
+        args = [_t(x[:, sl]) for x in (q, k, v, g, beta)]
+        o, hT = sp.chunk_gated_delta_rule_sp(*args, initial_state=_t(h0), output_final_state=True,
+                                             chunk_size=16, segment_fn=oracle_segment_fn(16))
+        ro, rh = orc.recurrent_ref(q, k, v, g, beta, h0)
+        results[rank] = (orc.max_abs_err(o.numpy(), ro[:, sl]), orc.max_abs_err(hT.numpy(), rh))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_split_across_gloo_ranks_matches_oracle(world):
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        port = 29500 + world * 7 + os.getpid() % 500
+        procs = [ctx.Process(target=_sp_worker, args=(r, world, port, 160, results))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+        for r in range(world):
+            eo, eh = results[r]
+            assert eo < 1e-10 and eh < 1e-10, (r, eo, eh)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,T,H,parts", [(1, 4096, 4, 4), (2, 1000, 2, 3), (1, 8192, 2, 8)])
+def test_split_cuda_matches_unsplit(cuda, B, T, H, parts):
+    from helpers import assert_close, device_inputs_fast, f64
+    from gated_deltanet_jax_b200 import ops
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, 128, seed=T, dtype="bf16", dev=cuda,
+                                           h0_std=0.02)
+    o_ref, h_ref = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                              output_final_state=True)
+    o, hT = sp.chunk_gated_delta_rule_split(q, k, v, g, b, initial_state=h0,
+                                            output_final_state=True, parts=parts)
+    assert_close(f64(o), f64(o_ref), "bf16", "o")
+    assert_close(f64(hT), f64(h_ref), "bf16", "state")
+
+
+def _nccl_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from helpers import device_inputs_fast, f64
+        from gated_deltanet_jax_b200 import ops
+        T = 2048 * world
+        q, k, v, g, b, h0 = device_inputs_fast(1, T, 4, 128, 128, seed=3, dtype="bf16", dev=dev,
+                                               h0_std=0.02)
+        seg = T // world
+        sl = slice(rank * seg, (rank + 1) * seg)
+        o, hT = sp.chunk_gated_delta_rule_sp(q[:, sl], k[:, sl], v[:, sl], g[:, sl], b[:, sl],
+                                             initial_state=h0, output_final_state=True,
+                                             local_parts=2)
+        o_ref, h_ref = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                                  output_final_state=True)
+        results[rank] = (orc.rel_err(f64(o), f64(o_ref[:, sl])), orc.rel_err(f64(hT), f64(h_ref)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_split_across_nccl_ranks(cuda):
+    """Two GPUs: each rank holds half of the sequence; NCCL all-gather hand-off."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        procs = [ctx.Process(target=_nccl_worker, args=(r, 2, 29611, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+        for r in range(2):
+            eo, eh = results[r]
+            assert eo <= orc.TOL_BF16_REL and eh <= orc.TOL_BF16_REL, (r, eo, eh)
