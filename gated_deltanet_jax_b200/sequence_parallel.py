@@ -74,43 +74,67 @@ def fold_states(h0: torch.Tensor, pairs) -> list:
     return states
 
 
+def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, parts, fn,
+              gather, world, rank):
+    """Both passes over this rank's tokens split into ``parts`` batched segments.
+
+    ``gather`` maps this rank's packed (S, M) pairs [B, parts, H, dk, dv + dk] to
+    the list of every rank's, in rank order; segments are ordered rank-major.
+    """
+    B, T, H, dk = k.shape
+    dv = v.shape[-1]
+    seg = -(-T // (parts * chunk_size)) * chunk_size          # tokens per segment
+    Tp = seg * parts
+    pad = Tp - T
+
+    def to_segments(x):
+        if pad:
+            x = torch.cat([x, torch.zeros((B, pad) + tuple(x.shape[2:]), dtype=x.dtype,
+                                          device=x.device)], dim=1)
+        return x.reshape((B * parts, seg) + tuple(x.shape[2:])).contiguous()
+
+    qs, ks, vs, gs, bs = (to_segments(x) for x in (q, k, v, g, beta))
+    S, M = segment_summary(qs, ks, vs, gs, bs, fn)                      # [B*parts, H, ...]
+    packed = torch.cat([S, M], dim=-1).view(B, parts, H, dk, dv + dk).contiguous()
+    pairs = [(x[:, p, ..., :dv], x[:, p, ..., dv:]) for x in gather(packed)
+             for p in range(parts)]
+    h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
+          if initial_state is None else initial_state.to(S.dtype))
+    states = fold_states(h0, pairs)
+    mine = states[rank * parts:(rank + 1) * parts]
+    s_in = torch.stack(mine, dim=1).reshape(B * parts, H, dk, dv).contiguous()
+    o, _ = fn(qs, ks, vs, gs, bs, s_in)
+    o = o.reshape(B, Tp, H, dv)[:, :T]
+    return (o, states[world * parts]) if output_final_state else (o, None)
+
+
 def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final_state=False,
                               chunk_size=64, group=None, segment_fn: Optional[SegmentFn] = None,
                               local_parts: int = 1):
     """Chunked forward with the sequence split across the ranks of ``group``.
 
     Every rank passes its own contiguous segment ``[B, T_p, H, D]`` (rank order =
-    token order; every segment but the last should hold whole chunks).
+    token order; every rank's T_p is the same, except possibly the last one's).
+    Each rank splits its segment again into ``local_parts`` segments that run
+    batched on its GPU; all world x local_parts (S, M) pairs are exchanged in one
+    all-gather, after which every rank folds the prefix locally.
     ``initial_state`` is the state before rank 0's segment and must be the same
-    on every rank (or None).  ``local_parts > 1`` also splits each rank's segment
-    on its GPU (:func:`chunk_gated_delta_rule_split`).  Returns
-    ``(o_segment, final_state or None)``; ``final_state`` is the state after the
-    LAST segment, on every rank.
+    on every rank (or None).  Returns ``(o_segment, final_state or None)``;
+    ``final_state`` is the state after the LAST segment, on every rank.
     """
     import torch.distributed as dist
 
     fn = segment_fn or _default_segment_fn(chunk_size)
-    if local_parts > 1:
-        inner = fn
-
-        def fn(q_, k_, v_, g_, b_, h_):  # noqa: F811
-            return chunk_gated_delta_rule_split(q_, k_, v_, g_, b_, initial_state=h_,
-                                                output_final_state=True, chunk_size=chunk_size,
-                                                parts=local_parts, segment_fn=inner)
-    B, T, H, dk = k.shape
-    dv = v.shape[-1]
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    S_p, M_p = segment_summary(q, k, v, g, beta, fn)
-    packed = torch.cat([S_p, M_p], dim=-1).contiguous()                # [B,H,dk,dv+dk]
-    gathered = [torch.empty_like(packed) for _ in range(world)]
-    dist.all_gather(gathered, packed, group=group)
-    pairs = [(x[..., :dv], x[..., dv:]) for x in gathered]
-    h0 = (torch.zeros(B, H, dk, dv, dtype=packed.dtype, device=v.device)
-          if initial_state is None else initial_state.to(packed.dtype))
-    states = fold_states(h0, pairs)
-    o, _ = fn(q, k, v, g, beta, states[rank].contiguous())
-    return (o, states[world]) if output_final_state else (o, None)
+
+    def gather(packed):
+        out = [torch.empty_like(packed) for _ in range(world)]
+        dist.all_gather(out, packed, group=group)
+        return out
+
+    return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
+                     max(1, int(local_parts)), fn, gather, world, rank)
 
 
 def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_final_state=False,
@@ -124,32 +148,12 @@ def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_fi
     ``(o, final_state or None)`` like the unsplit op.
     """
     fn = segment_fn or _default_segment_fn(chunk_size)
-    B, T, H, dk = k.shape
-    dv = v.shape[-1]
+    T = k.shape[1]
     if parts <= 1 or T <= chunk_size:
         o, hT = fn(q, k, v, g, beta, initial_state)
         return (o, hT) if output_final_state else (o, None)
-    seg = -(-T // (parts * chunk_size)) * chunk_size          # tokens per segment
-    Tp = seg * parts
-    pad = Tp - T
-
-    def to_segments(x):
-        if pad:
-            x = torch.cat([x, torch.zeros((B, pad) + tuple(x.shape[2:]), dtype=x.dtype,
-                                          device=x.device)], dim=1)
-        return x.reshape((B * parts, seg) + tuple(x.shape[2:])).contiguous()
-
-    qs, ks, vs, gs, bs = (to_segments(x) for x in (q, k, v, g, beta))
-    S, M = segment_summary(qs, ks, vs, gs, bs, fn)                      # [B*parts, H, ...]
-    S = S.view(B, parts, H, dk, dv)
-    M = M.view(B, parts, H, dk, dk)
-    h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
-          if initial_state is None else initial_state.to(S.dtype))
-    states = fold_states(h0, [(S[:, p], M[:, p]) for p in range(parts)])
-    s_in = torch.stack(states[:parts], dim=1).reshape(B * parts, H, dk, dv).contiguous()
-    o, _ = fn(qs, ks, vs, gs, bs, s_in)
-    o = o.reshape(B, Tp, H, dv)[:, :T]
-    return (o, states[parts]) if output_final_state else (o, None)
+    return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, parts, fn,
+                     lambda packed: [packed], 1, 0)
 
 
 __all__ = ["chunk_gated_delta_rule_sp", "chunk_gated_delta_rule_split", "segment_summary",

@@ -46,7 +46,7 @@ def test_segment_summary_is_affine_map():
     assert orc.max_abs_err((M @ _t(h0) + S).numpy(), hT) < 1e-10
 
 
-def _sp_worker(rank, world, port, T, results):
+def _sp_worker(rank, world, port, T, results, local_parts=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -56,20 +56,21 @@ def _sp_worker(rank, world, port, T, results):
         sl = slice(rank * seg, (rank + 1) * seg if rank < world - 1 else T)
         args = [_t(x[:, sl]) for x in (q, k, v, g, beta)]
         o, hT = sp.chunk_gated_delta_rule_sp(*args, initial_state=_t(h0), output_final_state=True,
-                                             chunk_size=16, segment_fn=oracle_segment_fn(16))
+                                             chunk_size=16, segment_fn=oracle_segment_fn(16),
+                                             local_parts=local_parts)
         ro, rh = orc.recurrent_ref(q, k, v, g, beta, h0)
         results[rank] = (orc.max_abs_err(o.numpy(), ro[:, sl]), orc.max_abs_err(hT.numpy(), rh))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_split_across_gloo_ranks_matches_oracle(world):
+@pytest.mark.parametrize("world,local_parts", [(2, 1), (3, 1), (2, 3)])
+def test_split_across_gloo_ranks_matches_oracle(world, local_parts):
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
         results = mgr.dict()
-        port = 29500 + world * 7 + os.getpid() % 500
-        procs = [ctx.Process(target=_sp_worker, args=(r, world, port, 160, results))
+        port = 29500 + world * 7 + local_parts * 31 + os.getpid() % 500
+        procs = [ctx.Process(target=_sp_worker, args=(r, world, port, 160, results, local_parts))
                  for r in range(world)]
         for p in procs:
             p.start()
