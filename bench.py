@@ -374,7 +374,7 @@ def decode_leg(d, a, lib, uuid):
     return res
 
 
-def prefill_leg(d, a, lib):
+def prefill_leg(d, a, lib, uuid=None):
     import torch
     from gated_deltanet_jax_b200 import _lib, ops
     from oracle import gdn_oracle as orc
@@ -402,10 +402,13 @@ def prefill_leg(d, a, lib):
 
     for _ in range(a.warmup):
         step()
-    ms, _ = _timed(d, step, a.steps)
+    # ~0.25 ms per launch: time enough launches for the clock sampler to see them.
+    steps = max(a.steps, 1000)
+    sampler = ClockSampler(uuid) if d.rank == 0 else None
+    ms, clocks = _timed(d, step, steps, sampler)
     flops = B * T * H * orc.flops_chunk_per_token_head(dk, dv, C)
     res = {"ms": ms, "value": d.world * B * T / (ms / 1e3), "flops_launch": flops,
-           "launch_s": ms / 1e3, "launches": a.steps,
+           "launch_s": ms / 1e3, "launches": steps, "steps": steps, "clocks": clocks,
            "bytes_launch": B * T * H * orc.bytes_chunk_per_token_head(dk, dv) + B * H * dk * dv * 4}
     if not a.no_e2e:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
@@ -498,7 +501,7 @@ def main():
         pass
 
     dec = decode_leg(d, a, lib, uuid)
-    pre = None if a.no_prefill else prefill_leg(d, a, lib)
+    pre = None if a.no_prefill else prefill_leg(d, a, lib, uuid)
     lng = None if a.no_long else long_context_leg(d, a)
 
     cpu = None
@@ -540,7 +543,7 @@ def main():
             bf16 = float(peaks["bf16_tflops"])
             pre_line = {
                 "metric": "chunk prefill tokens/s", "value": pre["value"], "unit": "tokens/s",
-                "ms_per_step": pre["ms"],
+                "ms_per_step": pre["ms"], "steps": pre["steps"], "clocks": pre["clocks"],
                 "config": {"workload": "chunked prefill B=4 T=4096 H=16 dk=dv=128 chunk=64, "
                                        "bf16 in, fp32 state, final state out",
                            "l2": "inputs larger than L2 (201 MB q/k/v per GPU)"},

@@ -26,8 +26,9 @@
 //     O = e^G (Q S) + P V'                   (rows 64-127 of D1 and D4)
 //
 // Warp roles (384 threads): warp 0 issues TMA loads, warp 1 the chain MMAs
-// and owns the tensor memory, warp 2 the prep MMAs; warps 4-7 do the prep
-// math, warps 8-11 the chain epilogues.  A warp reads only its own quarter of
+// and owns the tensor memory, warp 2 the prep MMAs, warp 3 computes the gate
+// vectors two chunks ahead; warps 4-7 do the prep math, warps 8-11 the chain
+// epilogues.  A warp reads only its own quarter of
 // the 128 TMEM lanes, so row r of every M=128 accumulator belongs to thread r
 // of a warpgroup.  All hand-offs are mbarriers; every wait is bounded.
 #include <cuda.h>
@@ -59,13 +60,15 @@ constexpr int SM_VP = SM_VPP + 8192;            // V'
 constexpr int SM_TP = SM_VP + 8192;             // 2 x [128 rows][128 B]: rows 0-63 T, 64-127 P
 constexpr int SM_AF = SM_TP + 2 * 16384;        // fp32 A [64][LDF]
 constexpr int SM_TF = SM_AF + 64 * LDF * 4;     // fp32 T [64][LDF]
-constexpr int SM_Y = SM_TF + 64 * LDF * 4;      // fp32 [3 warps][16][LDY]
-constexpr int SM_VEC = SM_Y + 3 * 16 * LDY * 4; // 2 x VecBuf
+constexpr int SM_Y = SM_TF + 64 * LDF * 4;      // fp32 [6 blocks][16][LDY] solve scratch
+constexpr int SM_VEC = SM_Y + 6 * 16 * LDY * 4; // 2 x VecBuf
 struct VecBuf {
   float G[C], eG[C], dec[C], beta[C];
   float F[C][4];  // e^{G_i - G_{16k}} for k <= i / 16 (gate factors, row part)
   float E[C];     // e^{G_{16 floor(j/16)} - G_j}      (gate factors, column part)
-  float eGC, pad[3];
+  float eGC;
+  int direct;     // 1: a factor exponent exceeds 40; form e^{G_i - G_j} directly
+  float pad[2];
 };
 constexpr int SM_BAR = SM_VEC + 2 * (int)sizeof(VecBuf);
 constexpr int NBAR = 24;
@@ -84,6 +87,7 @@ enum {
   B_TP_EMPTY = 10,   // [2] chain done with a chunk's TP / vectors
   B_D1 = 12, B_D2 = 13, B_D3 = 14, B_D4 = 15, B_D4_EMPTY = 16,
   B_X_READY = 17, B_VPP_READY = 18, B_S_READY = 19, B_CHAIN_DONE = 20,
+  B_VEC_FULL = 21,   // [2] gate vectors of a chunk ready
 };
 
 // TMEM columns
@@ -139,18 +143,60 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// OR of `pred` over the 128 threads of the prep warpgroup (named barrier 1).
-__device__ __forceinline__ int __syncthreads_or_named(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred)
-      : "memory");
-  return (int)r;
+// Warp-level 16x16 block products for the triangular solve (tf32 m16n8k8,
+// fp32 accumulate).  acc holds the C fragments of the two 16x8 halves:
+// thread (g = lane/4, t = lane%4) owns rows g, g+8 and columns 2t, 2t+1 of each.
+__device__ __forceinline__ void mma16x16(float (&acc)[2][4], const float* A, int lda,
+                                         const float* B, int ldb, int gq, int tq) {
+#pragma unroll
+  for (int kk = 0; kk < 16; kk += 8) {
+    const uint32_t a[4] = {to_tf32(A[gq * lda + kk + tq]), to_tf32(A[(gq + 8) * lda + kk + tq]),
+                           to_tf32(A[gq * lda + kk + tq + 4]),
+                           to_tf32(A[(gq + 8) * lda + kk + tq + 4])};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const uint32_t bb[2] = {to_tf32(B[(kk + tq) * ldb + nt * 8 + gq]),
+                              to_tf32(B[(kk + tq + 4) * ldb + nt * 8 + gq])};
+      mma_tf32(acc[nt], a, bb);
+    }
+  }
+}
+
+__device__ __forceinline__ void store16x16(float* D, int ld, const float (&acc)[2][4], float s,
+                                           int gq, int tq) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    *reinterpret_cast<float2*>(D + gq * ld + nt * 8 + 2 * tq) =
+        make_float2(s * acc[nt][0], s * acc[nt][1]);
+    *reinterpret_cast<float2*>(D + (gq + 8) * ld + nt * 8 + 2 * tq) =
+        make_float2(s * acc[nt][2], s * acc[nt][3]);
+  }
+}
+
+__device__ __forceinline__ void load16x16(float (&acc)[2][4], const float* D, int ld, int gq,
+                                          int tq) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const float2 x = *reinterpret_cast<const float2*>(D + gq * ld + nt * 8 + 2 * tq);
+    const float2 y = *reinterpret_cast<const float2*>(D + (gq + 8) * ld + nt * 8 + 2 * tq);
+    acc[nt][0] = x.x; acc[nt][1] = x.y; acc[nt][2] = y.x; acc[nt][3] = y.y;
+  }
+}
+
+// s * acc as bf16 into the 16x16 block at (r0, c0) of a 128-byte-swizzled tile.
+__device__ __forceinline__ void store16x16_bf16(unsigned char* tile, int r0, int c0,
+                                                const float (&acc)[2][4], float s, int gq,
+                                                int tq) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int col = c0 + nt * 8 + 2 * tq;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int row = r0 + gq + 8 * h2;
+      *reinterpret_cast<__nv_bfloat162*>(tile + sw128(row, col >> 3) + (col & 7) * 2) =
+          __floats2bfloat162_rn(s * acc[nt][2 * h2], s * acc[nt][2 * h2 + 1]);
+    }
+  }
 }
 
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
@@ -203,6 +249,8 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     mbar_init(&bars[B_VPP_READY], 2);
     mbar_init(&bars[B_S_READY], 4);
     mbar_init(&bars[B_CHAIN_DONE], 1);
+    mbar_init(&bars[B_VEC_FULL + 0], 1);
+    mbar_init(&bars[B_VEC_FULL + 1], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -323,22 +371,77 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         mma_commit(&bars[B_PRE_FULL + pb]);
       }
     }
+  } else if (warp == 3) {
+    // ------------------------------ gate warp ------------------------------
+    // Per chunk, as soon as its buffer is free (two chunks ahead of the chain):
+    // g and beta, the in-chunk cumulative gate G, e^G, e^{G_C - G}, e^{G_C}, and
+    // the separable factors e^{G_i - G_j} = F[i][j/16] * E[j] (j <= i).  Every
+    // factor exponent lies inside one 16-token block or runs from a block start
+    // to a later row; if any exceeds 40 (a factor could overflow, or hide a
+    // non-negligible product behind an underflowed partner) the chunk is flagged
+    // to form e^{G_i - G_j} directly.
+    const size_t gb = (size_t)b * T * H + h;
+    bool ok = true;
+    for (int n = 0; n < N && ok; ++n) {
+      const int pb = n & 1;
+      VecBuf& vb = vecs[pb];
+      const int t = n * C + 2 * lane;
+      const float g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
+      const float g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
+      const float b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
+      const float b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
+      if (n >= 2) ok = wait_bar(bars, B_TP_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
+      if (!ok) break;
+      const float pair = g0 + g1;
+      float incl = pair;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      const float G0 = incl - pair + g0, G1 = incl;
+      const float GC = __shfl_sync(0xffffffffu, incl, 31);
+      vb.G[2 * lane] = G0;
+      vb.G[2 * lane + 1] = G1;
+      vb.beta[2 * lane] = b0;
+      vb.beta[2 * lane + 1] = b1;
+      vb.eG[2 * lane] = gate_exp(G0);
+      vb.eG[2 * lane + 1] = gate_exp(G1);
+      vb.dec[2 * lane] = gate_exp(GC - G0);
+      vb.dec[2 * lane + 1] = gate_exp(GC - G1);
+      if (lane == 0) vb.eGC = gate_exp(GC);
+      __syncwarp();
+      float big = 0.f;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int i = lane + 32 * half;
+        const float Gi = vb.G[i];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float x = (16 * k <= i) ? Gi - vb.G[16 * k] : 0.f;
+          vb.F[i][k] = gate_exp(x);
+          big = fmaxf(big, x);
+        }
+        const float x = vb.G[i & ~15] - Gi;
+        vb.E[i] = gate_exp(x);
+        big = fmaxf(big, x);
+      }
+      const int direct = __any_sync(0xffffffffu, big > 40.f) ? 1 : 0;
+      if (lane == 0) vb.direct = direct;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[B_VEC_FULL + pb]);
+    }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------ prep warpgroup ------------------------------
     const int p = tid - 128;          // TMEM lane / row
     const int wq = warp - 4;          // lane quarter
-    const size_t gb = (size_t)b * T * H + h;
-    float gn0 = 0.f, gn1 = 0.f, bn0 = 0.f, bn1 = 0.f;
-    auto fetch = [&](int n) {
-      if (p < 32) {
-        const int t = n * C + 2 * p;
-        gn0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
-        gn1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
-        bn0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
-        bn1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
-      }
-    };
-    fetch(0);
+    // The strictly upper 16x16 blocks of T are never written below: zero them once.
+    for (int e = p; e < 2 * 64 * 8; e += 128) {
+      const int buf = e / 512, row = (e / 8) % 64, c8 = e % 8;
+      if (c8 >= 2 * (row / 16 + 1))
+        *reinterpret_cast<uint4*>(sm + SM_TP + buf * 16384 + sw128(row, c8)) =
+            make_uint4(0u, 0u, 0u, 0u);
+    }
     float* AF = reinterpret_cast<float*>(sm + SM_AF);
     float* TF = reinterpret_cast<float*>(sm + SM_TF);
     float* Y = reinterpret_cast<float*>(sm + SM_Y);
@@ -349,52 +452,9 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       unsigned char* tpt = sm + SM_TP + pb * 16384;
       if (n >= 2) ok = wait_bar(bars, B_TP_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
       if (!ok) break;
-      // per-chunk vectors: cumulative gate and its exponentials (warp 0)
-      if (p < 32) {
-        const float pair = gn0 + gn1;
-        float incl = pair;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float y = __shfl_up_sync(0xffffffffu, incl, off);
-          if (lane >= off) incl += y;
-        }
-        const float G0 = incl - pair + gn0, G1 = incl;
-        const float GC = __shfl_sync(0xffffffffu, incl, 31);
-        vb.G[2 * p] = G0;
-        vb.G[2 * p + 1] = G1;
-        vb.beta[2 * p] = bn0;
-        vb.beta[2 * p + 1] = bn1;
-        vb.eG[2 * p] = gate_exp(G0);
-        vb.eG[2 * p + 1] = gate_exp(G1);
-        vb.dec[2 * p] = gate_exp(GC - G0);
-        vb.dec[2 * p + 1] = gate_exp(GC - G1);
-        if (p == 0) vb.eGC = gate_exp(GC);
-        if (n + 1 < N) fetch(n + 1);
-      }
-      named_sync(1, 128);
-      // Separable gate factors: e^{G_i - G_j} = F[i][j/16] * E[j] for j <= i.
-      // Every exponent lies in one 16-token block or spans from a block start
-      // to a later row; if any exceeds 40 (a factor could then overflow, or
-      // hide a non-negligible product behind an underflowed partner) the
-      // chunk forms e^{G_i - G_j} directly instead.
-      bool direct;
-      {
-        const int i = p & 63, k0 = (p >> 6) * 2;
-        float big = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          const int k = k0 + kk;
-          const float x = (16 * k <= i) ? vb.G[i] - vb.G[16 * k] : 0.f;
-          vb.F[i][k] = gate_exp(x);
-          big = fmaxf(big, x);
-        }
-        if (p < 64) {
-          const float x = vb.G[p & ~15] - vb.G[p];
-          vb.E[p] = gate_exp(x);
-          big = fmaxf(big, x);
-        }
-        direct = __syncthreads_or_named(big > 40.f) != 0;
-      }
+      ok = wait_bar(bars, B_VEC_FULL + pb, (uint32_t)(n >> 1) & 1u);
+      if (!ok) break;
+      const bool direct = vb.direct != 0;
       // A (rows 0-63) and P (rows 64-127) from D_pre
       ok = wait_bar(bars, B_PRE_FULL + pb, (uint32_t)(n >> 1) & 1u);
       if (!ok) break;
@@ -403,26 +463,21 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         const int i = p & 63;
         const float Gi = vb.G[i], bi = vb.beta[i];
         const uint32_t ta = tmem + TM_PRE + (uint32_t)pb * 64 + ((uint32_t)(wq * 32) << 16);
-#pragma unroll
         const int jmax = p < 64 ? i - 1 : i;  // A is strictly lower, P includes the diagonal
         const float rs = p < 64 ? bi : 1.f;
+        float vrow[64];
+        tmem_ld64(ta, vrow);
+#pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          float v[16];
-          tmem_ld16(ta + q4 * 16, v);
+          const float* v = vrow + 16 * q4;
           float out[16];
-          const float fq = rs * vb.F[i][q4];
-          if (!direct) {
+          // direct exponents (steep gates only) use factor 1 here and are
+          // applied by a rolled pass below
+          const float fq = direct ? 1.f : rs * vb.F[i][q4];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int j = q4 * 16 + e;
-              out[e] = (j <= jmax) ? fq * vb.E[j] * v[e] : 0.f;
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int j = q4 * 16 + e;
-              out[e] = (j <= jmax) ? rs * gate_exp(Gi - vb.G[j]) * v[e] : 0.f;
-            }
+          for (int e = 0; e < 16; ++e) {
+            const int j = q4 * 16 + e;
+            out[e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) * v[e] : 0.f;
           }
           if (p < 64) {
 #pragma unroll
@@ -432,6 +487,21 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           } else {
             *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4)) = pack_bf16x8(out);
             *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4 + 1)) = pack_bf16x8(out + 8);
+          }
+        }
+      }
+      if (direct) {
+        // steep gates: scale the stored row by rs * e^{G_i - G_j} element by element
+        const int i = p & 63;
+        const float Gi = vb.G[i], rs = p < 64 ? vb.beta[i] : 1.f;
+#pragma unroll 1
+        for (int j = 0; j <= i; ++j) {
+          const float f = rs * gate_exp(Gi - vb.G[j]);
+          if (p < 64) {
+            AF[i * LDF + j] *= f;
+          } else {
+            __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(tpt + sw128(p, j >> 3) + (j & 7) * 2);
+            *e = __float2bfloat16_rn(__bfloat162float(*e) * f);
           }
         }
       }
@@ -453,80 +523,67 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         }
         float* Tb = TF + (blk * 16) * LDF + blk * 16;
 #pragma unroll
-        for (int r = 0; r < 16; ++r) Tb[r * LDF + c] = t[r];
-      }
-      named_sync(1, 128);
-      // ---- off-diagonal blocks, one block diagonal at a time:
-      //      T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj  (warp w: block j = w),
-      //      16x16 products on warp-level tf32 MMAs (m16n8k8), fp32 accumulate ----
-      {
-        const int gq = lane >> 2, tq = lane & 3;
-        float* Yw = Y + wq * 16 * LDY;
-        for (int L = 1; L < 4; ++L) {
-          if (wq < 4 - L) {
-            const int jb = wq, ib = jb + L;
-            float acc[2][4] = {};
-            for (int kb = jb; kb < ib; ++kb) {
-#pragma unroll
-              for (int kk = 0; kk < 16; kk += 8) {
-                const float* Ar = AF + (ib * 16) * LDF + kb * 16 + kk;
-                const uint32_t a[4] = {to_tf32(Ar[gq * LDF + tq]), to_tf32(Ar[(gq + 8) * LDF + tq]),
-                                       to_tf32(Ar[gq * LDF + tq + 4]),
-                                       to_tf32(Ar[(gq + 8) * LDF + tq + 4])};
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                  const float* Tr = TF + (kb * 16 + kk) * LDF + jb * 16 + nt * 8;
-                  const uint32_t bb[2] = {to_tf32(Tr[tq * LDF + gq]), to_tf32(Tr[(tq + 4) * LDF + gq])};
-                  mma_tf32(acc[nt], a, bb);
-                }
-              }
-            }
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              Yw[gq * LDY + nt * 8 + 2 * tq] = acc[nt][0];
-              Yw[gq * LDY + nt * 8 + 2 * tq + 1] = acc[nt][1];
-              Yw[(gq + 8) * LDY + nt * 8 + 2 * tq] = acc[nt][2];
-              Yw[(gq + 8) * LDY + nt * 8 + 2 * tq + 1] = acc[nt][3];
-            }
-            __syncwarp();
-            float acc2[2][4] = {};
-#pragma unroll
-            for (int kk = 0; kk < 16; kk += 8) {
-              const float* Tr = TF + (ib * 16) * LDF + ib * 16 + kk;
-              const uint32_t a[4] = {to_tf32(Tr[gq * LDF + tq]), to_tf32(Tr[(gq + 8) * LDF + tq]),
-                                     to_tf32(Tr[gq * LDF + tq + 4]),
-                                     to_tf32(Tr[(gq + 8) * LDF + tq + 4])};
-#pragma unroll
-              for (int nt = 0; nt < 2; ++nt) {
-                const uint32_t bb[2] = {to_tf32(Yw[(kk + tq) * LDY + nt * 8 + gq]),
-                                        to_tf32(Yw[(kk + tq + 4) * LDY + nt * 8 + gq])};
-                mma_tf32(acc2[nt], a, bb);
-              }
-            }
-            float* Td = TF + (ib * 16) * LDF + jb * 16;
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              Td[gq * LDF + nt * 8 + 2 * tq] = -acc2[nt][0];
-              Td[gq * LDF + nt * 8 + 2 * tq + 1] = -acc2[nt][1];
-              Td[(gq + 8) * LDF + nt * 8 + 2 * tq] = -acc2[nt][2];
-              Td[(gq + 8) * LDF + nt * 8 + 2 * tq + 1] = -acc2[nt][3];
-            }
-            __syncwarp();
-          }
-          named_sync(1, 128);
+        for (int r = 0; r < 16; ++r) {
+          Tb[r * LDF + c] = t[r];
+          const int row = blk * 16 + r, col = blk * 16 + c;
+          *reinterpret_cast<__nv_bfloat16*>(tpt + sw128(row, col >> 3) + (col & 7) * 2) =
+              __float2bfloat16_rn(t[r]);
         }
       }
-      // ---- T -> bf16 rows 0-63 of the TP tile (zero above the diagonal) ----
-      if (p < 64) {
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int j = c8 * 8 + e;
-            f[e] = (j <= p) ? TF[p * LDF + j] : 0.f;
+      named_sync(1, 128);
+      // ---- off-diagonal 16x16 blocks T_ij (i > j).  With Z = A_{2:4,0:2} T_{0:2,0:2}
+      //      (blocks Z00 Z01 / Z10 Z11) and scratch blocks W0, W1, four phases of
+      //      one warp task each -- acc = [C] + A1 B1 [+ A2 B2] -- on tf32 warp MMAs:
+      //   phase 0: W0 = A10 T00 | W1 = A32 T22 | Z01 = A21 T11 | Z11 = A31 T11
+      //   phase 1: T10 = -T11 W0 | T32 = -T33 W1 | Z00 = A20 T00 | Z10 = A30 T00
+      //   phase 2: Z00 += A21 T10 | Z10 += A31 T10 | - | -
+      //   phase 3: T20 = -T22 Z00 | T21 = -T22 Z01 | T30 = -(T32 Z00 + T33 Z10)
+      //            | T31 = -(T32 Z01 + T33 Z11)
+      //   Finished T blocks go to TF (when needed later) and to the bf16 tile.
+      //   The phases run as one rolled loop so the product code exists once. ----
+      {
+        const int gq = lane >> 2, tq = lane & 3;
+        auto Z = [&](int k) { return Y + k * 16 * LDY; };  // Z00 Z01 Z10 Z11 W0 W1
+        auto Ab = [&](int i, int j) { return AF + (i * 16) * LDF + j * 16; };
+        auto Tb = [&](int i, int j) { return TF + (i * 16) * LDF + j * 16; };
+#pragma unroll 1
+        for (int ph = 0; ph < 4; ++ph) {
+          const float *A1 = nullptr, *B1 = nullptr, *A2 = nullptr, *B2 = nullptr;
+          const float* Cin = nullptr;
+          float* D = nullptr;
+          int ldb1 = LDF, ldb2 = LDF, ldd = LDY, br = -1, bc = 0;
+          float sc = 1.f;
+          if (ph == 0) {
+            if (wq == 0) { A1 = Ab(1, 0); B1 = Tb(0, 0); D = Z(4); }
+            else if (wq == 1) { A1 = Ab(3, 2); B1 = Tb(2, 2); D = Z(5); }
+            else if (wq == 2) { A1 = Ab(2, 1); B1 = Tb(1, 1); D = Z(1); }
+            else { A1 = Ab(3, 1); B1 = Tb(1, 1); D = Z(3); }
+          } else if (ph == 1) {
+            if (wq < 2) {
+              const int i = 2 * wq + 1, j = 2 * wq;
+              A1 = Tb(i, i); B1 = Z(4 + wq); ldb1 = LDY; D = Tb(i, j); ldd = LDF;
+              br = i * 16; bc = j * 16; sc = -1.f;
+            } else if (wq == 2) { A1 = Ab(2, 0); B1 = Tb(0, 0); D = Z(0); }
+            else { A1 = Ab(3, 0); B1 = Tb(0, 0); D = Z(2); }
+          } else if (ph == 2) {
+            if (wq < 2) { Cin = Z(2 * wq); A1 = Ab(2 + wq, 1); B1 = Tb(1, 0); D = Z(2 * wq); }
+          } else {
+            const int j = wq & 1;
+            A1 = Tb(wq < 2 ? 2 : 3, 2); B1 = Z(j); ldb1 = LDY;
+            if (wq >= 2) { A2 = Tb(3, 3); B2 = Z(2 + j); ldb2 = LDY; }
+            br = (wq < 2 ? 2 : 3) * 16; bc = j * 16; sc = -1.f;
           }
-          *reinterpret_cast<uint4*>(tpt + sw128(p, c8)) = pack_bf16x8(f);
+          if (A1) {
+            float acc[2][4] = {};
+            if (Cin) load16x16(acc, Cin, LDY, gq, tq);
+#pragma unroll 1
+            for (int pi = 0; pi < (A2 ? 2 : 1); ++pi)
+              mma16x16(acc, pi ? A2 : A1, LDF, pi ? B2 : B1, pi ? ldb2 : ldb1, gq, tq);
+            if (D) store16x16(D, ldd, acc, sc, gq, tq);
+            if (br >= 0) store16x16_bf16(tpt, br, bc, acc, sc, gq, tq);
+          }
+          if (ph == 0) __syncwarp();
+          else named_sync(1, 128);
         }
       }
       fence_proxy_async_smem();
@@ -566,15 +623,18 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         const int i = r;
         ok = wait_bar(bars, B_D1, (uint32_t)n & 1u) &&
              wait_bar(bars, B_TP_READY + tb, (uint32_t)(n >> 1) & 1u) &&
-             wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u);
+             wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u) &&
+             wait_bar(bars, B_VEC_FULL + tb, (uint32_t)(n >> 1) & 1u);
         if (!ok) break;
         tc_fence_after();
         const float bi = vb.beta[i], egi = vb.eG[i];
         const unsigned char* Vt = sm + SM_V + s * 8192;
+        float ksrow[64];
+        tmem_ld64(d1, ksrow);
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          float ks[16], vv[16], x[16];
-          tmem_ld16(d1 + q4 * 16, ks);
+          float vv[16], x[16];
+          const float* ks = ksrow + 16 * q4;
           unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4)), vv);
           unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4 + 1)), vv + 8);
 #pragma unroll
@@ -591,10 +651,12 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         if (!ok) break;
         tc_fence_after();
         const float di = vb.dec[i];
+        float vprow[64];
+        tmem_ld64(tmem + TM_D2 + lane_off, vprow);
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          float vp[16], vpp[16];
-          tmem_ld16(tmem + TM_D2 + lane_off + q4 * 16, vp);
+          float vpp[16];
+          const float* vp = vprow + 16 * q4;
 #pragma unroll
           for (int e = 0; e < 16; ++e) vpp[e] = di * vp[e];
           *reinterpret_cast<uint4*>(sm + SM_VPP + sw128(i, 2 * q4)) = pack_bf16x8(vpp);
@@ -608,15 +670,18 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         if (lane == 0) mbar_arrive(&bars[B_VPP_READY]);
       }
       // ---- epilogue 3: S <- e^{G_C} S + K^T V''  (all 128 rows) ----
-      ok = wait_bar(bars, B_D3, (uint32_t)n & 1u);
+      // (warps 2-3 read the gate vectors from here on: acquire them directly)
+      ok = wait_bar(bars, B_D3, (uint32_t)n & 1u) &&
+           (wq < 2 || wait_bar(bars, B_VEC_FULL + tb, (uint32_t)(n >> 1) & 1u));
       if (!ok) break;
       tc_fence_after();
       {
         const float egc = vb.eGC;
+        float dsrow[64];
+        tmem_ld64(tmem + TM_D3 + lane_off, dsrow);
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          float ds[16];
-          tmem_ld16(tmem + TM_D3 + lane_off + q4 * 16, ds);
+          const float* ds = dsrow + 16 * q4;
 #pragma unroll
           for (int e = 0; e < 16; ++e) S[q4 * 16 + e] = fmaf(egc, S[q4 * 16 + e], ds[e]);
           *reinterpret_cast<uint4*>(Stile + sw128(r, 2 * q4)) = pack_bf16x8(S + q4 * 16);
