@@ -25,12 +25,13 @@
 //     S <- e^{G_C} S + D3                    -> bf16 tile for the next chunk
 //     O = e^G (Q S) + P V'                   (rows 64-127 of D1 and D4)
 //
-// Warp roles (384 threads): warp 0 issues TMA loads, warp 1 the chain MMAs
+// Warp roles (512 threads): warp 0 issues TMA loads, warp 1 the chain MMAs
 // and owns the tensor memory, warp 2 the prep MMAs, warp 3 computes the gate
-// vectors two chunks ahead; warps 4-7 do the prep math, warps 8-11 the chain
-// epilogues.  A warp reads only its own quarter of
-// the 128 TMEM lanes, so row r of every M=128 accumulator belongs to thread r
-// of a warpgroup.  All hand-offs are mbarriers; every wait is bounded.
+// vectors two chunks ahead; warps 4-11 do the prep math (two warps per TMEM
+// lane quarter, one per 32 columns), warps 12-15 the chain epilogues.  A warp
+// reads only its own quarter of the 128 TMEM lanes, so row r of every M=128
+// accumulator belongs to thread r of a warpgroup.  All hand-offs are
+// mbarriers; every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -46,9 +47,14 @@ constexpr int C = 64;
 constexpr int DK = 128;
 constexpr int DVT = 64;
 constexpr int NSTAGE = 2;
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
+// Register split (per thread): the kernel is compiled for, and launched with,
+// kLaunchRegs; warpgroup 0 (producer, MMA issuers, gate) gives registers to the
+// chain warpgroup.  4 x 128 threads x (56 + 128 + 128 + 200) = 512 x 128.
+constexpr int kLaunchRegs = 128;
+constexpr int kRegsRoles = 56, kRegsPrep = 128, kRegsChain = 200;
+static_assert(kRegsRoles + 2 * kRegsPrep + kRegsChain == 4 * kLaunchRegs, "register split");
 constexpr int LDF = 68;  // fp32 row stride of the A / T matrices (16-byte aligned rows)
-constexpr int LDY = 20;  // fp32 row stride of the per-warp 16x16 scratch
 
 // Shared-memory byte offsets from a 1024-byte aligned base.
 constexpr int SM_KQ = 0;                        // NSTAGE x [2 kblk][128 rows][128 B]
@@ -60,8 +66,7 @@ constexpr int SM_VP = SM_VPP + 8192;            // V'
 constexpr int SM_TP = SM_VP + 8192;             // 2 x [128 rows][128 B]: rows 0-63 T, 64-127 P
 constexpr int SM_AF = SM_TP + 2 * 16384;        // fp32 A [64][LDF]
 constexpr int SM_TF = SM_AF + 64 * LDF * 4;     // fp32 T [64][LDF]
-constexpr int SM_Y = SM_TF + 64 * LDF * 4;      // fp32 [6 blocks][16][LDY] solve scratch
-constexpr int SM_VEC = SM_Y + 6 * 16 * LDY * 4; // 2 x VecBuf
+constexpr int SM_VEC = SM_TF + 64 * LDF * 4;    // 2 x VecBuf
 struct VecBuf {
   float G[C], eG[C], dec[C], beta[C];
   float F[C][4];  // e^{G_i - G_{16k}} for k <= i / 16 (gate factors, row part)
@@ -143,20 +148,26 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
+// fp32 value rounded to tf32 (kept as an fp32 bit pattern with the low 13 bits clear).
+__device__ __forceinline__ float rtf32(float x) { return __uint_as_float(to_tf32(x)); }
+
 // Warp-level 16x16 block products for the triangular solve (tf32 m16n8k8,
-// fp32 accumulate).  acc holds the C fragments of the two 16x8 halves:
-// thread (g = lane/4, t = lane%4) owns rows g, g+8 and columns 2t, 2t+1 of each.
+// fp32 accumulate).  Operands are read as stored: every value in the solve
+// scratch is already rounded to tf32.  acc holds the C fragments of the two
+// 16x8 halves: thread (g = lane/4, t = lane%4) owns rows g, g+8 and columns
+// 2t, 2t+1 of each.
 __device__ __forceinline__ void mma16x16(float (&acc)[2][4], const float* A, int lda,
                                          const float* B, int ldb, int gq, int tq) {
 #pragma unroll
   for (int kk = 0; kk < 16; kk += 8) {
-    const uint32_t a[4] = {to_tf32(A[gq * lda + kk + tq]), to_tf32(A[(gq + 8) * lda + kk + tq]),
-                           to_tf32(A[gq * lda + kk + tq + 4]),
-                           to_tf32(A[(gq + 8) * lda + kk + tq + 4])};
+    const uint32_t a[4] = {__float_as_uint(A[gq * lda + kk + tq]),
+                           __float_as_uint(A[(gq + 8) * lda + kk + tq]),
+                           __float_as_uint(A[gq * lda + kk + tq + 4]),
+                           __float_as_uint(A[(gq + 8) * lda + kk + tq + 4])};
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      const uint32_t bb[2] = {to_tf32(B[(kk + tq) * ldb + nt * 8 + gq]),
-                              to_tf32(B[(kk + tq + 4) * ldb + nt * 8 + gq])};
+      const uint32_t bb[2] = {__float_as_uint(B[(kk + tq) * ldb + nt * 8 + gq]),
+                              __float_as_uint(B[(kk + tq + 4) * ldb + nt * 8 + gq])};
       mma_tf32(acc[nt], a, bb);
     }
   }
@@ -167,21 +178,70 @@ __device__ __forceinline__ void store16x16(float* D, int ld, const float (&acc)[
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
     *reinterpret_cast<float2*>(D + gq * ld + nt * 8 + 2 * tq) =
-        make_float2(s * acc[nt][0], s * acc[nt][1]);
+        make_float2(rtf32(s * acc[nt][0]), rtf32(s * acc[nt][1]));
     *reinterpret_cast<float2*>(D + (gq + 8) * ld + nt * 8 + 2 * tq) =
-        make_float2(s * acc[nt][2], s * acc[nt][3]);
+        make_float2(rtf32(s * acc[nt][2]), rtf32(s * acc[nt][3]));
   }
 }
 
-__device__ __forceinline__ void load16x16(float (&acc)[2][4], const float* D, int ld, int gq,
-                                          int tq) {
+__device__ __forceinline__ void load16x16(float (&acc)[2][4], const float* D, int ld, float s,
+                                          int gq, int tq) {
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
     const float2 x = *reinterpret_cast<const float2*>(D + gq * ld + nt * 8 + 2 * tq);
     const float2 y = *reinterpret_cast<const float2*>(D + (gq + 8) * ld + nt * 8 + 2 * tq);
-    acc[nt][0] = x.x; acc[nt][1] = x.y; acc[nt][2] = y.x; acc[nt][3] = y.y;
+    acc[nt][0] = s * x.x; acc[nt][1] = s * x.y; acc[nt][2] = s * y.x; acc[nt][3] = s * y.y;
   }
 }
+
+// Off-diagonal blocks of T = (I + A)^{-1} (4x4 blocks of 16; T_ii known from the
+// diagonal substitution).  With M_xy = A_xy T_yy the block recurrences
+//   T_x,x-1 = -T_xx M_x,x-1
+//   T_20 = T_22 (M_21 M_10 - M_20)             = T_22 N_20
+//   T_31 = T_33 (M_32 M_21 - M_31)             = T_33 N_31
+//   T_30 = T_33 (M_31 M_10 - M_30) + T_32 N_20 = T_33 N_30 + T_32 N_20
+// need three dependent product steps:
+//   phase 0: M_10 M_20 M_30 M_21 M_31 M_32
+//   phase 1: T_10 T_21 T_32, N_20 N_30 N_31
+//   phase 2: T_20 T_31 T_30
+// Intermediates live in the fp32 T scratch: the M blocks in its (unused) strictly
+// upper blocks, N_20 N_30 N_31 and T_32 in lower blocks whose fp32 values are
+// never needed (finished T blocks go straight to the bf16 tile).
+// One word per warp task, one byte per field: A1, B1, A2, B2 (second product
+// or -1), C (subtracted, or -1), fp32 destination, bf16 tile block (or -1),
+// output sign.  Block codes: 16 * (0 = A scratch, 1 = T scratch) + 4 *
+// block_row + block_col.
+constexpr uint64_t solve_task(int a1, int b1, int a2, int b2, int c, int d, int blk, int sc) {
+  return (uint64_t)(uint8_t)a1 | (uint64_t)(uint8_t)b1 << 8 | (uint64_t)(uint8_t)a2 << 16 |
+         (uint64_t)(uint8_t)b2 << 24 | (uint64_t)(uint8_t)c << 32 | (uint64_t)(uint8_t)d << 40 |
+         (uint64_t)(uint8_t)blk << 48 | (uint64_t)(uint8_t)sc << 56;
+}
+__device__ __forceinline__ int task_field(uint64_t t, int k) {
+  return (int)(signed char)(uint8_t)(t >> (8 * k));
+}
+constexpr uint64_t kNoTask = solve_task(-1, -1, -1, -1, -1, -1, -1, 0);
+#define SA(i, j) ((i) * 4 + (j))
+#define ST(i, j) (16 + (i) * 4 + (j))
+__constant__ uint64_t kSolveTask[3][6] = {
+    {solve_task(SA(1, 0), ST(0, 0), -1, -1, -1, ST(0, 1), -1, 1),
+     solve_task(SA(2, 0), ST(0, 0), -1, -1, -1, ST(0, 2), -1, 1),
+     solve_task(SA(3, 0), ST(0, 0), -1, -1, -1, ST(0, 3), -1, 1),
+     solve_task(SA(2, 1), ST(1, 1), -1, -1, -1, ST(1, 2), -1, 1),
+     solve_task(SA(3, 1), ST(1, 1), -1, -1, -1, ST(1, 3), -1, 1),
+     solve_task(SA(3, 2), ST(2, 2), -1, -1, -1, ST(2, 3), -1, 1)},
+    {solve_task(ST(1, 1), ST(0, 1), -1, -1, -1, -1, SA(1, 0), -1),
+     solve_task(ST(2, 2), ST(1, 2), -1, -1, -1, -1, SA(2, 1), -1),
+     solve_task(ST(3, 3), ST(2, 3), -1, -1, -1, ST(3, 2), SA(3, 2), -1),
+     solve_task(ST(1, 2), ST(0, 1), -1, -1, ST(0, 2), ST(1, 0), -1, 1),
+     solve_task(ST(1, 3), ST(0, 1), -1, -1, ST(0, 3), ST(2, 0), -1, 1),
+     solve_task(ST(2, 3), ST(1, 2), -1, -1, ST(1, 3), ST(2, 1), -1, 1)},
+    {solve_task(ST(2, 2), ST(1, 0), -1, -1, -1, -1, SA(2, 0), 1),
+     solve_task(ST(3, 3), ST(2, 1), -1, -1, -1, -1, SA(3, 1), 1),
+     solve_task(ST(3, 3), ST(2, 0), ST(3, 2), ST(1, 0), -1, -1, SA(3, 0), 1), kNoTask, kNoTask,
+     kNoTask},
+};
+#undef SA
+#undef ST
 
 // s * acc as bf16 into the 16x16 block at (r0, c0) of a 128-byte-swizzled tile.
 __device__ __forceinline__ void store16x16_bf16(unsigned char* tile, int r0, int c0,
@@ -236,8 +296,8 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     mbar_init(&bars[B_EMPTY + 1], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_PRE_FULL + i], 1);
-      mbar_init(&bars[B_PRE_EMPTY + i], 4);
-      mbar_init(&bars[B_TP_READY + i], 4);
+      mbar_init(&bars[B_PRE_EMPTY + i], 8);
+      mbar_init(&bars[B_TP_READY + i], 8);
       mbar_init(&bars[B_TP_EMPTY + i], 4);
     }
     mbar_init(&bars[B_D1], 1);
@@ -268,175 +328,180 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(sm);
 
-  if (warp == 0) {
-    // ------------------------------ TMA producer ------------------------------
-    if (elect_one()) {
-      int issued = 0;
+  if (warp < 4) {
+    regs_decrease<kRegsRoles>();
+    if (warp == 0) {
+      // ------------------------------ TMA producer ------------------------------
+      if (elect_one()) {
+        int issued = 0;
+        bool ok = true;
+        for (int n = 0; n < N && ok; ++n) {
+          const int s = n % NSTAGE;
+          if (n >= NSTAGE) ok = wait_bar(bars, B_EMPTY + s, (uint32_t)((n / NSTAGE) - 1) & 1u);
+          if (!ok) break;
+          unsigned char* kq = sm + SM_KQ + s * 32768;
+          uint64_t* fb = &bars[B_FULL + s];
+          mbar_arrive_expect_tx(fb, 4 * 8192 + 8192);
+          const int t0 = n * C;
+          tma_load_4d(kq, &tmK, 0, h, t0, b, fb);
+          tma_load_4d(kq + 16384, &tmK, 64, h, t0, b, fb);
+          tma_load_4d(kq + 8192, &tmQ, 0, h, t0, b, fb);
+          tma_load_4d(kq + 16384 + 8192, &tmQ, 64, h, t0, b, fb);
+          tma_load_4d(sm + SM_V + s * 8192, &tmV, c0, h, t0, b, fb);
+          issued = n + 1;
+        }
+        // Let every issued load land before the CTA can exit (bounded).
+        for (int n = issued > NSTAGE ? issued - NSTAGE : 0; n < issued; ++n)
+          wait_bar(bars, B_FULL + n % NSTAGE, (uint32_t)(n / NSTAGE) & 1u);
+      }
+    } else if (warp == 1) {
+      // ------------------------------ chain MMA issuer ------------------------------
+      if (elect_one()) {
+        bool ok = true;
+        for (int n = 0; n < N && ok; ++n) {
+          const int s = n % NSTAGE, tb = n & 1;
+          const uint32_t kq = sbase + SM_KQ + s * 32768;
+          const uint32_t tp = sbase + SM_TP + tb * 16384;
+          ok = wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u) &&
+               wait_bar(bars, B_S_READY, (uint32_t)n & 1u);
+          if (!ok) break;
+          tc_fence_after();
+          // D1 = [K;Q] S   (K-dim = dk: 8 steps of 16)
+          const uint32_t d1 = tmem + TM_D1 + (uint32_t)tb * 64;
+  #pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
+            const uint64_t bd = umma_desc(sbase + SM_S + k * 2048, 16384, 1024, SW128);
+            mma_bf16(d1, a, bd, IDESC_KM, k > 0);
+          }
+          mma_commit(&bars[B_D1]);
+          // D2 = [T;P] X   (K-dim = tokens: 4 steps)
+          ok = wait_bar(bars, B_TP_READY + tb, (uint32_t)(n >> 1) & 1u) &&
+               wait_bar(bars, B_X_READY, (uint32_t)n & 1u);
+          if (!ok) break;
+          tc_fence_after();
+  #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t a = umma_desc(tp + k * 32, 16, 1024, SW128);
+            const uint64_t bd = umma_desc(sbase + SM_X + k * 2048, 8192, 1024, SW128);
+            mma_bf16(tmem + TM_D2, a, bd, IDESC_KM, k > 0);
+          }
+          mma_commit(&bars[B_D2]);
+          // D3 = K^T V''  (A MN-major: M = dk in two 64-wide blocks 16 KB apart)
+          ok = wait_bar(bars, B_VPP_READY, (uint32_t)n & 1u);
+          if (!ok) break;
+          tc_fence_after();
+  #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t a = umma_desc(kq + k * 2048, 16384, 1024, SW128);
+            const uint64_t bd = umma_desc(sbase + SM_VPP + k * 2048, 8192, 1024, SW128);
+            mma_bf16(tmem + TM_D3, a, bd, IDESC_MM, k > 0);
+          }
+          mma_commit(&bars[B_D3]);
+          mma_commit(&bars[B_EMPTY + s]);  // K, Q, V of this stage are no longer read
+          // D4 = [T;P] V'
+          if (n > 0) ok = wait_bar(bars, B_D4_EMPTY, (uint32_t)(n - 1) & 1u);
+          if (!ok) break;
+          tc_fence_after();
+  #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t a = umma_desc(tp + k * 32, 16, 1024, SW128);
+            const uint64_t bd = umma_desc(sbase + SM_VP + k * 2048, 8192, 1024, SW128);
+            mma_bf16(tmem + TM_D4, a, bd, IDESC_KM, k > 0);
+          }
+          mma_commit(&bars[B_D4]);
+        }
+        mma_commit(&bars[B_CHAIN_DONE]);
+        wait_bar(bars, B_CHAIN_DONE, 0);
+      }
+    } else if (warp == 2) {
+      // ------------------------------ prep MMA issuer ------------------------------
+      if (elect_one()) {
+        bool ok = true;
+        for (int n = 0; n < N && ok; ++n) {
+          const int s = n % NSTAGE, pb = n & 1;
+          ok = wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u);
+          if (ok && n >= 2) ok = wait_bar(bars, B_PRE_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t kq = sbase + SM_KQ + s * 32768;
+  #pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
+            mma_bf16(tmem + TM_PRE + (uint32_t)pb * 64, a, a, IDESC_KK, k > 0);
+          }
+          mma_commit(&bars[B_PRE_FULL + pb]);
+        }
+      }
+    } else if (warp == 3) {
+      // ------------------------------ gate warp ------------------------------
+      // Per chunk, as soon as its buffer is free (two chunks ahead of the chain):
+      // g and beta, the in-chunk cumulative gate G, e^G, e^{G_C - G}, e^{G_C}, and
+      // the separable factors e^{G_i - G_j} = F[i][j/16] * E[j] (j <= i).  Every
+      // factor exponent lies inside one 16-token block or runs from a block start
+      // to a later row; if any exceeds 40 (a factor could overflow, or hide a
+      // non-negligible product behind an underflowed partner) the chunk is flagged
+      // to form e^{G_i - G_j} directly.
+      const size_t gb = (size_t)b * T * H + h;
       bool ok = true;
       for (int n = 0; n < N && ok; ++n) {
-        const int s = n % NSTAGE;
-        if (n >= NSTAGE) ok = wait_bar(bars, B_EMPTY + s, (uint32_t)((n / NSTAGE) - 1) & 1u);
+        const int pb = n & 1;
+        VecBuf& vb = vecs[pb];
+        const int t = n * C + 2 * lane;
+        const float g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
+        const float g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
+        const float b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
+        const float b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
+        if (n >= 2) ok = wait_bar(bars, B_TP_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
         if (!ok) break;
-        unsigned char* kq = sm + SM_KQ + s * 32768;
-        uint64_t* fb = &bars[B_FULL + s];
-        mbar_arrive_expect_tx(fb, 4 * 8192 + 8192);
-        const int t0 = n * C;
-        tma_load_4d(kq, &tmK, 0, h, t0, b, fb);
-        tma_load_4d(kq + 16384, &tmK, 64, h, t0, b, fb);
-        tma_load_4d(kq + 8192, &tmQ, 0, h, t0, b, fb);
-        tma_load_4d(kq + 16384 + 8192, &tmQ, 64, h, t0, b, fb);
-        tma_load_4d(sm + SM_V + s * 8192, &tmV, c0, h, t0, b, fb);
-        issued = n + 1;
-      }
-      // Let every issued load land before the CTA can exit (bounded).
-      for (int n = issued > NSTAGE ? issued - NSTAGE : 0; n < issued; ++n)
-        wait_bar(bars, B_FULL + n % NSTAGE, (uint32_t)(n / NSTAGE) & 1u);
-    }
-  } else if (warp == 1) {
-    // ------------------------------ chain MMA issuer ------------------------------
-    if (elect_one()) {
-      bool ok = true;
-      for (int n = 0; n < N && ok; ++n) {
-        const int s = n % NSTAGE, tb = n & 1;
-        const uint32_t kq = sbase + SM_KQ + s * 32768;
-        const uint32_t tp = sbase + SM_TP + tb * 16384;
-        ok = wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u) &&
-             wait_bar(bars, B_S_READY, (uint32_t)n & 1u);
-        if (!ok) break;
-        tc_fence_after();
-        // D1 = [K;Q] S   (K-dim = dk: 8 steps of 16)
-        const uint32_t d1 = tmem + TM_D1 + (uint32_t)tb * 64;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
-          const uint64_t bd = umma_desc(sbase + SM_S + k * 2048, 16384, 1024, SW128);
-          mma_bf16(d1, a, bd, IDESC_KM, k > 0);
+        const float pair = g0 + g1;
+        float incl = pair;
+  #pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += y;
         }
-        mma_commit(&bars[B_D1]);
-        // D2 = [T;P] X   (K-dim = tokens: 4 steps)
-        ok = wait_bar(bars, B_TP_READY + tb, (uint32_t)(n >> 1) & 1u) &&
-             wait_bar(bars, B_X_READY, (uint32_t)n & 1u);
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t a = umma_desc(tp + k * 32, 16, 1024, SW128);
-          const uint64_t bd = umma_desc(sbase + SM_X + k * 2048, 8192, 1024, SW128);
-          mma_bf16(tmem + TM_D2, a, bd, IDESC_KM, k > 0);
-        }
-        mma_commit(&bars[B_D2]);
-        // D3 = K^T V''  (A MN-major: M = dk in two 64-wide blocks 16 KB apart)
-        ok = wait_bar(bars, B_VPP_READY, (uint32_t)n & 1u);
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t a = umma_desc(kq + k * 2048, 16384, 1024, SW128);
-          const uint64_t bd = umma_desc(sbase + SM_VPP + k * 2048, 8192, 1024, SW128);
-          mma_bf16(tmem + TM_D3, a, bd, IDESC_MM, k > 0);
-        }
-        mma_commit(&bars[B_D3]);
-        mma_commit(&bars[B_EMPTY + s]);  // K, Q, V of this stage are no longer read
-        // D4 = [T;P] V'
-        if (n > 0) ok = wait_bar(bars, B_D4_EMPTY, (uint32_t)(n - 1) & 1u);
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t a = umma_desc(tp + k * 32, 16, 1024, SW128);
-          const uint64_t bd = umma_desc(sbase + SM_VP + k * 2048, 8192, 1024, SW128);
-          mma_bf16(tmem + TM_D4, a, bd, IDESC_KM, k > 0);
-        }
-        mma_commit(&bars[B_D4]);
-      }
-      mma_commit(&bars[B_CHAIN_DONE]);
-      wait_bar(bars, B_CHAIN_DONE, 0);
-    }
-  } else if (warp == 2) {
-    // ------------------------------ prep MMA issuer ------------------------------
-    if (elect_one()) {
-      bool ok = true;
-      for (int n = 0; n < N && ok; ++n) {
-        const int s = n % NSTAGE, pb = n & 1;
-        ok = wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u);
-        if (ok && n >= 2) ok = wait_bar(bars, B_PRE_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t kq = sbase + SM_KQ + s * 32768;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
-          mma_bf16(tmem + TM_PRE + (uint32_t)pb * 64, a, a, IDESC_KK, k > 0);
-        }
-        mma_commit(&bars[B_PRE_FULL + pb]);
-      }
-    }
-  } else if (warp == 3) {
-    // ------------------------------ gate warp ------------------------------
-    // Per chunk, as soon as its buffer is free (two chunks ahead of the chain):
-    // g and beta, the in-chunk cumulative gate G, e^G, e^{G_C - G}, e^{G_C}, and
-    // the separable factors e^{G_i - G_j} = F[i][j/16] * E[j] (j <= i).  Every
-    // factor exponent lies inside one 16-token block or runs from a block start
-    // to a later row; if any exceeds 40 (a factor could overflow, or hide a
-    // non-negligible product behind an underflowed partner) the chunk is flagged
-    // to form e^{G_i - G_j} directly.
-    const size_t gb = (size_t)b * T * H + h;
-    bool ok = true;
-    for (int n = 0; n < N && ok; ++n) {
-      const int pb = n & 1;
-      VecBuf& vb = vecs[pb];
-      const int t = n * C + 2 * lane;
-      const float g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
-      const float g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
-      const float b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
-      const float b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
-      if (n >= 2) ok = wait_bar(bars, B_TP_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
-      if (!ok) break;
-      const float pair = g0 + g1;
-      float incl = pair;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
-      }
-      const float G0 = incl - pair + g0, G1 = incl;
-      const float GC = __shfl_sync(0xffffffffu, incl, 31);
-      vb.G[2 * lane] = G0;
-      vb.G[2 * lane + 1] = G1;
-      vb.beta[2 * lane] = b0;
-      vb.beta[2 * lane + 1] = b1;
-      vb.eG[2 * lane] = gate_exp(G0);
-      vb.eG[2 * lane + 1] = gate_exp(G1);
-      vb.dec[2 * lane] = gate_exp(GC - G0);
-      vb.dec[2 * lane + 1] = gate_exp(GC - G1);
-      if (lane == 0) vb.eGC = gate_exp(GC);
-      __syncwarp();
-      float big = 0.f;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        const int i = lane + 32 * half;
-        const float Gi = vb.G[i];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float x = (16 * k <= i) ? Gi - vb.G[16 * k] : 0.f;
-          vb.F[i][k] = gate_exp(x);
+        const float G0 = incl - pair + g0, G1 = incl;
+        const float GC = __shfl_sync(0xffffffffu, incl, 31);
+        vb.G[2 * lane] = G0;
+        vb.G[2 * lane + 1] = G1;
+        vb.beta[2 * lane] = b0;
+        vb.beta[2 * lane + 1] = b1;
+        vb.eG[2 * lane] = gate_exp(G0);
+        vb.eG[2 * lane + 1] = gate_exp(G1);
+        vb.dec[2 * lane] = gate_exp(GC - G0);
+        vb.dec[2 * lane + 1] = gate_exp(GC - G1);
+        if (lane == 0) vb.eGC = gate_exp(GC);
+        __syncwarp();
+        float big = 0.f;
+  #pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          const int i = lane + 32 * half;
+          const float Gi = vb.G[i];
+  #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float x = (16 * k <= i) ? Gi - vb.G[16 * k] : 0.f;
+            vb.F[i][k] = gate_exp(x);
+            big = fmaxf(big, x);
+          }
+          const float x = vb.G[i & ~15] - Gi;
+          vb.E[i] = gate_exp(x);
           big = fmaxf(big, x);
         }
-        const float x = vb.G[i & ~15] - Gi;
-        vb.E[i] = gate_exp(x);
-        big = fmaxf(big, x);
+        const int direct = __any_sync(0xffffffffu, big > 40.f) ? 1 : 0;
+        if (lane == 0) vb.direct = direct;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[B_VEC_FULL + pb]);
       }
-      const int direct = __any_sync(0xffffffffu, big > 40.f) ? 1 : 0;
-      if (lane == 0) vb.direct = direct;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_VEC_FULL + pb]);
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ------------------------------ prep warpgroup ------------------------------
-    const int p = tid - 128;          // TMEM lane / row
-    const int wq = warp - 4;          // lane quarter
+  } else if (warp < 12) {
+    // ------------------------------ prep (eight warps) ------------------------------
+    const int pi = tid - 128;           // 0..255
+    const int wq = warp & 3;            // TMEM lane quarter
+    const int ch = (warp - 4) >> 2;     // which 32 of the 64 D_pre columns
+    const int p = wq * 32 + lane;       // TMEM lane = row of D_pre
     // The strictly upper 16x16 blocks of T are never written below: zero them once.
-    for (int e = p; e < 2 * 64 * 8; e += 128) {
+    for (int e = pi; e < 2 * 64 * 8; e += 256) {
       const int buf = e / 512, row = (e / 8) % 64, c8 = e % 8;
       if (c8 >= 2 * (row / 16 + 1))
         *reinterpret_cast<uint4*>(sm + SM_TP + buf * 16384 + sw128(row, c8)) =
@@ -444,7 +509,10 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     }
     float* AF = reinterpret_cast<float*>(sm + SM_AF);
     float* TF = reinterpret_cast<float*>(sm + SM_TF);
-    float* Y = reinterpret_cast<float*>(sm + SM_Y);
+    const int w8 = warp - 4;
+    const uint64_t task0 = w8 < 6 ? kSolveTask[0][w8] : kNoTask;
+    const uint64_t task1 = w8 < 6 ? kSolveTask[1][w8] : kNoTask;
+    const uint64_t task2 = w8 < 6 ? kSolveTask[2][w8] : kNoTask;
     bool ok = true;
     for (int n = 0; n < N && ok; ++n) {
       const int pb = n & 1;
@@ -455,35 +523,43 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       ok = wait_bar(bars, B_VEC_FULL + pb, (uint32_t)(n >> 1) & 1u);
       if (!ok) break;
       const bool direct = vb.direct != 0;
-      // A (rows 0-63) and P (rows 64-127) from D_pre
+      // A (rows 0-63) and P (rows 64-127) from D_pre; this warp: 32 columns.
+      // The gate factors are read while the product is still in flight;
+      // direct exponents (steep gates only) use factor 1 here and are applied
+      // by a rolled pass below.
+      const int i = p & 63;
+      const int jmax = p < 64 ? i - 1 : i;  // A is strictly lower, P includes the diagonal
+      const float rs = p < 64 ? vb.beta[i] : 1.f;
+      float fac[32];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const float fq = direct ? 1.f : rs * vb.F[i][2 * ch + h2];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int j = (2 * ch + h2) * 16 + e;
+          fac[16 * h2 + e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) : 0.f;
+        }
+      }
       ok = wait_bar(bars, B_PRE_FULL + pb, (uint32_t)(n >> 1) & 1u);
       if (!ok) break;
       tc_fence_after();
       {
-        const int i = p & 63;
-        const float Gi = vb.G[i], bi = vb.beta[i];
-        const uint32_t ta = tmem + TM_PRE + (uint32_t)pb * 64 + ((uint32_t)(wq * 32) << 16);
-        const int jmax = p < 64 ? i - 1 : i;  // A is strictly lower, P includes the diagonal
-        const float rs = p < 64 ? bi : 1.f;
-        float vrow[64];
-        tmem_ld64(ta, vrow);
+        const uint32_t ta =
+            tmem + TM_PRE + (uint32_t)pb * 64 + (uint32_t)ch * 32 + ((uint32_t)(wq * 32) << 16);
+        float vrow[32];
+        tmem_ld32(ta, vrow);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const float* v = vrow + 16 * q4;
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int q4 = 2 * ch + h2;
           float out[16];
-          // direct exponents (steep gates only) use factor 1 here and are
-          // applied by a rolled pass below
-          const float fq = direct ? 1.f : rs * vb.F[i][q4];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int j = q4 * 16 + e;
-            out[e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) * v[e] : 0.f;
-          }
+          for (int e = 0; e < 16; ++e) out[e] = fac[16 * h2 + e] * vrow[16 * h2 + e];
           if (p < 64) {
 #pragma unroll
             for (int e = 0; e < 16; e += 4)
               *reinterpret_cast<float4*>(AF + i * LDF + q4 * 16 + e) =
-                  make_float4(out[e], out[e + 1], out[e + 2], out[e + 3]);
+                  make_float4(rtf32(out[e]), rtf32(out[e + 1]), rtf32(out[e + 2]),
+                              rtf32(out[e + 3]));
           } else {
             *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4)) = pack_bf16x8(out);
             *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4 + 1)) = pack_bf16x8(out + 8);
@@ -492,15 +568,16 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       }
       if (direct) {
         // steep gates: scale the stored row by rs * e^{G_i - G_j} element by element
-        const int i = p & 63;
-        const float Gi = vb.G[i], rs = p < 64 ? vb.beta[i] : 1.f;
+        const float Gi = vb.G[i];
+        const int jend = min(i, ch * 32 + 31);
 #pragma unroll 1
-        for (int j = 0; j <= i; ++j) {
+        for (int j = ch * 32; j <= jend; ++j) {
           const float f = rs * gate_exp(Gi - vb.G[j]);
           if (p < 64) {
-            AF[i * LDF + j] *= f;
+            AF[i * LDF + j] = rtf32(AF[i * LDF + j] * f);
           } else {
-            __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(tpt + sw128(p, j >> 3) + (j & 7) * 2);
+            __nv_bfloat16* e =
+                reinterpret_cast<__nv_bfloat16*>(tpt + sw128(p, j >> 3) + (j & 7) * 2);
             *e = __float2bfloat16_rn(__bfloat162float(*e) * f);
           }
         }
@@ -508,92 +585,74 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_PRE_EMPTY + pb]);
-      named_sync(1, 128);
-      // ---- T = (I + A)^{-1}: 16x16 diagonal blocks by substitution ----
-      if (p < 64) {
-        const int blk = p >> 4, c = p & 15;
+      named_sync(1, 256);
+      // ---- T = (I + A)^{-1}: 16x16 diagonal blocks by column-oriented substitution
+      //      (one thread per column; the dependent chain is 15 FMAs long; A is
+      //      read four columns at a time) ----
+      if (pi < 64) {
+        const int blk = pi >> 4, c = pi & 15;
         const float* Ab = AF + (blk * 16) * LDF + blk * 16;
         float t[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          float acc = 0.f;
+        for (int r = 0; r < 16; ++r) t[r] = (r == c) ? 1.f : 0.f;
 #pragma unroll
-          for (int j = 0; j < r; ++j) acc = fmaf(Ab[r * LDF + j], t[j], acc);
-          t[r] = (r < c) ? 0.f : ((r == c) ? 1.f : -acc);
+        for (int j0 = 0; j0 < 16; j0 += 4) {
+          float a4[16][4];
+#pragma unroll
+          for (int r = j0 + 1; r < 16; ++r) {
+            const float4 x = *reinterpret_cast<const float4*>(Ab + r * LDF + j0);
+            a4[r][0] = x.x; a4[r][1] = x.y; a4[r][2] = x.z; a4[r][3] = x.w;
+          }
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+#pragma unroll
+            for (int r = j0 + jj + 1; r < 16; ++r) t[r] = fmaf(-a4[r][jj], t[j0 + jj], t[r]);
+          }
         }
         float* Tb = TF + (blk * 16) * LDF + blk * 16;
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-          Tb[r * LDF + c] = t[r];
+          Tb[r * LDF + c] = rtf32(t[r]);
           const int row = blk * 16 + r, col = blk * 16 + c;
           *reinterpret_cast<__nv_bfloat16*>(tpt + sw128(row, col >> 3) + (col & 7) * 2) =
               __float2bfloat16_rn(t[r]);
         }
       }
-      named_sync(1, 128);
-      // ---- off-diagonal 16x16 blocks T_ij (i > j).  With Z = A_{2:4,0:2} T_{0:2,0:2}
-      //      (blocks Z00 Z01 / Z10 Z11) and scratch blocks W0, W1, four phases of
-      //      one warp task each -- acc = [C] + A1 B1 [+ A2 B2] -- on tf32 warp MMAs:
-      //   phase 0: W0 = A10 T00 | W1 = A32 T22 | Z01 = A21 T11 | Z11 = A31 T11
-      //   phase 1: T10 = -T11 W0 | T32 = -T33 W1 | Z00 = A20 T00 | Z10 = A30 T00
-      //   phase 2: Z00 += A21 T10 | Z10 += A31 T10 | - | -
-      //   phase 3: T20 = -T22 Z00 | T21 = -T22 Z01 | T30 = -(T32 Z00 + T33 Z10)
-      //            | T31 = -(T32 Z01 + T33 Z11)
-      //   Finished T blocks go to TF (when needed later) and to the bf16 tile.
-      //   The phases run as one rolled loop so the product code exists once. ----
+      named_sync(1, 256);
+      // ---- off-diagonal 16x16 blocks in three phases of independent warp tasks
+      //      (tf32 warp MMAs); the schedule is the table above the kernel ----
       {
         const int gq = lane >> 2, tq = lane & 3;
-        auto Z = [&](int k) { return Y + k * 16 * LDY; };  // Z00 Z01 Z10 Z11 W0 W1
-        auto Ab = [&](int i, int j) { return AF + (i * 16) * LDF + j * 16; };
-        auto Tb = [&](int i, int j) { return TF + (i * 16) * LDF + j * 16; };
+        auto blk = [&](int code) {
+          return (code >= 16 ? TF : AF) + ((code >> 2) & 3) * 16 * LDF + (code & 3) * 16;
+        };
 #pragma unroll 1
-        for (int ph = 0; ph < 4; ++ph) {
-          const float *A1 = nullptr, *B1 = nullptr, *A2 = nullptr, *B2 = nullptr;
-          const float* Cin = nullptr;
-          float* D = nullptr;
-          int ldb1 = LDF, ldb2 = LDF, ldd = LDY, br = -1, bc = 0;
-          float sc = 1.f;
-          if (ph == 0) {
-            if (wq == 0) { A1 = Ab(1, 0); B1 = Tb(0, 0); D = Z(4); }
-            else if (wq == 1) { A1 = Ab(3, 2); B1 = Tb(2, 2); D = Z(5); }
-            else if (wq == 2) { A1 = Ab(2, 1); B1 = Tb(1, 1); D = Z(1); }
-            else { A1 = Ab(3, 1); B1 = Tb(1, 1); D = Z(3); }
-          } else if (ph == 1) {
-            if (wq < 2) {
-              const int i = 2 * wq + 1, j = 2 * wq;
-              A1 = Tb(i, i); B1 = Z(4 + wq); ldb1 = LDY; D = Tb(i, j); ldd = LDF;
-              br = i * 16; bc = j * 16; sc = -1.f;
-            } else if (wq == 2) { A1 = Ab(2, 0); B1 = Tb(0, 0); D = Z(0); }
-            else { A1 = Ab(3, 0); B1 = Tb(0, 0); D = Z(2); }
-          } else if (ph == 2) {
-            if (wq < 2) { Cin = Z(2 * wq); A1 = Ab(2 + wq, 1); B1 = Tb(1, 0); D = Z(2 * wq); }
-          } else {
-            const int j = wq & 1;
-            A1 = Tb(wq < 2 ? 2 : 3, 2); B1 = Z(j); ldb1 = LDY;
-            if (wq >= 2) { A2 = Tb(3, 3); B2 = Z(2 + j); ldb2 = LDY; }
-            br = (wq < 2 ? 2 : 3) * 16; bc = j * 16; sc = -1.f;
-          }
-          if (A1) {
+        for (int ph = 0; ph < 3; ++ph) {
+          const uint64_t tk = ph == 0 ? task0 : (ph == 1 ? task1 : task2);
+          if (task_field(tk, 0) >= 0) {
             float acc[2][4] = {};
-            if (Cin) load16x16(acc, Cin, LDY, gq, tq);
+            if (task_field(tk, 4) >= 0) load16x16(acc, blk(task_field(tk, 4)), LDF, -1.f, gq, tq);
 #pragma unroll 1
-            for (int pi = 0; pi < (A2 ? 2 : 1); ++pi)
-              mma16x16(acc, pi ? A2 : A1, LDF, pi ? B2 : B1, pi ? ldb2 : ldb1, gq, tq);
-            if (D) store16x16(D, ldd, acc, sc, gq, tq);
-            if (br >= 0) store16x16_bf16(tpt, br, bc, acc, sc, gq, tq);
+            for (int pi2 = 0; pi2 < (task_field(tk, 2) >= 0 ? 2 : 1); ++pi2)
+              mma16x16(acc, blk(task_field(tk, 2 * pi2)), LDF, blk(task_field(tk, 2 * pi2 + 1)),
+                       LDF, gq, tq);
+            const float sc = (float)task_field(tk, 7);
+            if (task_field(tk, 5) >= 0) store16x16(blk(task_field(tk, 5)), LDF, acc, sc, gq, tq);
+            const int bt = task_field(tk, 6);
+            if (bt >= 0) store16x16_bf16(tpt, (bt >> 2) * 16, (bt & 3) * 16, acc, sc, gq, tq);
           }
-          if (ph == 0) __syncwarp();
-          else named_sync(1, 128);
+          if (ph < 2) named_sync(1, 256);
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_TP_READY + pb]);
     }
-  } else if (warp >= 8) {
+  } else {
     // ------------------------------ chain warpgroup ------------------------------
-    const int r = tid - 256;          // TMEM lane / row
-    const int wq = warp - 8;
+    regs_increase<kRegsChain>();
+    const int r = tid - 384;          // TMEM lane / row
+    const int wq = warp - 12;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     unsigned char* Stile = sm + SM_S;
     float S[DVT];
@@ -622,7 +681,6 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         // ---- epilogue 1: X = beta (V - e^G K S) ----
         const int i = r;
         ok = wait_bar(bars, B_D1, (uint32_t)n & 1u) &&
-             wait_bar(bars, B_TP_READY + tb, (uint32_t)(n >> 1) & 1u) &&
              wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u) &&
              wait_bar(bars, B_VEC_FULL + tb, (uint32_t)(n >> 1) & 1u);
         if (!ok) break;
@@ -781,8 +839,14 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   if (!make_map(&mk, a.k, a.B, a.T, a.H, a.dk) || !make_map(&mq, a.q, a.B, a.T, a.H, a.dk) ||
       !make_map(&mv, a.v, a.B, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES);
+  // The in-kernel register split assumes exactly kLaunchRegs per thread at
+  // launch; with fewer, the chain warpgroup's increase could never be granted.
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, chunk_tc_kernel);
+  if (e != cudaSuccess) return e;
+  if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;
+  e = cudaFuncSetAttribute(chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           SMEM_BYTES);
   if (e != cudaSuccess) return e;
   dim3 grid(a.dv / DVT, a.B * a.H);
   chunk_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(
