@@ -33,6 +33,7 @@
 // accumulator belongs to thread r of a warpgroup.  All hand-offs are
 // mbarriers; every wait is bounded.
 #include <cuda.h>
+#include <cstdlib>
 #include <cudaTypedefs.h>
 
 #include "gdn_common.cuh"
@@ -63,10 +64,11 @@ constexpr int SM_S = SM_V + NSTAGE * 8192;      // [128 rows (dk)][128 B]
 constexpr int SM_X = SM_S + 16384;              // [64 rows (token)][128 B]
 constexpr int SM_VPP = SM_X + 8192;             // V'' = e^{G_C-G} V'
 constexpr int SM_VP = SM_VPP + 8192;            // V'
-constexpr int SM_TP = SM_VP + 8192;             // 2 x [128 rows][128 B]: rows 0-63 T, 64-127 P
-constexpr int SM_AF = SM_TP + 2 * 16384;        // fp32 A [64][LDF]
+constexpr int NTP = 3;                          // depth of the T/P tile and gate-vector rings
+constexpr int SM_TP = SM_VP + 8192;             // NTP x [128 rows][128 B]: rows 0-63 T, 64-127 P
+constexpr int SM_AF = SM_TP + NTP * 16384;      // fp32 A [64][LDF]
 constexpr int SM_TF = SM_AF + 64 * LDF * 4;     // fp32 T [64][LDF]
-constexpr int SM_VEC = SM_TF + 64 * LDF * 4;    // 2 x VecBuf
+constexpr int SM_VEC = SM_TF + 64 * LDF * 4;    // NTP x VecBuf
 struct VecBuf {
   float G[C], eG[C], dec[C], beta[C];
   float F[C][4];  // e^{G_i - G_{16k}} for k <= i / 16 (gate factors, row part)
@@ -75,8 +77,8 @@ struct VecBuf {
   int direct;     // 1: a factor exponent exceeds 40; form e^{G_i - G_j} directly
   float pad[2];
 };
-constexpr int SM_BAR = SM_VEC + 2 * (int)sizeof(VecBuf);
-constexpr int NBAR = 24;
+constexpr int SM_BAR = SM_VEC + NTP * (int)sizeof(VecBuf);
+constexpr int NBAR = 32;
 constexpr int SM_TMEM = SM_BAR + NBAR * 8;
 constexpr int SM_TOTAL = SM_TMEM + 16;
 constexpr int SMEM_BYTES = SM_TOTAL + 1024;  // + alignment slack
@@ -88,11 +90,12 @@ enum {
   B_EMPTY = 2,       // [NSTAGE] stage consumed by the MMAs
   B_PRE_FULL = 4,    // [2] D_pre ready
   B_PRE_EMPTY = 6,   // [2] D_pre read by prep
-  B_TP_READY = 8,    // [2] TP tile + vectors of a chunk ready
-  B_TP_EMPTY = 10,   // [2] chain done with a chunk's TP / vectors
-  B_D1 = 12, B_D2 = 13, B_D3 = 14, B_D4 = 15, B_D4_EMPTY = 16,
-  B_X_READY = 17, B_VPP_READY = 18, B_S_READY = 19, B_CHAIN_DONE = 20,
-  B_VEC_FULL = 21,   // [2] gate vectors of a chunk ready
+  B_TP_READY = 8,    // [NTP] T/P tile of a chunk in this CTA's ring (made here or copied in)
+  B_TP_EMPTY = 11,   // [NTP] every chain of the pair is done with a chunk's tile
+  B_VEC_FULL = 14,   // [NTP] gate vectors of a chunk ready
+  B_VEC_EMPTY = 17,  // [NTP] this CTA's chain is done with a chunk's gate vectors
+  B_D1 = 20, B_D2 = 21, B_D3 = 22, B_D4 = 23, B_D4_EMPTY = 24,
+  B_X_READY = 25, B_VPP_READY = 26, B_S_READY = 27, B_CHAIN_DONE = 28,
 };
 
 // TMEM columns
@@ -268,6 +271,18 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bars, int idx, uint32_t parit
   return mbar_wait(&bars[idx], parity);
 }
 
+// Waits on barriers that the other CTA of a pair also arrives on.
+template <bool kPair>
+__device__ __forceinline__ bool wait_shared_bar(uint64_t* bars, int idx, uint32_t parity) {
+  return kPair ? mbar_wait_cluster(&bars[idx], parity) : mbar_wait(&bars[idx], parity);
+}
+
+// kPair: the grid is launched in clusters of two CTAs, the two 64-column
+// tiles of one (b, h).  Each prepares the T/P tile of every other chunk (rank
+// r: chunks n with n % 2 == r) and copies it into the other CTA's ring, so
+// the state-independent preparation is done once per (b, h) rather than once
+// per column tile.
+template <bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
@@ -288,6 +303,16 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   const int b = bh / H, h = bh - b * H;
   const int c0 = blockIdx.x * DVT;
   const int N = (T + C - 1) / C;
+  // chunks whose T/P tile this CTA prepares: n = rank, rank + step, ...
+  const int rank = kPair ? (int)cluster_ctarank() : 0;
+  // TMEM read widths of the A/P pass and the chain epilogues.  Paired tiles
+  // run one launch per (b, h) pair at low occupancy, where the chain's latency
+  // decides: wide, unrolled reads.  Unpaired tiles run at high occupancy, where
+  // the instruction fetch of all warps of an SM decides: narrow, rolled reads.
+  constexpr int kWP = kPair ? 32 : 16;
+  constexpr int kWC = kPair ? 64 : 16;
+  const int step = kPair ? 2 : 1;
+  const uint32_t peer = (uint32_t)(rank ^ 1);
 
   if (tid == 0) {
     mbar_init(&bars[B_FULL + 0], 1);
@@ -297,8 +322,12 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_PRE_FULL + i], 1);
       mbar_init(&bars[B_PRE_EMPTY + i], 8);
-      mbar_init(&bars[B_TP_READY + i], 8);
-      mbar_init(&bars[B_TP_EMPTY + i], 4);
+    }
+    for (int i = 0; i < NTP; ++i) {
+      mbar_init(&bars[B_TP_READY + i], 1);
+      mbar_init(&bars[B_TP_EMPTY + i], kPair ? 8 : 4);
+      mbar_init(&bars[B_VEC_FULL + i], 1);
+      mbar_init(&bars[B_VEC_EMPTY + i], 4);
     }
     mbar_init(&bars[B_D1], 1);
     mbar_init(&bars[B_D2], 1);
@@ -309,8 +338,6 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     mbar_init(&bars[B_VPP_READY], 2);
     mbar_init(&bars[B_S_READY], 4);
     mbar_init(&bars[B_CHAIN_DONE], 1);
-    mbar_init(&bars[B_VEC_FULL + 0], 1);
-    mbar_init(&bars[B_VEC_FULL + 1], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -324,6 +351,8 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
+  // the other CTA's barriers are initialised before anything is sent to them
+  if (kPair) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(sm);
@@ -359,16 +388,16 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       if (elect_one()) {
         bool ok = true;
         for (int n = 0; n < N && ok; ++n) {
-          const int s = n % NSTAGE, tb = n & 1;
+          const int s = n % NSTAGE, tb = n & 1, rb = n % NTP;
           const uint32_t kq = sbase + SM_KQ + s * 32768;
-          const uint32_t tp = sbase + SM_TP + tb * 16384;
+          const uint32_t tp = sbase + SM_TP + rb * 16384;
           ok = wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u) &&
                wait_bar(bars, B_S_READY, (uint32_t)n & 1u);
           if (!ok) break;
           tc_fence_after();
           // D1 = [K;Q] S   (K-dim = dk: 8 steps of 16)
           const uint32_t d1 = tmem + TM_D1 + (uint32_t)tb * 64;
-  #pragma unroll
+  #pragma unroll (kPair ? 8 : 1)
           for (int k = 0; k < 8; ++k) {
             const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
             const uint64_t bd = umma_desc(sbase + SM_S + k * 2048, 16384, 1024, SW128);
@@ -376,11 +405,11 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           }
           mma_commit(&bars[B_D1]);
           // D2 = [T;P] X   (K-dim = tokens: 4 steps)
-          ok = wait_bar(bars, B_TP_READY + tb, (uint32_t)(n >> 1) & 1u) &&
+          ok = wait_shared_bar<kPair>(bars, B_TP_READY + rb, (uint32_t)(n / NTP) & 1u) &&
                wait_bar(bars, B_X_READY, (uint32_t)n & 1u);
           if (!ok) break;
           tc_fence_after();
-  #pragma unroll
+  #pragma unroll (kPair ? 4 : 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t a = umma_desc(tp + k * 32, 16, 1024, SW128);
             const uint64_t bd = umma_desc(sbase + SM_X + k * 2048, 8192, 1024, SW128);
@@ -391,7 +420,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           ok = wait_bar(bars, B_VPP_READY, (uint32_t)n & 1u);
           if (!ok) break;
           tc_fence_after();
-  #pragma unroll
+  #pragma unroll (kPair ? 4 : 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t a = umma_desc(kq + k * 2048, 16384, 1024, SW128);
             const uint64_t bd = umma_desc(sbase + SM_VPP + k * 2048, 8192, 1024, SW128);
@@ -403,7 +432,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           if (n > 0) ok = wait_bar(bars, B_D4_EMPTY, (uint32_t)(n - 1) & 1u);
           if (!ok) break;
           tc_fence_after();
-  #pragma unroll
+  #pragma unroll (kPair ? 4 : 1)
           for (int k = 0; k < 4; ++k) {
             const uint64_t a = umma_desc(tp + k * 32, 16, 1024, SW128);
             const uint64_t bd = umma_desc(sbase + SM_VP + k * 2048, 8192, 1024, SW128);
@@ -418,14 +447,14 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       // ------------------------------ prep MMA issuer ------------------------------
       if (elect_one()) {
         bool ok = true;
-        for (int n = 0; n < N && ok; ++n) {
-          const int s = n % NSTAGE, pb = n & 1;
+        for (int n = rank, j = 0; n < N && ok; n += step, ++j) {
+          const int s = n % NSTAGE, pb = j & 1;
           ok = wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u);
-          if (ok && n >= 2) ok = wait_bar(bars, B_PRE_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
+          if (ok && j >= 2) ok = wait_bar(bars, B_PRE_EMPTY + pb, (uint32_t)((j - 2) >> 1) & 1u);
           if (!ok) break;
           tc_fence_after();
           const uint32_t kq = sbase + SM_KQ + s * 32768;
-  #pragma unroll
+  #pragma unroll (kPair ? 8 : 1)
           for (int k = 0; k < 8; ++k) {
             const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
             mma_bf16(tmem + TM_PRE + (uint32_t)pb * 64, a, a, IDESC_KK, k > 0);
@@ -435,7 +464,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       }
     } else if (warp == 3) {
       // ------------------------------ gate warp ------------------------------
-      // Per chunk, as soon as its buffer is free (two chunks ahead of the chain):
+      // Per chunk, as soon as its buffer is free (NTP - 1 chunks ahead of the chain):
       // g and beta, the in-chunk cumulative gate G, e^G, e^{G_C - G}, e^{G_C}, and
       // the separable factors e^{G_i - G_j} = F[i][j/16] * E[j] (j <= i).  Every
       // factor exponent lies inside one 16-token block or runs from a block start
@@ -445,14 +474,14 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       const size_t gb = (size_t)b * T * H + h;
       bool ok = true;
       for (int n = 0; n < N && ok; ++n) {
-        const int pb = n & 1;
-        VecBuf& vb = vecs[pb];
+        const int rb = n % NTP;
+        VecBuf& vb = vecs[rb];
         const int t = n * C + 2 * lane;
         const float g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
         const float g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
         const float b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
         const float b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
-        if (n >= 2) ok = wait_bar(bars, B_TP_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
+        if (n >= NTP) ok = wait_bar(bars, B_VEC_EMPTY + rb, (uint32_t)((n / NTP) - 1) & 1u);
         if (!ok) break;
         const float pair = g0 + g1;
         float incl = pair;
@@ -474,8 +503,9 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         if (lane == 0) vb.eGC = gate_exp(GC);
         __syncwarp();
         float big = 0.f;
+        // (the gate factors only serve chunks this CTA prepares)
   #pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
+        for (int half = 0; half < ((n - rank) % step == 0 ? 2 : 0); ++half) {
           const int i = lane + 32 * half;
           const float Gi = vb.G[i];
   #pragma unroll
@@ -491,7 +521,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         const int direct = __any_sync(0xffffffffu, big > 40.f) ? 1 : 0;
         if (lane == 0) vb.direct = direct;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[B_VEC_FULL + pb]);
+        if (lane == 0) mbar_arrive(&bars[B_VEC_FULL + rb]);
       }
     }
   } else if (warp < 12) {
@@ -501,7 +531,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     const int ch = (warp - 4) >> 2;     // which 32 of the 64 D_pre columns
     const int p = wq * 32 + lane;       // TMEM lane = row of D_pre
     // The strictly upper 16x16 blocks of T are never written below: zero them once.
-    for (int e = pi; e < 2 * 64 * 8; e += 256) {
+    for (int e = pi; e < NTP * 64 * 8; e += 256) {
       const int buf = e / 512, row = (e / 8) % 64, c8 = e % 8;
       if (c8 >= 2 * (row / 16 + 1))
         *reinterpret_cast<uint4*>(sm + SM_TP + buf * 16384 + sw128(row, c8)) =
@@ -514,55 +544,74 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     const uint64_t task1 = w8 < 6 ? kSolveTask[1][w8] : kNoTask;
     const uint64_t task2 = w8 < 6 ? kSolveTask[2][w8] : kNoTask;
     bool ok = true;
-    for (int n = 0; n < N && ok; ++n) {
-      const int pb = n & 1;
-      VecBuf& vb = vecs[pb];
-      unsigned char* tpt = sm + SM_TP + pb * 16384;
-      if (n >= 2) ok = wait_bar(bars, B_TP_EMPTY + pb, (uint32_t)((n - 2) >> 1) & 1u);
+    int last = -1;  // last chunk whose tile was published
+    for (int n = rank, oc = 0; n < N && ok; n += step, ++oc) {
+      const int pb = oc & 1, rb = n % NTP;  // D_pre buffer, ring slot
+      VecBuf& vb = vecs[rb];
+      unsigned char* tpt = sm + SM_TP + rb * 16384;
+      // ring slot free in every chain of the pair (chunk n - NTP released)
+      if (n >= NTP)
+        ok = wait_shared_bar<kPair>(bars, B_TP_EMPTY + rb, (uint32_t)((n / NTP) - 1) & 1u);
       if (!ok) break;
-      ok = wait_bar(bars, B_VEC_FULL + pb, (uint32_t)(n >> 1) & 1u);
+      ok = wait_bar(bars, B_VEC_FULL + rb, (uint32_t)(n / NTP) & 1u);
       if (!ok) break;
       const bool direct = vb.direct != 0;
-      // A (rows 0-63) and P (rows 64-127) from D_pre; this warp: 32 columns.
-      // The gate factors are read while the product is still in flight;
-      // direct exponents (steep gates only) use factor 1 here and are applied
-      // by a rolled pass below.
+      // A (rows 0-63) and P (rows 64-127) from D_pre; this warp: 32 columns, in
+      // steps of kW columns.  Direct exponents (steep gates only) use factor 1
+      // here and are applied by a rolled pass below.
       const int i = p & 63;
       const int jmax = p < 64 ? i - 1 : i;  // A is strictly lower, P includes the diagonal
       const float rs = p < 64 ? vb.beta[i] : 1.f;
-      float fac[32];
+      // (paired form: the factors of the whole 32-column half are formed while
+      // the product may still be in flight)
+      float fac[kPair ? 32 : 1];
+      if constexpr (kPair) {
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const float fq = direct ? 1.f : rs * vb.F[i][2 * ch + h2];
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const float fq = direct ? 1.f : rs * vb.F[i][2 * ch + h2];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int j = (2 * ch + h2) * 16 + e;
-          fac[16 * h2 + e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) : 0.f;
+          for (int e = 0; e < 16; ++e) {
+            const int j = (2 * ch + h2) * 16 + e;
+            fac[16 * h2 + e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) : 0.f;
+          }
         }
       }
-      ok = wait_bar(bars, B_PRE_FULL + pb, (uint32_t)(n >> 1) & 1u);
+      ok = wait_bar(bars, B_PRE_FULL + pb, (uint32_t)(oc >> 1) & 1u);
       if (!ok) break;
       tc_fence_after();
       {
         const uint32_t ta =
             tmem + TM_PRE + (uint32_t)pb * 64 + (uint32_t)ch * 32 + ((uint32_t)(wq * 32) << 16);
-        float vrow[32];
-        tmem_ld32(ta, vrow);
+#pragma unroll 1
+        for (int cw = 0; cw < 32; cw += kWP) {
+          float vrow[kWP];
+          tmem_ldw<kWP>(ta + cw, vrow);
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int q4 = 2 * ch + h2;
-          float out[16];
+          for (int h2 = 0; h2 < kWP / 16; ++h2) {
+            const int q4 = 2 * ch + cw / 16 + h2;
+            const float* v = vrow + 16 * h2;
+            float out[16];
+            if constexpr (kPair) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) out[e] = fac[16 * h2 + e] * vrow[16 * h2 + e];
-          if (p < 64) {
+              for (int e = 0; e < 16; ++e) out[e] = fac[16 * h2 + e] * v[e];
+            } else {
+              const float fq = direct ? 1.f : rs * vb.F[i][q4];
 #pragma unroll
-            for (int e = 0; e < 16; e += 4)
-              *reinterpret_cast<float4*>(AF + i * LDF + q4 * 16 + e) =
-                  make_float4(rtf32(out[e]), rtf32(out[e + 1]), rtf32(out[e + 2]),
-                              rtf32(out[e + 3]));
-          } else {
-            *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4)) = pack_bf16x8(out);
-            *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4 + 1)) = pack_bf16x8(out + 8);
+              for (int e = 0; e < 16; ++e) {
+                const int j = q4 * 16 + e;
+                out[e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) * v[e] : 0.f;
+              }
+            }
+            if (p < 64) {
+#pragma unroll
+              for (int e = 0; e < 16; e += 4)
+                *reinterpret_cast<float4*>(AF + i * LDF + q4 * 16 + e) =
+                    make_float4(rtf32(out[e]), rtf32(out[e + 1]), rtf32(out[e + 2]),
+                                rtf32(out[e + 3]));
+            } else {
+              *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4)) = pack_bf16x8(out);
+              *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4 + 1)) = pack_bf16x8(out + 8);
+            }
           }
         }
       }
@@ -644,9 +693,29 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           if (ph < 2) named_sync(1, 256);
         }
       }
+      // publish the tile: here, and (pair) by a bulk copy into the other CTA's
+      // ring slot, completing on its barrier
       fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_TP_READY + pb]);
+      named_sync(1, 256);
+      if (pi == 0) {
+        mbar_arrive(&bars[B_TP_READY + rb]);
+        if (kPair) {
+          const uint32_t tp_local = sbase + SM_TP + rb * 16384;
+          const uint32_t bar_peer = mapa_shared(smem_u32(&bars[B_TP_READY + rb]), peer);
+          mbar_arrive_expect_tx_cluster(bar_peer, 16384);
+          bulk_s2s_cluster(mapa_shared(tp_local, peer), tp_local, 16384, bar_peer);
+        }
+      }
+      last = n;
+    }
+    if (kPair && pi == 0) {
+      // Before the CTA can exit, the tiles it copied out into ring slots that no
+      // later chunk reuses have been released by both chains, so no copy is
+      // still in flight (bounded waits; earlier copies were released before
+      // their slot was refilled).
+      for (int n = rank; n <= last; n += step)
+        if (n + NTP >= N)
+          wait_shared_bar<kPair>(bars, B_TP_EMPTY + n % NTP, (uint32_t)(n / NTP) & 1u);
     }
   } else {
     // ------------------------------ chain warpgroup ------------------------------
@@ -673,8 +742,8 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     }
     bool ok = true;
     for (int n = 0; n < N && ok; ++n) {
-      const int s = n % NSTAGE, tb = n & 1;
-      const VecBuf& vb = vecs[tb];
+      const int s = n % NSTAGE, tb = n & 1, rb = n % NTP;
+      const VecBuf& vb = vecs[rb];
       const int t0 = n * C;
       const uint32_t d1 = tmem + TM_D1 + (uint32_t)tb * 64 + lane_off;
       if (wq < 2) {
@@ -682,23 +751,27 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         const int i = r;
         ok = wait_bar(bars, B_D1, (uint32_t)n & 1u) &&
              wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u) &&
-             wait_bar(bars, B_VEC_FULL + tb, (uint32_t)(n >> 1) & 1u);
+             wait_bar(bars, B_VEC_FULL + rb, (uint32_t)(n / NTP) & 1u);
         if (!ok) break;
         tc_fence_after();
         const float bi = vb.beta[i], egi = vb.eG[i];
         const unsigned char* Vt = sm + SM_V + s * 8192;
-        float ksrow[64];
-        tmem_ld64(d1, ksrow);
+#pragma unroll 1
+        for (int cw = 0; cw < DVT; cw += kWC) {
+          float ksrow[kWC];
+          tmem_ldw<kWC>(d1 + cw, ksrow);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float vv[16], x[16];
-          const float* ks = ksrow + 16 * q4;
-          unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4)), vv);
-          unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4 + 1)), vv + 8);
+          for (int qq = 0; qq < kWC / 16; ++qq) {
+            const int q4 = cw / 16 + qq;
+            float vv[16], x[16];
+            const float* ks = ksrow + 16 * qq;
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4)), vv);
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(i, 2 * q4 + 1)), vv + 8);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) x[e] = bi * (vv[e] - egi * ks[e]);
-          *reinterpret_cast<uint4*>(sm + SM_X + sw128(i, 2 * q4)) = pack_bf16x8(x);
-          *reinterpret_cast<uint4*>(sm + SM_X + sw128(i, 2 * q4 + 1)) = pack_bf16x8(x + 8);
+            for (int e = 0; e < 16; ++e) x[e] = bi * (vv[e] - egi * ks[e]);
+            *reinterpret_cast<uint4*>(sm + SM_X + sw128(i, 2 * q4)) = pack_bf16x8(x);
+            *reinterpret_cast<uint4*>(sm + SM_X + sw128(i, 2 * q4 + 1)) = pack_bf16x8(x + 8);
+          }
         }
         fence_proxy_async_smem();
         tc_fence_before();
@@ -709,18 +782,22 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         if (!ok) break;
         tc_fence_after();
         const float di = vb.dec[i];
-        float vprow[64];
-        tmem_ld64(tmem + TM_D2 + lane_off, vprow);
+#pragma unroll 1
+        for (int cw = 0; cw < DVT; cw += kWC) {
+          float vprow[kWC];
+          tmem_ldw<kWC>(tmem + TM_D2 + lane_off + cw, vprow);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float vpp[16];
-          const float* vp = vprow + 16 * q4;
+          for (int qq = 0; qq < kWC / 16; ++qq) {
+            const int q4 = cw / 16 + qq;
+            float vpp[16];
+            const float* vp = vprow + 16 * qq;
 #pragma unroll
-          for (int e = 0; e < 16; ++e) vpp[e] = di * vp[e];
-          *reinterpret_cast<uint4*>(sm + SM_VPP + sw128(i, 2 * q4)) = pack_bf16x8(vpp);
-          *reinterpret_cast<uint4*>(sm + SM_VPP + sw128(i, 2 * q4 + 1)) = pack_bf16x8(vpp + 8);
-          *reinterpret_cast<uint4*>(sm + SM_VP + sw128(i, 2 * q4)) = pack_bf16x8(vp);
-          *reinterpret_cast<uint4*>(sm + SM_VP + sw128(i, 2 * q4 + 1)) = pack_bf16x8(vp + 8);
+            for (int e = 0; e < 16; ++e) vpp[e] = di * vp[e];
+            *reinterpret_cast<uint4*>(sm + SM_VPP + sw128(i, 2 * q4)) = pack_bf16x8(vpp);
+            *reinterpret_cast<uint4*>(sm + SM_VPP + sw128(i, 2 * q4 + 1)) = pack_bf16x8(vpp + 8);
+            *reinterpret_cast<uint4*>(sm + SM_VP + sw128(i, 2 * q4)) = pack_bf16x8(vp);
+            *reinterpret_cast<uint4*>(sm + SM_VP + sw128(i, 2 * q4 + 1)) = pack_bf16x8(vp + 8);
+          }
         }
         fence_proxy_async_smem();
         tc_fence_before();
@@ -730,7 +807,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       // ---- epilogue 3: S <- e^{G_C} S + K^T V''  (all 128 rows) ----
       // (warps 2-3 read the gate vectors from here on: acquire them directly)
       ok = wait_bar(bars, B_D3, (uint32_t)n & 1u) &&
-           (wq < 2 || wait_bar(bars, B_VEC_FULL + tb, (uint32_t)(n >> 1) & 1u));
+           (wq < 2 || wait_bar(bars, B_VEC_FULL + rb, (uint32_t)(n / NTP) & 1u));
       if (!ok) break;
       tc_fence_after();
       {
@@ -759,7 +836,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         const float egi = vb.eG[i];
         const int t = t0 + i;
         __nv_bfloat16* orow = o + (((size_t)b * T + t) * H + h) * dv + c0;
-#pragma unroll
+#pragma unroll (kPair ? 4 : 1)
         for (int q4 = 0; q4 < 4; ++q4) {
           float qs[16], pv[16], out[16];
           tmem_ld16(d1 + q4 * 16, qs);
@@ -776,7 +853,11 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         if (lane == 0) mbar_arrive(&bars[B_D4_EMPTY]);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[B_TP_EMPTY + tb]);
+      if (lane == 0) {
+        mbar_arrive(&bars[B_VEC_EMPTY + rb]);
+        mbar_arrive(&bars[B_TP_EMPTY + rb]);
+        if (kPair) mbar_arrive_cluster(mapa_shared(smem_u32(&bars[B_TP_EMPTY + rb]), peer));
+      }
     }
     if (ok && hT) {
       float* dst = hT + ((size_t)bh * DK + r) * dv + c0;
@@ -787,6 +868,8 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves while the other may still arrive on its barriers
+  if (kPair) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TM_COLS);
@@ -839,18 +922,44 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   if (!make_map(&mk, a.k, a.B, a.T, a.H, a.dk) || !make_map(&mq, a.q, a.B, a.T, a.H, a.dk) ||
       !make_map(&mv, a.v, a.B, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
+  // Pairs of column tiles share the preparation (clusters of two CTAs) when
+  // the tile count is even and the grid leaves every CTA pair a TPC (two SMs)
+  // of its own; at higher occupancy the SMs of a TPC compete for instruction
+  // fetch and the compact unpaired kernel is faster.  GDN_CHUNK_TC_PAIR=0 / 1
+  // forces either form (kernel cross-checks).
+  const int tiles = a.dv / DVT;
+  const long long ctas = (long long)tiles * a.B * a.H;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const char* pair_env = getenv("GDN_CHUNK_TC_PAIR");
+  bool pair = tiles % 2 == 0 && ctas <= sms / 2;
+  if (pair_env && pair_env[0] == '0') pair = false;
+  if (pair_env && pair_env[0] == '1') pair = tiles % 2 == 0;
+  auto kernel = pair ? chunk_tc_kernel<true> : chunk_tc_kernel<false>;
   // The in-kernel register split assumes exactly kLaunchRegs per thread at
   // launch; with fewer, the chain warpgroup's increase could never be granted.
   cudaFuncAttributes fa;
-  cudaError_t e = cudaFuncGetAttributes(&fa, chunk_tc_kernel);
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
   if (e != cudaSuccess) return e;
   if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;
-  e = cudaFuncSetAttribute(chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           SMEM_BYTES);
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  dim3 grid(a.dv / DVT, a.B * a.H);
-  chunk_tc_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(
-      mk, mq, mv, a.g, a.beta, a.h0, static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.dv);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.dv / DVT, a.B * a.H);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pair ? 2 : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, mk, mq, mv, a.g, a.beta, a.h0,
+                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.dv);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

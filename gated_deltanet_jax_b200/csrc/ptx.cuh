@@ -142,6 +142,85 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Thread-block clusters (distributed shared memory between the CTAs of one
+// cluster; nothing here reads or writes another GPU's memory)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of this CTA's shared-memory address `saddr` as
+// seen in CTA `rank` of the cluster (same offset, other CTA's window).
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   bar_cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar_cluster_addr,
+                                                              uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
+          bar_cluster_addr),
+      "r"(bytes)
+      : "memory");
+}
+
+// Bulk copy from this CTA's shared memory into another CTA's shared memory of
+// the cluster, completing `bytes` of transaction on that CTA's mbarrier.
+// Addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst_cluster_addr, uint32_t src_saddr,
+                                                 uint32_t bytes, uint32_t bar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster_addr),
+      "r"(src_saddr), "r"(bytes), "r"(bar_cluster_addr)
+      : "memory");
+}
+
+// All threads of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::
+               : "memory");
+}
+
+// Bounded wait with acquire at cluster scope: for barriers that other CTAs of
+// the cluster arrive on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  auto try_once = [&](uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_once(0u)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!try_once(1000000u)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicExch(&g_gdn_device_error, kDevErrWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Per-warpgroup register budgets (all four warps of a warpgroup execute the
 // same instruction).  The shares of all warpgroups must add up to at most the
 // registers the block was launched with, or an increase waits forever.
@@ -313,6 +392,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
                : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// W in {16, 32, 64} consecutive fp32 columns of this thread's TMEM lane.
+template <int W>
+__device__ __forceinline__ void tmem_ldw(uint32_t taddr, float (&v)[W]) {
+  if constexpr (W == 16) tmem_ld16(taddr, v);
+  else if constexpr (W == 32) tmem_ld32(taddr, v);
+  else tmem_ld64(taddr, v);
 }
 
 // Shared-memory matrix descriptor (sm_100 UMMA format, version 1).

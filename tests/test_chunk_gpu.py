@@ -110,20 +110,24 @@ def test_prefill_config_full_size(cuda):
     assert np.isfinite(ro).all()
 
 
-def _with_kernel(kind, fn):
+def _with_env(name, value, fn):
     import os
-    old = os.environ.get("GDN_CHUNK_KERNEL")
-    os.environ["GDN_CHUNK_KERNEL"] = kind
+    old = os.environ.get(name)
+    os.environ[name] = value
     try:
         return fn()
     finally:
         if old is None:
-            del os.environ["GDN_CHUNK_KERNEL"]
+            del os.environ[name]
         else:
-            os.environ["GDN_CHUNK_KERNEL"] = old
+            os.environ[name] = old
 
 
-@pytest.mark.parametrize("dv", [64, 128, 256])
+def _with_kernel(kind, fn):
+    return _with_env("GDN_CHUNK_KERNEL", kind, fn)
+
+
+@pytest.mark.parametrize("dv", [64, 128, 192, 256])
 @pytest.mark.parametrize("T", [1, 63, 64, 65, 300])
 @pytest.mark.parametrize("with_h0", [False, True])
 def test_tensor_core_path_against_oracle(cuda, dv, T, with_h0):
@@ -150,6 +154,25 @@ def test_tensor_core_matches_cuda_core_kernel(cuda, B, T, H, dv):
     o_cc, h_cc = _with_kernel("simt", run)
     assert_close(f64(o_tc), f64(o_cc), "bf16", "o")
     assert_close(f64(h_tc), f64(h_cc), "bf16", "state")
+
+
+@pytest.mark.parametrize("B,T,H,dv", [(2, 700, 3, 128), (1, 193, 2, 256), (1, 64, 1, 128),
+                                      (1, 130, 2, 128), (3, 1, 2, 128), (4, 300, 16, 128)])
+def test_paired_tiles_match_unpaired(cuda, B, T, H, dv):
+    """Column-tile pairs that share the per-chunk preparation (clusters of two
+    CTAs, each preparing every other chunk for both) give bit-identical results
+    to tiles that each prepare every chunk themselves."""
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, dv, seed=T + dv, dtype="bf16", dev=cuda,
+                                           h0_std=0.02)
+
+    def run():
+        return ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                          output_final_state=True)
+
+    o_p, h_p = _with_env("GDN_CHUNK_TC_PAIR", "1", run)
+    o_s, h_s = _with_env("GDN_CHUNK_TC_PAIR", "0", run)
+    assert torch.equal(o_p, o_s)
+    assert torch.equal(h_p, h_s)
 
 
 def test_no_device_error_recorded_chunk(cuda):
