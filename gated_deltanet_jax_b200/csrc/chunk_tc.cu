@@ -702,7 +702,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         if (kPair) {
           const uint32_t tp_local = sbase + SM_TP + rb * 16384;
           const uint32_t bar_peer = mapa_shared(smem_u32(&bars[B_TP_READY + rb]), peer);
-          mbar_arrive_expect_tx_cluster(bar_peer, 16384);
+          mbar_arrive_expect_tx_cluster_relaxed(bar_peer, 16384);
           bulk_s2s_cluster(mapa_shared(tp_local, peer), tp_local, 16384, bar_peer);
         }
       }
@@ -856,7 +856,9 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       if (lane == 0) {
         mbar_arrive(&bars[B_VEC_EMPTY + rb]);
         mbar_arrive(&bars[B_TP_EMPTY + rb]);
-        if (kPair) mbar_arrive_cluster(mapa_shared(smem_u32(&bars[B_TP_EMPTY + rb]), peer));
+        // (the tile's last reader, D4, completed before this warp went on)
+        if (kPair)
+          mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&bars[B_TP_EMPTY + rb]), peer));
       }
     }
     if (ok && hT) {

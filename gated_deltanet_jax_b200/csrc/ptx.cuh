@@ -161,17 +161,21 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   return r;
 }
 
-// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+// Arrive on an mbarrier of another CTA of the cluster.  Relaxed: it orders
+// none of this thread's own memory accesses, so it does not wait for earlier
+// global stores to drain.  Callers use it only where what the arrival
+// announces was finished by the asynchronous proxy (tensor-core reads already
+// committed, bulk copies that complete on the barrier themselves).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(
                    bar_cluster_addr)
                : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar_cluster_addr,
-                                                              uint32_t bytes) {
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster_relaxed(uint32_t bar_cluster_addr,
+                                                                      uint32_t bytes) {
   asm volatile(
-      "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
+      "mbarrier.arrive.expect_tx.relaxed.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
           bar_cluster_addr),
       "r"(bytes)
       : "memory");
