@@ -1,6 +1,7 @@
 """Sequence-split forward: host logic on CPU (oracle as the per-segment
 function, gloo ranks for the distributed hand-off) and the CUDA path on GPU."""
 
+import datetime
 import os
 
 import numpy as np
@@ -102,7 +103,8 @@ def _nccl_worker(rank, world, port, results):
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
     try:
         from helpers import device_inputs_fast, f64
         from gated_deltanet_jax_b200 import ops
@@ -134,6 +136,11 @@ def test_split_across_nccl_ranks(cuda):
             p.start()
         for p in procs:
             p.join(300)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(30)
+        for p in procs:
             assert p.exitcode == 0
         for r in range(2):
             eo, eh = results[r]
