@@ -27,6 +27,8 @@ GDN_SEMANTICS_REFERENCE = 1
 EXPORTED_SYMBOLS = (
     "gdn_recurrent_fwd",
     "gdn_chunk_fwd",
+    "gdn_recurrent_fwd_gva",
+    "gdn_chunk_fwd_gva",
     "gdn_chunk_workspace_bytes",
     "gdn_last_error",
     "gdn_device_error",
@@ -56,6 +58,12 @@ def _declare(lib):
     lib.gdn_chunk_fwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                   _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.gdn_chunk_fwd.restype = _i
+    lib.gdn_recurrent_fwd_gva.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                          _i, _i, _i, _i, _i, _i, _i, _vp]
+    lib.gdn_recurrent_fwd_gva.restype = _i
+    lib.gdn_chunk_fwd_gva.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                      _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.gdn_chunk_fwd_gva.restype = _i
     lib.gdn_chunk_workspace_bytes.argtypes = [_i] * 8
     lib.gdn_chunk_workspace_bytes.restype = _sz
     lib.gdn_last_error.argtypes = []

@@ -59,7 +59,7 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
                   const Tin* __restrict__ v, const float* __restrict__ g,
                   const float* __restrict__ beta, const float* __restrict__ h0,
                   Tin* __restrict__ o, float* __restrict__ hT,
-                  int T, int H, int DK, int dv, int C, int semantics) {
+                  int T, int H, int Hk, int DK, int dv, int C, int semantics) {
   constexpr int NT = kSimtThreads;
   constexpr int PARTS = NT / DVT;      // threads sharing one column in the solve
   static_assert(NT % DVT == 0 && PARTS <= 32 && (32 % PARTS) == 0, "solve layout");
@@ -100,7 +100,8 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
       const int t = t0 + i;
       float kv = 0.f, qv = 0.f;
       if (t < T) {
-        const size_t off = (((size_t)b * T + t) * H + h) * DK + d;
+        // value head h reads q/k head h * Hk / H (grouped heads)
+        const size_t off = (((size_t)b * T + t) * Hk + h * Hk / H) * DK + d;
         kv = to_f32(k[off]);
         qv = to_f32(q[off]);
       }
@@ -232,7 +233,7 @@ cudaError_t launch_simt_t(const ChunkArgs& a, cudaStream_t st) {
   dim3 grid(a.dv / DVT, a.B * a.H);
   kern<<<grid, kSimtThreads, smem, st>>>(
       static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k), static_cast<const Tin*>(a.v),
-      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.T, a.H, a.dk, a.dv, a.chunk,
+      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.T, a.H, a.Hk, a.dk, a.dv, a.chunk,
       a.semantics);
   return cudaGetLastError();
 }

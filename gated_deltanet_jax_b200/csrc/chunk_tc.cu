@@ -287,7 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
                 const float* __restrict__ beta, const float* __restrict__ h0,
-                __nv_bfloat16* __restrict__ o, float* __restrict__ hT, int T, int H, int dv) {
+                __nv_bfloat16* __restrict__ o, float* __restrict__ hT, int T, int H, int Hk,
+                int dv) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // Round up to 1024 bytes by offsetting the shared array itself, so that the
   // compiler keeps every access below in the shared address space.
@@ -301,6 +302,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   const int warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh - b * H;
+  const int hq = h * Hk / H;  // q/k head of this value head (grouped heads)
   const int c0 = blockIdx.x * DVT;
   const int N = (T + C - 1) / C;
   // chunks whose T/P tile this CTA prepares: n = rank, rank + step, ...
@@ -372,10 +374,10 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           uint64_t* fb = &bars[B_FULL + s];
           mbar_arrive_expect_tx(fb, 4 * 8192 + 8192);
           const int t0 = n * C;
-          tma_load_4d(kq, &tmK, 0, h, t0, b, fb);
-          tma_load_4d(kq + 16384, &tmK, 64, h, t0, b, fb);
-          tma_load_4d(kq + 8192, &tmQ, 0, h, t0, b, fb);
-          tma_load_4d(kq + 16384 + 8192, &tmQ, 64, h, t0, b, fb);
+          tma_load_4d(kq, &tmK, 0, hq, t0, b, fb);
+          tma_load_4d(kq + 16384, &tmK, 64, hq, t0, b, fb);
+          tma_load_4d(kq + 8192, &tmQ, 0, hq, t0, b, fb);
+          tma_load_4d(kq + 16384 + 8192, &tmQ, 64, hq, t0, b, fb);
           tma_load_4d(sm + SM_V + s * 8192, &tmV, c0, h, t0, b, fb);
           issued = n + 1;
         }
@@ -921,7 +923,7 @@ bool chunk_tc_supported(const ChunkArgs& a) {
 cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   CUtensorMap mk, mq, mv;
-  if (!make_map(&mk, a.k, a.B, a.T, a.H, a.dk) || !make_map(&mq, a.q, a.B, a.T, a.H, a.dk) ||
+  if (!make_map(&mk, a.k, a.B, a.T, a.Hk, a.dk) || !make_map(&mq, a.q, a.B, a.T, a.Hk, a.dk) ||
       !make_map(&mv, a.v, a.B, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
   // Pairs of column tiles share the preparation (clusters of two CTAs) when
@@ -960,7 +962,7 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kernel, mk, mq, mv, a.g, a.beta, a.h0,
-                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.dv);
+                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

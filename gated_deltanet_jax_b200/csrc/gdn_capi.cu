@@ -56,15 +56,21 @@ int cuda_status(cudaError_t e, const char* what) {
   return fail(GDN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-}  // namespace
+// Grouped heads: q and k carry Hk heads, v / g / beta / state H, with H % Hk == 0.
+int check_groups(int H, int Hk) {
+  if (Hk < 0) return fail(GDN_ERR_INVALID, "negative Hk=%d", Hk);
+  if (H > 0 && (Hk == 0 || H % Hk != 0))
+    return fail(GDN_ERR_INVALID, "H=%d value heads is not a multiple of Hk=%d q/k heads", H, Hk);
+  return GDN_OK;
+}
 
-extern "C" {
-
-int gdn_recurrent_fwd(const void* q, const void* k, const void* v, const float* g,
-                      const float* beta, const float* h0, void* o, float* hT, int B, int T,
-                      int H, int dk, int dv, int dtype, void* stream) {
+int recurrent_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                  const float* h0, void* o, float* hT, int B, int T, int H, int Hk, int dk,
+                  int dv, int dtype, void* stream) {
   g_err[0] = '\0';
   int rc = check_common(q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype);
+  if (rc) return rc;
+  rc = check_groups(H, Hk);
   if (rc) return rc;
   if (T == 0 && (B * H) > 0 && h0 != hT && hT) {
     // Nothing to run but the state must still be carried through.
@@ -74,8 +80,29 @@ int gdn_recurrent_fwd(const void* q, const void* k, const void* v, const float* 
                                          (cudaStream_t)stream);
     return cuda_status(e, "gdn_recurrent_fwd (T=0 state copy)");
   }
-  gdn::RecurrentArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype};
+  gdn::RecurrentArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype, Hk};
   return cuda_status(gdn::launch_recurrent(a, (cudaStream_t)stream), "gdn_recurrent_fwd");
+}
+
+int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
+              const float* h0, void* o, float* hT, int B, int T, int H, int Hk, int dk, int dv,
+              int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
+              void* stream);
+
+}  // namespace
+
+extern "C" {
+
+int gdn_recurrent_fwd(const void* q, const void* k, const void* v, const float* g,
+                      const float* beta, const float* h0, void* o, float* hT, int B, int T,
+                      int H, int dk, int dv, int dtype, void* stream) {
+  return recurrent_fwd(q, k, v, g, beta, h0, o, hT, B, T, H, H, dk, dv, dtype, stream);
+}
+
+int gdn_recurrent_fwd_gva(const void* q, const void* k, const void* v, const float* g,
+                          const float* beta, const float* h0, void* o, float* hT, int B, int T,
+                          int H, int Hk, int dk, int dv, int dtype, void* stream) {
+  return recurrent_fwd(q, k, v, g, beta, h0, o, hT, B, T, H, Hk, dk, dv, dtype, stream);
 }
 
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int dtype,
@@ -88,8 +115,30 @@ int gdn_chunk_fwd(const void* q, const void* k, const void* v, const float* g, c
                   const float* h0, void* o, float* hT, int B, int T, int H, int dk, int dv,
                   int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
                   void* stream) {
+  return chunk_fwd(q, k, v, g, beta, h0, o, hT, B, T, H, H, dk, dv, chunk, dtype, semantics,
+                   workspace, ws_bytes, stream);
+}
+
+int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v, const float* g,
+                      const float* beta, const float* h0, void* o, float* hT, int B, int T, int H,
+                      int Hk, int dk, int dv, int chunk, int dtype, int semantics,
+                      void* workspace, size_t ws_bytes, void* stream) {
+  return chunk_fwd(q, k, v, g, beta, h0, o, hT, B, T, H, Hk, dk, dv, chunk, dtype, semantics,
+                   workspace, ws_bytes, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
+              const float* h0, void* o, float* hT, int B, int T, int H, int Hk, int dk, int dv,
+              int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
+              void* stream) {
   g_err[0] = '\0';
   int rc = check_common(q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype);
+  if (rc) return rc;
+  rc = check_groups(H, Hk);
   if (rc) return rc;
   if (chunk != 16 && chunk != 32 && chunk != 64)
     return fail(GDN_ERR_UNSUPPORTED, "chunk=%d not supported (16, 32 or 64)", chunk);
@@ -106,7 +155,7 @@ int gdn_chunk_fwd(const void* q, const void* k, const void* v, const float* g, c
     return cuda_status(e, "gdn_chunk_fwd (T=0 state copy)");
   }
   gdn::ChunkArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, chunk, dtype, semantics,
-                   workspace, ws_bytes};
+                   workspace, ws_bytes, Hk};
   // GDN_CHUNK_KERNEL=simt forces the CUDA-core kernel (kernel cross-checks).
   const char* force = getenv("GDN_CHUNK_KERNEL");
   const bool simt_only = force && strcmp(force, "simt") == 0;
@@ -117,6 +166,10 @@ int gdn_chunk_fwd(const void* q, const void* k, const void* v, const float* g, c
   return cuda_status(gdn::launch_chunk_simt(a, (cudaStream_t)stream), "gdn_chunk_fwd");
 }
 
+}  // namespace
+
+extern "C" {
+
 const char* gdn_last_error(void) { return g_err; }
 
 int gdn_device_error(int clear) {
@@ -126,6 +179,6 @@ int gdn_device_error(int clear) {
   return a ? a : b;
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 0; }
+int gdn_abi_version(void) { return (1 << 16) | 1; }
 
 }  // extern "C"

@@ -19,6 +19,7 @@ struct RecurrentArgs {
   void* o;
   float* hT;
   int B, T, H, dk, dv, dtype;
+  int Hk;  // heads of q and k (H % Hk == 0); value head h reads q/k head h * Hk / H
 };
 
 struct ChunkArgs {
@@ -33,6 +34,7 @@ struct ChunkArgs {
   int B, T, H, dk, dv, chunk, dtype, semantics;
   void* workspace;
   size_t ws_bytes;
+  int Hk;  // heads of q and k (H % Hk == 0); value head h reads q/k head h * Hk / H
 };
 
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);

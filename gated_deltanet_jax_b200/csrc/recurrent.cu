@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(NT)
 recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
                  const Tin* __restrict__ v, const float* __restrict__ g,
                  const float* __restrict__ beta, const float* h0,
-                 Tin* __restrict__ o, float* hT, int T, int H, int dv) {
+                 Tin* __restrict__ o, float* hT, int T, int H, int Hk, int dv) {
   constexpr int LPR = CW / 4;        // threads across one row of the tile
   constexpr int RPP = NT / LPR;      // rows covered per pass of the CTA
   constexpr int RPT = DK / RPP;      // rows per thread
@@ -45,6 +45,7 @@ recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
   const int rb = tid / LPR;          // first row
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh - b * H;
+  const int hq = h * Hk / H;         // q/k head of this value head (grouped heads)
   const int col = blockIdx.x * CW + cg * 4;
 
   const size_t sbase = (size_t)bh * DK * dv + col;
@@ -60,9 +61,10 @@ recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
   for (int t = 0; t < T; ++t) {
     const int buf = t & 1;
     const size_t tok = ((size_t)b * T + t) * H + h;
+    const size_t tokq = ((size_t)b * T + t) * Hk + hq;
     for (int i = tid; i < DK; i += NT) {
-      s_k[buf][i] = to_f32(k[tok * DK + i]);
-      s_q[buf][i] = to_f32(q[tok * DK + i]);
+      s_k[buf][i] = to_f32(k[tokq * DK + i]);
+      s_q[buf][i] = to_f32(q[tokq * DK + i]);
     }
     const float4 vv = load4(v + tok * dv + col);
     const float alpha = __expf(g[tok]);
@@ -145,7 +147,7 @@ cudaError_t launch_cfg(const RecurrentArgs& a, cudaStream_t st) {
   dim3 grid(a.dv / CW, a.B * a.H);
   recurrent_kernel<Tin, DK, CW, NT><<<grid, NT, 0, st>>>(
       static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k), static_cast<const Tin*>(a.v),
-      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.T, a.H, a.dv);
+      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv);
   return cudaGetLastError();
 }
 

@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
                       const Tin* __restrict__ v, const float* __restrict__ g,
                       const float* __restrict__ beta, const float* h0, Tin* __restrict__ o,
-                      float* hT, int n_units) {
+                      float* hT, int n_units, int H, int Hk) {
   using L = BulkLayout<Tin, DK, DV>;
   constexpr int LPR = L::LPR;
   constexpr int RPP = kComputeThreads / LPR;
@@ -81,12 +81,14 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
     auto unit_of = [&](int j) { return (int)blockIdx.x + j * (int)gridDim.x; };
     auto load = [&](int j) {
       const int s = j % kStages, u = unit_of(j);
+      // q/k row of this (b, h): value head h reads q/k head h * Hk / H (grouped heads)
+      const int uq = (u / H) * Hk + (u % H) * Hk / H;
       unsigned char* st = stage(s);
       const uint32_t bytes = (h0 ? L::state_bytes : 0) + 2 * L::qk_bytes + L::v_bytes;
       mbar_arrive_expect_tx(&full_bar[s], bytes);
       if (h0) bulk_g2s(st, h0 + (size_t)u * DK * DV, L::state_bytes, &full_bar[s]);
-      bulk_g2s(st + L::state_bytes, q + (size_t)u * DK, L::qk_bytes, &full_bar[s]);
-      bulk_g2s(st + L::state_bytes + L::qk_bytes, k + (size_t)u * DK, L::qk_bytes, &full_bar[s]);
+      bulk_g2s(st + L::state_bytes, q + (size_t)uq * DK, L::qk_bytes, &full_bar[s]);
+      bulk_g2s(st + L::state_bytes + L::qk_bytes, k + (size_t)uq * DK, L::qk_bytes, &full_bar[s]);
       bulk_g2s(st + L::state_bytes + 2 * L::qk_bytes, v + (size_t)u * DV, L::v_bytes,
                &full_bar[s]);
     };
@@ -245,7 +247,7 @@ cudaError_t launch_bulk_t(const RecurrentArgs& a, cudaStream_t st) {
   const int grid = n_units < num_sms() ? n_units : num_sms();
   kern<<<grid, kThreads, L::total, st>>>(
       static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k), static_cast<const Tin*>(a.v),
-      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, n_units);
+      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, n_units, a.H, a.Hk);
   return cudaGetLastError();
 }
 

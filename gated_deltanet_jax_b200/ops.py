@@ -23,6 +23,10 @@ Differences from the reference, all additive:
   may be ``initial_state`` itself (in-place decode).
 * ``semantics="reference"`` on the chunk op reproduces ops.py:238-346 as
   written, including its deviations from the recurrence.
+* Grouped value heads: q and k may carry fewer heads (Hk) than v, g and beta
+  (H, a multiple of Hk).  Value head h then uses q/k head ``h * Hk // H``,
+  which is what the reference layer obtains by ``jnp.repeat`` of q and k
+  before calling its ops (model.py:132-135), without the repeated copies.
 """
 
 from __future__ import annotations
@@ -48,11 +52,13 @@ def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_stat
         if not t.is_cuda:
             raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path)")
     if q.dim() != 4 or k.shape != q.shape:
-        raise ValueError(f"q and k must both be [B,T,H,dk]; got {tuple(q.shape)}, {tuple(k.shape)}")
-    B, T, H, dk = q.shape
-    if v.dim() != 4 or tuple(v.shape[:3]) != (B, T, H):
-        raise ValueError(f"v must be [B,T,H,dv] with B,T,H={B},{T},{H}; got {tuple(v.shape)}")
-    dv = v.shape[3]
+        raise ValueError(f"q and k must both be [B,T,Hk,dk]; got {tuple(q.shape)}, {tuple(k.shape)}")
+    B, T, Hk, dk = q.shape
+    if v.dim() != 4 or tuple(v.shape[:2]) != (B, T):
+        raise ValueError(f"v must be [B,T,H,dv] with B,T={B},{T}; got {tuple(v.shape)}")
+    H, dv = v.shape[2], v.shape[3]
+    if (Hk == 0) != (H == 0) or (H and H % Hk):
+        raise ValueError(f"v's {H} heads must be a multiple of q/k's {Hk} heads")
     for name, t in (("g", g), ("beta", beta)):
         if tuple(t.shape) != (B, T, H):
             raise ValueError(f"{name} must be [B,T,H]=({B},{T},{H}); got {tuple(t.shape)}")
@@ -87,7 +93,7 @@ def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_stat
     elif output_final_state:
         hT = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
     o = torch.empty((B, T, H, dv), dtype=v.dtype, device=dev)
-    return q, k, v, g, beta, h0, hT, o, (B, T, H, dk, dv)
+    return q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv)
 
 
 def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_final_state=False,
@@ -103,7 +109,7 @@ def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_fina
     """
     if semantics not in _SEMANTICS:
         raise ValueError(f"semantics must be one of {sorted(_SEMANTICS)}; got {semantics!r}")
-    q, k, v, g, beta, h0, hT, o, (B, T, H, dk, dv) = _prepare(
+    q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv) = _prepare(
         q, k, v, g, beta, initial_state, final_state_out, output_final_state)
     lib = _lib.load()
     dtype = _DTYPES[q.dtype]
@@ -112,9 +118,14 @@ def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_fina
         ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, dk, dv, int(chunk_size), dtype, sem)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        rc = lib.gdn_chunk_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0), _ptr(o),
-                               _ptr(hT), B, T, H, dk, dv, int(chunk_size), dtype, sem, _ptr(ws),
-                               ws_bytes, stream)
+        if Hk == H:
+            rc = lib.gdn_chunk_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
+                                   _ptr(o), _ptr(hT), B, T, H, dk, dv, int(chunk_size), dtype,
+                                   sem, _ptr(ws), ws_bytes, stream)
+        else:
+            rc = lib.gdn_chunk_fwd_gva(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
+                                       _ptr(o), _ptr(hT), B, T, H, Hk, dk, dv, int(chunk_size),
+                                       dtype, sem, _ptr(ws), ws_bytes, stream)
     _lib.check(rc, "gdn_chunk_fwd")
     return o, hT
 
@@ -129,13 +140,19 @@ def fused_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None,
     reference call: zero initial state, returns ``(o, None)``.  For decode pass
     ``initial_state=S, final_state_out=S`` to update the state in place.
     """
-    q, k, v, g, beta, h0, hT, o, (B, T, H, dk, dv) = _prepare(
+    q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv) = _prepare(
         q, k, v, g, beta, initial_state, final_state_out, output_final_state)
     lib = _lib.load()
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        rc = lib.gdn_recurrent_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
-                                   _ptr(o), _ptr(hT), B, T, H, dk, dv, _DTYPES[q.dtype], stream)
+        if Hk == H:
+            rc = lib.gdn_recurrent_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
+                                       _ptr(o), _ptr(hT), B, T, H, dk, dv, _DTYPES[q.dtype],
+                                       stream)
+        else:
+            rc = lib.gdn_recurrent_fwd_gva(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                                           _ptr(h0), _ptr(o), _ptr(hT), B, T, H, Hk, dk, dv,
+                                           _DTYPES[q.dtype], stream)
     _lib.check(rc, "gdn_recurrent_fwd")
     return o, hT
 

@@ -51,8 +51,8 @@ def segment_summary(q, k, v, g, beta, segment_fn: SegmentFn):
     One call on v' = [v | 0] with h0' = [0 | I]; the returned state is [S | M]
     with S [B,H,dk,dv] and M [B,H,dk,dk].
     """
-    B, T, H, dk = k.shape
-    dv = v.shape[-1]
+    B, T, _, dk = k.shape
+    H, dv = v.shape[2], v.shape[-1]   # value heads (q/k may carry fewer, grouped)
     v_ext = torch.cat([v, torch.zeros(B, T, H, dk, dtype=v.dtype, device=v.device)], dim=-1)
     h_ext = torch.zeros(B, H, dk, dv + dk, dtype=torch.float32, device=v.device)
     h_ext[..., dv:] = torch.eye(dk, dtype=torch.float32, device=v.device)
@@ -81,8 +81,8 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
     ``gather`` maps this rank's packed (S, M) pairs [B, parts, H, dk, dv + dk] to
     the list of every rank's, in rank order; segments are ordered rank-major.
     """
-    B, T, H, dk = k.shape
-    dv = v.shape[-1]
+    B, T, _, dk = k.shape
+    H, dv = v.shape[2], v.shape[-1]   # value heads (q/k may carry fewer, grouped)
     seg = -(-T // (parts * chunk_size)) * chunk_size          # tokens per segment
     Tp = seg * parts
     pad = Tp - T

@@ -77,6 +77,27 @@ int gdn_chunk_fwd(const void* q, const void* k, const void* v,
                   int dtype, int semantics,
                   void* workspace, size_t ws_bytes, void* stream);
 
+/*
+ * Grouped value heads ("GVA"): q and k carry Hk heads, v, g, beta, o and the
+ * states carry H heads, H a multiple of Hk; value head h reads q/k head
+ * h * Hk / H.  The result equals gdn_recurrent_fwd / gdn_chunk_fwd called on
+ * q and k with each head repeated H / Hk times in place -- what the reference
+ * layer does with jnp.repeat before calling its ops (model.py:132-135) --
+ * without materialising the repeats.  Hk == H is the plain call.
+ */
+int gdn_recurrent_fwd_gva(const void* q, const void* k, const void* v,
+                          const float* g, const float* beta,
+                          const float* h0, void* o, float* hT,
+                          int B, int T, int H, int Hk, int dk, int dv, int dtype,
+                          void* stream);
+
+int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v,
+                      const float* g, const float* beta,
+                      const float* h0, void* o, float* hT,
+                      int B, int T, int H, int Hk, int dk, int dv, int chunk,
+                      int dtype, int semantics,
+                      void* workspace, size_t ws_bytes, void* stream);
+
 /* Device scratch bytes gdn_chunk_fwd needs for these sizes (0 = none). */
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
                                  int dtype, int semantics);
@@ -94,7 +115,7 @@ int gdn_device_error(int clear);
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
-/* ABI version of this header: (major << 16) | minor. */
+/* ABI version of this header: (major << 16) | minor (1.1: the _gva entry points). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

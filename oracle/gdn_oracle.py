@@ -352,6 +352,15 @@ TOL_FP32_ABS = 2e-3
 TOL_BF16_REL = 2e-2
 
 
+def repeat_heads(x: np.ndarray, rep: int) -> np.ndarray:
+    """Each head of x [B,T,Hk,...] repeated ``rep`` times in place along axis 2.
+
+    The layer's expansion of q and k for grouped value heads, model.py:132-135
+    (``jnp.repeat(x, rep, axis=2)``): value head h uses q/k head h // rep.
+    """
+    return np.repeat(x, rep, axis=2)
+
+
 def max_abs_err(out, ref) -> float:
     return float(np.max(np.abs(np.asarray(out, np.float64) - np.asarray(ref, np.float64))))
 

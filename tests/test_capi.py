@@ -96,6 +96,19 @@ def test_chunk_rejects_bad_arguments(lib, kw, code):
     assert msg
 
 
+@pytest.mark.parametrize("H,Hk", [(6, 4), (4, 0), (4, -1), (3, 6)])
+def test_grouped_heads_reject_bad_groups(lib, H, Hk):
+    """The _gva entry points need H (value heads) to be a multiple of Hk (q/k heads)."""
+    p = ctypes.c_void_p(16)
+    rc = lib.gdn_recurrent_fwd_gva(p, p, p, p, p, None, p, None, 1, 4, H, Hk, 16, 16,
+                                   _lib.GDN_DTYPE_BF16, None)
+    assert rc == _lib.GDN_ERR_INVALID, lib.gdn_last_error()
+    assert b"multiple" in lib.gdn_last_error() or b"Hk" in lib.gdn_last_error()
+    rc = lib.gdn_chunk_fwd_gva(p, p, p, p, p, None, p, None, 1, 4, H, Hk, 16, 16, 64,
+                               _lib.GDN_DTYPE_BF16, _lib.GDN_SEMANTICS_EXACT, None, 0, None)
+    assert rc == _lib.GDN_ERR_INVALID, lib.gdn_last_error()
+
+
 def test_empty_problem_is_a_no_op(lib):
     # B*H == 0: nothing to launch, no CUDA call, OK.
     assert _call_recurrent(lib, B=0) == _lib.GDN_OK

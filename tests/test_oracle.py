@@ -125,3 +125,21 @@ def test_work_accounting():
     assert orc.flops_chunk_per_token_head(128, 128, 64) == 180224
     assert orc.bytes_chunk_per_token_head(128, 128) == 1032
     assert orc.bytes_recurrent_per_head_step(128, 128) == 132104
+
+
+def test_repeat_heads_matches_layer_expansion():
+    """repeat_heads is the layer's jnp.repeat(axis=2): value head h uses q/k head h // rep."""
+    x = np.arange(2 * 3 * 2 * 4, dtype=np.float64).reshape(2, 3, 2, 4)
+    r = orc.repeat_heads(x, 3)
+    assert r.shape == (2, 3, 6, 4)
+    for h in range(6):
+        assert np.array_equal(r[:, :, h], x[:, :, h // 3])
+
+
+def test_grouped_heads_equal_repeated_recurrence():
+    """The grouped-head problem is the plain problem on repeated q, k (oracle level)."""
+    q, k, v, g, beta, h0 = orc.make_inputs(1, 40, 6, 16, 24, seed=8, h0_std=0.05)
+    qg, kg = q[:, :, ::3].copy(), k[:, :, ::3].copy()   # 2 q/k heads for 6 value heads
+    o1, h1 = orc.recurrent_ref(orc.repeat_heads(qg, 3), orc.repeat_heads(kg, 3), v, g, beta, h0)
+    o2, h2 = orc.chunk_exact(orc.repeat_heads(qg, 3), orc.repeat_heads(kg, 3), v, g, beta, h0, 16)
+    assert orc.max_abs_err(o1, o2) < 1e-12 and orc.max_abs_err(h1, h2) < 1e-12
