@@ -225,6 +225,18 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   return true;
 }
 
+// Programmatic dependent launch.  griddep_wait blocks until the grids this
+// one was launched behind (with programmatic stream serialization) have
+// completed and their memory is visible -- a no-op for an ordinary launch;
+// griddep_launch_dependents lets the next such grid be scheduled early (its
+// own griddep_wait still orders every read after this grid's writes).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Per-warpgroup register budgets (all four warps of a warpgroup execute the
 // same instruction).  The shares of all warpgroups must add up to at most the
 // registers the block was launched with, or an increase waits forever.

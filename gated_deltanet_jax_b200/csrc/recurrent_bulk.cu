@@ -17,6 +17,8 @@
 //
 // HBM traffic per head: the state read and written once, plus q, k, v, o,
 // g, beta.  Every mbarrier wait is bounded (ptx.cuh).
+#include <cstdlib>
+
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 #include "ptx.cuh"
@@ -72,6 +74,10 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
     fence_mbar_init();
   }
   __syncthreads();
+  // Everything above overlaps the previous decode step; nothing in global
+  // memory is read before that step has completed.
+  griddep_wait();
+  if (tid == 0) griddep_launch_dependents();
 
   auto stage = [&](int s) { return smem + (size_t)s * L::stage_bytes; };
 
@@ -245,9 +251,24 @@ cudaError_t launch_bulk_t(const RecurrentArgs& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int n_units = a.B * a.H;
   const int grid = n_units < num_sms() ? n_units : num_sms();
-  kern<<<grid, kThreads, L::total, st>>>(
-      static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k), static_cast<const Tin*>(a.v),
-      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, n_units, a.H, a.Hk);
+  // Consecutive decode steps on one stream may overlap their launch and
+  // set-up (programmatic dependent launch); GDN_DECODE_PDL=0 turns it off.
+  const char* pdl_env = getenv("GDN_DECODE_PDL");
+  const bool pdl = !(pdl_env && pdl_env[0] == '0');
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k),
+                         static_cast<const Tin*>(a.v), a.g, a.beta, a.h0, static_cast<Tin*>(a.o),
+                         a.hT, n_units, a.H, a.Hk);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
