@@ -29,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_fwd",
     "gdn_recurrent_fwd_gva",
     "gdn_chunk_fwd_gva",
+    "gdn_chunk_fwd_varlen",
     "gdn_chunk_workspace_bytes",
     "gdn_last_error",
     "gdn_device_error",
@@ -64,6 +65,9 @@ def _declare(lib):
     lib.gdn_chunk_fwd_gva.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.gdn_chunk_fwd_gva.restype = _i
+    lib.gdn_chunk_fwd_varlen.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                         _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
+    lib.gdn_chunk_fwd_varlen.restype = _i
     lib.gdn_chunk_workspace_bytes.argtypes = [_i] * 8
     lib.gdn_chunk_workspace_bytes.restype = _sz
     lib.gdn_last_error.argtypes = []

@@ -59,7 +59,8 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
                   const Tin* __restrict__ v, const float* __restrict__ g,
                   const float* __restrict__ beta, const float* __restrict__ h0,
                   Tin* __restrict__ o, float* __restrict__ hT,
-                  int T, int H, int Hk, int DK, int dv, int C, int semantics) {
+                  const int* __restrict__ cu_seqlens, int T, int H, int Hk, int DK, int dv,
+                  int C, int semantics) {
   constexpr int NT = kSimtThreads;
   constexpr int PARTS = NT / DVT;      // threads sharing one column in the solve
   static_assert(NT % DVT == 0 && PARTS <= 32 && (32 % PARTS) == 0, "solve layout");
@@ -80,7 +81,17 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
 
   const int tid = threadIdx.x;
   const int bh = blockIdx.y;
-  const int b = bh / H, h = bh - b * H;
+  int b = bh / H;
+  const int h = bh - b * H;
+  // Packed variable-length sequences (cu_seqlens != NULL): blockIdx.y = s * H + h,
+  // and sequence s is tokens [cu_seqlens[s], cu_seqlens[s + 1]) of the single
+  // row of T tokens (offsets clamped to [0, T], so no access leaves the row).
+  int tok0 = 0, Tn = T;
+  if (cu_seqlens) {
+    const int a0 = min(max(cu_seqlens[b], 0), T);
+    const int a1 = min(max(cu_seqlens[b + 1], a0), T);
+    b = 0, tok0 = a0, Tn = a1 - a0;
+  }
   const int c0 = blockIdx.x * DVT;
   const bool literal = semantics == kReference;
 
@@ -90,7 +101,7 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
     sS[e] = h0 ? h0[((size_t)bh * DK + r) * dv + c0 + c] : 0.f;
   }
 
-  const int N = (T + C - 1) / C;
+  const int N = (Tn + C - 1) / C;
   for (int n = 0; n < N; ++n) {
     const int t0 = n * C;
     __syncthreads();  // previous chunk done with every buffer
@@ -99,9 +110,9 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
       const int i = e / DK, d = e - i * DK;
       const int t = t0 + i;
       float kv = 0.f, qv = 0.f;
-      if (t < T) {
+      if (t < Tn) {
         // value head h reads q/k head h * Hk / H (grouped heads)
-        const size_t off = (((size_t)b * T + t) * Hk + h * Hk / H) * DK + d;
+        const size_t off = (((size_t)b * T + tok0 + t) * Hk + h * Hk / H) * DK + d;
         kv = to_f32(k[off]);
         qv = to_f32(q[off]);
       }
@@ -111,13 +122,13 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
     for (int e = tid; e < C * DVT; e += NT) {
       const int i = e / DVT, c = e - i * DVT;
       const int t = t0 + i;
-      sX[e] = t < T ? to_f32(v[(((size_t)b * T + t) * H + h) * dv + c0 + c]) : 0.f;
+      sX[e] = t < Tn ? to_f32(v[(((size_t)b * T + tok0 + t) * H + h) * dv + c0 + c]) : 0.f;
     }
     if (tid < C) {
       const int t = t0 + tid;
-      const size_t off = ((size_t)b * T + t) * H + h;
-      sG[tid] = t < T ? g[off] : 0.f;
-      sb[tid] = t < T ? beta[off] : 0.f;
+      const size_t off = ((size_t)b * T + tok0 + t) * H + h;
+      sG[tid] = t < Tn ? g[off] : 0.f;
+      sb[tid] = t < Tn ? beta[off] : 0.f;
     }
     __syncthreads();
     // ---- in-chunk cumulative gate (one warp, serial over <= 64 values) ----
@@ -191,12 +202,12 @@ chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
         t = f / H;
         hh = f - t * H;
       }
-      if (t < T) o[(((size_t)b * T + t) * H + hh) * dv + c0 + c] = from_f32<Tin>(acc);
+      if (t < Tn) o[(((size_t)b * T + tok0 + t) * H + hh) * dv + c0 + c] = from_f32<Tin>(acc);
     }
     // ---- S <- e^{G_C} S + (e^{G_C - G} K)^T V' ----
     {
       // the literal path decays by e^0 after a zero-padded last chunk
-      const float eGC = (literal && t0 + C > T) ? 1.f : __expf(GC);
+      const float eGC = (literal && t0 + C > Tn) ? 1.f : __expf(GC);
       for (int e = tid; e < DK * DVT; e += NT) {
         const int d = e / DVT, c = e - d * DVT;
         float acc = 0.f;
@@ -233,7 +244,8 @@ cudaError_t launch_simt_t(const ChunkArgs& a, cudaStream_t st) {
   dim3 grid(a.dv / DVT, a.B * a.H);
   kern<<<grid, kSimtThreads, smem, st>>>(
       static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k), static_cast<const Tin*>(a.v),
-      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.T, a.H, a.Hk, a.dk, a.dv, a.chunk,
+      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.cu_seqlens, a.T, a.H, a.Hk, a.dk, a.dv,
+      a.chunk,
       a.semantics);
   return cudaGetLastError();
 }

@@ -287,8 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
                 const float* __restrict__ beta, const float* __restrict__ h0,
-                __nv_bfloat16* __restrict__ o, float* __restrict__ hT, int T, int H, int Hk,
-                int dv) {
+                __nv_bfloat16* __restrict__ o, float* __restrict__ hT,
+                const int* __restrict__ cu_seqlens, int T, int H, int Hk, int dv) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // Round up to 1024 bytes by offsetting the shared array itself, so that the
   // compiler keeps every access below in the shared address space.
@@ -301,10 +301,23 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y;
-  const int b = bh / H, h = bh - b * H;
+  int b = bh / H;
+  const int h = bh - b * H;
   const int hq = h * Hk / H;  // q/k head of this value head (grouped heads)
+  // Packed variable-length sequences (cu_seqlens != NULL): blockIdx.y = s * H + h,
+  // and sequence s is tokens [cu_seqlens[s], cu_seqlens[s + 1]) of the single
+  // row of T tokens (offsets clamped to [0, T], so no access leaves the row).
+  // Rows of a chunk past the sequence's end hold the next sequence's tokens (or
+  // the zero fill past the row): they get g = beta = 0, which makes their rows
+  // of A, X and V' exactly zero, so they reach neither the state nor an output.
+  int tok0 = 0, Tn = T;
+  if (cu_seqlens) {
+    const int a0 = min(max(cu_seqlens[b], 0), T);
+    const int a1 = min(max(cu_seqlens[b + 1], a0), T);
+    b = 0, tok0 = a0, Tn = a1 - a0;
+  }
   const int c0 = blockIdx.x * DVT;
-  const int N = (T + C - 1) / C;
+  const int N = (Tn + C - 1) / C;
   // chunks whose T/P tile this CTA prepares: n = rank, rank + step, ...
   const int rank = kPair ? (int)cluster_ctarank() : 0;
   // TMEM read widths of the A/P pass and the chain epilogues.  Paired tiles
@@ -373,7 +386,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           unsigned char* kq = sm + SM_KQ + s * 32768;
           uint64_t* fb = &bars[B_FULL + s];
           mbar_arrive_expect_tx(fb, 4 * 8192 + 8192);
-          const int t0 = n * C;
+          const int t0 = tok0 + n * C;
           tma_load_4d(kq, &tmK, 0, hq, t0, b, fb);
           tma_load_4d(kq + 16384, &tmK, 64, hq, t0, b, fb);
           tma_load_4d(kq + 8192, &tmQ, 0, hq, t0, b, fb);
@@ -473,16 +486,16 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       // to a later row; if any exceeds 40 (a factor could overflow, or hide a
       // non-negligible product behind an underflowed partner) the chunk is flagged
       // to form e^{G_i - G_j} directly.
-      const size_t gb = (size_t)b * T * H + h;
+      const size_t gb = ((size_t)b * T + tok0) * H + h;
       bool ok = true;
       for (int n = 0; n < N && ok; ++n) {
         const int rb = n % NTP;
         VecBuf& vb = vecs[rb];
         const int t = n * C + 2 * lane;
-        const float g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
-        const float g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
-        const float b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
-        const float b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
+        const float g0 = t < Tn ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
+        const float g1 = t + 1 < Tn ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
+        const float b0 = t < Tn ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
+        const float b1 = t + 1 < Tn ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
         if (n >= NTP) ok = wait_bar(bars, B_VEC_EMPTY + rb, (uint32_t)((n / NTP) - 1) & 1u);
         if (!ok) break;
         const float pair = g0 + g1;
@@ -837,7 +850,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         tc_fence_after();
         const float egi = vb.eG[i];
         const int t = t0 + i;
-        __nv_bfloat16* orow = o + (((size_t)b * T + t) * H + h) * dv + c0;
+        __nv_bfloat16* orow = o + (((size_t)b * T + tok0 + t) * H + h) * dv + c0;
 #pragma unroll (kPair ? 4 : 1)
         for (int q4 = 0; q4 < 4; ++q4) {
           float qs[16], pv[16], out[16];
@@ -845,7 +858,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           tmem_ld16(tmem + TM_D4 + lane_off + q4 * 16, pv);
 #pragma unroll
           for (int e = 0; e < 16; ++e) out[e] = fmaf(egi, qs[e], pv[e]);
-          if (t < T) {
+          if (t < Tn) {
             *reinterpret_cast<uint4*>(orow + q4 * 16) = pack_bf16x8(out);
             *reinterpret_cast<uint4*>(orow + q4 * 16 + 8) = pack_bf16x8(out + 8);
           }
@@ -923,8 +936,9 @@ bool chunk_tc_supported(const ChunkArgs& a) {
 cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   CUtensorMap mk, mq, mv;
-  if (!make_map(&mk, a.k, a.B, a.T, a.Hk, a.dk) || !make_map(&mq, a.q, a.B, a.T, a.Hk, a.dk) ||
-      !make_map(&mv, a.v, a.B, a.T, a.H, a.dv))
+  const int rows = a.cu_seqlens ? 1 : a.B;  // packed sequences share one row of T tokens
+  if (!make_map(&mk, a.k, rows, a.T, a.Hk, a.dk) || !make_map(&mq, a.q, rows, a.T, a.Hk, a.dk) ||
+      !make_map(&mv, a.v, rows, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
   // Pairs of column tiles share the preparation (clusters of two CTAs) when
   // the tile count is even and the grid leaves every CTA pair a TPC (two SMs)
@@ -962,7 +976,8 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kernel, mk, mq, mv, a.g, a.beta, a.h0,
-                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv);
+                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.cu_seqlens, a.T, a.H, a.Hk,
+                         a.dv);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -85,9 +85,9 @@ int recurrent_fwd(const void* q, const void* k, const void* v, const float* g, c
 }
 
 int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
-              const float* h0, void* o, float* hT, int B, int T, int H, int Hk, int dk, int dv,
-              int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
-              void* stream);
+              const float* h0, void* o, float* hT, const int* cu_seqlens, int B, int T, int H,
+              int Hk, int dk, int dv, int chunk, int dtype, int semantics, void* workspace,
+              size_t ws_bytes, void* stream);
 
 }  // namespace
 
@@ -115,16 +115,32 @@ int gdn_chunk_fwd(const void* q, const void* k, const void* v, const float* g, c
                   const float* h0, void* o, float* hT, int B, int T, int H, int dk, int dv,
                   int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
                   void* stream) {
-  return chunk_fwd(q, k, v, g, beta, h0, o, hT, B, T, H, H, dk, dv, chunk, dtype, semantics,
-                   workspace, ws_bytes, stream);
+  return chunk_fwd(q, k, v, g, beta, h0, o, hT, nullptr, B, T, H, H, dk, dv, chunk, dtype,
+                   semantics, workspace, ws_bytes, stream);
 }
 
 int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v, const float* g,
                       const float* beta, const float* h0, void* o, float* hT, int B, int T, int H,
                       int Hk, int dk, int dv, int chunk, int dtype, int semantics,
                       void* workspace, size_t ws_bytes, void* stream) {
-  return chunk_fwd(q, k, v, g, beta, h0, o, hT, B, T, H, Hk, dk, dv, chunk, dtype, semantics,
-                   workspace, ws_bytes, stream);
+  return chunk_fwd(q, k, v, g, beta, h0, o, hT, nullptr, B, T, H, Hk, dk, dv, chunk, dtype,
+                   semantics, workspace, ws_bytes, stream);
+}
+
+int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v, const float* g,
+                         const float* beta, const float* h0, void* o, float* hT,
+                         const int* cu_seqlens, int n_seqs, int T, int H, int Hk, int dk, int dv,
+                         int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
+                         void* stream) {
+  g_err[0] = '\0';
+  if (n_seqs < 0) return fail(GDN_ERR_INVALID, "negative n_seqs=%d", n_seqs);
+  if (n_seqs > 0 && !cu_seqlens) return fail(GDN_ERR_INVALID, "cu_seqlens must be non-NULL");
+  if (cu_seqlens && (reinterpret_cast<uintptr_t>(cu_seqlens) & 3u))
+    return fail(GDN_ERR_INVALID, "cu_seqlens is not 4-byte aligned");
+  if (semantics != GDN_SEMANTICS_EXACT)
+    return fail(GDN_ERR_UNSUPPORTED, "packed sequences take exact semantics only");
+  return chunk_fwd(q, k, v, g, beta, h0, o, hT, cu_seqlens, n_seqs, T, H, Hk, dk, dv, chunk,
+                   dtype, semantics, workspace, ws_bytes, stream);
 }
 
 }  // extern "C"
@@ -132,11 +148,13 @@ int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v, const float* 
 namespace {
 
 int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
-              const float* h0, void* o, float* hT, int B, int T, int H, int Hk, int dk, int dv,
-              int chunk, int dtype, int semantics, void* workspace, size_t ws_bytes,
-              void* stream) {
+              const float* h0, void* o, float* hT, const int* cu_seqlens, int B, int T, int H,
+              int Hk, int dk, int dv, int chunk, int dtype, int semantics, void* workspace,
+              size_t ws_bytes, void* stream) {
   g_err[0] = '\0';
-  int rc = check_common(q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype);
+  // packed sequences: the token tensors are one row of T tokens, the states B = n_seqs
+  int rc = check_common(q, k, v, g, beta, h0, o, hT, cu_seqlens ? (B > 0 ? 1 : 0) : B, T, H, dk,
+                        dv, dtype);
   if (rc) return rc;
   rc = check_groups(H, Hk);
   if (rc) return rc;
@@ -155,7 +173,7 @@ int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const
     return cuda_status(e, "gdn_chunk_fwd (T=0 state copy)");
   }
   gdn::ChunkArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, chunk, dtype, semantics,
-                   workspace, ws_bytes, Hk};
+                   workspace, ws_bytes, Hk, cu_seqlens};
   // GDN_CHUNK_KERNEL=simt forces the CUDA-core kernel (kernel cross-checks).
   const char* force = getenv("GDN_CHUNK_KERNEL");
   const bool simt_only = force && strcmp(force, "simt") == 0;
@@ -179,6 +197,6 @@ int gdn_device_error(int clear) {
   return a ? a : b;
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 1; }
+int gdn_abi_version(void) { return (1 << 16) | 2; }
 
 }  // extern "C"

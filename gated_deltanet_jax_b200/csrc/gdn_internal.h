@@ -35,6 +35,9 @@ struct ChunkArgs {
   void* workspace;
   size_t ws_bytes;
   int Hk;  // heads of q and k (H % Hk == 0); value head h reads q/k head h * Hk / H
+  // Packed variable-length sequences: B sequences in one row of T tokens, sequence s
+  // being tokens [cu_seqlens[s], cu_seqlens[s + 1]) (device array of B + 1); NULL: dense.
+  const int* cu_seqlens = nullptr;
 };
 
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);

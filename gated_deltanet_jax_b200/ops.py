@@ -27,6 +27,11 @@ Differences from the reference, all additive:
   (H, a multiple of Hk).  Value head h then uses q/k head ``h * Hk // H``,
   which is what the reference layer obtains by ``jnp.repeat`` of q and k
   before calling its ops (model.py:132-135), without the repeated copies.
+* ``cu_seqlens=`` on the chunk op: several sequences packed back to back in
+  one row (q ``[1,T,Hk,dk]`` ...), sequence s being tokens
+  ``cu_seqlens[s]:cu_seqlens[s+1]``, with one state per sequence.  Each
+  sequence gets what a call on it alone gives.  (The reference takes one
+  dense batch only.)
 """
 
 from __future__ import annotations
@@ -45,7 +50,8 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
-def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_state):
+def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_state,
+             n_states=None):
     for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta)):
         if not isinstance(t, torch.Tensor):
             raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
@@ -67,17 +73,22 @@ def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_stat
     if q.dtype not in _DTYPES:
         raise TypeError(f"dtype {q.dtype} not supported (bfloat16 or float32)")
     dev = q.device
+    NS = B if n_states is None else n_states   # states: one per batch row or per sequence
     for name, t in (("k", k), ("v", v), ("g", g), ("beta", beta)):
         if t.device != dev:
             raise ValueError(f"{name} is on {t.device}, q on {dev}")
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     g = g.to(torch.float32).contiguous()
     beta = beta.to(torch.float32).contiguous()
+    # The kernels read 16-byte aligned rows; a view that starts mid-row (e.g. a
+    # token slice of g) is copied into fresh, aligned storage.
+    q, k, v, g, beta = (t if t.data_ptr() % 16 == 0 else t.clone()
+                        for t in (q, k, v, g, beta))
     h0 = None
     if initial_state is not None:
-        if tuple(initial_state.shape) != (B, H, dk, dv):
-            raise ValueError(f"initial_state must be [B,H,dk,dv]=({B},{H},{dk},{dv}); "
-                             f"got {tuple(initial_state.shape)}")
+        if tuple(initial_state.shape) != (NS, H, dk, dv):
+            raise ValueError(f"initial_state must be [{'B' if n_states is None else 'N'},H,dk,dv]"
+                             f"=({NS},{H},{dk},{dv}); got {tuple(initial_state.shape)}")
         if initial_state.device != dev:
             raise ValueError(f"initial_state is on {initial_state.device}, q on {dev}")
         h0 = initial_state
@@ -85,20 +96,21 @@ def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_stat
             h0 = h0.to(torch.float32).contiguous()
     hT = None
     if final_state_out is not None:
-        if (tuple(final_state_out.shape) != (B, H, dk, dv) or final_state_out.dtype != torch.float32
+        if (tuple(final_state_out.shape) != (NS, H, dk, dv) or final_state_out.dtype != torch.float32
                 or not final_state_out.is_contiguous() or final_state_out.device != dev):
             raise ValueError("final_state_out must be a contiguous float32 [B,H,dk,dv] tensor "
                              "on the inputs' device")
         hT = final_state_out
     elif output_final_state:
-        hT = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
+        hT = torch.empty((NS, H, dk, dv), dtype=torch.float32, device=dev)
     o = torch.empty((B, T, H, dv), dtype=v.dtype, device=dev)
     return q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv)
 
 
 def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_final_state=False,
                                chunk_size=64, *, semantics: str = "exact",
-                               final_state_out: Optional[torch.Tensor] = None
+                               final_state_out: Optional[torch.Tensor] = None,
+                               cu_seqlens: Optional[torch.Tensor] = None
                                ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Chunked gated delta rule (reference ``chunk_gated_delta_rule_fwd``, ops.py:299).
 
@@ -106,11 +118,27 @@ def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_fina
     ``final_state_out``) is given, else ``(o, None)`` (ops.py:344-346).
     ``chunk_size`` is 16, 32 or 64.  ``semantics="exact"`` (default) equals the
     recurrence; ``"reference"`` reproduces the reference chunk code as written.
+    ``cu_seqlens`` (integer ``[N+1]``, non-decreasing from 0 to T) packs N
+    sequences into one row: q ``[1,T,Hk,dk]``, states ``[N,H,dk,dv]``.
     """
     if semantics not in _SEMANTICS:
         raise ValueError(f"semantics must be one of {sorted(_SEMANTICS)}; got {semantics!r}")
+    n_seqs = None
+    if cu_seqlens is not None:
+        if not isinstance(cu_seqlens, torch.Tensor) or cu_seqlens.dim() != 1 or \
+                cu_seqlens.numel() < 1 or cu_seqlens.dtype not in (torch.int32, torch.int64):
+            raise ValueError("cu_seqlens must be a 1-D int32/int64 tensor of N+1 offsets")
+        if q.dim() != 4 or q.shape[0] != 1:
+            raise ValueError("with cu_seqlens, q, k, v, g, beta hold one packed row (B == 1)")
+        if semantics != "exact":
+            raise ValueError("packed sequences take semantics='exact' only")
+        if not cu_seqlens.is_cuda:
+            c = cu_seqlens.tolist()
+            if c[0] != 0 or c[-1] != q.shape[1] or any(b < a for a, b in zip(c, c[1:])):
+                raise ValueError(f"cu_seqlens must rise from 0 to T={q.shape[1]}; got {c}")
+        n_seqs = cu_seqlens.numel() - 1
     q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv) = _prepare(
-        q, k, v, g, beta, initial_state, final_state_out, output_final_state)
+        q, k, v, g, beta, initial_state, final_state_out, output_final_state, n_seqs)
     lib = _lib.load()
     dtype = _DTYPES[q.dtype]
     sem = _SEMANTICS[semantics]
@@ -118,7 +146,13 @@ def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_fina
         ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, dk, dv, int(chunk_size), dtype, sem)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        if Hk == H:
+        if n_seqs is not None:
+            cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+            rc = lib.gdn_chunk_fwd_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                                          _ptr(h0), _ptr(o), _ptr(hT), _ptr(cu), n_seqs, T, H, Hk,
+                                          dk, dv, int(chunk_size), dtype, sem, _ptr(ws), ws_bytes,
+                                          stream)
+        elif Hk == H:
             rc = lib.gdn_chunk_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
                                    _ptr(o), _ptr(hT), B, T, H, dk, dv, int(chunk_size), dtype,
                                    sem, _ptr(ws), ws_bytes, stream)

@@ -98,6 +98,23 @@ int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v,
                       int dtype, int semantics,
                       void* workspace, size_t ws_bytes, void* stream);
 
+/*
+ * Packed variable-length sequences for the chunked forward: n_seqs sequences
+ * stored back to back in one row of T tokens -- q, k [1, T, Hk, dk], v, o
+ * [1, T, H, dv], g, beta [1, T, H] -- with sequence s the tokens
+ * [cu_seqlens[s], cu_seqlens[s + 1]) (cu_seqlens: device int32[n_seqs + 1],
+ * non-decreasing from 0 to T; offsets are clamped to [0, T]).  h0 / hT are
+ * [n_seqs, H, dk, dv].  Each sequence gets exactly what gdn_chunk_fwd_gva
+ * gives it on its own.  No counterpart in the reference, whose ops take one
+ * dense [B, T] batch; exact semantics only.
+ */
+int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v,
+                         const float* g, const float* beta,
+                         const float* h0, void* o, float* hT,
+                         const int* cu_seqlens, int n_seqs, int T, int H, int Hk,
+                         int dk, int dv, int chunk, int dtype, int semantics,
+                         void* workspace, size_t ws_bytes, void* stream);
+
 /* Device scratch bytes gdn_chunk_fwd needs for these sizes (0 = none). */
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
                                  int dtype, int semantics);
@@ -115,7 +132,7 @@ int gdn_device_error(int clear);
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
-/* ABI version of this header: (major << 16) | minor (1.1: the _gva entry points). */
+/* ABI version of this header: (major << 16) | minor (1.2: _gva and _varlen entry points). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

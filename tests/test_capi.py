@@ -109,6 +109,18 @@ def test_grouped_heads_reject_bad_groups(lib, H, Hk):
     assert rc == _lib.GDN_ERR_INVALID, lib.gdn_last_error()
 
 
+def test_packed_sequences_reject_bad_arguments(lib):
+    p = ctypes.c_void_p(16)
+    args = lambda cu, n, sem: (p, p, p, p, p, None, p, None, cu, n, 64, 2, 2, 16, 16, 64,
+                               _lib.GDN_DTYPE_BF16, sem, None, 0, None)
+    assert lib.gdn_chunk_fwd_varlen(*args(None, 2, _lib.GDN_SEMANTICS_EXACT)) == _lib.GDN_ERR_INVALID
+    assert lib.gdn_chunk_fwd_varlen(*args(p, -1, _lib.GDN_SEMANTICS_EXACT)) == _lib.GDN_ERR_INVALID
+    assert lib.gdn_chunk_fwd_varlen(*args(ctypes.c_void_p(18), 2, _lib.GDN_SEMANTICS_EXACT)) == \
+        _lib.GDN_ERR_INVALID
+    assert lib.gdn_chunk_fwd_varlen(*args(p, 2, _lib.GDN_SEMANTICS_REFERENCE)) == \
+        _lib.GDN_ERR_UNSUPPORTED
+
+
 def test_empty_problem_is_a_no_op(lib):
     # B*H == 0: nothing to launch, no CUDA call, OK.
     assert _call_recurrent(lib, B=0) == _lib.GDN_OK
