@@ -342,35 +342,74 @@ def decode_leg(d, a, lib, uuid):
                                    "so this is not an HBM-bound figure"}
 
     if not a.no_e2e:
-        # Public API, host buffers: per token H2D of q/k/v/g/beta, op call, D2H of o.
-        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-        hg, hb = g.cpu().pin_memory(), beta.cpu().pin_memory()
+        # Public API with host buffers, driven the way a serving loop drives decode:
+        # the per-token op call is captured once, with its copies, into a CUDA graph
+        # that is replayed every step.  Per token: one H2D copy of the packed
+        # q/k/v/g/beta row from pinned memory (copy stream), the op (compute stream),
+        # one D2H copy of o into pinned memory (second copy stream); inputs are
+        # double-buffered so token t+1's copy and token t-1's readback overlap token
+        # t's kernel.  Every step moves all of its inputs and outputs over PCIe.
+        parts = [q[0], k[0], v[0], g[0], beta[0]]
+        sizes = [x.nbytes for x in parts]
+        offs = [sum(sizes[:i]) for i in range(len(sizes) + 1)]
+        tok_bytes = offs[-1]
+        hin = torch.empty((TOK, tok_bytes), dtype=torch.uint8).pin_memory()
+        for i, src in enumerate((q, k, v, g, beta)):
+            hin[:, offs[i]:offs[i + 1]].copy_(src.reshape(TOK, -1).cpu().view(torch.uint8))
+        din = torch.empty((2, tok_bytes), dtype=torch.uint8, device=d.dev)
+        views = [[din[j, offs[i]:offs[i + 1]].view(parts[i].dtype).view(parts[i].shape)
+                  for i in range(len(parts))] for j in range(2)]
         ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
-        dq, dk_, dv_ = torch.empty_like(q[0]), torch.empty_like(k[0]), torch.empty_like(v[0])
-        dg, db = torch.empty_like(g[0]), torch.empty_like(beta[0])
+        s_in, s_out = torch.cuda.Stream(d.dev), torch.cuda.Stream(d.dev)
 
-        def e2e_step():
+        def e2e_body():
+            cur = torch.cuda.current_stream(d.dev)
+            s_in.wait_stream(cur)
+            s_out.wait_stream(cur)
+            ev_k = [None, None]
+            outs = []
             for t in range(TOK):
-                dq.copy_(hq[t], non_blocking=True)
-                dk_.copy_(hk[t], non_blocking=True)
-                dv_.copy_(hv[t], non_blocking=True)
-                dg.copy_(hg[t], non_blocking=True)
-                db.copy_(hb[t], non_blocking=True)
+                j = t & 1
+                with torch.cuda.stream(s_in):
+                    if ev_k[j] is not None:
+                        s_in.wait_event(ev_k[j])      # token t-2's kernel is done with din[j]
+                    din[j].copy_(hin[t], non_blocking=True)
+                    e_in = torch.cuda.Event()
+                    e_in.record(s_in)
+                cur.wait_event(e_in)
                 st = S[t % NBUF]
-                ot, _ = ops.fused_recurrent_gated_delta_rule(dq, dk_, dv_, dg, db,
-                                                             initial_state=st, final_state_out=st)
-                ho[t].copy_(ot, non_blocking=True)
+                ot, _ = ops.fused_recurrent_gated_delta_rule(*views[j], initial_state=st,
+                                                             final_state_out=st)
+                e_k = torch.cuda.Event()
+                e_k.record(cur)
+                ev_k[j] = e_k
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(e_k)
+                    ho[t].copy_(ot, non_blocking=True)
+                outs.append(ot)                       # no output buffer is reused in a step
+            cur.wait_stream(s_in)
+            cur.wait_stream(s_out)
 
-        for _ in range(min(a.warmup, 2)):
-            e2e_step()
-        e2e_steps = max(1, min(a.steps, 10))
-        ms_e2e, _ = _timed(d, e2e_step, e2e_steps)
-        h2d = TOK * (q[0].nbytes + k[0].nbytes + v[0].nbytes + g[0].nbytes + beta[0].nbytes)
+        e2e_body()                                    # eager once (module loads)
+        torch.cuda.synchronize(d.dev)
+        e2e_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(e2e_graph):
+            e2e_body()
+        for _ in range(a.warmup):
+            e2e_graph.replay()
+        e2e_steps = max(1, min(a.steps, 20))
+        ms_e2e, _ = _timed(d, e2e_graph.replay, e2e_steps)
+        torch.cuda.synchronize(d.dev)
+        del e2e_graph
         res["e2e"] = {"value": d.world * B * TOK / (ms_e2e / 1e3), "unit": "tokens/s",
-                      "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(TOK * o[0].nbytes),
+                      "h2d_bytes_per_step": int(TOK * tok_bytes),
+                      "d2h_bytes_per_step": int(TOK * o[0].nbytes),
                       "steps": e2e_steps,
-                      "path": "ops.fused_recurrent_gated_delta_rule per token, pinned host "
-                              "buffers, state resident on the device"}
+                      "path": "ops.fused_recurrent_gated_delta_rule per token, captured with its "
+                              "copies into a CUDA graph replayed per step: packed q/k/v/g/beta "
+                              "H2D from pinned memory and o D2H into pinned memory every token, "
+                              "on two copy streams overlapping the kernels; state resident on "
+                              "the device"}
     return res
 
 
