@@ -491,7 +491,10 @@ def long_context_leg(d, a):
     v = torch.randn(B, seg, H, dv, device=d.dev, generator=gen).bfloat16()
     g = torch.nn.functional.logsigmoid(torch.randn(B, seg, H, device=d.dev, generator=gen))
     beta = torch.sigmoid(torch.randn(B, seg, H, device=d.dev, generator=gen))
-    local_parts = max(1, LONG["parts"] // d.world)
+    # one GPU: the split is timed against the direct launch below; several GPUs:
+    # segments per GPU chosen so that the second pass fills the GPU
+    local_parts = (LONG["parts"] if d.world == 1 else
+                   sp.auto_local_parts(B, seg, H, dv, C, torch.device(d.dev)))
     if d.world == 1:
         def step():
             sp.chunk_gated_delta_rule_split(q, k, v, g, beta, output_final_state=True,

@@ -74,6 +74,38 @@ def fold_states(h0: torch.Tensor, pairs) -> list:
     return states
 
 
+def fold_states_scan(h0: torch.Tensor, S: torch.Tensor, M: torch.Tensor) -> torch.Tensor:
+    """Same result as :func:`fold_states` in log2(P) rounds of batched products.
+
+    ``S`` [P, ..., dk, dv] and ``M`` [P, ..., dk, dk] are the segments' (S_p, M_p);
+    returns [P + 1, ..., dk, dv]: the state entering each segment and, last, the
+    state after the final one.  Segment p's map x -> M_p x + S_p composed with
+    those before it is built by an inclusive prefix scan (Hillis-Steele): in
+    round d, map i absorbs map i - d, (M_i, S_i) <- (M_i M_{i-d}, M_i S_{i-d} + S_i).
+    """
+    A, C = M, S
+    d = 1
+    P = S.shape[0]
+    while d < P:
+        A_new = torch.cat([A[:d], torch.matmul(A[d:], A[:-d])], dim=0)
+        C = torch.cat([C[:d], torch.matmul(A[d:], C[:-d]) + C[d:]], dim=0)
+        A = A_new
+        d *= 2
+    after = torch.matmul(A, h0.unsqueeze(0)) + C
+    return torch.cat([h0.unsqueeze(0), after], dim=0)
+
+
+def auto_local_parts(B: int, T: int, H: int, dv: int, chunk_size: int, device) -> int:
+    """Segments per GPU so that the second pass fills most SMs: about 0.86 x SMs
+    CTAs (one per (segment, head, 64 columns)), at least 4 chunks per segment."""
+    if not (isinstance(device, torch.device) and device.type == "cuda"):
+        return 1
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    per_part = max(1, B * H * max(1, dv // 64))
+    parts = max(1, round(0.86 * sms / per_part))
+    return max(1, min(parts, T // (4 * chunk_size)))
+
+
 def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, parts, fn,
               gather, world, rank):
     """Both passes over this rank's tokens split into ``parts`` batched segments.
@@ -96,13 +128,12 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
     qs, ks, vs, gs, bs = (to_segments(x) for x in (q, k, v, g, beta))
     S, M = segment_summary(qs, ks, vs, gs, bs, fn)                      # [B*parts, H, ...]
     packed = torch.cat([S, M], dim=-1).view(B, parts, H, dk, dv + dk).contiguous()
-    pairs = [(x[:, p, ..., :dv], x[:, p, ..., dv:]) for x in gather(packed)
-             for p in range(parts)]
+    allp = torch.cat(gather(packed), dim=1).transpose(0, 1)             # [world*parts, B, H, dk, dv+dk]
     h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
           if initial_state is None else initial_state.to(S.dtype))
-    states = fold_states(h0, pairs)
+    states = fold_states_scan(h0, allp[..., :dv], allp[..., dv:])      # [world*parts + 1, ...]
     mine = states[rank * parts:(rank + 1) * parts]
-    s_in = torch.stack(mine, dim=1).reshape(B * parts, H, dk, dv).contiguous()
+    s_in = mine.transpose(0, 1).reshape(B * parts, H, dk, dv).contiguous()
     o, _ = fn(qs, ks, vs, gs, bs, s_in)
     o = o.reshape(B, Tp, H, dv)[:, :T]
     return (o, states[world * parts]) if output_final_state else (o, None)
@@ -110,14 +141,16 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
 
 def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final_state=False,
                               chunk_size=64, group=None, segment_fn: Optional[SegmentFn] = None,
-                              local_parts: int = 1):
+                              local_parts: Optional[int] = None):
     """Chunked forward with the sequence split across the ranks of ``group``.
 
     Every rank passes its own contiguous segment ``[B, T_p, H, D]`` (rank order =
     token order; every rank's T_p is the same, except possibly the last one's).
     Each rank splits its segment again into ``local_parts`` segments that run
-    batched on its GPU; all world x local_parts (S, M) pairs are exchanged in one
-    all-gather, after which every rank folds the prefix locally.
+    batched on its GPU (None: chosen so the second pass fills the GPU, the same
+    on every rank for equal segment lengths); all world x local_parts (S, M)
+    pairs are exchanged in one all-gather, after which every rank folds the
+    prefix locally with a log-depth scan.
     ``initial_state`` is the state before rank 0's segment and must be the same
     on every rank (or None).  Returns ``(o_segment, final_state or None)``;
     ``final_state`` is the state after the LAST segment, on every rank.
@@ -133,6 +166,9 @@ def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final
         dist.all_gather(out, packed, group=group)
         return out
 
+    if local_parts is None:
+        local_parts = auto_local_parts(k.shape[0], k.shape[1], v.shape[2], v.shape[-1],
+                                       chunk_size, k.device)
     return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
                      max(1, int(local_parts)), fn, gather, world, rank)
 
@@ -157,4 +193,4 @@ def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_fi
 
 
 __all__ = ["chunk_gated_delta_rule_sp", "chunk_gated_delta_rule_split", "segment_summary",
-           "fold_states"]
+           "fold_states", "fold_states_scan", "auto_local_parts"]

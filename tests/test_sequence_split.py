@@ -98,6 +98,21 @@ def test_split_cuda_matches_unsplit(cuda, B, T, H, parts):
     assert_close(f64(hT), f64(h_ref), "bf16", "state")
 
 
+@pytest.mark.parametrize("P", [1, 2, 3, 5, 8, 9])
+def test_scan_fold_equals_sequential_fold(P):
+    """The log-depth prefix scan gives the sequential fold's states."""
+    gen = torch.Generator().manual_seed(P)
+    B, H, dk, dv = 2, 3, 8, 5
+    S = torch.randn(P, B, H, dk, dv, generator=gen, dtype=torch.float64)
+    M = torch.randn(P, B, H, dk, dk, generator=gen, dtype=torch.float64) / dk ** 0.5
+    h0 = torch.randn(B, H, dk, dv, generator=gen, dtype=torch.float64)
+    ref = sp.fold_states(h0, [(S[p], M[p]) for p in range(P)])
+    got = sp.fold_states_scan(h0, S, M)
+    assert got.shape[0] == P + 1
+    for p in range(P + 1):
+        torch.testing.assert_close(got[p], ref[p], rtol=1e-10, atol=1e-12)
+
+
 def _nccl_worker(rank, world, port, results):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
