@@ -239,7 +239,8 @@ template <typename Tin, int DVT>
 cudaError_t launch_simt_t(const ChunkArgs& a, cudaStream_t st) {
   const size_t smem = (size_t)simt_layout(a.chunk, a.dk, DVT).total * sizeof(float);
   auto kern = chunk_simt_kernel<Tin, DVT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static std::atomic<int> smem_set[kMaxDevices] = {};
+  cudaError_t e = ensure_smem(kern, (int)smem, smem_set);
   if (e != cudaSuccess) return e;
   dim3 grid(a.dv / DVT, a.B * a.H);
   kern<<<grid, kSimtThreads, smem, st>>>(

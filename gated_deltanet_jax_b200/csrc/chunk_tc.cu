@@ -947,9 +947,7 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   // forces either form (kernel cross-checks).
   const int tiles = a.dv / DVT;
   const long long ctas = (long long)tiles * a.B * a.H;
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sm_count();
   const char* pair_env = getenv("GDN_CHUNK_TC_PAIR");
   bool pair = tiles % 2 == 0 && ctas <= sms / 2;
   if (pair_env && pair_env[0] == '0') pair = false;
@@ -957,11 +955,17 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   auto kernel = pair ? chunk_tc_kernel<true> : chunk_tc_kernel<false>;
   // The in-kernel register split assumes exactly kLaunchRegs per thread at
   // launch; with fewer, the chain warpgroup's increase could never be granted.
-  cudaFuncAttributes fa;
-  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
-  if (e != cudaSuccess) return e;
-  if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  // (Checked, and shared memory opted in, once per device and form.)
+  static std::atomic<int> smem_set[2][kMaxDevices] = {};
+  std::atomic<int>(&slot)[kMaxDevices] = smem_set[pair ? 1 : 0];
+  cudaError_t e = cudaSuccess;
+  if (slot[current_device()].load(std::memory_order_acquire) < SMEM_BYTES) {
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;
+  }
+  e = ensure_smem(kernel, SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.dv / DVT, a.B * a.H);

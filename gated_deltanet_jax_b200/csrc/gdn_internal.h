@@ -4,7 +4,48 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include <atomic>
+
 namespace gdn {
+
+// One-time, per-device host set-up of a kernel (shared-memory opt-in, checks
+// of its compiled attributes), so that a launch does not repeat it.  The
+// set-up is idempotent: two threads racing on a first launch both run it.
+constexpr int kMaxDevices = 64;
+
+inline int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  return dev;
+}
+
+// Shared-memory opt-in of `kernel` to at least `bytes` on the current device.
+// `slot` is the caller's per-kernel cache (largest size set so far, per device).
+template <typename Kernel>
+cudaError_t ensure_smem(Kernel kernel, int bytes, std::atomic<int> (&slot)[kMaxDevices]) {
+  const int dev = current_device();
+  if (slot[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) {
+    int cur = slot[dev].load(std::memory_order_relaxed);
+    while (cur < bytes && !slot[dev].compare_exchange_weak(cur, bytes)) {
+    }
+  }
+  return e;
+}
+
+// Number of SMs of the current device (cached per device).
+inline int device_sm_count() {
+  static std::atomic<int> cache[kMaxDevices] = {};
+  const int dev = current_device();
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
 
 enum DType : int { kFP32 = 0, kBF16 = 1 };
 enum Semantics : int { kExact = 0, kReference = 1 };

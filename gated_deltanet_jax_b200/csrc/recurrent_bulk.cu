@@ -228,26 +228,14 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
   }
 }
 
-int g_num_sms[64] = {0};
-
-int num_sms() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (!g_num_sms[dev]) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
-      n = 148;
-    g_num_sms[dev] = n;
-  }
-  return g_num_sms[dev];
-}
+int num_sms() { return device_sm_count(); }
 
 template <typename Tin, int DK, int DV>
 cudaError_t launch_bulk_t(const RecurrentArgs& a, cudaStream_t st) {
   using L = BulkLayout<Tin, DK, DV>;
   auto kern = recurrent_bulk_kernel<Tin, DK, DV>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
+  static std::atomic<int> smem_set[kMaxDevices] = {};
+  cudaError_t e = ensure_smem(kern, L::total, smem_set);
   if (e != cudaSuccess) return e;
   const int n_units = a.B * a.H;
   const int grid = n_units < num_sms() ? n_units : num_sms();
