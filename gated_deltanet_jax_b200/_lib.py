@@ -30,6 +30,8 @@ EXPORTED_SYMBOLS = (
     "gdn_recurrent_fwd_gva",
     "gdn_chunk_fwd_gva",
     "gdn_chunk_fwd_varlen",
+    "gdn_chunk_bwd",
+    "gdn_chunk_bwd_workspace_bytes",
     "gdn_chunk_workspace_bytes",
     "gdn_last_error",
     "gdn_device_error",
@@ -68,6 +70,10 @@ def _declare(lib):
     lib.gdn_chunk_fwd_varlen.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                          _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.gdn_chunk_fwd_varlen.restype = _i
+    lib.gdn_chunk_bwd.argtypes = [_vp] * 14 + [_i] * 7 + [_vp, _sz, _vp]
+    lib.gdn_chunk_bwd.restype = _i
+    lib.gdn_chunk_bwd_workspace_bytes.argtypes = [_i] * 5
+    lib.gdn_chunk_bwd_workspace_bytes.restype = _sz
     lib.gdn_chunk_workspace_bytes.argtypes = [_i] * 8
     lib.gdn_chunk_workspace_bytes.restype = _sz
     lib.gdn_last_error.argtypes = []

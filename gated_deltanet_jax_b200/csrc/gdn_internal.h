@@ -81,6 +81,30 @@ struct ChunkArgs {
   const int* cu_seqlens = nullptr;
 };
 
+struct ChunkBwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* beta;
+  const float* h0;     // NULL: zero initial state
+  const void* dO;      // gradient of o [B,T,H,dv]
+  const float* dhT;    // gradient of the final state, NULL: zero
+  void* dq;            // [B,T,Hk,dk] input dtype
+  void* dk_out;        // [B,T,Hk,dk] input dtype
+  void* dv_out;        // [B,T,H,dv] input dtype
+  float* dg;           // [B,T,H]
+  float* dbeta;        // [B,T,H]
+  float* dh0;          // [B,H,dk,dv], NULL: not wanted
+  int B, T, H, Hk, dk, dv, dtype;
+  void* workspace;
+  size_t ws_bytes;
+};
+
+size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
+bool chunk_bwd_supported(const ChunkBwdArgs& a);
+cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st);
+
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);
 
 // Decode step (T == 1) with the state streamed by bulk copies (dk = dv = 128).

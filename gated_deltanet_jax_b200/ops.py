@@ -32,6 +32,9 @@ Differences from the reference, all additive:
   ``cu_seqlens[s]:cu_seqlens[s+1]``, with one state per sequence.  Each
   sequence gets what a call on it alone gives.  (The reference takes one
   dense batch only.)
+* Both ops are differentiable (exact semantics, dense inputs): when an input
+  requires grad, the backward runs the gdn_chunk_bwd kernels.  The reference
+  has no backward of its own; it differentiates its chunk path with JAX.
 """
 
 from __future__ import annotations
@@ -107,6 +110,65 @@ def _prepare(q, k, v, g, beta, initial_state, final_state_out, output_final_stat
     return q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv)
 
 
+def _wants_grad(*ts) -> bool:
+    return torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad
+                                           for t in ts)
+
+
+class _DeltaRuleFn(torch.autograd.Function):
+    """Autograd node of both ops (same function: the recurrence, exact semantics)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, h0, chunk_size, recurrent):
+        if recurrent:
+            o, hT = _recurrent_impl(q, k, v, g, beta, h0, True, None)
+        else:
+            o, hT = _chunk_impl(q, k, v, g, beta, h0, True, chunk_size, "exact", None, None)
+        ctx.set_materialize_grads(False)
+        ctx.has_h0 = h0 is not None
+        ctx.in_dtypes = (g.dtype, beta.dtype, None if h0 is None else h0.dtype)
+        ctx.save_for_backward(q, k, v, g, beta, h0)
+        return o, hT
+
+    @staticmethod
+    def backward(ctx, do, dhT):
+        q, k, v, g, beta, h0 = ctx.saved_tensors
+        dq, dk, dv, dg, db, dh0 = _chunk_backward(q, k, v, g, beta, h0, do, dhT)
+        gd, bd, hd = ctx.in_dtypes
+        return (dq, dk, dv, dg.to(gd), db.to(bd), dh0.to(hd) if ctx.has_h0 else None, None,
+                None)
+
+
+def _chunk_backward(q, k, v, g, beta, h0, do, dhT):
+    """Gradients of the recurrence through the C ABI (gdn_chunk_bwd)."""
+    q, k, v, g, beta, h0c, _, _, (B, T, H, Hk, dk, dv) = _prepare(
+        q, k, v, g, beta, h0, None, False)
+    dev = q.device
+    if do is None:
+        do = torch.zeros((B, T, H, dv), dtype=v.dtype, device=dev)
+    do = do.to(v.dtype).contiguous()
+    if do.data_ptr() % 16:
+        do = do.clone()
+    dhT_c = None if dhT is None else dhT.to(torch.float32).contiguous()
+    dq = torch.empty_like(q)
+    dk_ = torch.empty_like(k)
+    dv_ = torch.empty_like(v)
+    dg = torch.empty((B, T, H), dtype=torch.float32, device=dev)
+    db = torch.empty((B, T, H), dtype=torch.float32, device=dev)
+    dh0 = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.gdn_chunk_bwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0c),
+                               _ptr(do), _ptr(dhT_c), _ptr(dq), _ptr(dk_), _ptr(dv_), _ptr(dg),
+                               _ptr(db), _ptr(dh0), B, T, H, Hk, dk, dv, _DTYPES[q.dtype],
+                               _ptr(ws), ws_bytes, stream)
+    _lib.check(rc, "gdn_chunk_bwd")
+    return dq, dk_, dv_, dg, db, dh0
+
+
 def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_final_state=False,
                                chunk_size=64, *, semantics: str = "exact",
                                final_state_out: Optional[torch.Tensor] = None,
@@ -120,7 +182,20 @@ def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_fina
     recurrence; ``"reference"`` reproduces the reference chunk code as written.
     ``cu_seqlens`` (integer ``[N+1]``, non-decreasing from 0 to T) packs N
     sequences into one row: q ``[1,T,Hk,dk]``, states ``[N,H,dk,dv]``.
+    Differentiable (exact semantics, dense inputs) when an input requires grad.
     """
+    if _wants_grad(q, k, v, g, beta, initial_state):
+        if semantics != "exact" or cu_seqlens is not None or final_state_out is not None:
+            raise NotImplementedError("the backward covers exact semantics on dense inputs "
+                                      "without final_state_out")
+        o, hT = _DeltaRuleFn.apply(q, k, v, g, beta, initial_state, int(chunk_size), False)
+        return (o, hT) if output_final_state else (o, None)
+    return _chunk_impl(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
+                       semantics, final_state_out, cu_seqlens)
+
+
+def _chunk_impl(q, k, v, g, beta, initial_state, output_final_state, chunk_size, semantics,
+                final_state_out, cu_seqlens):
     if semantics not in _SEMANTICS:
         raise ValueError(f"semantics must be one of {sorted(_SEMANTICS)}; got {semantics!r}")
     n_seqs = None
@@ -173,7 +248,17 @@ def fused_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None,
     With neither ``initial_state`` nor ``output_final_state`` this is the
     reference call: zero initial state, returns ``(o, None)``.  For decode pass
     ``initial_state=S, final_state_out=S`` to update the state in place.
+    Differentiable (without ``final_state_out``) when an input requires grad.
     """
+    if _wants_grad(q, k, v, g, beta, initial_state):
+        if final_state_out is not None:
+            raise NotImplementedError("the backward does not cover final_state_out")
+        o, hT = _DeltaRuleFn.apply(q, k, v, g, beta, initial_state, 64, True)
+        return (o, hT) if output_final_state else (o, None)
+    return _recurrent_impl(q, k, v, g, beta, initial_state, output_final_state, final_state_out)
+
+
+def _recurrent_impl(q, k, v, g, beta, initial_state, output_final_state, final_state_out):
     q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv) = _prepare(
         q, k, v, g, beta, initial_state, final_state_out, output_final_state)
     lib = _lib.load()

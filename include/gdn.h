@@ -115,6 +115,30 @@ int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v,
                          int dk, int dv, int chunk, int dtype, int semantics,
                          void* workspace, size_t ws_bytes, void* stream);
 
+/*
+ * Gradients of the delta-rule forward (the recurrence, i.e. exact semantics)
+ * with respect to q, k, v, g, beta and the initial state, given the gradient
+ * dO of o and dhT of the final state (NULL = 0).  No counterpart in the
+ * reference, which differentiates its chunk path (ops.py:238-346) with JAX
+ * autodiff; this is the backward of gdn_chunk_fwd_gva / gdn_recurrent_fwd_gva
+ * (ops.py:170-184 with a state carry).  Layouts as the forward's: dq, dk
+ * [B,T,Hk,dk] and dv [B,T,H,dv] in the input dtype, dg, dbeta [B,T,H] and dh0
+ * [B,H,dk,dv] fp32 (dh0 NULL: not wanted).  Needs dk <= 128 and dv a multiple
+ * of 32, and a device workspace of gdn_chunk_bwd_workspace_bytes() (states of
+ * the forward re-run plus fp32 gradient accumulators).  dq and dk are summed
+ * from column tiles with fp32 atomic adds, so their last bits may vary from
+ * run to run.
+ */
+int gdn_chunk_bwd(const void* q, const void* k, const void* v,
+                  const float* g, const float* beta, const float* h0,
+                  const void* dO, const float* dhT,
+                  void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
+                  int B, int T, int H, int Hk, int dk_dim, int dv_dim, int dtype,
+                  void* workspace, size_t ws_bytes, void* stream);
+
+/* Device workspace bytes gdn_chunk_bwd needs for these sizes. */
+size_t gdn_chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
+
 /* Device scratch bytes gdn_chunk_fwd needs for these sizes (0 = none). */
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
                                  int dtype, int semantics);
@@ -132,7 +156,7 @@ int gdn_device_error(int clear);
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
-/* ABI version of this header: (major << 16) | minor (1.2: _gva and _varlen entry points). */
+/* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

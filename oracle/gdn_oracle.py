@@ -192,6 +192,115 @@ def chunk_exact(q, k, v, g, beta, h0=None, chunk_size=64, dtype=np.float64):
     return o, h
 
 
+def chunk_exact_backward(q, k, v, g, beta, h0, do, dhT=None, chunk_size=64, dtype=np.float64):
+    """Gradients of :func:`chunk_exact` (= of the recurrence) by reverse-mode
+    differentiation through its chunked form.  The reference has no backward
+    (it relies on JAX autodiff of its chunk path); this is the restatement the
+    backward kernel is checked against.
+
+    Given do [B,T,H,dv] (gradient of o) and dhT [B,H,dk,dv] (of the final
+    state, None = 0) returns (dq, dk, dv, dg, dbeta, dh0).  Per chunk, with the
+    forward's X = diag(beta)(V - diag(e^G) K h), V' = T X, T = (I + A)^{-1}:
+
+        dV'  = P^T dO + Kd dh_out                    (o, h_out)
+        dX   = T^T dV',   dT = dV' X^T,   dA = -T^T dT T^T  (strictly lower)
+        dh   = e^{G_C} dh_out + Q^T (e^G dO) + K^T dKh,  dKh = -(beta e^G) dX
+        gate terms through e^G, e^{G_i - G_j} and e^{G_C - G}; dg is the reverse
+        in-chunk cumulative sum of dG.
+    """
+    q = np.asarray(q, dtype); k = np.asarray(k, dtype); v = np.asarray(v, dtype)
+    g = np.asarray(g, dtype); beta = np.asarray(beta, dtype); do = np.asarray(do, dtype)
+    B, T, H, dk = k.shape
+    dv = v.shape[-1]
+    C = int(chunk_size)
+    N = max(1, -(-T // C))
+    qc, kc, vc, doc = (_to_chunks(x, C, N) for x in (q, k, v, do))
+    gc, bc = _to_chunks(g, C, N), _to_chunks(beta, C, N)
+    G = np.cumsum(gc, axis=-1)
+    causal = np.tril(np.ones((C, C), dtype=bool))
+    strict = np.tril(np.ones((C, C), dtype=bool), -1)
+    eye = np.eye(C, dtype=dtype)
+    sw = lambda x: np.swapaxes(x, -1, -2)  # noqa: E731
+    # forward, keeping the state entering every chunk
+    h = np.zeros((B, H, dk, dv), dtype) if h0 is None else np.array(h0, dtype)
+    hs = []
+    for n in range(N):
+        hs.append(h)
+        Kn, Vn, Gn, bn = kc[:, :, n], vc[:, :, n], G[:, :, n], bc[:, :, n]
+        E = np.exp(np.where(causal, Gn[..., :, None] - Gn[..., None, :], -np.inf))
+        A = np.where(strict, bn[..., :, None] * (Kn @ sw(Kn)) * E, 0.0)
+        X = bn[..., None] * (Vn - np.exp(Gn)[..., None] * (Kn @ h))
+        Vp = np.linalg.solve(eye + A, X)
+        GC = Gn[..., -1]
+        Kd = Kn * np.exp(GC[..., None] - Gn)[..., None]
+        h = np.exp(GC)[..., None, None] * h + sw(Kd) @ Vp
+    dqc, dkc, dvc = np.zeros_like(qc), np.zeros_like(kc), np.zeros_like(vc)
+    dgc, dbc = np.zeros_like(gc), np.zeros_like(bc)
+    dh = np.zeros((B, H, dk, dv), dtype) if dhT is None else np.array(dhT, dtype)
+    for n in reversed(range(N)):
+        h = hs[n]
+        Qn, Kn, Vn, dOn = qc[:, :, n], kc[:, :, n], vc[:, :, n], doc[:, :, n]
+        Gn, bn = G[:, :, n], bc[:, :, n]
+        eG = np.exp(Gn)
+        E = np.exp(np.where(causal, Gn[..., :, None] - Gn[..., None, :], -np.inf))
+        KK = Kn @ sw(Kn)
+        A = np.where(strict, bn[..., :, None] * KK * E, 0.0)
+        Tm = np.linalg.inv(eye + A)
+        Kh = Kn @ h
+        Qh = Qn @ h
+        X = bn[..., None] * (Vn - eG[..., None] * Kh)
+        Vp = Tm @ X
+        P = np.where(causal, (Qn @ sw(Kn)) * E, 0.0)
+        GC = Gn[..., -1]
+        dec = np.exp(GC[..., None] - Gn)
+        Kd = Kn * dec[..., None]
+        dG = np.zeros_like(Gn)
+        # h_out = e^{G_C} h + Kd^T V'
+        dh_out = dh
+        dVp = Kd @ dh_out
+        dKd = Vp @ sw(dh_out)
+        dGC = np.exp(GC) * np.einsum('bhkv,bhkv->bh', h, dh_out) + np.einsum('bhck,bhck->bh', dKd, Kd)
+        dG -= np.einsum('bhck,bhck->bhc', dKd, Kd)
+        dK = dKd * dec[..., None]
+        dh = np.exp(GC)[..., None, None] * dh_out
+        # o = e^G (Q h) + P V'
+        dVp += sw(P) @ dOn
+        dP = np.where(causal, dOn @ sw(Vp), 0.0)
+        dQ = eG[..., None] * (dOn @ sw(h))
+        dh += sw(Qn) @ (eG[..., None] * dOn)
+        dG += eG * np.einsum('bhcv,bhcv->bhc', dOn, Qh)
+        dPE = dP * E
+        dQ += dPE @ Kn
+        dK += sw(dPE) @ Qn
+        dPP = dP * P
+        dG += dPP.sum(-1) - dPP.sum(-2)
+        # V' = T X
+        dX = sw(Tm) @ dVp
+        dT = dVp @ sw(X)
+        dA = np.where(strict, -sw(Tm) @ dT @ sw(Tm), 0.0)
+        # X = beta (V - e^G K h)
+        dV = bn[..., None] * dX
+        dbeta = np.einsum('bhcv,bhcv->bhc', dX, Vn - eG[..., None] * Kh)
+        dKh = -(bn * eG)[..., None] * dX
+        dG += np.einsum('bhcv,bhcv->bhc', dKh, Kh)
+        dK += dKh @ sw(h)
+        dh += sw(Kn) @ dKh
+        # A = strict(beta_i (K K^T) e^{G_i - G_j})
+        dAE = dA * E
+        dbeta += (dAE * KK).sum(-1)
+        dK += (bn[..., None] * dAE) @ Kn + sw(dAE) @ (bn[..., None] * Kn)
+        dAA = dA * A
+        dG += dAA.sum(-1) - dAA.sum(-2)
+        dG[..., -1] += dGC
+        dgc[:, :, n] = np.cumsum(dG[..., ::-1], axis=-1)[..., ::-1]
+        dqc[:, :, n], dkc[:, :, n], dvc[:, :, n], dbc[:, :, n] = dQ, dK, dV, dbeta
+    unchunk = lambda x: np.moveaxis(x, 1, 3).reshape((B, N * C, H) + x.shape[4:])[:, :T]  # noqa
+    dq, dk_, dv_ = unchunk(dqc), unchunk(dkc), unchunk(dvc)
+    dg = np.moveaxis(dgc, 1, 3).reshape(B, N * C, H)[:, :T]
+    db = np.moveaxis(dbc, 1, 3).reshape(B, N * C, H)[:, :T]
+    return dq, dk_, dv_, dg, db, dh
+
+
 # ---------------------------------------------------------------------------
 # Literal restatement of the reference chunk path (ops.py:238-346)
 # ---------------------------------------------------------------------------

@@ -1,0 +1,105 @@
+"""GPU parity of the backward (gdn_chunk_bwd) against the oracle's reverse-mode
+restatement (itself pinned to torch autograd of the recurrence), and of the
+ops' autograd against it."""
+
+import numpy as np
+import pytest
+import torch
+
+from gated_deltanet_jax_b200 import ops
+from oracle import gdn_oracle as orc
+from helpers import assert_close, device_inputs, f64
+
+pytestmark = pytest.mark.gpu
+
+# Gradients are compared relative to their largest entry: fp32 inputs within
+# 1e-3, bf16 inputs (fp32 state and accumulation) within the bf16 bar 2e-2.
+TOL = {"fp32": 1e-3, "bf16": 2e-2}
+
+
+def _grads(dtype, B, T, H, dk, dv, seed, dev, with_h0=True, with_dhT=True):
+    (q, k, v, g, b, h0), host = device_inputs(B, T, H, dk, dv, seed=seed, dtype=dtype, dev=dev,
+                                              h0_std=0.05 if with_h0 else None)
+    gen = torch.Generator(device=dev).manual_seed(seed + 1)
+    do = torch.randn(B, T, H, dv, device=dev, generator=gen).to(q.dtype)
+    dhT = torch.randn(B, H, dk, dv, device=dev, generator=gen) if with_dhT else None
+    got = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
+    ref = orc.chunk_exact_backward(*host[:5], host[5], f64(do), None if dhT is None else f64(dhT),
+                                   32)
+    return got, ref
+
+
+def _check(got, ref, dtype, with_h0=True):
+    names = ["dq", "dk", "dv", "dg", "dbeta", "dh0"]
+    for n, a, r in zip(names, got, ref):
+        if n == "dh0" and not with_h0:
+            continue
+        err = orc.rel_err(f64(a), r)
+        assert err <= TOL[dtype], f"{n}: rel error {err:.2e}"
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("B,T,H,dk,dv", [(2, 1, 2, 16, 32), (1, 31, 2, 64, 32), (2, 32, 1, 32, 64),
+                                         (1, 33, 2, 128, 64), (2, 100, 3, 64, 96),
+                                         (1, 200, 2, 128, 128)])
+def test_backward_against_oracle(cuda, dtype, B, T, H, dk, dv):
+    got, ref = _grads(dtype, B, T, H, dk, dv, seed=T + dk, dev=cuda)
+    _check(got, ref, dtype)
+
+
+@pytest.mark.parametrize("with_h0,with_dhT", [(False, False), (False, True), (True, False)])
+def test_backward_state_modes(cuda, with_h0, with_dhT):
+    got, ref = _grads("fp32", 1, 70, 2, 32, 32, seed=5, dev=cuda, with_h0=with_h0,
+                      with_dhT=with_dhT)
+    _check(got, ref, "fp32", with_h0=with_h0)
+
+
+def test_backward_grouped_heads(cuda):
+    """q/k with Hk heads: their gradients are the repeated problem's, summed over the group."""
+    B, T, Hk, rep, dk, dv = 1, 90, 2, 3, 64, 32
+    H = Hk * rep
+    (q, k, v, g, b, h0), _ = device_inputs(B, T, H, dk, dv, seed=3, dtype="fp32", dev=cuda,
+                                           h0_std=0.05)
+    qg, kg = q[:, :, ::rep].contiguous(), k[:, :, ::rep].contiguous()
+    qr, kr = qg.repeat_interleave(rep, 2), kg.repeat_interleave(rep, 2)
+    do = torch.randn(B, T, H, dv, device=cuda)
+    dq_g, dk_g, dv_g, dg_g, db_g, dh_g = ops._chunk_backward(qg, kg, v, g, b, h0, do, None)
+    dq_r, dk_r, dv_r, dg_r, db_r, dh_r = ops._chunk_backward(qr, kr, v, g, b, h0, do, None)
+    torch.testing.assert_close(dq_g, dq_r.view(B, T, Hk, rep, dk).sum(3), rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(dk_g, dk_r.view(B, T, Hk, rep, dk).sum(3), rtol=1e-5, atol=1e-5)
+    for a, r in ((dv_g, dv_r), (dg_g, dg_r), (db_g, db_r), (dh_g, dh_r)):
+        torch.testing.assert_close(a, r, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("recurrent", [False, True])
+def test_autograd_through_ops(cuda, recurrent):
+    """loss.backward() through the public ops gives the oracle's gradients."""
+    B, T, H, dk, dv = 2, 45, 2, 32, 32
+    (q, k, v, g, b, h0), host = device_inputs(B, T, H, dk, dv, seed=11, dtype="fp32", dev=cuda,
+                                              h0_std=0.05)
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v, g, b, h0)]
+    fn = ops.fused_recurrent_gated_delta_rule if recurrent else ops.chunk_gated_delta_rule
+    o, hT = fn(*leaves[:5], initial_state=leaves[5], output_final_state=True)
+    gen = torch.Generator(device=cuda).manual_seed(2)
+    do = torch.randn(o.shape, device=cuda, generator=gen)
+    dhT = torch.randn(hT.shape, device=cuda, generator=gen)
+    ((o * do).sum() + (hT * dhT).sum()).backward()
+    ref = orc.chunk_exact_backward(*host[:5], host[5], f64(do), f64(dhT), 32)
+    for t, r in zip(leaves, ref):
+        assert orc.rel_err(f64(t.grad), r) <= TOL["fp32"]
+    # the forward under autograd is the plain forward
+    o2, h2 = fn(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    torch.testing.assert_close(o.detach(), o2)
+    torch.testing.assert_close(hT.detach(), h2)
+
+
+def test_backward_rejects_unsupported(cuda):
+    q = torch.zeros(1, 8, 1, 16, device=cuda, requires_grad=True)
+    g = torch.zeros(1, 8, 1, device=cuda)
+    with pytest.raises(NotImplementedError):
+        ops.chunk_gated_delta_rule(q, q, q, g, g, semantics="reference")
+
+
+def test_no_device_error_recorded_backward(cuda):
+    from gated_deltanet_jax_b200 import _lib
+    assert _lib.load().gdn_device_error(1) == 0

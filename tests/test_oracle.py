@@ -143,3 +143,34 @@ def test_grouped_heads_equal_repeated_recurrence():
     o1, h1 = orc.recurrent_ref(orc.repeat_heads(qg, 3), orc.repeat_heads(kg, 3), v, g, beta, h0)
     o2, h2 = orc.chunk_exact(orc.repeat_heads(qg, 3), orc.repeat_heads(kg, 3), v, g, beta, h0, 16)
     assert orc.max_abs_err(o1, o2) < 1e-12 and orc.max_abs_err(h1, h2) < 1e-12
+
+
+def _torch_recurrence(q, k, v, g, beta, h0):
+    import torch
+    h, outs = h0, []
+    for t in range(k.shape[1]):
+        h = h * torch.exp(g[:, t])[:, :, None, None]
+        proj = torch.einsum('bhk,bhkv->bhv', k[:, t], h)
+        vn = (v[:, t] - proj) * beta[:, t][:, :, None]
+        h = h + k[:, t][:, :, :, None] * vn[:, :, None, :]
+        outs.append(torch.einsum('bhkv,bhk->bhv', h, q[:, t]))
+    return torch.stack(outs, 1), h
+
+
+@pytest.mark.parametrize("shape", [(1, 40, 2, 8, 6, 16), (2, 33, 1, 4, 5, 8), (1, 64, 1, 16, 16, 64),
+                                   (1, 5, 2, 4, 4, 16)])
+def test_backward_matches_autograd_of_recurrence(shape):
+    """chunk_exact_backward == torch autograd (float64) through the token recurrence."""
+    import torch
+    B, T, H, dk, dv, C = shape
+    q, k, v, g, beta, h0 = orc.make_inputs(B, T, H, dk, dv, seed=T, h0_std=0.1)
+    rng = np.random.default_rng(1)
+    do = rng.standard_normal((B, T, H, dv))
+    dhT = rng.standard_normal((B, H, dk, dv))
+    ts = [torch.tensor(x, dtype=torch.float64, requires_grad=True) for x in (q, k, v, g, beta, h0)]
+    o, hT = _torch_recurrence(*ts)
+    ((o * torch.tensor(do)).sum() + (hT * torch.tensor(dhT)).sum()).backward()
+    got = orc.chunk_exact_backward(q, k, v, g, beta, h0, do, dhT, C)
+    for a, t in zip(got, ts):
+        ref = t.grad.numpy()
+        assert np.abs(a - ref).max() <= 1e-12 * max(1.0, np.abs(ref).max())
