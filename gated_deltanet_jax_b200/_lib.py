@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_fwd_gva",
     "gdn_chunk_fwd_varlen",
     "gdn_chunk_bwd",
+    "gdn_chunk_bwd_noalloc",
     "gdn_chunk_bwd_workspace_bytes",
     "gdn_chunk_workspace_bytes",
     "gdn_last_error",
@@ -72,6 +73,8 @@ def _declare(lib):
     lib.gdn_chunk_fwd_varlen.restype = _i
     lib.gdn_chunk_bwd.argtypes = [_vp] * 14 + [_i] * 7 + [_vp, _sz, _vp]
     lib.gdn_chunk_bwd.restype = _i
+    lib.gdn_chunk_bwd_noalloc.argtypes = [_vp] * 14 + [_i] * 7 + [_vp]
+    lib.gdn_chunk_bwd_noalloc.restype = _i
     lib.gdn_chunk_bwd_workspace_bytes.argtypes = [_i] * 5
     lib.gdn_chunk_bwd_workspace_bytes.restype = _sz
     lib.gdn_chunk_workspace_bytes.argtypes = [_i] * 8

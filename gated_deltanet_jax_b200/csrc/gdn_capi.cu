@@ -235,6 +235,32 @@ int gdn_chunk_bwd(const void* q, const void* k, const void* v, const float* g,
   return cuda_status(gdn::launch_chunk_bwd(a, (cudaStream_t)stream), "gdn_chunk_bwd");
 }
 
+int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v, const float* g,
+                          const float* beta, const float* h0, const void* dO, const float* dhT,
+                          void* dq, void* dk_out, void* dv_out, float* dg, float* dbeta,
+                          float* dh0, int B, int T, int H, int Hk, int dk, int dv, int dtype,
+                          void* stream) {
+  // gdn_chunk_bwd with the library's fixed scratch array as its workspace.
+  // The size check comes first and touches no device; gdn_chunk_bwd then
+  // checks everything else and zeroes the accumulators it uses.
+  g_err[0] = '\0';
+  const size_t need = gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv);
+  if (need > GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES)
+    return fail(GDN_ERR_UNSUPPORTED,
+                "these sizes need %zu bytes of backward scratch; the allocation-free entry "
+                "point has a fixed %zu (B*H*T too large: use gdn_chunk_bwd with a workspace)",
+                need, (size_t)GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (need) {
+    const int rc = cuda_status(gdn::chunk_bwd_static_scratch(&scratch),
+                               "gdn_chunk_bwd_noalloc (scratch address)");
+    if (rc) return rc;
+  }
+  return gdn_chunk_bwd(q, k, v, g, beta, h0, dO, dhT, dq, dk_out, dv_out, dg, dbeta, dh0, B, T,
+                       H, Hk, dk, dv, dtype, scratch,
+                       scratch ? (size_t)GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES : 0, stream);
+}
+
 const char* gdn_last_error(void) { return g_err; }
 
 int gdn_device_error(int clear) {

@@ -104,6 +104,9 @@ struct ChunkBwdArgs {
 size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
 bool chunk_bwd_supported(const ChunkBwdArgs& a);
 cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st);
+// Device address of the allocation-free backward's scratch array on the
+// current device (looked up on the first call per device, then kept).
+cudaError_t chunk_bwd_static_scratch(void** out);
 
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);
 

@@ -139,6 +139,40 @@ int gdn_chunk_bwd(const void* q, const void* k, const void* v,
 /* Device workspace bytes gdn_chunk_bwd needs for these sizes. */
 size_t gdn_chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
 
+/*
+ * The backward with no device allocation anywhere: no counterpart in the
+ * reference (which has no backward of its own), an addition for callers that
+ * cannot allocate device memory and cannot pass gdn_chunk_bwd its workspace --
+ * e.g. a jax.ffi handler inside XLA, which keeps most of HBM in its own pool
+ * and hands a custom call only the buffers it declared, or a loop that must
+ * not stop for cudaMalloc, which can synchronise the whole device.
+ *
+ * Arguments and results are gdn_chunk_bwd's, without the workspace: the
+ * caller still passes every input and output.  The scratch is instead a
+ * fixed array of GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES (64 MiB) in this
+ * library's own device memory; sizes whose gdn_chunk_bwd_workspace_bytes()
+ * is larger are rejected with GDN_ERR_UNSUPPORTED (e.g. B*H = 16 heads at
+ * dk = dv = 128 fit up to T = 1344 tokens).  The call itself allocates
+ * nothing: no cudaMalloc, cudaFree or allocating library routine.
+ *
+ * - The array is reserved on a GPU when the driver loads this library's code
+ *   there (CUDA's default lazy loading: at the first call of this entry point
+ *   on that GPU) and held until the process exits.
+ * - The first call on each device also finds the array's address and sets up
+ *   the kernels; make it before any stream capture.
+ * - Every call on a device uses the same array, which keeps the previous
+ *   call's contents (the call zeroes what must start at zero).  Calls that
+ *   overlap on the GPU -- on different streams, or from different threads --
+ *   race on it and give wrong gradients: order them on one stream.
+ */
+#define GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v,
+                          const float* g, const float* beta, const float* h0,
+                          const void* dO, const float* dhT,
+                          void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
+                          int B, int T, int H, int Hk, int dk_dim, int dv_dim, int dtype,
+                          void* stream);
+
 /* Device scratch bytes gdn_chunk_fwd needs for these sizes (0 = none). */
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
                                  int dtype, int semantics);
