@@ -3,488 +3,702 @@
 // The reference has no backward of its own: it relies on JAX autodiff of its
 // chunk path (ops.py:238-346).  This computes the gradients of the recurrence
 // (ops.py:170-184 with an initial / final state) by reverse-mode
-// differentiation through its chunked form, step for step as the oracle's
-// chunk_exact_backward:
+// differentiation through its chunked form, term for term the oracle's
+// chunk_exact_backward, rearranged so that only two or three short products
+// per chunk are sequential.
 //
-//   forward per chunk (C tokens, in-chunk cumulative gate G, state h entering):
-//     A = tril_{-1}(beta_i (K K^T) e^{G_i - G_j}),  T = (I + A)^{-1}
-//     X = diag(beta) (V - diag(e^G) K h),  V' = T X
-//     P = tril_0((Q K^T) e^{G_i - G_j}),   o = diag(e^G) Q h + P V'
-//     h_out = e^{G_C} h + (diag(e^{G_C - G}) K)^T V'
-//   backward per chunk, given dO and dh_out:
-//     dV' = P^T dO + Kd dh_out,  dX = T^T dV',  dT = dV' X^T,  dA = -T^T dT T^T
-//     dh  = e^{G_C} dh_out + Q^T (e^G dO) + K^T dKh,  dKh = -(beta e^G) dX
-//     plus the gate terms through e^G, e^{G_i - G_j} and e^{G_C - G}.
+// Per chunk of C tokens (in-chunk cumulative gate G, gamma = G_C, e = e^G,
+// d = e^{gamma - G}), with T = (I + A)^{-1}, A = tril_{-1}(beta_i K_i.K_j e^{G_i-G_j}),
+// P = tril_0(Q_i.K_j e^{G_i-G_j}) and the state h entering the chunk:
 //
-// One CTA per (b, h, DVT-column tile of the state), internal chunks of CB
-// tokens (the exact result does not depend on the chunk length).  Pass 1 runs
-// the forward over the chunks and stores the state entering each chunk in the
-// workspace; pass 2 walks the chunks in reverse.  Gradients that live in one
-// column tile (dv, dh0) are written directly; dq, dk, dbeta and the gate
-// gradient sum over all columns, so every tile adds its part into fp32
-// accumulators (atomic adds: the order of the tiles' additions, and so the
-// last bits, may vary from run to run).  A second kernel converts them,
-// sums grouped heads, and turns the gradient of the cumulative gate into that
-// of g by a reverse in-chunk cumulative sum.
+//   forward   V' = U - W h,          h_out = e^gamma h + K^T (d V')
+//             W = T diag(beta e) K,   U = T diag(beta) V
+//   backward  dX = Y + Z dh_out,      dh = e^gamma dh_out + Q^T (e dO) - K^T (beta e dX)
+//             Y = T^T P^T dO,         Z = T^T diag(d) K
+//   (dX = T^T dV' is the gradient of X = diag(beta)(V - diag(e) K h), with
+//    dV' = P^T dO + diag(d) K dh_out.)
+//
+// and, per chunk once h, dh_out, V' and dX are known,
+//
+//   dA = -tril_{-1}(dX V'^T), dP = tril_0(dO V'^T), dPE = dP e^{G_i-G_j}, dAE = dA e^{G_i-G_j}
+//   dQ = e (dO h^T) + dPE K
+//   dK = d (V' dh_out^T) - beta e (dX h^T) + dPE^T Q + beta (dAE K) + dAE^T (beta K)
+//   dV = beta dX
+//   dbeta = rowsum(dX o V) - e rowsum(K o dX h^T) + rowsum(dAE o K K^T)
+//   dG = -d rowsum(K o V' dh_out^T) + e rowsum(Q o dO h^T) - beta e rowsum(K o dX h^T)
+//        + rowsum - colsum of (dPE o Q K^T) and of (dAE o beta K K^T)
+//   dG_C += e^gamma <h, dh_out> + sum(d K o V' dh_out^T);  dg = reverse in-chunk cumsum of dG.
+//
+// Launches, in order on the caller's stream:
+//   1. bwd_prep    one CTA per (chunk, value head): T, W, U, Y, Z.
+//   2. bwd_states  one CTA per (32-column state tile, value head, direction):
+//                  the forward pass stores every chunk's entering state and V';
+//                  the reverse pass stores every chunk's dh_out and dX, and dh0.
+//   3. bwd_grads   one CTA per (chunk, value head): every gradient of the chunk.
+//   4. bwd_group   (grouped q/k heads only) sums dq, dk over each head group.
+// All products are fp32 on CUDA cores, from shared memory, each thread owning
+// a strided micro-tile of the output.  Nothing is summed with atomics, so the
+// gradients are the same on every run.
 #include <cstdint>
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
-#include "ptx.cuh"
 
 namespace gdn {
 
 namespace {
 
-constexpr int CB = 32;        // internal chunk length
-constexpr int DVT = 32;       // state columns per CTA
-constexpr int NTB = 256;      // threads
+constexpr int C = 64;        // chunk length (the exact result does not depend on it)
+constexpr int NT = 256;      // threads per CTA
+constexpr int KT = 32;       // dk columns per streamed tile
+constexpr int VT = 32;       // dv columns per streamed tile and per state tile
+constexpr int LC = C + 1;    // odd row strides keep row and column reads conflict-free
+constexpr int LT = VT + 1;
 
-struct BwdSmem {
-  int Q, K, V, dO, H, dH, E, KK, Tm, P, dP, dT, Kh, Qh, X, Vp, dVp, dX, dQ, dK, vec, total;
+struct BwdParams {
+  const void* q; const void* k; const void* v; const void* dO;
+  const float* g; const float* beta; const float* h0; const float* dhT;
+  void* dq; void* dk_out; void* dv_out; float* dg; float* dbeta; float* dh0;
+  // workspace
+  float* W;     // [B*H][Np][dk]
+  float* Z;     // [B*H][Np][dk]
+  float* UV;    // [B*H][Np][dv]      U, then V'
+  float* YX;    // [B*H][Np][dv]      Y, then dX
+  float* hs;    // [B*H][N][dk][dv]   state entering chunk n
+  float* dhs;   // [B*H][N][dk][dv]   gradient of the state leaving chunk n
+  float* dqk;   // [2][B][T][H][dk]   per value head dq, dk (grouped heads only)
+  int B, T, H, Hk, dk, dv, N;
 };
 
-__host__ __device__ inline BwdSmem bwd_layout(int DK) {
-  BwdSmem L{};
-  int o = 0;
-  auto take = [&](int n) { const int r = o; o += (n + 3) & ~3; return r; };
-  L.Q = take(CB * DK); L.K = take(CB * DK);
-  L.V = take(CB * DVT); L.dO = take(CB * DVT);
-  L.H = take(DK * DVT); L.dH = take(DK * DVT);
-  L.E = take(CB * CB); L.KK = take(CB * CB); L.Tm = take(CB * CB); L.P = take(CB * CB);
-  L.dP = take(CB * CB); L.dT = take(CB * CB);
-  L.Kh = take(CB * DVT); L.Qh = take(CB * DVT); L.X = take(CB * DVT); L.Vp = take(CB * DVT);
-  L.dVp = take(CB * DVT); L.dX = take(CB * DVT);
-  L.dQ = take(CB * DK); L.dK = take(CB * DK);
-  L.vec = take(8 * CB);       // G, eG, dec, beta, dG, dbeta, (2 spare)
+// acc[i][j] += sum_{k < K} a(m_i, k) b(k, n_j), m_i = tm + i GM, n_j = tn + j GN, with
+// a(m, k) = TA ? A[k lda + m] : A[m lda + k] and b(k, n) = TB ? B[n ldb + k] : B[k ldb + n].
+// Lanes of a warp take consecutive tn, so with odd row strides every load is
+// conflict-free or a broadcast.
+template <int TM, int TN, int GM, int GN, bool TA, bool TB>
+__device__ __forceinline__ void mac(float (&acc)[TM][TN], const float* A, int lda,
+                                    const float* B, int ldb, int tm, int tn, int K) {
+#pragma unroll 4
+  for (int k = 0; k < K; ++k) {
+    float a[TM], b[TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const int m = tm + i * GM;
+      a[i] = TA ? A[k * lda + m] : A[m * lda + k];
+    }
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int n = tn + j * GN;
+      b[j] = TB ? B[n * ldb + k] : B[k * ldb + n];
+    }
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+  }
+}
+
+template <int TM, int TN>
+__device__ __forceinline__ void zero(float (&acc)[TM][TN]) {
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+}
+
+// Rows t0 .. t0+C-1, columns c0 .. c0+W-1 of one head of a [B, T, heads, D]
+// tensor into shared memory (row stride ld), times rowscale[r] if given;
+// zero past T and past D.
+template <int W, typename Tin>
+__device__ __forceinline__ void load_tokens(float* s, int ld, const Tin* src, size_t bT, int t0,
+                                            int T, int heads, int hd, int D, int c0,
+                                            const float* rowscale) {
+  for (int e = threadIdx.x; e < C * W; e += NT) {
+    const int r = e / W, c = e - r * W, t = t0 + r, col = c0 + c;
+    float x = 0.f;
+    if (t < T && col < D) x = to_f32(src[((bT + t) * heads + hd) * D + col]);
+    s[r * ld + c] = rowscale ? x * rowscale[r] : x;
+  }
+}
+
+// C rows x W columns (from c0) of a row-major [rows][D] fp32 workspace block;
+// zero past D.
+template <int W>
+__device__ __forceinline__ void load_block(float* s, int ld, const float* src, int D, int c0) {
+  for (int e = threadIdx.x; e < C * W; e += NT) {
+    const int r = e / W, c = e - r * W, col = c0 + c;
+    s[r * ld + c] = col < D ? src[(size_t)r * D + col] : 0.f;
+  }
+}
+
+// Gate vectors of one chunk (warp 0): G (inclusive cumulative gate), e^G,
+// e^{gamma - G}, beta, beta e^G.  Tokens past T have g = beta = 0.
+__device__ __forceinline__ void chunk_gates(const BwdParams& p, int b, int h, int t0, float* sG,
+                                            float* se, float* sd, float* sb, float* sbe) {
+  if (threadIdx.x >= 32) return;
+  const int l = threadIdx.x;
+  const size_t base = (size_t)b * p.T;
+  const int ta = t0 + l, tb = t0 + 32 + l;
+  float x0 = ta < p.T ? p.g[(base + ta) * p.H + h] : 0.f;
+  float x1 = tb < p.T ? p.g[(base + tb) * p.H + h] : 0.f;
+  const float b0 = ta < p.T ? p.beta[(base + ta) * p.H + h] : 0.f;
+  const float b1 = tb < p.T ? p.beta[(base + tb) * p.H + h] : 0.f;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
+    const float y1 = __shfl_up_sync(0xffffffffu, x1, o);
+    if (l >= o) { x0 += y0; x1 += y1; }
+  }
+  x1 += __shfl_sync(0xffffffffu, x0, 31);
+  const float gam = __shfl_sync(0xffffffffu, x1, 31);
+  sG[l] = x0; sG[l + 32] = x1;
+  const float e0 = gate_exp(x0), e1 = gate_exp(x1);
+  se[l] = e0; se[l + 32] = e1;
+  sd[l] = gate_exp(gam - x0); sd[l + 32] = gate_exp(gam - x1);
+  sb[l] = b0; sb[l + 32] = b1;
+  sbe[l] = b0 * e0; sbe[l + 32] = b1 * e1;
+}
+
+__device__ __forceinline__ float half_warp_sum(float x) {
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// ---------------------------------------------------------------------------
+// 1. per chunk: T, W, U, Y, Z
+// ---------------------------------------------------------------------------
+constexpr int kPrepSmemFloats = 3 * C * LC + 3 * C * LT + 5 * C;
+
+template <typename Tin>
+__global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
+  extern __shared__ float sm[];
+  float* sA = sm;
+  float* sT = sA + C * LC;
+  float* sP = sT + C * LC;
+  float* s1 = sP + C * LC;
+  float* s2 = s1 + C * LT;
+  float* s3 = s2 + C * LT;
+  float* sG = s3 + C * LT;
+  float* se = sG + C; float* sd = se + C; float* sb = sd + C; float* sbe = sb + C;
+  const Tin* q = static_cast<const Tin*>(p.q);
+  const Tin* k = static_cast<const Tin*>(p.k);
+  const Tin* v = static_cast<const Tin*>(p.v);
+  const Tin* dO = static_cast<const Tin*>(p.dO);
+  const int n = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x;
+  const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
+  const size_t row0 = (size_t)bh * Np + t0;
+  const int tm = tid >> 4, tn = tid & 15;
+  chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
+
+  // Q K^T and K K^T over dk tiles
+  float aQK[4][4], aKK[4][4];
+  zero(aQK); zero(aKK);
+  for (int c0 = 0; c0 < p.dk; c0 += KT) {
+    __syncthreads();
+    load_tokens<KT>(s1, LT, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    __syncthreads();
+    mac<4, 4, 16, 16, false, true>(aQK, s1, LT, s2, LT, tm, tn, KT);
+    mac<4, 4, 16, 16, false, true>(aKK, s2, LT, s2, LT, tm, tn, KT);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = tm + 16 * i, c = tn + 16 * j;
+      const float E = c <= m ? gate_exp(sG[m] - sG[c]) : 0.f;
+      sA[m * LC + c] = c < m ? sb[m] * aKK[i][j] * E : 0.f;
+      sP[m * LC + c] = aQK[i][j] * E;
+    }
+  __syncthreads();
+  // T = (I + A)^{-1} by forward substitution, one column per thread
+  if (tid < C) {
+    const int c = tid;
+    for (int r = 0; r < C; ++r) {
+      float x0 = r == c ? 1.f : 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+      int j = c;
+      for (; j + 3 < r; j += 4) {
+        x0 = fmaf(-sA[r * LC + j], sT[j * LC + c], x0);
+        x1 = fmaf(-sA[r * LC + j + 1], sT[(j + 1) * LC + c], x1);
+        x2 = fmaf(-sA[r * LC + j + 2], sT[(j + 2) * LC + c], x2);
+        x3 = fmaf(-sA[r * LC + j + 3], sT[(j + 3) * LC + c], x3);
+      }
+      for (; j < r; ++j) x0 = fmaf(-sA[r * LC + j], sT[j * LC + c], x0);
+      sT[r * LC + c] = r < c ? 0.f : (x0 + x1) + (x2 + x3);
+    }
+  }
+  // W = T (beta e K), Z = T^T (d K), per dk tile
+  for (int c0 = 0; c0 < p.dk; c0 += KT) {
+    __syncthreads();
+    load_tokens<KT>(s1, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sbe);
+    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sd);
+    __syncthreads();
+    float aw[4][2], az[4][2];
+    zero(aw); zero(az);
+    mac<4, 2, 16, 16, false, false>(aw, sT, LC, s1, LT, tm, tn, C);
+    mac<4, 2, 16, 16, true, false>(az, sT, LC, s2, LT, tm, tn, C);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int m = tm + 16 * i, col = c0 + tn + 16 * j;
+        if (col < p.dk) {
+          p.W[(row0 + m) * p.dk + col] = aw[i][j];
+          p.Z[(row0 + m) * p.dk + col] = az[i][j];
+        }
+      }
+  }
+  // U = T (beta V), Y = T^T (P^T dO), per dv tile
+  for (int c0 = 0; c0 < p.dv; c0 += VT) {
+    __syncthreads();
+    load_tokens<VT>(s1, LT, v, bT, t0, p.T, p.H, h, p.dv, c0, sb);
+    load_tokens<VT>(s2, LT, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    __syncthreads();
+    float au[4][2], ap[4][2];
+    zero(au); zero(ap);
+    mac<4, 2, 16, 16, false, false>(au, sT, LC, s1, LT, tm, tn, C);
+    mac<4, 2, 16, 16, true, false>(ap, sP, LC, s2, LT, tm, tn, C);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int m = tm + 16 * i, c = tn + 16 * j;
+        p.UV[(row0 + m) * p.dv + c0 + c] = au[i][j];
+        s3[m * LT + c] = ap[i][j];
+      }
+    __syncthreads();
+    float ay[4][2];
+    zero(ay);
+    mac<4, 2, 16, 16, true, false>(ay, sT, LC, s3, LT, tm, tn, C);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int m = tm + 16 * i, c = tn + 16 * j;
+        p.YX[(row0 + m) * p.dv + c0 + c] = ay[i][j];
+      }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2. the two sequential passes over the chunks
+// ---------------------------------------------------------------------------
+// Map of a DKP x VT state-tile product onto the 256 threads.
+template <int DKP> struct StateMap;
+template <> struct StateMap<128> { static constexpr int TM = 4, TN = 4, GM = 32, GN = 8; };
+template <> struct StateMap<64> { static constexpr int TM = 4, TN = 2, GM = 16, GN = 16; };
+template <> struct StateMap<32> { static constexpr int TM = 2, TN = 2, GM = 16, GN = 16; };
+
+template <int DKP>
+constexpr int states_smem_floats() {
+  return DKP * VT + C * (DKP + 1) + C * DKP + 2 * C * VT + 5 * C;
+}
+
+template <typename Tin, int DKP>
+__global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
+  using SM = StateMap<DKP>;
+  constexpr int LW = DKP + 1;
+  extern __shared__ float sm[];
+  float* sS = sm;                   // DKP x VT   state (or state gradient) tile
+  float* sM = sS + DKP * VT;        // C x LW     W | Z, then Q
+  float* sK = sM + C * LW;          // C x DKP    K
+  float* sU = sK + C * DKP;         // C x VT     U -> d V'  |  Y -> -beta e dX
+  float* sO = sU + C * VT;          // C x VT     e dO
+  float* sG = sO + C * VT;
+  float* se = sG + C; float* sd = se + C; float* sb = sd + C; float* sbe = sb + C;
+  const Tin* q = static_cast<const Tin*>(p.q);
+  const Tin* k = static_cast<const Tin*>(p.k);
+  const Tin* dO = static_cast<const Tin*>(p.dO);
+  const int c0 = blockIdx.x * VT, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int hq = h * p.Hk / p.H, tid = threadIdx.x;
+  const bool rev = blockIdx.z != 0;
+  const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
+  const int tm = tid >> 4, tn = tid & 15;                    // C x VT products
+  const int rm = tid / SM::GN, rn = tid - rm * SM::GN;       // DKP x VT products
+  const float* init = rev ? p.dhT : p.h0;
+  for (int e = tid; e < DKP * VT; e += NT) {
+    const int r = e / VT, c = e - r * VT;
+    sS[e] = (init && r < p.dk) ? init[((size_t)bh * p.dk + r) * p.dv + c0 + c] : 0.f;
+  }
+  float* keep = rev ? p.dhs : p.hs;
+  for (int it = 0; it < p.N; ++it) {
+    const int n = rev ? p.N - 1 - it : it, t0 = n * C;
+    const size_t row0 = (size_t)bh * Np + t0;
+    __syncthreads();
+    for (int e = tid; e < DKP * VT; e += NT) {
+      const int r = e / VT, c = e - r * VT;
+      if (r < p.dk) keep[(((size_t)bh * p.N + n) * p.dk + r) * p.dv + c0 + c] = sS[e];
+    }
+    load_block<DKP>(sM, LW, (rev ? p.Z : p.W) + row0 * p.dk, p.dk, 0);
+    load_block<VT>(sU, VT, (rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
+    chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
+    if (!rev) load_tokens<DKP>(sK, DKP, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+    __syncthreads();
+    // forward: V' = U - W h;  reverse: dX = Y + Z dh
+    float acc[4][2];
+    zero(acc);
+    mac<4, 2, 16, 16, false, false>(acc, sM, LW, sS, VT, tm, tn, DKP);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int m = tm + 16 * i, c = tn + 16 * j;
+        const float u = sU[m * VT + c];
+        if (!rev) {
+          const float vp = u - acc[i][j];
+          p.UV[(row0 + m) * p.dv + c0 + c] = vp;
+          sU[m * VT + c] = sd[m] * vp;
+        } else {
+          const float dx = u + acc[i][j];
+          p.YX[(row0 + m) * p.dv + c0 + c] = dx;
+          sU[m * VT + c] = -sbe[m] * dx;
+        }
+      }
+    if (rev) {
+      __syncthreads();   // Z in sM has been read; sM now takes Q
+      load_tokens<DKP>(sM, LW, q, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+      load_tokens<DKP>(sK, DKP, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+      load_tokens<VT>(sO, VT, dO, bT, t0, p.T, p.H, h, p.dv, c0, se);
+    }
+    __syncthreads();
+    // forward: h = e^gamma h + K^T (d V');  reverse: dh = e^gamma dh + Q^T (e dO) + K^T (-beta e dX)
+    float accS[SM::TM][SM::TN];
+    zero(accS);
+    mac<SM::TM, SM::TN, SM::GM, SM::GN, true, false>(accS, sK, DKP, sU, VT, rm, rn, C);
+    if (rev) mac<SM::TM, SM::TN, SM::GM, SM::GN, true, false>(accS, sM, LW, sO, VT, rm, rn, C);
+    const float eg = se[C - 1];
+#pragma unroll
+    for (int i = 0; i < SM::TM; ++i)
+#pragma unroll
+      for (int j = 0; j < SM::TN; ++j) {
+        const int r = rm + i * SM::GM, c = rn + j * SM::GN;
+        sS[r * VT + c] = fmaf(eg, sS[r * VT + c], accS[i][j]);
+      }
+  }
+  if (rev && p.dh0) {
+    __syncthreads();
+    for (int e = tid; e < DKP * VT; e += NT) {
+      const int r = e / VT, c = e - r * VT;
+      if (r < p.dk) p.dh0[((size_t)bh * p.dk + r) * p.dv + c0 + c] = sS[e];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3. per chunk: every gradient
+// ---------------------------------------------------------------------------
+constexpr int kGradSmemFloats = 2 * C * LC + 4 * C * LT + 2 * KT * LT + 7 * C + 32;
+
+template <typename Tin>
+__global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
+  extern __shared__ float sm[];
+  float* sPE = sm;                  // C x LC  dP e^{G_i - G_j} (lower, with diagonal)
+  float* sAE = sPE + C * LC;        // C x LC  dA e^{G_i - G_j} (strictly lower)
+  float* s1 = sAE + C * LC;         // C x LT tiles
+  float* s2 = s1 + C * LT;
+  float* s3 = s2 + C * LT;
+  float* s4 = s3 + C * LT;
+  float* sH = s4 + C * LT;          // KT x LT  h tile      [dk row][dv col]
+  float* sD = sH + KT * LT;         // KT x LT  dh_out tile
+  float* sG = sD + KT * LT;
+  float* se = sG + C; float* sd = se + C; float* sb = sd + C; float* sbe = sb + C;
+  float* sdG = sbe + C; float* sdB = sdG + C; float* sred = sdB + C;
+  const Tin* q = static_cast<const Tin*>(p.q);
+  const Tin* k = static_cast<const Tin*>(p.k);
+  const Tin* v = static_cast<const Tin*>(p.v);
+  const Tin* dO = static_cast<const Tin*>(p.dO);
+  const int n = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x;
+  const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
+  const size_t row0 = (size_t)bh * Np + t0;
+  const int tm = tid >> 4, tn = tid & 15;
+  const bool grouped = p.Hk != p.H;
+  chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
+  if (tid < C) { sdG[tid] = 0.f; sdB[tid] = 0.f; }
+
+  // A. dP = dO V'^T and dX V'^T over dv tiles; rowsum(dX o V); dV = beta dX
+  float aP[4][4], aA[4][4];
+  zero(aP); zero(aA);
+  Tin* dv_out = static_cast<Tin*>(p.dv_out);
+  for (int c0 = 0; c0 < p.dv; c0 += VT) {
+    __syncthreads();
+    load_tokens<VT>(s1, LT, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_block<VT>(s2, LT, p.YX + row0 * p.dv, p.dv, c0);
+    load_block<VT>(s3, LT, p.UV + row0 * p.dv, p.dv, c0);
+    load_tokens<VT>(s4, LT, v, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    __syncthreads();
+    mac<4, 4, 16, 16, false, true>(aP, s1, LT, s3, LT, tm, tn, VT);
+    mac<4, 4, 16, 16, false, true>(aA, s2, LT, s3, LT, tm, tn, VT);
+    // one warp per row: 32 columns
+    for (int q8 = 0; q8 < C * VT / NT; ++q8) {
+      const int e = tid + q8 * NT, r = e >> 5, c = e & 31, t = t0 + r;
+      const float dx = s2[r * LT + c];
+      float part = dx * s4[r * LT + c];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (c == 0) sdB[r] += part;
+      if (t < p.T) dv_out[((bT + t) * p.H + h) * p.dv + c0 + c] = from_f32<Tin>(sb[r] * dx);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = tm + 16 * i, c = tn + 16 * j;
+      const float E = c <= m ? gate_exp(sG[m] - sG[c]) : 0.f;
+      sPE[m * LC + c] = aP[i][j] * E;
+      sAE[m * LC + c] = c < m ? -aA[i][j] * E : 0.f;
+    }
+
+  // B. Q K^T and K K^T; the gate and beta terms through P and A
+  float aQK[4][4], aKK[4][4];
+  zero(aQK); zero(aKK);
+  for (int c0 = 0; c0 < p.dk; c0 += KT) {
+    __syncthreads();
+    load_tokens<KT>(s1, LT, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    __syncthreads();
+    mac<4, 4, 16, 16, false, true>(aQK, s1, LT, s2, LT, tm, tn, KT);
+    mac<4, 4, 16, 16, false, true>(aKK, s2, LT, s2, LT, tm, tn, KT);
+  }
+  {
+    float rowg[4] = {0.f, 0.f, 0.f, 0.f}, rowb[4] = {0.f, 0.f, 0.f, 0.f};
+    float colg[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = tm + 16 * i, c = tn + 16 * j;
+        const float pe = sPE[m * LC + c], ae = sAE[m * LC + c];
+        const float x = fmaf(pe, aQK[i][j], ae * sb[m] * aKK[i][j]);
+        rowg[i] += x;
+        colg[j] -= x;
+        rowb[i] = fmaf(ae, aKK[i][j], rowb[i]);
+      }
+    // rows: the 16 lanes of a half warp share a row; columns: 16 row groups
+    // summed in a fixed order (no atomics: the result is the same every run)
+    float* scol = s3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float rg = half_warp_sum(rowg[i]), rb = half_warp_sum(rowb[i]);
+      if (tn == 0) {
+        sdG[tm + 16 * i] += rg;
+        sdB[tm + 16 * i] += rb;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) scol[tm * C + tn + 16 * j] = colg[j];
+    __syncthreads();
+    if (tid < C) {
+      float s = 0.f;
+      for (int r = 0; r < 16; ++r) s += scol[r * C + tid];
+      sdG[tid] += s;
+    }
+  }
+
+  // C. per dk tile: V' dh^T, dO h^T, dX h^T over dv; then dQ, dK and the row terms
+  float rG[4] = {0.f, 0.f, 0.f, 0.f}, rB[4] = {0.f, 0.f, 0.f, 0.f};
+  float rGC = 0.f, rHD = 0.f;
+  const size_t st0 = ((size_t)bh * p.N + n) * p.dk;
+  for (int kt = 0; kt < p.dk; kt += KT) {
+    float aKd[4][2], aQ0[4][2], aM[4][2];
+    zero(aKd); zero(aQ0); zero(aM);
+    for (int c0 = 0; c0 < p.dv; c0 += VT) {
+      __syncthreads();
+      load_tokens<VT>(s1, LT, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+      load_block<VT>(s2, LT, p.YX + row0 * p.dv, p.dv, c0);
+      load_block<VT>(s3, LT, p.UV + row0 * p.dv, p.dv, c0);
+      for (int e = tid; e < KT * VT; e += NT) {
+        const int r = e >> 5, c = e & 31;
+        float hv = 0.f, dhv = 0.f;
+        if (kt + r < p.dk) {
+          const size_t off = (st0 + kt + r) * p.dv + c0 + c;
+          hv = p.hs[off];
+          dhv = p.dhs[off];
+        }
+        sH[r * LT + c] = hv;
+        sD[r * LT + c] = dhv;
+        rHD = fmaf(hv, dhv, rHD);
+      }
+      __syncthreads();
+      mac<4, 2, 16, 16, false, true>(aKd, s3, LT, sD, LT, tm, tn, VT);
+      mac<4, 2, 16, 16, false, true>(aQ0, s1, LT, sH, LT, tm, tn, VT);
+      mac<4, 2, 16, 16, false, true>(aM, s2, LT, sH, LT, tm, tn, VT);
+    }
+    __syncthreads();
+    load_tokens<KT>(s1, LT, q, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT>(s4, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, sb);
+    __syncthreads();
+    float aq[4][2], ak[4][2], ak2[4][2];
+    zero(aq); zero(ak); zero(ak2);
+    mac<4, 2, 16, 16, false, false>(aq, sPE, LC, s2, LT, tm, tn, C);
+    mac<4, 2, 16, 16, true, false>(ak, sPE, LC, s1, LT, tm, tn, C);
+    mac<4, 2, 16, 16, true, false>(ak, sAE, LC, s4, LT, tm, tn, C);
+    mac<4, 2, 16, 16, false, false>(ak2, sAE, LC, s2, LT, tm, tn, C);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = tm + 16 * i, t = t0 + m;
+      const float em = se[m], dm = sd[m], bm = sb[m], bem = sbe[m];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = tn + 16 * j, col = kt + c;
+        const float kv = s2[m * LT + c], qv = s1[m * LT + c];
+        const float dq = fmaf(em, aQ0[i][j], aq[i][j]);
+        const float dkv = dm * aKd[i][j] - bem * aM[i][j] + ak[i][j] + bm * ak2[i][j];
+        rG[i] += -dm * aKd[i][j] * kv + em * aQ0[i][j] * qv - bem * aM[i][j] * kv;
+        rB[i] -= em * aM[i][j] * kv;
+        rGC = fmaf(dm * aKd[i][j], kv, rGC);
+        if (t < p.T && col < p.dk) {
+          if (grouped) {
+            const size_t off = ((bT + t) * p.H + h) * p.dk + col;
+            p.dqk[off] = dq;
+            p.dqk[(size_t)p.B * p.T * p.H * p.dk + off] = dkv;
+          } else {
+            const size_t off = ((bT + t) * p.Hk + hq) * p.dk + col;
+            static_cast<Tin*>(p.dq)[off] = from_f32<Tin>(dq);
+            static_cast<Tin*>(p.dk_out)[off] = from_f32<Tin>(dkv);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float rg = half_warp_sum(rG[i]), rb = half_warp_sum(rB[i]);
+    if (tn == 0) {
+      sdG[tm + 16 * i] += rg;
+      sdB[tm + 16 * i] += rb;
+    }
+  }
+  // dG_C = e^gamma <h, dh_out> + sum(d K o V' dh_out^T)
+  float x = fmaf(se[C - 1], rHD, rGC);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  if ((tid & 31) == 0) sred[tid >> 5] = x;
+  __syncthreads();
+  if (tid < 32) {
+    float y = tid < NT / 32 ? sred[tid] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+    // dg = reverse in-chunk cumulative sum of dG, dG_C added at the last
+    // position (tokens past T add nothing else), two tokens per lane
+    const int l = tid;
+    float x0 = sdG[l], x1 = sdG[l + 32] + (l == 31 ? y : 0.f);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_down_sync(0xffffffffu, x0, o);
+      const float y1 = __shfl_down_sync(0xffffffffu, x1, o);
+      if (l + o < 32) { x0 += y0; x1 += y1; }
+    }
+    x0 += __shfl_sync(0xffffffffu, x1, 0);
+    const int ta = t0 + l, tb = t0 + 32 + l;
+    if (ta < p.T) {
+      p.dg[(bT + ta) * p.H + h] = x0;
+      p.dbeta[(bT + ta) * p.H + h] = sdB[l];
+    }
+    if (tb < p.T) {
+      p.dg[(bT + tb) * p.H + h] = x1;
+      p.dbeta[(bT + tb) * p.H + h] = sdB[l + 32];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 4. grouped q/k heads: dq, dk summed over the value heads of each group
+// ---------------------------------------------------------------------------
+template <typename Tin>
+__global__ void bwd_group_kernel(const BwdParams p) {
+  const int rep = p.H / p.Hk;
+  const size_t total = (size_t)p.B * p.T * p.Hk * p.dk;
+  const size_t plane = (size_t)p.B * p.T * p.H * p.dk;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t d = i % p.dk, bt_hk = i / p.dk;
+    const size_t hk = bt_hk % p.Hk, bt = bt_hk / p.Hk;
+    const size_t src = (bt * p.H + hk * rep) * p.dk + d;
+    float sq = 0.f, sk = 0.f;
+    for (int r = 0; r < rep; ++r) {
+      sq += p.dqk[src + (size_t)r * p.dk];
+      sk += p.dqk[plane + src + (size_t)r * p.dk];
+    }
+    static_cast<Tin*>(p.dq)[i] = from_f32<Tin>(sq);
+    static_cast<Tin*>(p.dk_out)[i] = from_f32<Tin>(sk);
+  }
+}
+
+// Workspace: offsets in floats, each array on a 256-byte boundary.
+struct WsLayout {
+  size_t W, Z, UV, YX, hs, dhs, dqk, total;
+};
+
+WsLayout ws_layout(int B, int T, int H, int dk, int dv) {
+  const size_t N = (size_t)((T + C - 1) / C), Np = N * C, BH = (size_t)B * H;
+  WsLayout L{};
+  size_t o = 0;
+  auto take = [&](size_t n) { const size_t r = o; o += (n + 63) & ~size_t(63); return r; };
+  L.W = take(BH * Np * dk);
+  L.Z = take(BH * Np * dk);
+  L.UV = take(BH * Np * dv);
+  L.YX = take(BH * Np * dv);
+  L.hs = take(BH * N * dk * dv);
+  L.dhs = take(BH * N * dk * dv);
+  L.dqk = take(2 * (size_t)B * T * H * dk);
   L.total = o;
   return L;
 }
 
-// out[m][n] (=|+=) alpha * sum_k a(m, k) b(k, n) over an M x N output, all CTA threads.
-// a(m,k) = TA ? A[k*lda + m] : A[m*lda + k];  b(k,n) = TB ? B[n*ldb + k] : B[k*ldb + n].
-template <bool TA, bool TB>
-__device__ __forceinline__ void smm(float* out, int ldo, const float* A, int lda, const float* B,
-                                    int ldb, int M, int N, int K, float alpha, bool acc) {
-  for (int e = threadIdx.x; e < M * N; e += NTB) {
-    const int m = e / N, n = e - m * N;
-    float s = 0.f;
-    for (int kk = 0; kk < K; ++kk) {
-      const float a = TA ? A[kk * lda + m] : A[m * lda + kk];
-      const float b = TB ? B[n * ldb + kk] : B[kk * ldb + n];
-      s = fmaf(a, b, s);
-    }
-    out[m * ldo + n] = acc ? fmaf(alpha, s, out[m * ldo + n]) : alpha * s;
-  }
-}
-
-template <typename Tin>
-__device__ __forceinline__ float ld(const Tin* p, size_t i) { return to_f32(p[i]); }
-
-// Everything of chunk n that both passes need, recomputed from the inputs and
-// the state entering the chunk (in smem H): G, e^G, e^{G_C - G}, beta, E, KK,
-// T = (I + A)^{-1}, Kh = K h, X, V' = T X.  Returns e^{G_C}.
-template <typename Tin>
-__device__ float chunk_forward(float* sm, const BwdSmem& L, const Tin* q, const Tin* k,
-                               const Tin* v, const float* g, const float* beta, size_t row0,
-                               int t0, int T, int H, int Hk, int h, int DK, int dv, int c0,
-                               bool need_q) {
-  const int tid = threadIdx.x;
-  float* sQ = sm + L.Q; float* sK = sm + L.K; float* sV = sm + L.V;
-  float* sG = sm + L.vec; float* seG = sG + CB; float* sdec = sG + 2 * CB; float* sb = sG + 3 * CB;
-  const int hq = h * Hk / H;
-  for (int e = tid; e < CB * DK; e += NTB) {
-    const int i = e / DK, d = e - i * DK, t = t0 + i;
-    const size_t off = ((row0 + t) * Hk + hq) * DK + d;
-    sK[e] = t < T ? ld(k, off) : 0.f;
-    if (need_q) sQ[e] = t < T ? ld(q, off) : 0.f;
-  }
-  for (int e = tid; e < CB * DVT; e += NTB) {
-    const int i = e / DVT, c = e - i * DVT, t = t0 + i;
-    sV[e] = t < T ? ld(v, ((row0 + t) * H + h) * dv + c0 + c) : 0.f;
-  }
-  if (tid < 32) {
-    // in-chunk inclusive cumulative gate (CB == 32: one token per lane)
-    const int t = t0 + tid;
-    const size_t off = (row0 + t) * H + h;
-    const float gi = t < T ? g[off] : 0.f;
-    float incl = gi;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (tid >= o) incl += y;
-    }
-    const float GC = __shfl_sync(0xffffffffu, incl, 31);
-    sG[tid] = incl;
-    seG[tid] = __expf(incl);
-    sdec[tid] = __expf(GC - incl);
-    sb[tid] = t < T ? beta[off] : 0.f;
-  }
-  __syncthreads();
-  float* sE = sm + L.E; float* sKK = sm + L.KK; float* sT = sm + L.Tm;
-  for (int e = tid; e < CB * CB; e += NTB) {
-    const int i = e / CB, j = e - i * CB;
-    sE[e] = j <= i ? __expf(sG[i] - sG[j]) : 0.f;
-  }
-  smm<false, true>(sKK, CB, sK, DK, sK, DK, CB, CB, DK, 1.f, false);   // K K^T
-  __syncthreads();
-  // A (strictly lower) into dT as scratch, then T = (I + A)^{-1} by substitution
-  float* sA = sm + L.dT;
-  for (int e = tid; e < CB * CB; e += NTB) {
-    const int i = e / CB, j = e - i * CB;
-    sA[e] = j < i ? sb[i] * sKK[e] * sE[e] : 0.f;
-  }
-  __syncthreads();
-  if (tid < CB) {
-    const int c = tid;
-    for (int r = 0; r < CB; ++r) {
-      float s = (r == c) ? 1.f : 0.f;
-      for (int j = c; j < r; ++j) s = fmaf(-sA[r * CB + j], sT[j * CB + c], s);
-      sT[r * CB + c] = r < c ? 0.f : s;
-    }
-  }
-  // Kh = K h
-  float* sKh = sm + L.Kh; float* sH = sm + L.H;
-  smm<false, false>(sKh, DVT, sK, DK, sH, DVT, CB, DVT, DK, 1.f, false);
-  __syncthreads();
-  float* sX = sm + L.X;
-  for (int e = tid; e < CB * DVT; e += NTB) {
-    const int i = e / DVT;
-    sX[e] = sb[i] * (sV[e] - seG[i] * sKh[e]);
-  }
-  __syncthreads();
-  smm<false, false>(sm + L.Vp, DVT, sT, CB, sX, DVT, CB, DVT, CB, 1.f, false);   // V' = T X
-  __syncthreads();
-  return seG[CB - 1];
-}
-
-template <typename Tin>
-__global__ void __launch_bounds__(NTB)
-chunk_bwd_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k, const Tin* __restrict__ v,
-                 const float* __restrict__ g, const float* __restrict__ beta,
-                 const float* __restrict__ h0, const Tin* __restrict__ dO,
-                 const float* __restrict__ dhT, Tin* __restrict__ dv_out,
-                 float* __restrict__ dh0, float* __restrict__ states, float* __restrict__ acc_dq,
-                 float* __restrict__ acc_dk, float* __restrict__ acc_db,
-                 float* __restrict__ acc_dG, int T, int H, int Hk, int DK, int dv) {
-  extern __shared__ float sm[];
-  const BwdSmem L = bwd_layout(DK);
-  const int tid = threadIdx.x;
-  const int bh = blockIdx.y, b = bh / H, h = bh - b * H;
-  const int c0 = blockIdx.x * DVT;
-  const int N = (T + CB - 1) / CB;
-  const size_t row0 = (size_t)b * T;
-  float* sH = sm + L.H; float* sdH = sm + L.dH;
-  float* sK = sm + L.K; float* sQ = sm + L.Q; float* sV = sm + L.V; float* sdO = sm + L.dO;
-  float* sG = sm + L.vec; float* seG = sG + CB; float* sdec = sG + 2 * CB; float* sb = sG + 3 * CB;
-  float* sdG = sG + 4 * CB; float* sdb = sG + 5 * CB;
-
-  // ---- pass 1: forward, storing the state entering every chunk ----
-  for (int e = tid; e < DK * DVT; e += NTB) {
-    const int r = e / DVT, c = e - r * DVT;
-    sH[e] = h0 ? h0[((size_t)bh * DK + r) * dv + c0 + c] : 0.f;
-  }
-  __syncthreads();
-  for (int n = 0; n < N; ++n) {
-    for (int e = tid; e < DK * DVT; e += NTB) {
-      const int r = e / DVT, c = e - r * DVT;
-      states[(((size_t)bh * N + n) * DK + r) * dv + c0 + c] = sH[e];
-    }
-    const float eGC = chunk_forward(sm, L, q, k, v, g, beta, row0, n * CB, T, H, Hk, h, DK, dv,
-                                    c0, false);
-    // h <- e^{G_C} h + Kd^T V'
-    const float* sVp = sm + L.Vp;
-    for (int e = tid; e < DK * DVT; e += NTB) {
-      const int d = e / DVT, c = e - d * DVT;
-      float s = 0.f;
-      for (int i = 0; i < CB; ++i) s = fmaf(sdec[i] * sK[i * DK + d], sVp[i * DVT + c], s);
-      sH[e] = fmaf(eGC, sH[e], s);
-    }
-    __syncthreads();
-  }
-
-  // ---- pass 2: reverse ----
-  for (int e = tid; e < DK * DVT; e += NTB) {
-    const int r = e / DVT, c = e - r * DVT;
-    sdH[e] = dhT ? dhT[((size_t)bh * DK + r) * dv + c0 + c] : 0.f;
-  }
-  __syncthreads();
-  for (int n = N - 1; n >= 0; --n) {
-    const int t0 = n * CB;
-    for (int e = tid; e < DK * DVT; e += NTB) {
-      const int r = e / DVT, c = e - r * DVT;
-      sH[e] = states[(((size_t)bh * N + n) * DK + r) * dv + c0 + c];
-    }
-    for (int e = tid; e < CB * DVT; e += NTB) {
-      const int i = e / DVT, c = e - i * DVT, t = t0 + i;
-      sdO[e] = t < T ? ld(dO, ((row0 + t) * H + h) * dv + c0 + c) : 0.f;
-    }
-    __syncthreads();
-    const float eGC = chunk_forward(sm, L, q, k, v, g, beta, row0, t0, T, H, Hk, h, DK, dv, c0,
-                                    true);
-    float* sE = sm + L.E; float* sKK = sm + L.KK; float* sT = sm + L.Tm; float* sP = sm + L.P;
-    float* sdP = sm + L.dP; float* sdT = sm + L.dT;
-    float* sKh = sm + L.Kh; float* sQh = sm + L.Qh; float* sX = sm + L.X; float* sVp = sm + L.Vp;
-    float* sdVp = sm + L.dVp; float* sdX = sm + L.dX;
-    float* sdQ = sm + L.dQ; float* sdK = sm + L.dK;
-    // P, Qh
-    smm<false, true>(sP, CB, sQ, DK, sK, DK, CB, CB, DK, 1.f, false);
-    smm<false, false>(sQh, DVT, sQ, DK, sH, DVT, CB, DVT, DK, 1.f, false);
-    __syncthreads();
-    for (int e = tid; e < CB * CB; e += NTB) sP[e] *= sE[e];   // E is 0 above the diagonal
-    if (tid < CB) { sdG[tid] = 0.f; sdb[tid] = 0.f; }
-    __syncthreads();
-    // dV' = Kd dh_out + P^T dO
-    for (int e = tid; e < CB * DVT; e += NTB) {
-      const int i = e / DVT, c = e - i * DVT;
-      float s = 0.f;
-      for (int d = 0; d < DK; ++d) s = fmaf(sK[i * DK + d], sdH[d * DVT + c], s);
-      float s2 = 0.f;
-      for (int j = 0; j < CB; ++j) s2 = fmaf(sP[j * CB + i], sdO[j * DVT + c], s2);
-      sdVp[e] = fmaf(sdec[i], s, s2);
-    }
-    // dQ = e^G (dO h^T) ; dK = dec (V' dh_out^T)   (partials of this tile)
-    for (int e = tid; e < CB * DK; e += NTB) {
-      const int i = e / DK, d = e - i * DK;
-      float sq = 0.f, sk = 0.f;
-      for (int c = 0; c < DVT; ++c) {
-        sq = fmaf(sdO[i * DVT + c], sH[d * DVT + c], sq);
-        sk = fmaf(sVp[i * DVT + c], sdH[d * DVT + c], sk);
-      }
-      sdQ[e] = seG[i] * sq;
-      sdK[e] = sdec[i] * sk;
-    }
-    // dP = causal(dO V'^T);  dT = dV' X^T (after dV' is complete)
-    __syncthreads();
-    smm<false, true>(sdP, CB, sdO, DVT, sVp, DVT, CB, CB, DVT, 1.f, false);
-    smm<false, true>(sdT, CB, sdVp, DVT, sX, DVT, CB, CB, DVT, 1.f, false);
-    __syncthreads();
-    // gate terms: dG_C (e^{G_C}<h, dh_out> + sum_i <dKd_i, Kd_i>), -<dKd_i, Kd_i>,
-    // e^{G_i} <dO_i, Qh_i>, row/column sums of dP * P.  dG_C goes to the last real
-    // token of the chunk (padding carries no other gate gradient, so the reverse
-    // cumulative sum is the same as from the padded end).
-    const int last = min(CB, T - t0) - 1;
-    if (tid < 32) {
-      float part = 0.f;
-      for (int e = tid; e < DK * DVT; e += 32) part = fmaf(sH[e], sdH[e], part);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      if (tid == 0) atomicAdd(&sdG[last], eGC * part);
-    }
-    if (tid >= 32 && tid < 32 + CB) {
-      const int i = tid - 32;
-      // <dKd_i, Kd_i> = dec_i * <V'_i dh_out^T, K_i> ... = sum_d dK_i,d(before dec) * dec_i K_i,d
-      float kd = 0.f;
-      for (int d = 0; d < DK; ++d) kd = fmaf(sdK[i * DK + d], sK[i * DK + d], kd);
-      // sdK holds dec_i * (V' dh^T)_i, so <dKd_i, Kd_i> = kd
-      float oq = 0.f;
-      for (int c = 0; c < DVT; ++c) oq = fmaf(sdO[i * DVT + c], sQh[i * DVT + c], oq);
-      float pp = 0.f;
-      for (int j = 0; j <= i; ++j) pp = fmaf(sdP[i * CB + j], sP[i * CB + j], pp);
-      for (int j = i; j < CB; ++j) pp = fmaf(-sdP[j * CB + i], sP[j * CB + i], pp);
-      atomicAdd(&sdG[i], seG[i] * oq + pp - kd);
-      atomicAdd(&sdG[last], kd);
-    }
-    __syncthreads();
-    // dQ += (dP*E) K ; dK += (dP*E)^T Q   (dP*E formed in place: E = 0 above the diagonal)
-    for (int e = tid; e < CB * CB; e += NTB) sdP[e] *= sE[e];
-    __syncthreads();
-    smm<false, false>(sdQ, DK, sdP, CB, sK, DK, CB, DK, CB, 1.f, true);
-    smm<true, false>(sdK, DK, sdP, CB, sQ, DK, CB, DK, CB, 1.f, true);
-    // dX = T^T dV'
-    smm<true, false>(sdX, DVT, sT, CB, sdVp, DVT, CB, DVT, CB, 1.f, false);
-    __syncthreads();
-    // dA = -T^T dT T^T (strictly lower), into dP (free now)
-    smm<true, false>(sdP, CB, sT, CB, sdT, CB, CB, CB, CB, 1.f, false);   // T^T dT
-    __syncthreads();
-    smm<false, true>(sdT, CB, sdP, CB, sT, CB, CB, CB, CB, -1.f, false);  // (T^T dT) T^T
-    __syncthreads();
-    for (int e = tid; e < CB * CB; e += NTB) {
-      const int i = e / CB, j = e - i * CB;
-      if (j >= i) sdT[e] = 0.f;                                          // dA
-    }
-    // dV (this tile, direct), dbeta, dKh = -(beta e^G) dX, gate term <dKh, Kh>
-    for (int e = tid; e < CB * DVT; e += NTB) {
-      const int i = e / DVT, c = e - i * DVT, t = t0 + i;
-      if (t < T)
-        dv_out[((row0 + t) * H + h) * dv + c0 + c] = from_f32<Tin>(sb[i] * sdX[e]);
-    }
-    __syncthreads();
-    if (tid < CB) {
-      const int i = tid;
-      float db = 0.f, gk = 0.f;
-      for (int c = 0; c < DVT; ++c) {
-        const float dx = sdX[i * DVT + c], kh = sKh[i * DVT + c];
-        db = fmaf(dx, sV[i * DVT + c] - seG[i] * kh, db);
-        gk = fmaf(-sb[i] * seG[i] * dx, kh, gk);
-      }
-      sdb[i] += db;
-      sdG[i] += gk;
-    }
-    // dKh into dX (scaled in place)
-    __syncthreads();
-    for (int e = tid; e < CB * DVT; e += NTB) {
-      const int i = e / DVT;
-      sdX[e] *= -sb[i] * seG[i];
-    }
-    __syncthreads();
-    // dK += dKh h^T
-    smm<false, true>(sdK, DK, sdX, DVT, sH, DVT, CB, DK, DVT, 1.f, true);
-    // A-terms: dAE = dA * E;  dbeta_i += sum_j dAE_ij KK_ij;  dG from dA * A
-    for (int e = tid; e < CB * CB; e += NTB) sdP[e] = sdT[e] * sE[e];   // dAE
-    __syncthreads();
-    if (tid < CB) {
-      const int i = tid;
-      float db = 0.f, ga = 0.f;
-      for (int j = 0; j < i; ++j) {
-        const float a = sb[i] * sKK[i * CB + j] * sE[i * CB + j];
-        db = fmaf(sdP[i * CB + j], sKK[i * CB + j], db);
-        ga = fmaf(sdT[i * CB + j], a, ga);
-      }
-      for (int j = i + 1; j < CB; ++j) {
-        const float a = sb[j] * sKK[j * CB + i] * sE[j * CB + i];
-        ga = fmaf(-sdT[j * CB + i], a, ga);
-      }
-      sdb[i] += db;
-      sdG[i] += ga;
-    }
-    // dK += diag(beta) dAE K + dAE^T diag(beta) K
-    for (int e = tid; e < CB * DK; e += NTB) {
-      const int i = e / DK, d = e - i * DK;
-      float s1 = 0.f, s2 = 0.f;
-      for (int j = 0; j < CB; ++j) {
-        s1 = fmaf(sdP[i * CB + j], sK[j * DK + d], s1);
-        s2 = fmaf(sdP[j * CB + i], sb[j] * sK[j * DK + d], s2);
-      }
-      sdK[e] += sb[i] * s1 + s2;
-    }
-    __syncthreads();
-    // dh <- e^{G_C} dh_out + Q^T (e^G dO) + K^T dKh
-    for (int e = tid; e < DK * DVT; e += NTB) {
-      const int d = e / DVT, c = e - d * DVT;
-      float s = 0.f;
-      for (int i = 0; i < CB; ++i)
-        s = fmaf(sQ[i * DK + d], seG[i] * sdO[i * DVT + c], fmaf(sK[i * DK + d], sdX[i * DVT + c], s));
-      sdH[e] = fmaf(eGC, sdH[e], s);
-    }
-    // this tile's parts of dq, dk, dbeta and the cumulative-gate gradient
-    for (int e = tid; e < CB * DK; e += NTB) {
-      const int i = e / DK, d = e - i * DK, t = t0 + i;
-      if (t < T) {
-        const size_t off = ((row0 + t) * H + h) * DK + d;
-        atomicAdd(&acc_dq[off], sdQ[e]);
-        atomicAdd(&acc_dk[off], sdK[e]);
-      }
-    }
-    if (tid < CB && t0 + tid < T) {
-      const size_t off = (row0 + t0 + tid) * H + h;
-      atomicAdd(&acc_db[off], sdb[tid]);
-      atomicAdd(&acc_dG[off], sdG[tid]);
-    }
-    __syncthreads();
-  }
-  for (int e = tid; e < DK * DVT; e += NTB) {
-    const int r = e / DVT, c = e - r * DVT;
-    if (dh0) dh0[((size_t)bh * DK + r) * dv + c0 + c] = sdH[e];
-  }
-}
-
-// dq, dk in the input dtype (value heads of a group summed into their q/k
-// head), dbeta, and dg = reverse in-chunk cumulative sum of the gradient of G.
-template <typename Tin>
-__global__ void chunk_bwd_finish_kernel(const float* __restrict__ acc_dq,
-                                        const float* __restrict__ acc_dk,
-                                        const float* __restrict__ acc_db,
-                                        const float* __restrict__ acc_dG, Tin* __restrict__ dq,
-                                        Tin* __restrict__ dk, float* __restrict__ dg,
-                                        float* __restrict__ dbeta, int B, int T, int H, int Hk,
-                                        int DK) {
-  const int rep = H / Hk;
-  const size_t nqk = (size_t)B * T * Hk * DK;
-  for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < nqk;
-       e += (size_t)gridDim.x * blockDim.x) {
-    const int d = (int)(e % DK);
-    const size_t r = e / DK;                 // (b, t, hk)
-    const int hk = (int)(r % Hk);
-    const size_t bt = r / Hk;
-    float sq = 0.f, sk = 0.f;
-    for (int j = 0; j < rep; ++j) {
-      const size_t off = (bt * H + (size_t)hk * rep + j) * DK + d;
-      sq += acc_dq[off];
-      sk += acc_dk[off];
-    }
-    dq[e] = from_f32<Tin>(sq);
-    dk[e] = from_f32<Tin>(sk);
-  }
-  const size_t nseg = (size_t)B * H * ((T + CB - 1) / CB);
-  for (size_t s = blockIdx.x * (size_t)blockDim.x + threadIdx.x; s < nseg;
-       s += (size_t)gridDim.x * blockDim.x) {
-    const int nch = (T + CB - 1) / CB;
-    const int n = (int)(s % nch);
-    const size_t bhh = s / nch;
-    const int h = (int)(bhh % H);
-    const size_t b = bhh / H;
-    float run = 0.f;
-    const int t_end = min(T, (n + 1) * CB);
-    for (int t = t_end - 1; t >= n * CB; --t) {
-      const size_t off = (b * T + t) * H + h;
-      run += acc_dG[off];
-      dg[off] = run;
-      dbeta[off] = acc_db[off];
-    }
-  }
-}
-
-template <typename Tin>
+template <typename Tin, int DKP>
 cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
-  const BwdSmem L = bwd_layout(a.dk);
-  const size_t smem = (size_t)L.total * sizeof(float);
-  auto kern = chunk_bwd_kernel<Tin>;
-  static std::atomic<int> smem_set[kMaxDevices] = {};
-  cudaError_t e = ensure_smem(kern, (int)smem, smem_set);
-  if (e != cudaSuccess) return e;
+  const WsLayout L = ws_layout(a.B, a.T, a.H, a.dk, a.dv);
   float* ws = static_cast<float*>(a.workspace);
-  const int N = (a.T + CB - 1) / CB;
-  const size_t n_states = (size_t)a.B * a.H * N * a.dk * a.dv;
-  const size_t n_qk = (size_t)a.B * a.T * a.H * a.dk;
-  const size_t n_tok = (size_t)a.B * a.T * a.H;
-  float* states = ws;
-  float* acc_dq = states + n_states;
-  float* acc_dk = acc_dq + n_qk;
-  float* acc_db = acc_dk + n_qk;
-  float* acc_dG = acc_db + n_tok;
-  e = cudaMemsetAsync(acc_dq, 0, sizeof(float) * (2 * n_qk + 2 * n_tok), st);
+  const BwdParams p{a.q, a.k, a.v, a.dO, a.g, a.beta, a.h0, a.dhT, a.dq, a.dk_out, a.dv_out,
+                    a.dg, a.dbeta, a.dh0, ws + L.W, ws + L.Z, ws + L.UV, ws + L.YX,
+                    ws + L.hs, ws + L.dhs, ws + L.dqk, a.B, a.T, a.H, a.Hk, a.dk, a.dv,
+                    (a.T + C - 1) / C};
+  const int BH = a.B * a.H;
+  static std::atomic<int> set_prep[kMaxDevices] = {}, set_states[kMaxDevices] = {},
+                          set_grads[kMaxDevices] = {};
+  const int prep_bytes = kPrepSmemFloats * (int)sizeof(float);
+  const int states_bytes = states_smem_floats<DKP>() * (int)sizeof(float);
+  const int grads_bytes = kGradSmemFloats * (int)sizeof(float);
+  cudaError_t e = ensure_smem(bwd_prep_kernel<Tin>, prep_bytes, set_prep);
+  if (e == cudaSuccess) e = ensure_smem(bwd_states_kernel<Tin, DKP>, states_bytes, set_states);
+  if (e == cudaSuccess) e = ensure_smem(bwd_grads_kernel<Tin>, grads_bytes, set_grads);
   if (e != cudaSuccess) return e;
-  dim3 grid(a.dv / DVT, a.B * a.H);
-  kern<<<grid, NTB, smem, st>>>(
-      static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k), static_cast<const Tin*>(a.v),
-      a.g, a.beta, a.h0, static_cast<const Tin*>(a.dO), a.dhT, static_cast<Tin*>(a.dv_out),
-      a.dh0, states, acc_dq, acc_dk, acc_db, acc_dG, a.T, a.H, a.Hk, a.dk, a.dv);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  const size_t work = n_qk > n_tok ? n_qk : n_tok;
-  const int blocks = (int)((work + 255) / 256 < 8 * 148 ? (work + 255) / 256 : 8 * 148);
-  chunk_bwd_finish_kernel<Tin><<<blocks, 256, 0, st>>>(
-      acc_dq, acc_dk, acc_db, acc_dG, static_cast<Tin*>(a.dq), static_cast<Tin*>(a.dk_out),
-      a.dg, a.dbeta, a.B, a.T, a.H, a.Hk, a.dk);
+  bwd_prep_kernel<Tin><<<dim3(p.N, BH), NT, prep_bytes, st>>>(p);
+  bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, BH, 2), NT, states_bytes, st>>>(p);
+  bwd_grads_kernel<Tin><<<dim3(p.N, BH), NT, grads_bytes, st>>>(p);
+  if (a.Hk != a.H) {
+    const size_t total = (size_t)a.B * a.T * a.Hk * a.dk;
+    const size_t want = (total + 255) / 256, cap = (size_t)8 * device_sm_count();
+    bwd_group_kernel<Tin><<<(int)(want < cap ? want : cap), 256, 0, st>>>(p);
+  }
   return cudaGetLastError();
+}
+
+template <typename Tin>
+cudaError_t launch_bwd_dtype(const ChunkBwdArgs& a, cudaStream_t st) {
+  if (a.dk <= 32) return launch_bwd_t<Tin, 32>(a, st);
+  if (a.dk <= 64) return launch_bwd_t<Tin, 64>(a, st);
+  return launch_bwd_t<Tin, 128>(a, st);
 }
 
 }  // namespace
 
 size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
-  const size_t N = (size_t)((T + CB - 1) / CB);
-  return sizeof(float) * ((size_t)B * H * N * dk * dv + 2 * (size_t)B * T * H * dk +
-                          2 * (size_t)B * T * H);
+  return sizeof(float) * ws_layout(B, T, H, dk, dv).total;
 }
 
 bool chunk_bwd_supported(const ChunkBwdArgs& a) {
-  return a.dv % DVT == 0 && (size_t)bwd_layout(a.dk).total * sizeof(float) <= 200 * 1024;
+  return a.dk >= 1 && a.dk <= 128 && a.dv >= VT && a.dv % VT == 0;
 }
 
 cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
-  return a.dtype == kBF16 ? launch_bwd_t<__nv_bfloat16>(a, st) : launch_bwd_t<float>(a, st);
+  return a.dtype == kBF16 ? launch_bwd_dtype<__nv_bfloat16>(a, st)
+                          : launch_bwd_dtype<float>(a, st);
 }
 
 }  // namespace gdn

@@ -124,10 +124,10 @@ int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v,
  * (ops.py:170-184 with a state carry).  Layouts as the forward's: dq, dk
  * [B,T,Hk,dk] and dv [B,T,H,dv] in the input dtype, dg, dbeta [B,T,H] and dh0
  * [B,H,dk,dv] fp32 (dh0 NULL: not wanted).  Needs dk <= 128 and dv a multiple
- * of 32, and a device workspace of gdn_chunk_bwd_workspace_bytes() (states of
- * the forward re-run plus fp32 gradient accumulators).  dq and dk are summed
- * from column tiles with fp32 atomic adds, so their last bits may vary from
- * run to run.
+ * of 32, and a device workspace of gdn_chunk_bwd_workspace_bytes() (fp32
+ * per-chunk intermediates: the state entering and the state gradient leaving
+ * every chunk, and four [T, dk | dv] products per head).  Deterministic: the
+ * same inputs give the same bits on every run.
  */
 int gdn_chunk_bwd(const void* q, const void* k, const void* v,
                   const float* g, const float* beta, const float* h0,
@@ -152,7 +152,7 @@ size_t gdn_chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
  * fixed array of GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES (64 MiB) in this
  * library's own device memory; sizes whose gdn_chunk_bwd_workspace_bytes()
  * is larger are rejected with GDN_ERR_UNSUPPORTED (e.g. B*H = 16 heads at
- * dk = dv = 128 fit up to T = 1344 tokens).  The call itself allocates
+ * dk = dv = 128 fit up to T = 768 tokens).  The call itself allocates
  * nothing: no cudaMalloc, cudaFree or allocating library routine.
  *
  * - The array is reserved on a GPU when the driver loads this library's code

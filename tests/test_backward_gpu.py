@@ -93,6 +93,24 @@ def test_autograd_through_ops(cuda, recurrent):
     torch.testing.assert_close(hT.detach(), h2)
 
 
+@pytest.mark.parametrize("Hk", [4, 2])
+def test_backward_is_deterministic(cuda, Hk):
+    """No atomics anywhere: the same inputs give the same bits on every call."""
+    B, T, H, dk, dv = 2, 200, 4, 128, 64
+    (q, k, v, g, b, h0), _ = device_inputs(B, T, H, dk, dv, seed=4, dtype="bf16", dev=cuda,
+                                           h0_std=0.05)
+    rep = H // Hk
+    q, k = q[:, :, ::rep].contiguous(), k[:, :, ::rep].contiguous()
+    gen = torch.Generator(device=cuda).manual_seed(9)
+    do = torch.randn(B, T, H, dv, device=cuda, generator=gen).bfloat16()
+    dhT = torch.randn(B, H, dk, dv, device=cuda, generator=gen)
+    first = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
+    for _ in range(2):
+        again = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
+        for a, r in zip(again, first):
+            assert torch.equal(a, r)
+
+
 def test_backward_rejects_unsupported(cuda):
     q = torch.zeros(1, 8, 1, 16, device=cuda, requires_grad=True)
     g = torch.zeros(1, 8, 1, device=cuda)
