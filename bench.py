@@ -5,7 +5,8 @@ decode workload -- B=64, H=16, dk=dv=128, bf16 q/k/v, fp32 state ~N(0,0.02),
 one bench step = 512 consecutive single-token decode steps with the state
 updated in place (512 kernel launches, replayed as one CUDA graph).  The
 ``prefill`` object in the same line reports chunked prefill tokens/s on B=4,
-T=4096, H=16, dk=dv=128, chunk=64, bf16 in / fp32 state (one launch per step).
+T=4096, H=16, dk=dv=128, chunk=64, bf16 in / fp32 state (one launch per step);
+``long_context`` B=1 T=65536; ``backward`` the gradients on the prefill workload.
 
 Multi-GPU (torchrun, one rank per GPU): batch x head work is independent, so
 every rank runs its own full workload (weak scaling, no collective on the
@@ -48,6 +49,7 @@ def _args():
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end legs")
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill leg")
     p.add_argument("--no-long", action="store_true", help="skip the long-context leg")
+    p.add_argument("--no-backward", action="store_true", help="skip the backward leg")
     return p.parse_args()
 
 
@@ -287,7 +289,7 @@ def _timed(d, fn, steps, sampler=None):
 def decode_leg(d, a, lib, uuid):
     import torch
     from gated_deltanet_jax_b200 import _lib, ops
-    from oracle import gdn_oracle as orc
+    from gated_deltanet_jax_b200 import roofline as rl
     B, H, dk, dv, TOK = DEC["B"], DEC["H"], DEC["dk"], DEC["dv"], DEC["tokens"]
     gen = torch.Generator(device=d.dev)
     gen.manual_seed(1234 + d.rank)
@@ -328,7 +330,7 @@ def decode_leg(d, a, lib, uuid):
     ms, clocks = _timed(d, graph.replay, a.steps, sampler)
     del graph
     value = d.world * B * TOK / (ms / 1e3)
-    bytes_launch = B * H * orc.bytes_recurrent_per_head_step(dk, dv, 2)
+    bytes_launch = B * H * rl.bytes_recurrent_per_head_step(dk, dv, 2)
     launch_s = ms / 1e3 / TOK
     res = {"ms": ms, "value": value, "clocks": clocks, "launch_s": launch_s,
            "bytes_launch": bytes_launch, "launches": a.steps * TOK}
@@ -416,7 +418,7 @@ def decode_leg(d, a, lib, uuid):
 def prefill_leg(d, a, lib, uuid=None):
     import torch
     from gated_deltanet_jax_b200 import _lib, ops
-    from oracle import gdn_oracle as orc
+    from gated_deltanet_jax_b200 import roofline as rl
     B, T, H, dk, dv, C = (PRE[x] for x in ("B", "T", "H", "dk", "dv", "chunk"))
     gen = torch.Generator(device=d.dev)
     gen.manual_seed(99 + d.rank)
@@ -445,10 +447,10 @@ def prefill_leg(d, a, lib, uuid=None):
     steps = max(a.steps, 1000)
     sampler = ClockSampler(uuid) if d.rank == 0 else None
     ms, clocks = _timed(d, step, steps, sampler)
-    flops = B * T * H * orc.flops_chunk_per_token_head(dk, dv, C)
+    flops = B * T * H * rl.flops_chunk_per_token_head(dk, dv, C)
     res = {"ms": ms, "value": d.world * B * T / (ms / 1e3), "flops_launch": flops,
            "launch_s": ms / 1e3, "launches": steps, "steps": steps, "clocks": clocks,
-           "bytes_launch": B * T * H * orc.bytes_chunk_per_token_head(dk, dv) + B * H * dk * dv * 4}
+           "bytes_launch": B * T * H * rl.bytes_chunk_per_token_head(dk, dv) + B * H * dk * dv * 4}
     if not a.no_e2e:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         hg, hb = g.cpu().pin_memory(), beta.cpu().pin_memory()
@@ -474,13 +476,58 @@ def prefill_leg(d, a, lib, uuid=None):
     return res
 
 
+def backward_leg(d, a, lib):
+    """The chunked backward (gdn_chunk_bwd) on the prefill workload: gradients of
+    q, k, v, g, beta from dO, every buffer resident, one C-ABI call per step."""
+    import torch
+    from gated_deltanet_jax_b200 import _lib, roofline as rl
+    B, T, H, dk, dv, C = (PRE[x] for x in ("B", "T", "H", "dk", "dv", "chunk"))
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(199 + d.rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    k = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, device=d.dev, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, T, H, device=d.dev, generator=gen))
+    do = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
+    dq, dk_, dv_ = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg, db = torch.empty_like(g), torch.empty_like(beta)
+    ws_bytes = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=d.dev)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        rc = lib.gdn_chunk_bwd(ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), None, ptr(do), None,
+                               ptr(dq), ptr(dk_), ptr(dv_), ptr(dg), ptr(db), None,
+                               B, T, H, H, dk, dv, _lib.GDN_DTYPE_BF16, ptr(ws), ws_bytes,
+                               ctypes.c_void_p(torch.cuda.current_stream(d.dev).cuda_stream))
+        if rc:
+            _lib.check(rc, "gdn_chunk_bwd")
+
+    for _ in range(a.warmup):
+        step()
+    steps = max(1, min(a.steps, 30))
+    ms, _ = _timed(d, step, steps)
+    flops = B * T * H * rl.flops_chunk_bwd_per_token_head(dk, dv, C)
+    return {"metric": "chunk backward tokens/s", "value": d.world * B * T / (ms / 1e3),
+            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "launches": 3 * steps,
+            "config": {"workload": "gradients of q, k, v, g, beta for B=4 T=4096 H=16 "
+                                   "dk=dv=128, bf16 in, from a bf16 dO, no initial state",
+                       "l2": f"inputs and {ws_bytes / 1e9:.2f} GB of workspace, larger than L2",
+                       "path": "gdn_chunk_bwd: prep, state passes, gradients (3 launches)"},
+            "algorithmic_flops_per_step": flops,
+            "achieved_tflops": flops / (ms / 1e3) / 1e12,
+            "compute": "fp32 FMA on CUDA cores"}
+
+
 def long_context_leg(d, a):
     """B=1, T=65536, H=16 over all ranks (strong scaling: the sequence is split
     evenly across ranks, the state handed off by an NCCL all-gather), each rank's
     segment split again into parts on its GPU."""
     import torch
     from gated_deltanet_jax_b200 import ops, sequence_parallel as sp
-    from oracle import gdn_oracle as orc
+    from gated_deltanet_jax_b200 import roofline as rl
     B, T, H, dk, dv, C = (LONG[x] for x in ("B", "T", "H", "dk", "dv", "chunk"))
     seg = T // d.world
     gen = torch.Generator(device=d.dev)
@@ -521,7 +568,7 @@ def long_context_leg(d, a):
         extra = {"split_ms_per_step": ms, "unsplit_ms_per_step": ms_d}
         if ms_d < ms:
             ms, path = ms_d, "one launch (no split)"
-    flops = T * H * orc.flops_chunk_per_token_head(dk, dv, C)
+    flops = T * H * rl.flops_chunk_per_token_head(dk, dv, C)
     res = {"metric": "long-context chunk prefill tokens/s", "value": B * T / (ms / 1e3),
            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
            "config": {"workload": f"B=1 T={T} H=16 dk=dv=128 chunk=64 bf16, final state out",
@@ -551,6 +598,7 @@ def main():
     dec = decode_leg(d, a, lib, uuid)
     pre = None if a.no_prefill else prefill_leg(d, a, lib, uuid)
     lng = None if a.no_long else long_context_leg(d, a)
+    bwd = None if a.no_backward else backward_leg(d, a, lib)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not a.no_cpu:
@@ -578,7 +626,8 @@ def main():
                          "frac": ach / hbm, "peak_source": f"{peak_src} hbm_gbs",
                          "traffic": traffic,
                          "algorithmic_bytes_per_launch": dec["bytes_launch"]},
-            "gpu_launches": dec["launches"] + (pre["launches"] if pre else 0),
+            "gpu_launches": (dec["launches"] + (pre["launches"] if pre else 0)
+                             + (bwd["launches"] if bwd else 0)),
             "clocks": dec["clocks"],
         }
         if "e2e" in dec:
@@ -608,6 +657,11 @@ def main():
             line["prefill"] = pre_line
         if lng:
             line["long_context"] = lng
+        if bwd:
+            if pre:
+                bwd["fwd_plus_bwd_tokens_per_s"] = (d.world * PRE["B"] * PRE["T"]
+                                                    / ((pre["ms"] + bwd["ms_per_step"]) / 1e3))
+            line["backward"] = bwd
         print(json.dumps(line), flush=True)
     d.close()
 

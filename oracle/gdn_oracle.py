@@ -489,31 +489,10 @@ def within_tolerance(out, ref, input_dtype: str) -> Tuple[bool, float]:
     return e <= TOL_BF16_REL, e
 
 
-def flops_chunk_per_token_head(dk: int, dv: int, C: int) -> int:
-    """Algorithmic FLOP per token-head of the chunked forward.
-
-    KK^T, W and QK^T over dk; U and P V' over dv (2 C (3 dk + 2 dv)), plus
-    W h, Q h and K^T V' (6 dk dv).  The O(C^2) triangular solve is excluded.
-    """
-    return 2 * C * (3 * dk + 2 * dv) + 6 * dk * dv
-
-
-def bytes_recurrent_per_head_step(dk: int, dv: int, in_bytes: int = 2) -> int:
-    """HBM bytes per head-step of the decode kernel: fp32 state read + write,
-    q/k/v in, o out (input dtype), fp32 g and beta."""
-    return 8 * dk * dv + (2 * dk + dv) * in_bytes + dv * in_bytes + 8
-
-
-def bytes_chunk_per_token_head(dk: int, dv: int, in_bytes: int = 2) -> int:
-    """HBM bytes per token-head of the chunked forward (q/k/v in, o out, g/beta)."""
-    return (2 * dk + dv) * in_bytes + dv * in_bytes + 8
-
-
 __all__ = [
     "make_inputs", "round_bf16", "recurrent_ref", "chunk_exact",
     "chunk_reference_literal", "literal_output_permutation", "segment_transition",
     "two_pass_sp", "TOL_FP32_ABS", "TOL_BF16_REL", "max_abs_err", "rel_err",
-    "within_tolerance", "flops_chunk_per_token_head", "bytes_recurrent_per_head_step",
-    "bytes_chunk_per_token_head",
+    "within_tolerance",
 ]
 

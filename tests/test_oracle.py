@@ -122,9 +122,11 @@ def test_tolerance_rules():
 
 
 def test_work_accounting():
-    assert orc.flops_chunk_per_token_head(128, 128, 64) == 180224
-    assert orc.bytes_chunk_per_token_head(128, 128) == 1032
-    assert orc.bytes_recurrent_per_head_step(128, 128) == 132104
+    from gated_deltanet_jax_b200 import roofline as rl
+    assert rl.flops_chunk_per_token_head(128, 128, 64) == 180224
+    assert rl.flops_chunk_bwd_per_token_head(128, 128, 64) == 507904
+    assert rl.bytes_chunk_per_token_head(128, 128) == 1032
+    assert rl.bytes_recurrent_per_head_step(128, 128) == 132104
 
 
 def test_repeat_heads_matches_layer_expansion():
