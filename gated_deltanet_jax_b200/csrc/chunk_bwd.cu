@@ -60,14 +60,14 @@ struct BwdParams {
   const float* g; const float* beta; const float* h0; const float* dhT;
   void* dq; void* dk_out; void* dv_out; float* dg; float* dbeta; float* dh0;
   // workspace
-  float* W;     // [B*H][Np][dk]
-  float* Z;     // [B*H][Np][dk]
+  float* W;     // [B*H][Np][ldw]     ldw = dk rounded up to 32, zero past dk
+  float* Z;     // [B*H][Np][ldw]
   float* UV;    // [B*H][Np][dv]      U, then V'
   float* YX;    // [B*H][Np][dv]      Y, then dX
   float* hs;    // [B*H][N][dk][dv]   state entering chunk n
   float* dhs;   // [B*H][N][dk][dv]   gradient of the state leaving chunk n
   float* dqk;   // [2][B][T][H][dk]   per value head dq, dk (grouped heads only)
-  int B, T, H, Hk, dk, dv, N;
+  int B, T, H, Hk, dk, dv, N, ldw;
 };
 
 // acc[i][j] += sum_{k < K} a(m_i, k) b(k, n_j), m_i = tm + i GM, n_j = tn + j GN, with
@@ -105,28 +105,83 @@ __device__ __forceinline__ void zero(float (&acc)[TM][TN]) {
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 }
 
-// Rows t0 .. t0+C-1, columns c0 .. c0+W-1 of one head of a [B, T, heads, D]
-// tensor into shared memory (row stride ld), times rowscale[r] if given;
-// zero past T and past D.
-template <int W, typename Tin>
-__device__ __forceinline__ void load_tokens(float* s, int ld, const Tin* src, size_t bT, int t0,
-                                            int T, int heads, int hd, int D, int c0,
-                                            const float* rowscale) {
-  for (int e = threadIdx.x; e < C * W; e += NT) {
-    const int r = e / W, c = e - r * W, t = t0 + r, col = c0 + c;
-    float x = 0.f;
-    if (t < T && col < D) x = to_f32(src[((bT + t) * heads + hd) * D + col]);
-    s[r * ld + c] = rowscale ? x * rowscale[r] : x;
+// Four or eight input elements (16 bytes) as fp32.
+template <typename Tin> __device__ __forceinline__ void unpack16(const uint4& u, float* f);
+template <> __device__ __forceinline__ void unpack16<float>(const uint4& u, float* f) {
+  f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+  f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+}
+template <> __device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
   }
 }
 
-// C rows x W columns (from c0) of a row-major [rows][D] fp32 workspace block;
-// zero past D.
-template <int W>
-__device__ __forceinline__ void load_block(float* s, int ld, const float* src, int D, int c0) {
-  for (int e = threadIdx.x; e < C * W; e += NT) {
-    const int r = e / W, c = e - r * W, col = c0 + c;
-    s[r * ld + c] = col < D ? src[(size_t)r * D + col] : 0.f;
+// VE consecutive floats into shared memory at dst (16-byte stores when the
+// row stride LD keeps them aligned).
+template <int LD, int VE>
+__device__ __forceinline__ void put_row(float* dst, const float* f, float sc) {
+  if constexpr (LD % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < VE; j += 4)
+      *reinterpret_cast<float4*>(dst + j) =
+          make_float4(f[j] * sc, f[j + 1] * sc, f[j + 2] * sc, f[j + 3] * sc);
+  } else {
+#pragma unroll
+    for (int j = 0; j < VE; ++j) dst[j] = f[j] * sc;
+  }
+}
+
+// Rows t0 .. t0+C-1, columns c0 .. c0+W-1 of one head of a [B, T, heads, D]
+// input into shared memory (row stride LD), times rowscale[r] if given; zero
+// past T and past D.  Every load of the thread is issued before the first
+// store, as 16-byte vectors (inputs are 16-byte aligned and D is a multiple of
+// 8 elements).
+template <int W, int LD, typename Tin>
+__device__ __forceinline__ void load_tokens(float* s, const Tin* src, size_t bT, int t0, int T,
+                                            int heads, int hd, int D, int c0,
+                                            const float* rowscale) {
+  constexpr int VE = 16 / (int)sizeof(Tin), PR = W / VE, NV = C * PR / NT;
+  static_assert(W % VE == 0 && (C * PR) % NT == 0, "tile must split evenly into vectors");
+  uint4 raw[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int e = threadIdx.x + i * NT, r = e / PR, col = c0 + (e - r * PR) * VE, t = t0 + r;
+    raw[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (t < T && col < D)
+      raw[i] = __ldg(reinterpret_cast<const uint4*>(src + ((bT + t) * heads + hd) * D + col));
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int e = threadIdx.x + i * NT, r = e / PR, cv = (e - r * PR) * VE;
+    float f[VE];
+    unpack16<Tin>(raw[i], f);
+    put_row<LD, VE>(s + r * LD + cv, f, rowscale ? rowscale[r] : 1.f);
+  }
+}
+
+// C rows x W columns (from c0) of a row-major [rows][D] fp32 workspace block
+// (D a multiple of 4, 16-byte aligned rows); zero past D.  Loads first, as in
+// load_tokens.
+template <int W, int LD>
+__device__ __forceinline__ void load_block(float* s, const float* src, int D, int c0) {
+  constexpr int PR = W / 4, NV = C * PR / NT;
+  static_assert((C * PR) % NT == 0, "tile must split evenly into vectors");
+  float4 raw[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int e = threadIdx.x + i * NT, r = e / PR, col = c0 + (e - r * PR) * 4;
+    raw[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col < D) raw[i] = *reinterpret_cast<const float4*>(src + (size_t)r * D + col);
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int e = threadIdx.x + i * NT, r = e / PR, cv = (e - r * PR) * 4;
+    const float f[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+    put_row<LD, 4>(s + r * LD + cv, f, 1.f);
   }
 }
 
@@ -196,8 +251,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   zero(aQK); zero(aKK);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
-    load_tokens<KT>(s1, LT, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
-    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
     __syncthreads();
     mac<4, 4, 16, 16, false, true>(aQK, s1, LT, s2, LT, tm, tn, KT);
     mac<4, 4, 16, 16, false, true>(aKK, s2, LT, s2, LT, tm, tn, KT);
@@ -228,11 +283,11 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
       sT[r * LC + c] = r < c ? 0.f : (x0 + x1) + (x2 + x3);
     }
   }
-  // W = T (beta e K), Z = T^T (d K), per dk tile
-  for (int c0 = 0; c0 < p.dk; c0 += KT) {
+  // W = T (beta e K), Z = T^T (d K), per dk tile (columns past dk are zero)
+  for (int c0 = 0; c0 < p.ldw; c0 += KT) {
     __syncthreads();
-    load_tokens<KT>(s1, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sbe);
-    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sd);
+    load_tokens<KT, LT>(s1, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sbe);
+    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sd);
     __syncthreads();
     float aw[4][2], az[4][2];
     zero(aw); zero(az);
@@ -243,17 +298,15 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int m = tm + 16 * i, col = c0 + tn + 16 * j;
-        if (col < p.dk) {
-          p.W[(row0 + m) * p.dk + col] = aw[i][j];
-          p.Z[(row0 + m) * p.dk + col] = az[i][j];
-        }
+        p.W[(row0 + m) * p.ldw + col] = aw[i][j];
+        p.Z[(row0 + m) * p.ldw + col] = az[i][j];
       }
   }
   // U = T (beta V), Y = T^T (P^T dO), per dv tile
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
-    load_tokens<VT>(s1, LT, v, bT, t0, p.T, p.H, h, p.dv, c0, sb);
-    load_tokens<VT>(s2, LT, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_tokens<VT, LT>(s1, v, bT, t0, p.T, p.H, h, p.dv, c0, sb);
+    load_tokens<VT, LT>(s2, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
     __syncthreads();
     float au[4][2], ap[4][2];
     zero(au); zero(ap);
@@ -292,13 +345,13 @@ template <> struct StateMap<32> { static constexpr int TM = 2, TN = 2, GM = 16, 
 
 template <int DKP>
 constexpr int states_smem_floats() {
-  return DKP * VT + C * (DKP + 1) + C * DKP + 2 * C * VT + 5 * C;
+  return DKP * VT + C * (DKP + 4) + C * DKP + 2 * C * VT + 5 * C;
 }
 
 template <typename Tin, int DKP>
 __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
   using SM = StateMap<DKP>;
-  constexpr int LW = DKP + 1;
+  constexpr int LW = DKP + 4;   // 16-byte rows; rows 4 banks apart
   extern __shared__ float sm[];
   float* sS = sm;                   // DKP x VT   state (or state gradient) tile
   float* sM = sS + DKP * VT;        // C x LW     W | Z, then Q
@@ -326,14 +379,16 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
     const int n = rev ? p.N - 1 - it : it, t0 = n * C;
     const size_t row0 = (size_t)bh * Np + t0;
     __syncthreads();
-    for (int e = tid; e < DKP * VT; e += NT) {
+    for (int e = tid * 4; e < DKP * VT; e += NT * 4) {
       const int r = e / VT, c = e - r * VT;
-      if (r < p.dk) keep[(((size_t)bh * p.N + n) * p.dk + r) * p.dv + c0 + c] = sS[e];
+      if (r < p.dk)
+        *reinterpret_cast<float4*>(keep + (((size_t)bh * p.N + n) * p.dk + r) * p.dv + c0 + c) =
+            *reinterpret_cast<const float4*>(sS + e);
     }
-    load_block<DKP>(sM, LW, (rev ? p.Z : p.W) + row0 * p.dk, p.dk, 0);
-    load_block<VT>(sU, VT, (rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
+    load_block<DKP, LW>(sM, (rev ? p.Z : p.W) + row0 * p.ldw, p.ldw, 0);
+    load_block<VT, VT>(sU, (rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
     chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
-    if (!rev) load_tokens<DKP>(sK, DKP, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+    if (!rev) load_tokens<DKP, DKP>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
     __syncthreads();
     // forward: V' = U - W h;  reverse: dX = Y + Z dh
     float acc[4][2];
@@ -357,9 +412,9 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
       }
     if (rev) {
       __syncthreads();   // Z in sM has been read; sM now takes Q
-      load_tokens<DKP>(sM, LW, q, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<DKP>(sK, DKP, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<VT>(sO, VT, dO, bT, t0, p.T, p.H, h, p.dv, c0, se);
+      load_tokens<DKP, LW>(sM, q, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+      load_tokens<DKP, DKP>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+      load_tokens<VT, VT>(sO, dO, bT, t0, p.T, p.H, h, p.dv, c0, se);
     }
     __syncthreads();
     // forward: h = e^gamma h + K^T (d V');  reverse: dh = e^gamma dh + Q^T (e dO) + K^T (-beta e dX)
@@ -423,10 +478,10 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   Tin* dv_out = static_cast<Tin*>(p.dv_out);
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
-    load_tokens<VT>(s1, LT, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
-    load_block<VT>(s2, LT, p.YX + row0 * p.dv, p.dv, c0);
-    load_block<VT>(s3, LT, p.UV + row0 * p.dv, p.dv, c0);
-    load_tokens<VT>(s4, LT, v, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_tokens<VT, LT>(s1, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_block<VT, LT>(s2, p.YX + row0 * p.dv, p.dv, c0);
+    load_block<VT, LT>(s3, p.UV + row0 * p.dv, p.dv, c0);
+    load_tokens<VT, LT>(s4, v, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
     __syncthreads();
     mac<4, 4, 16, 16, false, true>(aP, s1, LT, s3, LT, tm, tn, VT);
     mac<4, 4, 16, 16, false, true>(aA, s2, LT, s3, LT, tm, tn, VT);
@@ -456,8 +511,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   zero(aQK); zero(aKK);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
-    load_tokens<KT>(s1, LT, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
-    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
     __syncthreads();
     mac<4, 4, 16, 16, false, true>(aQK, s1, LT, s2, LT, tm, tn, KT);
     mac<4, 4, 16, 16, false, true>(aKK, s2, LT, s2, LT, tm, tn, KT);
@@ -506,20 +561,25 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
     zero(aKd); zero(aQ0); zero(aM);
     for (int c0 = 0; c0 < p.dv; c0 += VT) {
       __syncthreads();
-      load_tokens<VT>(s1, LT, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
-      load_block<VT>(s2, LT, p.YX + row0 * p.dv, p.dv, c0);
-      load_block<VT>(s3, LT, p.UV + row0 * p.dv, p.dv, c0);
-      for (int e = tid; e < KT * VT; e += NT) {
-        const int r = e >> 5, c = e & 31;
-        float hv = 0.f, dhv = 0.f;
+      load_tokens<VT, LT>(s1, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+      load_block<VT, LT>(s2, p.YX + row0 * p.dv, p.dv, c0);
+      load_block<VT, LT>(s3, p.UV + row0 * p.dv, p.dv, c0);
+      {
+        static_assert(KT * VT == 4 * NT, "one 16-byte vector of h and of dh per thread");
+        const int r = tid >> 3, c = (tid & 7) * 4;
+        float4 hv = make_float4(0.f, 0.f, 0.f, 0.f), dhv = hv;
         if (kt + r < p.dk) {
           const size_t off = (st0 + kt + r) * p.dv + c0 + c;
-          hv = p.hs[off];
-          dhv = p.dhs[off];
+          hv = *reinterpret_cast<const float4*>(p.hs + off);
+          dhv = *reinterpret_cast<const float4*>(p.dhs + off);
         }
-        sH[r * LT + c] = hv;
-        sD[r * LT + c] = dhv;
-        rHD = fmaf(hv, dhv, rHD);
+        const float hf[4] = {hv.x, hv.y, hv.z, hv.w}, df[4] = {dhv.x, dhv.y, dhv.z, dhv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sH[r * LT + c + j] = hf[j];
+          sD[r * LT + c + j] = df[j];
+          rHD = fmaf(hf[j], df[j], rHD);
+        }
       }
       __syncthreads();
       mac<4, 2, 16, 16, false, true>(aKd, s3, LT, sD, LT, tm, tn, VT);
@@ -527,9 +587,9 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
       mac<4, 2, 16, 16, false, true>(aM, s2, LT, sH, LT, tm, tn, VT);
     }
     __syncthreads();
-    load_tokens<KT>(s1, LT, q, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
-    load_tokens<KT>(s2, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
-    load_tokens<KT>(s4, LT, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, sb);
+    load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT, LT>(s4, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, sb);
     __syncthreads();
     float aq[4][2], ak[4][2], ak2[4][2];
     zero(aq); zero(ak); zero(ak2);
@@ -633,13 +693,16 @@ struct WsLayout {
   size_t W, Z, UV, YX, hs, dhs, dqk, total;
 };
 
+int padded_dk(int dk) { return dk <= 32 ? 32 : dk <= 64 ? 64 : 128; }
+
 WsLayout ws_layout(int B, int T, int H, int dk, int dv) {
   const size_t N = (size_t)((T + C - 1) / C), Np = N * C, BH = (size_t)B * H;
+  const size_t ldw = (size_t)padded_dk(dk);
   WsLayout L{};
   size_t o = 0;
   auto take = [&](size_t n) { const size_t r = o; o += (n + 63) & ~size_t(63); return r; };
-  L.W = take(BH * Np * dk);
-  L.Z = take(BH * Np * dk);
+  L.W = take(BH * Np * ldw);
+  L.Z = take(BH * Np * ldw);
   L.UV = take(BH * Np * dv);
   L.YX = take(BH * Np * dv);
   L.hs = take(BH * N * dk * dv);
@@ -656,7 +719,7 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   const BwdParams p{a.q, a.k, a.v, a.dO, a.g, a.beta, a.h0, a.dhT, a.dq, a.dk_out, a.dv_out,
                     a.dg, a.dbeta, a.dh0, ws + L.W, ws + L.Z, ws + L.UV, ws + L.YX,
                     ws + L.hs, ws + L.dhs, ws + L.dqk, a.B, a.T, a.H, a.Hk, a.dk, a.dv,
-                    (a.T + C - 1) / C};
+                    (a.T + C - 1) / C, DKP};
   const int BH = a.B * a.H;
   static std::atomic<int> set_prep[kMaxDevices] = {}, set_states[kMaxDevices] = {},
                           set_grads[kMaxDevices] = {};
@@ -680,9 +743,11 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
 
 template <typename Tin>
 cudaError_t launch_bwd_dtype(const ChunkBwdArgs& a, cudaStream_t st) {
-  if (a.dk <= 32) return launch_bwd_t<Tin, 32>(a, st);
-  if (a.dk <= 64) return launch_bwd_t<Tin, 64>(a, st);
-  return launch_bwd_t<Tin, 128>(a, st);
+  switch (padded_dk(a.dk)) {
+    case 32: return launch_bwd_t<Tin, 32>(a, st);
+    case 64: return launch_bwd_t<Tin, 64>(a, st);
+    default: return launch_bwd_t<Tin, 128>(a, st);
+  }
 }
 
 }  // namespace
