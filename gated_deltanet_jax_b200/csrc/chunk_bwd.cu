@@ -1,4 +1,4 @@
-// Backward of the chunked gated delta rule (exact semantics), fp32 CUDA cores.
+// Backward of the chunked gated delta rule (exact semantics) on the tensor cores.
 //
 // The reference has no backward of its own: it relies on JAX autodiff of its
 // chunk path (ops.py:238-346).  This computes the gradients of the recurrence
@@ -36,9 +36,10 @@
 //                  the reverse pass stores every chunk's dh_out and dX, and dh0.
 //   3. bwd_grads   one CTA per (chunk, value head): every gradient of the chunk.
 //   4. bwd_group   (grouped q/k heads only) sums dq, dk over each head group.
-// All products are fp32 on CUDA cores, from shared memory, each thread owning
-// a strided micro-tile of the output.  Nothing is summed with atomics, so the
-// gradients are the same on every run.
+// Every product runs on the tensor cores (warp-level mma.sync, tf32 operands,
+// fp32 accumulation; three-term tf32 splitting for fp32 inputs) from fp32
+// tiles in shared memory.  Nothing is summed with atomics, so the gradients
+// are the same on every run.
 #include <cstdint>
 
 #include "gdn_common.cuh"
@@ -49,11 +50,15 @@ namespace gdn {
 namespace {
 
 constexpr int C = 64;        // chunk length (the exact result does not depend on it)
-constexpr int NT = 256;      // threads per CTA
+constexpr int NT = 256;      // threads per CTA (8 warps)
 constexpr int KT = 32;       // dk columns per streamed tile
 constexpr int VT = 32;       // dv columns per streamed tile and per state tile
-constexpr int LC = C + 1;    // odd row strides keep row and column reads conflict-free
-constexpr int LT = VT + 1;
+// Shared-memory row strides.  A fragment load reads 8 rows x 4 columns
+// (row stride = 4 banks apart: conflict-free) or 4 rows x 8 columns (8 banks
+// apart: conflict-free); the other pattern on the same matrix is 2-way.
+constexpr int LC = C + 4;    // C x C matrices
+constexpr int LT = VT + 4;   // 32-column tiles read by rows
+constexpr int LB = VT + 8;   // 32-column tiles read by columns
 
 struct BwdParams {
   const void* q; const void* k; const void* v; const void* dO;
@@ -70,39 +75,109 @@ struct BwdParams {
   int B, T, H, Hk, dk, dv, N, ldw;
 };
 
-// acc[i][j] += sum_{k < K} a(m_i, k) b(k, n_j), m_i = tm + i GM, n_j = tn + j GN, with
-// a(m, k) = TA ? A[k lda + m] : A[m lda + k] and b(k, n) = TB ? B[n ldb + k] : B[k ldb + n].
-// Lanes of a warp take consecutive tn, so with odd row strides every load is
-// conflict-free or a broadcast.
-template <int TM, int TN, int GM, int GN, bool TA, bool TB>
-__device__ __forceinline__ void mac(float (&acc)[TM][TN], const float* A, int lda,
-                                    const float* B, int ldb, int tm, int tn, int K) {
-#pragma unroll 4
-  for (int k = 0; k < K; ++k) {
-    float a[TM], b[TN];
+// ---------------------------------------------------------------------------
+// Warp-level tensor-core products: mma.sync m16n8k8 with tf32 operands and
+// fp32 accumulators.  bf16 inputs are exact in tf32, fp32 intermediates are
+// rounded to tf32 (11 significant bits).  With kSplit (fp32 inputs) every
+// operand is split as x = hi + lo (both tf32) and a b ~ hi_a hi_b + hi_a lo_b
+// + lo_a hi_b, which keeps about fp32 accuracy.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4],
+                                         const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+template <bool kSplit>
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = to_tf32(x);
+  if (kSplit) lo = to_tf32(x - __uint_as_float(hi));
+}
+
+// acc[i][j] += sum_{k < K} a(m, k) b(k, n) over the warp's MT x NTL tiles of
+// 16 x 8 at (m0 + 16 i, n0 + 8 j), with a(m, k) = TA ? A[k lda + m] : A[m lda + k]
+// and b(k, n) = TB ? B[n ldb + k] : B[k ldb + n].  K is a multiple of 8.
+// Accumulator element e of tile (i, j) is row m0 + 16 i + g + 8 (e >> 1),
+// column n0 + 8 j + 2 t + (e & 1), for lane = 4 g + t.
+template <int MT, int NTL, bool TA, bool TB, bool kSplit>
+__device__ __forceinline__ void warp_mma(float (&acc)[MT][NTL][4], const float* A, int lda,
+                                         const float* B, int ldb, int m0, int n0, int K) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll 2
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    uint32_t ah[MT][4], al[MT][4], bh[NTL][2], bl[NTL][2];
 #pragma unroll
-    for (int i = 0; i < TM; ++i) {
-      const int m = tm + i * GM;
-      a[i] = TA ? A[k * lda + m] : A[m * lda + k];
-    }
+    for (int i = 0; i < MT; ++i)
 #pragma unroll
-    for (int j = 0; j < TN; ++j) {
-      const int n = tn + j * GN;
-      b[j] = TB ? B[n * ldb + k] : B[k * ldb + n];
-    }
+      for (int e = 0; e < 4; ++e) {
+        const int m = m0 + 16 * i + g + 8 * (e & 1), kk = k0 + t + 4 * (e >> 1);
+        split_tf32<kSplit>(TA ? A[kk * lda + m] : A[m * lda + kk], ah[i][e], al[i][e]);
+      }
 #pragma unroll
-    for (int i = 0; i < TM; ++i)
+    for (int j = 0; j < NTL; ++j)
 #pragma unroll
-      for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+      for (int e = 0; e < 2; ++e) {
+        const int n = n0 + 8 * j + g, kk = k0 + t + 4 * e;
+        split_tf32<kSplit>(TB ? B[n * ldb + kk] : B[kk * ldb + n], bh[j][e], bl[j][e]);
+      }
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int j = 0; j < NTL; ++j) {
+        mma_tf32(acc[i][j], ah[i], bh[j]);
+        if (kSplit) {
+          mma_tf32(acc[i][j], ah[i], bl[j]);
+          mma_tf32(acc[i][j], al[i], bh[j]);
+        }
+      }
   }
 }
 
-template <int TM, int TN>
-__device__ __forceinline__ void zero(float (&acc)[TM][TN]) {
+template <int MT, int NTL>
+__device__ __forceinline__ void zero(float (&acc)[MT][NTL][4]) {
 #pragma unroll
-  for (int i = 0; i < TM; ++i)
+  for (int i = 0; i < MT; ++i)
 #pragma unroll
-    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < NTL; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
+}
+
+// Row and column of accumulator element e of tile (i, j) (see warp_mma).
+struct Frag {
+  int g, t;
+  __device__ Frag() : g((threadIdx.x & 31) >> 2), t(threadIdx.x & 3) {}
+  __device__ int row(int m0, int i, int e) const { return m0 + 16 * i + g + 8 * (e >> 1); }
+  __device__ int col(int n0, int j, int e) const { return n0 + 8 * j + 2 * t + (e & 1); }
+};
+
+// Sum over the 4 lanes of a quad (the lanes holding one accumulator row).
+__device__ __forceinline__ float quad_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  return x + __shfl_xor_sync(0xffffffffu, x, 2);
+}
+// Sum over the 8 quads (the lanes holding one accumulator column).
+__device__ __forceinline__ float column_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  x += __shfl_xor_sync(0xffffffffu, x, 8);
+  return x + __shfl_xor_sync(0xffffffffu, x, 16);
+}
+
+// Two adjacent output elements (col even) in the output dtype.
+__device__ __forceinline__ void store2(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+__device__ __forceinline__ void store2(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
 }
 
 // Four or eight input elements (16 bytes) as fp32.
@@ -213,123 +288,116 @@ __device__ __forceinline__ void chunk_gates(const BwdParams& p, int b, int h, in
   sbe[l] = b0 * e0; sbe[l + 32] = b1 * e1;
 }
 
-__device__ __forceinline__ float half_warp_sum(float x) {
-#pragma unroll
-  for (int o = 1; o < 16; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  return x;
-}
-
 // ---------------------------------------------------------------------------
 // 1. per chunk: T, W, U, Y, Z
 // ---------------------------------------------------------------------------
-constexpr int kPrepSmemFloats = 3 * C * LC + 3 * C * LT + 5 * C;
+constexpr int kPrepSmemFloats = 3 * C * LC + 3 * C * LB + 5 * C;
 
 template <typename Tin>
 __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
+  constexpr bool kSplit = sizeof(Tin) == 4;
   extern __shared__ float sm[];
   float* sA = sm;
   float* sT = sA + C * LC;
   float* sP = sT + C * LC;
-  float* s1 = sP + C * LC;
-  float* s2 = s1 + C * LT;
-  float* s3 = s2 + C * LT;
-  float* sG = s3 + C * LT;
+  float* s1 = sP + C * LC;          // C x 32 tiles (stride LT for Q K^T, LB after)
+  float* s2 = s1 + C * LB;
+  float* s3 = s2 + C * LB;
+  float* sG = s3 + C * LB;
   float* se = sG + C; float* sd = se + C; float* sb = sd + C; float* sbe = sb + C;
   const Tin* q = static_cast<const Tin*>(p.q);
   const Tin* k = static_cast<const Tin*>(p.k);
   const Tin* v = static_cast<const Tin*>(p.v);
   const Tin* dO = static_cast<const Tin*>(p.dO);
   const int n = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x;
+  const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x, w = tid >> 5;
   const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
   const size_t row0 = (size_t)bh * Np + t0;
-  const int tm = tid >> 4, tn = tid & 15;
+  const Frag f;
   chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
 
-  // Q K^T and K K^T over dk tiles
-  float aQK[4][4], aKK[4][4];
+  // Q K^T and K K^T over dk tiles; warp: rows mq.., columns nq..
+  const int mq = (w >> 1) * 16, nq = (w & 1) * 32;
+  float aQK[1][4][4], aKK[1][4][4];
   zero(aQK); zero(aKK);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
     load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
     load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
     __syncthreads();
-    mac<4, 4, 16, 16, false, true>(aQK, s1, LT, s2, LT, tm, tn, KT);
-    mac<4, 4, 16, 16, false, true>(aKK, s2, LT, s2, LT, tm, tn, KT);
+    warp_mma<1, 4, false, true, kSplit>(aQK, s1, LT, s2, LT, mq, nq, KT);
+    warp_mma<1, 4, false, true, kSplit>(aKK, s2, LT, s2, LT, mq, nq, KT);
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int m = tm + 16 * i, c = tn + 16 * j;
+    for (int e = 0; e < 4; ++e) {
+      const int m = f.row(mq, 0, e), c = f.col(nq, j, e);
       const float E = c <= m ? gate_exp(sG[m] - sG[c]) : 0.f;
-      sA[m * LC + c] = c < m ? sb[m] * aKK[i][j] * E : 0.f;
-      sP[m * LC + c] = aQK[i][j] * E;
+      sA[m * LC + c] = c < m ? sb[m] * aKK[0][j][e] * E : 0.f;
+      sP[m * LC + c] = aQK[0][j][e] * E;
     }
   __syncthreads();
-  // T = (I + A)^{-1} by forward substitution, one column per thread
-  if (tid < C) {
-    const int c = tid;
+  // T = (I + A)^{-1} by forward substitution: column c by the lane quad g of
+  // warp c / 8, one row after another (each lane sums every fourth term)
+  {
+    const int c = w * 8 + f.g;
     for (int r = 0; r < C; ++r) {
-      float x0 = r == c ? 1.f : 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
-      int j = c;
-      for (; j + 3 < r; j += 4) {
-        x0 = fmaf(-sA[r * LC + j], sT[j * LC + c], x0);
-        x1 = fmaf(-sA[r * LC + j + 1], sT[(j + 1) * LC + c], x1);
-        x2 = fmaf(-sA[r * LC + j + 2], sT[(j + 2) * LC + c], x2);
-        x3 = fmaf(-sA[r * LC + j + 3], sT[(j + 3) * LC + c], x3);
-      }
-      for (; j < r; ++j) x0 = fmaf(-sA[r * LC + j], sT[j * LC + c], x0);
-      sT[r * LC + c] = r < c ? 0.f : (x0 + x1) + (x2 + x3);
+      float s = 0.f;
+      for (int j = c + f.t; j < r; j += 4) s = fmaf(sA[r * LC + j], sT[j * LC + c], s);
+      s = quad_sum(s);
+      if (f.t == 0) sT[r * LC + c] = r < c ? 0.f : (r == c ? 1.f : -s);
+      __syncwarp();
     }
   }
-  // W = T (beta e K), Z = T^T (d K), per dk tile (columns past dk are zero)
+  // W = T (beta e K), Z = T^T (d K) per dk tile (columns past dk are zero)
+  const int mw = (w >> 1) * 16, nw = (w & 1) * 16;
   for (int c0 = 0; c0 < p.ldw; c0 += KT) {
     __syncthreads();
-    load_tokens<KT, LT>(s1, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sbe);
-    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sd);
+    load_tokens<KT, LB>(s1, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sbe);
+    load_tokens<KT, LB>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sd);
     __syncthreads();
-    float aw[4][2], az[4][2];
+    float aw[1][2][4], az[1][2][4];
     zero(aw); zero(az);
-    mac<4, 2, 16, 16, false, false>(aw, sT, LC, s1, LT, tm, tn, C);
-    mac<4, 2, 16, 16, true, false>(az, sT, LC, s2, LT, tm, tn, C);
+    warp_mma<1, 2, false, false, kSplit>(aw, sT, LC, s1, LB, mw, nw, C);
+    warp_mma<1, 2, true, false, kSplit>(az, sT, LC, s2, LB, mw, nw, C);
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int m = tm + 16 * i, col = c0 + tn + 16 * j;
-        p.W[(row0 + m) * p.ldw + col] = aw[i][j];
-        p.Z[(row0 + m) * p.ldw + col] = az[i][j];
+      for (int e = 0; e < 4; e += 2) {
+        const size_t off = (row0 + f.row(mw, 0, e)) * p.ldw + c0 + f.col(nw, j, e);
+        store2(p.W + off, aw[0][j][e], aw[0][j][e + 1]);
+        store2(p.Z + off, az[0][j][e], az[0][j][e + 1]);
       }
   }
-  // U = T (beta V), Y = T^T (P^T dO), per dv tile
+  // U = T (beta V), Y = T^T (P^T dO) per dv tile
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
-    load_tokens<VT, LT>(s1, v, bT, t0, p.T, p.H, h, p.dv, c0, sb);
-    load_tokens<VT, LT>(s2, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_tokens<VT, LB>(s1, v, bT, t0, p.T, p.H, h, p.dv, c0, sb);
+    load_tokens<VT, LB>(s2, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
     __syncthreads();
-    float au[4][2], ap[4][2];
+    float au[1][2][4], ap[1][2][4];
     zero(au); zero(ap);
-    mac<4, 2, 16, 16, false, false>(au, sT, LC, s1, LT, tm, tn, C);
-    mac<4, 2, 16, 16, true, false>(ap, sP, LC, s2, LT, tm, tn, C);
+    warp_mma<1, 2, false, false, kSplit>(au, sT, LC, s1, LB, mw, nw, C);
+    warp_mma<1, 2, true, false, kSplit>(ap, sP, LC, s2, LB, mw, nw, C);
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int m = tm + 16 * i, c = tn + 16 * j;
-        p.UV[(row0 + m) * p.dv + c0 + c] = au[i][j];
-        s3[m * LT + c] = ap[i][j];
+      for (int e = 0; e < 4; e += 2) {
+        const int m = f.row(mw, 0, e), c = f.col(nw, j, e);
+        store2(p.UV + (row0 + m) * p.dv + c0 + c, au[0][j][e], au[0][j][e + 1]);
+        store2(s3 + m * LB + c, ap[0][j][e], ap[0][j][e + 1]);
       }
     __syncthreads();
-    float ay[4][2];
+    float ay[1][2][4];
     zero(ay);
-    mac<4, 2, 16, 16, true, false>(ay, sT, LC, s3, LT, tm, tn, C);
+    warp_mma<1, 2, true, false, kSplit>(ay, sT, LC, s3, LB, mw, nw, C);
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int m = tm + 16 * i, c = tn + 16 * j;
-        p.YX[(row0 + m) * p.dv + c0 + c] = ay[i][j];
+      for (int e = 0; e < 4; e += 2) {
+        const int m = f.row(mw, 0, e), c = f.col(nw, j, e);
+        store2(p.YX + (row0 + m) * p.dv + c0 + c, ay[0][j][e], ay[0][j][e + 1]);
       }
   }
 }
@@ -337,42 +405,58 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
 // ---------------------------------------------------------------------------
 // 2. the two sequential passes over the chunks
 // ---------------------------------------------------------------------------
-// Map of a DKP x VT state-tile product onto the 256 threads.
-template <int DKP> struct StateMap;
-template <> struct StateMap<128> { static constexpr int TM = 4, TN = 4, GM = 32, GN = 8; };
-template <> struct StateMap<64> { static constexpr int TM = 4, TN = 2, GM = 16, GN = 16; };
-template <> struct StateMap<32> { static constexpr int TM = 2, TN = 2, GM = 16, GN = 16; };
+// Warp tiles of the DKP x VT state product.
+template <int DKP> struct StateTiles;
+template <> struct StateTiles<128> {
+  static constexpr int MT = 2, NTL = 2;
+  static __device__ int m0(int w) { return (w >> 1) * 32; }
+  static __device__ int n0(int w) { return (w & 1) * 16; }
+};
+template <> struct StateTiles<64> {
+  static constexpr int MT = 1, NTL = 2;
+  static __device__ int m0(int w) { return (w >> 1) * 16; }
+  static __device__ int n0(int w) { return (w & 1) * 16; }
+};
+template <> struct StateTiles<32> {
+  static constexpr int MT = 1, NTL = 1;
+  static __device__ int m0(int w) { return (w >> 2) * 16; }
+  static __device__ int n0(int w) { return (w & 3) * 8; }
+};
+
+constexpr int SS = VT + 8;   // state tile row stride (read by columns)
 
 template <int DKP>
 constexpr int states_smem_floats() {
-  return DKP * VT + C * (DKP + 4) + C * DKP + 2 * C * VT + 5 * C;
+  return DKP * SS + C * (DKP + 4) + C * (DKP + 8) + 2 * C * LB + 5 * C;
 }
 
 template <typename Tin, int DKP>
 __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
-  using SM = StateMap<DKP>;
-  constexpr int LW = DKP + 4;   // 16-byte rows; rows 4 banks apart
+  using ST = StateTiles<DKP>;
+  constexpr bool kSplit = sizeof(Tin) == 4;
+  constexpr int LW = DKP + 4, LK = DKP + 8;
   extern __shared__ float sm[];
-  float* sS = sm;                   // DKP x VT   state (or state gradient) tile
-  float* sM = sS + DKP * VT;        // C x LW     W | Z, then Q
-  float* sK = sM + C * LW;          // C x DKP    K
-  float* sU = sK + C * DKP;         // C x VT     U -> d V'  |  Y -> -beta e dX
-  float* sO = sU + C * VT;          // C x VT     e dO
-  float* sG = sO + C * VT;
+  float* sS = sm;                   // DKP x SS  state (or state gradient) tile
+  float* sM = sS + DKP * SS;        // C x LW    W | Z, then Q
+  float* sK = sM + C * LW;          // C x LK    K
+  float* sU = sK + C * LK;          // C x LB    U -> d V'  |  Y -> -beta e dX
+  float* sO = sU + C * LB;          // C x LB    e dO
+  float* sG = sO + C * LB;
   float* se = sG + C; float* sd = se + C; float* sb = sd + C; float* sbe = sb + C;
   const Tin* q = static_cast<const Tin*>(p.q);
   const Tin* k = static_cast<const Tin*>(p.k);
   const Tin* dO = static_cast<const Tin*>(p.dO);
   const int c0 = blockIdx.x * VT, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  const int hq = h * p.Hk / p.H, tid = threadIdx.x;
+  const int hq = h * p.Hk / p.H, tid = threadIdx.x, w = tid >> 5;
   const bool rev = blockIdx.z != 0;
   const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
-  const int tm = tid >> 4, tn = tid & 15;                    // C x VT products
-  const int rm = tid / SM::GN, rn = tid - rm * SM::GN;       // DKP x VT products
+  const Frag f;
+  const int mv = (w >> 1) * 16, nv = (w & 1) * 16;       // C x VT products
+  const int ms = ST::m0(w), ns = ST::n0(w);              // DKP x VT products
   const float* init = rev ? p.dhT : p.h0;
   for (int e = tid; e < DKP * VT; e += NT) {
     const int r = e / VT, c = e - r * VT;
-    sS[e] = (init && r < p.dk) ? init[((size_t)bh * p.dk + r) * p.dv + c0 + c] : 0.f;
+    sS[r * SS + c] = (init && r < p.dk) ? init[((size_t)bh * p.dk + r) * p.dv + c0 + c] : 0.f;
   }
   float* keep = rev ? p.dhs : p.hs;
   for (int it = 0; it < p.N; ++it) {
@@ -383,59 +467,62 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
       const int r = e / VT, c = e - r * VT;
       if (r < p.dk)
         *reinterpret_cast<float4*>(keep + (((size_t)bh * p.N + n) * p.dk + r) * p.dv + c0 + c) =
-            *reinterpret_cast<const float4*>(sS + e);
+            *reinterpret_cast<const float4*>(sS + r * SS + c);
     }
     load_block<DKP, LW>(sM, (rev ? p.Z : p.W) + row0 * p.ldw, p.ldw, 0);
-    load_block<VT, VT>(sU, (rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
+    load_block<VT, LB>(sU, (rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
     chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
-    if (!rev) load_tokens<DKP, DKP>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+    if (!rev) load_tokens<DKP, LK>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
     __syncthreads();
     // forward: V' = U - W h;  reverse: dX = Y + Z dh
-    float acc[4][2];
+    float acc[1][2][4];
     zero(acc);
-    mac<4, 2, 16, 16, false, false>(acc, sM, LW, sS, VT, tm, tn, DKP);
+    warp_mma<1, 2, false, false, kSplit>(acc, sM, LW, sS, SS, mv, nv, DKP);
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int m = tm + 16 * i, c = tn + 16 * j;
-        const float u = sU[m * VT + c];
+      for (int e = 0; e < 4; e += 2) {
+        const int m = f.row(mv, 0, e), c = f.col(nv, j, e);
+        float* u = sU + m * LB + c;
+        const size_t off = (row0 + m) * p.dv + c0 + c;
         if (!rev) {
-          const float vp = u - acc[i][j];
-          p.UV[(row0 + m) * p.dv + c0 + c] = vp;
-          sU[m * VT + c] = sd[m] * vp;
+          const float v0 = u[0] - acc[0][j][e], v1 = u[1] - acc[0][j][e + 1];
+          store2(p.UV + off, v0, v1);
+          u[0] = sd[m] * v0; u[1] = sd[m] * v1;
         } else {
-          const float dx = u + acc[i][j];
-          p.YX[(row0 + m) * p.dv + c0 + c] = dx;
-          sU[m * VT + c] = -sbe[m] * dx;
+          const float x0 = u[0] + acc[0][j][e], x1 = u[1] + acc[0][j][e + 1];
+          store2(p.YX + off, x0, x1);
+          u[0] = -sbe[m] * x0; u[1] = -sbe[m] * x1;
         }
       }
     if (rev) {
       __syncthreads();   // Z in sM has been read; sM now takes Q
       load_tokens<DKP, LW>(sM, q, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<DKP, DKP>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<VT, VT>(sO, dO, bT, t0, p.T, p.H, h, p.dv, c0, se);
+      load_tokens<DKP, LK>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+      load_tokens<VT, LB>(sO, dO, bT, t0, p.T, p.H, h, p.dv, c0, se);
     }
     __syncthreads();
     // forward: h = e^gamma h + K^T (d V');  reverse: dh = e^gamma dh + Q^T (e dO) + K^T (-beta e dX)
-    float accS[SM::TM][SM::TN];
+    float accS[ST::MT][ST::NTL][4];
     zero(accS);
-    mac<SM::TM, SM::TN, SM::GM, SM::GN, true, false>(accS, sK, DKP, sU, VT, rm, rn, C);
-    if (rev) mac<SM::TM, SM::TN, SM::GM, SM::GN, true, false>(accS, sM, LW, sO, VT, rm, rn, C);
+    warp_mma<ST::MT, ST::NTL, true, false, kSplit>(accS, sK, LK, sU, LB, ms, ns, C);
+    if (rev) warp_mma<ST::MT, ST::NTL, true, false, kSplit>(accS, sM, LW, sO, LB, ms, ns, C);
     const float eg = se[C - 1];
 #pragma unroll
-    for (int i = 0; i < SM::TM; ++i)
+    for (int i = 0; i < ST::MT; ++i)
 #pragma unroll
-      for (int j = 0; j < SM::TN; ++j) {
-        const int r = rm + i * SM::GM, c = rn + j * SM::GN;
-        sS[r * VT + c] = fmaf(eg, sS[r * VT + c], accS[i][j]);
-      }
+      for (int j = 0; j < ST::NTL; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float* s = sS + f.row(ms, i, e) * SS + f.col(ns, j, e);
+          *s = fmaf(eg, *s, accS[i][j][e]);
+        }
   }
   if (rev && p.dh0) {
     __syncthreads();
     for (int e = tid; e < DKP * VT; e += NT) {
       const int r = e / VT, c = e - r * VT;
-      if (r < p.dk) p.dh0[((size_t)bh * p.dk + r) * p.dv + c0 + c] = sS[e];
+      if (r < p.dk) p.dh0[((size_t)bh * p.dk + r) * p.dv + c0 + c] = sS[r * SS + c];
     }
   }
 }
@@ -443,37 +530,44 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
 // ---------------------------------------------------------------------------
 // 3. per chunk: every gradient
 // ---------------------------------------------------------------------------
-constexpr int kGradSmemFloats = 2 * C * LC + 4 * C * LT + 2 * KT * LT + 7 * C + 32;
+constexpr int kGradSmemFloats = 2 * C * LC + 4 * C * LB + 2 * KT * LT + 7 * C + 8 * C + 32;
 
 template <typename Tin>
 __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
+  constexpr bool kSplit = sizeof(Tin) == 4;
   extern __shared__ float sm[];
   float* sPE = sm;                  // C x LC  dP e^{G_i - G_j} (lower, with diagonal)
   float* sAE = sPE + C * LC;        // C x LC  dA e^{G_i - G_j} (strictly lower)
-  float* s1 = sAE + C * LC;         // C x LT tiles
-  float* s2 = s1 + C * LT;
-  float* s3 = s2 + C * LT;
-  float* s4 = s3 + C * LT;
-  float* sH = s4 + C * LT;          // KT x LT  h tile      [dk row][dv col]
+  float* s1 = sAE + C * LC;         // C x 32 tiles (stride LT, or LB for the dQ / dK products)
+  float* s2 = s1 + C * LB;
+  float* s3 = s2 + C * LB;
+  float* s4 = s3 + C * LB;
+  float* sH = s4 + C * LB;          // KT x LT  h tile      [dk row][dv col]
   float* sD = sH + KT * LT;         // KT x LT  dh_out tile
   float* sG = sD + KT * LT;
   float* se = sG + C; float* sd = se + C; float* sb = sd + C; float* sbe = sb + C;
-  float* sdG = sbe + C; float* sdB = sdG + C; float* sred = sdB + C;
+  float* sdG = sbe + C; float* sdB = sdG + C;
+  float* sRg = sdB + C;             // [2][C] row partials of the two column halves
+  float* sRb = sRg + 2 * C;         // [2][C]
+  float* sRc = sRb + 2 * C;         // [4][C] column partials of the four row blocks
+  float* sred = sRc + 4 * C;        // [8]
   const Tin* q = static_cast<const Tin*>(p.q);
   const Tin* k = static_cast<const Tin*>(p.k);
   const Tin* v = static_cast<const Tin*>(p.v);
   const Tin* dO = static_cast<const Tin*>(p.dO);
   const int n = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x;
+  const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x, w = tid >> 5;
   const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
   const size_t row0 = (size_t)bh * Np + t0;
-  const int tm = tid >> 4, tn = tid & 15;
+  const Frag f;
+  const int mq = (w >> 1) * 16, nq = (w & 1) * 32;   // C x C products
+  const int mw = (w >> 1) * 16, nw = (w & 1) * 16;   // C x 32 products
   const bool grouped = p.Hk != p.H;
   chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
   if (tid < C) { sdG[tid] = 0.f; sdB[tid] = 0.f; }
 
-  // A. dP = dO V'^T and dX V'^T over dv tiles; rowsum(dX o V); dV = beta dX
-  float aP[4][4], aA[4][4];
+  // A. dO V'^T and dX V'^T over dv tiles; rowsum(dX o V); dV = beta dX
+  float aP[1][4][4], aA[1][4][4];
   zero(aP); zero(aA);
   Tin* dv_out = static_cast<Tin*>(p.dv_out);
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
@@ -483,8 +577,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
     load_block<VT, LT>(s3, p.UV + row0 * p.dv, p.dv, c0);
     load_tokens<VT, LT>(s4, v, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
     __syncthreads();
-    mac<4, 4, 16, 16, false, true>(aP, s1, LT, s3, LT, tm, tn, VT);
-    mac<4, 4, 16, 16, false, true>(aA, s2, LT, s3, LT, tm, tn, VT);
+    warp_mma<1, 4, false, true, kSplit>(aP, s1, LT, s3, LT, mq, nq, VT);
+    warp_mma<1, 4, false, true, kSplit>(aA, s2, LT, s3, LT, mq, nq, VT);
     // one warp per row: 32 columns
     for (int q8 = 0; q8 < C * VT / NT; ++q8) {
       const int e = tid + q8 * NT, r = e >> 5, c = e & 31, t = t0 + r;
@@ -497,67 +591,72 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int m = tm + 16 * i, c = tn + 16 * j;
+    for (int e = 0; e < 4; ++e) {
+      const int m = f.row(mq, 0, e), c = f.col(nq, j, e);
       const float E = c <= m ? gate_exp(sG[m] - sG[c]) : 0.f;
-      sPE[m * LC + c] = aP[i][j] * E;
-      sAE[m * LC + c] = c < m ? -aA[i][j] * E : 0.f;
+      sPE[m * LC + c] = aP[0][j][e] * E;
+      sAE[m * LC + c] = c < m ? -aA[0][j][e] * E : 0.f;
     }
 
   // B. Q K^T and K K^T; the gate and beta terms through P and A
-  float aQK[4][4], aKK[4][4];
+  float aQK[1][4][4], aKK[1][4][4];
   zero(aQK); zero(aKK);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
     load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
     load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
     __syncthreads();
-    mac<4, 4, 16, 16, false, true>(aQK, s1, LT, s2, LT, tm, tn, KT);
-    mac<4, 4, 16, 16, false, true>(aKK, s2, LT, s2, LT, tm, tn, KT);
+    warp_mma<1, 4, false, true, kSplit>(aQK, s1, LT, s2, LT, mq, nq, KT);
+    warp_mma<1, 4, false, true, kSplit>(aKK, s2, LT, s2, LT, mq, nq, KT);
   }
   {
-    float rowg[4] = {0.f, 0.f, 0.f, 0.f}, rowb[4] = {0.f, 0.f, 0.f, 0.f};
-    float colg[4] = {0.f, 0.f, 0.f, 0.f};
+    // rows: quad sums, then the two column halves; columns: sums over the 8
+    // quads, then the four row blocks -- each in a fixed order (no atomics)
+    float rowg[2] = {0.f, 0.f}, rowb[2] = {0.f, 0.f}, colg[4][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 4; ++j) {
+      colg[j][0] = 0.f; colg[j][1] = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int m = tm + 16 * i, c = tn + 16 * j;
+      for (int e = 0; e < 4; ++e) {
+        const int m = f.row(mq, 0, e), c = f.col(nq, j, e);
         const float pe = sPE[m * LC + c], ae = sAE[m * LC + c];
-        const float x = fmaf(pe, aQK[i][j], ae * sb[m] * aKK[i][j]);
-        rowg[i] += x;
-        colg[j] -= x;
-        rowb[i] = fmaf(ae, aKK[i][j], rowb[i]);
-      }
-    // rows: the 16 lanes of a half warp share a row; columns: 16 row groups
-    // summed in a fixed order (no atomics: the result is the same every run)
-    float* scol = s3;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float rg = half_warp_sum(rowg[i]), rb = half_warp_sum(rowb[i]);
-      if (tn == 0) {
-        sdG[tm + 16 * i] += rg;
-        sdB[tm + 16 * i] += rb;
+        const float x = fmaf(pe, aQK[0][j][e], ae * sb[m] * aKK[0][j][e]);
+        rowg[e >> 1] += x;
+        colg[j][e & 1] -= x;
+        rowb[e >> 1] = fmaf(ae, aKK[0][j][e], rowb[e >> 1]);
       }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) scol[tm * C + tn + 16 * j] = colg[j];
+    for (int hh = 0; hh < 2; ++hh) {
+      const float rg = quad_sum(rowg[hh]), rb = quad_sum(rowb[hh]);
+      if (f.t == 0) {
+        sRg[(w & 1) * C + mq + f.g + 8 * hh] = rg;
+        sRb[(w & 1) * C + mq + f.g + 8 * hh] = rb;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) {
+        const float cg = column_sum(colg[j][c2]);
+        if (f.g == 0) sRc[(w >> 1) * C + nq + 8 * j + 2 * f.t + c2] = cg;
+      }
     __syncthreads();
     if (tid < C) {
-      float s = 0.f;
-      for (int r = 0; r < 16; ++r) s += scol[r * C + tid];
-      sdG[tid] += s;
+      sdG[tid] += (sRg[tid] + sRg[C + tid]) +
+                  ((sRc[tid] + sRc[C + tid]) + (sRc[2 * C + tid] + sRc[3 * C + tid]));
+      sdB[tid] += sRb[tid] + sRb[C + tid];
     }
   }
 
   // C. per dk tile: V' dh^T, dO h^T, dX h^T over dv; then dQ, dK and the row terms
-  float rG[4] = {0.f, 0.f, 0.f, 0.f}, rB[4] = {0.f, 0.f, 0.f, 0.f};
+  float rG[2] = {0.f, 0.f}, rB[2] = {0.f, 0.f};
   float rGC = 0.f, rHD = 0.f;
   const size_t st0 = ((size_t)bh * p.N + n) * p.dk;
   for (int kt = 0; kt < p.dk; kt += KT) {
-    float aKd[4][2], aQ0[4][2], aM[4][2];
+    float aKd[1][2][4], aQ0[1][2][4], aM[1][2][4];
     zero(aKd); zero(aQ0); zero(aM);
     for (int c0 = 0; c0 < p.dv; c0 += VT) {
       __syncthreads();
@@ -573,70 +672,74 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
           hv = *reinterpret_cast<const float4*>(p.hs + off);
           dhv = *reinterpret_cast<const float4*>(p.dhs + off);
         }
-        const float hf[4] = {hv.x, hv.y, hv.z, hv.w}, df[4] = {dhv.x, dhv.y, dhv.z, dhv.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sH[r * LT + c + j] = hf[j];
-          sD[r * LT + c + j] = df[j];
-          rHD = fmaf(hf[j], df[j], rHD);
-        }
+        *reinterpret_cast<float4*>(sH + r * LT + c) = hv;
+        *reinterpret_cast<float4*>(sD + r * LT + c) = dhv;
+        rHD = fmaf(hv.x, dhv.x, fmaf(hv.y, dhv.y, fmaf(hv.z, dhv.z, fmaf(hv.w, dhv.w, rHD))));
       }
       __syncthreads();
-      mac<4, 2, 16, 16, false, true>(aKd, s3, LT, sD, LT, tm, tn, VT);
-      mac<4, 2, 16, 16, false, true>(aQ0, s1, LT, sH, LT, tm, tn, VT);
-      mac<4, 2, 16, 16, false, true>(aM, s2, LT, sH, LT, tm, tn, VT);
+      warp_mma<1, 2, false, true, kSplit>(aKd, s3, LT, sD, LT, mw, nw, VT);
+      warp_mma<1, 2, false, true, kSplit>(aQ0, s1, LT, sH, LT, mw, nw, VT);
+      warp_mma<1, 2, false, true, kSplit>(aM, s2, LT, sH, LT, mw, nw, VT);
     }
     __syncthreads();
-    load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
-    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
-    load_tokens<KT, LT>(s4, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, sb);
+    load_tokens<KT, LB>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT, LB>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT, LB>(s4, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, sb);
     __syncthreads();
-    float aq[4][2], ak[4][2], ak2[4][2];
+    float aq[1][2][4], ak[1][2][4], ak2[1][2][4];
     zero(aq); zero(ak); zero(ak2);
-    mac<4, 2, 16, 16, false, false>(aq, sPE, LC, s2, LT, tm, tn, C);
-    mac<4, 2, 16, 16, true, false>(ak, sPE, LC, s1, LT, tm, tn, C);
-    mac<4, 2, 16, 16, true, false>(ak, sAE, LC, s4, LT, tm, tn, C);
-    mac<4, 2, 16, 16, false, false>(ak2, sAE, LC, s2, LT, tm, tn, C);
+    warp_mma<1, 2, false, false, kSplit>(aq, sPE, LC, s2, LB, mw, nw, C);
+    warp_mma<1, 2, true, false, kSplit>(ak, sPE, LC, s1, LB, mw, nw, C);
+    warp_mma<1, 2, true, false, kSplit>(ak, sAE, LC, s4, LB, mw, nw, C);
+    warp_mma<1, 2, false, false, kSplit>(ak2, sAE, LC, s2, LB, mw, nw, C);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int m = tm + 16 * i, t = t0 + m;
-      const float em = se[m], dm = sd[m], bm = sb[m], bem = sbe[m];
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int c = tn + 16 * j, col = kt + c;
-        const float kv = s2[m * LT + c], qv = s1[m * LT + c];
-        const float dq = fmaf(em, aQ0[i][j], aq[i][j]);
-        const float dkv = dm * aKd[i][j] - bem * aM[i][j] + ak[i][j] + bm * ak2[i][j];
-        rG[i] += -dm * aKd[i][j] * kv + em * aQ0[i][j] * qv - bem * aM[i][j] * kv;
-        rB[i] -= em * aM[i][j] * kv;
-        rGC = fmaf(dm * aKd[i][j], kv, rGC);
+      for (int e = 0; e < 4; e += 2) {
+        const int m = f.row(mw, 0, e), c = f.col(nw, j, e), col = kt + c, t = t0 + m;
+        const float em = se[m], dm = sd[m], bm = sb[m], bem = sbe[m];
+        float dq[2], dkv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float kv = s2[m * LB + c + u], qv = s1[m * LB + c + u];
+          const float kd = aKd[0][j][e + u], q0 = aQ0[0][j][e + u], mm = aM[0][j][e + u];
+          dq[u] = fmaf(em, q0, aq[0][j][e + u]);
+          dkv[u] = dm * kd - bem * mm + ak[0][j][e + u] + bm * ak2[0][j][e + u];
+          rG[e >> 1] += -dm * kd * kv + em * q0 * qv - bem * mm * kv;
+          rB[e >> 1] -= em * mm * kv;
+          rGC = fmaf(dm * kd, kv, rGC);
+        }
         if (t < p.T && col < p.dk) {
           if (grouped) {
             const size_t off = ((bT + t) * p.H + h) * p.dk + col;
-            p.dqk[off] = dq;
-            p.dqk[(size_t)p.B * p.T * p.H * p.dk + off] = dkv;
+            store2(p.dqk + off, dq[0], dq[1]);
+            store2(p.dqk + (size_t)p.B * p.T * p.H * p.dk + off, dkv[0], dkv[1]);
           } else {
             const size_t off = ((bT + t) * p.Hk + hq) * p.dk + col;
-            static_cast<Tin*>(p.dq)[off] = from_f32<Tin>(dq);
-            static_cast<Tin*>(p.dk_out)[off] = from_f32<Tin>(dkv);
+            store2(static_cast<Tin*>(p.dq) + off, dq[0], dq[1]);
+            store2(static_cast<Tin*>(p.dk_out) + off, dkv[0], dkv[1]);
           }
         }
       }
-    }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float rg = half_warp_sum(rG[i]), rb = half_warp_sum(rB[i]);
-    if (tn == 0) {
-      sdG[tm + 16 * i] += rg;
-      sdB[tm + 16 * i] += rb;
+  for (int hh = 0; hh < 2; ++hh) {
+    const float rg = quad_sum(rG[hh]), rb = quad_sum(rB[hh]);
+    if (f.t == 0) {
+      sRg[(w & 1) * C + mw + f.g + 8 * hh] = rg;
+      sRb[(w & 1) * C + mw + f.g + 8 * hh] = rb;
     }
   }
   // dG_C = e^gamma <h, dh_out> + sum(d K o V' dh_out^T)
   float x = fmaf(se[C - 1], rHD, rGC);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  if ((tid & 31) == 0) sred[tid >> 5] = x;
+  if ((tid & 31) == 0) sred[w] = x;
+  __syncthreads();
+  if (tid < C) {
+    sdG[tid] += sRg[tid] + sRg[C + tid];
+    sdB[tid] += sRb[tid] + sRb[C + tid];
+  }
   __syncthreads();
   if (tid < 32) {
     float y = tid < NT / 32 ? sred[tid] : 0.f;
