@@ -2,10 +2,13 @@
 
     python -m gated_deltanet_jax_b200._profile decode  --launches 3
     python -m gated_deltanet_jax_b200._profile prefill --launches 2 [--B 4 --T 4096]
+    python -m gated_deltanet_jax_b200._profile backward --launches 2 [--B 4 --T 4096]
 
 decode:  B=64 H=16 dk=dv=128, bf16 q/k/v, fp32 state ~N(0,0.02) updated in
          place, one token per launch (the decode workload of bench.py).
 prefill: B=4 T=4096 H=16 dk=dv=128 chunk=64, bf16 in, fp32 final state out.
+backward: gradients of q, k, v, g, beta for the prefill workload from a bf16
+         dO, no initial state (one gdn_chunk_bwd call per launch).
 """
 
 from __future__ import annotations
@@ -33,7 +36,7 @@ def _inputs(B, T, H, dk, dv, seed, dev):
 
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("workload", choices=["decode", "prefill"])
+    p.add_argument("workload", choices=["decode", "prefill", "backward"])
     p.add_argument("--launches", type=int, default=3)
     p.add_argument("--B", type=int, default=None)
     p.add_argument("--T", type=int, default=None)
@@ -51,13 +54,23 @@ def main(argv=None):
         for _ in range(a.launches):
             ops.fused_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=S,
                                                  final_state_out=S)
-    else:
+    elif a.workload == "prefill":
         B, T = a.B or 4, a.T or 4096
         q, k, v, g, beta = _inputs(B, T, a.H, a.dk, a.dv, 0, dev)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for _ in range(a.launches):
             ops.chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True)
+    else:
+        B, T = a.B or 4, a.T or 4096
+        q, k, v, g, beta = _inputs(B, T, a.H, a.dk, a.dv, 0, dev)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1)
+        do = torch.randn(B, T, a.H, a.dv, device=dev, generator=gen).bfloat16()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(a.launches):
+            ops._chunk_backward(q, k, v, g, beta, None, do, None)
     torch.cuda.synchronize()
     print(f"{a.workload}: {a.launches} launches in {time.perf_counter() - t0:.3f} s")
     return 0
