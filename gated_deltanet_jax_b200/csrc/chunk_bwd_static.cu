@@ -1,12 +1,13 @@
 // Fixed scratch for the allocation-free backward (gdn_chunk_bwd_noalloc).
 //
-// The backward needs device scratch: the state entering every chunk, kept
-// from its forward re-run, and fp32 accumulators for dq, dk, dbeta and the
-// gate gradient (gdn_chunk_bwd_workspace_bytes).  gdn_chunk_bwd takes that
-// scratch from the caller.  Some callers cannot hand it over or allocate it:
-// a host framework that owns the device memory (XLA reserves most of HBM for
-// its own pool and passes a custom call only the buffers it declared), or a
-// loop that must not stop for cudaMalloc, which can synchronise the device.
+// The backward needs device scratch (gdn_chunk_bwd_workspace_bytes): the
+// state entering and the state gradient leaving every chunk, four per-chunk
+// products, and per-value-head dq / dk for grouped heads.  gdn_chunk_bwd takes
+// that scratch from the caller.  Some callers cannot hand it over or allocate
+// it: a host framework that owns the device memory and gives the call no
+// scratch (XLA reserves most of HBM for its own pool, so a cudaMalloc inside
+// one of its custom calls can fail or fragment memory), or a loop that must
+// not stop for cudaMalloc, which can synchronise the device.
 // For them the scratch lives here, in one array of this library's own device
 // memory, reserved when the CUDA driver loads this file's code on a GPU and
 // held until the process exits.

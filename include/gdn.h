@@ -143,9 +143,10 @@ size_t gdn_chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
  * The backward with no device allocation anywhere: no counterpart in the
  * reference (which has no backward of its own), an addition for callers that
  * cannot allocate device memory and cannot pass gdn_chunk_bwd its workspace --
- * e.g. a jax.ffi handler inside XLA, which keeps most of HBM in its own pool
- * and hands a custom call only the buffers it declared, or a loop that must
- * not stop for cudaMalloc, which can synchronise the whole device.
+ * e.g. a custom-call handler inside XLA without access to its scratch allocator
+ * (XLA keeps most of HBM in its own pool, so a cudaMalloc there can fail or
+ * fragment memory), or a loop that must not stop for cudaMalloc, which can
+ * synchronise the whole device.
  *
  * Arguments and results are gdn_chunk_bwd's, without the workspace: the
  * caller still passes every input and output.  The scratch is instead a

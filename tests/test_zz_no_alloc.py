@@ -1,9 +1,9 @@
 """The allocation-free backward, gdn_chunk_bwd_noalloc, through the C ABI.
 
 It exists for callers that cannot allocate device memory or pass a workspace
-(a jax.ffi handler whose device memory XLA owns, a loop that must not stop
-for cudaMalloc): its scratch is one fixed array of the library's own device
-memory that every call on a GPU shares.  So the check is that consecutive
+(a custom call inside a framework that owns the device memory and gives it no
+scratch, a loop that must not stop for cudaMalloc): its scratch is one fixed
+array of the library's own device memory that every call on a GPU shares.  So the check is that consecutive
 calls each give what gdn_chunk_bwd gives with a workspace of its own on the
 same inputs, whatever the previous call left in the array: first the largest
 size the array holds, then a smaller call in another dtype (whose
