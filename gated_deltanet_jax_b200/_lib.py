@@ -33,6 +33,8 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_bwd",
     "gdn_chunk_bwd_noalloc",
     "gdn_chunk_bwd_workspace_bytes",
+    "gdn_chunk_bwd_varlen",
+    "gdn_chunk_bwd_varlen_workspace_bytes",
     "gdn_chunk_workspace_bytes",
     "gdn_last_error",
     "gdn_device_error",
@@ -77,6 +79,10 @@ def _declare(lib):
     lib.gdn_chunk_bwd_noalloc.restype = _i
     lib.gdn_chunk_bwd_workspace_bytes.argtypes = [_i] * 5
     lib.gdn_chunk_bwd_workspace_bytes.restype = _sz
+    lib.gdn_chunk_bwd_varlen.argtypes = [_vp] * 15 + [_i] * 7 + [_vp, _sz, _vp]
+    lib.gdn_chunk_bwd_varlen.restype = _i
+    lib.gdn_chunk_bwd_varlen_workspace_bytes.argtypes = [_i] * 5
+    lib.gdn_chunk_bwd_varlen_workspace_bytes.restype = _sz
     lib.gdn_chunk_workspace_bytes.argtypes = [_i] * 8
     lib.gdn_chunk_workspace_bytes.restype = _sz
     lib.gdn_last_error.argtypes = []

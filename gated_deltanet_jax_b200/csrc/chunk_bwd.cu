@@ -71,9 +71,49 @@ struct BwdParams {
   float* YX;    // [B*H][Np][dv]      Y, then dX
   float* hs;    // [B*H][N][dk][dv]   state entering chunk n
   float* dhs;   // [B*H][N][dk][dv]   gradient of the state leaving chunk n
-  float* dqk;   // [2][B][T][H][dk]   per value head dq, dk (grouped heads only)
+  float* dqk;   // [2][tokens][H][dk] per value head dq, dk (grouped heads only)
+  // Sequences: dense, B sequences of T tokens ([B, T, ...] is one row of B T
+  // tokens), N chunks each; packed (cu != NULL), n_seqs sequences of one row
+  // of T tokens, sequence s the tokens [cu[s], cu[s + 1]) and its chunks
+  // coff[s] .. coff[s + 1] - 1.  Chunk c of every head owns workspace rows
+  // (c H + h) C .. + C - 1 and state tile c H + h.
+  const int* cu;
+  const int* coff;
+  int n_seqs;
   int B, T, H, Hk, dk, dv, N, ldw;
 };
+
+// Tokens and chunks of sequence s.
+struct SeqSpan {
+  size_t tok0;   // first token in the packed row
+  int len;       // tokens
+  int cfirst;    // first global chunk
+  int nch;       // chunks
+};
+
+__device__ __forceinline__ SeqSpan seq_span(const BwdParams& p, int s) {
+  SeqSpan r;
+  if (!p.cu) {
+    r.tok0 = (size_t)s * p.T; r.len = p.T; r.cfirst = s * p.N; r.nch = p.N;
+  } else {
+    const int a0 = min(max(p.cu[s], 0), p.T);
+    const int a1 = min(max(p.cu[s + 1], a0), p.T);
+    r.tok0 = (size_t)a0; r.len = a1 - a0; r.cfirst = p.coff[s]; r.nch = p.coff[s + 1] - p.coff[s];
+  }
+  return r;
+}
+
+// The sequence that global chunk c belongs to, or -1 past the last chunk.
+__device__ __forceinline__ int seq_of_chunk(const BwdParams& p, int c) {
+  if (!p.cu) return c < p.B * p.N ? c / p.N : -1;
+  if (c >= p.coff[p.n_seqs]) return -1;
+  int lo = 0, hi = p.n_seqs;   // coff[lo] <= c < coff[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (p.coff[mid] <= c) lo = mid; else hi = mid;
+  }
+  return lo;
+}
 
 // ---------------------------------------------------------------------------
 // Warp-level tensor-core products: mma.sync m16n8k8 with tf32 operands and
@@ -261,17 +301,17 @@ __device__ __forceinline__ void load_block(float* s, const float* src, int D, in
 }
 
 // Gate vectors of one chunk (warp 0): G (inclusive cumulative gate), e^G,
-// e^{gamma - G}, beta, beta e^G.  Tokens past T have g = beta = 0.
-__device__ __forceinline__ void chunk_gates(const BwdParams& p, int b, int h, int t0, float* sG,
-                                            float* se, float* sd, float* sb, float* sbe) {
+// e^{gamma - G}, beta, beta e^G.  Tokens past the sequence's end have g = beta = 0.
+__device__ __forceinline__ void chunk_gates(const BwdParams& p, size_t base, int Tn, int h, int t0,
+                                            float* sG, float* se, float* sd, float* sb,
+                                            float* sbe) {
   if (threadIdx.x >= 32) return;
   const int l = threadIdx.x;
-  const size_t base = (size_t)b * p.T;
   const int ta = t0 + l, tb = t0 + 32 + l;
-  float x0 = ta < p.T ? p.g[(base + ta) * p.H + h] : 0.f;
-  float x1 = tb < p.T ? p.g[(base + tb) * p.H + h] : 0.f;
-  const float b0 = ta < p.T ? p.beta[(base + ta) * p.H + h] : 0.f;
-  const float b1 = tb < p.T ? p.beta[(base + tb) * p.H + h] : 0.f;
+  float x0 = ta < Tn ? p.g[(base + ta) * p.H + h] : 0.f;
+  float x1 = tb < Tn ? p.g[(base + tb) * p.H + h] : 0.f;
+  const float b0 = ta < Tn ? p.beta[(base + ta) * p.H + h] : 0.f;
+  const float b1 = tb < Tn ? p.beta[(base + tb) * p.H + h] : 0.f;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
@@ -309,12 +349,15 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   const Tin* k = static_cast<const Tin*>(p.k);
   const Tin* v = static_cast<const Tin*>(p.v);
   const Tin* dO = static_cast<const Tin*>(p.dO);
-  const int n = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int gc = blockIdx.x, h = blockIdx.y, sq = seq_of_chunk(p, gc);
+  if (sq < 0) return;   // past the last chunk (packed sequences)
+  const SeqSpan sp = seq_span(p, sq);
+  const int n = gc - sp.cfirst, Tn = sp.len;
   const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x, w = tid >> 5;
-  const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
-  const size_t row0 = (size_t)bh * Np + t0;
+  const size_t bT = sp.tok0;
+  const size_t row0 = ((size_t)gc * p.H + h) * C;
   const Frag f;
-  chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
+  chunk_gates(p, bT, Tn, h, t0, sG, se, sd, sb, sbe);
 
   // Q K^T and K K^T over dk tiles; warp: rows mq.., columns nq..
   const int mq = (w >> 1) * 16, nq = (w & 1) * 32;
@@ -322,8 +365,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   zero(aQK); zero(aKK);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
-    load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
-    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s1, q, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s2, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
     __syncthreads();
     warp_mma<1, 4, false, true, kSplit>(aQK, s1, LT, s2, LT, mq, nq, KT);
     warp_mma<1, 4, false, true, kSplit>(aKK, s2, LT, s2, LT, mq, nq, KT);
@@ -354,8 +397,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   const int mw = (w >> 1) * 16, nw = (w & 1) * 16;
   for (int c0 = 0; c0 < p.ldw; c0 += KT) {
     __syncthreads();
-    load_tokens<KT, LB>(s1, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sbe);
-    load_tokens<KT, LB>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, sd);
+    load_tokens<KT, LB>(s1, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, sbe);
+    load_tokens<KT, LB>(s2, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, sd);
     __syncthreads();
     float aw[1][2][4], az[1][2][4];
     zero(aw); zero(az);
@@ -373,8 +416,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   // U = T (beta V), Y = T^T (P^T dO) per dv tile
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
-    load_tokens<VT, LB>(s1, v, bT, t0, p.T, p.H, h, p.dv, c0, sb);
-    load_tokens<VT, LB>(s2, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_tokens<VT, LB>(s1, v, bT, t0, Tn, p.H, h, p.dv, c0, sb);
+    load_tokens<VT, LB>(s2, dO, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
     __syncthreads();
     float au[1][2][4], ap[1][2][4];
     zero(au); zero(ap);
@@ -446,10 +489,12 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
   const Tin* q = static_cast<const Tin*>(p.q);
   const Tin* k = static_cast<const Tin*>(p.k);
   const Tin* dO = static_cast<const Tin*>(p.dO);
-  const int c0 = blockIdx.x * VT, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int c0 = blockIdx.x * VT, bh = blockIdx.y, sq = bh / p.H, h = bh - sq * p.H;
   const int hq = h * p.Hk / p.H, tid = threadIdx.x, w = tid >> 5;
   const bool rev = blockIdx.z != 0;
-  const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
+  const SeqSpan sp = seq_span(p, sq);
+  const size_t bT = sp.tok0;
+  const int Tn = sp.len;
   const Frag f;
   const int mv = (w >> 1) * 16, nv = (w & 1) * 16;       // C x VT products
   const int ms = ST::m0(w), ns = ST::n0(w);              // DKP x VT products
@@ -459,20 +504,20 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
     sS[r * SS + c] = (init && r < p.dk) ? init[((size_t)bh * p.dk + r) * p.dv + c0 + c] : 0.f;
   }
   float* keep = rev ? p.dhs : p.hs;
-  for (int it = 0; it < p.N; ++it) {
-    const int n = rev ? p.N - 1 - it : it, t0 = n * C;
-    const size_t row0 = (size_t)bh * Np + t0;
+  for (int it = 0; it < sp.nch; ++it) {
+    const int n = rev ? sp.nch - 1 - it : it, t0 = n * C, gc = sp.cfirst + n;
+    const size_t row0 = ((size_t)gc * p.H + h) * C;
     __syncthreads();
     for (int e = tid * 4; e < DKP * VT; e += NT * 4) {
       const int r = e / VT, c = e - r * VT;
       if (r < p.dk)
-        *reinterpret_cast<float4*>(keep + (((size_t)bh * p.N + n) * p.dk + r) * p.dv + c0 + c) =
+        *reinterpret_cast<float4*>(keep + (((size_t)gc * p.H + h) * p.dk + r) * p.dv + c0 + c) =
             *reinterpret_cast<const float4*>(sS + r * SS + c);
     }
     load_block<DKP, LW>(sM, (rev ? p.Z : p.W) + row0 * p.ldw, p.ldw, 0);
     load_block<VT, LB>(sU, (rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
-    chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
-    if (!rev) load_tokens<DKP, LK>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
+    chunk_gates(p, bT, Tn, h, t0, sG, se, sd, sb, sbe);
+    if (!rev) load_tokens<DKP, LK>(sK, k, bT, t0, Tn, p.Hk, hq, p.dk, 0, nullptr);
     __syncthreads();
     // forward: V' = U - W h;  reverse: dX = Y + Z dh
     float acc[1][2][4];
@@ -497,9 +542,9 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
       }
     if (rev) {
       __syncthreads();   // Z in sM has been read; sM now takes Q
-      load_tokens<DKP, LW>(sM, q, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<DKP, LK>(sK, k, bT, t0, p.T, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<VT, LB>(sO, dO, bT, t0, p.T, p.H, h, p.dv, c0, se);
+      load_tokens<DKP, LW>(sM, q, bT, t0, Tn, p.Hk, hq, p.dk, 0, nullptr);
+      load_tokens<DKP, LK>(sK, k, bT, t0, Tn, p.Hk, hq, p.dk, 0, nullptr);
+      load_tokens<VT, LB>(sO, dO, bT, t0, Tn, p.H, h, p.dv, c0, se);
     }
     __syncthreads();
     // forward: h = e^gamma h + K^T (d V');  reverse: dh = e^gamma dh + Q^T (e dO) + K^T (-beta e dX)
@@ -555,15 +600,18 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   const Tin* k = static_cast<const Tin*>(p.k);
   const Tin* v = static_cast<const Tin*>(p.v);
   const Tin* dO = static_cast<const Tin*>(p.dO);
-  const int n = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int gc = blockIdx.x, h = blockIdx.y, sq = seq_of_chunk(p, gc);
+  if (sq < 0) return;   // past the last chunk (packed sequences)
+  const SeqSpan sp = seq_span(p, sq);
+  const int n = gc - sp.cfirst, Tn = sp.len;
   const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x, w = tid >> 5;
-  const size_t bT = (size_t)b * p.T, Np = (size_t)p.N * C;
-  const size_t row0 = (size_t)bh * Np + t0;
+  const size_t bT = sp.tok0;
+  const size_t row0 = ((size_t)gc * p.H + h) * C;
   const Frag f;
   const int mq = (w >> 1) * 16, nq = (w & 1) * 32;   // C x C products
   const int mw = (w >> 1) * 16, nw = (w & 1) * 16;   // C x 32 products
   const bool grouped = p.Hk != p.H;
-  chunk_gates(p, b, h, t0, sG, se, sd, sb, sbe);
+  chunk_gates(p, bT, Tn, h, t0, sG, se, sd, sb, sbe);
   if (tid < C) { sdG[tid] = 0.f; sdB[tid] = 0.f; }
 
   // A. dO V'^T and dX V'^T over dv tiles; rowsum(dX o V); dV = beta dX
@@ -572,10 +620,10 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   Tin* dv_out = static_cast<Tin*>(p.dv_out);
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
-    load_tokens<VT, LT>(s1, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_tokens<VT, LT>(s1, dO, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
     load_block<VT, LT>(s2, p.YX + row0 * p.dv, p.dv, c0);
     load_block<VT, LT>(s3, p.UV + row0 * p.dv, p.dv, c0);
-    load_tokens<VT, LT>(s4, v, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+    load_tokens<VT, LT>(s4, v, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
     __syncthreads();
     warp_mma<1, 4, false, true, kSplit>(aP, s1, LT, s3, LT, mq, nq, VT);
     warp_mma<1, 4, false, true, kSplit>(aA, s2, LT, s3, LT, mq, nq, VT);
@@ -587,7 +635,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
       if (c == 0) sdB[r] += part;
-      if (t < p.T) dv_out[((bT + t) * p.H + h) * p.dv + c0 + c] = from_f32<Tin>(sb[r] * dx);
+      if (t < Tn) dv_out[((bT + t) * p.H + h) * p.dv + c0 + c] = from_f32<Tin>(sb[r] * dx);
     }
   }
 #pragma unroll
@@ -605,8 +653,8 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   zero(aQK); zero(aKK);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
-    load_tokens<KT, LT>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
-    load_tokens<KT, LT>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s1, q, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
+    load_tokens<KT, LT>(s2, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
     __syncthreads();
     warp_mma<1, 4, false, true, kSplit>(aQK, s1, LT, s2, LT, mq, nq, KT);
     warp_mma<1, 4, false, true, kSplit>(aKK, s2, LT, s2, LT, mq, nq, KT);
@@ -654,13 +702,13 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   // C. per dk tile: V' dh^T, dO h^T, dX h^T over dv; then dQ, dK and the row terms
   float rG[2] = {0.f, 0.f}, rB[2] = {0.f, 0.f};
   float rGC = 0.f, rHD = 0.f;
-  const size_t st0 = ((size_t)bh * p.N + n) * p.dk;
+  const size_t st0 = ((size_t)gc * p.H + h) * p.dk;
   for (int kt = 0; kt < p.dk; kt += KT) {
     float aKd[1][2][4], aQ0[1][2][4], aM[1][2][4];
     zero(aKd); zero(aQ0); zero(aM);
     for (int c0 = 0; c0 < p.dv; c0 += VT) {
       __syncthreads();
-      load_tokens<VT, LT>(s1, dO, bT, t0, p.T, p.H, h, p.dv, c0, nullptr);
+      load_tokens<VT, LT>(s1, dO, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
       load_block<VT, LT>(s2, p.YX + row0 * p.dv, p.dv, c0);
       load_block<VT, LT>(s3, p.UV + row0 * p.dv, p.dv, c0);
       {
@@ -682,9 +730,9 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
       warp_mma<1, 2, false, true, kSplit>(aM, s2, LT, sH, LT, mw, nw, VT);
     }
     __syncthreads();
-    load_tokens<KT, LB>(s1, q, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
-    load_tokens<KT, LB>(s2, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, nullptr);
-    load_tokens<KT, LB>(s4, k, bT, t0, p.T, p.Hk, hq, p.dk, kt, sb);
+    load_tokens<KT, LB>(s1, q, bT, t0, Tn, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT, LB>(s2, k, bT, t0, Tn, p.Hk, hq, p.dk, kt, nullptr);
+    load_tokens<KT, LB>(s4, k, bT, t0, Tn, p.Hk, hq, p.dk, kt, sb);
     __syncthreads();
     float aq[1][2][4], ak[1][2][4], ak2[1][2][4];
     zero(aq); zero(ak); zero(ak2);
@@ -709,7 +757,7 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
           rB[e >> 1] -= em * mm * kv;
           rGC = fmaf(dm * kd, kv, rGC);
         }
-        if (t < p.T && col < p.dk) {
+        if (t < Tn && col < p.dk) {
           if (grouped) {
             const size_t off = ((bT + t) * p.H + h) * p.dk + col;
             store2(p.dqk + off, dq[0], dq[1]);
@@ -757,11 +805,11 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
     }
     x0 += __shfl_sync(0xffffffffu, x1, 0);
     const int ta = t0 + l, tb = t0 + 32 + l;
-    if (ta < p.T) {
+    if (ta < Tn) {
       p.dg[(bT + ta) * p.H + h] = x0;
       p.dbeta[(bT + ta) * p.H + h] = sdB[l];
     }
-    if (tb < p.T) {
+    if (tb < Tn) {
       p.dg[(bT + tb) * p.H + h] = x1;
       p.dbeta[(bT + tb) * p.H + h] = sdB[l + 32];
     }
@@ -791,39 +839,102 @@ __global__ void bwd_group_kernel(const BwdParams p) {
   }
 }
 
+// Packed sequences: coff[s] = sum over s' < s of the chunks of sequence s'
+// (offsets clamped to [0, T] as the forward does), coff[n_seqs] = all chunks.
+// Every value is also clamped to NC, the chunks the workspace holds: offsets
+// that rise from 0 to T never reach it, and malformed (overlapping) ones then
+// lose chunks instead of reaching past the workspace.
+// One CTA of 1024 threads, sequences in tiles of 1024.
+__global__ void __launch_bounds__(1024) bwd_chunk_offsets_kernel(const int* cu, int n_seqs, int T,
+                                                                 int NC, int* coff) {
+  __shared__ int warp_incl[32];
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < n_seqs; base += 1024) {
+    const int s = base + tid;
+    int cnt = 0;
+    if (s < n_seqs) {
+      const int a0 = min(max(cu[s], 0), T);
+      const int a1 = min(max(cu[s + 1], a0), T);
+      cnt = (a1 - a0 + C - 1) / C;
+    }
+    int x = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_incl[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int y = warp_incl[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int z = __shfl_up_sync(0xffffffffu, y, o);
+        if (lane >= o) y += z;
+      }
+      warp_incl[lane] = y;
+    }
+    __syncthreads();
+    const int incl = carry + (w ? warp_incl[w - 1] : 0) + x;
+    if (s < n_seqs) coff[s] = min(incl - cnt, NC);
+    __syncthreads();
+    if (tid == 1023) carry = incl;
+    __syncthreads();
+  }
+  if (tid == 0) coff[n_seqs] = min(carry, NC);
+}
+
 // Workspace: offsets in floats, each array on a 256-byte boundary.
 struct WsLayout {
-  size_t W, Z, UV, YX, hs, dhs, dqk, total;
+  size_t W, Z, UV, YX, hs, dhs, dqk, coff, total;
 };
 
 int padded_dk(int dk) { return dk <= 32 ? 32 : dk <= 64 ? 64 : 128; }
 
-WsLayout ws_layout(int B, int T, int H, int dk, int dv) {
-  const size_t N = (size_t)((T + C - 1) / C), Np = N * C, BH = (size_t)B * H;
+// NC chunks per head, tokens in all, n_seqs chunk offsets (0: dense).
+WsLayout ws_layout(size_t NC, size_t tokens, int H, int dk, int dv, int n_seqs) {
   const size_t ldw = (size_t)padded_dk(dk);
   WsLayout L{};
   size_t o = 0;
   auto take = [&](size_t n) { const size_t r = o; o += (n + 63) & ~size_t(63); return r; };
-  L.W = take(BH * Np * ldw);
-  L.Z = take(BH * Np * ldw);
-  L.UV = take(BH * Np * dv);
-  L.YX = take(BH * Np * dv);
-  L.hs = take(BH * N * dk * dv);
-  L.dhs = take(BH * N * dk * dv);
-  L.dqk = take(2 * (size_t)B * T * H * dk);
+  L.W = take(NC * H * C * ldw);
+  L.Z = take(NC * H * C * ldw);
+  L.UV = take(NC * H * C * dv);
+  L.YX = take(NC * H * C * dv);
+  L.hs = take(NC * H * dk * dv);
+  L.dhs = take(NC * H * dk * dv);
+  L.dqk = take(2 * tokens * H * dk);
+  L.coff = take(n_seqs ? (size_t)n_seqs + 1 : 0);
   L.total = o;
   return L;
 }
 
+// Chunks (an upper bound for packed sequences: sum of ceil(len / C) <= T / C + n_seqs).
+size_t chunk_count(const ChunkBwdArgs& a) {
+  return a.cu_seqlens ? (size_t)(a.T / C) + (size_t)a.B
+                      : (size_t)a.B * (size_t)((a.T + C - 1) / C);
+}
+
+WsLayout ws_layout(const ChunkBwdArgs& a) {
+  return ws_layout(chunk_count(a), a.cu_seqlens ? (size_t)a.T : (size_t)a.B * a.T, a.H, a.dk,
+                   a.dv, a.cu_seqlens ? a.B : 0);
+}
+
 template <typename Tin, int DKP>
 cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
-  const WsLayout L = ws_layout(a.B, a.T, a.H, a.dk, a.dv);
+  const WsLayout L = ws_layout(a);
+  const bool packed = a.cu_seqlens != nullptr;
   float* ws = static_cast<float*>(a.workspace);
+  int* coff = packed ? reinterpret_cast<int*>(ws + L.coff) : nullptr;
   const BwdParams p{a.q, a.k, a.v, a.dO, a.g, a.beta, a.h0, a.dhT, a.dq, a.dk_out, a.dv_out,
                     a.dg, a.dbeta, a.dh0, ws + L.W, ws + L.Z, ws + L.UV, ws + L.YX,
-                    ws + L.hs, ws + L.dhs, ws + L.dqk, a.B, a.T, a.H, a.Hk, a.dk, a.dv,
-                    (a.T + C - 1) / C, DKP};
-  const int BH = a.B * a.H;
+                    ws + L.hs, ws + L.dhs, ws + L.dqk, a.cu_seqlens, coff, packed ? a.B : 0,
+                    packed ? 1 : a.B, a.T, a.H, a.Hk, a.dk, a.dv,
+                    packed ? 0 : (a.T + C - 1) / C, DKP};
+  const int NC = (int)chunk_count(a);
   static std::atomic<int> set_prep[kMaxDevices] = {}, set_states[kMaxDevices] = {},
                           set_grads[kMaxDevices] = {};
   const int prep_bytes = kPrepSmemFloats * (int)sizeof(float);
@@ -833,11 +944,12 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   if (e == cudaSuccess) e = ensure_smem(bwd_states_kernel<Tin, DKP>, states_bytes, set_states);
   if (e == cudaSuccess) e = ensure_smem(bwd_grads_kernel<Tin>, grads_bytes, set_grads);
   if (e != cudaSuccess) return e;
-  bwd_prep_kernel<Tin><<<dim3(p.N, BH), NT, prep_bytes, st>>>(p);
-  bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, BH, 2), NT, states_bytes, st>>>(p);
-  bwd_grads_kernel<Tin><<<dim3(p.N, BH), NT, grads_bytes, st>>>(p);
+  if (packed) bwd_chunk_offsets_kernel<<<1, 1024, 0, st>>>(a.cu_seqlens, a.B, a.T, NC, coff);
+  bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);
+  bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 2), NT, states_bytes, st>>>(p);
+  bwd_grads_kernel<Tin><<<dim3(NC, a.H), NT, grads_bytes, st>>>(p);
   if (a.Hk != a.H) {
-    const size_t total = (size_t)a.B * a.T * a.Hk * a.dk;
+    const size_t total = (size_t)p.B * a.T * a.Hk * a.dk;
     const size_t want = (total + 255) / 256, cap = (size_t)8 * device_sm_count();
     bwd_group_kernel<Tin><<<(int)(want < cap ? want : cap), 256, 0, st>>>(p);
   }
@@ -856,15 +968,26 @@ cudaError_t launch_bwd_dtype(const ChunkBwdArgs& a, cudaStream_t st) {
 }  // namespace
 
 size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
-  return sizeof(float) * ws_layout(B, T, H, dk, dv).total;
+  ChunkBwdArgs a{};
+  a.B = B; a.T = T; a.H = H; a.dk = dk; a.dv = dv;
+  return sizeof(float) * ws_layout(a).total;
+}
+
+size_t chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv) {
+  ChunkBwdArgs a{};
+  static const int kPacked = 0;   // any non-NULL pointer: the layout of packed sequences
+  a.cu_seqlens = &kPacked;
+  a.B = n_seqs; a.T = T; a.H = H; a.dk = dk; a.dv = dv;
+  return sizeof(float) * ws_layout(a).total;
 }
 
 bool chunk_bwd_supported(const ChunkBwdArgs& a) {
-  return a.dk >= 1 && a.dk <= 128 && a.dv >= VT && a.dv % VT == 0;
+  return a.dk >= 1 && a.dk <= 128 && a.dv >= VT && a.dv % VT == 0 &&
+         (long long)a.B * a.H <= 65535;
 }
 
 cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st) {
-  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;   // (the caller handles dh0)
   return a.dtype == kBF16 ? launch_bwd_dtype<__nv_bfloat16>(a, st)
                           : launch_bwd_dtype<float>(a, st);
 }

@@ -89,6 +89,12 @@ int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const
               int Hk, int dk, int dv, int chunk, int dtype, int semantics, void* workspace,
               size_t ws_bytes, void* stream);
 
+int chunk_bwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
+              const float* h0, const void* dO, const float* dhT, void* dq, void* dk_out,
+              void* dv_out, float* dg, float* dbeta, float* dh0, const int* cu_seqlens, int B,
+              int T, int H, int Hk, int dk, int dv, int dtype, void* workspace, size_t ws_bytes,
+              void* stream, const char* what);
+
 }  // namespace
 
 extern "C" {
@@ -147,6 +153,52 @@ int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v, const floa
 
 namespace {
 
+// The backward, dense (cu_seqlens NULL: B sequences of T tokens) or packed
+// (B = n_seqs sequences in one row of T tokens).
+int chunk_bwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
+              const float* h0, const void* dO, const float* dhT, void* dq, void* dk_out,
+              void* dv_out, float* dg, float* dbeta, float* dh0, const int* cu_seqlens, int B,
+              int T, int H, int Hk, int dk, int dv, int dtype, void* workspace, size_t ws_bytes,
+              void* stream, const char* what) {
+  const int rows = cu_seqlens ? (B > 0 ? 1 : 0) : B;   // rows of the token tensors
+  int rc = check_common(q, k, v, g, beta, h0, dO, dhT, rows, T, H, dk, dv, dtype);
+  if (rc) return rc;
+  rc = check_groups(H, Hk);
+  if (rc) return rc;
+  if ((long long)rows * T * H > 0) {
+    const void* outs[5] = {dq, dk_out, dv_out, dg, dbeta};
+    const char* names[5] = {"dq", "dk", "dv", "dg", "dbeta"};
+    for (int i = 0; i < 5; ++i) {
+      if (!outs[i]) return fail(GDN_ERR_INVALID, "%s must be non-NULL", names[i]);
+      if (!aligned16(outs[i])) return fail(GDN_ERR_INVALID, "%s is not 16-byte aligned", names[i]);
+    }
+  }
+  if (dh0 && !aligned16(dh0)) return fail(GDN_ERR_INVALID, "dh0 is not 16-byte aligned");
+  gdn::ChunkBwdArgs a{q, k, v, g, beta, h0, dO, dhT, dq, dk_out, dv_out, dg, dbeta, dh0,
+                      B, T, H, Hk, dk, dv, dtype, workspace, ws_bytes};
+  a.cu_seqlens = cu_seqlens;
+  if (!gdn::chunk_bwd_supported(a))
+    return fail(GDN_ERR_UNSUPPORTED, "backward supports dk <= 128, dv a multiple of 32 and "
+                "sequences x heads <= 65535 (dk=%d dv=%d)", dk, dv);
+  const size_t need = cu_seqlens ? gdn_chunk_bwd_varlen_workspace_bytes(B, T, H, dk, dv)
+                                 : gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv);
+  if (ws_bytes < need || (need && !workspace))
+    return fail(GDN_ERR_INVALID, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  if (need && !aligned16(workspace)) return fail(GDN_ERR_INVALID, "workspace is not 16-byte aligned");
+  if (T == 0 || (long long)B * H == 0) {
+    // no tokens: the initial state's gradient is that of the final state
+    if (dh0 && (long long)B * H > 0) {
+      cudaError_t e = dhT ? cudaMemcpyAsync(dh0, dhT, sizeof(float) * (size_t)B * H * dk * dv,
+                                            cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
+                          : cudaMemsetAsync(dh0, 0, sizeof(float) * (size_t)B * H * dk * dv,
+                                            (cudaStream_t)stream);
+      return cuda_status(e, what);
+    }
+    return GDN_OK;
+  }
+  return cuda_status(gdn::launch_chunk_bwd(a, (cudaStream_t)stream), what);
+}
+
 int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
               const float* h0, void* o, float* hT, const int* cu_seqlens, int B, int T, int H,
               int Hk, int dk, int dv, int chunk, int dtype, int semantics, void* workspace,
@@ -199,40 +251,29 @@ int gdn_chunk_bwd(const void* q, const void* k, const void* v, const float* g,
                   int B, int T, int H, int Hk, int dk, int dv, int dtype, void* workspace,
                   size_t ws_bytes, void* stream) {
   g_err[0] = '\0';
-  int rc = check_common(q, k, v, g, beta, h0, dO, dhT, B, T, H, dk, dv, dtype);
-  if (rc) return rc;
-  rc = check_groups(H, Hk);
-  if (rc) return rc;
-  if ((long long)B * T * H > 0) {
-    const void* outs[5] = {dq, dk_out, dv_out, dg, dbeta};
-    const char* names[5] = {"dq", "dk", "dv", "dg", "dbeta"};
-    for (int i = 0; i < 5; ++i) {
-      if (!outs[i]) return fail(GDN_ERR_INVALID, "%s must be non-NULL", names[i]);
-      if (!aligned16(outs[i])) return fail(GDN_ERR_INVALID, "%s is not 16-byte aligned", names[i]);
-    }
-  }
-  if (dh0 && !aligned16(dh0)) return fail(GDN_ERR_INVALID, "dh0 is not 16-byte aligned");
-  gdn::ChunkBwdArgs a{q, k, v, g, beta, h0, dO, dhT, dq, dk_out, dv_out, dg, dbeta, dh0,
-                      B, T, H, Hk, dk, dv, dtype, workspace, ws_bytes};
-  if (!gdn::chunk_bwd_supported(a))
-    return fail(GDN_ERR_UNSUPPORTED, "backward supports dk <= 128 and dv a multiple of 32 "
-                "(dk=%d dv=%d)", dk, dv);
-  const size_t need = gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv);
-  if (ws_bytes < need || (need && !workspace))
-    return fail(GDN_ERR_INVALID, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
-  if (need && !aligned16(workspace)) return fail(GDN_ERR_INVALID, "workspace is not 16-byte aligned");
-  if (T == 0 || (long long)B * H == 0) {
-    // no tokens: the initial state's gradient is that of the final state
-    if (dh0 && (long long)B * H > 0) {
-      cudaError_t e = dhT ? cudaMemcpyAsync(dh0, dhT, sizeof(float) * (size_t)B * H * dk * dv,
-                                            cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
-                          : cudaMemsetAsync(dh0, 0, sizeof(float) * (size_t)B * H * dk * dv,
-                                            (cudaStream_t)stream);
-      return cuda_status(e, "gdn_chunk_bwd (T=0)");
-    }
-    return GDN_OK;
-  }
-  return cuda_status(gdn::launch_chunk_bwd(a, (cudaStream_t)stream), "gdn_chunk_bwd");
+  return chunk_bwd(q, k, v, g, beta, h0, dO, dhT, dq, dk_out, dv_out, dg, dbeta, dh0, nullptr, B,
+                   T, H, Hk, dk, dv, dtype, workspace, ws_bytes, stream, "gdn_chunk_bwd");
+}
+
+size_t gdn_chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv) {
+  if (n_seqs <= 0 || T <= 0 || H <= 0 || dk <= 0 || dv <= 0) return 0;
+  return gdn::chunk_bwd_varlen_workspace_bytes(n_seqs, T, H, dk, dv);
+}
+
+int gdn_chunk_bwd_varlen(const void* q, const void* k, const void* v, const float* g,
+                         const float* beta, const float* h0, const void* dO, const float* dhT,
+                         void* dq, void* dk_out, void* dv_out, float* dg, float* dbeta,
+                         float* dh0, const int* cu_seqlens, int n_seqs, int T, int H, int Hk,
+                         int dk, int dv, int dtype, void* workspace, size_t ws_bytes,
+                         void* stream) {
+  g_err[0] = '\0';
+  if (n_seqs < 0) return fail(GDN_ERR_INVALID, "negative n_seqs=%d", n_seqs);
+  if (n_seqs > 0 && !cu_seqlens) return fail(GDN_ERR_INVALID, "cu_seqlens must be non-NULL");
+  if (cu_seqlens && (reinterpret_cast<uintptr_t>(cu_seqlens) & 3u))
+    return fail(GDN_ERR_INVALID, "cu_seqlens is not 4-byte aligned");
+  return chunk_bwd(q, k, v, g, beta, h0, dO, dhT, dq, dk_out, dv_out, dg, dbeta, dh0,
+                   n_seqs > 0 ? cu_seqlens : nullptr, n_seqs, T, H, Hk, dk, dv, dtype, workspace,
+                   ws_bytes, stream, "gdn_chunk_bwd_varlen");
 }
 
 int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v, const float* g,
@@ -270,6 +311,6 @@ int gdn_device_error(int clear) {
   return a ? a : b;
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 3; }
+int gdn_abi_version(void) { return (1 << 16) | 4; }
 
 }  // extern "C"

@@ -99,9 +99,13 @@ struct ChunkBwdArgs {
   int B, T, H, Hk, dk, dv, dtype;
   void* workspace;
   size_t ws_bytes;
+  // Packed sequences: B = n_seqs sequences in one row of T tokens,
+  // sequence s = tokens [cu_seqlens[s], cu_seqlens[s + 1]).
+  const int* cu_seqlens = nullptr;
 };
 
 size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
+size_t chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv);
 bool chunk_bwd_supported(const ChunkBwdArgs& a);
 cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st);
 // Device address of the allocation-free backward's scratch array on the

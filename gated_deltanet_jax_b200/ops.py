@@ -32,9 +32,11 @@ Differences from the reference, all additive:
   ``cu_seqlens[s]:cu_seqlens[s+1]``, with one state per sequence.  Each
   sequence gets what a call on it alone gives.  (The reference takes one
   dense batch only.)
-* Both ops are differentiable (exact semantics, dense inputs): when an input
-  requires grad, the backward runs the gdn_chunk_bwd kernels.  The reference
-  has no backward of its own; it differentiates its chunk path with JAX.
+* Both ops are differentiable (exact semantics; the chunk op also with
+  ``cu_seqlens``): when an input requires grad, the backward runs the
+  gdn_chunk_bwd kernels (gdn_chunk_bwd_varlen for packed sequences).  The
+  reference has no backward of its own; it differentiates its chunk path with
+  JAX.
 """
 
 from __future__ import annotations
@@ -119,30 +121,48 @@ class _DeltaRuleFn(torch.autograd.Function):
     """Autograd node of both ops (same function: the recurrence, exact semantics)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, g, beta, h0, chunk_size, recurrent):
+    def forward(ctx, q, k, v, g, beta, h0, chunk_size, recurrent, cu_seqlens=None):
         if recurrent:
             o, hT = _recurrent_impl(q, k, v, g, beta, h0, True, None)
         else:
-            o, hT = _chunk_impl(q, k, v, g, beta, h0, True, chunk_size, "exact", None, None)
+            o, hT = _chunk_impl(q, k, v, g, beta, h0, True, chunk_size, "exact", None,
+                                cu_seqlens)
         ctx.set_materialize_grads(False)
         ctx.has_h0 = h0 is not None
         ctx.in_dtypes = (g.dtype, beta.dtype, None if h0 is None else h0.dtype)
-        ctx.save_for_backward(q, k, v, g, beta, h0)
+        ctx.save_for_backward(q, k, v, g, beta, h0, cu_seqlens)
         return o, hT
 
     @staticmethod
     def backward(ctx, do, dhT):
-        q, k, v, g, beta, h0 = ctx.saved_tensors
-        dq, dk, dv, dg, db, dh0 = _chunk_backward(q, k, v, g, beta, h0, do, dhT)
+        q, k, v, g, beta, h0, cu_seqlens = ctx.saved_tensors
+        dq, dk, dv, dg, db, dh0 = _chunk_backward(q, k, v, g, beta, h0, do, dhT, cu_seqlens)
         gd, bd, hd = ctx.in_dtypes
         return (dq, dk, dv, dg.to(gd), db.to(bd), dh0.to(hd) if ctx.has_h0 else None, None,
-                None)
+                None, None)
 
 
-def _chunk_backward(q, k, v, g, beta, h0, do, dhT):
-    """Gradients of the recurrence through the C ABI (gdn_chunk_bwd)."""
+def _check_cu_seqlens(q, cu_seqlens):
+    """Validate packed-sequence offsets (as the forward does); returns N."""
+    if not isinstance(cu_seqlens, torch.Tensor) or cu_seqlens.dim() != 1 or \
+            cu_seqlens.numel() < 1 or cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise ValueError("cu_seqlens must be a 1-D int32/int64 tensor of N+1 offsets")
+    if q.dim() != 4 or q.shape[0] != 1:
+        raise ValueError("with cu_seqlens, q, k, v, g, beta hold one packed row (B == 1)")
+    if not cu_seqlens.is_cuda:
+        c = cu_seqlens.tolist()
+        if c[0] != 0 or c[-1] != q.shape[1] or any(b < a for a, b in zip(c, c[1:])):
+            raise ValueError(f"cu_seqlens must rise from 0 to T={q.shape[1]}; got {c}")
+    return cu_seqlens.numel() - 1
+
+
+def _chunk_backward(q, k, v, g, beta, h0, do, dhT, cu_seqlens=None):
+    """Gradients of the recurrence through the C ABI: gdn_chunk_bwd, or
+    gdn_chunk_bwd_varlen for packed sequences (``cu_seqlens``)."""
+    n_seqs = None if cu_seqlens is None else _check_cu_seqlens(q, cu_seqlens)
     q, k, v, g, beta, h0c, _, _, (B, T, H, Hk, dk, dv) = _prepare(
-        q, k, v, g, beta, h0, None, False)
+        q, k, v, g, beta, h0, None, False, n_seqs)
+    NS = B if n_seqs is None else n_seqs
     dev = q.device
     if do is None:
         do = torch.zeros((B, T, H, dv), dtype=v.dtype, device=dev)
@@ -155,17 +175,26 @@ def _chunk_backward(q, k, v, g, beta, h0, do, dhT):
     dv_ = torch.empty_like(v)
     dg = torch.empty((B, T, H), dtype=torch.float32, device=dev)
     db = torch.empty((B, T, H), dtype=torch.float32, device=dev)
-    dh0 = torch.empty((B, H, dk, dv), dtype=torch.float32, device=dev)
+    dh0 = torch.empty((NS, H, dk, dv), dtype=torch.float32, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
-        ws_bytes = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv)
-        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
         stream = torch.cuda.current_stream(dev).cuda_stream
-        rc = lib.gdn_chunk_bwd(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0c),
-                               _ptr(do), _ptr(dhT_c), _ptr(dq), _ptr(dk_), _ptr(dv_), _ptr(dg),
-                               _ptr(db), _ptr(dh0), B, T, H, Hk, dk, dv, _DTYPES[q.dtype],
-                               _ptr(ws), ws_bytes, stream)
-    _lib.check(rc, "gdn_chunk_bwd")
+        args = (_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0c), _ptr(do),
+                _ptr(dhT_c), _ptr(dq), _ptr(dk_), _ptr(dv_), _ptr(dg), _ptr(db), _ptr(dh0))
+        if n_seqs is None:
+            ws_bytes = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv)
+            ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+            rc = lib.gdn_chunk_bwd(*args, B, T, H, Hk, dk, dv, _DTYPES[q.dtype], _ptr(ws),
+                                   ws_bytes, stream)
+            what = "gdn_chunk_bwd"
+        else:
+            cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+            ws_bytes = lib.gdn_chunk_bwd_varlen_workspace_bytes(n_seqs, T, H, dk, dv)
+            ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+            rc = lib.gdn_chunk_bwd_varlen(*args, _ptr(cu), n_seqs, T, H, Hk, dk, dv,
+                                          _DTYPES[q.dtype], _ptr(ws), ws_bytes, stream)
+            what = "gdn_chunk_bwd_varlen"
+    _lib.check(rc, what)
     return dq, dk_, dv_, dg, db, dh0
 
 
@@ -182,13 +211,17 @@ def chunk_gated_delta_rule_fwd(q, k, v, g, beta, initial_state=None, output_fina
     recurrence; ``"reference"`` reproduces the reference chunk code as written.
     ``cu_seqlens`` (integer ``[N+1]``, non-decreasing from 0 to T) packs N
     sequences into one row: q ``[1,T,Hk,dk]``, states ``[N,H,dk,dv]``.
-    Differentiable (exact semantics, dense inputs) when an input requires grad.
+    Differentiable (exact semantics, dense or packed) when an input requires grad.
     """
     if _wants_grad(q, k, v, g, beta, initial_state):
-        if semantics != "exact" or cu_seqlens is not None or final_state_out is not None:
-            raise NotImplementedError("the backward covers exact semantics on dense inputs "
-                                      "without final_state_out")
-        o, hT = _DeltaRuleFn.apply(q, k, v, g, beta, initial_state, int(chunk_size), False)
+        if semantics != "exact" or final_state_out is not None:
+            raise NotImplementedError("the backward covers exact semantics without "
+                                      "final_state_out")
+        cu = None
+        if cu_seqlens is not None:
+            _check_cu_seqlens(q, cu_seqlens)
+            cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+        o, hT = _DeltaRuleFn.apply(q, k, v, g, beta, initial_state, int(chunk_size), False, cu)
         return (o, hT) if output_final_state else (o, None)
     return _chunk_impl(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
                        semantics, final_state_out, cu_seqlens)
@@ -200,18 +233,9 @@ def _chunk_impl(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
         raise ValueError(f"semantics must be one of {sorted(_SEMANTICS)}; got {semantics!r}")
     n_seqs = None
     if cu_seqlens is not None:
-        if not isinstance(cu_seqlens, torch.Tensor) or cu_seqlens.dim() != 1 or \
-                cu_seqlens.numel() < 1 or cu_seqlens.dtype not in (torch.int32, torch.int64):
-            raise ValueError("cu_seqlens must be a 1-D int32/int64 tensor of N+1 offsets")
-        if q.dim() != 4 or q.shape[0] != 1:
-            raise ValueError("with cu_seqlens, q, k, v, g, beta hold one packed row (B == 1)")
+        n_seqs = _check_cu_seqlens(q, cu_seqlens)
         if semantics != "exact":
             raise ValueError("packed sequences take semantics='exact' only")
-        if not cu_seqlens.is_cuda:
-            c = cu_seqlens.tolist()
-            if c[0] != 0 or c[-1] != q.shape[1] or any(b < a for a, b in zip(c, c[1:])):
-                raise ValueError(f"cu_seqlens must rise from 0 to T={q.shape[1]}; got {c}")
-        n_seqs = cu_seqlens.numel() - 1
     q, k, v, g, beta, h0, hT, o, (B, T, H, Hk, dk, dv) = _prepare(
         q, k, v, g, beta, initial_state, final_state_out, output_final_state, n_seqs)
     lib = _lib.load()

@@ -140,6 +140,27 @@ int gdn_chunk_bwd(const void* q, const void* k, const void* v,
 size_t gdn_chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
 
 /*
+ * The backward of gdn_chunk_fwd_varlen: n_seqs sequences packed back to back
+ * in one row of T tokens (q, k, dq, dk [1, T, Hk, dk]; v, dO, dv [1, T, H, dv];
+ * g, beta, dg, dbeta [1, T, H]; sequence s the tokens [cu_seqlens[s],
+ * cu_seqlens[s + 1]), device int32, offsets clamped to [0, T]); h0, dhT, dh0
+ * [n_seqs, H, dk, dv].  Every sequence gets what gdn_chunk_bwd gives it on its
+ * own.  No counterpart in the reference, whose ops take one dense [B, T]
+ * batch; limits as gdn_chunk_bwd's, and the workspace of
+ * gdn_chunk_bwd_varlen_workspace_bytes().
+ */
+int gdn_chunk_bwd_varlen(const void* q, const void* k, const void* v,
+                         const float* g, const float* beta, const float* h0,
+                         const void* dO, const float* dhT,
+                         void* dq, void* dk, void* dv, float* dg, float* dbeta, float* dh0,
+                         const int* cu_seqlens, int n_seqs, int T, int H, int Hk,
+                         int dk_dim, int dv_dim, int dtype,
+                         void* workspace, size_t ws_bytes, void* stream);
+
+/* Device workspace bytes gdn_chunk_bwd_varlen needs for these sizes. */
+size_t gdn_chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv);
+
+/*
  * The backward with no device allocation anywhere: no counterpart in the
  * reference (which has no backward of its own), an addition for callers that
  * cannot allocate device memory and cannot pass gdn_chunk_bwd its workspace --
@@ -191,7 +212,8 @@ int gdn_device_error(int clear);
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
-/* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward). */
+/* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward;
+ * 1.4: backward of packed sequences, the allocation-free backward). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

@@ -121,3 +121,86 @@ def test_backward_rejects_unsupported(cuda):
 def test_no_device_error_recorded_backward(cuda):
     from gated_deltanet_jax_b200 import _lib
     assert _lib.load().gdn_device_error(1) == 0
+
+
+# ---------------------------------------------------------------------------
+# packed sequences (cu_seqlens)
+# ---------------------------------------------------------------------------
+
+def _packed_problem(lengths, H, Hk, dk, dv, dtype, dev, seed):
+    import numpy as np
+    T = int(sum(lengths))
+    (q, k, v, g, b, _), _ = device_inputs(1, T, H, dk, dv, seed=seed, dtype=dtype, dev=dev)
+    rep = H // Hk
+    q, k = q[:, :, ::rep].contiguous(), k[:, :, ::rep].contiguous()
+    gen = torch.Generator(device=dev).manual_seed(seed + 1)
+    h0 = torch.randn(len(lengths), H, dk, dv, device=dev, generator=gen) * 0.05
+    do = torch.randn(1, T, H, dv, device=dev, generator=gen).to(v.dtype)
+    dhT = torch.randn(len(lengths), H, dk, dv, device=dev, generator=gen)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device=dev)
+    return q, k, v, g, b, h0, do, dhT, cu
+
+
+PACKED = [
+    ([200, 1, 63, 64, 65, 0, 130], 2, 2, 128, 128, "bf16"),
+    ([300, 77], 4, 2, 128, 64, "bf16"),
+    ([33, 0, 70, 16], 2, 1, 32, 64, "fp32"),
+    ([5, 129, 40], 3, 3, 64, 32, "fp32"),
+]
+
+
+@pytest.mark.parametrize("lengths,H,Hk,dk,dv,dtype", PACKED)
+def test_packed_backward_equals_each_sequence_alone(cuda, lengths, H, Hk, dk, dv, dtype):
+    """Every packed sequence gets, bit for bit, what the dense backward gives it alone."""
+    q, k, v, g, b, h0, do, dhT, cu = _packed_problem(lengths, H, Hk, dk, dv, dtype, cuda,
+                                                     seed=len(lengths) + dk)
+    got = ops._chunk_backward(q, k, v, g, b, h0, do, dhT, cu)
+    for s in range(len(lengths)):
+        a0, a1 = int(cu[s]), int(cu[s + 1])
+        sl = slice(a0, a1)
+        one = ops._chunk_backward(q[:, sl], k[:, sl], v[:, sl], g[:, sl], b[:, sl],
+                                  h0[s:s + 1], do[:, sl], dhT[s:s + 1])
+        for name, a, r in zip(("dq", "dk", "dv", "dg", "dbeta"), got[:5], one[:5]):
+            assert torch.equal(a[:, sl], r), f"sequence {s}: {name}"
+        assert torch.equal(got[5][s:s + 1], one[5]), f"sequence {s}: dh0"
+
+
+@pytest.mark.parametrize("lengths,H,Hk,dk,dv,dtype", PACKED[:2] + PACKED[3:])
+def test_packed_backward_against_oracle(cuda, lengths, H, Hk, dk, dv, dtype):
+    q, k, v, g, b, h0, do, dhT, cu = _packed_problem(lengths, H, Hk, dk, dv, dtype, cuda,
+                                                     seed=3 * len(lengths))
+    got = ops._chunk_backward(q, k, v, g, b, h0, do, dhT, cu)
+    rep = H // Hk
+    hq, hk = orc.repeat_heads(f64(q), rep), orc.repeat_heads(f64(k), rep)
+    hv, hg, hb, hh0, hdo, hdhT = f64(v), f64(g), f64(b), f64(h0), f64(do), f64(dhT)
+    for s in range(len(lengths)):
+        a0, a1 = int(cu[s]), int(cu[s + 1])
+        sl = slice(a0, a1)
+        if a1 == a0:
+            torch.testing.assert_close(got[5][s], dhT[s])   # no tokens: dh0 = dhT
+            continue
+        ref = orc.chunk_exact_backward(hq[:, sl], hk[:, sl], hv[:, sl], hg[:, sl], hb[:, sl],
+                                       hh0[s:s + 1], hdo[:, sl], hdhT[s:s + 1], 32)
+        dq_r = ref[0].reshape(1, a1 - a0, Hk, rep, dk).sum(3)
+        dk_r = ref[1].reshape(1, a1 - a0, Hk, rep, dk).sum(3)
+        refs = (dq_r, dk_r) + tuple(ref[2:5])
+        for name, a, r in zip(("dq", "dk", "dv", "dg", "dbeta"), got[:5], refs):
+            err = orc.rel_err(f64(a[:, sl]), r)
+            assert err <= TOL[dtype], f"sequence {s} {name}: rel error {err:.2e}"
+        err = orc.rel_err(f64(got[5][s:s + 1]), ref[5])
+        assert err <= TOL[dtype], f"sequence {s} dh0: rel error {err:.2e}"
+
+
+def test_autograd_through_packed_chunk_op(cuda):
+    lengths = [70, 0, 33, 64]
+    q, k, v, g, b, h0, do, dhT, cu = _packed_problem(lengths, 2, 2, 32, 32, "fp32", cuda, seed=8)
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v, g, b, h0)]
+    o, hT = ops.chunk_gated_delta_rule(*leaves[:5], initial_state=leaves[5],
+                                       output_final_state=True, cu_seqlens=cu)
+    ((o * do).sum() + (hT * dhT).sum()).backward()
+    want = ops._chunk_backward(q, k, v, g, b, h0, do, dhT, cu)
+    for t, r in zip(leaves, want):
+        assert torch.equal(t.grad, r)
+    o2, h2 = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True,
+                                        cu_seqlens=cu)
+    assert torch.equal(o.detach(), o2) and torch.equal(hT.detach(), h2)
