@@ -250,54 +250,83 @@ __device__ __forceinline__ void put_row(float* dst, const float* f, float sc) {
   }
 }
 
-// Rows t0 .. t0+C-1, columns c0 .. c0+W-1 of one head of a [B, T, heads, D]
-// input into shared memory (row stride LD), times rowscale[r] if given; zero
-// past T and past D.  Every load of the thread is issued before the first
-// store, as 16-byte vectors (inputs are 16-byte aligned and D is a multiple of
-// 8 elements).
+// A C x W tile of one head of a [rows, heads, D] input: rows t0 .. t0+C-1 of
+// the sequence starting at row bT, columns c0 .. c0+W-1, zero past the
+// sequence's end (T) and past D.  fetch() issues the thread's 16-byte loads
+// into registers (inputs are 16-byte aligned, D a multiple of 8 elements);
+// put() converts them to fp32 and stores them into shared memory (row stride
+// LD), times rowscale[r] if given.  Between the two the loads are in flight,
+// so a tile fetched before a product arrives while the product runs.
+template <int W, typename Tin>
+struct TokenTile {
+  static constexpr int VE = 16 / (int)sizeof(Tin), PR = W / VE, NV = C * PR / NT;
+  static_assert(W % VE == 0 && (C * PR) % NT == 0, "tile must split evenly into vectors");
+  uint4 raw[NV];
+
+  __device__ __forceinline__ void fetch(const Tin* src, size_t bT, int t0, int T, int heads,
+                                        int hd, int D, int c0) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int e = threadIdx.x + i * NT, r = e / PR, col = c0 + (e - r * PR) * VE, t = t0 + r;
+      raw[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (t < T && col < D)
+        raw[i] = __ldg(reinterpret_cast<const uint4*>(src + ((bT + t) * heads + hd) * D + col));
+    }
+  }
+  template <int LD>
+  __device__ __forceinline__ void put(float* s, const float* rowscale) const {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int e = threadIdx.x + i * NT, r = e / PR, cv = (e - r * PR) * VE;
+      float f[VE];
+      unpack16<Tin>(raw[i], f);
+      put_row<LD, VE>(s + r * LD + cv, f, rowscale ? rowscale[r] : 1.f);
+    }
+  }
+};
+
+// C rows x W columns (from c0) of a row-major [rows][D] fp32 workspace block
+// (D a multiple of 4, 16-byte aligned rows), zero past D; fetch / put as
+// TokenTile.
+template <int W>
+struct BlockTile {
+  static constexpr int PR = W / 4, NV = C * PR / NT;
+  static_assert((C * PR) % NT == 0, "tile must split evenly into vectors");
+  float4 raw[NV];
+
+  __device__ __forceinline__ void fetch(const float* src, int D, int c0) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int e = threadIdx.x + i * NT, r = e / PR, col = c0 + (e - r * PR) * 4;
+      raw[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (col < D) raw[i] = *reinterpret_cast<const float4*>(src + (size_t)r * D + col);
+    }
+  }
+  template <int LD>
+  __device__ __forceinline__ void put(float* s) const {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int e = threadIdx.x + i * NT, r = e / PR, cv = (e - r * PR) * 4;
+      const float f[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+      put_row<LD, 4>(s + r * LD + cv, f, 1.f);
+    }
+  }
+};
+
 template <int W, int LD, typename Tin>
 __device__ __forceinline__ void load_tokens(float* s, const Tin* src, size_t bT, int t0, int T,
                                             int heads, int hd, int D, int c0,
                                             const float* rowscale) {
-  constexpr int VE = 16 / (int)sizeof(Tin), PR = W / VE, NV = C * PR / NT;
-  static_assert(W % VE == 0 && (C * PR) % NT == 0, "tile must split evenly into vectors");
-  uint4 raw[NV];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int e = threadIdx.x + i * NT, r = e / PR, col = c0 + (e - r * PR) * VE, t = t0 + r;
-    raw[i] = make_uint4(0u, 0u, 0u, 0u);
-    if (t < T && col < D)
-      raw[i] = __ldg(reinterpret_cast<const uint4*>(src + ((bT + t) * heads + hd) * D + col));
-  }
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int e = threadIdx.x + i * NT, r = e / PR, cv = (e - r * PR) * VE;
-    float f[VE];
-    unpack16<Tin>(raw[i], f);
-    put_row<LD, VE>(s + r * LD + cv, f, rowscale ? rowscale[r] : 1.f);
-  }
+  TokenTile<W, Tin> tile;
+  tile.fetch(src, bT, t0, T, heads, hd, D, c0);
+  tile.template put<LD>(s, rowscale);
 }
 
-// C rows x W columns (from c0) of a row-major [rows][D] fp32 workspace block
-// (D a multiple of 4, 16-byte aligned rows); zero past D.  Loads first, as in
-// load_tokens.
 template <int W, int LD>
 __device__ __forceinline__ void load_block(float* s, const float* src, int D, int c0) {
-  constexpr int PR = W / 4, NV = C * PR / NT;
-  static_assert((C * PR) % NT == 0, "tile must split evenly into vectors");
-  float4 raw[NV];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int e = threadIdx.x + i * NT, r = e / PR, col = c0 + (e - r * PR) * 4;
-    raw[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (col < D) raw[i] = *reinterpret_cast<const float4*>(src + (size_t)r * D + col);
-  }
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int e = threadIdx.x + i * NT, r = e / PR, cv = (e - r * PR) * 4;
-    const float f[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-    put_row<LD, 4>(s + r * LD + cv, f, 1.f);
-  }
+  BlockTile<W> tile;
+  tile.fetch(src, D, c0);
+  tile.template put<LD>(s);
 }
 
 // Gate vectors of one chunk (warp 0): G (inclusive cumulative gate), e^G,
@@ -363,14 +392,23 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   const int mq = (w >> 1) * 16, nq = (w & 1) * 32;
   float aQK[1][4][4], aKK[1][4][4];
   zero(aQK); zero(aKK);
+  // every tile loop below fetches its next tile before the current products
+  TokenTile<KT, Tin> t1, t2;
+  t1.fetch(q, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+  t2.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, 0);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
-    load_tokens<KT, LT>(s1, q, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
-    load_tokens<KT, LT>(s2, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
+    t1.put<LT>(s1, nullptr);
+    t2.put<LT>(s2, nullptr);
     __syncthreads();
+    if (c0 + KT < p.dk) {
+      t1.fetch(q, bT, t0, Tn, p.Hk, hq, p.dk, c0 + KT);
+      t2.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, c0 + KT);
+    }
     warp_mma<1, 4, false, true, kSplit>(aQK, s1, LT, s2, LT, mq, nq, KT);
     warp_mma<1, 4, false, true, kSplit>(aKK, s2, LT, s2, LT, mq, nq, KT);
   }
+  t2.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, 0);   // first K tile of W, Z (arrives during T)
 #pragma unroll
   for (int j = 0; j < 4; ++j)
 #pragma unroll
@@ -397,9 +435,15 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   const int mw = (w >> 1) * 16, nw = (w & 1) * 16;
   for (int c0 = 0; c0 < p.ldw; c0 += KT) {
     __syncthreads();
-    load_tokens<KT, LB>(s1, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, sbe);
-    load_tokens<KT, LB>(s2, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, sd);
+    t2.put<LB>(s1, sbe);
+    t2.put<LB>(s2, sd);
     __syncthreads();
+    if (c0 + KT < p.ldw) {
+      t2.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, c0 + KT);
+    } else {   // first tiles of U, Y
+      t1.fetch(v, bT, t0, Tn, p.H, h, p.dv, 0);
+      t2.fetch(dO, bT, t0, Tn, p.H, h, p.dv, 0);
+    }
     float aw[1][2][4], az[1][2][4];
     zero(aw); zero(az);
     warp_mma<1, 2, false, false, kSplit>(aw, sT, LC, s1, LB, mw, nw, C);
@@ -416,9 +460,13 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
   // U = T (beta V), Y = T^T (P^T dO) per dv tile
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
-    load_tokens<VT, LB>(s1, v, bT, t0, Tn, p.H, h, p.dv, c0, sb);
-    load_tokens<VT, LB>(s2, dO, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
+    t1.put<LB>(s1, sb);
+    t2.put<LB>(s2, nullptr);
     __syncthreads();
+    if (c0 + VT < p.dv) {
+      t1.fetch(v, bT, t0, Tn, p.H, h, p.dv, c0 + VT);
+      t2.fetch(dO, bT, t0, Tn, p.H, h, p.dv, c0 + VT);
+    }
     float au[1][2][4], ap[1][2][4];
     zero(au); zero(ap);
     warp_mma<1, 2, false, false, kSplit>(au, sT, LC, s1, LB, mw, nw, C);
@@ -618,13 +666,26 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   float aP[1][4][4], aA[1][4][4];
   zero(aP); zero(aA);
   Tin* dv_out = static_cast<Tin*>(p.dv_out);
+  // every tile loop below fetches its next tiles before the current products
+  TokenTile<VT, Tin> tO, tV;
+  BlockTile<VT> tX, tP;
+  tO.fetch(dO, bT, t0, Tn, p.H, h, p.dv, 0);
+  tX.fetch(p.YX + row0 * p.dv, p.dv, 0);
+  tP.fetch(p.UV + row0 * p.dv, p.dv, 0);
+  tV.fetch(v, bT, t0, Tn, p.H, h, p.dv, 0);
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
-    load_tokens<VT, LT>(s1, dO, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
-    load_block<VT, LT>(s2, p.YX + row0 * p.dv, p.dv, c0);
-    load_block<VT, LT>(s3, p.UV + row0 * p.dv, p.dv, c0);
-    load_tokens<VT, LT>(s4, v, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
+    tO.put<LT>(s1, nullptr);
+    tX.put<LT>(s2);
+    tP.put<LT>(s3);
+    tV.put<LT>(s4, nullptr);
     __syncthreads();
+    if (c0 + VT < p.dv) {
+      tO.fetch(dO, bT, t0, Tn, p.H, h, p.dv, c0 + VT);
+      tX.fetch(p.YX + row0 * p.dv, p.dv, c0 + VT);
+      tP.fetch(p.UV + row0 * p.dv, p.dv, c0 + VT);
+      tV.fetch(v, bT, t0, Tn, p.H, h, p.dv, c0 + VT);
+    }
     warp_mma<1, 4, false, true, kSplit>(aP, s1, LT, s3, LT, mq, nq, VT);
     warp_mma<1, 4, false, true, kSplit>(aA, s2, LT, s3, LT, mq, nq, VT);
     // one warp per row: 32 columns
@@ -651,11 +712,18 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   // B. Q K^T and K K^T; the gate and beta terms through P and A
   float aQK[1][4][4], aKK[1][4][4];
   zero(aQK); zero(aKK);
+  TokenTile<KT, Tin> tQ, tK;
+  tQ.fetch(q, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+  tK.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, 0);
   for (int c0 = 0; c0 < p.dk; c0 += KT) {
     __syncthreads();
-    load_tokens<KT, LT>(s1, q, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
-    load_tokens<KT, LT>(s2, k, bT, t0, Tn, p.Hk, hq, p.dk, c0, nullptr);
+    tQ.put<LT>(s1, nullptr);
+    tK.put<LT>(s2, nullptr);
     __syncthreads();
+    if (c0 + KT < p.dk) {
+      tQ.fetch(q, bT, t0, Tn, p.Hk, hq, p.dk, c0 + KT);
+      tK.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, c0 + KT);
+    }
     warp_mma<1, 4, false, true, kSplit>(aQK, s1, LT, s2, LT, mq, nq, KT);
     warp_mma<1, 4, false, true, kSplit>(aKK, s2, LT, s2, LT, mq, nq, KT);
   }
@@ -703,28 +771,46 @@ __global__ void __launch_bounds__(NT, 2) bwd_grads_kernel(const BwdParams p) {
   float rG[2] = {0.f, 0.f}, rB[2] = {0.f, 0.f};
   float rGC = 0.f, rHD = 0.f;
   const size_t st0 = ((size_t)gc * p.H + h) * p.dk;
+  // h and dh_out tiles (KT rows from kt, VT columns from c0): one 16-byte
+  // vector of each per thread
+  static_assert(KT * VT == 4 * NT, "one 16-byte vector of h and of dh per thread");
+  const int hr = tid >> 3, hc = (tid & 7) * 4;
+  float4 hv, dhv;
+  auto fetch_state = [&](int kt, int c0) {
+    hv = make_float4(0.f, 0.f, 0.f, 0.f);
+    dhv = hv;
+    if (kt + hr < p.dk) {
+      const size_t off = (st0 + kt + hr) * p.dv + c0 + hc;
+      hv = *reinterpret_cast<const float4*>(p.hs + off);
+      dhv = *reinterpret_cast<const float4*>(p.dhs + off);
+    }
+  };
+  tO.fetch(dO, bT, t0, Tn, p.H, h, p.dv, 0);
+  tX.fetch(p.YX + row0 * p.dv, p.dv, 0);
+  tP.fetch(p.UV + row0 * p.dv, p.dv, 0);
+  fetch_state(0, 0);
   for (int kt = 0; kt < p.dk; kt += KT) {
     float aKd[1][2][4], aQ0[1][2][4], aM[1][2][4];
     zero(aKd); zero(aQ0); zero(aM);
     for (int c0 = 0; c0 < p.dv; c0 += VT) {
       __syncthreads();
-      load_tokens<VT, LT>(s1, dO, bT, t0, Tn, p.H, h, p.dv, c0, nullptr);
-      load_block<VT, LT>(s2, p.YX + row0 * p.dv, p.dv, c0);
-      load_block<VT, LT>(s3, p.UV + row0 * p.dv, p.dv, c0);
-      {
-        static_assert(KT * VT == 4 * NT, "one 16-byte vector of h and of dh per thread");
-        const int r = tid >> 3, c = (tid & 7) * 4;
-        float4 hv = make_float4(0.f, 0.f, 0.f, 0.f), dhv = hv;
-        if (kt + r < p.dk) {
-          const size_t off = (st0 + kt + r) * p.dv + c0 + c;
-          hv = *reinterpret_cast<const float4*>(p.hs + off);
-          dhv = *reinterpret_cast<const float4*>(p.dhs + off);
-        }
-        *reinterpret_cast<float4*>(sH + r * LT + c) = hv;
-        *reinterpret_cast<float4*>(sD + r * LT + c) = dhv;
-        rHD = fmaf(hv.x, dhv.x, fmaf(hv.y, dhv.y, fmaf(hv.z, dhv.z, fmaf(hv.w, dhv.w, rHD))));
-      }
+      tO.put<LT>(s1, nullptr);
+      tX.put<LT>(s2);
+      tP.put<LT>(s3);
+      *reinterpret_cast<float4*>(sH + hr * LT + hc) = hv;
+      *reinterpret_cast<float4*>(sD + hr * LT + hc) = dhv;
+      rHD = fmaf(hv.x, dhv.x, fmaf(hv.y, dhv.y, fmaf(hv.z, dhv.z, fmaf(hv.w, dhv.w, rHD))));
       __syncthreads();
+      {
+        // the next (dk tile, dv tile) pair
+        const int nc0 = c0 + VT < p.dv ? c0 + VT : 0, nkt = c0 + VT < p.dv ? kt : kt + KT;
+        if (nkt < p.dk) {
+          tO.fetch(dO, bT, t0, Tn, p.H, h, p.dv, nc0);
+          tX.fetch(p.YX + row0 * p.dv, p.dv, nc0);
+          tP.fetch(p.UV + row0 * p.dv, p.dv, nc0);
+          fetch_state(nkt, nc0);
+        }
+      }
       warp_mma<1, 2, false, true, kSplit>(aKd, s3, LT, sD, LT, mw, nw, VT);
       warp_mma<1, 2, false, true, kSplit>(aQ0, s1, LT, sH, LT, mw, nw, VT);
       warp_mma<1, 2, false, true, kSplit>(aM, s2, LT, sH, LT, mw, nw, VT);
