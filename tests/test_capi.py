@@ -121,6 +121,47 @@ def test_packed_sequences_reject_bad_arguments(lib):
         _lib.GDN_ERR_UNSUPPORTED
 
 
+def _bwd_args(p, B=1, T=64, H=2, Hk=2, dk=16, dv=32, ws=None, ws_bytes=0, out=None):
+    o = p if out is None else out
+    return ([p, p, p, p, p, None, p, None, o, o, o, o, o, None]
+            + [B, T, H, Hk, dk, dv, _lib.GDN_DTYPE_BF16, ws, ws_bytes, None])
+
+
+def test_backward_rejects_bad_arguments(lib):
+    """Checked on the host before any CUDA call."""
+    p = ctypes.c_void_p(16)
+    big = 1 << 30
+    assert lib.gdn_chunk_bwd(*_bwd_args(p, dk=256, ws=p, ws_bytes=big)) == _lib.GDN_ERR_UNSUPPORTED
+    assert b"dk <= 128" in lib.gdn_last_error()
+    assert lib.gdn_chunk_bwd(*_bwd_args(p, dv=48, ws=p, ws_bytes=big)) == _lib.GDN_ERR_UNSUPPORTED
+    assert lib.gdn_chunk_bwd(*_bwd_args(p, Hk=3)) == _lib.GDN_ERR_INVALID          # H % Hk
+    assert lib.gdn_chunk_bwd(*_bwd_args(p)) == _lib.GDN_ERR_INVALID                # no workspace
+    assert b"workspace" in lib.gdn_last_error()
+    assert lib.gdn_chunk_bwd(*_bwd_args(p, ws=p, ws_bytes=big,
+                                        out=ctypes.c_void_p(24))) == _lib.GDN_ERR_INVALID
+    assert b"aligned" in lib.gdn_last_error()
+    # packed sequences
+    def varlen(cu, n):
+        a = _bwd_args(p, ws=p, ws_bytes=big)
+        return lib.gdn_chunk_bwd_varlen(*a[:14], cu, n, *a[15:])
+    assert varlen(None, 2) == _lib.GDN_ERR_INVALID
+    assert varlen(p, -1) == _lib.GDN_ERR_INVALID
+    assert varlen(ctypes.c_void_p(18), 2) == _lib.GDN_ERR_INVALID
+    assert b"aligned" in lib.gdn_last_error()
+
+
+def test_backward_workspace_queries(lib):
+    dense = lib.gdn_chunk_bwd_workspace_bytes(4, 4096, 16, 128, 128)
+    assert dense > 1 << 30
+    # packed: an upper bound over any split of the tokens into n_seqs sequences
+    assert lib.gdn_chunk_bwd_varlen_workspace_bytes(4, 4 * 4096, 16, 128, 128) >= dense
+    assert lib.gdn_chunk_bwd_varlen_workspace_bytes(4, 4 * 4096, 16, 128, 128) > \
+        lib.gdn_chunk_bwd_varlen_workspace_bytes(1, 4 * 4096, 16, 128, 128)
+    for args in ((0, 64, 2, 16, 32), (1, 0, 2, 16, 32), (1, 64, -1, 16, 32)):
+        assert lib.gdn_chunk_bwd_workspace_bytes(*args) == 0
+        assert lib.gdn_chunk_bwd_varlen_workspace_bytes(*args) == 0
+
+
 def test_empty_problem_is_a_no_op(lib):
     # B*H == 0: nothing to launch, no CUDA call, OK.
     assert _call_recurrent(lib, B=0) == _lib.GDN_OK
