@@ -331,16 +331,27 @@ __device__ __forceinline__ void load_block(float* s, const float* src, int D, in
 
 // Gate vectors of one chunk (warp 0): G (inclusive cumulative gate), e^G,
 // e^{gamma - G}, beta, beta e^G.  Tokens past the sequence's end have g = beta = 0.
-__device__ __forceinline__ void chunk_gates(const BwdParams& p, size_t base, int Tn, int h, int t0,
-                                            float* sG, float* se, float* sd, float* sb,
-                                            float* sbe) {
+struct GateRegs {
+  float x0, x1, b0, b1;   // g and beta of tokens lane and lane + 32 (warp 0)
+};
+
+__device__ __forceinline__ void gates_fetch(GateRegs& r, const BwdParams& p, size_t base, int Tn,
+                                            int h, int t0) {
   if (threadIdx.x >= 32) return;
   const int l = threadIdx.x;
   const int ta = t0 + l, tb = t0 + 32 + l;
-  float x0 = ta < Tn ? p.g[(base + ta) * p.H + h] : 0.f;
-  float x1 = tb < Tn ? p.g[(base + tb) * p.H + h] : 0.f;
-  const float b0 = ta < Tn ? p.beta[(base + ta) * p.H + h] : 0.f;
-  const float b1 = tb < Tn ? p.beta[(base + tb) * p.H + h] : 0.f;
+  r.x0 = ta < Tn ? p.g[(base + ta) * p.H + h] : 0.f;
+  r.x1 = tb < Tn ? p.g[(base + tb) * p.H + h] : 0.f;
+  r.b0 = ta < Tn ? p.beta[(base + ta) * p.H + h] : 0.f;
+  r.b1 = tb < Tn ? p.beta[(base + tb) * p.H + h] : 0.f;
+}
+
+__device__ __forceinline__ void gates_put(const GateRegs& r, float* sG, float* se, float* sd,
+                                          float* sb, float* sbe) {
+  if (threadIdx.x >= 32) return;
+  const int l = threadIdx.x;
+  float x0 = r.x0, x1 = r.x1;
+  const float b0 = r.b0, b1 = r.b1;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const float y0 = __shfl_up_sync(0xffffffffu, x0, o);
@@ -355,6 +366,14 @@ __device__ __forceinline__ void chunk_gates(const BwdParams& p, size_t base, int
   sd[l] = gate_exp(gam - x0); sd[l + 32] = gate_exp(gam - x1);
   sb[l] = b0; sb[l + 32] = b1;
   sbe[l] = b0 * e0; sbe[l + 32] = b1 * e1;
+}
+
+__device__ __forceinline__ void chunk_gates(const BwdParams& p, size_t base, int Tn, int h, int t0,
+                                            float* sG, float* se, float* sd, float* sb,
+                                            float* sbe) {
+  GateRegs r;
+  gates_fetch(r, p, base, Tn, h, t0);
+  gates_put(r, sG, se, sd, sb, sbe);
 }
 
 // ---------------------------------------------------------------------------
@@ -555,6 +574,23 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
   for (int it = 0; it < sp.nch; ++it) {
     const int n = rev ? sp.nch - 1 - it : it, t0 = n * C, gc = sp.cfirst + n;
     const size_t row0 = ((size_t)gc * p.H + h) * C;
+    // every global load of the step is issued here, before the first wait (fp32
+    // inputs: the reverse pass's Q, K, dO after the dX product -- their rows
+    // would need twice the registers)
+    constexpr bool kEarly = sizeof(Tin) == 2;
+    BlockTile<DKP> tM;
+    BlockTile<VT> tU;
+    TokenTile<DKP, Tin> tK, tQ;
+    TokenTile<VT, Tin> tO;
+    GateRegs gr;
+    tM.fetch((rev ? p.Z : p.W) + row0 * p.ldw, p.ldw, 0);
+    tU.fetch((rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
+    gates_fetch(gr, p, bT, Tn, h, t0);
+    if (!rev || kEarly) tK.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+    if (rev && kEarly) {
+      tQ.fetch(q, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+      tO.fetch(dO, bT, t0, Tn, p.H, h, p.dv, c0);
+    }
     __syncthreads();
     for (int e = tid * 4; e < DKP * VT; e += NT * 4) {
       const int r = e / VT, c = e - r * VT;
@@ -562,10 +598,10 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
         *reinterpret_cast<float4*>(keep + (((size_t)gc * p.H + h) * p.dk + r) * p.dv + c0 + c) =
             *reinterpret_cast<const float4*>(sS + r * SS + c);
     }
-    load_block<DKP, LW>(sM, (rev ? p.Z : p.W) + row0 * p.ldw, p.ldw, 0);
-    load_block<VT, LB>(sU, (rev ? p.YX : p.UV) + row0 * p.dv, p.dv, c0);
-    chunk_gates(p, bT, Tn, h, t0, sG, se, sd, sb, sbe);
-    if (!rev) load_tokens<DKP, LK>(sK, k, bT, t0, Tn, p.Hk, hq, p.dk, 0, nullptr);
+    tM.put<LW>(sM);
+    tU.put<LB>(sU);
+    gates_put(gr, sG, se, sd, sb, sbe);
+    if (!rev) tK.put<LK>(sK, nullptr);
     __syncthreads();
     // forward: V' = U - W h;  reverse: dX = Y + Z dh
     float acc[1][2][4];
@@ -589,10 +625,15 @@ __global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
         }
       }
     if (rev) {
+      if (!kEarly) {
+        tK.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+        tQ.fetch(q, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+        tO.fetch(dO, bT, t0, Tn, p.H, h, p.dv, c0);
+      }
       __syncthreads();   // Z in sM has been read; sM now takes Q
-      load_tokens<DKP, LW>(sM, q, bT, t0, Tn, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<DKP, LK>(sK, k, bT, t0, Tn, p.Hk, hq, p.dk, 0, nullptr);
-      load_tokens<VT, LB>(sO, dO, bT, t0, Tn, p.H, h, p.dv, c0, se);
+      tQ.put<LW>(sM, nullptr);
+      tK.put<LK>(sK, nullptr);
+      tO.put<LB>(sO, se);
     }
     __syncthreads();
     // forward: h = e^gamma h + K^T (d V');  reverse: dh = e^gamma dh + Q^T (e dO) + K^T (-beta e dX)
