@@ -50,6 +50,7 @@ def _args():
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill leg")
     p.add_argument("--no-long", action="store_true", help="skip the long-context leg")
     p.add_argument("--no-backward", action="store_true", help="skip the backward leg")
+    p.add_argument("--no-layer", action="store_true", help="skip the decode layer-core leg")
     return p.parse_args()
 
 
@@ -476,6 +477,72 @@ def prefill_leg(d, a, lib, uuid=None):
     return res
 
 
+def decode_layer_leg(d, a):
+    """One decode token of the layer core (gates from the raw projections, the
+    step, the gated RMSNorm) on the decode workload, two ways, each replayed
+    from a CUDA graph of 64 tokens: the fused kernel (gdn_recurrent_fwd_layer)
+    against the op between the same operations done separately in torch, as
+    the reference layer does them (model.py:136-153)."""
+    import torch
+    from gated_deltanet_jax_b200 import ops
+    B, H, dk, dv, TOK = DEC["B"], DEC["H"], DEC["dk"], DEC["dv"], 64
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(4321 + d.rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(TOK, B, 1, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    k = nrm(torch.randn(TOK, B, 1, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(TOK, B, 1, H, dv, device=d.dev, generator=gen).bfloat16()
+    ra = torch.randn(TOK, B, 1, H, device=d.dev, generator=gen)
+    rb = torch.randn(TOK, B, 1, H, device=d.dev, generator=gen)
+    gate = torch.randn(TOK, B, 1, H, dv, device=d.dev, generator=gen).bfloat16()
+    A_log = torch.log(torch.rand(H, device=d.dev, generator=gen) * 16 + 1e-4)
+    dt_bias = torch.randn(H, device=d.dev, generator=gen) * 0.5
+    w = torch.ones(dv, device=d.dev)
+    S = torch.randn(NBUF, B, H, dk, dv, device=d.dev, generator=gen) * 0.02
+
+    def fused():
+        for t in range(TOK):
+            st = S[t % NBUF]
+            ops.gated_delta_rule_decode_layer(q[t], k[t], v[t], ra[t], rb[t], A_log, dt_bias,
+                                              gate=gate[t], norm_weight=w, initial_state=st,
+                                              final_state_out=st)
+
+    def unfused():
+        for t in range(TOK):
+            st = S[t % NBUF]
+            gd = -torch.exp(A_log) * torch.nn.functional.softplus(ra[t] + dt_bias)
+            bd = torch.sigmoid(rb[t])
+            o, _ = ops.fused_recurrent_gated_delta_rule(q[t], k[t], v[t], gd, bd,
+                                                        initial_state=st, final_state_out=st)
+            x = o.float()
+            var = x.pow(2).mean(-1, keepdim=True)
+            (x * torch.rsqrt(var + 1e-5) * w
+             * torch.nn.functional.silu(gate[t].float())).to(o.dtype)
+
+    res = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        fn()                                   # load modules, allocate
+        torch.cuda.synchronize(d.dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(a.warmup):
+            graph.replay()
+        steps = max(1, min(a.steps, 50))
+        ms, _ = _timed(d, graph.replay, steps)
+        res[name] = ms * 1e3 / TOK
+        del graph
+    return {"workload": "one decode token of the layer core: B=64 H=16 dk=dv=128 bf16, gates "
+                        "from raw a/b projections, gated RMSNorm (eps 1e-5) of the output; "
+                        f"states round robin over {NBUF} x 64 MiB; 64 tokens per CUDA graph",
+            "fused_us_per_token": res["fused"], "unfused_us_per_token": res["unfused"],
+            "speedup": res["unfused"] / res["fused"],
+            "launches": 2 * TOK * max(1, min(a.steps, 50)),
+            "fused_tokens_per_s": d.world * B / (res["fused"] / 1e6),
+            "path": "fused: gdn_recurrent_fwd_layer (1 launch per token); unfused: torch gates, "
+                    "gdn_recurrent_fwd, torch gated RMSNorm"}
+
+
 def backward_leg(d, a, lib):
     """The chunked backward (gdn_chunk_bwd) on the prefill workload: gradients of
     q, k, v, g, beta from dO, every buffer resident, one C-ABI call per step."""
@@ -599,6 +666,7 @@ def main():
     pre = None if a.no_prefill else prefill_leg(d, a, lib, uuid)
     lng = None if a.no_long else long_context_leg(d, a)
     bwd = None if a.no_backward else backward_leg(d, a, lib)
+    lay = None if a.no_layer else decode_layer_leg(d, a)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not a.no_cpu:
@@ -627,7 +695,7 @@ def main():
                          "traffic": traffic,
                          "algorithmic_bytes_per_launch": dec["bytes_launch"]},
             "gpu_launches": (dec["launches"] + (pre["launches"] if pre else 0)
-                             + (bwd["launches"] if bwd else 0)),
+                             + (bwd["launches"] if bwd else 0) + (lay["launches"] if lay else 0)),
             "clocks": dec["clocks"],
         }
         if "e2e" in dec:
@@ -657,6 +725,8 @@ def main():
             line["prefill"] = pre_line
         if lng:
             line["long_context"] = lng
+        if lay:
+            line["decode_layer"] = lay
         if bwd:
             if pre:
                 bwd["fwd_plus_bwd_tokens_per_s"] = (d.world * PRE["B"] * PRE["T"]

@@ -112,11 +112,24 @@ cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st);
 // current device (looked up on the first call per device, then kept).
 cudaError_t chunk_bwd_static_scratch(void** out);
 
+// The layer form of the decode step (model.py:136-139 before it, :47-53 after).
+struct LayerArgs {
+  const float* a = nullptr;         // raw a_proj output, one per (b, h)
+  const float* b = nullptr;         // raw b_proj output, one per (b, h)
+  const float* A_log = nullptr;     // [H]
+  const float* dt_bias = nullptr;   // [H]
+  const void* gate = nullptr;       // [B, H, dv] output gate (input dtype), NULL: plain RMSNorm
+  const float* weight = nullptr;    // [dv] norm weight
+  float eps = 1e-5f;
+};
+
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);
 
 // Decode step (T == 1) with the state streamed by bulk copies (dk = dv = 128).
 bool recurrent_bulk_supported(const RecurrentArgs& a);
 cudaError_t launch_recurrent_bulk(const RecurrentArgs& a, cudaStream_t st);
+cudaError_t launch_recurrent_bulk_layer(const RecurrentArgs& a, const LayerArgs& la,
+                                        cudaStream_t st);
 
 // Device error words of the kernel files with bounded waits (0 = none).
 int device_error_recurrent_bulk(bool clear);

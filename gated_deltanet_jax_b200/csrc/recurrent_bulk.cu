@@ -17,6 +17,14 @@
 //
 // HBM traffic per head: the state read and written once, plus q, k, v, o,
 // g, beta.  Every mbarrier wait is bounded (ptx.cuh).
+//
+// The layer form (kLayer) also does the work of the GatedDeltaNet layer on
+// either side of the step (model.py:136-139 and :47-53), for one token:
+//   prologue  beta = sigmoid(b), g = -exp(A_log[h]) softplus(a + dt_bias[h]),
+//             from the raw a_proj / b_proj outputs a, b;
+//   epilogue  y = o rsqrt(mean(o^2) + eps) w (silu(gate) if a gate is given),
+//             over the head's dv outputs, which warp 0 holds (4 per lane), in
+//             fp32 before the one rounding to the output dtype.
 #include <cstdlib>
 
 #include "gdn_common.cuh"
@@ -44,17 +52,21 @@ struct BulkLayout {
   static_assert(state_bytes % 16 == 0 && qk_bytes % 16 == 0 && v_bytes % 16 == 0, "bulk sizes");
 };
 
-template <typename Tin, int DK, int DV>
+__device__ __forceinline__ float softplus(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
+__device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+
+template <typename Tin, int DK, int DV, bool kLayer>
 __global__ void __launch_bounds__(kThreads, 1)
 recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
                       const Tin* __restrict__ v, const float* __restrict__ g,
                       const float* __restrict__ beta, const float* h0, Tin* __restrict__ o,
-                      float* hT, int n_units, int H, int Hk) {
+                      float* hT, int n_units, int H, int Hk, const LayerArgs la) {
   using L = BulkLayout<Tin, DK, DV>;
   constexpr int LPR = L::LPR;
   constexpr int RPP = kComputeThreads / LPR;
   constexpr int RPT = DK / RPP;
   static_assert(LPR <= 32 && 32 % LPR == 0 && DK % RPP == 0 && RPT >= 1, "tile");
+  static_assert(!kLayer || LPR == 32, "the layer epilogue needs a head's outputs in one warp");
 
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t full_bar[kStages], free_bar[kStages], red_bar[2];
@@ -132,17 +144,31 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
   float4* red = reinterpret_cast<float4*>(smem + (size_t)kStages * L::stage_bytes);
   const int cg = tid % LPR, rb = tid / LPR;
   const int unit0 = blockIdx.x;
+  // (layer form: g_next / b_next hold the raw a / b, gate_next the output gate)
   float g_next = 0.f, b_next = 0.f;
+  float4 gate_next = make_float4(0.f, 0.f, 0.f, 0.f), w4 = gate_next;
+  const Tin* gate = static_cast<const Tin*>(la.gate);
+  if (kLayer && rb == 0) w4 = *reinterpret_cast<const float4*>(la.weight + cg * 4);
   if (my_units > 0) {
-    g_next = g[unit0];
-    b_next = beta[unit0];
+    g_next = kLayer ? la.a[unit0] : g[unit0];
+    b_next = kLayer ? la.b[unit0] : beta[unit0];
+    if (kLayer && gate && rb == 0) gate_next = load4(gate + (size_t)unit0 * DV + cg * 4);
   }
   for (int j = 0; j < my_units; ++j) {
     const int s = j % kStages, u = unit0 + j * (int)gridDim.x;
-    const float alpha = __expf(g_next), bt = b_next;
+    float gg = g_next, bt = b_next;
+    const float4 gate4 = gate_next;
+    if (kLayer) {   // model.py:136-139
+      const int hh = u % H;
+      gg = -expf(la.A_log[hh]) * softplus(gg + la.dt_bias[hh]);
+      bt = sigmoid(bt);
+    }
+    const float alpha = __expf(gg);
     if (j + 1 < my_units) {  // prefetch the next head's gate and beta
-      g_next = g[u + (int)gridDim.x];
-      b_next = beta[u + (int)gridDim.x];
+      const int un = u + (int)gridDim.x;
+      g_next = kLayer ? la.a[un] : g[un];
+      b_next = kLayer ? la.b[un] : beta[un];
+      if (kLayer && gate && rb == 0) gate_next = load4(gate + (size_t)un * DV + cg * 4);
     }
     if (!mbar_wait(&full_bar[s], (uint32_t)(j / kStages) & 1u)) return;
     unsigned char* st = stage(s);
@@ -207,6 +233,19 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
       out.y = fmaf(alpha, qh.y, qk * uu.y);
       out.z = fmaf(alpha, qh.z, qk * uu.z);
       out.w = fmaf(alpha, qh.w, qk * uu.w);
+      if (kLayer) {   // model.py:47-53, over the head's DV outputs held by this warp
+        float ss = out.x * out.x + out.y * out.y + out.z * out.z + out.w * out.w;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float rs = rsqrtf(ss * (1.f / DV) + la.eps);
+        out.x *= rs * w4.x; out.y *= rs * w4.y; out.z *= rs * w4.z; out.w *= rs * w4.w;
+        if (gate) {
+          out.x *= gate4.x * sigmoid(gate4.x);
+          out.y *= gate4.y * sigmoid(gate4.y);
+          out.z *= gate4.z * sigmoid(gate4.z);
+          out.w *= gate4.w * sigmoid(gate4.w);
+        }
+      }
       store4(o + (size_t)u * DV + cg * 4, out);
     }
     if (hT) {
@@ -230,10 +269,10 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
 
 int num_sms() { return device_sm_count(); }
 
-template <typename Tin, int DK, int DV>
-cudaError_t launch_bulk_t(const RecurrentArgs& a, cudaStream_t st) {
+template <typename Tin, int DK, int DV, bool kLayer>
+cudaError_t launch_bulk_t(const RecurrentArgs& a, const LayerArgs& la, cudaStream_t st) {
   using L = BulkLayout<Tin, DK, DV>;
-  auto kern = recurrent_bulk_kernel<Tin, DK, DV>;
+  auto kern = recurrent_bulk_kernel<Tin, DK, DV, kLayer>;
   static std::atomic<int> smem_set[kMaxDevices] = {};
   cudaError_t e = ensure_smem(kern, L::total, smem_set);
   if (e != cudaSuccess) return e;
@@ -255,7 +294,7 @@ cudaError_t launch_bulk_t(const RecurrentArgs& a, cudaStream_t st) {
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kern, static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k),
                          static_cast<const Tin*>(a.v), a.g, a.beta, a.h0, static_cast<Tin*>(a.o),
-                         a.hT, n_units, a.H, a.Hk);
+                         a.hT, n_units, a.H, a.Hk, la);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -270,8 +309,16 @@ bool recurrent_bulk_supported(const RecurrentArgs& a) {
 
 cudaError_t launch_recurrent_bulk(const RecurrentArgs& a, cudaStream_t st) {
   if (a.B * a.H == 0) return cudaSuccess;
-  return a.dtype == kBF16 ? launch_bulk_t<__nv_bfloat16, 128, 128>(a, st)
-                          : launch_bulk_t<float, 128, 128>(a, st);
+  const LayerArgs none{};
+  return a.dtype == kBF16 ? launch_bulk_t<__nv_bfloat16, 128, 128, false>(a, none, st)
+                          : launch_bulk_t<float, 128, 128, false>(a, none, st);
+}
+
+cudaError_t launch_recurrent_bulk_layer(const RecurrentArgs& a, const LayerArgs& la,
+                                        cudaStream_t st) {
+  if (a.B * a.H == 0) return cudaSuccess;
+  return a.dtype == kBF16 ? launch_bulk_t<__nv_bfloat16, 128, 128, true>(a, la, st)
+                          : launch_bulk_t<float, 128, 128, true>(a, la, st);
 }
 
 }  // namespace gdn

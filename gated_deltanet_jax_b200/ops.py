@@ -300,6 +300,60 @@ def _recurrent_impl(q, k, v, g, beta, initial_state, output_final_state, final_s
     return o, hT
 
 
+def gated_delta_rule_decode_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
+                                  norm_weight=None, eps: float = 1e-5, initial_state=None,
+                                  output_final_state=False,
+                                  final_state_out: Optional[torch.Tensor] = None
+                                  ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """One decode token of the GatedDeltaNet layer's core in one kernel
+    (gdn_recurrent_fwd_layer): the gates from the raw projections, the
+    recurrent step, and the gated RMSNorm of its output.
+
+    The reference layer (model.py:136-153) runs these as separate operations:
+    ``beta = sigmoid(b)``, ``g = -exp(A_log) * softplus(a + dt_bias)``, the op,
+    then ``FusedRMSNormGated`` (model.py:41-53; with ``gate=None`` the plain
+    RMSNorm of the ungated layer, whose epsilon is 1e-6).
+
+    q, k ``[B,1,Hk,128]``; v ``[B,1,H,128]``; a, b ``[B,1,H]`` (a_proj, b_proj
+    outputs); A_log, dt_bias ``[H]``; gate ``[B,1,H,128]`` in v's dtype or None;
+    norm_weight ``[128]`` (None: ones).  Returns ``(y, final_state)`` like the
+    recurrent op (``final_state_out=S`` with ``initial_state=S`` updates S in
+    place).  Inference only: there is no backward for this form.
+    """
+    if _wants_grad(q, k, v, a, b, initial_state):
+        raise NotImplementedError("gated_delta_rule_decode_layer has no backward")
+    q, k, v, a, b, h0, hT, y, (B, T, H, Hk, dk, dv) = _prepare(
+        q, k, v, a, b, initial_state, final_state_out, output_final_state)
+    dev = q.device
+
+    def vec(t, n, name):
+        if t is None:
+            return None
+        t = torch.as_tensor(t, device=dev).to(torch.float32).contiguous()
+        if t.shape != (n,):
+            raise ValueError(f"{name} must be [{n}]; got {tuple(t.shape)}")
+        return t
+
+    A_log, dt_bias = vec(A_log, H, "A_log"), vec(dt_bias, H, "dt_bias")
+    w = vec(norm_weight, dv, "norm_weight")
+    if w is None:
+        w = torch.ones(dv, dtype=torch.float32, device=dev)
+    if gate is not None:
+        if tuple(gate.shape) != (B, T, H, dv):
+            raise ValueError(f"gate must be [B,T,H,dv]=({B},{T},{H},{dv}); got {tuple(gate.shape)}")
+        gate = gate.to(device=dev, dtype=v.dtype).contiguous()
+        if gate.data_ptr() % 16:
+            gate = gate.clone()
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.gdn_recurrent_fwd_layer(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), _ptr(A_log), _ptr(dt_bias), _ptr(h0),
+            _ptr(hT), _ptr(gate), _ptr(w), float(eps), _ptr(y), B, T, H, Hk, dk, dv,
+            _DTYPES[q.dtype], torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(rc, "gdn_recurrent_fwd_layer")
+    return y, hT
+
+
 # Aliases with the reference's public names (ops.py:350-352).
 fused_recurrent_gated_delta_rule_fwd = fused_recurrent_gated_delta_rule
 fused_recurrent_gated_delta_rule_pallas = fused_recurrent_gated_delta_rule
@@ -308,4 +362,5 @@ chunk_gated_delta_rule = chunk_gated_delta_rule_fwd
 __all__ = [
     "chunk_gated_delta_rule", "chunk_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule_pallas",
+    "gated_delta_rule_decode_layer",
 ]

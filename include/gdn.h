@@ -99,6 +99,28 @@ int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v,
                       void* workspace, size_t ws_bytes, void* stream);
 
 /*
+ * The decode step with the GatedDeltaNet layer's work on either side of it,
+ * in the same kernel (single token, dk = dv = 128):
+ *   before  beta = sigmoid(b), g = -exp(A_log[h]) * softplus(a + dt_bias[h])
+ *           from the raw a_proj / b_proj outputs a, b [B, 1, H] (model.py:136-139);
+ *   after   y = o * rsqrt(mean(o^2) + eps) * norm_weight, times silu(gate) when
+ *           gate [B, 1, H, dv] (input dtype) is given, over each head's dv
+ *           outputs (FusedRMSNormGated, model.py:41-53; gate NULL: the
+ *           ungated RMSNorm of model.py:150-151).
+ * The recurrent step itself is gdn_recurrent_fwd_gva's (state in / out,
+ * h0 == hT in place).  y [B, 1, H, dv] in the input dtype; A_log, dt_bias [H]
+ * and norm_weight [dv] fp32.  No counterpart in the reference, where these are
+ * separate jax.numpy operations around the op.
+ */
+int gdn_recurrent_fwd_layer(const void* q, const void* k, const void* v,
+                            const float* a, const float* b,
+                            const float* A_log, const float* dt_bias,
+                            const float* h0, float* hT,
+                            const void* gate, const float* norm_weight, float eps,
+                            void* y, int B, int T, int H, int Hk, int dk, int dv,
+                            int dtype, void* stream);
+
+/*
  * Packed variable-length sequences for the chunked forward: n_seqs sequences
  * stored back to back in one row of T tokens -- q, k [1, T, Hk, dk], v, o
  * [1, T, H, dv], g, beta [1, T, H] -- with sequence s the tokens
@@ -213,7 +235,8 @@ int gdn_device_error(int clear);
 const char* gdn_last_error(void);
 
 /* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward;
- * 1.4: backward of packed sequences, the allocation-free backward). */
+ * 1.4: backward of packed sequences, the allocation-free backward;
+ * 1.5: the layer form of the decode step). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

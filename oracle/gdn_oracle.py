@@ -489,10 +489,40 @@ def within_tolerance(out, ref, input_dtype: str) -> Tuple[bool, float]:
     return e <= TOL_BF16_REL, e
 
 
+# ---------------------------------------------------------------------------
+# The layer's work on either side of the op (model.py:136-139, :41-53)
+# ---------------------------------------------------------------------------
+
+
+def layer_gates(a, b, A_log, dt_bias, dtype=np.float64):
+    """beta and g from the raw a_proj / b_proj outputs, as model.py:136-139:
+    ``beta = sigmoid(b)``, ``g = -exp(A_log) * softplus(a + dt_bias)``, with
+    A_log and dt_bias per value head (the last axis of a and b)."""
+    a = np.asarray(a, dtype); b = np.asarray(b, dtype)
+    A_log = np.asarray(A_log, dtype); dt_bias = np.asarray(dt_bias, dtype)
+    beta = 1.0 / (1.0 + np.exp(-b))
+    x = a + dt_bias
+    softplus = np.maximum(x, 0.0) + np.log1p(np.exp(-np.abs(x)))
+    return -np.exp(A_log) * softplus, beta
+
+
+def rms_norm_gated(o, weight, gate=None, eps=1e-5, dtype=np.float64):
+    """FusedRMSNormGated (model.py:41-53) over the last axis:
+    ``o * rsqrt(mean(o^2) + eps) * weight``, times ``silu(gate)`` if given
+    (without a gate, the ungated layer's RMSNorm, model.py:150-151)."""
+    o = np.asarray(o, dtype)
+    var = np.mean(o * o, axis=-1, keepdims=True)
+    y = o / np.sqrt(var + eps) * np.asarray(weight, dtype)
+    if gate is not None:
+        gt = np.asarray(gate, dtype)
+        y = y * gt / (1.0 + np.exp(-gt))
+    return y
+
+
 __all__ = [
     "make_inputs", "round_bf16", "recurrent_ref", "chunk_exact",
     "chunk_reference_literal", "literal_output_permutation", "segment_transition",
     "two_pass_sp", "TOL_FP32_ABS", "TOL_BF16_REL", "max_abs_err", "rel_err",
-    "within_tolerance",
+    "within_tolerance", "layer_gates", "rms_norm_gated",
 ]
 

@@ -162,6 +162,23 @@ def test_backward_workspace_queries(lib):
         assert lib.gdn_chunk_bwd_varlen_workspace_bytes(*args) == 0
 
 
+def test_decode_layer_rejects_bad_arguments(lib):
+    """Checked on the host before any CUDA call."""
+    p = ctypes.c_void_p(16)
+
+    def call(T=1, dk=128, dv=128, A=p, gate=None, w=p, eps=1e-5):
+        return lib.gdn_recurrent_fwd_layer(p, p, p, p, p, A, p, None, None, gate, w, eps, p,
+                                           2, T, 2, 2, dk, dv, _lib.GDN_DTYPE_BF16, None)
+    assert call(T=2) == _lib.GDN_ERR_UNSUPPORTED
+    assert b"single-token" in lib.gdn_last_error()
+    assert call(dk=64, dv=64) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(A=None) == _lib.GDN_ERR_INVALID
+    assert call(w=None) == _lib.GDN_ERR_INVALID
+    assert call(w=ctypes.c_void_p(20)) == _lib.GDN_ERR_INVALID
+    assert call(gate=ctypes.c_void_p(24)) == _lib.GDN_ERR_INVALID
+    assert call(eps=-1.0) == _lib.GDN_ERR_INVALID
+
+
 def test_empty_problem_is_a_no_op(lib):
     # B*H == 0: nothing to launch, no CUDA call, OK.
     assert _call_recurrent(lib, B=0) == _lib.GDN_OK

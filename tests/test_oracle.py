@@ -176,3 +176,17 @@ def test_backward_matches_autograd_of_recurrence(shape):
     for a, t in zip(got, ts):
         ref = t.grad.numpy()
         assert np.abs(a - ref).max() <= 1e-12 * max(1.0, np.abs(ref).max())
+
+
+def test_layer_gates_and_norm_formulas():
+    """model.py:136-139 and :41-53 on hand-checked values."""
+    A_log = np.log(np.array([1.0, 2.0]))
+    g, beta = orc.layer_gates(np.array([[0.0, 30.0]]), np.array([[0.0, 2.0]]), A_log,
+                              np.zeros(2))
+    np.testing.assert_allclose(g, [[-np.log(2.0), -2.0 * (30.0 + np.log1p(np.exp(-30.0)))]])
+    np.testing.assert_allclose(beta, [[0.5, 1.0 / (1.0 + np.exp(-2.0))]])
+    o = np.array([[3.0, -4.0]])
+    y = orc.rms_norm_gated(o, np.array([1.0, 2.0]), eps=0.0)
+    np.testing.assert_allclose(y, [[3.0 / np.sqrt(12.5), -8.0 / np.sqrt(12.5)]])
+    yg = orc.rms_norm_gated(o, np.ones(2), gate=np.array([[0.0, 1.0]]), eps=0.0)
+    np.testing.assert_allclose(yg, [[0.0, -4.0 / np.sqrt(12.5) / (1.0 + np.exp(-1.0))]])
