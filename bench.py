@@ -519,8 +519,17 @@ def decode_layer_leg(d, a):
             (x * torch.rsqrt(var + 1e-5) * w
              * torch.nn.functional.silu(gate[t].float())).to(o.dtype)
 
+    gd_all = -torch.exp(A_log) * torch.nn.functional.softplus(ra + dt_bias)
+    bd_all = torch.sigmoid(rb)
+
+    def op_only():   # the step alone, gates given (what the plain decode leg runs)
+        for t in range(TOK):
+            st = S[t % NBUF]
+            ops.fused_recurrent_gated_delta_rule(q[t], k[t], v[t], gd_all[t], bd_all[t],
+                                                 initial_state=st, final_state_out=st)
+
     res = {}
-    for name, fn in (("fused", fused), ("unfused", unfused)):
+    for name, fn in (("fused", fused), ("unfused", unfused), ("op_only", op_only)):
         fn()                                   # load modules, allocate
         torch.cuda.synchronize(d.dev)
         graph = torch.cuda.CUDAGraph()
@@ -536,11 +545,13 @@ def decode_layer_leg(d, a):
                         "from raw a/b projections, gated RMSNorm (eps 1e-5) of the output; "
                         f"states round robin over {NBUF} x 64 MiB; 64 tokens per CUDA graph",
             "fused_us_per_token": res["fused"], "unfused_us_per_token": res["unfused"],
+            "op_only_us_per_token": res["op_only"],
             "speedup": res["unfused"] / res["fused"],
-            "launches": 2 * TOK * max(1, min(a.steps, 50)),
+            "launches": 3 * TOK * max(1, min(a.steps, 50)),
             "fused_tokens_per_s": d.world * B / (res["fused"] / 1e6),
             "path": "fused: gdn_recurrent_fwd_layer (1 launch per token); unfused: torch gates, "
-                    "gdn_recurrent_fwd, torch gated RMSNorm"}
+                    "gdn_recurrent_fwd, torch gated RMSNorm; op_only: gdn_recurrent_fwd with "
+                    "precomputed gates and no norm"}
 
 
 def backward_leg(d, a, lib):

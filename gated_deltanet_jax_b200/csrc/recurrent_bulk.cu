@@ -53,6 +53,23 @@ struct BulkLayout {
 };
 
 __device__ __forceinline__ float softplus(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
+
+// Four consecutive input elements kept as loaded (no conversion yet), so that
+// a load issued ahead of its use does not wait for its data where it is issued.
+template <typename Tin> struct Raw4;
+template <> struct Raw4<float> {
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+  __device__ void load(const float* p) { r = *reinterpret_cast<const float4*>(p); }
+  __device__ float4 get() const { return r; }
+};
+template <> struct Raw4<__nv_bfloat16> {
+  uint2 r = make_uint2(0u, 0u);
+  __device__ void load(const __nv_bfloat16* p) { r = *reinterpret_cast<const uint2*>(p); }
+  __device__ float4 get() const {
+    return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xffff0000u),
+                       __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xffff0000u));
+  }
+};
 __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
 
 template <typename Tin, int DK, int DV, bool kLayer>
@@ -146,29 +163,49 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
   const int unit0 = blockIdx.x;
   // (layer form: g_next / b_next hold the raw a / b, gate_next the output gate)
   float g_next = 0.f, b_next = 0.f;
-  float4 gate_next = make_float4(0.f, 0.f, 0.f, 0.f), w4 = gate_next;
+  Raw4<Tin> gate_next;
+  float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
   const Tin* gate = static_cast<const Tin*>(la.gate);
   if (kLayer && rb == 0) w4 = *reinterpret_cast<const float4*>(la.weight + cg * 4);
+  // layer form: model.py:136-139 from the raw a, b and the head's A_log, dt_bias
+  auto layer_gates = [&](float a_raw, float b_raw, float A, float dtb, float& gg, float& bb) {
+    gg = -expf(A) * softplus(a_raw + dtb);
+    bb = sigmoid(b_raw);
+  };
+  float g_cur = 0.f, b_cur = 0.f;   // layer form: the current unit's g and beta
+  float A_next = 0.f, dtb_next = 0.f;
   if (my_units > 0) {
     g_next = kLayer ? la.a[unit0] : g[unit0];
     b_next = kLayer ? la.b[unit0] : beta[unit0];
-    if (kLayer && gate && rb == 0) gate_next = load4(gate + (size_t)unit0 * DV + cg * 4);
+    if (kLayer) {
+      A_next = la.A_log[unit0 % H];
+      dtb_next = la.dt_bias[unit0 % H];
+      if (gate && rb == 0) gate_next.load(gate + (size_t)unit0 * DV + cg * 4);
+      layer_gates(g_next, b_next, A_next, dtb_next, g_cur, b_cur);
+    }
   }
   for (int j = 0; j < my_units; ++j) {
     const int s = j % kStages, u = unit0 + j * (int)gridDim.x;
-    float gg = g_next, bt = b_next;
-    const float4 gate4 = gate_next;
-    if (kLayer) {   // model.py:136-139
-      const int hh = u % H;
-      gg = -expf(la.A_log[hh]) * softplus(gg + la.dt_bias[hh]);
-      bt = sigmoid(bt);
+    // layer form, warp 0: norm weight x silu(gate) of this unit, computed before
+    // the unit's state arrives (the gate was fetched with the previous unit)
+    float4 gw = w4;
+    if (kLayer && gate && rb == 0) {
+      const float4 gv = gate_next.get();
+      gw.x *= gv.x * sigmoid(gv.x); gw.y *= gv.y * sigmoid(gv.y);
+      gw.z *= gv.z * sigmoid(gv.z); gw.w *= gv.w * sigmoid(gv.w);
     }
-    const float alpha = __expf(gg);
+    // (layer form: the gates were computed at the end of the previous unit, off
+    // this unit's critical path)
+    const float alpha = __expf(kLayer ? g_cur : g_next), bt = kLayer ? b_cur : b_next;
     if (j + 1 < my_units) {  // prefetch the next head's gate and beta
       const int un = u + (int)gridDim.x;
       g_next = kLayer ? la.a[un] : g[un];
       b_next = kLayer ? la.b[un] : beta[un];
-      if (kLayer && gate && rb == 0) gate_next = load4(gate + (size_t)un * DV + cg * 4);
+      if (kLayer) {
+        A_next = la.A_log[un % H];
+        dtb_next = la.dt_bias[un % H];
+        if (gate && rb == 0) gate_next.load(gate + (size_t)un * DV + cg * 4);
+      }
     }
     if (!mbar_wait(&full_bar[s], (uint32_t)(j / kStages) & 1u)) return;
     unsigned char* st = stage(s);
@@ -238,13 +275,7 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         const float rs = rsqrtf(ss * (1.f / DV) + la.eps);
-        out.x *= rs * w4.x; out.y *= rs * w4.y; out.z *= rs * w4.z; out.w *= rs * w4.w;
-        if (gate) {
-          out.x *= gate4.x * sigmoid(gate4.x);
-          out.y *= gate4.y * sigmoid(gate4.y);
-          out.z *= gate4.z * sigmoid(gate4.z);
-          out.w *= gate4.w * sigmoid(gate4.w);
-        }
+        out.x *= rs * gw.x; out.y *= rs * gw.y; out.z *= rs * gw.z; out.w *= rs * gw.w;
       }
       store4(o + (size_t)u * DV + cg * 4, out);
     }
@@ -264,6 +295,7 @@ recurrent_bulk_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&free_bar[s]);
+    if (kLayer && j + 1 < my_units) layer_gates(g_next, b_next, A_next, dtb_next, g_cur, b_cur);
   }
 }
 
