@@ -11,6 +11,7 @@ from .ops import (
     chunk_gated_delta_rule_fwd,
     fused_recurrent_gated_delta_rule,
     fused_recurrent_gated_delta_rule_fwd,
+    gated_delta_rule_decode_layer,
 )
 
 __all__ = [
@@ -20,4 +21,5 @@ __all__ = [
     "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fwd",
     "delta_rule",
+    "gated_delta_rule_decode_layer",
 ]
