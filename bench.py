@@ -50,7 +50,7 @@ def _args():
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill leg")
     p.add_argument("--no-long", action="store_true", help="skip the long-context leg")
     p.add_argument("--no-backward", action="store_true", help="skip the backward leg")
-    p.add_argument("--no-layer", action="store_true", help="skip the decode layer-core leg")
+    p.add_argument("--no-layer", action="store_true", help="skip the layer-core legs")
     return p.parse_args()
 
 
@@ -477,6 +477,17 @@ def prefill_leg(d, a, lib, uuid=None):
     return res
 
 
+def _layer_gate_params(H, dev, gen):
+    """A_log and dt_bias drawn as the layer initialises them (model.py:103-113):
+    A ~ U(1e-4, 16); dt log-uniform in [1e-3, 0.1], dt_bias = softplus^-1(dt)."""
+    import math
+    import torch
+    A_log = torch.log(torch.rand(H, device=dev, generator=gen) * (16 - 1e-4) + 1e-4)
+    u = torch.rand(H, device=dev, generator=gen)
+    dt = torch.exp(u * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp_min(1e-4)
+    return A_log, dt + torch.log(-torch.expm1(-dt))
+
+
 def decode_layer_leg(d, a):
     """One decode token of the layer core (gates from the raw projections, the
     step, the gated RMSNorm) on the decode workload, two ways, each replayed
@@ -495,8 +506,7 @@ def decode_layer_leg(d, a):
     ra = torch.randn(TOK, B, 1, H, device=d.dev, generator=gen)
     rb = torch.randn(TOK, B, 1, H, device=d.dev, generator=gen)
     gate = torch.randn(TOK, B, 1, H, dv, device=d.dev, generator=gen).bfloat16()
-    A_log = torch.log(torch.rand(H, device=d.dev, generator=gen) * 16 + 1e-4)
-    dt_bias = torch.randn(H, device=d.dev, generator=gen) * 0.5
+    A_log, dt_bias = _layer_gate_params(H, d.dev, gen)
     w = torch.ones(dv, device=d.dev)
     S = torch.randn(NBUF, B, H, dk, dv, device=d.dev, generator=gen) * 0.02
 
@@ -551,6 +561,74 @@ def decode_layer_leg(d, a):
             "fused_tokens_per_s": d.world * B / (res["fused"] / 1e6),
             "path": "fused: gdn_recurrent_fwd_layer (1 launch per token); unfused: torch gates, "
                     "gdn_recurrent_fwd, torch gated RMSNorm; op_only: gdn_recurrent_fwd with "
+                    "precomputed gates and no norm"}
+
+
+def prefill_layer_leg(d, a):
+    """The layer core over the prefill workload (gates from the raw
+    projections, the chunked forward, the gated RMSNorm of every output row),
+    two ways: the fused kernel (gdn_chunk_fwd_layer) against the op between
+    the same operations done separately in torch, as the reference layer does
+    them (model.py:136-153); and the op alone with the gates given."""
+    import torch
+    from gated_deltanet_jax_b200 import ops
+    B, T, H, dk, dv = PRE["B"], PRE["T"], PRE["H"], PRE["dk"], PRE["dv"]
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(8765 + d.rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    k = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
+    ra = torch.randn(B, T, H, device=d.dev, generator=gen)
+    rb = torch.randn(B, T, H, device=d.dev, generator=gen)
+    gate = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
+    A_log, dt_bias = _layer_gate_params(H, d.dev, gen)
+    w = torch.ones(dv, device=d.dev)
+    hT = torch.empty(B, H, dk, dv, device=d.dev)
+
+    def fused():
+        ops.gated_delta_rule_chunk_layer(q, k, v, ra, rb, A_log, dt_bias, gate=gate,
+                                         norm_weight=w, final_state_out=hT)
+
+    def unfused():
+        gd = -torch.exp(A_log) * torch.nn.functional.softplus(ra + dt_bias)
+        bd = torch.sigmoid(rb)
+        o, _ = ops.chunk_gated_delta_rule(q, k, v, gd, bd, final_state_out=hT)
+        x = o.float()
+        var = x.pow(2).mean(-1, keepdim=True)
+        (x * torch.rsqrt(var + 1e-5) * w * torch.nn.functional.silu(gate.float())).to(o.dtype)
+
+    gd_all = -torch.exp(A_log) * torch.nn.functional.softplus(ra + dt_bias)
+    bd_all = torch.sigmoid(rb)
+
+    def op_only():
+        ops.chunk_gated_delta_rule(q, k, v, gd_all, bd_all, final_state_out=hT)
+
+    # Each variant is replayed from a CUDA graph of REP calls, so that the
+    # host's per-call Python work (longer than the kernel) is not what is timed.
+    REP = 8
+    res = {}
+    steps = max(1, min(a.steps, 50))
+    for name, fn in (("fused", fused), ("unfused", unfused), ("op_only", op_only)):
+        fn()                                   # load modules, allocate
+        torch.cuda.synchronize(d.dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(REP):
+                fn()
+        for _ in range(a.warmup):
+            graph.replay()
+        ms, _ = _timed(d, graph.replay, steps)
+        res[name] = ms / REP
+        del graph
+    return {"workload": "the layer core over B=4 T=4096 H=16 dk=dv=128 bf16: gates from raw "
+                        "a/b projections, chunked forward, gated RMSNorm (eps 1e-5) of every "
+                        "output row; final state out; 8 calls per CUDA graph",
+            "fused_ms": res["fused"], "unfused_ms": res["unfused"], "op_only_ms": res["op_only"],
+            "speedup": res["unfused"] / res["fused"], "launches": 3 * REP * steps,
+            "fused_tokens_per_s": d.world * B * T / (res["fused"] / 1e3),
+            "path": "fused: gdn_chunk_fwd_layer (1 launch, CTA pairs); unfused: torch gates, "
+                    "gdn_chunk_fwd, torch gated RMSNorm; op_only: gdn_chunk_fwd with "
                     "precomputed gates and no norm"}
 
 
@@ -678,6 +756,7 @@ def main():
     lng = None if a.no_long else long_context_leg(d, a)
     bwd = None if a.no_backward else backward_leg(d, a, lib)
     lay = None if a.no_layer else decode_layer_leg(d, a)
+    play = None if (a.no_layer or a.no_prefill) else prefill_layer_leg(d, a)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not a.no_cpu:
@@ -706,7 +785,8 @@ def main():
                          "traffic": traffic,
                          "algorithmic_bytes_per_launch": dec["bytes_launch"]},
             "gpu_launches": (dec["launches"] + (pre["launches"] if pre else 0)
-                             + (bwd["launches"] if bwd else 0) + (lay["launches"] if lay else 0)),
+                             + (bwd["launches"] if bwd else 0) + (lay["launches"] if lay else 0)
+                             + (play["launches"] if play else 0)),
             "clocks": dec["clocks"],
         }
         if "e2e" in dec:
@@ -738,6 +818,8 @@ def main():
             line["long_context"] = lng
         if lay:
             line["decode_layer"] = lay
+        if play:
+            line["prefill_layer"] = play
         if bwd:
             if pre:
                 bwd["fwd_plus_bwd_tokens_per_s"] = (d.world * PRE["B"] * PRE["T"]

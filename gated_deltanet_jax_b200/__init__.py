@@ -11,6 +11,7 @@ from .ops import (
     chunk_gated_delta_rule_fwd,
     fused_recurrent_gated_delta_rule,
     fused_recurrent_gated_delta_rule_fwd,
+    gated_delta_rule_chunk_layer,
     gated_delta_rule_decode_layer,
 )
 
@@ -21,5 +22,6 @@ __all__ = [
     "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fwd",
     "delta_rule",
+    "gated_delta_rule_chunk_layer",
     "gated_delta_rule_decode_layer",
 ]

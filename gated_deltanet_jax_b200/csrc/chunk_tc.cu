@@ -32,6 +32,15 @@
 // reads only its own quarter of the 128 TMEM lanes, so row r of every M=128
 // accumulator belongs to thread r of a warpgroup.  All hand-offs are
 // mbarriers; every wait is bounded.
+//
+// Layer form (kLayer, dv = 128 as one CTA pair): the GatedDeltaNet layer's
+// work on either side of the op in the same kernel (model.py:136-139, :47-53).
+// The gate warp forms beta = sigmoid(b) and g = -exp(A_log[h]) softplus(a +
+// dt_bias[h]) from the raw projections; the output epilogue sums the squares
+// of its 64 columns of each row in fp32, exchanges the partial sum with the
+// other CTA of the pair (one st.async per row into the other CTA's shared
+// memory, completing on its barrier), and stores
+// y = o rsqrt(mean(o^2) + eps) w silu(gate) instead of o.
 #include <cuda.h>
 #include <cstdlib>
 #include <cudaTypedefs.h>
@@ -78,9 +87,17 @@ struct VecBuf {
   float pad[2];
 };
 constexpr int SM_BAR = SM_VEC + NTP * (int)sizeof(VecBuf);
-constexpr int NBAR = 32;
+constexpr int NBAR = 40;
+// Layer form: ring of the other tile's row sums of squares.  A row is finished
+// one chunk after its products (its sum is read at the start of the next
+// chunk), and a CTA's chain runs at most NTP chunks ahead of the other's, so
+// NTP + 1 slots keep a slot from being rewritten before it was read.
+constexpr int NSS = NTP + 1;
 constexpr int SM_TMEM = SM_BAR + NBAR * 8;
-constexpr int SM_TOTAL = SM_TMEM + 16;
+constexpr int SM_SS = SM_TMEM + 16;             // layer form: NSS x [64] row partial sums, other tile
+constexpr int SM_W = SM_SS + NSS * 64 * 4;      // layer form: norm weight of this column tile
+constexpr int SM_OB = SM_W + DVT * 4;           // layer form: [64 rows][128 B] bf16 output rows
+constexpr int SM_TOTAL = SM_OB + 8192;
 constexpr int SMEM_BYTES = SM_TOTAL + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 
@@ -96,7 +113,9 @@ enum {
   B_VEC_EMPTY = 17,  // [NTP] this CTA's chain is done with a chunk's gate vectors
   B_D1 = 20, B_D2 = 21, B_D3 = 22, B_D4 = 23, B_D4_EMPTY = 24,
   B_X_READY = 25, B_VPP_READY = 26, B_S_READY = 27, B_CHAIN_DONE = 28,
+  B_SS = 29,         // [NSS] layer form: the other tile's row sums of squares of a chunk arrived
 };
+static_assert(B_SS + NSS <= NBAR, "barriers");
 
 // TMEM columns
 constexpr uint32_t TM_PRE = 0;    // 2 x 64
@@ -133,6 +152,17 @@ __device__ __forceinline__ void unpack_bf16x8(uint4 u, float* f) {
     f[2 * i] = p.x;
     f[2 * i + 1] = p.y;
   }
+}
+
+// silu(z) = z sigmoid(z) = z (1 + tanh(z / 2)) / 2, on the PTX instruction
+// tanh.approx.f32 (documented maximum relative error about 2^-11, one
+// special-function op where e^-z and a reciprocal take two): its error stays
+// far below the bf16 rounding of the layer output it scales.
+__device__ __forceinline__ float silu_fast(float z) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * z));
+  const float hz = 0.5f * z;
+  return fmaf(hz, t, hz);
 }
 
 __device__ __forceinline__ uint32_t to_tf32(float x) {
@@ -282,13 +312,17 @@ __device__ __forceinline__ bool wait_shared_bar(uint64_t* bars, int idx, uint32_
 // r: chunks n with n % 2 == r) and copies it into the other CTA's ring, so
 // the state-independent preparation is done once per (b, h) rather than once
 // per column tile.
-template <bool kPair>
+// kLayer (pairs, dv = 128 only): g and beta hold the raw a_proj / b_proj
+// outputs, and o receives the gated RMSNorm of the output (la).
+template <bool kPair, bool kLayer>
 __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
                 const float* __restrict__ beta, const float* __restrict__ h0,
                 __nv_bfloat16* __restrict__ o, float* __restrict__ hT,
-                const int* __restrict__ cu_seqlens, int T, int H, int Hk, int dv) {
+                const int* __restrict__ cu_seqlens, int T, int H, int Hk, int dv,
+                const LayerArgs la) {
+  static_assert(!kLayer || kPair, "the layer form runs the two column tiles of a row as a pair");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // Round up to 1024 bytes by offsetting the shared array itself, so that the
   // compiler keeps every access below in the shared address space.
@@ -353,6 +387,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     mbar_init(&bars[B_VPP_READY], 2);
     mbar_init(&bars[B_S_READY], 4);
     mbar_init(&bars[B_CHAIN_DONE], 1);
+    for (int i = 0; i < NSS; ++i) mbar_init(&bars[B_SS + i], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -487,15 +522,20 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       // non-negligible product behind an underflowed partner) the chunk is flagged
       // to form e^{G_i - G_j} directly.
       const size_t gb = ((size_t)b * T + tok0) * H + h;
+      // layer form: g = -exp(A_log[h]) softplus(a + dt_bias[h]), beta = sigmoid(b)
+      const float negA = kLayer ? -expf(ldg_f32(la.A_log + h)) : 0.f;
+      const float dtb = kLayer ? ldg_f32(la.dt_bias + h) : 0.f;
+      auto gate_of = [&](float x) { return kLayer ? negA * softplus(x + dtb) : x; };
+      auto beta_of = [&](float x) { return kLayer ? sigmoid(x) : x; };
       bool ok = true;
       for (int n = 0; n < N && ok; ++n) {
         const int rb = n % NTP;
         VecBuf& vb = vecs[rb];
         const int t = n * C + 2 * lane;
-        const float g0 = t < Tn ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
-        const float g1 = t + 1 < Tn ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
-        const float b0 = t < Tn ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
-        const float b1 = t + 1 < Tn ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
+        const float g0 = t < Tn ? gate_of(ldg_f32(g + gb + (size_t)t * H)) : 0.f;
+        const float g1 = t + 1 < Tn ? gate_of(ldg_f32(g + gb + (size_t)(t + 1) * H)) : 0.f;
+        const float b0 = t < Tn ? beta_of(ldg_f32(beta + gb + (size_t)t * H)) : 0.f;
+        const float b1 = t + 1 < Tn ? beta_of(ldg_f32(beta + gb + (size_t)(t + 1) * H)) : 0.f;
         if (n >= NTP) ok = wait_bar(bars, B_VEC_EMPTY + rb, (uint32_t)((n / NTP) - 1) & 1u);
         if (!ok) break;
         const float pair = g0 + g1;
@@ -572,22 +612,24 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       if (!ok) break;
       const bool direct = vb.direct != 0;
       // A (rows 0-63) and P (rows 64-127) from D_pre; this warp: 32 columns, in
-      // steps of kW columns.  Direct exponents (steep gates only) use factor 1
-      // here and are applied by a rolled pass below.
+      // steps of kW columns.  Steep gates (direct) form each e^{G_i - G_j}
+      // from its own exponent instead of the separable factors.
       const int i = p & 63;
       const int jmax = p < 64 ? i - 1 : i;  // A is strictly lower, P includes the diagonal
       const float rs = p < 64 ? vb.beta[i] : 1.f;
+      const float Gi = vb.G[i];
       // (paired form: the factors of the whole 32-column half are formed while
       // the product may still be in flight)
       float fac[kPair ? 32 : 1];
       if constexpr (kPair) {
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          const float fq = direct ? 1.f : rs * vb.F[i][2 * ch + h2];
+          const float fq = rs * vb.F[i][2 * ch + h2];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int j = (2 * ch + h2) * 16 + e;
-            fac[16 * h2 + e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) : 0.f;
+            fac[16 * h2 + e] =
+                (j <= jmax) ? (direct ? rs * gate_exp(Gi - vb.G[j]) : fq * vb.E[j]) : 0.f;
           }
         }
       }
@@ -609,12 +651,18 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
             if constexpr (kPair) {
 #pragma unroll
               for (int e = 0; e < 16; ++e) out[e] = fac[16 * h2 + e] * v[e];
-            } else {
-              const float fq = direct ? 1.f : rs * vb.F[i][q4];
+            } else if (direct) {
 #pragma unroll
               for (int e = 0; e < 16; ++e) {
                 const int j = q4 * 16 + e;
-                out[e] = (j <= jmax) ? (direct ? 1.f : fq * vb.E[j]) * v[e] : 0.f;
+                out[e] = (j <= jmax) ? rs * gate_exp(Gi - vb.G[j]) * v[e] : 0.f;
+              }
+            } else {
+              const float fq = rs * vb.F[i][q4];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int j = q4 * 16 + e;
+                out[e] = (j <= jmax) ? fq * vb.E[j] * v[e] : 0.f;
               }
             }
             if (p < 64) {
@@ -627,22 +675,6 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
               *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4)) = pack_bf16x8(out);
               *reinterpret_cast<uint4*>(tpt + sw128(p, 2 * q4 + 1)) = pack_bf16x8(out + 8);
             }
-          }
-        }
-      }
-      if (direct) {
-        // steep gates: scale the stored row by rs * e^{G_i - G_j} element by element
-        const float Gi = vb.G[i];
-        const int jend = min(i, ch * 32 + 31);
-#pragma unroll 1
-        for (int j = ch * 32; j <= jend; ++j) {
-          const float f = rs * gate_exp(Gi - vb.G[j]);
-          if (p < 64) {
-            AF[i * LDF + j] = rtf32(AF[i * LDF + j] * f);
-          } else {
-            __nv_bfloat16* e =
-                reinterpret_cast<__nv_bfloat16*>(tpt + sw128(p, j >> 3) + (j & 7) * 2);
-            *e = __float2bfloat16_rn(__bfloat162float(*e) * f);
           }
         }
       }
@@ -755,12 +787,73 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_S_READY]);
     }
+    // layer form: the norm weight of this column tile, for the output warps
+    const bool gated = kLayer && la.gate != nullptr;
+    if constexpr (kLayer) {
+      if (wq >= 2) {
+        reinterpret_cast<float*>(sm + SM_W)[r - 64] = ldg_f32(la.weight + c0 + r - 64);
+        named_sync(2, 64);
+      }
+    }
+    // Layer form, output warps: the row of chunk m is finished at the start of
+    // chunk m + 1 (or after the last chunk), where these warps would otherwise
+    // wait for D3: by then the other CTA's partial sum has long arrived.  Its
+    // 64 gate values are fetched at the start of chunk m, a whole chain step
+    // before they are used; the bf16 row waits in SM_OB (128-byte swizzled
+    // rows, each thread its own row).
+    uint4 zr[8];
+    float ss_own = 0.f;
+    auto fetch_gate = [&](int m) {
+      const int t = m * C + r - 64;
+      const bool have = gated && t < Tn;
+      const uint4* zp =
+          have ? reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(la.gate) +
+                                                (((size_t)b * T + tok0 + t) * H + h) * dv + c0)
+               : nullptr;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) zr[j] = have ? ldg_u4(zp + j) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    auto finish_row = [&](int m) -> bool {
+      const int i = r - 64, t = m * C + i, sb = m % NSS;
+      if (!mbar_wait_cluster(&bars[B_SS + sb], (uint32_t)(m / NSS) & 1u)) return false;
+      const float* ssb = reinterpret_cast<const float*>(sm + SM_SS) + sb * 64;
+      const float rs = rsqrtf((ss_own + ssb[i]) * (1.f / (2 * DVT)) + la.eps);
+      const float* wsm = reinterpret_cast<const float*>(sm + SM_W);
+      __nv_bfloat16* orow = o + (((size_t)b * T + tok0 + t) * H + h) * dv + c0;
+      // (rolled: this runs in slack time, and instruction fetch is what a CTA
+      // pair's SMs compete for)
+#pragma unroll 1
+      for (int q8 = 0; q8 < 8; ++q8) {
+        float x[8], zz[8];
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + SM_OB + sw128(i, q8)), x);
+        uint4 zq = zr[0];  // zr[q8] by selects, so that zr stays in registers
+#pragma unroll
+        for (int j = 1; j < 8; ++j) zq = q8 == j ? zr[j] : zq;
+        unpack_bf16x8(zq, zz);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float gf = gated ? silu_fast(zz[e]) : 1.f;
+          x[e] *= rs * wsm[q8 * 8 + e] * gf;
+        }
+        if (t < Tn) *reinterpret_cast<uint4*>(orow + q8 * 8) = pack_bf16x8(x);
+      }
+      return true;
+    };
     bool ok = true;
     for (int n = 0; n < N && ok; ++n) {
       const int s = n % NSTAGE, tb = n & 1, rb = n % NTP;
       const VecBuf& vb = vecs[rb];
       const int t0 = n * C;
       const uint32_t d1 = tmem + TM_D1 + (uint32_t)tb * 64 + lane_off;
+      if constexpr (kLayer) {
+        if (wq >= 2) {
+          if (n > 0 && !finish_row(n - 1)) {
+            ok = false;
+            break;
+          }
+          fetch_gate(n);
+        }
+      }
       if (wq < 2) {
         // ---- epilogue 1: X = beta (V - e^G K S) ----
         const int i = r;
@@ -851,21 +944,53 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         const float egi = vb.eG[i];
         const int t = t0 + i;
         __nv_bfloat16* orow = o + (((size_t)b * T + tok0 + t) * H + h) * dv + c0;
-#pragma unroll (kPair ? 4 : 1)
-        for (int q4 = 0; q4 < 4; ++q4) {
-          float qs[16], pv[16], out[16];
-          tmem_ld16(d1 + q4 * 16, qs);
-          tmem_ld16(tmem + TM_D4 + lane_off + q4 * 16, pv);
+        if constexpr (kLayer) {
+          // ---- layer form, first half: y = O rsqrt(mean(O^2) + eps) w silu(gate)
+          //      over the row's 128 columns, 64 here and 64 in the other CTA of the
+          //      pair.  One pass over TMEM sums the squares of the fp32 row and
+          //      stages it as bf16 (as the op's own output would be); the partial
+          //      sum goes to the other CTA, and TMEM is released at once. ----
+          float ss = 0.f;
+#pragma unroll 1
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float qs[16], pv[16];
+            tmem_ld16x2(d1 + q4 * 16, tmem + TM_D4 + lane_off + q4 * 16, qs, pv);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) out[e] = fmaf(egi, qs[e], pv[e]);
-          if (t < Tn) {
-            *reinterpret_cast<uint4*>(orow + q4 * 16) = pack_bf16x8(out);
-            *reinterpret_cast<uint4*>(orow + q4 * 16 + 8) = pack_bf16x8(out + 8);
+            for (int e = 0; e < 16; ++e) {
+              qs[e] = fmaf(egi, qs[e], pv[e]);
+              ss = fmaf(qs[e], qs[e], ss);
+            }
+            *reinterpret_cast<uint4*>(sm + SM_OB + sw128(i, 2 * q4)) = pack_bf16x8(qs);
+            *reinterpret_cast<uint4*>(sm + SM_OB + sw128(i, 2 * q4 + 1)) = pack_bf16x8(qs + 8);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[B_D4_EMPTY]);
+          const int sb = n % NSS;
+          st_async_cluster_f32(
+              mapa_shared(smem_u32(reinterpret_cast<float*>(sm + SM_SS) + sb * 64 + i), peer), ss,
+              mapa_shared(smem_u32(&bars[B_SS + sb]), peer));
+          if (i == 0) mbar_arrive_expect_tx(&bars[B_SS + sb], 64 * 4);
+          ss_own = ss;
+        } else {
+#pragma unroll (kPair ? 4 : 1)
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float qs[16], pv[16], out[16];
+            tmem_ld16(d1 + q4 * 16, qs);
+            tmem_ld16(tmem + TM_D4 + lane_off + q4 * 16, pv);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) out[e] = fmaf(egi, qs[e], pv[e]);
+            if (t < Tn) {
+              *reinterpret_cast<uint4*>(orow + q4 * 16) = pack_bf16x8(out);
+              *reinterpret_cast<uint4*>(orow + q4 * 16 + 8) = pack_bf16x8(out + 8);
+            }
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[B_D4_EMPTY]);
+        if constexpr (!kLayer) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[B_D4_EMPTY]);
+        }
       }
       __syncwarp();
       if (lane == 0) {
@@ -875,6 +1000,9 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         if (kPair)
           mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&bars[B_TP_EMPTY + rb]), peer));
       }
+    }
+    if constexpr (kLayer) {
+      if (ok && wq >= 2 && N > 0) ok = finish_row(N - 1);
     }
     if (ok && hT) {
       float* dst = hT + ((size_t)bh * DK + r) * dv + c0;
@@ -937,31 +1065,20 @@ bool chunk_tc_supported(const ChunkArgs& a) {
          a.T > 0 && encode_fn() != nullptr;
 }
 
-cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
-  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+namespace {
+
+template <bool kPair, bool kLayer>
+cudaError_t launch_tc_form(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
   CUtensorMap mk, mq, mv;
   const int rows = a.cu_seqlens ? 1 : a.B;  // packed sequences share one row of T tokens
   if (!make_map(&mk, a.k, rows, a.T, a.Hk, a.dk) || !make_map(&mq, a.q, rows, a.T, a.Hk, a.dk) ||
       !make_map(&mv, a.v, rows, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
-  // Pairs of column tiles share the preparation (clusters of two CTAs) when
-  // the tile count is even and the grid leaves every CTA pair a TPC (two SMs)
-  // of its own; at higher occupancy the SMs of a TPC compete for instruction
-  // fetch and the compact unpaired kernel is faster.  GDN_CHUNK_TC_PAIR=0 / 1
-  // forces either form (kernel cross-checks).
-  const int tiles = a.dv / DVT;
-  const long long ctas = (long long)tiles * a.B * a.H;
-  const int sms = device_sm_count();
-  const char* pair_env = getenv("GDN_CHUNK_TC_PAIR");
-  bool pair = tiles % 2 == 0 && ctas <= sms / 2;
-  if (pair_env && pair_env[0] == '0') pair = false;
-  if (pair_env && pair_env[0] == '1') pair = tiles % 2 == 0;
-  auto kernel = pair ? chunk_tc_kernel<true> : chunk_tc_kernel<false>;
+  auto kernel = chunk_tc_kernel<kPair, kLayer>;
   // The in-kernel register split assumes exactly kLaunchRegs per thread at
   // launch; with fewer, the chain warpgroup's increase could never be granted.
   // (Checked, and shared memory opted in, once per device and form.)
-  static std::atomic<int> smem_set[2][kMaxDevices] = {};
-  std::atomic<int>(&slot)[kMaxDevices] = smem_set[pair ? 1 : 0];
+  static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = cudaSuccess;
   if (slot[current_device()].load(std::memory_order_acquire) < SMEM_BYTES) {
     cudaFuncAttributes fa;
@@ -978,16 +1095,44 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = pair ? 2 : 1;
+  attr[0].val.clusterDim.x = kPair ? 2 : 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kernel, mk, mq, mv, a.g, a.beta, a.h0,
                          static_cast<__nv_bfloat16*>(a.o), a.hT, a.cu_seqlens, a.T, a.H, a.Hk,
-                         a.dv);
+                         a.dv, la);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
+  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  // Pairs of column tiles share the preparation (clusters of two CTAs) when
+  // the tile count is even and the grid leaves every CTA pair a TPC (two SMs)
+  // of its own; at higher occupancy the SMs of a TPC compete for instruction
+  // fetch and the compact unpaired kernel is faster.  GDN_CHUNK_TC_PAIR=0 / 1
+  // forces either form (kernel cross-checks).
+  const int tiles = a.dv / DVT;
+  const long long ctas = (long long)tiles * a.B * a.H;
+  const int sms = device_sm_count();
+  const char* pair_env = getenv("GDN_CHUNK_TC_PAIR");
+  bool pair = tiles % 2 == 0 && ctas <= sms / 2;
+  if (pair_env && pair_env[0] == '0') pair = false;
+  if (pair_env && pair_env[0] == '1') pair = tiles % 2 == 0;
+  const LayerArgs none;
+  return pair ? launch_tc_form<true, false>(a, none, st) : launch_tc_form<false, false>(a, none, st);
+}
+
+// The layer form always runs the two 64-column tiles of a row as a pair: the
+// norm of a row needs both halves.
+cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
+  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_tc_supported(a) || a.dv != 2 * DVT) return cudaErrorInvalidValue;
+  return launch_tc_form<true, true>(a, la, st);
 }
 
 }  // namespace gdn

@@ -140,6 +140,38 @@ int gdn_recurrent_fwd_layer(const void* q, const void* k, const void* v, const f
                      "gdn_recurrent_fwd_layer");
 }
 
+int gdn_chunk_fwd_layer(const void* q, const void* k, const void* v, const float* a,
+                        const float* b, const float* A_log, const float* dt_bias,
+                        const float* h0, float* hT, const void* gate, const float* norm_weight,
+                        float eps, void* y, int B, int T, int H, int Hk, int dk, int dv,
+                        int dtype, void* stream) {
+  g_err[0] = '\0';
+  // a, b take the places of g, beta in the common checks (same shapes)
+  int rc = check_common(q, k, v, a, b, h0, y, hT, B, T, H, dk, dv, dtype);
+  if (rc) return rc;
+  rc = check_groups(H, Hk);
+  if (rc) return rc;
+  if (T == 0 || (long long)B * H == 0)   // nothing to normalise: carry the state through
+    return chunk_fwd(q, k, v, a, b, h0, y, hT, nullptr, B, T, H, Hk, dk, dv, 64, dtype,
+                     GDN_SEMANTICS_EXACT, nullptr, 0, stream);
+  if (dtype != GDN_DTYPE_BF16 || dk != 128 || dv != 128)
+    return fail(GDN_ERR_UNSUPPORTED, "the chunked layer form covers bf16 inputs with dk = dv = "
+                "128 (dtype=%d dk=%d dv=%d)", dtype, dk, dv);
+  if (!A_log || !dt_bias || !norm_weight)
+    return fail(GDN_ERR_INVALID, "A_log, dt_bias and norm_weight must be non-NULL");
+  if (gate && !aligned16(gate)) return fail(GDN_ERR_INVALID, "gate is not 16-byte aligned");
+  if (!(eps >= 0.f) || eps > 1.f) return fail(GDN_ERR_INVALID, "eps=%g outside [0, 1]", (double)eps);
+  gdn::ChunkArgs ca{q, k, v, a, b, h0, y, hT, B, T, H, dk, dv, 64, dtype, GDN_SEMANTICS_EXACT,
+                    nullptr, 0, Hk};
+  if (!gdn::chunk_tc_supported(ca))
+    return fail(GDN_ERR_UNSUPPORTED, "the tensor-core chunk kernel is unavailable on this device");
+  gdn::LayerArgs la;
+  la.a = a; la.b = b; la.A_log = A_log; la.dt_bias = dt_bias;
+  la.gate = gate; la.weight = norm_weight; la.eps = eps;
+  return cuda_status(gdn::launch_chunk_tc_layer(ca, la, (cudaStream_t)stream),
+                     "gdn_chunk_fwd_layer");
+}
+
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int dtype,
                                  int semantics) {
   (void)B; (void)T; (void)H; (void)dk; (void)dv; (void)chunk; (void)dtype; (void)semantics;
@@ -340,6 +372,6 @@ int gdn_device_error(int clear) {
   return a ? a : b;
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 5; }
+int gdn_abi_version(void) { return (1 << 16) | 6; }
 
 }  // extern "C"

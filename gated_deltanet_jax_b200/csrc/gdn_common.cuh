@@ -66,4 +66,9 @@ __device__ __forceinline__ float gate_exp(float x) {
   return y;
 }
 
+// The GatedDeltaNet layer's gate functions (model.py:136-139, :53), on the
+// accurate expf / log1pf.
+__device__ __forceinline__ float softplus(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
+__device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+
 }  // namespace gdn

@@ -112,13 +112,14 @@ cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st);
 // current device (looked up on the first call per device, then kept).
 cudaError_t chunk_bwd_static_scratch(void** out);
 
-// The layer form of the decode step (model.py:136-139 before it, :47-53 after).
+// The layer form of the decode step and of the chunked forward (model.py:136-139
+// before the op, :47-53 after it).
 struct LayerArgs {
-  const float* a = nullptr;         // raw a_proj output, one per (b, h)
-  const float* b = nullptr;         // raw b_proj output, one per (b, h)
+  const float* a = nullptr;         // raw a_proj output [B, T, H]
+  const float* b = nullptr;         // raw b_proj output [B, T, H]
   const float* A_log = nullptr;     // [H]
   const float* dt_bias = nullptr;   // [H]
-  const void* gate = nullptr;       // [B, H, dv] output gate (input dtype), NULL: plain RMSNorm
+  const void* gate = nullptr;       // [B, T, H, dv] output gate (input dtype), NULL: plain RMSNorm
   const float* weight = nullptr;    // [dv] norm weight
   float eps = 1e-5f;
 };
@@ -138,6 +139,10 @@ int device_error_chunk_tc(bool clear);
 // Tensor-core chunk kernel: bf16, dk = 128, dv % 64 == 0, chunk = 64, exact.
 bool chunk_tc_supported(const ChunkArgs& a);
 cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
+// Its layer form (dv = 128, the two column tiles as one CTA pair): the gates
+// from the raw projections (a.g / a.beta unused) and the gated RMSNorm of
+// every output row, written to a.o.
+cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st);
 
 // Portable CUDA-core chunk kernel (any supported shape, fp32 or bf16 inputs).
 cudaError_t launch_chunk_simt(const ChunkArgs& a, cudaStream_t st);

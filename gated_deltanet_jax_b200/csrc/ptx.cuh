@@ -38,6 +38,15 @@ __device__ __forceinline__ float ldg_f32(const float* p) {
   return v;
 }
 
+// 16 bytes, read-only, issued exactly here (as ldg_f32).
+__device__ __forceinline__ uint4 ldg_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -190,6 +199,19 @@ __device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst_cluster_addr, uint
       "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
       "[%3];" ::"r"(dst_cluster_addr),
       "r"(src_saddr), "r"(bytes), "r"(bar_cluster_addr)
+      : "memory");
+}
+
+// One 32-bit store into another CTA's shared memory of the cluster, completing
+// 4 bytes of transaction on that CTA's mbarrier (the value is visible to a
+// thread that then sees the barrier's phase complete with a cluster-scope
+// acquire).
+__device__ __forceinline__ void st_async_cluster_f32(uint32_t dst_cluster_addr, float v,
+                                                     uint32_t bar_cluster_addr) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+          dst_cluster_addr),
+      "r"(__float_as_uint(v)), "r"(bar_cluster_addr)
       : "memory");
 }
 
@@ -408,6 +430,38 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
                : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 consecutive fp32 columns from each of two TMEM addresses of this
+// thread's lane (two x16 loads, one wait naming all 32 destinations).
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float (&a)[16],
+                                            float (&b)[16]) {
+  uint32_t r[32];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[16 * q + 0]), "=r"(r[16 * q + 1]), "=r"(r[16 * q + 2]), "=r"(r[16 * q + 3]),
+          "=r"(r[16 * q + 4]), "=r"(r[16 * q + 5]), "=r"(r[16 * q + 6]), "=r"(r[16 * q + 7]),
+          "=r"(r[16 * q + 8]), "=r"(r[16 * q + 9]), "=r"(r[16 * q + 10]), "=r"(r[16 * q + 11]),
+          "=r"(r[16 * q + 12]), "=r"(r[16 * q + 13]), "=r"(r[16 * q + 14]), "=r"(r[16 * q + 15])
+        : "r"(q == 0 ? ta : tb));
+  }
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    a[i] = __uint_as_float(r[i]);
+    b[i] = __uint_as_float(r[16 + i]);
+  }
 }
 
 // W in {16, 32, 64} consecutive fp32 columns of this thread's TMEM lane.

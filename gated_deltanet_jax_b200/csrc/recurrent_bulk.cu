@@ -52,8 +52,6 @@ struct BulkLayout {
   static_assert(state_bytes % 16 == 0 && qk_bytes % 16 == 0 && v_bytes % 16 == 0, "bulk sizes");
 };
 
-__device__ __forceinline__ float softplus(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
-
 // Four consecutive input elements kept as loaded (no conversion yet), so that
 // a load issued ahead of its use does not wait for its data where it is issued.
 template <typename Tin> struct Raw4;
@@ -70,7 +68,6 @@ template <> struct Raw4<__nv_bfloat16> {
                        __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xffff0000u));
   }
 };
-__device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
 
 template <typename Tin, int DK, int DV, bool kLayer>
 __global__ void __launch_bounds__(kThreads, 1)

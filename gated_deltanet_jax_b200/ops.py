@@ -320,8 +320,34 @@ def gated_delta_rule_decode_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
     recurrent op (``final_state_out=S`` with ``initial_state=S`` updates S in
     place).  Inference only: there is no backward for this form.
     """
+    return _layer_impl("gdn_recurrent_fwd_layer", q, k, v, a, b, A_log, dt_bias, gate,
+                       norm_weight, eps, initial_state, output_final_state, final_state_out)
+
+
+def gated_delta_rule_chunk_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
+                                 norm_weight=None, eps: float = 1e-5, initial_state=None,
+                                 output_final_state=False,
+                                 final_state_out: Optional[torch.Tensor] = None
+                                 ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """The GatedDeltaNet layer's core over a whole sequence (prefill) in one
+    kernel (gdn_chunk_fwd_layer): the gates from the raw projections, the
+    chunked forward (exact semantics), and the gated RMSNorm of every output
+    row -- what model.py:136-153 computes around chunk_gated_delta_rule_fwd
+    as separate operations.
+
+    q, k ``[B,T,Hk,128]`` and v ``[B,T,H,128]`` in bfloat16; a, b ``[B,T,H]``;
+    A_log, dt_bias ``[H]``; gate ``[B,T,H,128]`` in v's dtype or None;
+    norm_weight ``[128]`` (None: ones).  Returns ``(y, final_state)`` like
+    chunk_gated_delta_rule.  Inference only: there is no backward for this form.
+    """
+    return _layer_impl("gdn_chunk_fwd_layer", q, k, v, a, b, A_log, dt_bias, gate,
+                       norm_weight, eps, initial_state, output_final_state, final_state_out)
+
+
+def _layer_impl(entry, q, k, v, a, b, A_log, dt_bias, gate, norm_weight, eps, initial_state,
+                output_final_state, final_state_out):
     if _wants_grad(q, k, v, a, b, initial_state):
-        raise NotImplementedError("gated_delta_rule_decode_layer has no backward")
+        raise NotImplementedError("the layer forms have no backward")
     q, k, v, a, b, h0, hT, y, (B, T, H, Hk, dk, dv) = _prepare(
         q, k, v, a, b, initial_state, final_state_out, output_final_state)
     dev = q.device
@@ -346,11 +372,11 @@ def gated_delta_rule_decode_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
             gate = gate.clone()
     lib = _lib.load()
     with torch.cuda.device(dev):
-        rc = lib.gdn_recurrent_fwd_layer(
+        rc = getattr(lib, entry)(
             _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), _ptr(A_log), _ptr(dt_bias), _ptr(h0),
             _ptr(hT), _ptr(gate), _ptr(w), float(eps), _ptr(y), B, T, H, Hk, dk, dv,
             _DTYPES[q.dtype], torch.cuda.current_stream(dev).cuda_stream)
-    _lib.check(rc, "gdn_recurrent_fwd_layer")
+    _lib.check(rc, entry)
     return y, hT
 
 
@@ -363,4 +389,5 @@ __all__ = [
     "chunk_gated_delta_rule", "chunk_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule_pallas",
     "gated_delta_rule_decode_layer",
+    "gated_delta_rule_chunk_layer",
 ]

@@ -121,6 +121,25 @@ int gdn_recurrent_fwd_layer(const void* q, const void* k, const void* v,
                             int dtype, void* stream);
 
 /*
+ * The chunked forward with the same layer work on either side of it
+ * (prefill): gdn_recurrent_fwd_layer's prologue and epilogue around
+ * gdn_chunk_fwd_gva (exact semantics), for any T >= 0.  a, b [B, T, H] fp32
+ * (raw a_proj / b_proj outputs); gate [B, T, H, dv] (input dtype) or NULL;
+ * y [B, T, H, dv] in the input dtype.  Supported: bf16 inputs, dk = dv = 128
+ * (GDN_ERR_UNSUPPORTED otherwise).  The RMS statistic is taken over the fp32
+ * outputs before any rounding.  Replaces the separate operations of
+ * model.py:136-139 and :147-153 around chunk_gated_delta_rule_fwd
+ * (ops.py:299); no single counterpart in the reference.
+ */
+int gdn_chunk_fwd_layer(const void* q, const void* k, const void* v,
+                        const float* a, const float* b,
+                        const float* A_log, const float* dt_bias,
+                        const float* h0, float* hT,
+                        const void* gate, const float* norm_weight, float eps,
+                        void* y, int B, int T, int H, int Hk, int dk, int dv,
+                        int dtype, void* stream);
+
+/*
  * Packed variable-length sequences for the chunked forward: n_seqs sequences
  * stored back to back in one row of T tokens -- q, k [1, T, Hk, dk], v, o
  * [1, T, H, dv], g, beta [1, T, H] -- with sequence s the tokens
@@ -236,7 +255,8 @@ const char* gdn_last_error(void);
 
 /* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward;
  * 1.4: backward of packed sequences, the allocation-free backward;
- * 1.5: the layer form of the decode step). */
+ * 1.5: the layer form of the decode step; 1.6: the layer form of the chunked
+ * forward). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

@@ -179,6 +179,23 @@ def test_decode_layer_rejects_bad_arguments(lib):
     assert call(eps=-1.0) == _lib.GDN_ERR_INVALID
 
 
+def test_chunk_layer_rejects_bad_arguments(lib):
+    """Checked on the host before any CUDA call."""
+    p = ctypes.c_void_p(16)
+
+    def call(dk=128, dv=128, dtype=_lib.GDN_DTYPE_BF16, A=p, gate=None, w=p, eps=1e-5):
+        return lib.gdn_chunk_fwd_layer(p, p, p, p, p, A, p, None, None, gate, w, eps, p,
+                                       2, 100, 2, 2, dk, dv, dtype, None)
+    assert call(dtype=_lib.GDN_DTYPE_FP32) == _lib.GDN_ERR_UNSUPPORTED
+    assert b"bf16" in lib.gdn_last_error()
+    assert call(dk=64, dv=64) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(dv=256) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(A=None) == _lib.GDN_ERR_INVALID
+    assert call(w=None) == _lib.GDN_ERR_INVALID
+    assert call(gate=ctypes.c_void_p(24)) == _lib.GDN_ERR_INVALID
+    assert call(eps=float("nan")) == _lib.GDN_ERR_INVALID
+
+
 def test_empty_problem_is_a_no_op(lib):
     # B*H == 0: nothing to launch, no CUDA call, OK.
     assert _call_recurrent(lib, B=0) == _lib.GDN_OK
