@@ -90,8 +90,11 @@ constexpr int SM_BAR = SM_VEC + NTP * (int)sizeof(VecBuf);
 constexpr int NBAR = 40;
 // Layer form: ring of the other tile's row sums of squares.  A row is finished
 // one chunk after its products (its sum is read at the start of the next
-// chunk), and a CTA's chain runs at most NTP chunks ahead of the other's, so
-// NTP + 1 slots keep a slot from being rewritten before it was read.
+// chunk).  A CTA's chain runs at most NTP chunks ahead of the other's: with
+// shared preparation, because a T/P slot is refilled only after both chains
+// released it; without, because finishing row m waits for the other CTA's sum
+// of chunk m.  So NTP + 1 slots keep a slot from being rewritten before it
+// was read.
 constexpr int NSS = NTP + 1;
 constexpr int SM_TMEM = SM_BAR + NBAR * 8;
 constexpr int SM_SS = SM_TMEM + 16;             // layer form: NSS x [64] row partial sums, other tile
@@ -312,8 +315,11 @@ __device__ __forceinline__ bool wait_shared_bar(uint64_t* bars, int idx, uint32_
 // r: chunks n with n % 2 == r) and copies it into the other CTA's ring, so
 // the state-independent preparation is done once per (b, h) rather than once
 // per column tile.
-// kLayer (pairs, dv = 128 only): g and beta hold the raw a_proj / b_proj
-// outputs, and o receives the gated RMSNorm of the output (la).
+// kLayer (dv = 128 only): g and beta hold the raw a_proj / b_proj outputs,
+// and o receives the gated RMSNorm of the output (la).  The two column tiles
+// of a row always run as a cluster of two CTAs, which exchange the rows'
+// partial sums of squares; without kPair each still prepares every chunk (the
+// compact form, for high occupancy).
 template <bool kPair, bool kLayer>
 __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
@@ -322,7 +328,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
                 __nv_bfloat16* __restrict__ o, float* __restrict__ hT,
                 const int* __restrict__ cu_seqlens, int T, int H, int Hk, int dv,
                 const LayerArgs la) {
-  static_assert(!kLayer || kPair, "the layer form runs the two column tiles of a row as a pair");
+  constexpr bool kCluster = kPair || kLayer;  // launched in clusters of two CTAs
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // Round up to 1024 bytes by offsetting the shared array itself, so that the
   // compiler keeps every access below in the shared address space.
@@ -361,7 +367,8 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   constexpr int kWP = kPair ? 32 : 16;
   constexpr int kWC = kPair ? 64 : 16;
   const int step = kPair ? 2 : 1;
-  const uint32_t peer = (uint32_t)(rank ^ 1);
+  // the other CTA of the cluster (pairs: the T/P tiles; layer form: the row sums)
+  const uint32_t peer = kCluster ? (cluster_ctarank() ^ 1u) : 0u;
 
   if (tid == 0) {
     mbar_init(&bars[B_FULL + 0], 1);
@@ -402,7 +409,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   tc_fence_before();
   __syncthreads();
   // the other CTA's barriers are initialised before anything is sent to them
-  if (kPair) cluster_sync_all();
+  if (kCluster) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(sm);
@@ -1013,8 +1020,8 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
-  // neither CTA of a pair leaves while the other may still arrive on its barriers
-  if (kPair) cluster_sync_all();
+  // neither CTA of a cluster leaves while the other may still reach its shared memory
+  if (kCluster) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TM_COLS);
@@ -1095,7 +1102,7 @@ cudaError_t launch_tc_form(const ChunkArgs& a, const LayerArgs& la, cudaStream_t
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kPair ? 2 : 1;
+  attr[0].val.clusterDim.x = (kPair || kLayer) ? 2 : 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
@@ -1127,12 +1134,18 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   return pair ? launch_tc_form<true, false>(a, none, st) : launch_tc_form<false, false>(a, none, st);
 }
 
-// The layer form always runs the two 64-column tiles of a row as a pair: the
-// norm of a row needs both halves.
+// The layer form always runs the two 64-column tiles of a row as one cluster:
+// the norm of a row needs both halves.  Whether the two CTAs also share the
+// preparation follows the op's rule (GDN_CHUNK_TC_PAIR forces it too).
 cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   if (!chunk_tc_supported(a) || a.dv != 2 * DVT) return cudaErrorInvalidValue;
-  return launch_tc_form<true, true>(a, la, st);
+  const long long ctas = 2LL * a.B * a.H;
+  const char* pair_env = getenv("GDN_CHUNK_TC_PAIR");
+  bool pair = ctas <= device_sm_count() / 2;
+  if (pair_env && pair_env[0] == '0') pair = false;
+  if (pair_env && pair_env[0] == '1') pair = true;
+  return pair ? launch_tc_form<true, true>(a, la, st) : launch_tc_form<false, true>(a, la, st);
 }
 
 }  // namespace gdn

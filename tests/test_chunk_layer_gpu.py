@@ -81,6 +81,23 @@ def test_chunk_layer_full_size_equals_separate_operations(cuda):
     assert torch.isfinite(y).all()
 
 
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_chunk_layer_forms_agree(cuda, monkeypatch, pair):
+    """With and without shared preparation (GDN_CHUNK_TC_PAIR forces either
+    form; both are clusters of two CTAs exchanging row sums) the outputs are
+    bit-identical to the form the dispatcher picks for a small grid (pairs)."""
+    B, T, H = 2, 300, 4
+    (q, k, v, _, _, S), _ = device_inputs(B, T, H, 128, 128, seed=9, dtype="bf16", dev=cuda,
+                                          h0_std=0.02)
+    a, b, A_log, dt_bias, gate, w = _layer_extras(B, T, H, cuda, 9, True)
+    args = (q, k, v, a, b, A_log, dt_bias)
+    kw = dict(gate=gate, norm_weight=w, initial_state=S, output_final_state=True)
+    y0, h0 = ops.gated_delta_rule_chunk_layer(*args, **kw)
+    monkeypatch.setenv("GDN_CHUNK_TC_PAIR", pair)
+    y1, h1 = ops.gated_delta_rule_chunk_layer(*args, **kw)
+    assert torch.equal(y0, y1) and torch.equal(h0, h1)
+
+
 def test_chunk_layer_in_place_state_and_empty(cuda):
     B, T, H = 2, 130, 4
     (q, k, v, _, _, S), _ = device_inputs(B, T, H, 128, 128, seed=5, dtype="bf16", dev=cuda,
