@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "gdn_recurrent_fwd_gva",
     "gdn_recurrent_fwd_layer",
     "gdn_chunk_fwd_layer",
+    "gdn_chunk_fwd_layer_varlen",
     "gdn_chunk_fwd_gva",
     "gdn_chunk_fwd_varlen",
     "gdn_chunk_bwd",
@@ -68,6 +69,9 @@ def _declare(lib):
     lib.gdn_recurrent_fwd_layer.restype = _i
     lib.gdn_chunk_fwd_layer.argtypes = ([_vp] * 11 + [ctypes.c_float, _vp] + [_i] * 7 + [_vp])
     lib.gdn_chunk_fwd_layer.restype = _i
+    lib.gdn_chunk_fwd_layer_varlen.argtypes = ([_vp] * 11 + [ctypes.c_float, _vp, _vp]
+                                               + [_i] * 7 + [_vp])
+    lib.gdn_chunk_fwd_layer_varlen.restype = _i
     lib.gdn_chunk_fwd.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                   _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]
     lib.gdn_chunk_fwd.restype = _i

@@ -95,6 +95,41 @@ int chunk_bwd(const void* q, const void* k, const void* v, const float* g, const
               int T, int H, int Hk, int dk, int dv, int dtype, void* workspace, size_t ws_bytes,
               void* stream, const char* what);
 
+// The chunked layer form, dense (cu_seqlens NULL: B rows of T tokens) or packed
+// (B = n_seqs sequences in one row of T tokens).
+int chunk_fwd_layer(const void* q, const void* k, const void* v, const float* a,
+                    const float* b, const float* A_log, const float* dt_bias, const float* h0,
+                    float* hT, const void* gate, const float* norm_weight, float eps, void* y,
+                    const int* cu_seqlens, int B, int T, int H, int Hk, int dk, int dv,
+                    int dtype, void* stream) {
+  g_err[0] = '\0';
+  const int rows = cu_seqlens ? (B > 0 ? 1 : 0) : B;   // rows of the token tensors
+  // a, b take the places of g, beta in the common checks (same shapes)
+  int rc = check_common(q, k, v, a, b, h0, y, hT, rows, T, H, dk, dv, dtype);
+  if (rc) return rc;
+  rc = check_groups(H, Hk);
+  if (rc) return rc;
+  if (T == 0 || (long long)B * H == 0)   // nothing to normalise: carry the state through
+    return chunk_fwd(q, k, v, a, b, h0, y, hT, cu_seqlens, B, T, H, Hk, dk, dv, 64, dtype,
+                     GDN_SEMANTICS_EXACT, nullptr, 0, stream);
+  if (dtype != GDN_DTYPE_BF16 || dk != 128 || dv != 128)
+    return fail(GDN_ERR_UNSUPPORTED, "the chunked layer form covers bf16 inputs with dk = dv = "
+                "128 (dtype=%d dk=%d dv=%d)", dtype, dk, dv);
+  if (!A_log || !dt_bias || !norm_weight)
+    return fail(GDN_ERR_INVALID, "A_log, dt_bias and norm_weight must be non-NULL");
+  if (gate && !aligned16(gate)) return fail(GDN_ERR_INVALID, "gate is not 16-byte aligned");
+  if (!(eps >= 0.f) || eps > 1.f) return fail(GDN_ERR_INVALID, "eps=%g outside [0, 1]", (double)eps);
+  gdn::ChunkArgs ca{q, k, v, a, b, h0, y, hT, B, T, H, dk, dv, 64, dtype, GDN_SEMANTICS_EXACT,
+                    nullptr, 0, Hk, cu_seqlens};
+  if (!gdn::chunk_tc_supported(ca))
+    return fail(GDN_ERR_UNSUPPORTED, "the tensor-core chunk kernel is unavailable on this device");
+  gdn::LayerArgs la;
+  la.a = a; la.b = b; la.A_log = A_log; la.dt_bias = dt_bias;
+  la.gate = gate; la.weight = norm_weight; la.eps = eps;
+  return cuda_status(gdn::launch_chunk_tc_layer(ca, la, (cudaStream_t)stream),
+                     "gdn_chunk_fwd_layer");
+}
+
 }  // namespace
 
 extern "C" {
@@ -145,31 +180,23 @@ int gdn_chunk_fwd_layer(const void* q, const void* k, const void* v, const float
                         const float* h0, float* hT, const void* gate, const float* norm_weight,
                         float eps, void* y, int B, int T, int H, int Hk, int dk, int dv,
                         int dtype, void* stream) {
+  return chunk_fwd_layer(q, k, v, a, b, A_log, dt_bias, h0, hT, gate, norm_weight, eps, y,
+                         nullptr, B, T, H, Hk, dk, dv, dtype, stream);
+}
+
+int gdn_chunk_fwd_layer_varlen(const void* q, const void* k, const void* v, const float* a,
+                               const float* b, const float* A_log, const float* dt_bias,
+                               const float* h0, float* hT, const void* gate,
+                               const float* norm_weight, float eps, void* y,
+                               const int* cu_seqlens, int n_seqs, int T, int H, int Hk, int dk,
+                               int dv, int dtype, void* stream) {
   g_err[0] = '\0';
-  // a, b take the places of g, beta in the common checks (same shapes)
-  int rc = check_common(q, k, v, a, b, h0, y, hT, B, T, H, dk, dv, dtype);
-  if (rc) return rc;
-  rc = check_groups(H, Hk);
-  if (rc) return rc;
-  if (T == 0 || (long long)B * H == 0)   // nothing to normalise: carry the state through
-    return chunk_fwd(q, k, v, a, b, h0, y, hT, nullptr, B, T, H, Hk, dk, dv, 64, dtype,
-                     GDN_SEMANTICS_EXACT, nullptr, 0, stream);
-  if (dtype != GDN_DTYPE_BF16 || dk != 128 || dv != 128)
-    return fail(GDN_ERR_UNSUPPORTED, "the chunked layer form covers bf16 inputs with dk = dv = "
-                "128 (dtype=%d dk=%d dv=%d)", dtype, dk, dv);
-  if (!A_log || !dt_bias || !norm_weight)
-    return fail(GDN_ERR_INVALID, "A_log, dt_bias and norm_weight must be non-NULL");
-  if (gate && !aligned16(gate)) return fail(GDN_ERR_INVALID, "gate is not 16-byte aligned");
-  if (!(eps >= 0.f) || eps > 1.f) return fail(GDN_ERR_INVALID, "eps=%g outside [0, 1]", (double)eps);
-  gdn::ChunkArgs ca{q, k, v, a, b, h0, y, hT, B, T, H, dk, dv, 64, dtype, GDN_SEMANTICS_EXACT,
-                    nullptr, 0, Hk};
-  if (!gdn::chunk_tc_supported(ca))
-    return fail(GDN_ERR_UNSUPPORTED, "the tensor-core chunk kernel is unavailable on this device");
-  gdn::LayerArgs la;
-  la.a = a; la.b = b; la.A_log = A_log; la.dt_bias = dt_bias;
-  la.gate = gate; la.weight = norm_weight; la.eps = eps;
-  return cuda_status(gdn::launch_chunk_tc_layer(ca, la, (cudaStream_t)stream),
-                     "gdn_chunk_fwd_layer");
+  if (n_seqs < 0) return fail(GDN_ERR_INVALID, "negative n_seqs=%d", n_seqs);
+  if (n_seqs > 0 && !cu_seqlens) return fail(GDN_ERR_INVALID, "cu_seqlens must be non-NULL");
+  if (cu_seqlens && (reinterpret_cast<uintptr_t>(cu_seqlens) & 3u))
+    return fail(GDN_ERR_INVALID, "cu_seqlens is not 4-byte aligned");
+  return chunk_fwd_layer(q, k, v, a, b, A_log, dt_bias, h0, hT, gate, norm_weight, eps, y,
+                         cu_seqlens, n_seqs, T, H, Hk, dk, dv, dtype, stream);
 }
 
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int dtype,

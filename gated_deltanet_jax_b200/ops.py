@@ -327,7 +327,8 @@ def gated_delta_rule_decode_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
 def gated_delta_rule_chunk_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
                                  norm_weight=None, eps: float = 1e-5, initial_state=None,
                                  output_final_state=False,
-                                 final_state_out: Optional[torch.Tensor] = None
+                                 final_state_out: Optional[torch.Tensor] = None,
+                                 cu_seqlens: Optional[torch.Tensor] = None
                                  ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """The GatedDeltaNet layer's core over a whole sequence (prefill) in one
     kernel (gdn_chunk_fwd_layer): the gates from the raw projections, the
@@ -338,18 +339,22 @@ def gated_delta_rule_chunk_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
     q, k ``[B,T,Hk,128]`` and v ``[B,T,H,128]`` in bfloat16; a, b ``[B,T,H]``;
     A_log, dt_bias ``[H]``; gate ``[B,T,H,128]`` in v's dtype or None;
     norm_weight ``[128]`` (None: ones).  Returns ``(y, final_state)`` like
-    chunk_gated_delta_rule.  Inference only: there is no backward for this form.
+    chunk_gated_delta_rule, packed sequences included (``cu_seqlens``: one row
+    of T tokens holding N sequences, states ``[N,H,128,128]``).  Inference
+    only: there is no backward for this form.
     """
     return _layer_impl("gdn_chunk_fwd_layer", q, k, v, a, b, A_log, dt_bias, gate,
-                       norm_weight, eps, initial_state, output_final_state, final_state_out)
+                       norm_weight, eps, initial_state, output_final_state, final_state_out,
+                       cu_seqlens)
 
 
 def _layer_impl(entry, q, k, v, a, b, A_log, dt_bias, gate, norm_weight, eps, initial_state,
-                output_final_state, final_state_out):
+                output_final_state, final_state_out, cu_seqlens=None):
     if _wants_grad(q, k, v, a, b, initial_state):
         raise NotImplementedError("the layer forms have no backward")
+    n_seqs = None if cu_seqlens is None else _check_cu_seqlens(q, cu_seqlens)
     q, k, v, a, b, h0, hT, y, (B, T, H, Hk, dk, dv) = _prepare(
-        q, k, v, a, b, initial_state, final_state_out, output_final_state)
+        q, k, v, a, b, initial_state, final_state_out, output_final_state, n_seqs)
     dev = q.device
 
     def vec(t, n, name):
@@ -372,10 +377,16 @@ def _layer_impl(entry, q, k, v, a, b, A_log, dt_bias, gate, norm_weight, eps, in
             gate = gate.clone()
     lib = _lib.load()
     with torch.cuda.device(dev):
-        rc = getattr(lib, entry)(
-            _ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), _ptr(A_log), _ptr(dt_bias), _ptr(h0),
-            _ptr(hT), _ptr(gate), _ptr(w), float(eps), _ptr(y), B, T, H, Hk, dk, dv,
-            _DTYPES[q.dtype], torch.cuda.current_stream(dev).cuda_stream)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        head = (_ptr(q), _ptr(k), _ptr(v), _ptr(a), _ptr(b), _ptr(A_log), _ptr(dt_bias),
+                _ptr(h0), _ptr(hT), _ptr(gate), _ptr(w), float(eps), _ptr(y))
+        if n_seqs is not None:
+            entry += "_varlen"
+            cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+            rc = getattr(lib, entry)(*head, _ptr(cu), n_seqs, T, H, Hk, dk, dv,
+                                     _DTYPES[q.dtype], stream)
+        else:
+            rc = getattr(lib, entry)(*head, B, T, H, Hk, dk, dv, _DTYPES[q.dtype], stream)
     _lib.check(rc, entry)
     return y, hT
 

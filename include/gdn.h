@@ -140,6 +140,23 @@ int gdn_chunk_fwd_layer(const void* q, const void* k, const void* v,
                         int dtype, void* stream);
 
 /*
+ * gdn_chunk_fwd_layer on packed variable-length sequences, laid out as for
+ * gdn_chunk_fwd_varlen: n_seqs sequences back to back in one row of T tokens
+ * (q, k [1, T, Hk, dk]; v, gate, y [1, T, H, dv]; a, b [1, T, H]), sequence s
+ * the tokens [cu_seqlens[s], cu_seqlens[s + 1]); h0 / hT [n_seqs, H, dk, dv].
+ * Each sequence gets what gdn_chunk_fwd_layer gives it on its own.  No
+ * counterpart in the reference, whose layer takes one dense [B, T] batch.
+ */
+int gdn_chunk_fwd_layer_varlen(const void* q, const void* k, const void* v,
+                               const float* a, const float* b,
+                               const float* A_log, const float* dt_bias,
+                               const float* h0, float* hT,
+                               const void* gate, const float* norm_weight, float eps,
+                               void* y, const int* cu_seqlens, int n_seqs,
+                               int T, int H, int Hk, int dk, int dv,
+                               int dtype, void* stream);
+
+/*
  * Packed variable-length sequences for the chunked forward: n_seqs sequences
  * stored back to back in one row of T tokens -- q, k [1, T, Hk, dk], v, o
  * [1, T, H, dv], g, beta [1, T, H] -- with sequence s the tokens

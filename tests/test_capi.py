@@ -196,6 +196,19 @@ def test_chunk_layer_rejects_bad_arguments(lib):
     assert call(eps=float("nan")) == _lib.GDN_ERR_INVALID
 
 
+def test_chunk_layer_varlen_rejects_bad_arguments(lib):
+    """Checked on the host before any CUDA call."""
+    p = ctypes.c_void_p(16)
+
+    def call(cu=p, n=2, dtype=_lib.GDN_DTYPE_BF16):
+        return lib.gdn_chunk_fwd_layer_varlen(p, p, p, p, p, p, p, None, None, None, p, 1e-5, p,
+                                              cu, n, 100, 2, 2, 128, 128, dtype, None)
+    assert call(n=-1) == _lib.GDN_ERR_INVALID
+    assert call(cu=None) == _lib.GDN_ERR_INVALID
+    assert call(cu=ctypes.c_void_p(18)) == _lib.GDN_ERR_INVALID
+    assert call(dtype=_lib.GDN_DTYPE_FP32) == _lib.GDN_ERR_UNSUPPORTED
+
+
 def test_empty_problem_is_a_no_op(lib):
     # B*H == 0: nothing to launch, no CUDA call, OK.
     assert _call_recurrent(lib, B=0) == _lib.GDN_OK

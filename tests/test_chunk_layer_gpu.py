@@ -6,6 +6,7 @@ against the same parts run as separate operations on the GPU."""
 
 import math
 
+import numpy as np
 import pytest
 import torch
 
@@ -117,6 +118,29 @@ def test_chunk_layer_in_place_state_and_empty(cuda):
                                               gate=e[5], norm_weight=w, initial_state=S,
                                               output_final_state=True)
     assert y0.shape == (B, 0, H, 128) and torch.equal(h0, S)
+
+
+@pytest.mark.parametrize("lens", [(100, 1, 101), (64, 0, 128, 7)])
+def test_chunk_layer_packed_sequences_equal_each_alone(cuda, lens):
+    """Packed sequences (cu_seqlens) in one row: every sequence's y and final
+    state equal the same layer form run on that sequence alone."""
+    T, H = sum(lens), 4
+    (q, k, v, _, _, _), _ = device_inputs(1, T, H, 128, 128, seed=T, dtype="bf16", dev=cuda)
+    a, b, A_log, dt_bias, gate, w = _layer_extras(1, T, H, cuda, T, True)
+    gen = torch.Generator(device=cuda).manual_seed(T + 1)
+    S = torch.randn(len(lens), H, 128, 128, device=cuda, generator=gen) * 0.02
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=cuda)
+    y, hT = ops.gated_delta_rule_chunk_layer(q, k, v, a, b, A_log, dt_bias, gate=gate,
+                                             norm_weight=w, initial_state=S,
+                                             output_final_state=True, cu_seqlens=cu)
+    assert y.shape == v.shape and hT.shape == S.shape
+    for s, (t0, t1) in enumerate(zip(cu.tolist(), cu.tolist()[1:])):
+        part = [t[:, t0:t1].contiguous() for t in (q, k, v, a, b, gate)]
+        ys, hs = ops.gated_delta_rule_chunk_layer(*part[:5], A_log, dt_bias, gate=part[5],
+                                                  norm_weight=w, initial_state=S[s:s + 1],
+                                                  output_final_state=True)
+        assert torch.equal(y[:, t0:t1], ys), s
+        assert torch.equal(hT[s:s + 1], hs), s
 
 
 def test_no_device_error_recorded_chunk_layer(cuda):
