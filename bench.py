@@ -627,7 +627,8 @@ def prefill_layer_leg(d, a):
             "fused_ms": res["fused"], "unfused_ms": res["unfused"], "op_only_ms": res["op_only"],
             "speedup": res["unfused"] / res["fused"], "launches": 3 * REP * steps,
             "fused_tokens_per_s": d.world * B * T / (res["fused"] / 1e3),
-            "path": "fused: gdn_chunk_fwd_layer (1 launch, CTA pairs); unfused: torch gates, "
+            "path": "fused: gdn_chunk_fwd_layer (1 launch; the two column tiles of a row as one "
+                    "cluster of two CTAs); unfused: torch gates, "
                     "gdn_chunk_fwd, torch gated RMSNorm; op_only: gdn_chunk_fwd with "
                     "precomputed gates and no norm"}
 
