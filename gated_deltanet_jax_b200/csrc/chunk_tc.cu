@@ -54,9 +54,7 @@ namespace gdn {
 namespace {
 
 constexpr int C = 64;
-constexpr int DK = 128;
 constexpr int DVT = 64;
-constexpr int NSTAGE = 2;
 constexpr int kThreads = 512;
 // Register split (per thread): the kernel is compiled for, and launched with,
 // kLaunchRegs; warpgroup 0 (producer, MMA issuers, gate) gives registers to the
@@ -65,19 +63,7 @@ constexpr int kLaunchRegs = 128;
 constexpr int kRegsRoles = 56, kRegsPrep = 128, kRegsChain = 200;
 static_assert(kRegsRoles + 2 * kRegsPrep + kRegsChain == 4 * kLaunchRegs, "register split");
 constexpr int LDF = 68;  // fp32 row stride of the A / T matrices (16-byte aligned rows)
-
-// Shared-memory byte offsets from a 1024-byte aligned base.
-constexpr int SM_KQ = 0;                        // NSTAGE x [2 kblk][128 rows][128 B]
-constexpr int SM_V = SM_KQ + NSTAGE * 32768;    // NSTAGE x [64 rows][128 B]
-constexpr int SM_S = SM_V + NSTAGE * 8192;      // [128 rows (dk)][128 B]
-constexpr int SM_X = SM_S + 16384;              // [64 rows (token)][128 B]
-constexpr int SM_VPP = SM_X + 8192;             // V'' = e^{G_C-G} V'
-constexpr int SM_VP = SM_VPP + 8192;            // V'
-constexpr int NTP = 3;                          // depth of the T/P tile and gate-vector rings
-constexpr int SM_TP = SM_VP + 8192;             // NTP x [128 rows][128 B]: rows 0-63 T, 64-127 P
-constexpr int SM_AF = SM_TP + NTP * 16384;      // fp32 A [64][LDF]
-constexpr int SM_TF = SM_AF + 64 * LDF * 4;     // fp32 T [64][LDF]
-constexpr int SM_VEC = SM_TF + 64 * LDF * 4;    // NTP x VecBuf
+constexpr int NTP = 3;   // depth of the T/P tile and gate-vector rings
 struct VecBuf {
   float G[C], eG[C], dec[C], beta[C];
   float F[C][4];  // e^{G_i - G_{16k}} for k <= i / 16 (gate factors, row part)
@@ -86,7 +72,6 @@ struct VecBuf {
   int direct;     // 1: a factor exponent exceeds 40; form e^{G_i - G_j} directly
   float pad[2];
 };
-constexpr int SM_BAR = SM_VEC + NTP * (int)sizeof(VecBuf);
 constexpr int NBAR = 40;
 // Layer form: ring of the other tile's row sums of squares.  A row is finished
 // one chunk after its products (its sum is read at the start of the next
@@ -96,13 +81,36 @@ constexpr int NBAR = 40;
 // of chunk m.  So NTP + 1 slots keep a slot from being rewritten before it
 // was read.
 constexpr int NSS = NTP + 1;
-constexpr int SM_TMEM = SM_BAR + NBAR * 8;
-constexpr int SM_SS = SM_TMEM + 16;             // layer form: NSS x [64] row partial sums, other tile
-constexpr int SM_W = SM_SS + NSS * 64 * 4;      // layer form: norm weight of this column tile
-constexpr int SM_OB = SM_W + DVT * 4;           // layer form: [64 rows][128 B] bf16 output rows
-constexpr int SM_TOTAL = SM_OB + 8192;
-constexpr int SMEM_BYTES = SM_TOTAL + 1024;  // + alignment slack
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+
+// Shared-memory byte offsets from a 1024-byte aligned base, for key width DK
+// (128 or 256).  K and Q of a chunk sit in DK / 64 blocks of [128 rows][128 B]
+// (rows 0-63 K, 64-127 Q, 64 key dimensions each).  DK = 256 keeps one such
+// stage (64 KB) instead of two, and has no layer-form buffers, to stay within
+// 227 KB.
+template <int DK>
+struct Lay {
+  static constexpr int NSTAGE = DK == 128 ? 2 : 1;
+  static constexpr int KQ_STAGE = DK / 64 * 16384;
+  static constexpr int SM_KQ = 0;                          // NSTAGE x KQ_STAGE
+  static constexpr int SM_V = SM_KQ + NSTAGE * KQ_STAGE;   // NSTAGE x [64 rows][128 B]
+  static constexpr int SM_S = SM_V + NSTAGE * 8192;        // [DK rows][128 B]
+  static constexpr int SM_X = SM_S + DK * 128;             // [64 rows (token)][128 B]
+  static constexpr int SM_VPP = SM_X + 8192;               // V'' = e^{G_C-G} V'
+  static constexpr int SM_VP = SM_VPP + 8192;              // V'
+  static constexpr int SM_TP = SM_VP + 8192;               // NTP x [128 rows][128 B]: T, P
+  static constexpr int SM_AF = SM_TP + NTP * 16384;        // fp32 A [64][LDF]
+  static constexpr int SM_TF = SM_AF + 64 * LDF * 4;       // fp32 T [64][LDF]
+  static constexpr int SM_VEC = SM_TF + 64 * LDF * 4;      // NTP x VecBuf
+  static constexpr int SM_BAR = SM_VEC + NTP * (int)sizeof(VecBuf);
+  static constexpr int SM_TMEM = SM_BAR + NBAR * 8;
+  static constexpr bool kHasLayer = DK == 128;
+  static constexpr int SM_SS = SM_TMEM + 16;               // layer form: NSS x [64] row sums
+  static constexpr int SM_W = SM_SS + (kHasLayer ? NSS * 64 * 4 : 0);  // layer: norm weight
+  static constexpr int SM_OB = SM_W + (kHasLayer ? DVT * 4 : 0);       // layer: bf16 rows
+  static constexpr int SM_TOTAL = SM_OB + (kHasLayer ? 8192 : 0);
+  static constexpr int SMEM_BYTES = SM_TOTAL + 1024;       // + alignment slack
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
 
 // barrier indices
 enum {
@@ -124,7 +132,7 @@ static_assert(B_SS + NSS <= NBAR, "barriers");
 constexpr uint32_t TM_PRE = 0;    // 2 x 64
 constexpr uint32_t TM_D1 = 128;   // 2 x 64
 constexpr uint32_t TM_D2 = 256;
-constexpr uint32_t TM_D3 = 320;
+constexpr uint32_t TM_D3 = 320;   // DK = 256: a second M = 128 half at TM_D3 + 128
 constexpr uint32_t TM_D4 = 384;
 constexpr uint32_t TM_COLS = 512;
 
@@ -320,7 +328,7 @@ __device__ __forceinline__ bool wait_shared_bar(uint64_t* bars, int idx, uint32_
 // of a row always run as a cluster of two CTAs, which exchange the rows'
 // partial sums of squares; without kPair each still prepares every chunk (the
 // compact form, for high occupancy).
-template <bool kPair, bool kLayer>
+template <int DK, bool kPair, bool kLayer>
 __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
@@ -329,6 +337,16 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
                 const int* __restrict__ cu_seqlens, int T, int H, int Hk, int dv,
                 const LayerArgs la) {
   constexpr bool kCluster = kPair || kLayer;  // launched in clusters of two CTAs
+  static_assert(DK == 128 || (DK == 256 && !kPair && !kLayer), "key width");
+  using L = Lay<DK>;
+  constexpr int NSTAGE = L::NSTAGE, KQ_STAGE = L::KQ_STAGE;
+  constexpr int SM_KQ = L::SM_KQ, SM_V = L::SM_V, SM_S = L::SM_S, SM_X = L::SM_X;
+  constexpr int SM_VPP = L::SM_VPP, SM_VP = L::SM_VP, SM_TP = L::SM_TP, SM_AF = L::SM_AF;
+  constexpr int SM_TF = L::SM_TF, SM_VEC = L::SM_VEC, SM_BAR = L::SM_BAR, SM_TMEM = L::SM_TMEM;
+  constexpr int SM_SS = L::SM_SS, SM_W = L::SM_W, SM_OB = L::SM_OB;
+  constexpr int KB = DK / 64;    // 64-dimension key blocks
+  constexpr int KSTEPS = DK / 16;  // MMA steps over the key dimension
+  constexpr int RG = DK / 128;   // state rows per chain thread (rows r, r + 128)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // Round up to 1024 bytes by offsetting the shared array itself, so that the
   // compiler keeps every access below in the shared address space.
@@ -425,14 +443,14 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           const int s = n % NSTAGE;
           if (n >= NSTAGE) ok = wait_bar(bars, B_EMPTY + s, (uint32_t)((n / NSTAGE) - 1) & 1u);
           if (!ok) break;
-          unsigned char* kq = sm + SM_KQ + s * 32768;
+          unsigned char* kq = sm + SM_KQ + s * KQ_STAGE;
           uint64_t* fb = &bars[B_FULL + s];
-          mbar_arrive_expect_tx(fb, 4 * 8192 + 8192);
+          mbar_arrive_expect_tx(fb, KB * 2 * 8192 + 8192);
           const int t0 = tok0 + n * C;
-          tma_load_4d(kq, &tmK, 0, hq, t0, b, fb);
-          tma_load_4d(kq + 16384, &tmK, 64, hq, t0, b, fb);
-          tma_load_4d(kq + 8192, &tmQ, 0, hq, t0, b, fb);
-          tma_load_4d(kq + 16384 + 8192, &tmQ, 64, hq, t0, b, fb);
+          for (int kb = 0; kb < KB; ++kb) {
+            tma_load_4d(kq + kb * 16384, &tmK, 64 * kb, hq, t0, b, fb);
+            tma_load_4d(kq + kb * 16384 + 8192, &tmQ, 64 * kb, hq, t0, b, fb);
+          }
           tma_load_4d(sm + SM_V + s * 8192, &tmV, c0, h, t0, b, fb);
           issued = n + 1;
         }
@@ -446,16 +464,16 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         bool ok = true;
         for (int n = 0; n < N && ok; ++n) {
           const int s = n % NSTAGE, tb = n & 1, rb = n % NTP;
-          const uint32_t kq = sbase + SM_KQ + s * 32768;
+          const uint32_t kq = sbase + SM_KQ + s * KQ_STAGE;
           const uint32_t tp = sbase + SM_TP + rb * 16384;
           ok = wait_bar(bars, B_FULL + s, (uint32_t)(n / NSTAGE) & 1u) &&
                wait_bar(bars, B_S_READY, (uint32_t)n & 1u);
           if (!ok) break;
           tc_fence_after();
-          // D1 = [K;Q] S   (K-dim = dk: 8 steps of 16)
+          // D1 = [K;Q] S   (K-dim = dk: DK / 16 steps of 16)
           const uint32_t d1 = tmem + TM_D1 + (uint32_t)tb * 64;
   #pragma unroll (kPair ? 8 : 1)
-          for (int k = 0; k < 8; ++k) {
+          for (int k = 0; k < KSTEPS; ++k) {
             const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
             const uint64_t bd = umma_desc(sbase + SM_S + k * 2048, 16384, 1024, SW128);
             mma_bf16(d1, a, bd, IDESC_KM, k > 0);
@@ -477,11 +495,15 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           ok = wait_bar(bars, B_VPP_READY, (uint32_t)n & 1u);
           if (!ok) break;
           tc_fence_after();
+          // (DK = 256: rows 128-255 of the increment, key blocks 2-3, into TM_D3 + 128)
+  #pragma unroll
+          for (int rg = 0; rg < RG; ++rg) {
   #pragma unroll (kPair ? 4 : 1)
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t a = umma_desc(kq + k * 2048, 16384, 1024, SW128);
-            const uint64_t bd = umma_desc(sbase + SM_VPP + k * 2048, 8192, 1024, SW128);
-            mma_bf16(tmem + TM_D3, a, bd, IDESC_MM, k > 0);
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t a = umma_desc(kq + rg * 32768 + k * 2048, 16384, 1024, SW128);
+              const uint64_t bd = umma_desc(sbase + SM_VPP + k * 2048, 8192, 1024, SW128);
+              mma_bf16(tmem + TM_D3 + (uint32_t)rg * 128, a, bd, IDESC_MM, k > 0);
+            }
           }
           mma_commit(&bars[B_D3]);
           mma_commit(&bars[B_EMPTY + s]);  // K, Q, V of this stage are no longer read
@@ -510,9 +532,9 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
           if (ok && j >= 2) ok = wait_bar(bars, B_PRE_EMPTY + pb, (uint32_t)((j - 2) >> 1) & 1u);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t kq = sbase + SM_KQ + s * 32768;
+          const uint32_t kq = sbase + SM_KQ + s * KQ_STAGE;
   #pragma unroll (kPair ? 8 : 1)
-          for (int k = 0; k < 8; ++k) {
+          for (int k = 0; k < KSTEPS; ++k) {
             const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
             mma_bf16(tmem + TM_PRE + (uint32_t)pb * 64, a, a, IDESC_KK, k > 0);
           }
@@ -778,18 +800,23 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
     const int wq = warp - 12;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     unsigned char* Stile = sm + SM_S;
-    float S[DVT];
-    {
-      const float* src = h0 ? h0 + ((size_t)bh * DK + r) * dv + c0 : nullptr;
+    // state rows r (and, DK = 256, r + 128) of this column tile
+    float S[RG][DVT];
+#pragma unroll
+    for (int rg = 0; rg < RG; ++rg) {
+      const int row = r + 128 * rg;
+      const float* src = h0 ? h0 + ((size_t)bh * DK + row) * dv + c0 : nullptr;
 #pragma unroll
       for (int c = 0; c < DVT; c += 4) {
         const float4 v = src ? *reinterpret_cast<const float4*>(src + c)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
-        S[c] = v.x; S[c + 1] = v.y; S[c + 2] = v.z; S[c + 3] = v.w;
+        S[rg][c] = v.x; S[rg][c + 1] = v.y; S[rg][c + 2] = v.z; S[rg][c + 3] = v.w;
       }
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8)
-        *reinterpret_cast<uint4*>(Stile + sw128(r, c8)) = pack_bf16x8(S + c8 * 8);
+        *reinterpret_cast<uint4*>(Stile + sw128(row, c8)) = pack_bf16x8(S[rg] + c8 * 8);
+    }
+    {
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[B_S_READY]);
@@ -919,23 +946,43 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[B_VPP_READY]);
       }
-      // ---- epilogue 3: S <- e^{G_C} S + K^T V''  (all 128 rows) ----
+      // ---- epilogue 3: S <- e^{G_C} S + K^T V''  (all DK rows) ----
       // (warps 2-3 read the gate vectors from here on: acquire them directly)
       ok = wait_bar(bars, B_D3, (uint32_t)n & 1u) &&
            (wq < 2 || wait_bar(bars, B_VEC_FULL + rb, (uint32_t)(n / NTP) & 1u));
       if (!ok) break;
       tc_fence_after();
-      {
+      if constexpr (DK == 128) {
         const float egc = vb.eGC;
         float dsrow[64];
         tmem_ld64(tmem + TM_D3 + lane_off, dsrow);
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const float* ds = dsrow + 16 * q4;
+          float* Sr = S[0];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) S[q4 * 16 + e] = fmaf(egc, S[q4 * 16 + e], ds[e]);
-          *reinterpret_cast<uint4*>(Stile + sw128(r, 2 * q4)) = pack_bf16x8(S + q4 * 16);
-          *reinterpret_cast<uint4*>(Stile + sw128(r, 2 * q4 + 1)) = pack_bf16x8(S + q4 * 16 + 8);
+          for (int e = 0; e < 16; ++e) Sr[q4 * 16 + e] = fmaf(egc, Sr[q4 * 16 + e], ds[e]);
+          *reinterpret_cast<uint4*>(Stile + sw128(r, 2 * q4)) = pack_bf16x8(Sr + q4 * 16);
+          *reinterpret_cast<uint4*>(Stile + sw128(r, 2 * q4 + 1)) = pack_bf16x8(Sr + q4 * 16 + 8);
+        }
+      } else {
+        // (two row groups: 32 columns of the increment per TMEM read, to stay
+        // within the chain's registers next to the 128 state values)
+        const float egc = vb.eGC;
+#pragma unroll
+        for (int rg = 0; rg < RG; ++rg) {
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            float ds[32];
+            tmem_ld32(tmem + TM_D3 + (uint32_t)rg * 128 + lane_off + h2 * 32, ds);
+            float* Sr = S[rg] + 32 * h2;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) Sr[e] = fmaf(egc, Sr[e], ds[e]);
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8)
+              *reinterpret_cast<uint4*>(Stile + sw128(r + 128 * rg, 4 * h2 + c8)) =
+                  pack_bf16x8(Sr + 8 * c8);
+          }
         }
       }
       fence_proxy_async_smem();
@@ -1012,10 +1059,14 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       if (ok && wq >= 2 && N > 0) ok = finish_row(N - 1);
     }
     if (ok && hT) {
-      float* dst = hT + ((size_t)bh * DK + r) * dv + c0;
 #pragma unroll
-      for (int c = 0; c < DVT; c += 4)
-        *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+      for (int rg = 0; rg < RG; ++rg) {
+        float* dst = hT + ((size_t)bh * DK + r + 128 * rg) * dv + c0;
+#pragma unroll
+        for (int c = 0; c < DVT; c += 4)
+          *reinterpret_cast<float4*>(dst + c) =
+              make_float4(S[rg][c], S[rg][c + 1], S[rg][c + 2], S[rg][c + 3]);
+      }
     }
   }
   tc_fence_before();
@@ -1068,20 +1119,21 @@ GDN_DEVICE_ERROR_ACCESSOR(device_error_chunk_tc)
 // reference-literal semantics depend on the chunk length (partial-chunk decay,
 // output order) and stay with the CUDA-core kernel.
 bool chunk_tc_supported(const ChunkArgs& a) {
-  return a.dtype == kBF16 && a.semantics == kExact && a.dk == DK && a.dv % DVT == 0 &&
-         a.T > 0 && encode_fn() != nullptr;
+  return a.dtype == kBF16 && a.semantics == kExact && (a.dk == 128 || a.dk == 256) &&
+         a.dv % DVT == 0 && a.T > 0 && encode_fn() != nullptr;
 }
 
 namespace {
 
-template <bool kPair, bool kLayer>
+template <int DK, bool kPair, bool kLayer>
 cudaError_t launch_tc_form(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
+  constexpr int SMEM_BYTES = Lay<DK>::SMEM_BYTES;
   CUtensorMap mk, mq, mv;
   const int rows = a.cu_seqlens ? 1 : a.B;  // packed sequences share one row of T tokens
   if (!make_map(&mk, a.k, rows, a.T, a.Hk, a.dk) || !make_map(&mq, a.q, rows, a.T, a.Hk, a.dk) ||
       !make_map(&mv, a.v, rows, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
-  auto kernel = chunk_tc_kernel<kPair, kLayer>;
+  auto kernel = chunk_tc_kernel<DK, kPair, kLayer>;
   // The in-kernel register split assumes exactly kLaunchRegs per thread at
   // launch; with fewer, the chain warpgroup's increase could never be granted.
   // (Checked, and shared memory opted in, once per device and form.)
@@ -1131,7 +1183,10 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
   if (pair_env && pair_env[0] == '0') pair = false;
   if (pair_env && pair_env[0] == '1') pair = tiles % 2 == 0;
   const LayerArgs none;
-  return pair ? launch_tc_form<true, false>(a, none, st) : launch_tc_form<false, false>(a, none, st);
+  // (DK = 256: the unpaired form only)
+  if (a.dk == 256) return launch_tc_form<256, false, false>(a, none, st);
+  return pair ? launch_tc_form<128, true, false>(a, none, st)
+              : launch_tc_form<128, false, false>(a, none, st);
 }
 
 // The layer form always runs the two 64-column tiles of a row as one cluster:
@@ -1139,13 +1194,14 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
 // preparation follows the op's rule (GDN_CHUNK_TC_PAIR forces it too).
 cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
-  if (!chunk_tc_supported(a) || a.dv != 2 * DVT) return cudaErrorInvalidValue;
+  if (!chunk_tc_supported(a) || a.dk != 128 || a.dv != 2 * DVT) return cudaErrorInvalidValue;
   const long long ctas = 2LL * a.B * a.H;
   const char* pair_env = getenv("GDN_CHUNK_TC_PAIR");
   bool pair = ctas <= device_sm_count() / 2;
   if (pair_env && pair_env[0] == '0') pair = false;
   if (pair_env && pair_env[0] == '1') pair = true;
-  return pair ? launch_tc_form<true, true>(a, la, st) : launch_tc_form<false, true>(a, la, st);
+  return pair ? launch_tc_form<128, true, true>(a, la, st)
+              : launch_tc_form<128, false, true>(a, la, st);
 }
 
 }  // namespace gdn

@@ -193,3 +193,65 @@ def test_tensor_core_gate_ranges(cuda, gscale, gshift):
     assert np.isfinite(ro).all()
     assert_close(f64(o), ro, "bf16", "o")
     assert_close(f64(hT), rh, "bf16", "state")
+
+
+@pytest.mark.parametrize("dv", [64, 512])
+@pytest.mark.parametrize("T", [1, 65, 300])
+@pytest.mark.parametrize("Hk", [2, 1])
+def test_tensor_core_dk256_against_oracle(cuda, dv, T, Hk):
+    """bf16, dk=256 (the head_dim of the reference's default configuration):
+    the tcgen05 kernel with one K/Q stage and two state rows per chain thread,
+    partial chunks and grouped q/k heads included."""
+    H = 2
+    (q, k, v, g, b, h0), host = device_inputs(2, T, H, 256, dv, seed=dv + T + Hk, dtype="bf16",
+                                              dev=cuda, h0_std=0.05)
+    rep = H // Hk
+    q, k = q[:, :, ::rep].contiguous(), k[:, :, ::rep].contiguous()
+    o, hT = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    ro, rh = orc.chunk_exact(orc.repeat_heads(f64(q), rep), orc.repeat_heads(f64(k), rep),
+                             *host[2:5], host[5], 64)
+    assert_close(f64(o), ro, "bf16", "o")
+    assert_close(f64(hT), rh, "bf16", "state")
+
+
+def test_tensor_core_dk256_matches_cuda_core_kernel(cuda):
+    """The reference configuration's head dims (dk=256, dv=512) on both kernels."""
+    q, k, v, g, b, h0 = device_inputs_fast(2, 300, 3, 256, 512, seed=5, dtype="bf16", dev=cuda,
+                                           h0_std=0.02)
+
+    def run():
+        return ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                          output_final_state=True)
+
+    o_tc, h_tc = run()
+    o_cc, h_cc = _with_kernel("simt", run)
+    assert_close(f64(o_tc), f64(o_cc), "bf16", "o")
+    assert_close(f64(h_tc), f64(h_cc), "bf16", "state")
+
+
+def test_tensor_core_dk256_packed_sequences_equal_each_alone(cuda):
+    lens = (100, 0, 129, 7)
+    T, H = sum(lens), 2
+    q, k, v, g, b, _ = device_inputs_fast(1, T, H, 256, 128, seed=3, dtype="bf16", dev=cuda)
+    gen = torch.Generator(device=cuda).manual_seed(4)
+    S = torch.randn(len(lens), H, 256, 128, device=cuda, generator=gen) * 0.02
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=cuda)
+    o, hT = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=S, output_final_state=True,
+                                       cu_seqlens=cu)
+    for s, (t0, t1) in enumerate(zip(cu.tolist(), cu.tolist()[1:])):
+        part = [t[:, t0:t1].contiguous() for t in (q, k, v, g, b)]
+        os_, hs = ops.chunk_gated_delta_rule(*part, initial_state=S[s:s + 1],
+                                             output_final_state=True)
+        assert torch.equal(o[:, t0:t1], os_), s
+        assert torch.equal(hT[s:s + 1], hs), s
+
+
+def test_tensor_core_dk256_steep_gates(cuda):
+    (q, k, v, g, b, h0), host = device_inputs(1, 200, 2, 256, 128, seed=23, dtype="bf16",
+                                              dev=cuda, h0_std=0.05)
+    g = (g * 8.0).contiguous()
+    host[3] = f64(g)
+    o, hT = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    ro, rh = orc.chunk_exact(*host[:5], host[5], 64)
+    assert_close(f64(o), ro, "bf16", "o")
+    assert_close(f64(hT), rh, "bf16", "state")
