@@ -1,10 +1,17 @@
 // Chunked gated delta-rule forward on 5th-generation tensor cores, sm_100a.
 //
 // Replaces chunk_gated_delta_rule_fwd (ops.py:299-346) for bf16 inputs with
-// dk = 128, dv a multiple of 64 (exact semantics, in chunks of 64 whatever the
-// requested chunk length).  Every matrix product is a tcgen05.mma (bf16
-// operands in shared memory, fp32 accumulators in tensor memory) fed by TMA
-// tile loads; the state stays on chip for the whole sequence.
+// dk = 128 or 256, dv a multiple of 64 (exact semantics, in chunks of 64
+// whatever the requested chunk length).  Every matrix product is a tcgen05.mma
+// (bf16 operands in shared memory, fp32 accumulators in tensor memory) fed by
+// TMA tile loads; the state stays on chip for the whole sequence.
+//
+// dk = 256 (the head_dim of the reference's default configuration) uses the
+// same roles and products with twice the key steps: one K/Q stage of 64 KB
+// instead of two (so the next chunk's tiles load only once this one's are
+// released), the state increment K^T V'' as two M = 128 products (TMEM
+// columns 320 and 448), and two state rows (r, r + 128) per chain thread.
+// Only the unpaired form exists for it.
 //
 // One CTA owns one (b, h) and a tile of 64 state columns, and walks the
 // chunks in order.  Per chunk n (C = 64 tokens, in-chunk cumulative gate G):

@@ -136,7 +136,7 @@ cudaError_t launch_recurrent_bulk_layer(const RecurrentArgs& a, const LayerArgs&
 int device_error_recurrent_bulk(bool clear);
 int device_error_chunk_tc(bool clear);
 
-// Tensor-core chunk kernel: bf16, dk = 128, dv % 64 == 0, chunk = 64, exact.
+// Tensor-core chunk kernel: bf16, dk = 128 or 256, dv % 64 == 0, chunk = 64, exact.
 bool chunk_tc_supported(const ChunkArgs& a);
 cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
 // Its layer form (dv = 128, the two column tiles as one CTA pair): the gates
