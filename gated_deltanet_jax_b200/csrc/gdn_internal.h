@@ -139,7 +139,8 @@ int device_error_chunk_tc(bool clear);
 // Tensor-core chunk kernel: bf16, dk = 128 or 256, dv % 64 == 0, chunk = 64, exact.
 bool chunk_tc_supported(const ChunkArgs& a);
 cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
-// Its layer form (dv = 128, the two column tiles as one CTA pair): the gates
+// Its layer form (dk = dv = 128, the two column tiles as one cluster of two
+// CTAs): the gates
 // from the raw projections (a.g / a.beta unused) and the gated RMSNorm of
 // every output row, written to a.o.
 cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st);
