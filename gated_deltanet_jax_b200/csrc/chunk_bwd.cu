@@ -517,6 +517,11 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
 // ---------------------------------------------------------------------------
 // Warp tiles of the DKP x VT state product.
 template <int DKP> struct StateTiles;
+template <> struct StateTiles<256> {
+  static constexpr int MT = 4, NTL = 2;
+  static __device__ int m0(int w) { return (w >> 1) * 64; }
+  static __device__ int n0(int w) { return (w & 1) * 16; }
+};
 template <> struct StateTiles<128> {
   static constexpr int MT = 2, NTL = 2;
   static __device__ int m0(int w) { return (w >> 1) * 32; }
@@ -540,8 +545,10 @@ constexpr int states_smem_floats() {
   return DKP * SS + C * (DKP + 4) + C * (DKP + 8) + 2 * C * LB + 5 * C;
 }
 
+// (DKP = 256: 197 KB of shared memory, one CTA per SM, and the registers for
+// its 256-column prefetch tiles)
 template <typename Tin, int DKP>
-__global__ void __launch_bounds__(NT, 2) bwd_states_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(NT, DKP == 256 ? 1 : 2) bwd_states_kernel(const BwdParams p) {
   using ST = StateTiles<DKP>;
   constexpr bool kSplit = sizeof(Tin) == 4;
   constexpr int LW = DKP + 4, LK = DKP + 8;
@@ -1019,7 +1026,7 @@ struct WsLayout {
   size_t W, Z, UV, YX, hs, dhs, dqk, coff, total;
 };
 
-int padded_dk(int dk) { return dk <= 32 ? 32 : dk <= 64 ? 64 : 128; }
+int padded_dk(int dk) { return dk <= 32 ? 32 : dk <= 64 ? 64 : dk <= 128 ? 128 : 256; }
 
 // NC chunks per head, tokens in all, n_seqs chunk offsets (0: dense).
 WsLayout ws_layout(size_t NC, size_t tokens, int H, int dk, int dv, int n_seqs) {
@@ -1088,7 +1095,8 @@ cudaError_t launch_bwd_dtype(const ChunkBwdArgs& a, cudaStream_t st) {
   switch (padded_dk(a.dk)) {
     case 32: return launch_bwd_t<Tin, 32>(a, st);
     case 64: return launch_bwd_t<Tin, 64>(a, st);
-    default: return launch_bwd_t<Tin, 128>(a, st);
+    case 128: return launch_bwd_t<Tin, 128>(a, st);
+    default: return launch_bwd_t<Tin, 256>(a, st);
   }
 }
 
@@ -1109,7 +1117,7 @@ size_t chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv
 }
 
 bool chunk_bwd_supported(const ChunkBwdArgs& a) {
-  return a.dk >= 1 && a.dk <= 128 && a.dv >= VT && a.dv % VT == 0 &&
+  return a.dk >= 1 && a.dk <= 256 && a.dv >= VT && a.dv % VT == 0 &&
          (long long)a.B * a.H <= 65535;
 }
 

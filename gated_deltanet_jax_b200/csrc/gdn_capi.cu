@@ -266,7 +266,7 @@ int chunk_bwd(const void* q, const void* k, const void* v, const float* g, const
                       B, T, H, Hk, dk, dv, dtype, workspace, ws_bytes};
   a.cu_seqlens = cu_seqlens;
   if (!gdn::chunk_bwd_supported(a))
-    return fail(GDN_ERR_UNSUPPORTED, "backward supports dk <= 128, dv a multiple of 32 and "
+    return fail(GDN_ERR_UNSUPPORTED, "backward supports dk <= 256, dv a multiple of 32 and "
                 "sequences x heads <= 65535 (dk=%d dv=%d)", dk, dv);
   const size_t need = cu_seqlens ? gdn_chunk_bwd_varlen_workspace_bytes(B, T, H, dk, dv)
                                  : gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv);

@@ -181,7 +181,7 @@ int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v,
  * autodiff; this is the backward of gdn_chunk_fwd_gva / gdn_recurrent_fwd_gva
  * (ops.py:170-184 with a state carry).  Layouts as the forward's: dq, dk
  * [B,T,Hk,dk] and dv [B,T,H,dv] in the input dtype, dg, dbeta [B,T,H] and dh0
- * [B,H,dk,dv] fp32 (dh0 NULL: not wanted).  Needs dk <= 128 and dv a multiple
+ * [B,H,dk,dv] fp32 (dh0 NULL: not wanted).  Needs dk <= 256 and dv a multiple
  * of 32, and a device workspace of gdn_chunk_bwd_workspace_bytes() (fp32
  * per-chunk intermediates: the state entering and the state gradient leaving
  * every chunk, and four [T, dk | dv] products per head).  Deterministic: the

@@ -42,7 +42,8 @@ def _check(got, ref, dtype, with_h0=True):
 @pytest.mark.parametrize("B,T,H,dk,dv", [(2, 1, 2, 16, 32), (1, 31, 2, 64, 32), (2, 32, 1, 32, 64),
                                          (1, 33, 2, 128, 64), (2, 100, 3, 64, 96),
                                          (1, 200, 2, 128, 128), (1, 128, 2, 128, 256),
-                                         (1, 65, 1, 16, 512)])
+                                         (1, 65, 1, 16, 512), (1, 130, 2, 256, 64),
+                                         (1, 70, 1, 256, 512)])
 def test_backward_against_oracle(cuda, dtype, B, T, H, dk, dv):
     got, ref = _grads(dtype, B, T, H, dk, dv, seed=T + dk, dev=cuda)
     _check(got, ref, dtype)
@@ -147,6 +148,7 @@ PACKED = [
     ([300, 77], 4, 2, 128, 64, "bf16"),
     ([33, 0, 70, 16], 2, 1, 32, 64, "fp32"),
     ([5, 129, 40], 3, 3, 64, 32, "fp32"),
+    ([100, 0, 70], 2, 1, 256, 64, "bf16"),
 ]
 
 

@@ -131,9 +131,9 @@ def test_backward_rejects_bad_arguments(lib):
     """Checked on the host before any CUDA call."""
     p = ctypes.c_void_p(16)
     big = 1 << 30
-    assert lib.gdn_chunk_bwd(*_bwd_args(p, dk=256, ws=p, ws_bytes=big)) == _lib.GDN_ERR_UNSUPPORTED
-    assert b"dk <= 128" in lib.gdn_last_error()
     assert lib.gdn_chunk_bwd(*_bwd_args(p, dv=48, ws=p, ws_bytes=big)) == _lib.GDN_ERR_UNSUPPORTED
+    assert b"dk <= 256" in lib.gdn_last_error()
+    assert lib.gdn_chunk_bwd(*_bwd_args(p, dk=512, ws=p, ws_bytes=big)) == _lib.GDN_ERR_UNSUPPORTED
     assert lib.gdn_chunk_bwd(*_bwd_args(p, Hk=3)) == _lib.GDN_ERR_INVALID          # H % Hk
     assert lib.gdn_chunk_bwd(*_bwd_args(p)) == _lib.GDN_ERR_INVALID                # no workspace
     assert b"workspace" in lib.gdn_last_error()
