@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_bwd_varlen",
     "gdn_chunk_bwd_varlen_workspace_bytes",
     "gdn_chunk_workspace_bytes",
+    "gdn_chunk_varlen_workspace_bytes",
     "gdn_last_error",
     "gdn_device_error",
     "gdn_abi_version",
@@ -96,6 +97,8 @@ def _declare(lib):
     lib.gdn_chunk_bwd_varlen_workspace_bytes.restype = _sz
     lib.gdn_chunk_workspace_bytes.argtypes = [_i] * 8
     lib.gdn_chunk_workspace_bytes.restype = _sz
+    lib.gdn_chunk_varlen_workspace_bytes.argtypes = [_i] * 8
+    lib.gdn_chunk_varlen_workspace_bytes.restype = _sz
     lib.gdn_last_error.argtypes = []
     lib.gdn_last_error.restype = ctypes.c_char_p
     lib.gdn_device_error.argtypes = [_i]

@@ -81,6 +81,9 @@ struct BwdParams {
   const int* coff;
   int n_seqs;
   int B, T, H, Hk, dk, dv, N, ldw;
+  // The forward on these kernels (dO == NULL): the final state (or NULL) and o.
+  float* hTout = nullptr;
+  void* o = nullptr;
 };
 
 // Tokens and chunks of sequence s.
@@ -461,43 +464,44 @@ __global__ void __launch_bounds__(NT, 2) bwd_prep_kernel(const BwdParams p) {
       t2.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, c0 + KT);
     } else {   // first tiles of U, Y
       t1.fetch(v, bT, t0, Tn, p.H, h, p.dv, 0);
-      t2.fetch(dO, bT, t0, Tn, p.H, h, p.dv, 0);
+      if (dO) t2.fetch(dO, bT, t0, Tn, p.H, h, p.dv, 0);
     }
     float aw[1][2][4], az[1][2][4];
     zero(aw); zero(az);
     warp_mma<1, 2, false, false, kSplit>(aw, sT, LC, s1, LB, mw, nw, C);
-    warp_mma<1, 2, true, false, kSplit>(az, sT, LC, s2, LB, mw, nw, C);
+    if (dO) warp_mma<1, 2, true, false, kSplit>(az, sT, LC, s2, LB, mw, nw, C);
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         const size_t off = (row0 + f.row(mw, 0, e)) * p.ldw + c0 + f.col(nw, j, e);
         store2(p.W + off, aw[0][j][e], aw[0][j][e + 1]);
-        store2(p.Z + off, az[0][j][e], az[0][j][e + 1]);
+        if (dO) store2(p.Z + off, az[0][j][e], az[0][j][e + 1]);
       }
   }
-  // U = T (beta V), Y = T^T (P^T dO) per dv tile
+  // U = T (beta V), Y = T^T (P^T dO) per dv tile (the forward: U only)
   for (int c0 = 0; c0 < p.dv; c0 += VT) {
     __syncthreads();
     t1.put<LB>(s1, sb);
-    t2.put<LB>(s2, nullptr);
+    if (dO) t2.put<LB>(s2, nullptr);
     __syncthreads();
     if (c0 + VT < p.dv) {
       t1.fetch(v, bT, t0, Tn, p.H, h, p.dv, c0 + VT);
-      t2.fetch(dO, bT, t0, Tn, p.H, h, p.dv, c0 + VT);
+      if (dO) t2.fetch(dO, bT, t0, Tn, p.H, h, p.dv, c0 + VT);
     }
     float au[1][2][4], ap[1][2][4];
     zero(au); zero(ap);
     warp_mma<1, 2, false, false, kSplit>(au, sT, LC, s1, LB, mw, nw, C);
-    warp_mma<1, 2, true, false, kSplit>(ap, sP, LC, s2, LB, mw, nw, C);
+    if (dO) warp_mma<1, 2, true, false, kSplit>(ap, sP, LC, s2, LB, mw, nw, C);
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         const int m = f.row(mw, 0, e), c = f.col(nw, j, e);
         store2(p.UV + (row0 + m) * p.dv + c0 + c, au[0][j][e], au[0][j][e + 1]);
-        store2(s3 + m * LB + c, ap[0][j][e], ap[0][j][e + 1]);
+        if (dO) store2(s3 + m * LB + c, ap[0][j][e], ap[0][j][e + 1]);
       }
+    if (!dO) continue;
     __syncthreads();
     float ay[1][2][4];
     zero(ay);
@@ -665,6 +669,112 @@ __global__ void __launch_bounds__(NT, DKP == 256 ? 1 : 2) bwd_states_kernel(cons
       const int r = e / VT, c = e - r * VT;
       if (r < p.dk) p.dh0[((size_t)bh * p.dk + r) * p.dv + c0 + c] = sS[r * SS + c];
     }
+  }
+  if (!rev && p.hTout) {   // the forward on these kernels: the final state
+    __syncthreads();
+    for (int e = tid; e < DKP * VT; e += NT) {
+      const int r = e / VT, c = e - r * VT;
+      if (r < p.dk) p.hTout[((size_t)bh * p.dk + r) * p.dv + c0 + c] = sS[r * SS + c];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The forward on these kernels, for the shapes the tcgen05 kernel does not take
+// (fp32 inputs; bf16 with dk < 128 or dv not a multiple of 64): bwd_prep
+// without dO (T, W, U), the forward state pass (V' = U - W h and every chunk's
+// entering state h, the final state), then per chunk
+//   O = e^G (Q h) + P V',   P = tril_0(Q K^T e^{G_i - G_j})
+// on the same warp-level products (three-term tf32 for fp32 inputs).
+// ---------------------------------------------------------------------------
+template <int DKP>
+constexpr int out_smem_floats() {
+  return C * (DKP + 4) + C * LT + C * LC + KT * LB + C * LB + 5 * C;
+}
+
+template <typename Tin, int DKP>
+__global__ void __launch_bounds__(NT, 2) fwd_out_kernel(const BwdParams p) {
+  constexpr bool kSplit = sizeof(Tin) == 4;
+  constexpr int LQ = DKP + 4;
+  extern __shared__ float sm[];
+  float* sQ = sm;                 // C x LQ   Q, every key column (zero past dk)
+  float* sK = sQ + C * LQ;        // C x LT   one 32-column tile of K
+  float* sP = sK + C * LT;        // C x LC   P
+  float* sH = sP + C * LC;        // KT x LB  32 x 32 tile of the entering state
+  float* sV = sH + KT * LB;       // C x LB   32-column tile of V'
+  float* sG = sV + C * LB;
+  float* se = sG + C; float* sd = se + C; float* sb = sd + C; float* sbe = sb + C;
+  const Tin* q = static_cast<const Tin*>(p.q);
+  const Tin* k = static_cast<const Tin*>(p.k);
+  Tin* o = static_cast<Tin*>(p.o);
+  const int gc = blockIdx.x, h = blockIdx.y, sq = seq_of_chunk(p, gc);
+  if (sq < 0) return;
+  const SeqSpan sp = seq_span(p, sq);
+  const int n = gc - sp.cfirst, Tn = sp.len;
+  const int hq = h * p.Hk / p.H, t0 = n * C, tid = threadIdx.x, w = tid >> 5;
+  const size_t bT = sp.tok0;
+  const size_t row0 = ((size_t)gc * p.H + h) * C;
+  const Frag f;
+  chunk_gates(p, bT, Tn, h, t0, sG, se, sd, sb, sbe);
+  {
+    TokenTile<DKP, Tin> tQ;
+    tQ.fetch(q, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+    tQ.put<LQ>(sQ, nullptr);
+  }
+  // P = tril_0(Q K^T e^{G_i - G_j}); warp: rows mq.., columns nq..
+  const int mq = (w >> 1) * 16, nq = (w & 1) * 32;
+  float aQK[1][4][4];
+  zero(aQK);
+  TokenTile<KT, Tin> tK;
+  tK.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, 0);
+  for (int c0 = 0; c0 < p.dk; c0 += KT) {
+    __syncthreads();
+    tK.put<LT>(sK, nullptr);
+    __syncthreads();
+    if (c0 + KT < p.dk) tK.fetch(k, bT, t0, Tn, p.Hk, hq, p.dk, c0 + KT);
+    warp_mma<1, 4, false, true, kSplit>(aQK, sQ + c0, LQ, sK, LT, mq, nq, KT);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int m = f.row(mq, 0, e), c = f.col(nq, j, e);
+      sP[m * LC + c] = c <= m ? aQK[0][j][e] * gate_exp(sG[m] - sG[c]) : 0.f;
+    }
+  // O, 32 columns at a time: e^G (Q h) over 32-row tiles of h, then + P V'
+  const int mv = (w >> 1) * 16, nv = (w & 1) * 16;
+  const float* hs = p.hs + ((size_t)gc * p.H + h) * p.dk * p.dv;
+  for (int c0 = 0; c0 < p.dv; c0 += VT) {
+    BlockTile<VT> tU;
+    tU.fetch(p.UV + row0 * p.dv, p.dv, c0);
+    float acc[1][2][4];
+    zero(acc);
+    for (int kt = 0; kt < p.dk; kt += KT) {
+      __syncthreads();   // the previous tiles' readers are done (first pass: P is written)
+      for (int e = tid * 4; e < KT * VT; e += NT * 4) {
+        const int r = e / VT, c = e - r * VT;
+        *reinterpret_cast<float4*>(sH + r * LB + c) =
+            kt + r < p.dk ? *reinterpret_cast<const float4*>(hs + (size_t)(kt + r) * p.dv + c0 + c)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      __syncthreads();
+      warp_mma<1, 2, false, false, kSplit>(acc, sQ + kt, LQ, sH, LB, mv, nv, KT);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[0][j][e] *= se[f.row(mv, 0, e)];
+    tU.put<LB>(sV);
+    __syncthreads();
+    warp_mma<1, 2, false, false, kSplit>(acc, sP, LC, sV, LB, mv, nv, C);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int m = f.row(mv, 0, e), c = f.col(nv, j, e);
+        if (t0 + m < Tn)
+          store2(o + ((bT + t0 + m) * p.H + h) * p.dv + c0 + c, acc[0][j][e], acc[0][j][e + 1]);
+      }
   }
 }
 
@@ -1100,6 +1210,65 @@ cudaError_t launch_bwd_dtype(const ChunkBwdArgs& a, cudaStream_t st) {
   }
 }
 
+// Workspace of the forward on these kernels: W, U -> V', the entering states
+// (and, packed sequences, the chunk offsets).  n_seqs == 0: B dense rows.
+struct FwdWs {
+  size_t W, UV, hs, coff, total;
+};
+
+FwdWs fwd_ws_layout(int B, int T, int H, int dk, int dv, int n_seqs) {
+  const size_t NC = n_seqs ? (size_t)(T / C) + (size_t)n_seqs
+                           : (size_t)B * (size_t)((T + C - 1) / C);
+  FwdWs L{};
+  size_t o = 0;
+  auto take = [&](size_t n) { const size_t r = o; o += (n + 63) & ~size_t(63); return r; };
+  L.W = take(NC * H * C * (size_t)padded_dk(dk));
+  L.UV = take(NC * H * C * dv);
+  L.hs = take(NC * H * (size_t)dk * dv);
+  L.coff = take(n_seqs ? (size_t)n_seqs + 1 : 0);
+  L.total = o;
+  return L;
+}
+
+template <typename Tin, int DKP>
+cudaError_t launch_fwd_t(const ChunkArgs& a, cudaStream_t st) {
+  const bool packed = a.cu_seqlens != nullptr;   // B = n_seqs sequences in one row of T tokens
+  const FwdWs L = fwd_ws_layout(a.B, a.T, a.H, a.dk, a.dv, packed ? a.B : 0);
+  float* ws = static_cast<float*>(a.workspace);
+  int* coff = packed ? reinterpret_cast<int*>(ws + L.coff) : nullptr;
+  BwdParams p{a.q, a.k, a.v, nullptr, a.g, a.beta, a.h0, nullptr, nullptr, nullptr, nullptr,
+              nullptr, nullptr, nullptr, ws + L.W, nullptr, ws + L.UV, nullptr, ws + L.hs,
+              nullptr, nullptr, a.cu_seqlens, coff, packed ? a.B : 0, packed ? 1 : a.B, a.T,
+              a.H, a.Hk, a.dk, a.dv, packed ? 0 : (a.T + C - 1) / C, DKP};
+  p.hTout = a.hT;
+  p.o = a.o;
+  const int NC = packed ? a.T / C + a.B : a.B * ((a.T + C - 1) / C);
+  static std::atomic<int> set_prep[kMaxDevices] = {}, set_states[kMaxDevices] = {},
+                          set_out[kMaxDevices] = {};
+  const int prep_bytes = kPrepSmemFloats * (int)sizeof(float);
+  const int states_bytes = states_smem_floats<DKP>() * (int)sizeof(float);
+  const int out_bytes = out_smem_floats<DKP>() * (int)sizeof(float);
+  cudaError_t e = ensure_smem(bwd_prep_kernel<Tin>, prep_bytes, set_prep);
+  if (e == cudaSuccess) e = ensure_smem(bwd_states_kernel<Tin, DKP>, states_bytes, set_states);
+  if (e == cudaSuccess) e = ensure_smem(fwd_out_kernel<Tin, DKP>, out_bytes, set_out);
+  if (e != cudaSuccess) return e;
+  if (packed) bwd_chunk_offsets_kernel<<<1, 1024, 0, st>>>(a.cu_seqlens, a.B, a.T, NC, coff);
+  bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);
+  bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 1), NT, states_bytes, st>>>(p);
+  fwd_out_kernel<Tin, DKP><<<dim3(NC, a.H), NT, out_bytes, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename Tin>
+cudaError_t launch_fwd_dtype(const ChunkArgs& a, cudaStream_t st) {
+  switch (padded_dk(a.dk)) {
+    case 32: return launch_fwd_t<Tin, 32>(a, st);
+    case 64: return launch_fwd_t<Tin, 64>(a, st);
+    case 128: return launch_fwd_t<Tin, 128>(a, st);
+    default: return launch_fwd_t<Tin, 256>(a, st);
+  }
+}
+
 }  // namespace
 
 size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
@@ -1125,6 +1294,22 @@ cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;   // (the caller handles dh0)
   return a.dtype == kBF16 ? launch_bwd_dtype<__nv_bfloat16>(a, st)
                           : launch_bwd_dtype<float>(a, st);
+}
+
+bool chunk_fwd_warp_supported(const ChunkArgs& a) {
+  return a.semantics == kExact && (a.dtype == kFP32 || a.dtype == kBF16) && a.dk >= 16 &&
+         a.dk <= 256 && a.dk % 16 == 0 && a.dv >= VT && a.dv % VT == 0 &&
+         (long long)a.B * a.H <= 65535;
+}
+
+size_t chunk_fwd_warp_workspace_bytes(int B, int T, int H, int dk, int dv, int n_seqs) {
+  return sizeof(float) * fwd_ws_layout(B, T, H, dk, dv, n_seqs).total;
+}
+
+cudaError_t launch_chunk_fwd_warp(const ChunkArgs& a, cudaStream_t st) {
+  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  return a.dtype == kBF16 ? launch_fwd_dtype<__nv_bfloat16>(a, st)
+                          : launch_fwd_dtype<float>(a, st);
 }
 
 }  // namespace gdn

@@ -95,6 +95,20 @@ int chunk_bwd(const void* q, const void* k, const void* v, const float* g, const
               int T, int H, int Hk, int dk, int dv, int dtype, void* workspace, size_t ws_bytes,
               void* stream, const char* what);
 
+// Workspace of a chunked forward (n_seqs: packed sequences, B == n_seqs; 0: dense).
+size_t chunk_workspace(int B, int T, int H, int dk, int dv, int chunk, int dtype, int semantics,
+                       int n_seqs) {
+  (void)chunk;   // exact semantics do not depend on the chunk length
+  if (B <= 0 || T <= 0 || H <= 0) return 0;
+  gdn::ChunkArgs a{};
+  a.B = B; a.T = T; a.H = H; a.Hk = H; a.dk = dk; a.dv = dv; a.chunk = 64; a.dtype = dtype;
+  a.semantics = semantics;
+  const bool tc_shape = dtype == GDN_DTYPE_BF16 && semantics == GDN_SEMANTICS_EXACT &&
+                        (dk == 128 || dk == 256) && dv % 64 == 0;
+  if (tc_shape || !dk_supported(dk) || !gdn::chunk_fwd_warp_supported(a)) return 0;
+  return gdn::chunk_fwd_warp_workspace_bytes(B, T, H, dk, dv, n_seqs);
+}
+
 // The chunked layer form, dense (cu_seqlens NULL: B rows of T tokens) or packed
 // (B = n_seqs sequences in one row of T tokens).
 int chunk_fwd_layer(const void* q, const void* k, const void* v, const float* a,
@@ -199,10 +213,17 @@ int gdn_chunk_fwd_layer_varlen(const void* q, const void* k, const void* v, cons
                          cu_seqlens, n_seqs, T, H, Hk, dk, dv, dtype, stream);
 }
 
+// Non-zero for the calls that run on the warp-level tensor-core kernels (exact
+// semantics; fp32 inputs, or bf16 shapes outside the tcgen05 kernel's): their
+// per-chunk W, U -> V' and entering states.
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk, int dtype,
                                  int semantics) {
-  (void)B; (void)T; (void)H; (void)dk; (void)dv; (void)chunk; (void)dtype; (void)semantics;
-  return 0;
+  return chunk_workspace(B, T, H, dk, dv, chunk, dtype, semantics, 0);
+}
+
+size_t gdn_chunk_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv, int chunk,
+                                        int dtype, int semantics) {
+  return chunk_workspace(n_seqs, T, H, dk, dv, chunk, dtype, semantics, n_seqs);
 }
 
 int gdn_chunk_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta,
@@ -302,9 +323,11 @@ int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const
     return fail(GDN_ERR_UNSUPPORTED, "chunk=%d not supported (16, 32 or 64)", chunk);
   if (semantics != GDN_SEMANTICS_EXACT && semantics != GDN_SEMANTICS_REFERENCE)
     return fail(GDN_ERR_INVALID, "semantics %d unknown", semantics);
-  const size_t need = gdn_chunk_workspace_bytes(B, T, H, dk, dv, chunk, dtype, semantics);
+  const size_t need =
+      chunk_workspace(B, T, H, dk, dv, chunk, dtype, semantics, cu_seqlens ? B : 0);
   if (ws_bytes < need || (need && !workspace))
     return fail(GDN_ERR_INVALID, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  if (need && !aligned16(workspace)) return fail(GDN_ERR_INVALID, "workspace is not 16-byte aligned");
   if (T == 0 && (B * H) > 0 && hT && h0 != hT) {
     cudaError_t e = h0 ? cudaMemcpyAsync(hT, h0, sizeof(float) * (size_t)B * H * dk * dv,
                                          cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
@@ -319,6 +342,8 @@ int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const
   const bool simt_only = force && strcmp(force, "simt") == 0;
   if (!simt_only && gdn::chunk_tc_supported(a))
     return cuda_status(gdn::launch_chunk_tc(a, (cudaStream_t)stream), "gdn_chunk_fwd");
+  if (!simt_only && need > 0)
+    return cuda_status(gdn::launch_chunk_fwd_warp(a, (cudaStream_t)stream), "gdn_chunk_fwd");
   if (gdn::chunk_simt_smem_bytes(a) == 0)
     return fail(GDN_ERR_UNSUPPORTED, "no chunk kernel fits dk=%d dv=%d chunk=%d", dk, dv, chunk);
   return cuda_status(gdn::launch_chunk_simt(a, (cudaStream_t)stream), "gdn_chunk_fwd");
@@ -399,6 +424,6 @@ int gdn_device_error(int clear) {
   return a ? a : b;
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 6; }
+int gdn_abi_version(void) { return (1 << 16) | 7; }
 
 }  // extern "C"

@@ -145,6 +145,14 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
 // every output row, written to a.o.
 cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st);
 
+// The chunked forward on the backward's warp-level tensor-core kernels (exact
+// semantics, dk in 16..256, dv % 32 == 0, dense or packed): fp32 inputs, and
+// the bf16 shapes the tcgen05 kernel does not take.  Needs a device workspace
+// of chunk_fwd_warp_workspace_bytes() (n_seqs: packed sequences, 0: dense).
+bool chunk_fwd_warp_supported(const ChunkArgs& a);
+size_t chunk_fwd_warp_workspace_bytes(int B, int T, int H, int dk, int dv, int n_seqs);
+cudaError_t launch_chunk_fwd_warp(const ChunkArgs& a, cudaStream_t st);
+
 // Portable CUDA-core chunk kernel (any supported shape, fp32 or bf16 inputs).
 cudaError_t launch_chunk_simt(const ChunkArgs& a, cudaStream_t st);
 // Shared-memory bytes launch_chunk_simt needs for this shape (0 = unsupported).

@@ -242,7 +242,12 @@ def _chunk_impl(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
     dtype = _DTYPES[q.dtype]
     sem = _SEMANTICS[semantics]
     with torch.cuda.device(q.device):
-        ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, dk, dv, int(chunk_size), dtype, sem)
+        if n_seqs is not None:
+            ws_bytes = lib.gdn_chunk_varlen_workspace_bytes(n_seqs, T, H, dk, dv,
+                                                            int(chunk_size), dtype, sem)
+        else:
+            ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, dk, dv, int(chunk_size), dtype,
+                                                     sem)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
         stream = torch.cuda.current_stream(q.device).cuda_stream
         if n_seqs is not None:

@@ -68,7 +68,9 @@ int gdn_recurrent_fwd(const void* q, const void* k, const void* v,
  * (to rounding).  `chunk` is the chunk length C (16, 32 or 64).  h0 == NULL
  * starts from zeros (ops.py:318-319); hT == NULL skips the final state
  * (output_final_state=False, ops.py:344-346).  `workspace` / `ws_bytes` may be
- * NULL / 0 when gdn_chunk_workspace_bytes() returns 0.
+ * NULL / 0 when gdn_chunk_workspace_bytes() returns 0; it is non-zero where the
+ * call runs on the warp-level tensor-core kernels (exact semantics with fp32
+ * inputs, or bf16 shapes other than dk = 128 / 256 with dv % 64 == 0).
  */
 int gdn_chunk_fwd(const void* q, const void* k, const void* v,
                   const float* g, const float* beta,
@@ -163,8 +165,9 @@ int gdn_chunk_fwd_layer_varlen(const void* q, const void* k, const void* v,
  * [cu_seqlens[s], cu_seqlens[s + 1]) (cu_seqlens: device int32[n_seqs + 1],
  * non-decreasing from 0 to T; offsets are clamped to [0, T]).  h0 / hT are
  * [n_seqs, H, dk, dv].  Each sequence gets exactly what gdn_chunk_fwd_gva
- * gives it on its own.  No counterpart in the reference, whose ops take one
- * dense [B, T] batch; exact semantics only.
+ * gives it on its own.  The workspace is gdn_chunk_varlen_workspace_bytes().
+ * No counterpart in the reference, whose ops take one dense [B, T] batch;
+ * exact semantics only.
  */
 int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v,
                          const float* g, const float* beta,
@@ -257,6 +260,11 @@ int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v,
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
                                  int dtype, int semantics);
 
+/* Device scratch bytes gdn_chunk_fwd_varlen needs for n_seqs packed sequences
+ * in one row of T tokens (0 = none).  No counterpart in the reference. */
+size_t gdn_chunk_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv, int chunk,
+                                        int dtype, int semantics);
+
 /*
  * Device-side error word of the current device (0 = none; 1 = a bounded wait
  * inside a kernel gave up, so that launch's results are invalid).  Kernels
@@ -273,7 +281,8 @@ const char* gdn_last_error(void);
 /* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward;
  * 1.4: backward of packed sequences, the allocation-free backward;
  * 1.5: the layer form of the decode step; 1.6: the layer form of the chunked
- * forward). */
+ * forward; 1.7: dk = 256 on the tensor cores, the chunked forward's workspace
+ * for fp32 inputs, gdn_chunk_varlen_workspace_bytes). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

@@ -255,3 +255,30 @@ def test_tensor_core_dk256_steep_gates(cuda):
     ro, rh = orc.chunk_exact(*host[:5], host[5], 64)
     assert_close(f64(o), ro, "bf16", "o")
     assert_close(f64(hT), rh, "bf16", "state")
+
+
+@pytest.mark.parametrize("dtype,B,T,H,dk,dv", [
+    ("fp32", 2, 200, 3, 128, 128), ("fp32", 1, 130, 2, 256, 512), ("fp32", 3, 65, 2, 16, 32),
+    ("fp32", 1, 1, 2, 64, 96), ("bf16", 2, 150, 2, 64, 64), ("bf16", 1, 100, 3, 128, 96),
+])
+def test_warp_tensor_core_forward_matches_cuda_core_kernel(cuda, dtype, B, T, H, dk, dv):
+    """fp32 inputs (and bf16 shapes outside the tcgen05 kernel) run on the
+    warp-level tensor-core kernels with a workspace; the CUDA-core kernel is
+    the cross-check, within the fp32 / bf16 bars."""
+    (q, k, v, g, b, h0), host = device_inputs(B, T, H, dk, dv, seed=T + dk, dtype=dtype,
+                                              dev=cuda, h0_std=0.05)
+    from gated_deltanet_jax_b200 import _lib
+    assert _lib.load().gdn_chunk_workspace_bytes(B, T, H, dk, dv, 64,
+                                                 ops._DTYPES[q.dtype], 0) > 0
+
+    def run():
+        return ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                          output_final_state=True)
+
+    o_w, h_w = run()
+    o_c, h_c = _with_kernel("simt", run)
+    assert_close(f64(o_w), f64(o_c), dtype, "o")
+    assert_close(f64(h_w), f64(h_c), dtype, "state")
+    ro, rh = orc.chunk_exact(*host, chunk_size=64)
+    assert_close(f64(o_w), ro, dtype, "o vs oracle")
+    assert_close(f64(h_w), rh, dtype, "state vs oracle")
