@@ -633,6 +633,51 @@ def prefill_layer_leg(d, a):
                     "precomputed gates and no norm"}
 
 
+def model_core_leg(d, a):
+    """The delta-rule core of the reference's default model configuration
+    (head_dim 256, expand_v 2: dk=256, dv=512; 6 heads; B=8 T=2048 as the
+    full-model configuration quotes): the chunked forward in bf16 and in
+    fp32, and the bf16 backward, per layer call.  The full model (projections,
+    MLPs, 24 layers) is outside the operator path."""
+    import torch
+    from gated_deltanet_jax_b200 import ops
+    from gated_deltanet_jax_b200 import roofline as rl
+    B, T, H, dk, dv = 8, 2048, 6, 256, 512
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(97 + d.rank)
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1)
+    k = nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1)
+    v = torch.randn(B, T, H, dv, device=d.dev, generator=gen)
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, device=d.dev, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, T, H, device=d.dev, generator=gen))
+    qb, kb, vb = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    do = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
+    steps = max(1, min(a.steps, 10))
+    res = {}
+    for name, fn in (("fwd_bf16", lambda: ops.chunk_gated_delta_rule(qb, kb, vb, g, beta)),
+                     ("fwd_fp32", lambda: ops.chunk_gated_delta_rule(q, k, v, g, beta)),
+                     ("bwd_bf16", lambda: ops._chunk_backward(qb, kb, vb, g, beta, None, do,
+                                                              None))):
+        for _ in range(a.warmup):
+            fn()
+        ms, _ = _timed(d, fn, steps)
+        res[name] = ms
+    th = B * T * H
+    fl_f = th * rl.flops_chunk_per_token_head(dk, dv, 64)
+    fl_b = th * rl.flops_chunk_bwd_per_token_head(dk, dv, 64)
+    return {"workload": "delta-rule core of the reference's default configuration: B=8 T=2048 "
+                        "H=6 dk=256 dv=512 chunk=64, one layer call",
+            "fwd_bf16_ms": res["fwd_bf16"], "fwd_bf16_tflops": fl_f / res["fwd_bf16"] / 1e9,
+            "fwd_fp32_ms": res["fwd_fp32"], "fwd_fp32_tflops": fl_f / res["fwd_fp32"] / 1e9,
+            "bwd_bf16_ms": res["bwd_bf16"], "bwd_bf16_tflops": fl_b / res["bwd_bf16"] / 1e9,
+            "fwd_plus_bwd_bf16_tokens_per_s": d.world * B * T / ((res["fwd_bf16"]
+                                                                  + res["bwd_bf16"]) / 1e3),
+            "launches": steps * (1 + 3 + 3),
+            "path": "bf16 forward: tcgen05 kernel (dk=256 form); fp32 forward: warp-level "
+                    "tensor-core kernels (three-term tf32); backward: gdn_chunk_bwd"}
+
+
 def backward_leg(d, a, lib):
     """The chunked backward (gdn_chunk_bwd) on the prefill workload: gradients of
     q, k, v, g, beta from dO, every buffer resident, one C-ABI call per step."""
@@ -758,6 +803,7 @@ def main():
     bwd = None if a.no_backward else backward_leg(d, a, lib)
     lay = None if a.no_layer else decode_layer_leg(d, a)
     play = None if (a.no_layer or a.no_prefill) else prefill_layer_leg(d, a)
+    mcore = None if a.no_prefill else model_core_leg(d, a)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not a.no_cpu:
@@ -787,7 +833,8 @@ def main():
                          "algorithmic_bytes_per_launch": dec["bytes_launch"]},
             "gpu_launches": (dec["launches"] + (pre["launches"] if pre else 0)
                              + (bwd["launches"] if bwd else 0) + (lay["launches"] if lay else 0)
-                             + (play["launches"] if play else 0)),
+                             + (play["launches"] if play else 0)
+                             + (mcore["launches"] if mcore else 0)),
             "clocks": dec["clocks"],
         }
         if "e2e" in dec:
@@ -821,6 +868,8 @@ def main():
             line["decode_layer"] = lay
         if play:
             line["prefill_layer"] = play
+        if mcore:
+            line["model_config_core"] = mcore
         if bwd:
             if pre:
                 bwd["fwd_plus_bwd_tokens_per_s"] = (d.world * PRE["B"] * PRE["T"]
