@@ -896,7 +896,12 @@ def main():
                              "frac": tf / bf16, "peak_source": f"{peak_src} bf16_tflops (burst)",
                              "traffic": _profile_traffic("chunk_prefill_b4_t4096_h16_d128"),
                              "algorithmic_flops_per_launch": pre["flops_launch"],
-                             "hbm_achieved_gbs": pre["bytes_launch"] / pre["launch_s"] / 1e9},
+                             "hbm_achieved_gbs": pre["bytes_launch"] / pre["launch_s"] / 1e9,
+                             # min(peak, arithmetic intensity x HBM bandwidth): the attainable
+                             # FLOP/s at this kernel's FLOP per algorithmic byte
+                             "ai_flop_per_byte": pre["flops_launch"] / pre["bytes_launch"],
+                             "frac_of_attainable": tf / min(bf16, pre["flops_launch"]
+                                                            / pre["bytes_launch"] * hbm / 1e3)},
             }
             if "e2e" in pre:
                 pre_line["e2e"] = pre["e2e"]
