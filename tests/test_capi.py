@@ -216,7 +216,32 @@ def test_empty_problem_is_a_no_op(lib):
 
 
 def test_workspace_query(lib):
-    assert lib.gdn_chunk_workspace_bytes(4, 4096, 16, 128, 128, 64, 1, 0) >= 0
+    """Zero on the tcgen05 shapes (bf16, dk 128 / 256, dv % 64 == 0) and for the
+    reference semantics; non-zero where the call runs on the warp-level
+    tensor-core kernels (fp32 inputs, other bf16 shapes), growing with the work."""
+    bf16, fp32 = _lib.GDN_DTYPE_BF16, _lib.GDN_DTYPE_FP32
+    q = lib.gdn_chunk_workspace_bytes
+    assert q(4, 4096, 16, 128, 128, 64, bf16, 0) == 0
+    assert q(8, 2048, 6, 256, 512, 64, bf16, 0) == 0
+    assert q(2, 100, 2, 128, 128, 64, fp32, _lib.GDN_SEMANTICS_REFERENCE) == 0
+    assert q(2, 100, 2, 128, 48, 64, fp32, 0) == 0          # dv % 32 != 0: CUDA cores
+    small = q(1, 64, 1, 64, 64, 64, fp32, 0)
+    assert small > 0 and q(2, 64, 1, 64, 64, 64, fp32, 0) > small
+    assert q(1, 64, 1, 64, 64, 64, bf16, 0) == small        # same fp32 intermediates
+    assert q(1, 64, 1, 128, 96, 64, bf16, 0) > 0            # dv % 64 != 0
+    assert q(0, 64, 1, 64, 64, 64, fp32, 0) == 0 and q(1, 0, 1, 64, 64, 64, fp32, 0) == 0
+    # packed sequences: room for one partial chunk per sequence, and the offsets
+    v = lib.gdn_chunk_varlen_workspace_bytes
+    assert v(3, 64, 1, 64, 64, 64, fp32, 0) > q(1, 64, 1, 64, 64, 64, fp32, 0)
+    assert v(3, 64, 1, 128, 128, 64, bf16, 0) == 0
+
+
+def test_chunk_rejects_missing_workspace(lib):
+    """A call that needs a workspace and gets none is refused on the host."""
+    p = ctypes.c_void_p(16)
+    rc = lib.gdn_chunk_fwd(p, p, p, p, p, None, p, None, 1, 64, 1, 64, 64, 64,
+                           _lib.GDN_DTYPE_FP32, 0, None, 0, None)
+    assert rc == _lib.GDN_ERR_INVALID and b"workspace" in lib.gdn_last_error()
 
 
 def test_error_raises_with_message(lib):
