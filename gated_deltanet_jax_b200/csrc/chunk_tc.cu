@@ -40,14 +40,16 @@
 // accumulator belongs to thread r of a warpgroup.  All hand-offs are
 // mbarriers; every wait is bounded.
 //
-// Layer form (kLayer, dv = 128 as one CTA pair): the GatedDeltaNet layer's
-// work on either side of the op in the same kernel (model.py:136-139, :47-53).
-// The gate warp forms beta = sigmoid(b) and g = -exp(A_log[h]) softplus(a +
-// dt_bias[h]) from the raw projections; the output epilogue sums the squares
-// of its 64 columns of each row in fp32, exchanges the partial sum with the
-// other CTA of the pair (one st.async per row into the other CTA's shared
-// memory, completing on its barrier), and stores
-// y = o rsqrt(mean(o^2) + eps) w silu(gate) instead of o.
+// Layer form (kLayer, dk = dv = 128, the two column tiles of a row as one
+// cluster of two CTAs, with or without shared preparation): the GatedDeltaNet
+// layer's work on either side of the op in the same kernel (model.py:136-139,
+// :47-53).  The gate warp forms beta = sigmoid(b) and g = -exp(A_log[h])
+// softplus(a + dt_bias[h]) from the raw projections.  The output epilogue sums
+// the squares of its 64 fp32 columns of each row, stages the row as bf16 in
+// shared memory, releases TMEM, and sends the partial sum into the other CTA's
+// shared memory (one st.async per row, completing on its barrier).  The row is
+// finished at the start of the next chunk, when the other CTA's sum has
+// arrived: y = o rsqrt(mean(o^2) + eps) w silu(gate) replaces o.
 #include <cuda.h>
 #include <cstdlib>
 #include <cudaTypedefs.h>
