@@ -3,7 +3,8 @@ oracle would take too long: for fixed q, k, g, beta the delta rule is linear
 in (v, initial state), so o(v1 + 2 v2, h1 + 2 h2) = o(v1, h1) + 2 o(v2, h2),
 and so is the final state.  Checked on the tcgen05 chunk kernel (bf16,
 B=4 T=4096 H=16 dk=dv=128), the warp-level chunk path (fp32, same sizes) and
-the decode kernel (bf16, B=64 H=16 dk=dv=128, one token)."""
+the decode kernel (bf16, B=64 H=16 dk=dv=128, one token).  Also bit-exact
+determinism and state carry across a chunk-aligned split of a sequence."""
 
 import pytest
 import torch
@@ -56,3 +57,27 @@ def test_decode_linear_in_values_and_state_full_size(cuda):
     eo, es = _linearity(run, v, cuda, (B, H, D, D), q.dtype, 42)
     assert eo < 2e-2, eo
     assert es < 2e-2, es
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
+def test_chunk_forward_deterministic_and_state_carry_exact(cuda, dtype):
+    """Repeated calls give the same bits, and a sequence split at a chunk
+    boundary, with the fp32 state carried from the first call into the second,
+    gives the same bits as one call over the whole sequence."""
+    B, T, H, D = 2, 1024, 8, 128
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, D, D, seed=51, dtype=dtype, dev=cuda,
+                                           h0_std=0.02)
+
+    def run(sl, h):
+        return ops.chunk_gated_delta_rule(q[:, sl].contiguous(), k[:, sl].contiguous(),
+                                          v[:, sl].contiguous(), g[:, sl].contiguous(),
+                                          b[:, sl].contiguous(), initial_state=h,
+                                          output_final_state=True)
+
+    o, hT = run(slice(0, T), h0)
+    o2, hT2 = run(slice(0, T), h0)
+    assert torch.equal(o, o2) and torch.equal(hT, hT2)
+    oa, ha = run(slice(0, 384), h0)
+    ob, hb = run(slice(384, T), ha)
+    assert torch.equal(torch.cat([oa, ob], 1), o)
+    assert torch.equal(hb, hT)
