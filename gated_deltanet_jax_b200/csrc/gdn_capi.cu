@@ -80,6 +80,19 @@ int recurrent_fwd(const void* q, const void* k, const void* v, const float* g, c
                                          (cudaStream_t)stream);
     return cuda_status(e, "gdn_recurrent_fwd (T=0 state copy)");
   }
+  // Whole sequences (T >= 64) on the tcgen05 shapes run on the chunked kernel:
+  // the same recurrence (exact semantics) computed chunk by chunk on the
+  // tensor cores instead of token by token.  Each CTA reads its tile of h0
+  // before it writes the same tile of hT, so h0 == hT stays an in-place update.
+  // GDN_RECURRENT_KERNEL=token keeps the token loop (kernel cross-checks).
+  const char* force = getenv("GDN_RECURRENT_KERNEL");
+  const bool token_only = force && strcmp(force, "token") == 0;
+  if (!token_only && T >= 64) {
+    gdn::ChunkArgs ca{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, 64, dtype,
+                      GDN_SEMANTICS_EXACT, nullptr, 0, Hk};
+    if (gdn::chunk_tc_supported(ca))
+      return cuda_status(gdn::launch_chunk_tc(ca, (cudaStream_t)stream), "gdn_recurrent_fwd");
+  }
   gdn::RecurrentArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, dtype, Hk};
   return cuda_status(gdn::launch_recurrent(a, (cudaStream_t)stream), "gdn_recurrent_fwd");
 }

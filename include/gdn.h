@@ -50,7 +50,9 @@ extern "C" {
  *     o_t = S^T q_t
  * h0 == NULL starts from zeros (the reference's only mode, ops.py:168);
  * hT == NULL drops the final state (the reference returns None, ops.py:219).
- * h0 == hT updates the state in place (decode).
+ * h0 == hT updates the state in place (decode).  Whole sequences (T >= 64)
+ * with bf16 inputs, dk = 128 or 256 and dv % 64 == 0 are computed chunk by
+ * chunk on the tensor cores: the same recurrence, equal within bf16 rounding.
  */
 int gdn_recurrent_fwd(const void* q, const void* k, const void* v,
                       const float* g, const float* beta,

@@ -82,13 +82,21 @@ def test_split_resume_equals_one_shot(cuda):
 
 
 def test_chunk_equals_recurrent_kernel(cuda):
+    """The tcgen05 chunk kernel against the token-by-token recurrent kernel
+    (GDN_RECURRENT_KERNEL=token: whole sequences otherwise go to the chunk
+    kernel too)."""
     q, k, v, g, b, h0 = device_inputs_fast(2, 1000, 4, 128, 128, seed=4, dtype="bf16", dev=cuda,
                                            h0_std=0.02)
     oc, hc = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
-    orr, hr = ops.fused_recurrent_gated_delta_rule(q, k, v, g, b, initial_state=h0,
-                                                   output_final_state=True)
+    orr, hr = _with_env("GDN_RECURRENT_KERNEL", "token", lambda: ops.fused_recurrent_gated_delta_rule(
+        q, k, v, g, b, initial_state=h0, output_final_state=True))
     assert_close(f64(oc), f64(orr), "bf16", "o")
     assert_close(f64(hc), f64(hr), "bf16", "state")
+    # and the recurrent op's own whole-sequence path (the chunk kernel), in place
+    S = h0.clone()
+    o2, _ = ops.fused_recurrent_gated_delta_rule(q, k, v, g, b, initial_state=S,
+                                                 final_state_out=S)
+    assert torch.equal(o2, oc) and torch.equal(S, hc)
 
 
 def test_prefill_config_full_size(cuda):
