@@ -1199,14 +1199,17 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st) {
 }
 
 // The layer form always runs the two 64-column tiles of a row as one cluster:
-// the norm of a row needs both halves.  Whether the two CTAs also share the
-// preparation follows the op's rule (GDN_CHUNK_TC_PAIR forces it too).
+// the norm of a row needs both halves.  The two CTAs also share the
+// preparation at low occupancy; the layer form's larger code makes the compact
+// form win from fewer CTAs than the op's rule (measured: pairs at 32 CTAs,
+// 216 against 244 us; compact at 64, 238 against 248 us).  GDN_CHUNK_TC_PAIR
+// forces either form.
 cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   if (!chunk_tc_supported(a) || a.dk != 128 || a.dv != 2 * DVT) return cudaErrorInvalidValue;
   const long long ctas = 2LL * a.B * a.H;
   const char* pair_env = getenv("GDN_CHUNK_TC_PAIR");
-  bool pair = ctas <= device_sm_count() / 2;
+  bool pair = ctas <= device_sm_count() / 3;
   if (pair_env && pair_env[0] == '0') pair = false;
   if (pair_env && pair_env[0] == '1') pair = true;
   return pair ? launch_tc_form<128, true, true>(a, la, st)
