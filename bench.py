@@ -338,6 +338,7 @@ def decode_leg(d, a, lib, uuid):
     # The literal single-state form of the workload (its 64 MiB state stays in L2).
     graph = capture(1)
     ms1, _ = _timed(d, graph.replay, a.steps)
+    res["launches"] += a.steps * TOK
     del graph
     res["single_state"] = {"value": d.world * B * TOK / (ms1 / 1e3), "unit": "tokens/s",
                            "ms_per_step": ms1,
@@ -402,6 +403,7 @@ def decode_leg(d, a, lib, uuid):
             e2e_graph.replay()
         e2e_steps = max(1, min(a.steps, 20))
         ms_e2e, _ = _timed(d, e2e_graph.replay, e2e_steps)
+        res["launches"] += e2e_steps * TOK
         torch.cuda.synchronize(d.dev)
         del e2e_graph
         res["e2e"] = {"value": d.world * B * TOK / (ms_e2e / 1e3), "unit": "tokens/s",
@@ -508,6 +510,7 @@ def prefill_leg(d, a, lib, uuid=None):
         torch.cuda.synchronize(d.dev)
         d.barrier()
         ms_e2e = d.max(e0.elapsed_time(e1) / e2e_steps)
+        res["launches"] += e2e_steps
         res["e2e"] = {"value": d.world * B * T / (ms_e2e / 1e3), "unit": "tokens/s",
                       "h2d_bytes_per_step": int(q.nbytes + k.nbytes + v.nbytes + g.nbytes
                                                 + beta.nbytes),
@@ -816,7 +819,9 @@ def long_context_leg(d, a):
            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
            "config": {"workload": f"B=1 T={T} H=16 dk=dv=128 chunk=64 bf16, final state out",
                       "path": path, "parallelism": f"sequence split sp{d.world}"},
-           "algorithmic_tflops": flops / (ms / 1e3) / 1e12}
+           "algorithmic_tflops": flops / (ms / 1e3) / 1e12,
+           # the split's two passes per step, and (one GPU) the direct launch per step
+           "launches": 2 * steps + (steps if d.world == 1 else 0)}
     res.update(extra)
     return res
 
@@ -875,7 +880,8 @@ def main():
             "gpu_launches": (dec["launches"] + (pre["launches"] if pre else 0)
                              + (bwd["launches"] if bwd else 0) + (lay["launches"] if lay else 0)
                              + (play["launches"] if play else 0)
-                             + (mcore["launches"] if mcore else 0)),
+                             + (mcore["launches"] if mcore else 0)
+                             + (lng["launches"] if lng else 0)),
             "clocks": dec["clocks"],
         }
         if "e2e" in dec:
