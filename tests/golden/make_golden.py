@@ -128,6 +128,9 @@ CASES = {
     "lm": (1, 32, 4, 16, 32, 64, 4, None),
     # a single head: the reference output reshape is then the identity
     "h1": (1, 96, 1, 16, 16, 32, 5, 0.02),
+    # the head dims of the reference's default configuration (head_dim 256, expand_v 2),
+    # with an initial state and a partial last chunk
+    "d256": (1, 70, 1, 256, 512, 64, 6, 0.02),
 }
 
 

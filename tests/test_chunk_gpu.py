@@ -11,7 +11,7 @@ from helpers import assert_close, device_inputs, device_inputs_fast, f64, to_dev
 
 pytestmark = pytest.mark.gpu
 
-GOLDEN_CASES = ["c0", "h0", "tail", "layer", "lm", "h1"]
+GOLDEN_CASES = ["c0", "h0", "tail", "layer", "lm", "h1", "d256"]
 
 
 def _golden_args(c, dev):

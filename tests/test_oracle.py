@@ -17,7 +17,7 @@ def test_golden_cases_present(golden):
     assert (B, T, H, dk, dv, C) == (1, 256, 2, 64, 64, 64)
 
 
-@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1", "d256"])
 def test_recurrent_matches_reference_kernel(golden, name):
     """recurrent_ref == the reference Pallas kernel (ops.py:162-184), zero state."""
     c = golden[name]
@@ -25,7 +25,7 @@ def test_recurrent_matches_reference_kernel(golden, name):
     assert orc.rel_err(o, c["o_recurrent"]) < 1e-6
 
 
-@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1", "d256"])
 def test_literal_chunk_matches_reference_chunk(golden, name):
     """chunk_reference_literal == the reference chunk path (ops.py:299-346)."""
     c = golden[name]
@@ -37,7 +37,7 @@ def test_literal_chunk_matches_reference_chunk(golden, name):
     assert orc.rel_err(h, c["h_chunk"]) < 1e-6
 
 
-@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1", "d256"])
 def test_exact_chunk_matches_reference_recurrence(golden, name):
     """The exact chunked form reproduces the reference recurrent kernel."""
     c = golden[name]

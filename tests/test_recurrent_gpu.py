@@ -13,7 +13,7 @@ from helpers import (assert_close, device_inputs, device_inputs_fast, f64, to_de
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1"])
+@pytest.mark.parametrize("name", ["c0", "h0", "tail", "layer", "lm", "h1", "d256"])
 def test_matches_reference_kernel_outputs(golden, cuda, name):
     """Zero initial state, no final state: the reference call form (ops.py:187)."""
     c = golden[name]
