@@ -190,3 +190,24 @@ def test_layer_gates_and_norm_formulas():
     np.testing.assert_allclose(y, [[3.0 / np.sqrt(12.5), -8.0 / np.sqrt(12.5)]])
     yg = orc.rms_norm_gated(o, np.ones(2), gate=np.array([[0.0, 1.0]]), eps=0.0)
     np.testing.assert_allclose(yg, [[0.0, -4.0 / np.sqrt(12.5) / (1.0 + np.exp(-1.0))]])
+
+
+@pytest.mark.parametrize("chunked", [False, True])
+def test_oracle_linear_in_values_and_state(chunked):
+    """For fixed q, k, g, beta the delta rule is linear in (v, initial state):
+    the property the full-size GPU tests check the kernels against."""
+    rng = np.random.default_rng(11)
+    q, k, v1, g, beta, h1 = orc.make_inputs(2, 90, 3, 32, 24, seed=12, h0_std=0.05)
+    v2 = rng.standard_normal(v1.shape)
+    h2 = rng.standard_normal(h1.shape) * 0.05
+
+    def run(v, h0):
+        if chunked:
+            return orc.chunk_exact(q, k, v, g, beta, h0, 32)
+        return orc.recurrent_ref(q, k, v, g, beta, h0)
+
+    o1, s1 = run(v1, h1)
+    o2, s2 = run(v2, h2)
+    o3, s3 = run(v1 + 2 * v2, h1 + 2 * h2)
+    np.testing.assert_allclose(o3, o1 + 2 * o2, rtol=0, atol=1e-10)
+    np.testing.assert_allclose(s3, s1 + 2 * s2, rtol=0, atol=1e-10)
