@@ -5,9 +5,11 @@ Loading fails loudly: there is no CPU fallback anywhere in this package.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
+from typing import Optional
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libgdn_b200.so")
@@ -41,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_workspace_bytes",
     "gdn_chunk_varlen_workspace_bytes",
     "gdn_last_error",
+    "gdn_reload_kernel_overrides",
     "gdn_device_error",
     "gdn_abi_version",
 )
@@ -101,6 +104,8 @@ def _declare(lib):
     lib.gdn_chunk_varlen_workspace_bytes.restype = _sz
     lib.gdn_last_error.argtypes = []
     lib.gdn_last_error.restype = ctypes.c_char_p
+    lib.gdn_reload_kernel_overrides.argtypes = []
+    lib.gdn_reload_kernel_overrides.restype = None
     lib.gdn_device_error.argtypes = [_i]
     lib.gdn_device_error.restype = _i
     lib.gdn_abi_version.argtypes = []
@@ -120,6 +125,28 @@ def load(path: str = LIB_PATH):
             _declare(lib)
             _lib = lib
         return _lib
+
+
+@contextlib.contextmanager
+def kernel_env(name: str, value: Optional[str]):
+    """Run the body with environment variable ``name`` set to ``value`` (None:
+    unset) as the library's kernel choice, then restore it (cross-checks of one
+    kernel against another; the library reads these variables only on
+    gdn_reload_kernel_overrides)."""
+    old = os.environ.get(name)
+    if value is None:
+        os.environ.pop(name, None)
+    else:
+        os.environ[name] = value
+    load().gdn_reload_kernel_overrides()
+    try:
+        yield
+    finally:
+        if old is None:
+            os.environ.pop(name, None)
+        else:
+            os.environ[name] = old
+        load().gdn_reload_kernel_overrides()
 
 
 def check(rc: int, func: str) -> None:

@@ -1,0 +1,802 @@
+// Chunked gated delta-rule forward in two launches, sm_100a: a preparation
+// kernel over every (chunk, head) pair, then a scan kernel over the chunks of
+// each (head, 64-column state tile).
+//
+// Replaces chunk_gated_delta_rule_fwd (ops.py:299-346) for bf16 inputs with
+// dk = 128, dv a multiple of 64, dense rows (exact semantics, chunks of 64).
+// The reference computes A, inv(I - A), W and U for every chunk with batched
+// XLA ops (ops.py:249-297) and then runs a lax.scan over the chunks
+// (ops.py:322-341).  Here the state-independent work is moved into its own,
+// fully parallel launch, and the sequential scan keeps only two tensor-core
+// round trips per chunk.
+//
+// Per chunk n (C = 64 tokens, in-chunk cumulative gate G, gamma = e^{G_C},
+// dec = e^{G_C - G}):
+//
+//   preparation (chunk_prep_kernel, persistent, two CTAs per SM, one item per
+//   (n, b, h)):
+//     D_pre = [K;Q] K^T                           (tcgen05, M = 128)
+//     A = tril_{-1}(beta_i e^{G_i-G_j} K K^T),  P = tril_0(e^{G_i-G_j} Q K^T)
+//     T = (I + A)^{-1}                            (shared solve, chunk_common.cuh)
+//     Z = K^T diag(dec) T   [dk x 64]             (tcgen05: K^T times the tile dec*T)
+//     PT = P T              [64 x 64]             (tcgen05: [T;P] times T, rows 64-127)
+//     -> 24 KB per chunk-head in the workspace: Z then PT, bf16, in the
+//        128-byte-swizzled layout the scan's tensor-core reads take as is
+//   scan (chunk_scan_kernel, one CTA per (b, h, 64 state columns)):
+//     D1 = [K;Q] S_bf16                           rows 0-63: K S, rows 64-127: Q S
+//     X  = beta (V - e^G (K S))                   -> bf16 tile
+//     D3 = Z X,  S <- gamma S + D3                (the state increment K^T dec T X)
+//     D2 = [Z_hi;PT] X                            rows 64-127: P T X = P V'
+//     O  = e^G (Q S) + P T X
+//
+// This is the recurrence of ops.py:170-184 (V' = T X is the chunk's corrected
+// value; the reference's literal chunk path differs, see the CUDA-core kernel).
+// The scan's critical path per chunk is D1 -> X -> D3 -> S: two MMA round
+// trips and two epilogues, each epilogue spread over eight warps.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "chunk_common.cuh"
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+#include "ptx.cuh"
+
+namespace gdn {
+
+namespace {
+
+constexpr int DK = 128;
+constexpr int DVT = 64;
+constexpr int kTileBytes = 24576;  // workspace per chunk-head: Z [128][64] | PT [64][64], bf16
+
+// ---------------------------------------------------------------------------
+// preparation kernel
+// ---------------------------------------------------------------------------
+
+// Persistent: two CTAs per SM, each walking its share of the (chunk, head)
+// items.  Warp 0 loads, issues the MMAs and stores each result; warp 1 forms
+// the gate vectors one item ahead; warps 2-9 do the math.  The next item's K
+// and Q load while this one is solved (K in two alternating slots, Q in one
+// that frees as soon as the item's first product read it), its first product
+// runs before this item's result is stored, and the store's read of the
+// result tile overlaps the next item's A/P pass (which keeps its rows in
+// registers until the tile's space is free).
+constexpr int kPrepThreads = 320;
+
+// Shared memory from a 1024-byte aligned base.  Each 64-dimension key block is
+// [K slot 0 | Q | K slot 1] (8 KB each): item parity 0 reads [K0; Q] as the
+// 128-row operand of its first product, parity 1 reads [Q; K1].  The result
+// tile (Z then PT, 24 KB) is written over the fp32 solve scratch.
+struct PrepLay {
+  static constexpr int KB_STRIDE = 24576;                 // one key block: K0 | Q | K1
+  static constexpr int SM_KQ = 0;                         // 2 key blocks, 48 KB
+  static constexpr int SM_AF = SM_KQ + 2 * KB_STRIDE;     // fp32 A [64][LDF]
+  static constexpr int SM_TF = SM_AF + 64 * LDF * 4;      // fp32 T scratch [64][LDF]
+  static constexpr int SM_OUT = SM_AF;                    // Z (16 KB) | PT (8 KB)
+  static constexpr int SM_TP = SM_TF + 64 * LDF * 4;      // bf16 [T; P], 128 rows
+  static constexpr int SM_TD = SM_TP + 16384;             // bf16 dec * T, 64 rows
+  static constexpr int SM_VEC = SM_TD + 8192;             // 2 x VecBuf
+  static constexpr int SM_BAR = SM_VEC + 2 * (int)sizeof(VecBuf);
+  static constexpr int SM_TMEM = SM_BAR + 16 * 8;
+  static constexpr int SMEM_BYTES = SM_TMEM + 16 + 1024;  // + alignment slack
+  static_assert(SM_AF % 1024 == 0 && SM_TP % 1024 == 0 && SM_TD % 1024 == 0, "tiles");
+  static_assert(2 * 64 * LDF * 4 >= kTileBytes, "result tile over the solve scratch");
+  static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two CTAs per SM");
+};
+
+enum {
+  P_FULL = 0,    // [2] K and Q of an item landed (by item parity)
+  P_PRE = 2,     // [2] first product of an item in TMEM (by item parity)
+  P_VFULL = 4,   // [2] gate vectors ready
+  P_VEMPTY = 6,  // [2] gate vectors no longer read
+  P_TP = 8,      // T, P, dec T tiles written
+  P_MMA = 9,     // PT and Z in TMEM
+  P_OUT = 10,    // result tile written (8 warps)
+  P_OFREE = 11,  // result tile read by its store: the solve scratch is free again
+};
+
+// TMEM columns of a preparation CTA (256 allocated: two CTAs fit one SM)
+constexpr uint32_t PT_PRE = 0, PT_PT = 128, PT_Z = 192, PT_COLS = 256;
+
+__global__ void __launch_bounds__(kPrepThreads, 2)
+chunk_prep_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
+                  const float* __restrict__ g, const float* __restrict__ beta,
+                  unsigned char* __restrict__ ws, int T, int H, int Hk, int BH, int N) {
+  using L = PrepLay;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::SM_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::SM_TMEM);
+  VecBuf* vecs = reinterpret_cast<VecBuf*>(sm + L::SM_VEC);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Items w = blockIdx.x + j gridDim.x, last chunks first: what the scan reads
+  // first was written last, and is the likeliest to still sit in L2.
+  const long long total = (long long)BH * N;
+  const int cnt = blockIdx.x < total
+                      ? (int)((total - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  auto item = [&](int j, int& n, int& b, int& h, int& hq) {
+    const long long w = blockIdx.x + (long long)j * gridDim.x;
+    const int bh = (int)(w % BH);
+    n = N - 1 - (int)(w / BH);
+    b = bh / H;
+    h = bh - b * H;
+    hq = h * Hk / H;
+    return bh;
+  };
+
+  // The scan grid may launch once every CTA here has started: it then takes
+  // SMs only as these CTAs finish (its reads of the workspace wait for this
+  // whole grid).
+  griddep_launch_dependents();
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[P_FULL + i], 1);
+      mbar_init(&bars[P_PRE + i], 1);
+      mbar_init(&bars[P_VFULL + i], 1);
+      mbar_init(&bars[P_VEMPTY + i], 1);
+    }
+    mbar_init(&bars[P_TP], 1);
+    mbar_init(&bars[P_MMA], 1);
+    mbar_init(&bars[P_OUT], 8);
+    mbar_init(&bars[P_OFREE], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, PT_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) {
+    // ---- loads, MMAs, stores ----
+    if (lane == 0 && cnt > 0) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmQ);
+      auto load_k = [&](int j) {
+        int n, b, h, hq;
+        item(j, n, b, h, hq);
+        const int s = j & 1;
+        mbar_arrive_expect_tx(&bars[P_FULL + s], 32768);  // K now, Q later
+        for (int kb = 0; kb < 2; ++kb)
+          tma_load_4d(sm + L::SM_KQ + kb * L::KB_STRIDE + s * 16384, &tmK, 64 * kb, hq, n * C,
+                      b, &bars[P_FULL + s]);
+      };
+      auto load_q = [&](int j) {
+        int n, b, h, hq;
+        item(j, n, b, h, hq);
+        for (int kb = 0; kb < 2; ++kb)
+          tma_load_4d(sm + L::SM_KQ + kb * L::KB_STRIDE + 8192, &tmQ, 64 * kb, hq, n * C, b,
+                      &bars[P_FULL + (j & 1)]);
+      };
+      // D_pre = [K;Q] K^T (parity 0) or [Q;K] K^T (parity 1), K-dim = dk
+      auto first_product = [&](int j) {
+        const int s = j & 1;
+        const uint32_t a0 = sbase + L::SM_KQ + (s ? 8192u : 0u);
+        const uint32_t b0 = sbase + L::SM_KQ + (s ? 16384u : 0u);
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k) {
+          const uint32_t off = (k >> 2) * L::KB_STRIDE + (k & 3) * 32;
+          mma_bf16(tmem + PT_PRE + (uint32_t)s * 64, umma_desc(a0 + off, 16, 1024, SW128),
+                   umma_desc(b0 + off, 16, 1024, SW128), IDESC_KK, k > 0);
+        }
+        mma_commit(&bars[P_PRE + s]);
+      };
+      load_k(0);
+      load_q(0);
+      bool ok = mbar_wait(&bars[P_FULL], 0);
+      if (ok) {
+        tc_fence_after();
+        first_product(0);
+      }
+      for (int j = 0; j < cnt && ok; ++j) {
+        const int s = j & 1;
+        const bool next = j + 1 < cnt;
+        int n, b, h, hq;
+        const int bh = item(j, n, b, h, hq);
+        // the other K slot was last read by item j - 1's Z, complete by now
+        // (its result was written, so the math warps saw it complete)
+        if (next) load_k(j + 1);
+        // Q is free once this item's first product completed
+        ok = mbar_wait(&bars[P_PRE + s], (uint32_t)(j >> 1) & 1u);
+        if (!ok) break;
+        if (next) load_q(j + 1);
+        ok = mbar_wait(&bars[P_TP], (uint32_t)j & 1u);
+        if (!ok) break;
+        tc_fence_after();
+        // PT: [T;P] T (A K-major over the chunk's tokens; B = T, MN-major)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + PT_PT, umma_desc(sbase + L::SM_TP + k * 32, 16, 1024, SW128),
+                   umma_desc(sbase + L::SM_TP + k * 2048, 8192, 1024, SW128), IDESC_KM, k > 0);
+        // Z: K^T (dec T) (A = K^T, MN-major: M = dk in two 64-wide blocks)
+        const uint32_t ks = sbase + L::SM_KQ + (s ? 16384u : 0u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + PT_Z, umma_desc(ks + k * 2048, L::KB_STRIDE, 1024, SW128),
+                   umma_desc(sbase + L::SM_TD + k * 2048, 8192, 1024, SW128), IDESC_MM, k > 0);
+        mma_commit(&bars[P_MMA]);
+        // the next item's first product, before this one's result is stored
+        if (next) {
+          ok = mbar_wait(&bars[P_FULL + (s ^ 1)], (uint32_t)((j + 1) >> 1) & 1u);
+          if (!ok) break;
+          tc_fence_after();
+          first_product(j + 1);
+        }
+        ok = mbar_wait(&bars[P_OUT], (uint32_t)j & 1u);
+        if (!ok) break;
+        bulk_s2g(ws + ((size_t)bh * N + n) * kTileBytes, sm + L::SM_OUT, kTileBytes);
+        bulk_commit();
+        bulk_wait_read<0>();
+        mbar_arrive(&bars[P_OFREE]);
+      }
+      bulk_wait<0>();
+    }
+  } else if (warp == 1) {
+    // ---- gate vectors, one item ahead ----
+    float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
+    auto fetch = [&](int j) {
+      int n, b, h, hq;
+      item(j, n, b, h, hq);
+      const size_t gb = (size_t)b * T * H + h;
+      const int t = n * C + 2 * lane;
+      g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
+      g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
+      b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
+      b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
+    };
+    if (cnt > 0) fetch(0);
+    for (int j = 0; j < cnt; ++j) {
+      const int s = j & 1;
+      if (j >= 2 && !mbar_wait(&bars[P_VEMPTY + s], (uint32_t)((j - 2) >> 1) & 1u)) break;
+      chunk_gate_vectors(vecs[s], g0, g1, b0, b1, true, lane);
+      if (lane == 0) mbar_arrive(&bars[P_VFULL + s]);
+      if (j + 1 < cnt) fetch(j + 1);
+    }
+  } else {
+    // ---- the math warps: A/P, the solve, the result epilogue ----
+    const int pw = warp - 2;          // 0..7
+    const int pi = tid - 64;          // 0..255
+    const int wq = warp & 3;          // TMEM lane quarter this warp may read
+    const int ch = pw >> 2;           // which 32 of the 64 D_pre columns
+    const int p = wq * 32 + lane;     // TMEM lane = accumulator row
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    float* AF = reinterpret_cast<float*>(sm + L::SM_AF);
+    float* TF = reinterpret_cast<float*>(sm + L::SM_TF);
+    unsigned char* tpt = sm + L::SM_TP;
+    unsigned char* tdt = sm + L::SM_TD;
+    // The strictly upper 16x16 blocks of T (and dec T) are never written below.
+    for (int e = pi; e < 64 * 8; e += 256) {
+      const int row = e / 8, c8 = e % 8;
+      if (c8 >= 2 * (row / 16 + 1)) {
+        *reinterpret_cast<uint4*>(tpt + sw128(row, c8)) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(tdt + sw128(row, c8)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    // (a timed-out wait is recorded in the device error word; the math warps
+    // agree on it at the first named barrier of the item and leave together,
+    // so none of them waits at a barrier the others no longer reach)
+    bool ok = true;
+    for (int j = 0; j < cnt; ++j) {
+      const int s = j & 1;
+      const VecBuf& vb = vecs[s];
+      ok = mbar_wait(&bars[P_VFULL + s], (uint32_t)(j >> 1) & 1u) && ok;
+      ok = mbar_wait(&bars[P_PRE + s], (uint32_t)(j >> 1) & 1u) && ok;
+      tc_fence_after();
+      // A (strictly lower) and P (lower with the diagonal) from D_pre: this
+      // warp's 32 columns of row p, which holds K K^T (A) or Q K^T (P)
+      // depending on the item's parity.  Steep gates (direct) form each
+      // e^{G_i - G_j} from its own exponent.  The row waits in registers
+      // until the previous result tile (over A's scratch) has been read out.
+      const bool isA = (p < 64) == (s == 0);
+      const int i = p & 63;
+      float row[32];
+      {
+        const int jmax = isA ? i - 1 : i;
+        const float rs = isA ? vb.beta[i] : 1.f;
+        const float Gi = vb.G[i];
+        tmem_ld32(tmem + PT_PRE + (uint32_t)s * 64 + (uint32_t)ch * 32 + lane_off, row);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int q4 = 2 * ch + h2;
+          if (vb.direct) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int jj = q4 * 16 + e;
+              row[16 * h2 + e] = (jj <= jmax) ? rs * gate_exp(Gi - vb.G[jj]) * row[16 * h2 + e]
+                                              : 0.f;
+            }
+          } else {
+            const float fq = rs * vb.F[i][q4];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int jj = q4 * 16 + e;
+              row[16 * h2 + e] = (jj <= jmax) ? fq * vb.E[jj] * row[16 * h2 + e] : 0.f;
+            }
+          }
+        }
+      }
+      if (j > 0) ok = mbar_wait(&bars[P_OFREE], (uint32_t)(j - 1) & 1u) && ok;
+      if (isA) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(AF + i * LDF + 32 * ch + e) =
+              make_float4(rtf32(row[e]), rtf32(row[e + 1]), rtf32(row[e + 2]), rtf32(row[e + 3]));
+      } else {
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8)
+          *reinterpret_cast<uint4*>(tpt + sw128(64 + i, 4 * ch + c8)) = pack_bf16x8(row + 8 * c8);
+      }
+      // ---- T = (I + A)^{-1}: diagonal blocks, then off-diagonal blocks ----
+      if (!named_sync_and(1, 256, ok)) break;
+      if (pi < 64) solve_diag(AF, TF, tpt, nullptr, vb.dec, pi);
+      named_sync(1, 256);
+      solve_offdiag(AF, TF, tpt, nullptr, vb.dec, pw, lane, 1, 256);
+      named_sync(1, 256);
+      {
+        // dec T (the B operand of Z), from the bf16 T: row pi / 4, 16 columns
+        const int r = pi >> 2, c8 = 2 * (pi & 3);
+        const float d = vb.dec[r];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float t8[8];
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(tpt + sw128(r, c8 + u)), t8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t8[e] *= d;
+          *reinterpret_cast<uint4*>(tdt + sw128(r, c8 + u)) = pack_bf16x8(t8);
+        }
+      }
+      fence_proxy_async_smem();
+      named_sync(1, 256);
+      if (pi == 0) {
+        mbar_arrive(&bars[P_TP]);
+        mbar_arrive(&bars[P_VEMPTY + s]);
+      }
+      // ---- result: Z (rows 0-127) and PT (rows 64-127 of the [T;P] T
+      //      product), bf16, over the solve scratch ----
+      ok = mbar_wait(&bars[P_MMA], (uint32_t)j & 1u) && ok;
+      tc_fence_after();
+      {
+        float z[32];
+        tmem_ld32(tmem + PT_Z + (uint32_t)ch * 32 + lane_off, z);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8)
+          *reinterpret_cast<uint4*>(sm + L::SM_OUT + sw128(p, 4 * ch + c8)) =
+              pack_bf16x8(z + 8 * c8);
+        if (wq >= 2) {
+          float pt[32];
+          tmem_ld32(tmem + PT_PT + (uint32_t)ch * 32 + lane_off, pt);
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8)
+            *reinterpret_cast<uint4*>(sm + L::SM_OUT + 16384 + sw128(p - 64, 4 * ch + c8)) =
+                pack_bf16x8(pt + 8 * c8);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[P_OUT]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, PT_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// scan kernel
+// ---------------------------------------------------------------------------
+
+constexpr int kScanThreads = 384;  // warps 0-3 roles, 4-11 epilogues
+constexpr int NS = 3;              // K/Q/V stages
+constexpr int NR = 3;              // ring of preparation tiles
+constexpr int NV = 3;              // ring of gate vectors
+
+// barrier indices
+enum {
+  S_FULL = 0,                 // [NS] K, Q, V of a chunk loaded
+  S_EMPTY = S_FULL + NS,      // [NS] the MMAs are done with a stage (V: epilogue 1 read it before X)
+  S_RFULL = S_EMPTY + NS,     // [NR] preparation tile loaded
+  S_REMPTY = S_RFULL + NR,    // [NR] preparation tile read by the MMAs
+  S_VFULL = S_REMPTY + NR,    // [NV] gate vectors ready
+  S_VEMPTY = S_VFULL + NV,    // [NV] gate vectors read by every epilogue warp
+  S_D1 = S_VEMPTY + NV,       // D1 in TMEM
+  S_X,                        // X tile written (4 warps)
+  S_D3,                       // D3 in TMEM
+  S_D2,                       // D2 in TMEM
+  S_D2FREE,                   // D2 read (4 warps)
+  S_S,                        // state tile written (8 warps)
+  S_D1FREE,                   // [2] a D1 buffer's Q S rows read (4 warps)
+  S_DONE = S_D1FREE + 2,
+  S_NBAR,
+};
+
+struct ScanVec {
+  float beta[C], eG[C];
+  float eGC;
+  float pad[3];
+};
+
+struct ScanLay {
+  static constexpr int SM_KQ = 0;                        // NS x [2 key blocks][K | Q] (32 KB)
+  static constexpr int SM_V = SM_KQ + NS * 32768;        // NS x [64 tokens][128 B]
+  static constexpr int SM_R = SM_V + NS * 8192;          // NR x (Z | PT), 24 KB
+  static constexpr int SM_S = SM_R + NR * kTileBytes;    // bf16 state tile [128][128 B]
+  static constexpr int SM_X = SM_S + 16384;              // bf16 X [64 tokens][128 B]
+  static constexpr int SM_VEC = SM_X + 8192;             // NV x ScanVec
+  static constexpr int SM_BAR = SM_VEC + NV * (int)sizeof(ScanVec);
+  static constexpr int SM_TMEM = SM_BAR + S_NBAR * 8;
+  static constexpr int SMEM_BYTES = SM_TMEM + 16 + 1024;
+  static_assert(SM_R % 1024 == 0 && SM_S % 1024 == 0 && SM_X % 1024 == 0, "swizzled tiles");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
+
+// TMEM columns of a scan CTA
+constexpr uint32_t ST_D1 = 0;    // 2 x 64
+constexpr uint32_t ST_D3 = 128;
+constexpr uint32_t ST_D2 = 192;
+constexpr uint32_t ST_COLS = 256;
+
+__global__ void __launch_bounds__(kScanThreads, 1)
+chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
+                  const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
+                  const float* __restrict__ beta, const unsigned char* __restrict__ ws,
+                  const float* h0, __nv_bfloat16* __restrict__ o, float* hT, int T, int H,
+                  int Hk, int dv) {
+  // (h0 and hT may be the same array: each CTA reads its tile of h0 before it
+  // writes the same tile of hT)
+  using L = ScanLay;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::SM_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::SM_TMEM);
+  ScanVec* vecs = reinterpret_cast<ScanVec*>(sm + L::SM_VEC);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - b * H;
+  const int hq = h * Hk / H;
+  const int c0 = blockIdx.x * DVT;
+  const int N = (T + C - 1) / C;
+
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&bars[S_FULL + i], 1);
+      mbar_init(&bars[S_EMPTY + i], 1);
+    }
+    for (int i = 0; i < NR; ++i) {
+      mbar_init(&bars[S_RFULL + i], 1);
+      mbar_init(&bars[S_REMPTY + i], 1);
+    }
+    for (int i = 0; i < NV; ++i) {
+      mbar_init(&bars[S_VFULL + i], 1);
+      mbar_init(&bars[S_VEMPTY + i], 8);
+    }
+    mbar_init(&bars[S_D1], 1);
+    mbar_init(&bars[S_X], 4);
+    mbar_init(&bars[S_D3], 1);
+    mbar_init(&bars[S_D2], 1);
+    mbar_init(&bars[S_D2FREE], 4);
+    mbar_init(&bars[S_S], 8);
+    mbar_init(&bars[S_D1FREE + 0], 4);
+    mbar_init(&bars[S_D1FREE + 1], 4);
+    mbar_init(&bars[S_DONE], 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, ST_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) {
+    // ---- K, Q, V of each chunk (TMA) ----
+    if (elect_one()) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmV);
+      int issued = 0;
+      for (int n = 0; n < N; ++n) {
+        const int s = n % NS;
+        if (n >= NS && !mbar_wait(&bars[S_EMPTY + s], (uint32_t)((n / NS) - 1) & 1u)) break;
+        unsigned char* kq = sm + L::SM_KQ + s * 32768;
+        uint64_t* fb = &bars[S_FULL + s];
+        mbar_arrive_expect_tx(fb, 32768 + 8192);
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_load_4d(kq + kb * 16384, &tmK, 64 * kb, hq, n * C, b, fb);
+          tma_load_4d(kq + kb * 16384 + 8192, &tmQ, 64 * kb, hq, n * C, b, fb);
+        }
+        tma_load_4d(sm + L::SM_V + s * 8192, &tmV, c0, h, n * C, b, fb);
+        issued = n + 1;
+      }
+      // every issued load lands before the CTA can exit (bounded)
+      for (int n = issued > NS ? issued - NS : 0; n < issued; ++n)
+        mbar_wait(&bars[S_FULL + n % NS], (uint32_t)(n / NS) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (elect_one()) {
+      bool ok = true;
+      for (int n = 0; n < N && ok; ++n) {
+        const int s = n % NS, r = n % NR, buf = n & 1;
+        const uint32_t kq = sbase + L::SM_KQ + s * 32768;
+        const uint32_t rt = sbase + L::SM_R + r * kTileBytes;
+        ok = mbar_wait(&bars[S_FULL + s], (uint32_t)(n / NS) & 1u) &&
+             mbar_wait(&bars[S_S], (uint32_t)n & 1u) &&
+             (n < 2 || mbar_wait(&bars[S_D1FREE + buf], (uint32_t)((n - 2) >> 1) & 1u));
+        if (!ok) break;
+        tc_fence_after();
+        // D1 = [K;Q] S   (K-dim = dk: 8 steps of 16)
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k) {
+          const uint64_t a = umma_desc(kq + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, SW128);
+          const uint64_t bd = umma_desc(sbase + L::SM_S + k * 2048, 16384, 1024, SW128);
+          mma_bf16(tmem + ST_D1 + (uint32_t)buf * 64, a, bd, IDESC_KM, k > 0);
+        }
+        mma_commit(&bars[S_D1]);
+        ok = mbar_wait(&bars[S_X], (uint32_t)n & 1u) &&
+             mbar_wait(&bars[S_RFULL + r], (uint32_t)(n / NR) & 1u) &&
+             (n < 1 || mbar_wait(&bars[S_D2FREE], (uint32_t)(n - 1) & 1u));
+        if (!ok) break;
+        tc_fence_after();
+        // D3 = Z X, the state increment (K-dim = tokens: 4 steps)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t a = umma_desc(rt + k * 32, 16, 1024, SW128);
+          const uint64_t bd = umma_desc(sbase + L::SM_X + k * 2048, 8192, 1024, SW128);
+          mma_bf16(tmem + ST_D3, a, bd, IDESC_KM, k > 0);
+        }
+        mma_commit(&bars[S_D3]);
+        // D2 = [Z rows 64-127; PT] X: rows 64-127 are P T X
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t a = umma_desc(rt + 8192 + k * 32, 16, 1024, SW128);
+          const uint64_t bd = umma_desc(sbase + L::SM_X + k * 2048, 8192, 1024, SW128);
+          mma_bf16(tmem + ST_D2, a, bd, IDESC_KM, k > 0);
+        }
+        mma_commit(&bars[S_D2]);
+        mma_commit(&bars[S_EMPTY + s]);
+        mma_commit(&bars[S_REMPTY + r]);
+      }
+      mma_commit(&bars[S_DONE]);
+      mbar_wait(&bars[S_DONE], 0);
+    }
+  } else if (warp == 2) {
+    // ---- gate warp: beta, e^G and e^{G_C} of each chunk, NV - 1 chunks ahead ----
+    const size_t gb = (size_t)b * T * H + h;
+    for (int n = 0; n < N; ++n) {
+      const int v = n % NV;
+      const int t = n * C + 2 * lane;
+      const float g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
+      const float g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
+      const float b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
+      const float b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
+      if (n >= NV && !mbar_wait(&bars[S_VEMPTY + v], (uint32_t)((n / NV) - 1) & 1u)) break;
+      ScanVec& vb = vecs[v];
+      const float pair = g0 + g1;
+      float incl = pair;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      vb.beta[2 * lane] = b0;
+      vb.beta[2 * lane + 1] = b1;
+      vb.eG[2 * lane] = gate_exp(incl - pair + g0);
+      vb.eG[2 * lane + 1] = gate_exp(incl);
+      if (lane == 31) vb.eGC = gate_exp(incl);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[S_VFULL + v]);
+    }
+  } else if (warp == 3) {
+    // ---- preparation tiles (bulk copies from the workspace) ----
+    if (elect_one()) {
+      // the preparation grid's writes are complete and visible past this point
+      griddep_wait();
+      const unsigned char* src = ws + (size_t)bh * N * kTileBytes;
+      int issued = 0;
+      for (int n = 0; n < N; ++n) {
+        const int r = n % NR;
+        if (n >= NR && !mbar_wait(&bars[S_REMPTY + r], (uint32_t)((n / NR) - 1) & 1u)) break;
+        mbar_arrive_expect_tx(&bars[S_RFULL + r], kTileBytes);
+        bulk_g2s(sm + L::SM_R + r * kTileBytes, src + (size_t)n * kTileBytes, kTileBytes,
+                 &bars[S_RFULL + r]);
+        issued = n + 1;
+      }
+      for (int n = issued > NR ? issued - NR : 0; n < issued; ++n)
+        mbar_wait(&bars[S_RFULL + n % NR], (uint32_t)(n / NR) & 1u);
+    }
+  } else {
+    // ---- epilogue warps: quarter wq of the TMEM lanes, 32 of the 64 columns ----
+    const int wq = warp & 3;
+    const int cb = 32 * ((warp - 4) >> 2);  // column offset within the tile
+    const int r = wq * 32 + lane;           // TMEM lane: state row, or token row
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    unsigned char* Stile = sm + L::SM_S;
+    float S[32];
+    {
+      const float* src = h0 ? h0 + ((size_t)bh * DK + r) * dv + c0 + cb : nullptr;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4) {
+        const float4 x = src ? *reinterpret_cast<const float4*>(src + c)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        S[c] = x.x; S[c + 1] = x.y; S[c + 2] = x.z; S[c + 3] = x.w;
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8)
+        *reinterpret_cast<uint4*>(Stile + sw128(r, cb / 8 + c8)) = pack_bf16x8(S + 8 * c8);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[S_S]);
+    }
+    bool ok = true;
+    for (int n = 0; n < N && ok; ++n) {
+      const int s = n % NS, v = n % NV, buf = n & 1;
+      const ScanVec& vb = vecs[v];
+      const uint32_t d1 = tmem + ST_D1 + (uint32_t)buf * 64 + (uint32_t)cb + lane_off;
+      ok = mbar_wait(&bars[S_VFULL + v], (uint32_t)(n / NV) & 1u);
+      if (!ok) break;
+      if (wq < 2) {
+        // ---- epilogue 1: X = beta (V - e^G K S), token row r ----
+        ok = mbar_wait(&bars[S_D1], (uint32_t)n & 1u) &&
+             mbar_wait(&bars[S_FULL + s], (uint32_t)(n / NS) & 1u);
+        if (!ok) break;
+        tc_fence_after();
+        float ks[32];
+        tmem_ld32(d1, ks);
+        const float bi = vb.beta[r], egi = vb.eG[r];
+        const unsigned char* Vt = sm + L::SM_V + s * 8192;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float vv[8], x[8];
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(r, cb / 8 + c8)), vv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = bi * (vv[e] - egi * ks[8 * c8 + e]);
+          *reinterpret_cast<uint4*>(sm + L::SM_X + sw128(r, cb / 8 + c8)) = pack_bf16x8(x);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[S_X]);
+      }
+      // ---- epilogue 3: S <- e^{G_C} S + Z X, state row r ----
+      ok = mbar_wait(&bars[S_D3], (uint32_t)n & 1u);
+      if (!ok) break;
+      tc_fence_after();
+      {
+        float ds[32];
+        tmem_ld32(tmem + ST_D3 + (uint32_t)cb + lane_off, ds);
+        const float egc = vb.eGC;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) S[e] = fmaf(egc, S[e], ds[e]);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8)
+          *reinterpret_cast<uint4*>(Stile + sw128(r, cb / 8 + c8)) = pack_bf16x8(S + 8 * c8);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[S_S]);
+      }
+      if (wq >= 2) {
+        // ---- output: O = e^G (Q S) + P T X, token row r - 64 ----
+        ok = mbar_wait(&bars[S_D2], (uint32_t)n & 1u);
+        if (!ok) break;
+        tc_fence_after();
+        const int i = r - 64, t = n * C + i;
+        float qs[16], pv[16];
+        const float egi = vb.eG[i];
+        __nv_bfloat16* orow = o + (((size_t)b * T + t) * H + h) * dv + c0 + cb;
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          tmem_ld16x2(d1 + 16 * q2, tmem + ST_D2 + (uint32_t)cb + lane_off + 16 * q2, qs, pv);
+          float out[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) out[e] = fmaf(egi, qs[e], pv[e]);
+          if (t < T) {
+            *reinterpret_cast<uint4*>(orow + 16 * q2) = pack_bf16x8(out);
+            *reinterpret_cast<uint4*>(orow + 16 * q2 + 8) = pack_bf16x8(out + 8);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bars[S_D2FREE]);
+          mbar_arrive(&bars[S_D1FREE + buf]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[S_VEMPTY + v]);
+    }
+    if (ok && hT) {
+      float* dst = hT + ((size_t)bh * DK + r) * dv + c0 + cb;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4)
+        *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ST_COLS);
+  }
+}
+
+}  // namespace
+
+GDN_DEVICE_ERROR_ACCESSOR(device_error_chunk_scan)
+
+bool chunk_scan_shape_ok(const ChunkArgs& a) {
+  return a.dtype == kBF16 && a.semantics == kExact && a.dk == DK && a.dv % DVT == 0 &&
+         a.T > 0 && !a.cu_seqlens && (long long)a.B * a.H <= 65535;
+}
+
+bool chunk_scan_supported(const ChunkArgs& a) {
+  return chunk_scan_shape_ok(a) && encode_fn() != nullptr;
+}
+
+size_t chunk_scan_workspace_bytes(int B, int T, int H) {
+  if (B <= 0 || T <= 0 || H <= 0) return 0;
+  const size_t N = ((size_t)T + C - 1) / C;
+  return (size_t)B * H * N * kTileBytes;
+}
+
+cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st) {
+  if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_scan_supported(a) || !a.workspace ||
+      a.ws_bytes < chunk_scan_workspace_bytes(a.B, a.T, a.H) ||
+      (reinterpret_cast<uintptr_t>(a.workspace) & 15u))
+    return cudaErrorInvalidValue;
+  CUtensorMap mk, mq, mv;
+  if (!make_bf16_map_4d(&mk, a.k, a.B, a.T, a.Hk, DK) ||
+      !make_bf16_map_4d(&mq, a.q, a.B, a.T, a.Hk, DK) ||
+      !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv))
+    return cudaErrorInvalidValue;
+  static std::atomic<int> prep_slot[kMaxDevices] = {};
+  static std::atomic<int> scan_slot[kMaxDevices] = {};
+  cudaError_t e = ensure_smem(chunk_prep_kernel, PrepLay::SMEM_BYTES, prep_slot);
+  if (e != cudaSuccess) return e;
+  e = ensure_smem(chunk_scan_kernel, ScanLay::SMEM_BYTES, scan_slot);
+  if (e != cudaSuccess) return e;
+  const int N = (a.T + C - 1) / C;
+  const long long items = (long long)a.B * a.H * N;
+  const int prep_ctas = (int)(items < 2LL * device_sm_count() ? items : 2LL * device_sm_count());
+  unsigned char* ws = static_cast<unsigned char*>(a.workspace);
+  chunk_prep_kernel<<<prep_ctas, kPrepThreads, PrepLay::SMEM_BYTES, st>>>(
+      mk, mq, a.g, a.beta, ws, a.T, a.H, a.Hk, a.B * a.H, N);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // The scan is launched behind the preparation with programmatic stream
+  // serialization: its set-up overlaps the preparation's last wave, and its
+  // reads of the workspace wait for the whole preparation grid (griddep_wait).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.dv / DVT, a.B * a.H);
+  cfg.blockDim = dim3(kScanThreads);
+  cfg.dynamicSmemBytes = ScanLay::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, chunk_scan_kernel, mk, mq, mv, a.g, a.beta,
+                         static_cast<const unsigned char*>(ws), a.h0,
+                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace gdn

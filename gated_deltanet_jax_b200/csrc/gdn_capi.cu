@@ -6,8 +6,55 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <atomic>
+
 #include "gdn.h"
 #include "gdn_internal.h"
+
+namespace gdn {
+
+namespace {
+
+KernelOverrides read_overrides() {
+  KernelOverrides k;
+  const char* chunk = getenv("GDN_CHUNK_KERNEL");
+  k.chunk_simt = chunk && strcmp(chunk, "simt") == 0;
+  k.chunk_fused = chunk && strcmp(chunk, "fused") == 0;
+  const char* pair = getenv("GDN_CHUNK_TC_PAIR");
+  if (pair && pair[0] == '0') k.tc_pair = 0;
+  if (pair && pair[0] == '1') k.tc_pair = 1;
+  const char* rec = getenv("GDN_RECURRENT_KERNEL");
+  k.recurrent_token = rec && strcmp(rec, "token") == 0;
+  const char* pdl = getenv("GDN_DECODE_PDL");
+  k.decode_pdl = !(pdl && pdl[0] == '0');
+  return k;
+}
+
+// The current choices, packed into one word so that a reload is atomic.
+int pack(const KernelOverrides& k) {
+  return (k.chunk_simt ? 1 : 0) | (k.chunk_fused ? 2 : 0) | ((k.tc_pair + 1) << 2) |
+         (k.recurrent_token ? 16 : 0) | (k.decode_pdl ? 32 : 0);
+}
+
+std::atomic<int>& override_word() {
+  static std::atomic<int> w{pack(read_overrides())};
+  return w;
+}
+
+}  // namespace
+
+KernelOverrides kernel_overrides() {
+  const int w = override_word().load(std::memory_order_relaxed);
+  KernelOverrides k;
+  k.chunk_simt = (w & 1) != 0;
+  k.chunk_fused = (w & 2) != 0;
+  k.tc_pair = ((w >> 2) & 3) - 1;
+  k.recurrent_token = (w & 16) != 0;
+  k.decode_pdl = (w & 32) != 0;
+  return k;
+}
+
+}  // namespace gdn
 
 namespace {
 
@@ -85,9 +132,7 @@ int recurrent_fwd(const void* q, const void* k, const void* v, const float* g, c
   // tensor cores instead of token by token.  Each CTA reads its tile of h0
   // before it writes the same tile of hT, so h0 == hT stays an in-place update.
   // GDN_RECURRENT_KERNEL=token keeps the token loop (kernel cross-checks).
-  const char* force = getenv("GDN_RECURRENT_KERNEL");
-  const bool token_only = force && strcmp(force, "token") == 0;
-  if (!token_only && T >= 64) {
+  if (!gdn::kernel_overrides().recurrent_token && T >= 64) {
     gdn::ChunkArgs ca{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, 64, dtype,
                       GDN_SEMANTICS_EXACT, nullptr, 0, Hk};
     if (gdn::chunk_tc_supported(ca))
@@ -118,6 +163,9 @@ size_t chunk_workspace(int B, int T, int H, int dk, int dv, int chunk, int dtype
   a.semantics = semantics;
   const bool tc_shape = dtype == GDN_DTYPE_BF16 && semantics == GDN_SEMANTICS_EXACT &&
                         (dk == 128 || dk == 256) && dv % 64 == 0;
+  // dense rows at dk = 128: the two-launch form's per-chunk operands
+  if (tc_shape && n_seqs == 0 && gdn::chunk_scan_shape_ok(a))
+    return gdn::chunk_scan_workspace_bytes(B, T, H);
   if (tc_shape || !dk_supported(dk) || !gdn::chunk_fwd_warp_supported(a)) return 0;
   return gdn::chunk_fwd_warp_workspace_bytes(B, T, H, dk, dv, n_seqs);
 }
@@ -350,9 +398,12 @@ int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const
   }
   gdn::ChunkArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, chunk, dtype, semantics,
                    workspace, ws_bytes, Hk, cu_seqlens};
-  // GDN_CHUNK_KERNEL=simt forces the CUDA-core kernel (kernel cross-checks).
-  const char* force = getenv("GDN_CHUNK_KERNEL");
-  const bool simt_only = force && strcmp(force, "simt") == 0;
+  // GDN_CHUNK_KERNEL=simt forces the CUDA-core kernel, =fused the one-launch
+  // tensor-core kernel (kernel cross-checks; read once).
+  const gdn::KernelOverrides ov = gdn::kernel_overrides();
+  const bool simt_only = ov.chunk_simt;
+  if (!simt_only && !ov.chunk_fused && gdn::chunk_scan_supported(a) && need > 0)
+    return cuda_status(gdn::launch_chunk_scan(a, (cudaStream_t)stream), "gdn_chunk_fwd");
   if (!simt_only && gdn::chunk_tc_supported(a))
     return cuda_status(gdn::launch_chunk_tc(a, (cudaStream_t)stream), "gdn_chunk_fwd");
   if (!simt_only && need > 0)
@@ -430,13 +481,18 @@ int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v, const flo
 
 const char* gdn_last_error(void) { return g_err; }
 
+void gdn_reload_kernel_overrides(void) {
+  gdn::override_word().store(gdn::pack(gdn::read_overrides()), std::memory_order_relaxed);
+}
+
 int gdn_device_error(int clear) {
   // Synchronous: waits for the current device's outstanding work.
   const int a = gdn::device_error_recurrent_bulk(clear != 0);
   const int b = gdn::device_error_chunk_tc(clear != 0);
-  return a ? a : b;
+  const int c = gdn::device_error_chunk_scan(clear != 0);
+  return a ? a : (b ? b : c);
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 7; }
+int gdn_abi_version(void) { return (1 << 16) | 8; }
 
 }  // extern "C"

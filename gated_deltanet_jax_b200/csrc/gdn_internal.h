@@ -1,6 +1,8 @@
 // Internal launch interface shared by the kernels and the C ABI (gdn_capi.cu).
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -46,6 +48,23 @@ inline int device_sm_count() {
   }
   return n;
 }
+
+// Kernel choices a test can force for cross-checks, read from the environment
+// on the library's first call that consults them and again at each
+// gdn_reload_kernel_overrides() (never per call):
+//   GDN_CHUNK_KERNEL=simt    the CUDA-core chunk kernel
+//   GDN_CHUNK_KERNEL=fused   the one-launch tensor-core chunk kernel (no workspace)
+//   GDN_CHUNK_TC_PAIR=0 / 1  its unpaired / paired form
+//   GDN_RECURRENT_KERNEL=token  the token loop for whole sequences
+//   GDN_DECODE_PDL=0         decode steps without programmatic dependent launch
+struct KernelOverrides {
+  bool chunk_simt = false;
+  bool chunk_fused = false;
+  int tc_pair = -1;  // -1: by occupancy
+  bool recurrent_token = false;
+  bool decode_pdl = true;
+};
+KernelOverrides kernel_overrides();
 
 enum DType : int { kFP32 = 0, kBF16 = 1 };
 enum Semantics : int { kExact = 0, kReference = 1 };
@@ -136,6 +155,12 @@ cudaError_t launch_recurrent_bulk_layer(const RecurrentArgs& a, const LayerArgs&
 int device_error_recurrent_bulk(bool clear);
 int device_error_chunk_tc(bool clear);
 
+// The driver's tensor-map encoder (NULL when the driver does not provide it).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
+// [B, T, H, D] bf16 as a 4-D TMA map (D, H, T, B), boxes of 64 x 1 x 64 x 1
+// with 128-byte swizzle; tokens past T read as zero.
+bool make_bf16_map_4d(CUtensorMap* m, const void* base, int B, int T, int H, int D);
+
 // Tensor-core chunk kernel: bf16, dk = 128 or 256, dv % 64 == 0, chunk = 64, exact.
 bool chunk_tc_supported(const ChunkArgs& a);
 cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
@@ -144,6 +169,15 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
 // from the raw projections (a.g / a.beta unused) and the gated RMSNorm of
 // every output row, written to a.o.
 cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st);
+
+// Two-launch chunked forward (bf16, dk = 128, dv % 64 == 0, exact, dense rows):
+// a preparation kernel over every (chunk, head) writes the state-independent
+// per-chunk operands into the workspace, then a scan kernel walks the chunks.
+bool chunk_scan_shape_ok(const ChunkArgs& a);    // the shapes it takes (no device query)
+bool chunk_scan_supported(const ChunkArgs& a);   // ... and the driver can encode TMA maps
+size_t chunk_scan_workspace_bytes(int B, int T, int H);
+cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st);
+int device_error_chunk_scan(bool clear);
 
 // The chunked forward on the backward's warp-level tensor-core kernels (exact
 // semantics, dk in 16..256, dv % 32 == 0, dense or packed): fp32 inputs, and

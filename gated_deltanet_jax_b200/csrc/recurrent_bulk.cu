@@ -309,8 +309,7 @@ cudaError_t launch_bulk_t(const RecurrentArgs& a, const LayerArgs& la, cudaStrea
   const int grid = n_units < num_sms() ? n_units : num_sms();
   // Consecutive decode steps on one stream may overlap their launch and
   // set-up (programmatic dependent launch); GDN_DECODE_PDL=0 turns it off.
-  const char* pdl_env = getenv("GDN_DECODE_PDL");
-  const bool pdl = !(pdl_env && pdl_env[0] == '0');
+  const bool pdl = kernel_overrides().decode_pdl;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

@@ -280,11 +280,22 @@ int gdn_device_error(int clear);
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
+/*
+ * Re-read the kernel-choice variables of the environment (GDN_CHUNK_KERNEL =
+ * simt | fused, GDN_CHUNK_TC_PAIR = 0 | 1, GDN_RECURRENT_KERNEL = token,
+ * GDN_DECODE_PDL = 0), which the library otherwise reads once, on its first
+ * call that consults them.  For cross-checks of one kernel against another in
+ * one process; the default choices need none of them.  No counterpart in the
+ * reference, which has one kernel per op.
+ */
+void gdn_reload_kernel_overrides(void);
+
 /* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward;
  * 1.4: backward of packed sequences, the allocation-free backward;
  * 1.5: the layer form of the decode step; 1.6: the layer form of the chunked
  * forward; 1.7: dk = 256 on the tensor cores, the chunked forward's workspace
- * for fp32 inputs, gdn_chunk_varlen_workspace_bytes). */
+ * for fp32 inputs, gdn_chunk_varlen_workspace_bytes; 1.8: the two-launch chunked
+ * forward and its workspace (bf16, dk = 128), gdn_reload_kernel_overrides). */
 int gdn_abi_version(void);
 
 #ifdef __cplusplus

@@ -216,12 +216,15 @@ def test_empty_problem_is_a_no_op(lib):
 
 
 def test_workspace_query(lib):
-    """Zero on the tcgen05 shapes (bf16, dk 128 / 256, dv % 64 == 0) and for the
-    reference semantics; non-zero where the call runs on the warp-level
-    tensor-core kernels (fp32 inputs, other bf16 shapes), growing with the work."""
+    """The two-launch form (bf16, dk 128, dv % 64 == 0, dense): 24 KB per
+    chunk-head for the per-chunk operands.  Zero on the other tcgen05 shapes
+    (dk 256, packed sequences) and for the reference semantics; non-zero where
+    the call runs on the warp-level tensor-core kernels (fp32 inputs, other
+    bf16 shapes), growing with the work."""
     bf16, fp32 = _lib.GDN_DTYPE_BF16, _lib.GDN_DTYPE_FP32
     q = lib.gdn_chunk_workspace_bytes
-    assert q(4, 4096, 16, 128, 128, 64, bf16, 0) == 0
+    assert q(4, 4096, 16, 128, 128, 64, bf16, 0) == 4 * 16 * 64 * 24576
+    assert q(1, 65, 2, 128, 192, 64, bf16, 0) == 2 * 2 * 24576    # partial last chunk
     assert q(8, 2048, 6, 256, 512, 64, bf16, 0) == 0
     assert q(2, 100, 2, 128, 128, 64, fp32, _lib.GDN_SEMANTICS_REFERENCE) == 0
     assert q(2, 100, 2, 128, 48, 64, fp32, 0) == 0          # dv % 32 != 0: CUDA cores

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from gated_deltanet_jax_b200 import ops
+from gated_deltanet_jax_b200 import _lib, ops
 from oracle import gdn_oracle as orc
 from helpers import assert_close, device_inputs, device_inputs_fast, f64, to_dev
 
@@ -92,11 +92,15 @@ def test_chunk_equals_recurrent_kernel(cuda):
         q, k, v, g, b, initial_state=h0, output_final_state=True))
     assert_close(f64(oc), f64(orr), "bf16", "o")
     assert_close(f64(hc), f64(hr), "bf16", "state")
-    # and the recurrent op's own whole-sequence path (the chunk kernel), in place
+    # and the recurrent op's own whole-sequence path (the one-launch chunk
+    # kernel, which needs no workspace), in place
     S = h0.clone()
     o2, _ = ops.fused_recurrent_gated_delta_rule(q, k, v, g, b, initial_state=S,
                                                  final_state_out=S)
-    assert torch.equal(o2, oc) and torch.equal(S, hc)
+    of, hf = _with_kernel("fused", lambda: ops.chunk_gated_delta_rule(
+        q, k, v, g, b, initial_state=h0, output_final_state=True))
+    assert torch.equal(o2, of) and torch.equal(S, hf)
+    assert_close(f64(o2), f64(orr), "bf16", "o (whole-sequence recurrent op)")
 
 
 def test_prefill_config_full_size(cuda):
@@ -119,16 +123,8 @@ def test_prefill_config_full_size(cuda):
 
 
 def _with_env(name, value, fn):
-    import os
-    old = os.environ.get(name)
-    os.environ[name] = value
-    try:
+    with _lib.kernel_env(name, value):
         return fn()
-    finally:
-        if old is None:
-            del os.environ[name]
-        else:
-            os.environ[name] = old
 
 
 def _with_kernel(kind, fn):
@@ -167,9 +163,10 @@ def test_tensor_core_matches_cuda_core_kernel(cuda, B, T, H, dv):
 @pytest.mark.parametrize("B,T,H,dv", [(2, 700, 3, 128), (1, 193, 2, 256), (1, 64, 1, 128),
                                       (1, 130, 2, 128), (3, 1, 2, 128), (4, 300, 16, 128)])
 def test_paired_tiles_match_unpaired(cuda, B, T, H, dv):
-    """Column-tile pairs that share the per-chunk preparation (clusters of two
-    CTAs, each preparing every other chunk for both) give bit-identical results
-    to tiles that each prepare every chunk themselves."""
+    """The one-launch kernel's column-tile pairs that share the per-chunk
+    preparation (clusters of two CTAs, each preparing every other chunk for
+    both) give bit-identical results to tiles that each prepare every chunk
+    themselves."""
     q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, dv, seed=T + dv, dtype="bf16", dev=cuda,
                                            h0_std=0.02)
 
@@ -177,8 +174,9 @@ def test_paired_tiles_match_unpaired(cuda, B, T, H, dv):
         return ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
                                           output_final_state=True)
 
-    o_p, h_p = _with_env("GDN_CHUNK_TC_PAIR", "1", run)
-    o_s, h_s = _with_env("GDN_CHUNK_TC_PAIR", "0", run)
+    with _lib.kernel_env("GDN_CHUNK_KERNEL", "fused"):
+        o_p, h_p = _with_env("GDN_CHUNK_TC_PAIR", "1", run)
+        o_s, h_s = _with_env("GDN_CHUNK_TC_PAIR", "0", run)
     assert torch.equal(o_p, o_s)
     assert torch.equal(h_p, h_s)
 
@@ -290,3 +288,39 @@ def test_warp_tensor_core_forward_matches_cuda_core_kernel(cuda, dtype, B, T, H,
     ro, rh = orc.chunk_exact(*host, chunk_size=64)
     assert_close(f64(o_w), ro, dtype, "o vs oracle")
     assert_close(f64(h_w), rh, dtype, "state vs oracle")
+
+
+@pytest.mark.parametrize("B,T,H,Hk,dv", [(2, 700, 3, 3, 128), (1, 193, 2, 1, 256), (3, 1, 2, 2, 64),
+                                         (1, 64, 4, 2, 192), (4, 300, 16, 16, 128)])
+def test_two_launch_matches_one_launch(cuda, B, T, H, Hk, dv):
+    """The two-launch form (preparation over every chunk-head, then the scan)
+    against the one-launch kernel: the same recurrence, rounded at different
+    points, so within the bf16 bar of each other (and of the oracle)."""
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, dv, seed=T + dv + Hk, dtype="bf16",
+                                           dev=cuda, h0_std=0.02)
+    q, k = q[:, :, ::H // Hk].contiguous(), k[:, :, ::H // Hk].contiguous()
+
+    def run():
+        return ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
+                                          output_final_state=True)
+
+    from gated_deltanet_jax_b200 import _lib as lib_mod
+    assert lib_mod.load().gdn_chunk_workspace_bytes(B, T, H, 128, dv, 64, 1, 0) > 0
+    o2, h2 = run()
+    o1, h1 = _with_kernel("fused", run)
+    assert_close(f64(o2), f64(o1), "bf16", "o")
+    assert_close(f64(h2), f64(h1), "bf16", "state")
+    assert torch.isfinite(o2.float()).all() and torch.isfinite(h2).all()
+
+
+def test_two_launch_in_place_and_repeatable(cuda):
+    """h0 == hT (in-place state) gives what separate buffers give, and a
+    repeated call is bit-identical (no atomics, fixed reduction order)."""
+    q, k, v, g, b, h0 = device_inputs_fast(2, 333, 4, 128, 128, seed=31, dtype="bf16", dev=cuda,
+                                           h0_std=0.02)
+    o1, h1 = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    o2, h2 = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    S = h0.clone()
+    o3, _ = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=S, final_state_out=S)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
+    assert torch.equal(o1, o3) and torch.equal(h1, S)

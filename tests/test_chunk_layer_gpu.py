@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gated_deltanet_jax_b200 import ops
+from gated_deltanet_jax_b200 import _lib, ops
 from oracle import gdn_oracle as orc
 from helpers import assert_close, device_inputs, device_inputs_fast, f64
 
@@ -83,7 +83,7 @@ def test_chunk_layer_full_size_equals_separate_operations(cuda):
 
 
 @pytest.mark.parametrize("pair", ["0", "1"])
-def test_chunk_layer_forms_agree(cuda, monkeypatch, pair):
+def test_chunk_layer_forms_agree(cuda, pair):
     """With and without shared preparation (GDN_CHUNK_TC_PAIR forces either
     form; both are clusters of two CTAs exchanging row sums) the outputs are
     bit-identical to the form the dispatcher picks for a small grid (pairs)."""
@@ -94,8 +94,8 @@ def test_chunk_layer_forms_agree(cuda, monkeypatch, pair):
     args = (q, k, v, a, b, A_log, dt_bias)
     kw = dict(gate=gate, norm_weight=w, initial_state=S, output_final_state=True)
     y0, h0 = ops.gated_delta_rule_chunk_layer(*args, **kw)
-    monkeypatch.setenv("GDN_CHUNK_TC_PAIR", pair)
-    y1, h1 = ops.gated_delta_rule_chunk_layer(*args, **kw)
+    with _lib.kernel_env("GDN_CHUNK_TC_PAIR", pair):
+        y1, h1 = ops.gated_delta_rule_chunk_layer(*args, **kw)
     assert torch.equal(y0, y1) and torch.equal(h0, h1)
 
 

@@ -4,12 +4,10 @@ model.py:132-135) before its ops; the ops here take the unrepeated tensors.
 Every kernel must give exactly what it gives on the repeated tensors, and the
 oracle's answer on the repeated inputs."""
 
-import os
-
 import pytest
 import torch
 
-from gated_deltanet_jax_b200 import ops, sequence_parallel as sp
+from gated_deltanet_jax_b200 import _lib, ops, sequence_parallel as sp
 from oracle import gdn_oracle as orc
 from helpers import assert_close, device_inputs, device_inputs_fast, f64
 
@@ -23,35 +21,22 @@ def _grouped(q, k, rep):
     return qg, kg, qg.repeat_interleave(rep, dim=2), kg.repeat_interleave(rep, dim=2)
 
 
-def _env(name, value):
-    old = os.environ.get(name)
-    os.environ[name] = value
-    return old
-
-
-def _restore(name, old):
-    if old is None:
-        os.environ.pop(name, None)
-    else:
-        os.environ[name] = old
-
-
-@pytest.mark.parametrize("pair", ["0", "1"])
+@pytest.mark.parametrize("pair", [None, "0", "1"])
 @pytest.mark.parametrize("B,T,Hk,rep,dv", [(2, 300, 2, 3, 128), (1, 129, 1, 4, 256),
                                           (3, 64, 4, 2, 64)])
 def test_chunk_tensor_core_grouped_equals_repeated(cuda, pair, B, T, Hk, rep, dv):
+    """pair None: the two-launch form (the default); "0" / "1": the one-launch
+    kernel's unpaired / paired form."""
     H = Hk * rep
     q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, dv, seed=T + rep, dtype="bf16",
                                            dev=cuda, h0_std=0.02)
     qg, kg, qr, kr = _grouped(q, k, rep)
-    old = _env("GDN_CHUNK_TC_PAIR", pair)
-    try:
+    with _lib.kernel_env("GDN_CHUNK_KERNEL", None if pair is None else "fused"), \
+            _lib.kernel_env("GDN_CHUNK_TC_PAIR", pair):
         o_g, h_g = ops.chunk_gated_delta_rule(qg, kg, v, g, b, initial_state=h0,
                                               output_final_state=True)
         o_r, h_r = ops.chunk_gated_delta_rule(qr, kr, v, g, b, initial_state=h0,
                                               output_final_state=True)
-    finally:
-        _restore("GDN_CHUNK_TC_PAIR", old)
     assert torch.equal(o_g, o_r)
     assert torch.equal(h_g, h_r)
 

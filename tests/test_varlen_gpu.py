@@ -5,13 +5,11 @@ what the same kernel gives it on its own, and the oracle's answer.  The rows
 of a chunk past a sequence's end hold the next sequence's tokens, so these
 tests also check that nothing leaks across a boundary."""
 
-import os
-
 import numpy as np
 import pytest
 import torch
 
-from gated_deltanet_jax_b200 import ops
+from gated_deltanet_jax_b200 import _lib, ops
 from oracle import gdn_oracle as orc
 from helpers import assert_close, device_inputs, f64
 
@@ -30,16 +28,10 @@ def _packed(lengths, H, Hk, dk, dv, dtype, dev, seed):
 
 
 def _run(pair, fn):
-    old = os.environ.get("GDN_CHUNK_TC_PAIR")
-    if pair is not None:
-        os.environ["GDN_CHUNK_TC_PAIR"] = pair
-    try:
+    """fn() on the one-launch tensor-core kernel (the one packed sequences
+    take), in its default form (pair None) or forced unpaired / paired."""
+    with _lib.kernel_env("GDN_CHUNK_KERNEL", "fused"), _lib.kernel_env("GDN_CHUNK_TC_PAIR", pair):
         return fn()
-    finally:
-        if old is None:
-            os.environ.pop("GDN_CHUNK_TC_PAIR", None)
-        else:
-            os.environ["GDN_CHUNK_TC_PAIR"] = old
 
 
 CASES = [
