@@ -51,6 +51,19 @@ def _args():
     p.add_argument("--no-long", action="store_true", help="skip the long-context leg")
     p.add_argument("--no-backward", action="store_true", help="skip the backward leg")
     p.add_argument("--no-layer", action="store_true", help="skip the layer-core legs")
+    # A fixed workload for ncu captures (one process, one GPU, no timing):
+    #   --profile-workload decode --launches 3        (B=64 H=16 dk=dv=128, state in place)
+    #   --profile-workload prefill --launches 2 [--B 4 --T 4096 --H 16 --dk 128 --dv 128]
+    #   --profile-workload backward --launches 2 [--B 4 --T 4096]
+    #   --profile-workload prefill_layer --launches 2 [--B 4 --T 4096]
+    p.add_argument("--profile-workload", choices=["decode", "prefill", "backward",
+                                                   "prefill_layer"], default=None)
+    p.add_argument("--launches", type=int, default=3)
+    p.add_argument("--B", type=int, default=None)
+    p.add_argument("--T", type=int, default=None)
+    p.add_argument("--H", type=int, default=16)
+    p.add_argument("--dk", type=int, default=128)
+    p.add_argument("--dv", type=int, default=128)
     return p.parse_args()
 
 
@@ -825,8 +838,76 @@ def long_context_leg(d, a):
     res.update(extra)
     return res
 
+def profile_workload(a):
+    """Run one fixed workload ``a.launches`` times on cuda:0 for an ncu capture.
+
+    decode: B=64 H=16 dk=dv=128, bf16 q/k/v, fp32 state ~N(0,0.02) updated in
+    place, one token per launch.  prefill: B=4 T=4096 H=16 dk=dv=128, bf16 in,
+    fp32 final state out.  backward: gradients of q, k, v, g, beta for the
+    prefill workload from a bf16 dO, no initial state.  prefill_layer: the
+    prefill workload through gdn_chunk_fwd_layer (gates from raw a/b
+    projections initialised as the layer does, a bf16 output gate, norm
+    weight 1, eps 1e-5).
+    """
+    import math
+    import torch
+    from gated_deltanet_jax_b200 import ops
+    dev = torch.device("cuda:0")
+
+    def inputs(B, T, seed):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        nrm = torch.nn.functional.normalize
+        q = nrm(torch.randn(B, T, a.H, a.dk, device=dev, generator=gen), dim=-1).bfloat16()
+        k = nrm(torch.randn(B, T, a.H, a.dk, device=dev, generator=gen), dim=-1).bfloat16()
+        v = torch.randn(B, T, a.H, a.dv, device=dev, generator=gen).bfloat16()
+        g = torch.nn.functional.logsigmoid(torch.randn(B, T, a.H, device=dev, generator=gen))
+        beta = torch.sigmoid(torch.randn(B, T, a.H, device=dev, generator=gen))
+        return q, k, v, g, beta
+
+    w = a.profile_workload
+    if w == "decode":
+        B = a.B or 64
+        q, k, v, g, beta = inputs(B, 1, 0)
+        S = torch.randn(B, a.H, a.dk, a.dv, device=dev) * 0.02
+        run = lambda: ops.fused_recurrent_gated_delta_rule(  # noqa: E731
+            q, k, v, g, beta, initial_state=S, final_state_out=S)
+    elif w == "prefill":
+        q, k, v, g, beta = inputs(a.B or 4, a.T or 4096, 0)
+        run = lambda: ops.chunk_gated_delta_rule(  # noqa: E731
+            q, k, v, g, beta, output_final_state=True)
+    elif w == "prefill_layer":
+        B, T = a.B or 4, a.T or 4096
+        q, k, v, ra, rb = inputs(B, T, 0)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(2)
+        gate = torch.randn(B, T, a.H, a.dv, device=dev, generator=gen).bfloat16()
+        A_log = torch.log(torch.rand(a.H, device=dev, generator=gen) * 16 + 1e-4)
+        u = torch.rand(a.H, device=dev, generator=gen)
+        dt = torch.exp(u * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3)).clamp_min(1e-4)
+        dt_bias = dt + torch.log(-torch.expm1(-dt))
+        run = lambda: ops.gated_delta_rule_chunk_layer(  # noqa: E731
+            q, k, v, ra, rb, A_log, dt_bias, gate=gate, output_final_state=True)
+    else:
+        B, T = a.B or 4, a.T or 4096
+        q, k, v, g, beta = inputs(B, T, 0)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1)
+        do = torch.randn(B, T, a.H, a.dv, device=dev, generator=gen).bfloat16()
+        run = lambda: ops._chunk_backward(q, k, v, g, beta, None, do, None)  # noqa: E731
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(a.launches):
+        run()
+    torch.cuda.synchronize()
+    print(f"{w}: {a.launches} launches in {time.perf_counter() - t0:.3f} s")
+
+
 def main():
     a = _args()
+    if a.profile_workload:
+        profile_workload(a)
+        return
     if a.impl == "reference":
         run_reference_arm(a)
         return

@@ -57,7 +57,14 @@ def _stale(target, deps) -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile every ``csrc/*.cu`` and link ``libgdn_b200.so``; returns its path."""
+    """Compile every ``csrc/*.cu`` and link ``libgdn_b200.so``; returns its path.
+
+    Each file is compiled as a module of its own, without relocatable device
+    code (no ``-rdc``, no device link).  chunk_bwd_static.cu relies on this:
+    its 64 MiB ``__device__`` scratch array then lives in a module that CUDA's
+    lazy loading brings onto a GPU only when the allocation-free backward is
+    first called there, not whenever the library is loaded.
+    """
     nvcc = _nvcc()
     os.makedirs(BUILD_DIR, exist_ok=True)
     srcs, hdrs = _sources(), _headers()

@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "gdn_reload_kernel_overrides",
     "gdn_device_error",
     "gdn_abi_version",
+    "gdn_binary_version",
 )
 
 _lock = threading.Lock()
@@ -110,6 +111,8 @@ def _declare(lib):
     lib.gdn_device_error.restype = _i
     lib.gdn_abi_version.argtypes = []
     lib.gdn_abi_version.restype = _i
+    lib.gdn_binary_version.argtypes = []
+    lib.gdn_binary_version.restype = _i
 
 
 def load(path: str = LIB_PATH):

@@ -10,7 +10,9 @@
 // not stop for cudaMalloc, which can synchronise the device.
 // For them the scratch lives here, in one array of this library's own device
 // memory, reserved when the CUDA driver loads this file's code on a GPU and
-// held until the process exits.
+// held until the process exits.  This file must stay a module of its own (no
+// relocatable device code): under CUDA's default lazy loading the array is
+// then reserved only on GPUs where this entry point is called.
 //
 // This file only holds the array and finds its device address; the kernels
 // are gdn_chunk_bwd's own, given that address as their workspace.

@@ -739,6 +739,12 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 
 GDN_DEVICE_ERROR_ACCESSOR(device_error_chunk_scan)
 
+int chunk_scan_binary_version() {
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, chunk_scan_kernel) != cudaSuccess) return -1;
+  return fa.binaryVersion;
+}
+
 bool chunk_scan_shape_ok(const ChunkArgs& a) {
   return a.dtype == kBF16 && a.semantics == kExact && a.dk == DK && a.dv % DVT == 0 &&
          a.T > 0 && !a.cu_seqlens && (long long)a.B * a.H <= 65535;

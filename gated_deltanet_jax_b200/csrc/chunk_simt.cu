@@ -53,12 +53,14 @@ __host__ __device__ inline SimtSmem simt_layout(int C, int DK, int DVT) {
   return L;
 }
 
+// h0 and hT may be the same array (in-place state): each CTA reads its tile of
+// h0 before its first chunk and writes the same tile of hT after its last.
 template <typename Tin, int DVT>
 __global__ void __launch_bounds__(kSimtThreads)
 chunk_simt_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
                   const Tin* __restrict__ v, const float* __restrict__ g,
-                  const float* __restrict__ beta, const float* __restrict__ h0,
-                  Tin* __restrict__ o, float* __restrict__ hT,
+                  const float* __restrict__ beta, const float* h0,
+                  Tin* __restrict__ o, float* hT,
                   const int* __restrict__ cu_seqlens, int T, int H, int Hk, int DK, int dv,
                   int C, int semantics) {
   constexpr int NT = kSimtThreads;

@@ -168,12 +168,14 @@ __device__ __forceinline__ bool wait_shared_bar(uint64_t* bars, int idx, uint32_
 // of a row always run as a cluster of two CTAs, which exchange the rows'
 // partial sums of squares; without kPair each still prepares every chunk (the
 // compact form, for high occupancy).
+// h0 and hT may be the same array (in-place state): each CTA reads its tile of
+// h0 before the loop and writes the same tile of hT after it.
 template <int DK, bool kPair, bool kLayer>
 __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
-                const float* __restrict__ beta, const float* __restrict__ h0,
-                __nv_bfloat16* __restrict__ o, float* __restrict__ hT,
+                const float* __restrict__ beta, const float* h0,
+                __nv_bfloat16* __restrict__ o, float* hT,
                 const int* __restrict__ cu_seqlens, int T, int H, int Hk, int dv,
                 const LayerArgs la) {
   constexpr bool kCluster = kPair || kLayer;  // launched in clusters of two CTAs

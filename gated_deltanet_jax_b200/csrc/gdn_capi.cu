@@ -495,4 +495,6 @@ int gdn_device_error(int clear) {
 
 int gdn_abi_version(void) { return (1 << 16) | 8; }
 
+int gdn_binary_version(void) { return gdn::chunk_scan_binary_version(); }
+
 }  // extern "C"

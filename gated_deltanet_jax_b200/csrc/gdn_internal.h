@@ -178,6 +178,8 @@ bool chunk_scan_supported(const ChunkArgs& a);   // ... and the driver can encod
 size_t chunk_scan_workspace_bytes(int B, int T, int H);
 cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st);
 int device_error_chunk_scan(bool clear);
+// Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
+int chunk_scan_binary_version();
 
 // The chunked forward on the backward's warp-level tensor-core kernels (exact
 // semantics, dk in 16..256, dv % 32 == 0, dense or packed): fp32 inputs, and

@@ -147,8 +147,9 @@ def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final
     Every rank passes its own contiguous segment ``[B, T_p, H, D]`` (rank order =
     token order; every rank's T_p is the same, except possibly the last one's).
     Each rank splits its segment again into ``local_parts`` segments that run
-    batched on its GPU (None: chosen so the second pass fills the GPU, the same
-    on every rank for equal segment lengths); all world x local_parts (S, M)
+    batched on its GPU (None: chosen so the second pass fills the GPU; the ranks
+    take the smallest of their choices, so a shorter last segment is fine; an
+    explicit value must be the same on every rank); all world x local_parts (S, M)
     pairs are exchanged in one all-gather, after which every rank folds the
     prefix locally with a log-depth scan.
     ``initial_state`` is the state before rank 0's segment and must be the same
@@ -166,11 +167,22 @@ def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final
         dist.all_gather(out, packed, group=group)
         return out
 
-    if local_parts is None:
-        local_parts = auto_local_parts(k.shape[0], k.shape[1], v.shape[2], v.shape[-1],
-                                       chunk_size, k.device)
-    return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
-                     max(1, int(local_parts)), fn, gather, world, rank)
+    # Every rank must split into the same number of local segments: the
+    # all-gather exchanges [B, parts, H, dk, dv + dk] summaries, and the fold
+    # indexes them rank-major.  A chosen count depends on this rank's T (the
+    # last rank's may be shorter), so the ranks agree on the smallest choice;
+    # counts passed in must already agree, or every rank raises.
+    auto = local_parts is None
+    mine = (auto_local_parts(k.shape[0], k.shape[1], v.shape[2], v.shape[-1], chunk_size,
+                             k.device) if auto else max(1, int(local_parts)))
+    span = torch.tensor([mine, -mine], dtype=torch.int64, device=k.device)
+    dist.all_reduce(span, op=dist.ReduceOp.MIN, group=group)
+    lo, hi = int(span[0]), -int(span[1])
+    if not auto and lo != hi:
+        raise ValueError(f"local_parts differs across ranks ({lo} .. {hi}); pass the same value "
+                         "on every rank, or None")
+    return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, lo, fn,
+                     gather, world, rank)
 
 
 def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_final_state=False,

@@ -240,9 +240,13 @@ size_t gdn_chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, in
  * dk = dv = 128 fit up to T = 768 tokens).  The call itself allocates
  * nothing: no cudaMalloc, cudaFree or allocating library routine.
  *
- * - The array is reserved on a GPU when the driver loads this library's code
- *   there (CUDA's default lazy loading: at the first call of this entry point
- *   on that GPU) and held until the process exits.
+ * - The array is reserved on a GPU when the driver loads the module that
+ *   holds it there, and held until the process exits.  The library keeps that
+ *   array in a module of its own (its files are compiled separately, without
+ *   relocatable device code), so under CUDA's default lazy loading the 64 MiB
+ *   are reserved at the first call of this entry point on a GPU.  With eager
+ *   loading (CUDA_MODULE_LOADING=EAGER) every process that loads the library
+ *   reserves them on every GPU it initialises, whether or not it calls this.
  * - The first call on each device also finds the array's address and sets up
  *   the kernels; make it before any stream capture.
  * - Every call on a device uses the same array, which keeps the previous
@@ -297,6 +301,14 @@ void gdn_reload_kernel_overrides(void);
  * for fp32 inputs, gdn_chunk_varlen_workspace_bytes; 1.8: the two-launch chunked
  * forward and its workspace (bf16, dk = 128), gdn_reload_kernel_overrides). */
 int gdn_abi_version(void);
+
+/*
+ * The GPU architecture the library's kernels were compiled for, as the CUDA
+ * runtime reports it for one of them (major * 10 + minor: 100 for sm_100a), or
+ * -1 when no device can be queried.  Diagnostics only; no counterpart in the
+ * reference.
+ */
+int gdn_binary_version(void);
 
 #ifdef __cplusplus
 }

@@ -26,7 +26,8 @@ rounding.  Inputs are stored as float32 values; outputs as float32.
 
 Run once, in a container that has the reference checkout::
 
-    python tests/golden/make_golden.py [path/to/reference]
+    python tests/golden/make_golden.py path/to/reference
+    (or GDN_REFERENCE_ROOT=path/to/reference python tests/golden/make_golden.py)
 
 The tests only read the ``.npz``; nothing at test time needs the reference.
 """
@@ -134,7 +135,11 @@ CASES = {
 }
 
 
-def main(ref_root="/root/reference"):
+def main(ref_root=None):
+    ref_root = ref_root or os.environ.get("GDN_REFERENCE_ROOT")
+    if not ref_root:
+        raise SystemExit("usage: make_golden.py path/to/reference "
+                         "(or set GDN_REFERENCE_ROOT to the reference checkout)")
     _install_jax_standin()
     ops = _load_reference_ops(ref_root)
     out = {}

@@ -181,6 +181,12 @@ def test_paired_tiles_match_unpaired(cuda, B, T, H, dv):
     assert torch.equal(h_p, h_s)
 
 
+def test_kernels_report_sm100(cuda):
+    """The CUDA runtime reports the library's kernels as built for compute
+    capability 10.0 (sm_100a), on the device itself."""
+    assert _lib.load().gdn_binary_version() == 100
+
+
 def test_no_device_error_recorded_chunk(cuda):
     from gated_deltanet_jax_b200 import _lib
     assert _lib.load().gdn_device_error(1) == 0

@@ -47,13 +47,18 @@ def test_segment_summary_is_affine_map():
     assert orc.max_abs_err((M @ _t(h0) + S).numpy(), hT) < 1e-10
 
 
-def _sp_worker(rank, world, port, T, results, local_parts=1):
+def _sp_worker(rank, world, port, T, results, local_parts=1, seg=None, auto_by_length=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        if auto_by_length:
+            # local_parts=None on CPU tensors: a per-rank choice that grows with the
+            # rank's own T (as the CUDA choice does), so a shorter last rank would
+            # pick fewer parts than the others without the agreement step
+            sp.auto_local_parts = lambda B, T_, H, dv, C, dev: max(1, T_ // (2 * C))
         q, k, v, g, beta, h0 = orc.make_inputs(1, T, 2, 16, 16, seed=5, h0_std=0.05)
-        seg = T // world
+        seg = seg or T // world
         sl = slice(rank * seg, (rank + 1) * seg if rank < world - 1 else T)
         args = [_t(x[:, sl]) for x in (q, k, v, g, beta)]
         o, hT = sp.chunk_gated_delta_rule_sp(*args, initial_state=_t(h0), output_final_state=True,
@@ -160,3 +165,25 @@ def test_split_across_nccl_ranks(cuda):
         for r in range(2):
             eo, eh = results[r]
             assert eo <= orc.TOL_BF16_REL and eh <= orc.TOL_BF16_REL, (r, eo, eh)
+
+
+def test_split_ranks_agree_on_local_parts_with_a_shorter_last_rank():
+    """local_parts=None with a last rank holding fewer tokens: the ranks'
+    own choices differ (3 against 1 here); they must agree before the
+    all-gather, and the result still matches the oracle."""
+    world, T, seg = 3, 250, 96          # ranks hold 96, 96 and 58 tokens
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        port = 29500 + 401 + os.getpid() % 500
+        procs = [ctx.Process(target=_sp_worker,
+                             args=(r, world, port, T, results, None, seg, True))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+        for r in range(world):
+            eo, eh = results[r]
+            assert eo < 1e-10 and eh < 1e-10, (r, eo, eh)

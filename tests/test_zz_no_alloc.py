@@ -94,8 +94,11 @@ def test_no_alloc_matches_workspace_entry_on_consecutive_calls(cuda):
         got = _call(lib, pr, no_alloc=True)
         want = _call(lib, pr, no_alloc=False)
         for n, a, r in zip(names, got, want):
-            err = orc.rel_err(f64(a), f64(r))
-            assert err <= TOL[dt], f"call {step}: {n} rel error {err:.2e}"
+            # the backward is deterministic (no atomics, fixed summation order),
+            # so the scratch's address must not change a single bit; the bar
+            # the other tests use is reported for a mismatch
+            assert torch.equal(a, r), (f"call {step}: {n} differs, rel error "
+                                       f"{orc.rel_err(f64(a), f64(r)):.2e} (bar {TOL[dt]})")
     assert lib.gdn_device_error(1) == 0
 
 
