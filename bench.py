@@ -465,7 +465,8 @@ def prefill_leg(d, a, lib, uuid=None):
     ms, clocks = _timed(d, step, steps, sampler)
     flops = B * T * H * rl.flops_chunk_per_token_head(dk, dv, C)
     res = {"ms": ms, "value": d.world * B * T / (ms / 1e3), "flops_launch": flops,
-           "launch_s": ms / 1e3, "launches": steps, "steps": steps, "clocks": clocks,
+           # two launches per call: the per-chunk preparation, then the scan
+           "launch_s": ms / 1e3, "launches": 2 * steps, "steps": steps, "clocks": clocks,
            "bytes_launch": B * T * H * rl.bytes_chunk_per_token_head(dk, dv) + B * H * dk * dv * 4}
     if not a.no_e2e:
         # Through the public op with pinned host buffers, every step: H2D of the
@@ -523,7 +524,7 @@ def prefill_leg(d, a, lib, uuid=None):
         torch.cuda.synchronize(d.dev)
         d.barrier()
         ms_e2e = d.max(e0.elapsed_time(e1) / e2e_steps)
-        res["launches"] += e2e_steps
+        res["launches"] += 2 * e2e_steps
         res["e2e"] = {"value": d.world * B * T / (ms_e2e / 1e3), "unit": "tokens/s",
                       "h2d_bytes_per_step": int(q.nbytes + k.nbytes + v.nbytes + g.nbytes
                                                 + beta.nbytes),
@@ -682,7 +683,8 @@ def prefill_layer_leg(d, a):
                         "a/b projections, chunked forward, gated RMSNorm (eps 1e-5) of every "
                         "output row; final state out; 8 calls per CUDA graph",
             "fused_ms": res["fused"], "unfused_ms": res["unfused"], "op_only_ms": res["op_only"],
-            "speedup": res["unfused"] / res["fused"], "launches": 3 * REP * steps,
+            # fused: one launch per call; unfused and op_only: the op's two each
+            "speedup": res["unfused"] / res["fused"], "launches": 5 * REP * steps,
             "fused_tokens_per_s": d.world * B * T / (res["fused"] / 1e3),
             "path": "fused: gdn_chunk_fwd_layer (1 launch; the two column tiles of a row as one "
                     "cluster of two CTAs); unfused: torch gates, "
@@ -783,60 +785,87 @@ def backward_leg(d, a, lib):
 def long_context_leg(d, a):
     """B=1, T=65536, H=16 over all ranks (strong scaling: the sequence is split
     evenly across ranks, the state handed off by an NCCL all-gather), each rank's
-    segment split again into parts on its GPU."""
+    segment split again into parts on its GPU.  Every rank generates the whole
+    sequence from one seed and keeps its segment, so that after the timed region
+    each rank can check its outputs and the final state against one unsplit
+    launch over the whole sequence on its own GPU (max over ranks reported)."""
     import torch
     from gated_deltanet_jax_b200 import ops, sequence_parallel as sp
     from gated_deltanet_jax_b200 import roofline as rl
     B, T, H, dk, dv, C = (LONG[x] for x in ("B", "T", "H", "dk", "dv", "chunk"))
     seg = T // d.world
     gen = torch.Generator(device=d.dev)
-    gen.manual_seed(7 + d.rank)
+    gen.manual_seed(7)
     nrm = torch.nn.functional.normalize
-    q = nrm(torch.randn(B, seg, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
-    k = nrm(torch.randn(B, seg, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16()
-    v = torch.randn(B, seg, H, dv, device=d.dev, generator=gen).bfloat16()
-    g = torch.nn.functional.logsigmoid(torch.randn(B, seg, H, device=d.dev, generator=gen))
-    beta = torch.sigmoid(torch.randn(B, seg, H, device=d.dev, generator=gen))
+    full = [nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16(),
+            nrm(torch.randn(B, T, H, dk, device=d.dev, generator=gen), dim=-1).bfloat16(),
+            torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16(),
+            torch.nn.functional.logsigmoid(torch.randn(B, T, H, device=d.dev, generator=gen)),
+            torch.sigmoid(torch.randn(B, T, H, device=d.dev, generator=gen))]
+    sl = slice(d.rank * seg, (d.rank + 1) * seg)
+    q, k, v, g, beta = (x[:, sl].contiguous() for x in full)
     # one GPU: the split is timed against the direct launch below; several GPUs:
     # segments per GPU chosen so that the second pass fills the GPU
     local_parts = (LONG["parts"] if d.world == 1 else
                    sp.auto_local_parts(B, seg, H, dv, C, torch.device(d.dev)))
-    if d.world == 1:
-        def step():
-            sp.chunk_gated_delta_rule_split(q, k, v, g, beta, output_final_state=True,
-                                            parts=local_parts)
-    else:
-        def step():
-            sp.chunk_gated_delta_rule_sp(q, k, v, g, beta, output_final_state=True,
-                                         local_parts=local_parts)
+
+    def split(marks=None):
+        if d.world == 1:
+            return sp.chunk_gated_delta_rule_split(q, k, v, g, beta, output_final_state=True,
+                                                   parts=local_parts, marks=marks)
+        return sp.chunk_gated_delta_rule_sp(q, k, v, g, beta, output_final_state=True,
+                                            local_parts=local_parts, marks=marks)
+
     for _ in range(a.warmup):
-        step()
+        split()
     steps = max(1, min(a.steps, 20))
-    ms, _ = _timed(d, step, steps)
+    ms, _ = _timed(d, split, steps)
+    # per-phase times of the split (outside the timed region, max over ranks)
+    phase_ms = {}
+    for _ in range(3):
+        marks = []
+        start = torch.cuda.Event(enable_timing=True)
+        start.record()
+        split(marks)
+        torch.cuda.synchronize(d.dev)
+        prev = start
+        for name, ev in marks:
+            phase_ms[name] = phase_ms.get(name, 0.0) + prev.elapsed_time(ev) / 3
+            prev = ev
+    phase_ms = {n: d.max(t) for n, t in phase_ms.items()}
     path = (f"sequence split over {d.world} GPU(s) x {local_parts} segment(s) per GPU"
             if d.world > 1 or local_parts > 1 else "one launch")
-    extra = {}
+    extra = {"split_phase_ms": phase_ms}
+    direct = lambda: ops.chunk_gated_delta_rule(  # noqa: E731
+        *full, output_final_state=True)
     if d.world == 1:
         # On one GPU the split is an option, not a necessity: time the direct launch
         # too and report whichever path is faster for this workload.
-        def direct():
-            ops.chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True)
         for _ in range(a.warmup):
             direct()
         ms_d, _ = _timed(d, direct, steps)
-        extra = {"split_ms_per_step": ms, "unsplit_ms_per_step": ms_d}
+        extra.update({"split_ms_per_step": ms, "unsplit_ms_per_step": ms_d})
         if ms_d < ms:
             ms, path = ms_d, "one launch (no split)"
+    # correctness of the split against one unsplit launch (outside the timed region)
+    o_s, h_s = split()
+    o_ref, h_ref = direct()
+    rel = lambda x, r: float((x.float() - r.float()).abs().max() / r.float().abs().max())  # noqa: E731
+    extra["max_rel_err"] = {"o": d.max(rel(o_s, o_ref[:, sl])), "state": d.max(rel(h_s, h_ref)),
+                            "against": "one unsplit launch over the whole sequence (every rank, "
+                                       "its own segment of o; max over ranks)"}
     flops = T * H * rl.flops_chunk_per_token_head(dk, dv, C)
     res = {"metric": "long-context chunk prefill tokens/s", "value": B * T / (ms / 1e3),
            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
            "config": {"workload": f"B=1 T={T} H=16 dk=dv=128 chunk=64 bf16, final state out",
                       "path": path, "parallelism": f"sequence split sp{d.world}"},
            "algorithmic_tflops": flops / (ms / 1e3) / 1e12,
-           # the split's two passes per step, and (one GPU) the direct launch per step
-           "launches": 2 * steps + (steps if d.world == 1 else 0)}
+           # two launches per chunked call: the split's two passes per step, and (one
+           # GPU) the direct call per step
+           "launches": 4 * steps + (2 * steps if d.world == 1 else 0)}
     res.update(extra)
     return res
+
 
 def profile_workload(a):
     """Run one fixed workload ``a.launches`` times on cuda:0 for an ncu capture.

@@ -107,12 +107,20 @@ def auto_local_parts(B: int, T: int, H: int, dv: int, chunk_size: int, device) -
 
 
 def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, parts, fn,
-              gather, world, rank):
+              gather, world, rank, marks=None):
     """Both passes over this rank's tokens split into ``parts`` batched segments.
 
     ``gather`` maps this rank's packed (S, M) pairs [B, parts, H, dk, dv + dk] to
     the list of every rank's, in rank order; segments are ordered rank-major.
+    ``marks`` (a list, or None) receives (phase, CUDA event) pairs recorded on
+    the current stream after each phase: "pass1", "exchange", "fold", "pass2".
     """
+    def mark(name):
+        if marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            marks.append((name, ev))
+
     B, T, _, dk = k.shape
     H, dv = v.shape[2], v.shape[-1]   # value heads (q/k may carry fewer, grouped)
     seg = -(-T // (parts * chunk_size)) * chunk_size          # tokens per segment
@@ -127,21 +135,25 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
 
     qs, ks, vs, gs, bs = (to_segments(x) for x in (q, k, v, g, beta))
     S, M = segment_summary(qs, ks, vs, gs, bs, fn)                      # [B*parts, H, ...]
+    mark("pass1")
     packed = torch.cat([S, M], dim=-1).view(B, parts, H, dk, dv + dk).contiguous()
     allp = torch.cat(gather(packed), dim=1).transpose(0, 1)             # [world*parts, B, H, dk, dv+dk]
+    mark("exchange")
     h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
           if initial_state is None else initial_state.to(S.dtype))
     states = fold_states_scan(h0, allp[..., :dv], allp[..., dv:])      # [world*parts + 1, ...]
     mine = states[rank * parts:(rank + 1) * parts]
     s_in = mine.transpose(0, 1).reshape(B * parts, H, dk, dv).contiguous()
+    mark("fold")
     o, _ = fn(qs, ks, vs, gs, bs, s_in)
+    mark("pass2")
     o = o.reshape(B, Tp, H, dv)[:, :T]
     return (o, states[world * parts]) if output_final_state else (o, None)
 
 
 def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final_state=False,
                               chunk_size=64, group=None, segment_fn: Optional[SegmentFn] = None,
-                              local_parts: Optional[int] = None):
+                              local_parts: Optional[int] = None, marks: Optional[list] = None):
     """Chunked forward with the sequence split across the ranks of ``group``.
 
     Every rank passes its own contiguous segment ``[B, T_p, H, D]`` (rank order =
@@ -155,6 +167,7 @@ def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final
     ``initial_state`` is the state before rank 0's segment and must be the same
     on every rank (or None).  Returns ``(o_segment, final_state or None)``;
     ``final_state`` is the state after the LAST segment, on every rank.
+    ``marks``: see ``_two_pass`` (per-phase CUDA events, for timing).
     """
     import torch.distributed as dist
 
@@ -182,12 +195,13 @@ def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final
         raise ValueError(f"local_parts differs across ranks ({lo} .. {hi}); pass the same value "
                          "on every rank, or None")
     return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, lo, fn,
-                     gather, world, rank)
+                     gather, world, rank, marks)
 
 
 def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_final_state=False,
                                  chunk_size=64, parts: int = 4,
-                                 segment_fn: Optional[SegmentFn] = None):
+                                 segment_fn: Optional[SegmentFn] = None,
+                                 marks: Optional[list] = None):
     """Chunked forward of B long sequences, each split into ``parts`` segments
     that run side by side in the batch dimension of two wide launches.
 
@@ -201,7 +215,7 @@ def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_fi
         o, hT = fn(q, k, v, g, beta, initial_state)
         return (o, hT) if output_final_state else (o, None)
     return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, parts, fn,
-                     lambda packed: [packed], 1, 0)
+                     lambda packed: [packed], 1, 0, marks)
 
 
 __all__ = ["chunk_gated_delta_rule_sp", "chunk_gated_delta_rule_split", "segment_summary",

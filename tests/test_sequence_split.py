@@ -103,6 +103,30 @@ def test_split_cuda_matches_unsplit(cuda, B, T, H, parts):
     assert_close(f64(hT), f64(h_ref), "bf16", "state")
 
 
+@pytest.mark.gpu
+def test_long_context_config_against_oracle(cuda):
+    """The long-context configuration at full length: B=1 T=65536 H=16
+    dk=dv=128, bf16 in, fp32 state.  Two sampled heads over all 65536 tokens
+    (1024 chunks) against the float64 oracle, for the one-call kernel and for
+    the one-GPU sequence split (4 segments): the drift of the bf16-rounded
+    state operand over the whole sequence stays inside the bf16 bar."""
+    from helpers import assert_close, device_inputs_fast, f64
+    from gated_deltanet_jax_b200 import ops
+    B, T, H = 1, 65536, 16
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, 128, seed=4, dtype="bf16", dev=cuda,
+                                           h0_std=0.02)
+    o1, h1 = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    o2, h2 = sp.chunk_gated_delta_rule_split(q, k, v, g, b, initial_state=h0,
+                                             output_final_state=True, parts=4)
+    for h in (0, 11):
+        host = [f64(t[:, :, h:h + 1]) for t in (q, k, v, g, b)]
+        ro, rh = orc.chunk_exact(*host, f64(h0[:, h:h + 1]), 64)
+        for name, o, hT in (("one call", o1, h1), ("split", o2, h2)):
+            assert_close(f64(o[:, :, h:h + 1]), ro, "bf16", f"{name} head {h} o")
+            assert_close(f64(hT[:, h:h + 1]), rh, "bf16", f"{name} head {h} state")
+    assert torch.isfinite(o1.float()).all() and torch.isfinite(o2.float()).all()
+
+
 @pytest.mark.parametrize("P", [1, 2, 3, 5, 8, 9])
 def test_scan_fold_equals_sequential_fold(P):
     """The log-depth prefix scan gives the sequential fold's states."""
