@@ -847,13 +847,19 @@ def long_context_leg(d, a):
         extra.update({"split_ms_per_step": ms, "unsplit_ms_per_step": ms_d})
         if ms_d < ms:
             ms, path = ms_d, "one launch (no split)"
-    # correctness of the split against one unsplit launch (outside the timed region)
+    # Correctness of the split against one unsplit launch (outside the timed
+    # region).  The workload's gates decay the state by about e^-51 per chunk, so
+    # almost nothing crosses a segment boundary; the check therefore runs on the
+    # same inputs with gates 50x milder (about e^-1 per chunk), whose state spans
+    # every boundary.
+    full[3] = full[3] * 0.02
+    g = full[3][:, sl].contiguous()
     o_s, h_s = split()
     o_ref, h_ref = direct()
     rel = lambda x, r: float((x.float() - r.float()).abs().max() / r.float().abs().max())  # noqa: E731
     extra["max_rel_err"] = {"o": d.max(rel(o_s, o_ref[:, sl])), "state": d.max(rel(h_s, h_ref)),
                             "against": "one unsplit launch over the whole sequence (every rank, "
-                                       "its own segment of o; max over ranks)"}
+                                       "its own segment of o; max over ranks), gates x 0.02"}
     flops = T * H * rl.flops_chunk_per_token_head(dk, dv, C)
     res = {"metric": "long-context chunk prefill tokens/s", "value": B * T / (ms / 1e3),
            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",

@@ -450,9 +450,13 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                   const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
                   const float* __restrict__ beta, const unsigned char* __restrict__ ws,
                   const float* h0, __nv_bfloat16* __restrict__ o, float* hT, int T, int H,
-                  int Hk, int dv) {
+                  int Hk, int dv, int ds) {
   // (h0 and hT may be the same array: each CTA reads its tile of h0 before it
   // writes the same tile of hT)
+  // The state has ds columns: dv of them follow v (and give o); with ds = dv +
+  // dk the last dk are the transition, the same recurrence started from the
+  // identity with v = 0 (no V loads, no output, h0 unused there).  o may be
+  // NULL (no output stored).
   using L = ScanLay;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -466,6 +470,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
   const int b = bh / H, h = bh - b * H;
   const int hq = h * Hk / H;
   const int c0 = blockIdx.x * DVT;
+  const bool trans = c0 >= dv;  // a transition tile
   const int N = (T + C - 1) / C;
 
   if (tid == 0) {
@@ -501,6 +506,11 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(sm);
+  // Launched with programmatic stream serialization, the set-up above may
+  // overlap the previous kernel on the stream; everything below reads memory
+  // that kernel may write (the workspace after the preparation; h0, q, k, v, g,
+  // beta after any other), so every thread waits for it to complete here.
+  griddep_wait();
 
   if (warp == 0) {
     // ---- K, Q, V of each chunk (TMA) ----
@@ -514,12 +524,12 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         if (n >= NS && !mbar_wait(&bars[S_EMPTY + s], (uint32_t)((n / NS) - 1) & 1u)) break;
         unsigned char* kq = sm + L::SM_KQ + s * 32768;
         uint64_t* fb = &bars[S_FULL + s];
-        mbar_arrive_expect_tx(fb, 32768 + 8192);
+        mbar_arrive_expect_tx(fb, 32768 + (trans ? 0 : 8192));
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_4d(kq + kb * 16384, &tmK, 64 * kb, hq, n * C, b, fb);
           tma_load_4d(kq + kb * 16384 + 8192, &tmQ, 64 * kb, hq, n * C, b, fb);
         }
-        tma_load_4d(sm + L::SM_V + s * 8192, &tmV, c0, h, n * C, b, fb);
+        if (!trans) tma_load_4d(sm + L::SM_V + s * 8192, &tmV, c0, h, n * C, b, fb);
         issued = n + 1;
       }
       // every issued load lands before the CTA can exit (bounded)
@@ -604,8 +614,6 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
   } else if (warp == 3) {
     // ---- preparation tiles (bulk copies from the workspace) ----
     if (elect_one()) {
-      // the preparation grid's writes are complete and visible past this point
-      griddep_wait();
       const unsigned char* src = ws + (size_t)bh * N * kTileBytes;
       int issued = 0;
       for (int n = 0; n < N; ++n) {
@@ -628,12 +636,16 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     unsigned char* Stile = sm + L::SM_S;
     float S[32];
     {
-      const float* src = h0 ? h0 + ((size_t)bh * DK + r) * dv + c0 + cb : nullptr;
+      const float* src = h0 && !trans ? h0 + ((size_t)bh * DK + r) * ds + c0 + cb : nullptr;
 #pragma unroll
       for (int c = 0; c < 32; c += 4) {
         const float4 x = src ? *reinterpret_cast<const float4*>(src + c)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
         S[c] = x.x; S[c + 1] = x.y; S[c + 2] = x.z; S[c + 3] = x.w;
+      }
+      if (trans) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) S[c] = (c0 - dv + cb + c == r) ? 1.f : 0.f;
       }
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8)
@@ -662,7 +674,12 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
           float vv[8], x[8];
-          unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(r, cb / 8 + c8)), vv);
+          if (trans) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vv[e] = 0.f;
+          } else {
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(r, cb / 8 + c8)), vv);
+          }
 #pragma unroll
           for (int e = 0; e < 8; ++e) x[e] = bi * (vv[e] - egi * ks[8 * c8 + e]);
           *reinterpret_cast<uint4*>(sm + L::SM_X + sw128(r, cb / 8 + c8)) = pack_bf16x8(x);
@@ -698,14 +715,15 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         const int i = r - 64, t = n * C + i;
         float qs[16], pv[16];
         const float egi = vb.eG[i];
-        __nv_bfloat16* orow = o + (((size_t)b * T + t) * H + h) * dv + c0 + cb;
+        __nv_bfloat16* orow =
+            o && !trans ? o + (((size_t)b * T + t) * H + h) * dv + c0 + cb : nullptr;
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
           tmem_ld16x2(d1 + 16 * q2, tmem + ST_D2 + (uint32_t)cb + lane_off + 16 * q2, qs, pv);
           float out[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) out[e] = fmaf(egi, qs[e], pv[e]);
-          if (t < T) {
+          if (t < T && orow) {
             *reinterpret_cast<uint4*>(orow + 16 * q2) = pack_bf16x8(out);
             *reinterpret_cast<uint4*>(orow + 16 * q2 + 8) = pack_bf16x8(out + 8);
           }
@@ -721,7 +739,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       if (lane == 0) mbar_arrive(&bars[S_VEMPTY + v]);
     }
     if (ok && hT) {
-      float* dst = hT + ((size_t)bh * DK + r) * dv + c0 + cb;
+      float* dst = hT + ((size_t)bh * DK + r) * ds + c0 + cb;
 #pragma unroll
       for (int c = 0; c < 32; c += 4)
         *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
@@ -760,36 +778,54 @@ size_t chunk_scan_workspace_bytes(int B, int T, int H) {
   return (size_t)B * H * N * kTileBytes;
 }
 
-cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st) {
+namespace {
+
+// TMA maps of q and k (dk = 128) over the dense rows.
+bool qk_maps(const ChunkArgs& a, CUtensorMap* mk, CUtensorMap* mq) {
+  return make_bf16_map_4d(mk, a.k, a.B, a.T, a.Hk, DK) &&
+         make_bf16_map_4d(mq, a.q, a.B, a.T, a.Hk, DK);
+}
+
+bool workspace_ok(const ChunkArgs& a) {
+  return a.workspace && a.ws_bytes >= chunk_scan_workspace_bytes(a.B, a.T, a.H) &&
+         (reinterpret_cast<uintptr_t>(a.workspace) & 15u) == 0;
+}
+
+}  // namespace
+
+cudaError_t launch_chunk_prepare(const ChunkArgs& a, cudaStream_t st) {
   if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
-  if (!chunk_scan_supported(a) || !a.workspace ||
-      a.ws_bytes < chunk_scan_workspace_bytes(a.B, a.T, a.H) ||
-      (reinterpret_cast<uintptr_t>(a.workspace) & 15u))
-    return cudaErrorInvalidValue;
-  CUtensorMap mk, mq, mv;
-  if (!make_bf16_map_4d(&mk, a.k, a.B, a.T, a.Hk, DK) ||
-      !make_bf16_map_4d(&mq, a.q, a.B, a.T, a.Hk, DK) ||
-      !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv))
-    return cudaErrorInvalidValue;
+  if (!chunk_scan_supported(a) || !workspace_ok(a)) return cudaErrorInvalidValue;
+  CUtensorMap mk, mq;
+  if (!qk_maps(a, &mk, &mq)) return cudaErrorInvalidValue;
   static std::atomic<int> prep_slot[kMaxDevices] = {};
-  static std::atomic<int> scan_slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(chunk_prep_kernel, PrepLay::SMEM_BYTES, prep_slot);
-  if (e != cudaSuccess) return e;
-  e = ensure_smem(chunk_scan_kernel, ScanLay::SMEM_BYTES, scan_slot);
   if (e != cudaSuccess) return e;
   const int N = (a.T + C - 1) / C;
   const long long items = (long long)a.B * a.H * N;
   const int prep_ctas = (int)(items < 2LL * device_sm_count() ? items : 2LL * device_sm_count());
-  unsigned char* ws = static_cast<unsigned char*>(a.workspace);
   chunk_prep_kernel<<<prep_ctas, kPrepThreads, PrepLay::SMEM_BYTES, st>>>(
-      mk, mq, a.g, a.beta, ws, a.T, a.H, a.Hk, a.B * a.H, N);
-  e = cudaGetLastError();
+      mk, mq, a.g, a.beta, static_cast<unsigned char*>(a.workspace), a.T, a.H, a.Hk,
+      a.B * a.H, N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cudaStream_t st) {
+  if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_scan_supported(a) || !workspace_ok(a)) return cudaErrorInvalidValue;
+  CUtensorMap mk, mq, mv;
+  if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv))
+    return cudaErrorInvalidValue;
+  static std::atomic<int> scan_slot[kMaxDevices] = {};
+  cudaError_t e = ensure_smem(chunk_scan_kernel, ScanLay::SMEM_BYTES, scan_slot);
   if (e != cudaSuccess) return e;
-  // The scan is launched behind the preparation with programmatic stream
-  // serialization: its set-up overlaps the preparation's last wave, and its
-  // reads of the workspace wait for the whole preparation grid (griddep_wait).
+  const int ds = a.dv + (transition ? DK : 0);
+  // Launched with programmatic stream serialization: when the preparation runs
+  // right before on the stream, the scan's set-up overlaps the preparation's
+  // last wave, and its reads of the workspace wait for the whole preparation
+  // grid (griddep_wait); otherwise this is an ordinary launch.
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.dv / DVT, a.B * a.H);
+  cfg.gridDim = dim3(ds / DVT, a.B * a.H);
   cfg.blockDim = dim3(kScanThreads);
   cfg.dynamicSmemBytes = ScanLay::SMEM_BYTES;
   cfg.stream = st;
@@ -799,10 +835,16 @@ cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, chunk_scan_kernel, mk, mq, mv, a.g, a.beta,
-                         static_cast<const unsigned char*>(ws), a.h0,
-                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv);
+                         static_cast<const unsigned char*>(a.workspace), a.h0,
+                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv, ds);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st) {
+  cudaError_t e = launch_chunk_prepare(a, st);
+  if (e != cudaSuccess) return e;
+  return launch_chunk_scan_prepared(a, false, st);
 }
 
 }  // namespace gdn

@@ -170,6 +170,35 @@ size_t chunk_workspace(int B, int T, int H, int dk, int dv, int chunk, int dtype
   return gdn::chunk_fwd_warp_workspace_bytes(B, T, H, dk, dv, n_seqs);
 }
 
+// Arguments of the two-phase chunked forward (gdn_chunk_prepare / gdn_chunk_scan):
+// bf16, dk = 128, dv a multiple of 64 (v may be NULL for the preparation), dense
+// rows, a workspace of gdn_chunk_workspace_bytes(); T > 0 and B * H > 0.
+int check_two_phase(const void* q, const void* k, const void* v, const float* g,
+                    const float* beta, int B, int T, int H, int Hk, int dk, int dv, int dtype,
+                    const void* workspace, size_t ws_bytes) {
+  if (B <= 0 || T <= 0 || H <= 0)
+    return fail(GDN_ERR_INVALID, "the two-phase form needs B, T, H > 0 (B=%d T=%d H=%d)", B, T, H);
+  if (dtype != GDN_DTYPE_BF16 || dk != 128 || dv % 64 || dv <= 0 || dv > 512)
+    return fail(GDN_ERR_UNSUPPORTED, "the two-phase form covers bf16 inputs with dk = 128 and "
+                "dv a multiple of 64 up to 512 (dtype=%d dk=%d dv=%d)", dtype, dk, dv);
+  int rc = check_groups(H, Hk);
+  if (rc) return rc;
+  if ((long long)B * H > 65535)
+    return fail(GDN_ERR_UNSUPPORTED, "B*H=%lld heads exceed 65535", (long long)B * H);
+  const void* ptrs[4] = {q, k, g, beta};
+  const char* names[4] = {"q", "k", "g", "beta"};
+  for (int i = 0; i < 4; ++i) {
+    if (!ptrs[i]) return fail(GDN_ERR_INVALID, "%s must be non-NULL", names[i]);
+    if (!aligned16(ptrs[i])) return fail(GDN_ERR_INVALID, "%s is not 16-byte aligned", names[i]);
+  }
+  if (v && !aligned16(v)) return fail(GDN_ERR_INVALID, "v is not 16-byte aligned");
+  const size_t need = gdn::chunk_scan_workspace_bytes(B, T, H);
+  if (!workspace || ws_bytes < need)
+    return fail(GDN_ERR_INVALID, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  if (!aligned16(workspace)) return fail(GDN_ERR_INVALID, "workspace is not 16-byte aligned");
+  return GDN_OK;
+}
+
 // The chunked layer form, dense (cu_seqlens NULL: B rows of T tokens) or packed
 // (B = n_seqs sequences in one row of T tokens).
 int chunk_fwd_layer(const void* q, const void* k, const void* v, const float* a,
@@ -477,6 +506,42 @@ int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v, const flo
   return gdn_chunk_bwd(q, k, v, g, beta, h0, dO, dhT, dq, dk_out, dv_out, dg, dbeta, dh0, B, T,
                        H, Hk, dk, dv, dtype, scratch,
                        scratch ? (size_t)GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES : 0, stream);
+}
+
+int gdn_chunk_prepare(const void* q, const void* k, const float* g, const float* beta, int B,
+                      int T, int H, int Hk, int dk, int dtype, void* workspace, size_t ws_bytes,
+                      void* stream) {
+  g_err[0] = '\0';
+  int rc = check_two_phase(q, k, nullptr, g, beta, B, T, H, Hk, dk, 64, dtype, workspace,
+                           ws_bytes);
+  if (rc) return rc;
+  gdn::ChunkArgs a{q, k, nullptr, g, beta, nullptr, nullptr, nullptr, B, T, H, dk, 64, 64,
+                   dtype, GDN_SEMANTICS_EXACT, workspace, ws_bytes, Hk};
+  return cuda_status(gdn::launch_chunk_prepare(a, (cudaStream_t)stream), "gdn_chunk_prepare");
+}
+
+int gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g,
+                   const float* beta, const float* h0, void* o, float* hT, int B, int T, int H,
+                   int Hk, int dk, int dv, int dtype, int transition, const void* workspace,
+                   size_t ws_bytes, void* stream) {
+  g_err[0] = '\0';
+  int rc = check_two_phase(q, k, v, g, beta, B, T, H, Hk, dk, dv, dtype, workspace, ws_bytes);
+  if (rc) return rc;
+  if (transition != 0 && transition != 1)
+    return fail(GDN_ERR_INVALID, "transition must be 0 or 1 (got %d)", transition);
+  if (transition && h0)
+    return fail(GDN_ERR_INVALID, "with transition, the state starts from [0 | I]: h0 must be NULL");
+  if (transition && !hT)
+    return fail(GDN_ERR_INVALID, "with transition, hT ([B,H,dk,dv+dk]) must be non-NULL");
+  const void* ptrs[3] = {h0, o, hT};
+  const char* names[3] = {"h0", "o", "hT"};
+  for (int i = 0; i < 3; ++i)
+    if (ptrs[i] && !aligned16(ptrs[i]))
+      return fail(GDN_ERR_INVALID, "%s is not 16-byte aligned", names[i]);
+  gdn::ChunkArgs a{q, k, v, g, beta, h0, o, hT, B, T, H, dk, dv, 64, dtype, GDN_SEMANTICS_EXACT,
+                   const_cast<void*>(workspace), ws_bytes, Hk};
+  return cuda_status(gdn::launch_chunk_scan_prepared(a, transition != 0, (cudaStream_t)stream),
+                     "gdn_chunk_scan");
 }
 
 const char* gdn_last_error(void) { return g_err; }

@@ -176,7 +176,13 @@ cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaS
 bool chunk_scan_shape_ok(const ChunkArgs& a);    // the shapes it takes (no device query)
 bool chunk_scan_supported(const ChunkArgs& a);   // ... and the driver can encode TMA maps
 size_t chunk_scan_workspace_bytes(int B, int T, int H);
-cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st);
+cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st);   // both launches
+// The two launches on their own: the preparation of (q, k, g, beta) into the
+// workspace, and the scan over a prepared workspace (a.o may be NULL; with
+// transition, the state -- a.hT, [B,H,dk,dv+dk] -- gains dk columns that start
+// from the identity with v = 0, and a.h0 must be NULL).
+cudaError_t launch_chunk_prepare(const ChunkArgs& a, cudaStream_t st);
+cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cudaStream_t st);
 int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
 int chunk_scan_binary_version();

@@ -268,6 +268,53 @@ def _chunk_impl(q, k, v, g, beta, initial_state, output_final_state, chunk_size,
     return o, hT
 
 
+def _two_phase_ok(q, k, v) -> bool:
+    """Whether gdn_chunk_prepare / gdn_chunk_scan take these tensors (bf16, dk =
+    128, dv a multiple of 64 up to 512, dense rows on a CUDA device)."""
+    return (isinstance(q, torch.Tensor) and q.is_cuda and q.dim() == 4
+            and q.dtype == torch.bfloat16 and k.dtype == q.dtype and v.dtype == q.dtype
+            and q.shape[-1] == 128 and v.shape[-1] % 64 == 0 and 0 < v.shape[-1] <= 512
+            and q.shape[0] * v.shape[2] <= 65535 and q.shape[1] > 0 and q.shape[0] > 0)
+
+
+def _chunk_prepare(q, k, g, beta):
+    """gdn_chunk_prepare: the per-chunk operands of (q, k, g, beta) in a new
+    workspace (uint8 CUDA tensor) for _chunk_scan."""
+    B, T, Hk, dk = q.shape
+    H = g.shape[2]
+    lib = _lib.load()
+    ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, dk, 64, 64, _lib.GDN_DTYPE_BF16,
+                                             _lib.GDN_SEMANTICS_EXACT)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.gdn_chunk_prepare(_ptr(q), _ptr(k), _ptr(g), _ptr(beta), B, T, H, Hk, dk,
+                                   _lib.GDN_DTYPE_BF16, _ptr(ws), ws_bytes,
+                                   torch.cuda.current_stream(q.device).cuda_stream)
+    _lib.check(rc, "gdn_chunk_prepare")
+    return ws
+
+
+def _chunk_scan(q, k, v, g, beta, ws, initial_state=None, transition=False, output=True):
+    """gdn_chunk_scan over a workspace from _chunk_prepare of the same q, k, g,
+    beta.  Returns (o or None, final state); with ``transition`` the final
+    state is [B,H,dk,dv+dk]: the end state from a zero start, then the
+    transition matrix (initial_state must be None)."""
+    B, T, Hk, dk = q.shape
+    H, dv = v.shape[2], v.shape[3]
+    hT = torch.empty((B, H, dk, dv + (dk if transition else 0)), dtype=torch.float32,
+                     device=q.device)
+    o = torch.empty((B, T, H, dv), dtype=v.dtype, device=q.device) if output else None
+    h0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        rc = lib.gdn_chunk_scan(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0),
+                                _ptr(o), _ptr(hT), B, T, H, Hk, dk, dv, _lib.GDN_DTYPE_BF16,
+                                int(bool(transition)), _ptr(ws), ws.numel(),
+                                torch.cuda.current_stream(q.device).cuda_stream)
+    _lib.check(rc, "gdn_chunk_scan")
+    return o, hT
+
+
 def fused_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None,
                                      output_final_state=False, *,
                                      final_state_out: Optional[torch.Tensor] = None

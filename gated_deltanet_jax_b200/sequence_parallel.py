@@ -24,7 +24,10 @@ Two placements of the segments:
   wide launches.
 
 Both are exact (same math as the unsplit op, up to rounding).  The per-segment
-work runs through ``segment_fn`` -- by default the CUDA chunked op.
+work runs through ``segment_fn`` -- by default the CUDA chunked op, whose
+two-phase form (gdn_chunk_prepare, then gdn_chunk_scan) lets both passes share
+one per-chunk preparation and lets pass 1 take the transition columns without
+materialising [v | 0] or [0 | I].
 """
 
 from __future__ import annotations
@@ -134,7 +137,21 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
         return x.reshape((B * parts, seg) + tuple(x.shape[2:])).contiguous()
 
     qs, ks, vs, gs, bs = (to_segments(x) for x in (q, k, v, g, beta))
-    S, M = segment_summary(qs, ks, vs, gs, bs, fn)                      # [B*parts, H, ...]
+    # On the CUDA op (no segment_fn given) with its two-phase form available, the
+    # per-chunk preparation runs once for both passes, and pass 1 needs neither
+    # [v | 0] nor [0 | I] in memory, nor an output: the scan's transition
+    # columns start from the identity with v = 0 by themselves.
+    ws = None
+    if fn is None:
+        qs, ks, vs, gs, bs = (x.contiguous() for x in (qs, ks, vs, gs.float(), bs.float()))
+        if ops._two_phase_ok(qs, ks, vs):
+            ws = ops._chunk_prepare(qs, ks, gs, bs)
+            _, ext = ops._chunk_scan(qs, ks, vs, gs, bs, ws, transition=True, output=False)
+            S, M = ext[..., :dv], ext[..., dv:]
+        else:
+            fn = _default_segment_fn(chunk_size)
+    if ws is None:
+        S, M = segment_summary(qs, ks, vs, gs, bs, fn)                  # [B*parts, H, ...]
     mark("pass1")
     packed = torch.cat([S, M], dim=-1).view(B, parts, H, dk, dv + dk).contiguous()
     allp = torch.cat(gather(packed), dim=1).transpose(0, 1)             # [world*parts, B, H, dk, dv+dk]
@@ -145,7 +162,10 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
     mine = states[rank * parts:(rank + 1) * parts]
     s_in = mine.transpose(0, 1).reshape(B * parts, H, dk, dv).contiguous()
     mark("fold")
-    o, _ = fn(qs, ks, vs, gs, bs, s_in)
+    if ws is not None:
+        o, _ = ops._chunk_scan(qs, ks, vs, gs, bs, ws, initial_state=s_in)
+    else:
+        o, _ = fn(qs, ks, vs, gs, bs, s_in)
     mark("pass2")
     o = o.reshape(B, Tp, H, dv)[:, :T]
     return (o, states[world * parts]) if output_final_state else (o, None)
@@ -171,7 +191,7 @@ def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final
     """
     import torch.distributed as dist
 
-    fn = segment_fn or _default_segment_fn(chunk_size)
+    fn = segment_fn   # None: the CUDA op (its two-phase form where it applies)
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
 
@@ -209,10 +229,10 @@ def chunk_gated_delta_rule_split(q, k, v, g, beta, initial_state=None, output_fi
     ``parts * chunk_size``; padded tokens leave the state unchanged.  Returns
     ``(o, final_state or None)`` like the unsplit op.
     """
-    fn = segment_fn or _default_segment_fn(chunk_size)
+    fn = segment_fn   # None: the CUDA op (its two-phase form where it applies)
     T = k.shape[1]
     if parts <= 1 or T <= chunk_size:
-        o, hT = fn(q, k, v, g, beta, initial_state)
+        o, hT = (fn or _default_segment_fn(chunk_size))(q, k, v, g, beta, initial_state)
         return (o, hT) if output_final_state else (o, None)
     return _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, parts, fn,
                      lambda packed: [packed], 1, 0, marks)

@@ -281,6 +281,31 @@ size_t gdn_chunk_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv
  */
 int gdn_device_error(int clear);
 
+/*
+ * The chunked forward's two launches on their own (bf16 inputs, dk = 128, dv a
+ * multiple of 64, exact semantics, dense rows): gdn_chunk_prepare computes the
+ * per-chunk operands that depend on q, k, g and beta only (the triangular
+ * solve of each chunk, ops.py:249-297) into `workspace`
+ * (gdn_chunk_workspace_bytes() for this shape); gdn_chunk_scan then runs the
+ * sequential scan over chunks (the lax.scan of ops.py:322-341) for any v and
+ * initial state, reading that workspace.  gdn_chunk_fwd is the two in a row.
+ * A caller that scans the same q, k, g, beta more than once -- the two passes
+ * of a sequence split -- prepares once.
+ *
+ * gdn_chunk_scan: o may be NULL (no output stored).  transition = 1 adds dk
+ * state columns that run the same recurrence from the identity with v = 0, so
+ * hT ([B,H,dk,dv+dk], required) holds the segment's end state from h0 = 0 and
+ * its transition matrix side by side (h0 must then be NULL).  No counterpart
+ * in the reference, whose chunk path is one jitted function.
+ */
+int gdn_chunk_prepare(const void* q, const void* k, const float* g, const float* beta, int B,
+                      int T, int H, int Hk, int dk, int dtype, void* workspace, size_t ws_bytes,
+                      void* stream);
+int gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g,
+                   const float* beta, const float* h0, void* o, float* hT, int B, int T, int H,
+                   int Hk, int dk, int dv, int dtype, int transition, const void* workspace,
+                   size_t ws_bytes, void* stream);
+
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
@@ -299,7 +324,8 @@ void gdn_reload_kernel_overrides(void);
  * 1.5: the layer form of the decode step; 1.6: the layer form of the chunked
  * forward; 1.7: dk = 256 on the tensor cores, the chunked forward's workspace
  * for fp32 inputs, gdn_chunk_varlen_workspace_bytes; 1.8: the two-launch chunked
- * forward and its workspace (bf16, dk = 128), gdn_reload_kernel_overrides). */
+ * forward and its workspace (bf16, dk = 128), gdn_chunk_prepare / gdn_chunk_scan,
+ * gdn_reload_kernel_overrides, gdn_binary_version). */
 int gdn_abi_version(void);
 
 /*

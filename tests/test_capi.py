@@ -295,3 +295,30 @@ def test_config_defaults_match_reference():
             c.num_hidden_layers, c.norm_eps, c.vocab_size) == \
         ("chunk", 2048, 256, 6, 2.0, 4, 21, 1e-6, 32000)
     assert c.num_v_heads is None and c.use_gate and c.use_short_conv
+
+
+def test_two_phase_entry_points_check_arguments_on_the_host(lib):
+    """gdn_chunk_prepare / gdn_chunk_scan refuse, before any CUDA call: shapes
+    outside bf16 dk=128 dv%64, a missing or short workspace, a transition scan
+    with an initial state or without hT, unaligned pointers."""
+    p = ctypes.c_void_p(16)
+    bf16 = _lib.GDN_DTYPE_BF16
+    need = lib.gdn_chunk_workspace_bytes(1, 64, 2, 128, 64, 64, bf16, 0)
+    assert need == 2 * 24576
+    prep = lambda dk=128, dtype=bf16, ws=p, nb=need: lib.gdn_chunk_prepare(  # noqa: E731
+        p, p, p, p, 1, 64, 2, 2, dk, dtype, ws, nb, None)
+    assert prep(dk=64) == _lib.GDN_ERR_UNSUPPORTED
+    assert prep(dtype=_lib.GDN_DTYPE_FP32) == _lib.GDN_ERR_UNSUPPORTED
+    assert prep(ws=None) == _lib.GDN_ERR_INVALID and b"workspace" in lib.gdn_last_error()
+    assert prep(nb=need - 1) == _lib.GDN_ERR_INVALID
+    assert prep(ws=ctypes.c_void_p(24)) == _lib.GDN_ERR_INVALID
+
+    def scan(h0=None, hT=p, transition=1, dv=64, o=None, q=p):
+        return lib.gdn_chunk_scan(q, p, p, p, p, h0, o, hT, 1, 64, 2, 2, 128, dv, bf16,
+                                  transition, p, need, None)
+    assert scan(h0=p) == _lib.GDN_ERR_INVALID and b"h0 must be NULL" in lib.gdn_last_error()
+    assert scan(hT=None) == _lib.GDN_ERR_INVALID
+    assert scan(transition=2) == _lib.GDN_ERR_INVALID
+    assert scan(dv=96) == _lib.GDN_ERR_UNSUPPORTED
+    assert scan(transition=0, o=ctypes.c_void_p(40)) == _lib.GDN_ERR_INVALID
+    assert scan(q=None) == _lib.GDN_ERR_INVALID

@@ -89,12 +89,17 @@ def test_split_across_gloo_ranks_matches_oracle(world, local_parts):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("gscale", [1.0, 0.02])
 @pytest.mark.parametrize("B,T,H,parts", [(1, 4096, 4, 4), (2, 1000, 2, 3), (1, 8192, 2, 8)])
-def test_split_cuda_matches_unsplit(cuda, B, T, H, parts):
+def test_split_cuda_matches_unsplit(cuda, B, T, H, parts, gscale):
+    """gscale 1: the configurations' gates (about e^-51 per chunk, so little
+    state crosses a segment boundary); 0.02: about e^-1 per chunk, so the
+    hand-off carries real state over every boundary."""
     from helpers import assert_close, device_inputs_fast, f64
     from gated_deltanet_jax_b200 import ops
     q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, 128, seed=T, dtype="bf16", dev=cuda,
                                            h0_std=0.02)
+    g = (g * gscale).contiguous()
     o_ref, h_ref = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0,
                                               output_final_state=True)
     o, hT = sp.chunk_gated_delta_rule_split(q, k, v, g, b, initial_state=h0,
@@ -115,6 +120,10 @@ def test_long_context_config_against_oracle(cuda):
     B, T, H = 1, 65536, 16
     q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, 128, seed=4, dtype="bf16", dev=cuda,
                                            h0_std=0.02)
+    # half of the heads with the configuration's gates, half with gates 50x
+    # milder (about e^-1 per chunk), whose state spans many chunks and every
+    # segment boundary of the split
+    g = torch.cat([g[:, :, :8], g[:, :, 8:] * 0.02], dim=2).contiguous()
     o1, h1 = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
     o2, h2 = sp.chunk_gated_delta_rule_split(q, k, v, g, b, initial_state=h0,
                                              output_final_state=True, parts=4)
@@ -155,6 +164,7 @@ def _nccl_worker(rank, world, port, results):
         T = 2048 * world
         q, k, v, g, b, h0 = device_inputs_fast(1, T, 4, 128, 128, seed=3, dtype="bf16", dev=dev,
                                                h0_std=0.02)
+        g = (g * 0.02).contiguous()   # mild gates: state crosses the rank boundary
         seg = T // world
         sl = slice(rank * seg, (rank + 1) * seg)
         o, hT = sp.chunk_gated_delta_rule_sp(q[:, sl], k[:, sl], v[:, sl], g[:, sl], b[:, sl],
@@ -211,3 +221,33 @@ def test_split_ranks_agree_on_local_parts_with_a_shorter_last_rank():
         for r in range(world):
             eo, eh = results[r]
             assert eo < 1e-10 and eh < 1e-10, (r, eo, eh)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,T,H,Hk,dv", [(2, 300, 4, 2, 128), (1, 1000, 2, 2, 64), (3, 64, 2, 1, 192)])
+def test_two_phase_scan_transition_is_the_segment_map(cuda, B, T, H, Hk, dv):
+    """gdn_chunk_scan's transition columns: [S | M] with hT(h0) = M h0 + S for
+    the scan of the same segment from h0 (mild gates, so M is far from zero);
+    one preparation serves both scans, and a scan with an output equals the
+    one-call forward."""
+    from helpers import assert_close, device_inputs_fast, f64
+    from gated_deltanet_jax_b200 import ops
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, dv, seed=T + dv, dtype="bf16",
+                                           dev=cuda, h0_std=0.05)
+    q, k = q[:, :, ::H // Hk].contiguous(), k[:, :, ::H // Hk].contiguous()
+    g = (g * 0.02).contiguous()
+    ws = ops._chunk_prepare(q, k, g, b)
+    none, ext = ops._chunk_scan(q, k, v, g, b, ws, transition=True, output=False)
+    assert none is None and ext.shape == (B, H, 128, dv + 128)
+    S, M = ext[..., :dv], ext[..., dv:]
+    o2, h2 = ops._chunk_scan(q, k, v, g, b, ws, initial_state=h0)
+    o1, h1 = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
+    assert_close(f64(M @ h0 + S), f64(h1), "bf16", "M h0 + S")
+    # (the map's linear part, which the hand-off carries, against the float64
+    # recurrence started from the identity with v = 0, for one head)
+    from oracle import gdn_oracle as orc
+    eye = np.broadcast_to(np.eye(128), (1, 1, 128, 128)).copy()
+    _, rM = orc.recurrent_ref(f64(q[:1, :, :1]), f64(k[:1, :, :1]), np.zeros((1, T, 1, 128)),
+                              f64(g[:1, :, :1]), f64(b[:1, :, :1]), eye)
+    assert_close(f64(M[:1, :1]), rM, "bf16", "transition vs oracle")
