@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_varlen_workspace_bytes",
     "gdn_chunk_prepare",
     "gdn_chunk_scan",
+    "gdn_fold_states",
     "gdn_last_error",
     "gdn_reload_kernel_overrides",
     "gdn_device_error",
@@ -109,6 +110,8 @@ def _declare(lib):
     lib.gdn_chunk_prepare.restype = _i
     lib.gdn_chunk_scan.argtypes = [_vp] * 8 + [_i] * 8 + [_vp, _sz, _vp]
     lib.gdn_chunk_scan.restype = _i
+    lib.gdn_fold_states.argtypes = [_vp] * 4 + [_i] * 5 + [_vp]
+    lib.gdn_fold_states.restype = _i
     lib.gdn_last_error.argtypes = []
     lib.gdn_last_error.restype = ctypes.c_char_p
     lib.gdn_reload_kernel_overrides.argtypes = []

@@ -544,6 +544,29 @@ int gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g,
                      "gdn_chunk_scan");
 }
 
+int gdn_fold_states(const float* S, const float* M, const float* h0, float* out, int P, int BH,
+                    int dk, int dv, int ld, void* stream) {
+  g_err[0] = '\0';
+  if (P < 0 || BH < 0) return fail(GDN_ERR_INVALID, "negative P=%d or BH=%d", P, BH);
+  if (!gdn::state_fold_supported(dk, dv))
+    return fail(GDN_ERR_UNSUPPORTED, "the fold covers dk = 128 and dv a multiple of 32 "
+                "(dk=%d dv=%d)", dk, dv);
+  if (ld % 4 || ld < dv || ld < dk)
+    return fail(GDN_ERR_INVALID, "row stride ld=%d must be a multiple of 4 and >= dv, dk", ld);
+  if ((long long)BH > 65535) return fail(GDN_ERR_UNSUPPORTED, "BH=%d exceeds 65535", BH);
+  if (BH == 0) return GDN_OK;
+  if (!out || (P > 0 && (!S || !M)))
+    return fail(GDN_ERR_INVALID, "out (and S, M when P > 0) must be non-NULL");
+  const void* ptrs[4] = {S, M, h0, out};
+  const char* names[4] = {"S", "M", "h0", "out"};
+  for (int i = 0; i < 4; ++i)
+    if (ptrs[i] && !aligned16(ptrs[i]))
+      return fail(GDN_ERR_INVALID, "%s is not 16-byte aligned", names[i]);
+  return cuda_status(gdn::launch_state_fold(S, M, h0, out, P, BH, dk, dv, ld,
+                                            (cudaStream_t)stream),
+                     "gdn_fold_states");
+}
+
 const char* gdn_last_error(void) { return g_err; }
 
 void gdn_reload_kernel_overrides(void) {

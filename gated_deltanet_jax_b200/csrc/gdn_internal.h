@@ -187,6 +187,12 @@ int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
 int chunk_scan_binary_version();
 
+// The sequence split's hand-off: out[0] = h0, out[p + 1] = M_p out[p] + S_p for
+// P segments of BH heads (dk = 128, dv % 32 == 0; S, M rows of `ld` floats).
+bool state_fold_supported(int dk, int dv);
+cudaError_t launch_state_fold(const float* S, const float* M, const float* h0, float* out, int P,
+                              int BH, int dk, int dv, int ld, cudaStream_t st);
+
 // The chunked forward on the backward's warp-level tensor-core kernels (exact
 // semantics, dk in 16..256, dv % 32 == 0, dense or packed): fp32 inputs, and
 // the bf16 shapes the tcgen05 kernel does not take.  Needs a device workspace

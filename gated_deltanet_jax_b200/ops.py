@@ -315,6 +315,24 @@ def _chunk_scan(q, k, v, g, beta, ws, initial_state=None, transition=False, outp
     return o, hT
 
 
+def _fold_states(packed, h0, dv):
+    """gdn_fold_states over the gathered summaries ``packed`` [P, B, H, dk,
+    dv + dk] fp32 (end state from zero, then transition, per segment) from h0
+    [B, H, dk, dv] (None: zero).  Returns [P + 1, B, H, dk, dv]: the state
+    entering each segment and, last, the state after the final one."""
+    packed = packed.contiguous()
+    P, B, H, dk, ld = packed.shape
+    out = torch.empty((P + 1, B, H, dk, dv), dtype=torch.float32, device=packed.device)
+    h0 = None if h0 is None else h0.to(torch.float32).contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(packed.device):
+        rc = lib.gdn_fold_states(_ptr(packed), packed.data_ptr() + 4 * dv, _ptr(h0), _ptr(out),
+                                 P, B * H, dk, dv, ld,
+                                 torch.cuda.current_stream(packed.device).cuda_stream)
+    _lib.check(rc, "gdn_fold_states")
+    return out
+
+
 def fused_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=None,
                                      output_final_state=False, *,
                                      final_state_out: Optional[torch.Tensor] = None

@@ -156,9 +156,13 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
     packed = torch.cat([S, M], dim=-1).view(B, parts, H, dk, dv + dk).contiguous()
     allp = torch.cat(gather(packed), dim=1).transpose(0, 1)             # [world*parts, B, H, dk, dv+dk]
     mark("exchange")
-    h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
-          if initial_state is None else initial_state.to(S.dtype))
-    states = fold_states_scan(h0, allp[..., :dv], allp[..., dv:])      # [world*parts + 1, ...]
+    if ws is not None and dk == 128 and dv % 32 == 0:
+        # one launch walks every segment: out[p + 1] = M_p out[p] + S_p
+        states = ops._fold_states(allp, initial_state, dv)               # [world*parts + 1, ...]
+    else:
+        h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
+              if initial_state is None else initial_state.to(S.dtype))
+        states = fold_states_scan(h0, allp[..., :dv], allp[..., dv:])  # [world*parts + 1, ...]
     mine = states[rank * parts:(rank + 1) * parts]
     s_in = mine.transpose(0, 1).reshape(B * parts, H, dk, dv).contiguous()
     mark("fold")

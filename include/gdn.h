@@ -306,6 +306,19 @@ int gdn_chunk_scan(const void* q, const void* k, const void* v, const float* g,
                    int Hk, int dk, int dv, int dtype, int transition, const void* workspace,
                    size_t ws_bytes, void* stream);
 
+/*
+ * The hand-off of a sequence split over P segments: segment p maps the state
+ * entering it to S_p + M_p h (its end state from zero and its transition, as
+ * gdn_chunk_scan's transition columns give them).  Writes out[0] = h0 (zero if
+ * NULL) and out[p + 1] = M_p out[p] + S_p, fp32, for BH heads; dk = 128, dv a
+ * multiple of 32.  S and M are [P][BH][dk] rows of `ld` floats (they may
+ * interleave in one array: S = base, M = base + dv, ld = dv + dk); h0 is
+ * [BH][dk][dv] and out [P + 1][BH][dk][dv].  No counterpart in the reference,
+ * which has no sequence split.
+ */
+int gdn_fold_states(const float* S, const float* M, const float* h0, float* out, int P, int BH,
+                    int dk, int dv, int ld, void* stream);
+
 /* Message for the last non-OK return on the calling thread ("" if none). */
 const char* gdn_last_error(void);
 
@@ -325,6 +338,7 @@ void gdn_reload_kernel_overrides(void);
  * forward; 1.7: dk = 256 on the tensor cores, the chunked forward's workspace
  * for fp32 inputs, gdn_chunk_varlen_workspace_bytes; 1.8: the two-launch chunked
  * forward and its workspace (bf16, dk = 128), gdn_chunk_prepare / gdn_chunk_scan,
+ * gdn_fold_states,
  * gdn_reload_kernel_overrides, gdn_binary_version). */
 int gdn_abi_version(void);
 

@@ -322,3 +322,17 @@ def test_two_phase_entry_points_check_arguments_on_the_host(lib):
     assert scan(dv=96) == _lib.GDN_ERR_UNSUPPORTED
     assert scan(transition=0, o=ctypes.c_void_p(40)) == _lib.GDN_ERR_INVALID
     assert scan(q=None) == _lib.GDN_ERR_INVALID
+
+
+def test_fold_states_checks_arguments_on_the_host(lib):
+    p = ctypes.c_void_p(16)
+    fold = lambda dk=128, dv=64, ld=192, P=2, BH=3, out=p: lib.gdn_fold_states(  # noqa: E731
+        p, p, None, out, P, BH, dk, dv, ld, None)
+    assert fold(dk=64) == _lib.GDN_ERR_UNSUPPORTED
+    assert fold(dv=48) == _lib.GDN_ERR_UNSUPPORTED
+    assert fold(ld=190) == _lib.GDN_ERR_INVALID and b"ld" in lib.gdn_last_error()
+    assert fold(ld=32) == _lib.GDN_ERR_INVALID
+    assert fold(P=-1) == _lib.GDN_ERR_INVALID
+    assert fold(out=None) == _lib.GDN_ERR_INVALID
+    assert fold(out=ctypes.c_void_p(20)) == _lib.GDN_ERR_INVALID
+    assert fold(BH=0) == _lib.GDN_OK          # nothing to fold

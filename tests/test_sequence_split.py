@@ -251,3 +251,27 @@ def test_two_phase_scan_transition_is_the_segment_map(cuda, B, T, H, Hk, dv):
     _, rM = orc.recurrent_ref(f64(q[:1, :, :1]), f64(k[:1, :, :1]), np.zeros((1, T, 1, 128)),
                               f64(g[:1, :, :1]), f64(b[:1, :, :1]), eye)
     assert_close(f64(M[:1, :1]), rM, "bf16", "transition vs oracle")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("P,B,H,dv,with_h0", [(1, 1, 2, 32, True), (3, 2, 3, 128, False),
+                                               (9, 1, 16, 128, True), (5, 1, 2, 192, True),
+                                               (0, 1, 2, 64, True)])
+def test_fold_kernel_equals_sequential_fold(cuda, P, B, H, dv, with_h0):
+    """gdn_fold_states on the interleaved [S | M] summaries gives the states of
+    the float64 sequential fold (fp32 products of 128 terms: 1e-5 relative)."""
+    from gated_deltanet_jax_b200 import ops
+    gen = torch.Generator(device=cuda).manual_seed(P * 7 + dv)
+    dk = 128
+    packed = torch.randn(P, B, H, dk, dv + dk, device=cuda, generator=gen)
+    packed[..., dv:] /= dk ** 0.5
+    h0 = torch.randn(B, H, dk, dv, device=cuda, generator=gen) if with_h0 else None
+    got = ops._fold_states(packed, h0, dv)
+    pk = packed.double().cpu()
+    ref = sp.fold_states(torch.zeros(B, H, dk, dv, dtype=torch.float64) if h0 is None
+                         else h0.double().cpu(),
+                         [(pk[p, ..., :dv], pk[p, ..., dv:]) for p in range(P)])
+    assert got.shape == (P + 1, B, H, dk, dv)
+    for p in range(P + 1):
+        err = float((got[p].double().cpu() - ref[p]).abs().max() / ref[p].abs().max().clamp_min(1e-30))
+        assert err < 1e-5, (p, err)
