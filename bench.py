@@ -173,21 +173,40 @@ def _cpu_decode_tokens(inputs, state, ntok, pool, nthreads):
     return np.concatenate([f.result() for f in futs], 0)
 
 
-def cpu_decode_baseline(budget_s=10.0):
+# Decode tokens of the batch per host dispatch: the CPU baseline and the
+# reference arm both step the batch this many tokens per call, so the two time
+# one code path at one granularity.
+CPU_DECODE_TOKENS = 4
+
+
+def cpu_decode_timed(steps=None, warmup=1, budget_s=None):
+    """Time the host decode recurrence: `warmup` untimed then `steps` timed
+    dispatches of CPU_DECODE_TOKENS tokens of the B=64 batch (or as many as fit
+    in `budget_s` seconds).  Returns (tokens/s, dispatches, seconds, threads)."""
     import concurrent.futures as cf
     nthreads = os.cpu_count() or 1
     inputs, state = _cpu_decode_inputs()
     with cf.ThreadPoolExecutor(nthreads) as pool:
-        _cpu_decode_tokens(inputs, state, 1, pool, nthreads)  # warm-up
-        ntok, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < budget_s or ntok < 2:
-            state = _cpu_decode_tokens(inputs, state, 1, pool, nthreads)
-            ntok += 1
+        for _ in range(warmup):
+            state = _cpu_decode_tokens(inputs, state, CPU_DECODE_TOKENS, pool, nthreads)
+        n, t0 = 0, time.perf_counter()
+        while (n < steps) if steps is not None else (time.perf_counter() - t0 < budget_s or n < 2):
+            state = _cpu_decode_tokens(inputs, state, CPU_DECODE_TOKENS, pool, nthreads)
+            n += 1
         el = time.perf_counter() - t0
-    return {"value": DEC["B"] * ntok / el, "unit": "tokens/s", "cores": nthreads, "kind": "port",
-            "sample": f"{ntok} decode steps of the B=64 H=16 dk=dv=128 batch (float32 NumPy "
-                      f"restatement of the reference recurrence, batch split over {nthreads} "
-                      f"threads), {el:.1f} s"}
+    return DEC["B"] * CPU_DECODE_TOKENS * n / el, n, el, nthreads
+
+
+def _cpu_decode_sample(n, el, nthreads):
+    return (f"{n} dispatches of {CPU_DECODE_TOKENS} decode tokens x B=64 (H=16 dk=dv=128), "
+            f"float32 NumPy restatement of the reference recurrence, batch split over "
+            f"{nthreads} threads, {el:.1f} s")
+
+
+def cpu_decode_baseline(budget_s=10.0):
+    value, n, el, nthreads = cpu_decode_timed(budget_s=budget_s)
+    return {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+            "sample": _cpu_decode_sample(n, el, nthreads)}
 
 
 def cpu_prefill_baseline(budget_s=10.0):
@@ -210,21 +229,12 @@ def cpu_prefill_baseline(budget_s=10.0):
 
 
 def run_reference_arm(a):
-    """--impl reference: the CPU restatement, rank 0 only."""
+    """--impl reference: the CPU restatement, rank 0 only (the same code path
+    and dispatch granularity as the GPU arm's cpu_baseline)."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    import concurrent.futures as cf
-    nthreads = os.cpu_count() or 1
-    inputs, state = _cpu_decode_inputs()
-    ntok_step = 4
-    with cf.ThreadPoolExecutor(nthreads) as pool:
-        for _ in range(a.warmup):
-            state = _cpu_decode_tokens(inputs, state, ntok_step, pool, nthreads)
-        t0 = time.perf_counter()
-        for _ in range(a.steps):
-            state = _cpu_decode_tokens(inputs, state, ntok_step, pool, nthreads)
-        el = time.perf_counter() - t0
-    value = DEC["B"] * ntok_step * a.steps / el
+    value, n, el, nthreads = cpu_decode_timed(steps=a.steps, warmup=a.warmup)
+    ntok_step = CPU_DECODE_TOKENS
     print(json.dumps({
         "impl": "reference", "metric": "recurrent decode tokens/s", "value": value,
         "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
@@ -234,8 +244,7 @@ def run_reference_arm(a):
                                f"sample of {ntok_step} decode tokens of the batch",
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
-                         "sample": f"{ntok_step} decode tokens x B=64 per step, float32 NumPy "
-                                   "restatement of the reference recurrence (JAX is not "
+                         "sample": _cpu_decode_sample(n, el, nthreads) + " (JAX is not "
                                    "installable here, so the reference itself cannot run)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
