@@ -5,7 +5,8 @@ decode workload -- B=64, H=16, dk=dv=128, bf16 q/k/v, fp32 state ~N(0,0.02),
 one bench step = 512 consecutive single-token decode steps with the state
 updated in place (512 kernel launches, replayed as one CUDA graph).  The
 ``prefill`` object in the same line reports chunked prefill tokens/s on B=4,
-T=4096, H=16, dk=dv=128, chunk=64, bf16 in / fp32 state (one launch per step);
+T=4096, H=16, dk=dv=128, chunk=64, bf16 in / fp32 state (two launches per step:
+the per-chunk preparation, then the scan, each also timed alone);
 ``long_context`` B=1 T=65536; ``backward`` the gradients on the prefill workload.
 
 Multi-GPU (torchrun, one rank per GPU): batch x head work is independent, so
@@ -477,6 +478,43 @@ def prefill_leg(d, a, lib, uuid=None):
            # two launches per call: the per-chunk preparation, then the scan
            "launch_s": ms / 1e3, "launches": 2 * steps, "steps": steps, "clocks": clocks,
            "bytes_launch": B * T * H * rl.bytes_chunk_per_token_head(dk, dv) + B * H * dk * dv * 4}
+    if ws_bytes:
+        # Each of the two kernels timed on its own over the same workspace: the
+        # preparation reads q/k (bf16), g/beta and writes 24 KiB per (chunk,
+        # head); the scan reads q/k/v, g/beta and that workspace, writes o and
+        # the final state.
+        cs = lambda: ctypes.c_void_p(torch.cuda.current_stream(d.dev).cuda_stream)  # noqa: E731
+
+        def prep():
+            _lib.check(lib.gdn_chunk_prepare(ptr(q), ptr(k), ptr(g), ptr(beta), B, T, H, H, dk,
+                                             _lib.GDN_DTYPE_BF16, ptr(ws), ws_bytes, cs()),
+                       "gdn_chunk_prepare")
+
+        def scan():
+            _lib.check(lib.gdn_chunk_scan(ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), None, ptr(o),
+                                          ptr(hT), B, T, H, H, dk, dv, _lib.GDN_DTYPE_BF16, 0,
+                                          ptr(ws), ws_bytes, cs()), "gdn_chunk_scan")
+
+        ksteps = max(a.steps, 200)
+        for fn in (prep, scan):
+            for _ in range(3):
+                fn()
+        ms_prep, _ = _timed(d, prep, ksteps)
+        ms_scan, _ = _timed(d, scan, ksteps)
+        nch = B * H * ((T + C - 1) // C)
+        prep_bytes = B * T * H * (2 * dk * 2 + 8) + nch * 24576
+        scan_bytes = (B * T * H * ((2 * dk + 2 * dv) * 2 + 8) + nch * 24576
+                      + B * H * dk * dv * 4)
+        res["launches"] += 2 * (ksteps + 3)
+        res["kernels"] = {
+            "chunk_prep_kernel": {"ms": ms_prep, "share": ms_prep / (ms_prep + ms_scan),
+                                  "bytes_per_launch": prep_bytes,
+                                  "gbs": prep_bytes / ms_prep / 1e6},
+            "chunk_scan_kernel": {"ms": ms_scan, "share": ms_scan / (ms_prep + ms_scan),
+                                  "bytes_per_launch": scan_bytes,
+                                  "gbs": scan_bytes / ms_scan / 1e6},
+            "note": "each kernel timed alone over the same inputs and workspace "
+                    f"({ksteps} launches, CUDA events)"}
     if not a.no_e2e:
         # Through the public op with pinned host buffers, every step: H2D of the
         # step's q/k/v/g/beta, the op, D2H of o and the final state.  Pipelined
@@ -1034,6 +1072,8 @@ def main():
                              "frac_of_attainable": tf / min(bf16, pre["flops_launch"]
                                                             / pre["bytes_launch"] * hbm / 1e3)},
             }
+            if "kernels" in pre:
+                pre_line["kernels"] = pre["kernels"]
             if "e2e" in pre:
                 pre_line["e2e"] = pre["e2e"]
             if cpu and cpu_pre:

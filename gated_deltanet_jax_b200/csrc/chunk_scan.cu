@@ -663,23 +663,27 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       if (!ok) break;
       if (wq < 2) {
         // ---- epilogue 1: X = beta (V - e^G K S), token row r ----
-        ok = mbar_wait(&bars[S_D1], (uint32_t)n & 1u) &&
-             mbar_wait(&bars[S_FULL + s], (uint32_t)(n / NS) & 1u);
+        // The row of V (landed with the chunk's K and Q, usually chunks ago)
+        // is read into registers before the wait for D1, so that its
+        // shared-memory latency overlaps the MMA instead of following it.
+        ok = mbar_wait(&bars[S_FULL + s], (uint32_t)(n / NS) & 1u);
+        if (!ok) break;
+        const unsigned char* Vt = sm + L::SM_V + s * 8192;
+        uint4 vrow[4];
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8)
+          vrow[c8] = trans ? make_uint4(0u, 0u, 0u, 0u)
+                           : *reinterpret_cast<const uint4*>(Vt + sw128(r, cb / 8 + c8));
+        const float bi = vb.beta[r], egi = vb.eG[r];
+        ok = mbar_wait(&bars[S_D1], (uint32_t)n & 1u);
         if (!ok) break;
         tc_fence_after();
         float ks[32];
         tmem_ld32(d1, ks);
-        const float bi = vb.beta[r], egi = vb.eG[r];
-        const unsigned char* Vt = sm + L::SM_V + s * 8192;
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
           float vv[8], x[8];
-          if (trans) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) vv[e] = 0.f;
-          } else {
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(Vt + sw128(r, cb / 8 + c8)), vv);
-          }
+          unpack_bf16x8(vrow[c8], vv);
 #pragma unroll
           for (int e = 0; e < 8; ++e) x[e] = bi * (vv[e] - egi * ks[8 * c8 + e]);
           *reinterpret_cast<uint4*>(sm + L::SM_X + sw128(r, cb / 8 + c8)) = pack_bf16x8(x);
