@@ -415,9 +415,15 @@ int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const
     return fail(GDN_ERR_INVALID, "semantics %d unknown", semantics);
   const size_t need =
       chunk_workspace(B, T, H, dk, dv, chunk, dtype, semantics, cu_seqlens ? B : 0);
-  if (ws_bytes < need || (need && !workspace))
+  // The two-launch form's workspace is optional: a call without it (or with a
+  // shorter one) runs the one-launch tensor-core kernel, which needs none.
+  const bool scan_shape = need > 0 && !cu_seqlens && dtype == GDN_DTYPE_BF16 &&
+                          semantics == GDN_SEMANTICS_EXACT && dk == 128 && dv % 64 == 0;
+  const bool have_ws = workspace && ws_bytes >= need;
+  if (need && !have_ws && !scan_shape)
     return fail(GDN_ERR_INVALID, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
-  if (need && !aligned16(workspace)) return fail(GDN_ERR_INVALID, "workspace is not 16-byte aligned");
+  if (need && have_ws && !aligned16(workspace))
+    return fail(GDN_ERR_INVALID, "workspace is not 16-byte aligned");
   if (T == 0 && (B * H) > 0 && hT && h0 != hT) {
     cudaError_t e = h0 ? cudaMemcpyAsync(hT, h0, sizeof(float) * (size_t)B * H * dk * dv,
                                          cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
@@ -431,11 +437,11 @@ int chunk_fwd(const void* q, const void* k, const void* v, const float* g, const
   // tensor-core kernel (kernel cross-checks; read once).
   const gdn::KernelOverrides ov = gdn::kernel_overrides();
   const bool simt_only = ov.chunk_simt;
-  if (!simt_only && !ov.chunk_fused && gdn::chunk_scan_supported(a) && need > 0)
+  if (!simt_only && !ov.chunk_fused && scan_shape && have_ws && gdn::chunk_scan_supported(a))
     return cuda_status(gdn::launch_chunk_scan(a, (cudaStream_t)stream), "gdn_chunk_fwd");
   if (!simt_only && gdn::chunk_tc_supported(a))
     return cuda_status(gdn::launch_chunk_tc(a, (cudaStream_t)stream), "gdn_chunk_fwd");
-  if (!simt_only && need > 0)
+  if (!simt_only && need > 0 && !scan_shape)
     return cuda_status(gdn::launch_chunk_fwd_warp(a, (cudaStream_t)stream), "gdn_chunk_fwd");
   if (gdn::chunk_simt_smem_bytes(a) == 0)
     return fail(GDN_ERR_UNSUPPORTED, "no chunk kernel fits dk=%d dv=%d chunk=%d", dk, dv, chunk);

@@ -70,9 +70,12 @@ int gdn_recurrent_fwd(const void* q, const void* k, const void* v,
  * (to rounding).  `chunk` is the chunk length C (16, 32 or 64).  h0 == NULL
  * starts from zeros (ops.py:318-319); hT == NULL skips the final state
  * (output_final_state=False, ops.py:344-346).  `workspace` / `ws_bytes` may be
- * NULL / 0 when gdn_chunk_workspace_bytes() returns 0; it is non-zero where the
- * call runs on the warp-level tensor-core kernels (exact semantics with fp32
- * inputs, or bf16 shapes other than dk = 128 / 256 with dv % 64 == 0).
+ * NULL / 0 when gdn_chunk_workspace_bytes() returns 0.  It is required where
+ * the call runs on the warp-level tensor-core kernels (exact semantics with
+ * fp32 inputs, or bf16 shapes other than dk = 128 / 256 with dv % 64 == 0).
+ * For bf16 with dk = 128 and dv % 64 == 0 (exact semantics) it is optional:
+ * with it the call runs in two launches (gdn_chunk_prepare, gdn_chunk_scan),
+ * without it (or with a shorter one) in one.
  */
 int gdn_chunk_fwd(const void* q, const void* k, const void* v,
                   const float* g, const float* beta,
@@ -262,7 +265,9 @@ int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v,
                           int B, int T, int H, int Hk, int dk_dim, int dv_dim, int dtype,
                           void* stream);
 
-/* Device scratch bytes gdn_chunk_fwd needs for these sizes (0 = none). */
+/* Device scratch bytes gdn_chunk_fwd takes for these sizes (0 = none; for bf16
+ * with dk = 128 and dv % 64 == 0, the two-launch form's, which the call may go
+ * without). */
 size_t gdn_chunk_workspace_bytes(int B, int T, int H, int dk, int dv, int chunk,
                                  int dtype, int semantics);
 

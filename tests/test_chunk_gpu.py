@@ -330,3 +330,35 @@ def test_two_launch_in_place_and_repeatable(cuda):
     o3, _ = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=S, final_state_out=S)
     assert torch.equal(o1, o2) and torch.equal(h1, h2)
     assert torch.equal(o1, o3) and torch.equal(h1, S)
+
+
+def test_two_launch_workspace_optional(cuda):
+    """gdn_chunk_fwd at the two-launch shapes without a workspace (or with a
+    short one) runs the one-launch kernel: bit-identical to forcing it."""
+    import ctypes
+    from gated_deltanet_jax_b200 import _lib as lib_mod
+    lib = lib_mod.load()
+    B, T, H, dv = 2, 200, 4, 128
+    q, k, v, g, b, h0 = device_inputs_fast(B, T, H, 128, dv, seed=5, dtype="bf16", dev=cuda,
+                                           h0_std=0.02)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    need = lib.gdn_chunk_workspace_bytes(B, T, H, 128, dv, 64, lib_mod.GDN_DTYPE_BF16, 0)
+    assert need > 0
+    short = torch.empty(need // 2, dtype=torch.uint8, device=cuda)
+
+    def call(ws, ws_bytes):
+        o = torch.empty_like(v)
+        hT = torch.empty_like(h0)
+        rc = lib.gdn_chunk_fwd(ptr(q), ptr(k), ptr(v), ptr(g), ptr(b), ptr(h0), ptr(o), ptr(hT),
+                               B, T, H, 128, dv, 64, lib_mod.GDN_DTYPE_BF16, 0, ptr(ws), ws_bytes,
+                               ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream))
+        lib_mod.check(rc, "gdn_chunk_fwd")
+        torch.cuda.synchronize(cuda)
+        return o, hT
+
+    o0, h_0 = call(None, 0)
+    o1, h_1 = call(short, short.numel())
+    o2, h_2 = _with_kernel("fused", lambda: call(None, 0))
+    assert torch.equal(o0, o2) and torch.equal(h_0, h_2)
+    assert torch.equal(o1, o2) and torch.equal(h_1, h_2)
+    assert lib.gdn_device_error(0) == 0
