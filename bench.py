@@ -1063,7 +1063,8 @@ def main():
                            "l2": "inputs larger than L2 (201 MB q/k/v per GPU)"},
                 "roofline": {"bound": "tensor", "achieved": tf, "peak": bf16, "unit": "TFLOP/s",
                              "frac": tf / bf16, "peak_source": f"{peak_src} bf16_tflops (burst)",
-                             "traffic": _profile_traffic("chunk_prefill_b4_t4096_h16_d128"),
+                             "traffic": _profile_traffic("chunk_scan_two_launch_b4_t4096_h16_d128"),
+                             "traffic_note": "DRAM bytes of one call (both launches) from ncu",
                              "algorithmic_flops_per_launch": pre["flops_launch"],
                              "hbm_achieved_gbs": pre["bytes_launch"] / pre["launch_s"] / 1e9,
                              # min(peak, arithmetic intensity x HBM bandwidth): the attainable
