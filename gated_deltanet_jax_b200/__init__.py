@@ -13,6 +13,8 @@ from .ops import (
     fused_recurrent_gated_delta_rule_fwd,
     gated_delta_rule_chunk_layer,
     gated_delta_rule_decode_layer,
+    gated_rms_norm,
+    short_convolution,
 )
 
 __all__ = [
@@ -24,4 +26,6 @@ __all__ = [
     "delta_rule",
     "gated_delta_rule_chunk_layer",
     "gated_delta_rule_decode_layer",
+    "gated_rms_norm",
+    "short_convolution",
 ]

@@ -45,6 +45,8 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_prepare",
     "gdn_chunk_scan",
     "gdn_fold_states",
+    "gdn_short_conv_fwd",
+    "gdn_gated_rmsnorm_fwd",
     "gdn_last_error",
     "gdn_reload_kernel_overrides",
     "gdn_device_error",
@@ -112,6 +114,11 @@ def _declare(lib):
     lib.gdn_chunk_scan.restype = _i
     lib.gdn_fold_states.argtypes = [_vp] * 4 + [_i] * 5 + [_vp]
     lib.gdn_fold_states.restype = _i
+    lib.gdn_short_conv_fwd.argtypes = [_vp] * 5 + [_i] * 6 + [_vp]
+    lib.gdn_short_conv_fwd.restype = _i
+    lib.gdn_gated_rmsnorm_fwd.argtypes = [_vp] * 3 + [ctypes.c_float, _vp, ctypes.c_longlong,
+                                                      _i, _i, _vp]
+    lib.gdn_gated_rmsnorm_fwd.restype = _i
     lib.gdn_last_error.argtypes = []
     lib.gdn_last_error.restype = ctypes.c_char_p
     lib.gdn_reload_kernel_overrides.argtypes = []

@@ -168,9 +168,13 @@ __device__ __forceinline__ bool wait_shared_bar(uint64_t* bars, int idx, uint32_
 // of a row always run as a cluster of two CTAs, which exchange the rows'
 // partial sums of squares; without kPair each still prepares every chunk (the
 // compact form, for high occupancy).
+// kGates (implied by kLayer): g and beta hold the raw a_proj / b_proj outputs
+// and the gate warp forms g and beta from them (la.A_log, la.dt_bias); without
+// kLayer the output is the op's o, for a separate gated RMSNorm (the layer at
+// head dims other than dk = dv = 128).
 // h0 and hT may be the same array (in-place state): each CTA reads its tile of
 // h0 before the loop and writes the same tile of hT after it.
-template <int DK, bool kPair, bool kLayer>
+template <int DK, bool kPair, bool kLayer, bool kGates = kLayer>
 __global__ void __launch_bounds__(kThreads, 1)
 chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
@@ -180,6 +184,7 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
                 const LayerArgs la) {
   constexpr bool kCluster = kPair || kLayer;  // launched in clusters of two CTAs
   static_assert(DK == 128 || (DK == 256 && !kPair && !kLayer), "key width");
+  static_assert(kGates || !kLayer, "the layer form forms its own gates");
   using L = Lay<DK>;
   constexpr int NSTAGE = L::NSTAGE, KQ_STAGE = L::KQ_STAGE;
   constexpr int SM_KQ = L::SM_KQ, SM_V = L::SM_V, SM_S = L::SM_S, SM_X = L::SM_X;
@@ -389,10 +394,10 @@ chunk_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__
       // g and beta, then the gate vectors of chunk_gate_vectors.
       const size_t gb = ((size_t)b * T + tok0) * H + h;
       // layer form: g = -exp(A_log[h]) softplus(a + dt_bias[h]), beta = sigmoid(b)
-      const float negA = kLayer ? -expf(ldg_f32(la.A_log + h)) : 0.f;
-      const float dtb = kLayer ? ldg_f32(la.dt_bias + h) : 0.f;
-      auto gate_of = [&](float x) { return kLayer ? negA * softplus(x + dtb) : x; };
-      auto beta_of = [&](float x) { return kLayer ? sigmoid(x) : x; };
+      const float negA = kGates ? -expf(ldg_f32(la.A_log + h)) : 0.f;
+      const float dtb = kGates ? ldg_f32(la.dt_bias + h) : 0.f;
+      auto gate_of = [&](float x) { return kGates ? negA * softplus(x + dtb) : x; };
+      auto beta_of = [&](float x) { return kGates ? sigmoid(x) : x; };
       bool ok = true;
       for (int n = 0; n < N && ok; ++n) {
         const int rb = n % NTP;
@@ -870,7 +875,7 @@ bool chunk_tc_supported(const ChunkArgs& a) {
 
 namespace {
 
-template <int DK, bool kPair, bool kLayer>
+template <int DK, bool kPair, bool kLayer, bool kGates = kLayer>
 cudaError_t launch_tc_form(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
   constexpr int SMEM_BYTES = Lay<DK>::SMEM_BYTES;
   CUtensorMap mk, mq, mv;
@@ -879,7 +884,7 @@ cudaError_t launch_tc_form(const ChunkArgs& a, const LayerArgs& la, cudaStream_t
       !make_bf16_map_4d(&mq, a.q, rows, a.T, a.Hk, a.dk) ||
       !make_bf16_map_4d(&mv, a.v, rows, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
-  auto kernel = chunk_tc_kernel<DK, kPair, kLayer>;
+  auto kernel = chunk_tc_kernel<DK, kPair, kLayer, kGates>;
   // The in-kernel register split assumes exactly kLaunchRegs per thread at
   // launch; with fewer, the chain warpgroup's increase could never be granted.
   // (Checked, and shared memory opted in, once per device and form.)
@@ -951,6 +956,17 @@ cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaS
   if (force == 1) pair = true;
   return pair ? launch_tc_form<128, true, true>(a, la, st)
               : launch_tc_form<128, false, true>(a, la, st);
+}
+
+// The gates-only form (compact, unpaired): g and beta from the raw
+// projections in the gate warp, o as the op writes it.  The layer at the
+// other tcgen05 shapes (dk = 256, or dv other than 128) runs this and then a
+// gated RMSNorm over o.
+cudaError_t launch_chunk_tc_gates(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st) {
+  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_tc_supported(a)) return cudaErrorInvalidValue;
+  if (a.dk == 256) return launch_tc_form<256, false, false, true>(a, la, st);
+  return launch_tc_form<128, false, false, true>(a, la, st);
 }
 
 }  // namespace gdn

@@ -216,9 +216,13 @@ int chunk_fwd_layer(const void* q, const void* k, const void* v, const float* a,
   if (T == 0 || (long long)B * H == 0)   // nothing to normalise: carry the state through
     return chunk_fwd(q, k, v, a, b, h0, y, hT, cu_seqlens, B, T, H, Hk, dk, dv, 64, dtype,
                      GDN_SEMANTICS_EXACT, nullptr, 0, stream);
-  if (dtype != GDN_DTYPE_BF16 || dk != 128 || dv != 128)
-    return fail(GDN_ERR_UNSUPPORTED, "the chunked layer form covers bf16 inputs with dk = dv = "
-                "128 (dtype=%d dk=%d dv=%d)", dtype, dk, dv);
+  // dk = dv = 128: one fused launch; the other tensor-core shapes (dk = 256,
+  // dv a multiple of 64): the op with the gates formed in its gate warp, then
+  // the gated RMSNorm over its output in place.
+  const bool fused = dtype == GDN_DTYPE_BF16 && dk == 128 && dv == 128;
+  if (dtype != GDN_DTYPE_BF16 || (dk != 128 && dk != 256) || dv % 64)
+    return fail(GDN_ERR_UNSUPPORTED, "the chunked layer form covers bf16 inputs with dk = 128 "
+                "or 256 and dv a multiple of 64 (dtype=%d dk=%d dv=%d)", dtype, dk, dv);
   if (!A_log || !dt_bias || !norm_weight)
     return fail(GDN_ERR_INVALID, "A_log, dt_bias and norm_weight must be non-NULL");
   if (gate && !aligned16(gate)) return fail(GDN_ERR_INVALID, "gate is not 16-byte aligned");
@@ -230,8 +234,14 @@ int chunk_fwd_layer(const void* q, const void* k, const void* v, const float* a,
   gdn::LayerArgs la;
   la.a = a; la.b = b; la.A_log = A_log; la.dt_bias = dt_bias;
   la.gate = gate; la.weight = norm_weight; la.eps = eps;
-  return cuda_status(gdn::launch_chunk_tc_layer(ca, la, (cudaStream_t)stream),
-                     "gdn_chunk_fwd_layer");
+  if (fused)
+    return cuda_status(gdn::launch_chunk_tc_layer(ca, la, (cudaStream_t)stream),
+                       "gdn_chunk_fwd_layer");
+  cudaError_t e = gdn::launch_chunk_tc_gates(ca, la, (cudaStream_t)stream);
+  if (e == cudaSuccess)
+    e = gdn::launch_gated_norm(y, gate, norm_weight, y, (long long)rows * T * H, dv, eps, dtype,
+                               (cudaStream_t)stream);
+  return cuda_status(e, "gdn_chunk_fwd_layer");
 }
 
 }  // namespace
@@ -263,20 +273,36 @@ int gdn_recurrent_fwd_layer(const void* q, const void* k, const void* v, const f
   if (rc) return rc;
   if (T == 0 || (long long)B * H == 0)   // nothing to normalise: carry the state through
     return recurrent_fwd(q, k, v, a, b, h0, y, hT, B, T, H, Hk, dk, dv, dtype, stream);
-  if (T != 1 || dk != 128 || dv != 128)
-    return fail(GDN_ERR_UNSUPPORTED, "the layer form covers single-token decode with dk = dv = "
-                "128 (T=%d dk=%d dv=%d)", T, dk, dv);
   if (!A_log || !dt_bias || !norm_weight)
     return fail(GDN_ERR_INVALID, "A_log, dt_bias and norm_weight must be non-NULL");
   if (!aligned16(norm_weight)) return fail(GDN_ERR_INVALID, "norm_weight is not 16-byte aligned");
   if (gate && !aligned16(gate)) return fail(GDN_ERR_INVALID, "gate is not 16-byte aligned");
   if (!(eps >= 0.f) || eps > 1.f) return fail(GDN_ERR_INVALID, "eps=%g outside [0, 1]", (double)eps);
-  gdn::RecurrentArgs ra{q, k, v, nullptr, nullptr, h0, y, hT, B, T, H, dk, dv, dtype, Hk};
+  if (!gdn::gated_norm_supported(dv, dtype))
+    return fail(GDN_ERR_UNSUPPORTED, "the layer form's norm takes dv a multiple of 8 (bf16) or "
+                "4 (fp32) up to 1024 / 512 (dv=%d)", dv);
   gdn::LayerArgs la;
   la.a = a; la.b = b; la.A_log = A_log; la.dt_bias = dt_bias;
   la.gate = gate; la.weight = norm_weight; la.eps = eps;
-  return cuda_status(gdn::launch_recurrent_bulk_layer(ra, la, (cudaStream_t)stream),
-                     "gdn_recurrent_fwd_layer");
+  // Single-token decode at dk = dv = 128: one fused launch.
+  if (T == 1 && dk == 128 && dv == 128) {
+    gdn::RecurrentArgs ra{q, k, v, nullptr, nullptr, h0, y, hT, B, T, H, dk, dv, dtype, Hk};
+    return cuda_status(gdn::launch_recurrent_bulk_layer(ra, la, (cudaStream_t)stream),
+                       "gdn_recurrent_fwd_layer");
+  }
+  // Whole sequences on the tensor-core shapes: the chunked layer form (the
+  // same recurrence, as gdn_recurrent_fwd does for the op).
+  if (T >= 64 && dtype == GDN_DTYPE_BF16 && (dk == 128 || dk == 256) && dv % 64 == 0)
+    return chunk_fwd_layer(q, k, v, a, b, A_log, dt_bias, h0, hT, gate, norm_weight, eps, y,
+                           nullptr, B, T, H, Hk, dk, dv, dtype, stream);
+  // Otherwise the general recurrent kernel with the gates formed per token,
+  // then the gated RMSNorm over its output in place.
+  gdn::RecurrentArgs ra{q, k, v, a, b, h0, y, hT, B, T, H, dk, dv, dtype, Hk};
+  cudaError_t e = gdn::launch_recurrent_gates(ra, la, (cudaStream_t)stream);
+  if (e == cudaSuccess)
+    e = gdn::launch_gated_norm(y, gate, norm_weight, y, (long long)B * T * H, dv, eps, dtype,
+                               (cudaStream_t)stream);
+  return cuda_status(e, "gdn_recurrent_fwd_layer");
 }
 
 int gdn_chunk_fwd_layer(const void* q, const void* k, const void* v, const float* a,
@@ -587,8 +613,66 @@ int gdn_device_error(int clear) {
   return a ? a : (b ? b : c);
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 8; }
+int gdn_abi_version(void) { return (1 << 16) | 9; }
 
 int gdn_binary_version(void) { return gdn::chunk_scan_binary_version(); }
+
+int gdn_short_conv_fwd(const void* x, const float* weight, const void* state_in, void* state_out,
+                       void* y, int B, int T, int C, int K, int activation, int dtype,
+                       void* stream) {
+  g_err[0] = '\0';
+  if (B < 0 || T < 0 || C < 0) return fail(GDN_ERR_INVALID, "negative size B=%d T=%d C=%d", B, T, C);
+  if (dtype != GDN_DTYPE_FP32 && dtype != GDN_DTYPE_BF16)
+    return fail(GDN_ERR_INVALID, "dtype %d is neither GDN_DTYPE_FP32 nor GDN_DTYPE_BF16", dtype);
+  if (activation != 0 && activation != 1)
+    return fail(GDN_ERR_INVALID, "activation %d is neither 0 (none) nor 1 (silu)", activation);
+  if (K < 1 || K > gdn::kShortConvMaxK)
+    return fail(GDN_ERR_UNSUPPORTED, "kernel size K=%d not supported (1 .. %d)", K,
+                gdn::kShortConvMaxK);
+  if (B > 65535) return fail(GDN_ERR_UNSUPPORTED, "B=%d exceeds 65535", B);
+  if (B == 0 || C == 0) return GDN_OK;
+  if (!gdn::short_conv_supported(C, K, dtype))
+    return fail(GDN_ERR_UNSUPPORTED, "C=%d channels must be a multiple of %d for this dtype", C,
+                dtype == GDN_DTYPE_BF16 ? 8 : 4);
+  if ((long long)B * ((long long)T + K) * C > (1LL << 40))
+    return fail(GDN_ERR_INVALID, "tensor too large (B*T*C > 2^40)");
+  if (!weight || !aligned16(weight))
+    return fail(GDN_ERR_INVALID, "weight must be non-NULL and 16-byte aligned");
+  if (T > 0 && (!x || !y || !aligned16(x) || !aligned16(y)))
+    return fail(GDN_ERR_INVALID, "x and y must be non-NULL and 16-byte aligned");
+  if ((state_in && !aligned16(state_in)) || (state_out && !aligned16(state_out)))
+    return fail(GDN_ERR_INVALID, "the conv states must be 16-byte aligned");
+  if (T == 0) {
+    // nothing to convolve; the state still carries through
+    if (!state_out || state_out == state_in || K == 1) return GDN_OK;
+    const size_t bytes = (size_t)B * (K - 1) * C * (dtype == GDN_DTYPE_BF16 ? 2 : 4);
+    cudaError_t e = state_in ? cudaMemcpyAsync(state_out, state_in, bytes,
+                                               cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
+                             : cudaMemsetAsync(state_out, 0, bytes, (cudaStream_t)stream);
+    return cuda_status(e, "gdn_short_conv_fwd (T=0 state copy)");
+  }
+  return cuda_status(gdn::launch_short_conv(x, weight, state_in, state_out, y, B, T, C, K,
+                                            activation, dtype, (cudaStream_t)stream),
+                     "gdn_short_conv_fwd");
+}
+
+int gdn_gated_rmsnorm_fwd(const void* o, const void* gate, const float* weight, float eps,
+                          void* y, long long rows, int dv, int dtype, void* stream) {
+  g_err[0] = '\0';
+  if (rows < 0 || dv < 0) return fail(GDN_ERR_INVALID, "negative size rows=%lld dv=%d", rows, dv);
+  if (dtype != GDN_DTYPE_FP32 && dtype != GDN_DTYPE_BF16)
+    return fail(GDN_ERR_INVALID, "dtype %d is neither GDN_DTYPE_FP32 nor GDN_DTYPE_BF16", dtype);
+  if (!gdn::gated_norm_supported(dv, dtype))
+    return fail(GDN_ERR_UNSUPPORTED, "dv=%d: a multiple of 8 (bf16) or 4 (fp32) up to 1024 / "
+                "512", dv);
+  if (!(eps >= 0.f) || eps > 1.f) return fail(GDN_ERR_INVALID, "eps=%g outside [0, 1]", (double)eps);
+  if (rows == 0) return GDN_OK;
+  if (!o || !y || !weight) return fail(GDN_ERR_INVALID, "o, y and weight must be non-NULL");
+  if (!aligned16(o) || !aligned16(y) || (gate && !aligned16(gate)))
+    return fail(GDN_ERR_INVALID, "o, y and gate must be 16-byte aligned");
+  return cuda_status(gdn::launch_gated_norm(o, gate, weight, y, rows, dv, eps, dtype,
+                                            (cudaStream_t)stream),
+                     "gdn_gated_rmsnorm_fwd");
+}
 
 }  // extern "C"

@@ -144,6 +144,9 @@ struct LayerArgs {
 };
 
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st);
+// The general recurrent kernel with the layer's prologue: a.g / a.beta hold the
+// raw a_proj / b_proj outputs, la.A_log / la.dt_bias the gate parameters.
+cudaError_t launch_recurrent_gates(const RecurrentArgs& a, const LayerArgs& la, cudaStream_t st);
 
 // Decode step (T == 1) with the state streamed by bulk copies (dk = dv = 128).
 bool recurrent_bulk_supported(const RecurrentArgs& a);
@@ -169,6 +172,9 @@ cudaError_t launch_chunk_tc(const ChunkArgs& a, cudaStream_t st);
 // from the raw projections (a.g / a.beta unused) and the gated RMSNorm of
 // every output row, written to a.o.
 cudaError_t launch_chunk_tc_layer(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st);
+// Its gates-only form (any tcgen05 shape, unpaired): g and beta from the raw
+// projections (a.g / a.beta hold them), o as the op writes it.
+cudaError_t launch_chunk_tc_gates(const ChunkArgs& a, const LayerArgs& la, cudaStream_t st);
 
 // Two-launch chunked forward (bf16, dk = 128, dv % 64 == 0, exact, dense rows):
 // a preparation kernel over every (chunk, head) writes the state-independent
@@ -186,6 +192,19 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
 int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
 int chunk_scan_binary_version();
+
+// The layer's elementwise work (layer_ops.cu).  Short convolution + SiLU
+// (model.py:15-40): x, y [B,T,C], w [K,C] fp32, states [B,K-1,C] in x's dtype;
+// C a multiple of 8 (bf16) or 4 (fp32), K <= kShortConvMaxK.
+constexpr int kShortConvMaxK = 8;
+bool short_conv_supported(int C, int K, int dtype);
+cudaError_t launch_short_conv(const void* x, const float* w, const void* state_in,
+                              void* state_out, void* y, int B, int T, int C, int K, int act,
+                              int dtype, cudaStream_t st);
+// Gated RMSNorm (model.py:41-53) over `rows` rows of dv; o and y may alias.
+bool gated_norm_supported(int dv, int dtype);
+cudaError_t launch_gated_norm(const void* o, const void* gate, const float* w, void* y,
+                              long long rows, int dv, float eps, int dtype, cudaStream_t st);
 
 // The sequence split's hand-off: out[0] = h0, out[p + 1] = M_p out[p] + S_p for
 // P segments of BH heads (dk = 128, dv % 32 == 0; S, M rows of `ld` floats).

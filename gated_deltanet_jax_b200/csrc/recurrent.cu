@@ -21,12 +21,16 @@
 
 namespace gdn {
 
-template <typename Tin, int DK, int CW, int NT>
+// kGates: g and beta hold the raw a_proj / b_proj outputs, and each token's
+// g = -exp(A_log[h]) softplus(a + dt_bias[h]), beta = sigmoid(b) are formed
+// here (the layer's prologue, model.py:136-139; the norm runs afterwards).
+template <typename Tin, int DK, int CW, int NT, bool kGates>
 __global__ void __launch_bounds__(NT)
 recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
                  const Tin* __restrict__ v, const float* __restrict__ g,
                  const float* __restrict__ beta, const float* h0,
-                 Tin* __restrict__ o, float* hT, int T, int H, int Hk, int dv) {
+                 Tin* __restrict__ o, float* hT, int T, int H, int Hk, int dv,
+                 const float* __restrict__ A_log, const float* __restrict__ dt_bias) {
   constexpr int LPR = CW / 4;        // threads across one row of the tile
   constexpr int RPP = NT / LPR;      // rows covered per pass of the CTA
   constexpr int RPT = DK / RPP;      // rows per thread
@@ -49,6 +53,8 @@ recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
   const int col = blockIdx.x * CW + cg * 4;
 
   const size_t sbase = (size_t)bh * DK * dv + col;
+  const float negA = kGates ? -expf(A_log[h]) : 0.f;
+  const float dtb = kGates ? dt_bias[h] : 0.f;
   float4 S[RPT];
   if (h0 != nullptr) {
 #pragma unroll
@@ -67,8 +73,8 @@ recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
       s_q[buf][i] = to_f32(q[tokq * DK + i]);
     }
     const float4 vv = load4(v + tok * dv + col);
-    const float alpha = __expf(g[tok]);
-    const float bt = beta[tok];
+    const float alpha = __expf(kGates ? negA * softplus(g[tok] + dtb) : g[tok]);
+    const float bt = kGates ? sigmoid(beta[tok]) : beta[tok];
     __syncthreads();
 
     float4 kh = make_float4(0.f, 0.f, 0.f, 0.f), qh = kh;
@@ -139,33 +145,34 @@ recurrent_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
 
 namespace {
 
-template <typename Tin, int DK, int CW>
-cudaError_t launch_cfg(const RecurrentArgs& a, cudaStream_t st) {
+template <typename Tin, int DK, int CW, bool kGates>
+cudaError_t launch_cfg(const RecurrentArgs& a, const LayerArgs& la, cudaStream_t st) {
   constexpr int LPR = CW / 4;
   constexpr int NT0 = DK * LPR / 16;  // aim for 16 state rows per thread
   constexpr int NT = NT0 < 32 ? 32 : (NT0 > 256 ? 256 : NT0);
   dim3 grid(a.dv / CW, a.B * a.H);
-  recurrent_kernel<Tin, DK, CW, NT><<<grid, NT, 0, st>>>(
+  recurrent_kernel<Tin, DK, CW, NT, kGates><<<grid, NT, 0, st>>>(
       static_cast<const Tin*>(a.q), static_cast<const Tin*>(a.k), static_cast<const Tin*>(a.v),
-      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv);
+      a.g, a.beta, a.h0, static_cast<Tin*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv, la.A_log,
+      la.dt_bias);
   return cudaGetLastError();
 }
 
-template <typename Tin, int DK>
-cudaError_t launch_dk(const RecurrentArgs& a, cudaStream_t st) {
-  if (a.dv % 64 == 0) return launch_cfg<Tin, DK, 64>(a, st);
-  if (a.dv % 32 == 0) return launch_cfg<Tin, DK, 32>(a, st);
-  return launch_cfg<Tin, DK, 16>(a, st);
+template <typename Tin, int DK, bool kGates>
+cudaError_t launch_dk(const RecurrentArgs& a, const LayerArgs& la, cudaStream_t st) {
+  if (a.dv % 64 == 0) return launch_cfg<Tin, DK, 64, kGates>(a, la, st);
+  if (a.dv % 32 == 0) return launch_cfg<Tin, DK, 32, kGates>(a, la, st);
+  return launch_cfg<Tin, DK, 16, kGates>(a, la, st);
 }
 
-template <typename Tin>
-cudaError_t launch_t(const RecurrentArgs& a, cudaStream_t st) {
+template <typename Tin, bool kGates>
+cudaError_t launch_t(const RecurrentArgs& a, const LayerArgs& la, cudaStream_t st) {
   switch (a.dk) {
-    case 16: return launch_dk<Tin, 16>(a, st);
-    case 32: return launch_dk<Tin, 32>(a, st);
-    case 64: return launch_dk<Tin, 64>(a, st);
-    case 128: return launch_dk<Tin, 128>(a, st);
-    case 256: return launch_dk<Tin, 256>(a, st);
+    case 16: return launch_dk<Tin, 16, kGates>(a, la, st);
+    case 32: return launch_dk<Tin, 32, kGates>(a, la, st);
+    case 64: return launch_dk<Tin, 64, kGates>(a, la, st);
+    case 128: return launch_dk<Tin, 128, kGates>(a, la, st);
+    case 256: return launch_dk<Tin, 256, kGates>(a, la, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -175,7 +182,15 @@ cudaError_t launch_t(const RecurrentArgs& a, cudaStream_t st) {
 cudaError_t launch_recurrent(const RecurrentArgs& a, cudaStream_t st) {
   if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   if (recurrent_bulk_supported(a)) return launch_recurrent_bulk(a, st);
-  return a.dtype == kBF16 ? launch_t<__nv_bfloat16>(a, st) : launch_t<float>(a, st);
+  const LayerArgs none;
+  return a.dtype == kBF16 ? launch_t<__nv_bfloat16, false>(a, none, st)
+                          : launch_t<float, false>(a, none, st);
+}
+
+cudaError_t launch_recurrent_gates(const RecurrentArgs& a, const LayerArgs& la, cudaStream_t st) {
+  if (a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  return a.dtype == kBF16 ? launch_t<__nv_bfloat16, true>(a, la, st)
+                          : launch_t<float, true>(a, la, st);
 }
 
 }  // namespace gdn

@@ -375,18 +375,21 @@ def gated_delta_rule_decode_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
                                   output_final_state=False,
                                   final_state_out: Optional[torch.Tensor] = None
                                   ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-    """One decode token of the GatedDeltaNet layer's core in one kernel
+    """The GatedDeltaNet layer's core around the recurrent op
     (gdn_recurrent_fwd_layer): the gates from the raw projections, the
-    recurrent step, and the gated RMSNorm of its output.
+    recurrent step, and the gated RMSNorm of its output.  Single-token decode
+    at dk = dv = 128 is one kernel; other shapes run the recurrent kernel with
+    the gates formed in it, then the norm kernel (whole sequences on the
+    tensor-core shapes take the chunked layer form).
 
     The reference layer (model.py:136-153) runs these as separate operations:
     ``beta = sigmoid(b)``, ``g = -exp(A_log) * softplus(a + dt_bias)``, the op,
     then ``FusedRMSNormGated`` (model.py:41-53; with ``gate=None`` the plain
     RMSNorm of the ungated layer, whose epsilon is 1e-6).
 
-    q, k ``[B,1,Hk,128]``; v ``[B,1,H,128]``; a, b ``[B,1,H]`` (a_proj, b_proj
-    outputs); A_log, dt_bias ``[H]``; gate ``[B,1,H,128]`` in v's dtype or None;
-    norm_weight ``[128]`` (None: ones).  Returns ``(y, final_state)`` like the
+    q, k ``[B,T,Hk,dk]``; v ``[B,T,H,dv]``; a, b ``[B,T,H]`` (a_proj, b_proj
+    outputs); A_log, dt_bias ``[H]``; gate ``[B,T,H,dv]`` in v's dtype or None;
+    norm_weight ``[dv]`` (None: ones).  Returns ``(y, final_state)`` like the
     recurrent op (``final_state_out=S`` with ``initial_state=S`` updates S in
     place).  Inference only: there is no backward for this form.
     """
@@ -400,17 +403,20 @@ def gated_delta_rule_chunk_layer(q, k, v, a, b, A_log, dt_bias, *, gate=None,
                                  final_state_out: Optional[torch.Tensor] = None,
                                  cu_seqlens: Optional[torch.Tensor] = None
                                  ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-    """The GatedDeltaNet layer's core over a whole sequence (prefill) in one
-    kernel (gdn_chunk_fwd_layer): the gates from the raw projections, the
-    chunked forward (exact semantics), and the gated RMSNorm of every output
-    row -- what model.py:136-153 computes around chunk_gated_delta_rule_fwd
-    as separate operations.
+    """The GatedDeltaNet layer's core over a whole sequence (prefill)
+    (gdn_chunk_fwd_layer): the gates from the raw projections, the chunked
+    forward (exact semantics), and the gated RMSNorm of every output row --
+    what model.py:136-153 computes around chunk_gated_delta_rule_fwd as
+    separate operations.  One kernel at dk = dv = 128; at the other
+    tensor-core shapes (dk = 256, dv a multiple of 64 -- the reference's
+    default dk = 256, dv = 512) the chunk kernel forms the gates and a second
+    kernel normalises its output in place.
 
-    q, k ``[B,T,Hk,128]`` and v ``[B,T,H,128]`` in bfloat16; a, b ``[B,T,H]``;
-    A_log, dt_bias ``[H]``; gate ``[B,T,H,128]`` in v's dtype or None;
-    norm_weight ``[128]`` (None: ones).  Returns ``(y, final_state)`` like
+    q, k ``[B,T,Hk,dk]`` and v ``[B,T,H,dv]`` in bfloat16; a, b ``[B,T,H]``;
+    A_log, dt_bias ``[H]``; gate ``[B,T,H,dv]`` in v's dtype or None;
+    norm_weight ``[dv]`` (None: ones).  Returns ``(y, final_state)`` like
     chunk_gated_delta_rule, packed sequences included (``cu_seqlens``: one row
-    of T tokens holding N sequences, states ``[N,H,128,128]``).  Inference
+    of T tokens holding N sequences, states ``[N,H,dk,dv]``).  Inference
     only: there is no backward for this form.
     """
     return _layer_impl("gdn_chunk_fwd_layer", q, k, v, a, b, A_log, dt_bias, gate,
@@ -461,6 +467,99 @@ def _layer_impl(entry, q, k, v, a, b, A_log, dt_bias, gate, norm_weight, eps, in
     return y, hT
 
 
+def short_convolution(x, weight, *, activation: Optional[str] = "silu", conv_state=None,
+                      output_final_state: bool = False,
+                      final_state_out: Optional[torch.Tensor] = None
+                      ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """ShortConvolution (model.py:15-40) on the GPU (gdn_short_conv_fwd): a
+    causal depthwise convolution over time, kernel K, no bias, then SiLU for
+    ``activation`` ``'silu'`` / ``'swish'`` (None: none).
+
+    x ``[B,T,C]`` bfloat16 or float32 on a CUDA device; weight ``[K,C]`` or the
+    flax kernel ``[K,1,C]`` (float32).  ``conv_state`` ``[B,K-1,C]`` in x's
+    dtype replaces the zero padding before token 0 (the inputs a previous call
+    ended with).  Returns ``(y, state)``: state ``[B,K-1,C]`` holds the last
+    K - 1 inputs when ``output_final_state`` or ``final_state_out`` (which may
+    be ``conv_state``, updated in place) is given, else None.  The reference's
+    call is ``short_convolution(x, w)`` (no state).  Inference only.
+    """
+    if _wants_grad(x, conv_state):
+        raise NotImplementedError("the short convolution has no backward here")
+    if not (isinstance(x, torch.Tensor) and x.is_cuda and x.dim() == 3):
+        raise ValueError("x must be a [B,T,C] CUDA tensor")
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"x must be bfloat16 or float32; got {x.dtype}")
+    B, T, C = x.shape
+    w = torch.as_tensor(weight, device=x.device).to(torch.float32)
+    if w.dim() == 3:
+        w = w.reshape(w.shape[0], w.shape[-1])
+    if w.dim() != 2 or w.shape[1] != C:
+        raise ValueError(f"weight must be [K,{C}] or [K,1,{C}]; got {tuple(weight.shape)}")
+    K = w.shape[0]
+    w = w.contiguous()
+    act = {"silu": 1, "swish": 1, None: 0}.get(activation)
+    if act is None:
+        raise ValueError(f"activation must be 'silu', 'swish' or None; got {activation!r}")
+    x = x.contiguous()
+    if x.data_ptr() % 16:
+        x = x.clone()
+    shape = (B, K - 1, C)
+
+    def state(t, name):
+        if t is None:
+            return None
+        if tuple(t.shape) != shape or t.dtype != x.dtype or t.device != x.device:
+            raise ValueError(f"{name} must be {shape} {x.dtype} on {x.device}")
+        if not t.is_contiguous() or t.data_ptr() % 16:
+            raise ValueError(f"{name} must be contiguous and 16-byte aligned")
+        return t
+
+    s_in = state(conv_state, "conv_state")
+    s_out = state(final_state_out, "final_state_out")
+    if s_out is None and output_final_state:
+        s_out = torch.empty(shape, dtype=x.dtype, device=x.device)
+    y = torch.empty_like(x)
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.gdn_short_conv_fwd(_ptr(x), _ptr(w), _ptr(s_in), _ptr(s_out), _ptr(y), B, T, C,
+                                    K, act, _DTYPES[x.dtype],
+                                    torch.cuda.current_stream(x.device).cuda_stream)
+    _lib.check(rc, "gdn_short_conv_fwd")
+    return y, s_out
+
+
+def gated_rms_norm(o, gate=None, weight=None, eps: float = 1e-5, *,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FusedRMSNormGated (model.py:41-53) on the GPU (gdn_gated_rmsnorm_fwd):
+    ``o * rsqrt(mean(o^2, -1) + eps) * weight``, times ``silu(gate)`` when a
+    gate is given.  o ``[..., dv]`` bfloat16 or float32; gate like o or None;
+    weight ``[dv]`` (None: ones).  ``out`` may be o (in place)."""
+    if not (isinstance(o, torch.Tensor) and o.is_cuda and o.dtype in _DTYPES):
+        raise ValueError("o must be a bfloat16 or float32 CUDA tensor")
+    dv = o.shape[-1]
+    o = o.contiguous()
+    if gate is not None:
+        if gate.shape != o.shape:
+            raise ValueError(f"gate must have o's shape {tuple(o.shape)}")
+        gate = gate.to(dtype=o.dtype).contiguous()
+        if gate.data_ptr() % 16:
+            gate = gate.clone()
+    w = torch.ones(dv, dtype=torch.float32, device=o.device) if weight is None else \
+        torch.as_tensor(weight, device=o.device).to(torch.float32).contiguous()
+    if w.shape != (dv,):
+        raise ValueError(f"weight must be [{dv}]")
+    y = torch.empty_like(o) if out is None else out
+    if y.shape != o.shape or y.dtype != o.dtype or not y.is_contiguous():
+        raise ValueError("out must be a contiguous tensor of o's shape and dtype")
+    lib = _lib.load()
+    with torch.cuda.device(o.device):
+        rc = lib.gdn_gated_rmsnorm_fwd(_ptr(o), _ptr(gate), _ptr(w), float(eps), _ptr(y),
+                                       o.numel() // max(dv, 1), dv, _DTYPES[o.dtype],
+                                       torch.cuda.current_stream(o.device).cuda_stream)
+    _lib.check(rc, "gdn_gated_rmsnorm_fwd")
+    return y
+
+
 # Aliases with the reference's public names (ops.py:350-352).
 fused_recurrent_gated_delta_rule_fwd = fused_recurrent_gated_delta_rule
 fused_recurrent_gated_delta_rule_pallas = fused_recurrent_gated_delta_rule
@@ -471,4 +570,6 @@ __all__ = [
     "fused_recurrent_gated_delta_rule_fwd", "fused_recurrent_gated_delta_rule_pallas",
     "gated_delta_rule_decode_layer",
     "gated_delta_rule_chunk_layer",
+    "short_convolution",
+    "gated_rms_norm",
 ]

@@ -106,8 +106,7 @@ int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v,
                       void* workspace, size_t ws_bytes, void* stream);
 
 /*
- * The decode step with the GatedDeltaNet layer's work on either side of it,
- * in the same kernel (single token, dk = dv = 128):
+ * The recurrent op with the GatedDeltaNet layer's work on either side of it:
  *   before  beta = sigmoid(b), g = -exp(A_log[h]) * softplus(a + dt_bias[h])
  *           from the raw a_proj / b_proj outputs a, b [B, 1, H] (model.py:136-139);
  *   after   y = o * rsqrt(mean(o^2) + eps) * norm_weight, times silu(gate) when
@@ -115,9 +114,14 @@ int gdn_chunk_fwd_gva(const void* q, const void* k, const void* v,
  *           outputs (FusedRMSNormGated, model.py:41-53; gate NULL: the
  *           ungated RMSNorm of model.py:150-151).
  * The recurrent step itself is gdn_recurrent_fwd_gva's (state in / out,
- * h0 == hT in place).  y [B, 1, H, dv] in the input dtype; A_log, dt_bias [H]
- * and norm_weight [dv] fp32.  No counterpart in the reference, where these are
- * separate jax.numpy operations around the op.
+ * h0 == hT in place).  y [B, T, H, dv] in the input dtype; A_log, dt_bias [H]
+ * and norm_weight [dv] fp32 (16-byte aligned).  Single-token decode at
+ * dk = dv = 128 runs all of it in one kernel.  Other shapes: whole sequences
+ * (T >= 64) on the tensor-core shapes take gdn_chunk_fwd_layer; the rest run
+ * the general recurrent kernel with the gates formed per token, then the gated
+ * RMSNorm (gdn_gated_rmsnorm_fwd) over its output in place (dv a multiple of 8
+ * (bf16) or 4 (fp32), up to 512).  No counterpart in the reference, where these
+ * are separate jax.numpy operations around the op.
  */
 int gdn_recurrent_fwd_layer(const void* q, const void* k, const void* v,
                             const float* a, const float* b,
@@ -132,9 +136,13 @@ int gdn_recurrent_fwd_layer(const void* q, const void* k, const void* v,
  * (prefill): gdn_recurrent_fwd_layer's prologue and epilogue around
  * gdn_chunk_fwd_gva (exact semantics), for any T >= 0.  a, b [B, T, H] fp32
  * (raw a_proj / b_proj outputs); gate [B, T, H, dv] (input dtype) or NULL;
- * y [B, T, H, dv] in the input dtype.  Supported: bf16 inputs, dk = dv = 128
- * (GDN_ERR_UNSUPPORTED otherwise).  The RMS statistic is taken over the fp32
- * outputs before any rounding.  Replaces the separate operations of
+ * y [B, T, H, dv] in the input dtype.  Supported: bf16 inputs with dk = 128
+ * or 256 and dv a multiple of 64 (GDN_ERR_UNSUPPORTED otherwise; dk = 256,
+ * dv = 512 are the reference's default head dims).  At dk = dv = 128 it is one
+ * launch, and the RMS statistic is taken over the fp32 outputs before any
+ * rounding; at the other shapes the chunk kernel forms the gates itself and
+ * writes o into y, and a second launch normalises y in place (the statistic
+ * over the bf16 o).  Replaces the separate operations of
  * model.py:136-139 and :147-153 around chunk_gated_delta_rule_fwd
  * (ops.py:299); no single counterpart in the reference.
  */
@@ -337,6 +345,34 @@ const char* gdn_last_error(void);
  */
 void gdn_reload_kernel_overrides(void);
 
+/*
+ * The layer's short convolution (ShortConvolution, model.py:15-40, applied to
+ * q, k and v at :119-122): a causal depthwise convolution over time with
+ * kernel K (no bias), then SiLU when activation = 1 (0: none):
+ *   y[b, t, c] = act(sum_j weight[j, c] * x[b, t - (K - 1) + j, c]),
+ * with the inputs before token 0 taken from state_in [B, K - 1, C] (x's
+ * dtype; NULL: zeros, the reference's left padding).  state_out [B, K - 1, C]
+ * (NULL: not wanted) receives the last K - 1 inputs, for the next decode
+ * step; it may be state_in (in place).  x, y [B, T, C] bf16 or fp32; weight
+ * [K, C] fp32 (the flax kernel (K, 1, C) as stored).  C a multiple of 8
+ * (bf16) or 4 (fp32), K <= 8, 16-byte aligned pointers.  The reference's
+ * layer has no conv state (it reruns whole sequences); with state_in = NULL
+ * and state_out = NULL this is its call.
+ */
+int gdn_short_conv_fwd(const void* x, const float* weight, const void* state_in,
+                       void* state_out, void* y, int B, int T, int C, int K,
+                       int activation, int dtype, void* stream);
+
+/*
+ * FusedRMSNormGated (model.py:41-53) over `rows` rows of dv elements:
+ * y = o * rsqrt(mean(o^2) + eps) * weight, times silu(gate) when gate (same
+ * shape as o) is given.  o, gate, y bf16 or fp32 (dtype); weight [dv] fp32;
+ * y may be o (in place).  dv a multiple of 8 (bf16) or 4 (fp32), up to 1024 /
+ * 512.
+ */
+int gdn_gated_rmsnorm_fwd(const void* o, const void* gate, const float* weight, float eps,
+                          void* y, long long rows, int dv, int dtype, void* stream);
+
 /* ABI version of this header: (major << 16) | minor (1.3: _gva, _varlen, backward;
  * 1.4: backward of packed sequences, the allocation-free backward;
  * 1.5: the layer form of the decode step; 1.6: the layer form of the chunked
@@ -344,7 +380,9 @@ void gdn_reload_kernel_overrides(void);
  * for fp32 inputs, gdn_chunk_varlen_workspace_bytes; 1.8: the two-launch chunked
  * forward and its workspace (bf16, dk = 128), gdn_chunk_prepare / gdn_chunk_scan,
  * gdn_fold_states,
- * gdn_reload_kernel_overrides, gdn_binary_version). */
+ * gdn_reload_kernel_overrides, gdn_binary_version; 1.9: the layer forms at
+ * the other tensor-core shapes and the general recurrent shapes,
+ * gdn_short_conv_fwd, gdn_gated_rmsnorm_fwd). */
 int gdn_abi_version(void);
 
 /*

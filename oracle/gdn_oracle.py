@@ -519,10 +519,35 @@ def rms_norm_gated(o, weight, gate=None, eps=1e-5, dtype=np.float64):
     return y
 
 
+def short_conv(x, weight, activation="silu", state=None, dtype=np.float64):
+    """ShortConvolution (model.py:15-40): ``nnx.Conv`` with
+    ``feature_group_count = C`` (depthwise), kernel ``K``, no bias and padding
+    ``[(K - 1, 0)]`` (causal), then SiLU for ``'silu'`` / ``'swish'``:
+
+        y[b, t, c] = act(sum_j w[j, c] * x[b, t - (K - 1) + j, c])
+
+    x [B, T, C]; weight [K, C] (the flax kernel (K, 1, C) squeezed).  ``state``
+    [B, K - 1, C] stands in for the zero padding (the K - 1 inputs before token
+    0).  Returns (y, the last K - 1 inputs, the state a next call continues
+    from)."""
+    x = np.asarray(x, dtype)
+    w = np.asarray(weight, dtype).reshape(-1, x.shape[-1])
+    K = w.shape[0]
+    B, T, C = x.shape
+    pad = np.zeros((B, K - 1, C), dtype) if state is None else np.asarray(state, dtype)
+    xe = np.concatenate([pad, x], axis=1)          # token t of x is row t + K - 1
+    y = np.zeros((B, T, C), dtype)
+    for j in range(K):
+        y += w[j] * xe[:, j:j + T]
+    if activation in ("silu", "swish"):
+        y = y / (1.0 + np.exp(-y))
+    return y, xe[:, T:T + K - 1].copy()
+
+
 __all__ = [
     "make_inputs", "round_bf16", "recurrent_ref", "chunk_exact",
     "chunk_reference_literal", "literal_output_permutation", "segment_transition",
     "two_pass_sp", "TOL_FP32_ABS", "TOL_BF16_REL", "max_abs_err", "rel_err",
-    "within_tolerance", "layer_gates", "rms_norm_gated",
+    "within_tolerance", "layer_gates", "rms_norm_gated", "short_conv",
 ]
 

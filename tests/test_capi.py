@@ -169,9 +169,7 @@ def test_decode_layer_rejects_bad_arguments(lib):
     def call(T=1, dk=128, dv=128, A=p, gate=None, w=p, eps=1e-5):
         return lib.gdn_recurrent_fwd_layer(p, p, p, p, p, A, p, None, None, gate, w, eps, p,
                                            2, T, 2, 2, dk, dv, _lib.GDN_DTYPE_BF16, None)
-    assert call(T=2) == _lib.GDN_ERR_UNSUPPORTED
-    assert b"single-token" in lib.gdn_last_error()
-    assert call(dk=64, dv=64) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(dk=48) == _lib.GDN_ERR_UNSUPPORTED
     assert call(A=None) == _lib.GDN_ERR_INVALID
     assert call(w=None) == _lib.GDN_ERR_INVALID
     assert call(w=ctypes.c_void_p(20)) == _lib.GDN_ERR_INVALID
@@ -189,11 +187,51 @@ def test_chunk_layer_rejects_bad_arguments(lib):
     assert call(dtype=_lib.GDN_DTYPE_FP32) == _lib.GDN_ERR_UNSUPPORTED
     assert b"bf16" in lib.gdn_last_error()
     assert call(dk=64, dv=64) == _lib.GDN_ERR_UNSUPPORTED
-    assert call(dv=256) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(dv=96) == _lib.GDN_ERR_UNSUPPORTED
+    assert b"multiple of 64" in lib.gdn_last_error()
     assert call(A=None) == _lib.GDN_ERR_INVALID
     assert call(w=None) == _lib.GDN_ERR_INVALID
     assert call(gate=ctypes.c_void_p(24)) == _lib.GDN_ERR_INVALID
     assert call(eps=float("nan")) == _lib.GDN_ERR_INVALID
+
+
+def test_short_conv_rejects_bad_arguments(lib):
+    """Checked on the host before any CUDA call."""
+    p = ctypes.c_void_p(16)
+    bf16, fp32 = _lib.GDN_DTYPE_BF16, _lib.GDN_DTYPE_FP32
+
+    def call(x=p, w=p, si=None, so=None, y=p, B=2, T=10, C=64, K=4, act=1, dtype=bf16):
+        return lib.gdn_short_conv_fwd(x, w, si, so, y, B, T, C, K, act, dtype, None)
+    assert call(K=0) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(K=9) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(C=60) == _lib.GDN_ERR_UNSUPPORTED          # bf16: multiple of 8
+    assert call(C=62, dtype=fp32) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(act=2) == _lib.GDN_ERR_INVALID
+    assert call(dtype=7) == _lib.GDN_ERR_INVALID
+    assert call(w=None) == _lib.GDN_ERR_INVALID
+    assert call(w=ctypes.c_void_p(20)) == _lib.GDN_ERR_INVALID
+    assert call(x=ctypes.c_void_p(24)) == _lib.GDN_ERR_INVALID
+    assert call(si=ctypes.c_void_p(40)) == _lib.GDN_ERR_INVALID
+    assert call(B=-1) == _lib.GDN_ERR_INVALID
+    assert call(B=0) == _lib.GDN_OK and call(C=0) == _lib.GDN_OK
+    assert call(T=0) == _lib.GDN_OK                          # no state to carry
+
+
+def test_gated_rmsnorm_rejects_bad_arguments(lib):
+    """Checked on the host before any CUDA call."""
+    p = ctypes.c_void_p(16)
+    bf16, fp32 = _lib.GDN_DTYPE_BF16, _lib.GDN_DTYPE_FP32
+
+    def call(o=p, gate=None, w=p, eps=1e-5, y=p, rows=4, dv=128, dtype=bf16):
+        return lib.gdn_gated_rmsnorm_fwd(o, gate, w, eps, y, rows, dv, dtype, None)
+    assert call(dv=100) == _lib.GDN_ERR_UNSUPPORTED          # bf16: multiple of 8
+    assert call(dv=2048) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(dv=1024, dtype=fp32) == _lib.GDN_ERR_UNSUPPORTED
+    assert call(eps=-1.0) == _lib.GDN_ERR_INVALID
+    assert call(w=None) == _lib.GDN_ERR_INVALID
+    assert call(gate=ctypes.c_void_p(24)) == _lib.GDN_ERR_INVALID
+    assert call(rows=-1) == _lib.GDN_ERR_INVALID
+    assert call(rows=0) == _lib.GDN_OK
 
 
 def test_chunk_layer_varlen_rejects_bad_arguments(lib):

@@ -211,3 +211,45 @@ def test_oracle_linear_in_values_and_state(chunked):
     o3, s3 = run(v1 + 2 * v2, h1 + 2 * h2)
     np.testing.assert_allclose(o3, o1 + 2 * o2, rtol=0, atol=1e-10)
     np.testing.assert_allclose(s3, s1 + 2 * s2, rtol=0, atol=1e-10)
+
+
+@pytest.mark.parametrize("K", [1, 2, 4])
+@pytest.mark.parametrize("activation", ["silu", None])
+def test_short_conv_matches_grouped_conv1d(K, activation):
+    """The oracle's ShortConvolution (model.py:15-40) against torch's grouped
+    conv1d with the same definition: feature_group_count = C (depthwise),
+    left padding K - 1, cross-correlation (no kernel flip), no bias."""
+    import torch
+    rng = np.random.default_rng(K)
+    B, T, C = 2, 13, 24
+    x = rng.standard_normal((B, T, C))
+    w = rng.standard_normal((K, C))
+    y, st = orc.short_conv(x, w, activation)
+    xt = torch.tensor(x).permute(0, 2, 1)                       # [B, C, T]
+    wt = torch.tensor(w).t().reshape(C, 1, K)                   # [C, 1, K]
+    ref = torch.nn.functional.conv1d(torch.nn.functional.pad(xt, (K - 1, 0)), wt, groups=C)
+    if activation == "silu":
+        ref = torch.nn.functional.silu(ref)
+    np.testing.assert_allclose(y, ref.permute(0, 2, 1).numpy(), rtol=1e-12, atol=1e-12)
+    np.testing.assert_array_equal(st, x[:, T - (K - 1):T] if K > 1 else x[:, :0])
+
+
+def test_short_conv_state_carries_across_calls():
+    """A sequence convolved in two calls, the first call's final state passed
+    to the second, equals one call over the whole sequence (decode
+    continuity); short calls (T < K - 1) keep part of the incoming state."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((3, 20, 16))
+    w = rng.standard_normal((4, 16))
+    y, st = orc.short_conv(x, w)
+    for cut in (1, 2, 7, 19):
+        y1, s1 = orc.short_conv(x[:, :cut], w)
+        y2, s2 = orc.short_conv(x[:, cut:], w, state=s1)
+        np.testing.assert_allclose(np.concatenate([y1, y2], 1), y, rtol=1e-12, atol=1e-12)
+        np.testing.assert_array_equal(s2, st)
+    # one token at a time
+    s, ys = None, []
+    for t in range(20):
+        yt, s = orc.short_conv(x[:, t:t + 1], w, state=s)
+        ys.append(yt)
+    np.testing.assert_allclose(np.concatenate(ys, 1), y, rtol=1e-12, atol=1e-12)
