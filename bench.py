@@ -739,6 +739,91 @@ def prefill_layer_leg(d, a):
                     "precomputed gates and no norm"}
 
 
+def prefill_layer_default_leg(d, a):
+    """The layer core at the reference's default head dims (head_dim 256,
+    expand_v 2: dk=256, dv=512; 6 heads; B=8 T=2048), from the raw q/k/v
+    projection outputs: the short convolution + SiLU of q, k and v
+    (model.py:15-40, :119-122), the gates from the raw a/b projections
+    (:136-139), the chunked forward, the gated RMSNorm of every output row
+    (:41-53, :147-153).  Two ways: this library's kernels (gdn_short_conv_fwd
+    three times, gdn_chunk_fwd_layer) against the same operations done
+    separately in torch around the op, as the reference layer does them."""
+    import torch
+    import torch.nn.functional as F
+    from gated_deltanet_jax_b200 import ops
+    B, T, H, dk, dv, KC = 8, 2048, 6, 256, 512, 4
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(5150 + d.rank)
+    # raw projection outputs scaled so that the convolved keys and queries have
+    # norms of order one (the reference normalises neither)
+    xq = (torch.randn(B, T, H * dk, device=d.dev, generator=gen) / dk ** 0.5).bfloat16()
+    xk = (torch.randn(B, T, H * dk, device=d.dev, generator=gen) / dk ** 0.5).bfloat16()
+    xv = torch.randn(B, T, H * dv, device=d.dev, generator=gen).bfloat16()
+    wq, wk, wv = (torch.randn(KC, c, device=d.dev, generator=gen) * 0.5
+                  for c in (H * dk, H * dk, H * dv))
+    ra = torch.randn(B, T, H, device=d.dev, generator=gen)
+    rb = torch.randn(B, T, H, device=d.dev, generator=gen)
+    gate = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
+    A_log, dt_bias = _layer_gate_params(H, d.dev, gen)
+    w = torch.ones(dv, device=d.dev)
+    hT = torch.empty(B, H, dk, dv, device=d.dev)
+
+    def fused():
+        q, _ = ops.short_convolution(xq, wq)
+        k, _ = ops.short_convolution(xk, wk)
+        v, _ = ops.short_convolution(xv, wv)
+        ops.gated_delta_rule_chunk_layer(q.view(B, T, H, dk), k.view(B, T, H, dk),
+                                         v.view(B, T, H, dv), ra, rb, A_log, dt_bias,
+                                         gate=gate, norm_weight=w, final_state_out=hT)
+
+    def conv_t(x, wt):   # depthwise causal conv1d + SiLU, as separate torch operations
+        C = x.shape[-1]
+        y = F.conv1d(F.pad(x.transpose(1, 2), (KC - 1, 0)), wt.t().unsqueeze(1).to(x.dtype),
+                     groups=C)
+        return F.silu(y).transpose(1, 2)
+
+    def unfused():
+        q = conv_t(xq, wq).reshape(B, T, H, dk)
+        k = conv_t(xk, wk).reshape(B, T, H, dk)
+        v = conv_t(xv, wv).reshape(B, T, H, dv)
+        gd = -torch.exp(A_log) * F.softplus(ra + dt_bias)
+        bd = torch.sigmoid(rb)
+        o, _ = ops.chunk_gated_delta_rule(q, k, v, gd, bd, final_state_out=hT)
+        x = o.float()
+        var = x.pow(2).mean(-1, keepdim=True)
+        (x * torch.rsqrt(var + 1e-5) * w * F.silu(gate.float())).to(o.dtype)
+
+    REP = 4
+    res = {}
+    steps = max(1, min(a.steps, 20))
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        fn()                                   # load modules, allocate
+        torch.cuda.synchronize(d.dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(REP):
+                fn()
+        for _ in range(a.warmup):
+            graph.replay()
+        ms, _ = _timed(d, graph.replay, steps)
+        res[name] = ms / REP
+        del graph
+    return {"workload": "the layer core at the reference's default head dims, B=8 T=2048 H=6 "
+                        "dk=256 dv=512 bf16: short conv (kernel 4) + SiLU of the raw q/k/v "
+                        "projections, gates from raw a/b projections, chunked forward, gated "
+                        "RMSNorm (eps 1e-5) of every output row; final state out; 4 calls per "
+                        "CUDA graph",
+            "fused_ms": res["fused"], "unfused_ms": res["unfused"],
+            "speedup": res["unfused"] / res["fused"],
+            # fused: three convolutions, the chunk kernel, the in-place norm
+            "launches": 5 * REP * steps,
+            "fused_tokens_per_s": d.world * B * T / (res["fused"] / 1e3),
+            "path": "fused: gdn_short_conv_fwd x3, gdn_chunk_fwd_layer (the dk=256 tcgen05 "
+                    "kernel forms the gates; a second launch normalises the output in place); "
+                    "unfused: torch conv1d + SiLU, torch gates, gdn_chunk_fwd, torch gated "
+                    "RMSNorm"}
+
+
 def model_core_leg(d, a):
     """The delta-rule core of the reference's default model configuration
     (head_dim 256, expand_v 2: dk=256, dv=512; 6 heads; B=8 T=2048 as the
@@ -1012,6 +1097,7 @@ def main():
     bwd = None if a.no_backward else backward_leg(d, a, lib)
     lay = None if a.no_layer else decode_layer_leg(d, a)
     play = None if (a.no_layer or a.no_prefill) else prefill_layer_leg(d, a)
+    pdef = None if (a.no_layer or a.no_prefill) else prefill_layer_default_leg(d, a)
     mcore = None if a.no_prefill else model_core_leg(d, a)
 
     cpu = None
@@ -1043,6 +1129,7 @@ def main():
             "gpu_launches": (dec["launches"] + (pre["launches"] if pre else 0)
                              + (bwd["launches"] if bwd else 0) + (lay["launches"] if lay else 0)
                              + (play["launches"] if play else 0)
+                             + (pdef["launches"] if pdef else 0)
                              + (mcore["launches"] if mcore else 0)
                              + (lng["launches"] if lng else 0)),
             "clocks": dec["clocks"],
@@ -1086,6 +1173,8 @@ def main():
             line["decode_layer"] = lay
         if play:
             line["prefill_layer"] = play
+        if pdef:
+            line["prefill_layer_default_dims"] = pdef
         if mcore:
             line["model_config_core"] = mcore
         if bwd:

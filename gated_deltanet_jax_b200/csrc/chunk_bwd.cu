@@ -1189,7 +1189,15 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   if (e == cudaSuccess) e = ensure_smem(bwd_grads_kernel<Tin>, grads_bytes, set_grads);
   if (e != cudaSuccess) return e;
   if (packed) bwd_chunk_offsets_kernel<<<1, 1024, 0, st>>>(a.cu_seqlens, a.B, a.T, NC, coff);
-  bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);
+  if (sizeof(Tin) == 2 && bwd_prep_tc_supported(a.dtype, a.dk, a.dv) &&
+      !kernel_overrides().bwd_prep_warp) {
+    // bf16, dk = dv = 128: the per-chunk preparation on tcgen05
+    e = launch_bwd_prep_tc(a.q, a.k, a.v, a.dO, a.g, a.beta, p.W, p.Z, p.UV, p.YX, a.cu_seqlens,
+                           coff, packed ? a.B : 0, NC, a.B, a.T, a.H, a.Hk, st);
+    if (e != cudaSuccess) return e;
+  } else {
+    bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);
+  }
   bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 2), NT, states_bytes, st>>>(p);
   bwd_grads_kernel<Tin><<<dim3(NC, a.H), NT, grads_bytes, st>>>(p);
   if (a.Hk != a.H) {

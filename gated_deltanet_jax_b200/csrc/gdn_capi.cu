@@ -27,13 +27,15 @@ KernelOverrides read_overrides() {
   k.recurrent_token = rec && strcmp(rec, "token") == 0;
   const char* pdl = getenv("GDN_DECODE_PDL");
   k.decode_pdl = !(pdl && pdl[0] == '0');
+  const char* bprep = getenv("GDN_BWD_PREP");
+  k.bwd_prep_warp = bprep && strcmp(bprep, "warp") == 0;
   return k;
 }
 
 // The current choices, packed into one word so that a reload is atomic.
 int pack(const KernelOverrides& k) {
   return (k.chunk_simt ? 1 : 0) | (k.chunk_fused ? 2 : 0) | ((k.tc_pair + 1) << 2) |
-         (k.recurrent_token ? 16 : 0) | (k.decode_pdl ? 32 : 0);
+         (k.recurrent_token ? 16 : 0) | (k.decode_pdl ? 32 : 0) | (k.bwd_prep_warp ? 64 : 0);
 }
 
 std::atomic<int>& override_word() {
@@ -51,6 +53,7 @@ KernelOverrides kernel_overrides() {
   k.tc_pair = ((w >> 2) & 3) - 1;
   k.recurrent_token = (w & 16) != 0;
   k.decode_pdl = (w & 32) != 0;
+  k.bwd_prep_warp = (w & 64) != 0;
   return k;
 }
 
@@ -610,7 +613,8 @@ int gdn_device_error(int clear) {
   const int a = gdn::device_error_recurrent_bulk(clear != 0);
   const int b = gdn::device_error_chunk_tc(clear != 0);
   const int c = gdn::device_error_chunk_scan(clear != 0);
-  return a ? a : (b ? b : c);
+  const int d = gdn::device_error_bwd_prep(clear != 0);
+  return a ? a : (b ? b : (c ? c : d));
 }
 
 int gdn_abi_version(void) { return (1 << 16) | 9; }

@@ -57,12 +57,14 @@ inline int device_sm_count() {
 //   GDN_CHUNK_TC_PAIR=0 / 1  its unpaired / paired form
 //   GDN_RECURRENT_KERNEL=token  the token loop for whole sequences
 //   GDN_DECODE_PDL=0         decode steps without programmatic dependent launch
+//   GDN_BWD_PREP=warp        the backward's warp-level per-chunk preparation
 struct KernelOverrides {
   bool chunk_simt = false;
   bool chunk_fused = false;
   int tc_pair = -1;  // -1: by occupancy
   bool recurrent_token = false;
   bool decode_pdl = true;
+  bool bwd_prep_warp = false;
 };
 KernelOverrides kernel_overrides();
 
@@ -192,6 +194,19 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
 int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
 int chunk_scan_binary_version();
+
+// The backward's per-chunk preparation on tcgen05 (chunk_bwd_prep.cu): W, Z, U, Y
+// of every (chunk, head) into the backward's fp32 workspace (rows (gc H + h) C of
+// global chunk gc, strides dk and dv).  bf16, dk = dv = 128.  Dense: n_seqs = 0,
+// B rows of T tokens, NC = B ceil(T / 64).  Packed: n_seqs sequences in one row
+// of T tokens (cu, n_seqs + 1 device offsets), coff their chunk offsets on the
+// device, NC an upper bound of the chunks.
+bool bwd_prep_tc_supported(int dtype, int dk, int dv);
+cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, const void* dO,
+                               const float* g, const float* beta, float* W, float* Z, float* U,
+                               float* Y, const int* cu, const int* coff, int n_seqs, int NC,
+                               int B, int T, int H, int Hk, cudaStream_t st);
+int device_error_bwd_prep(bool clear);
 
 // The layer's elementwise work (layer_ops.cu).  Short convolution + SiLU
 // (model.py:15-40): x, y [B,T,C], w [K,C] fp32, states [B,K-1,C] in x's dtype;

@@ -207,3 +207,60 @@ def test_autograd_through_packed_chunk_op(cuda):
     o2, h2 = ops.chunk_gated_delta_rule(q, k, v, g, b, initial_state=h0, output_final_state=True,
                                         cu_seqlens=cu)
     assert torch.equal(o.detach(), o2) and torch.equal(hT.detach(), h2)
+
+
+# The per-chunk preparation at bf16, dk = dv = 128 on dense rows runs on the
+# tcgen05 kernel (bf16 operands, fp32 accumulation); GDN_BWD_PREP=warp keeps
+# the warp-level one (tf32 operands) for cross-checks.  Both against the
+# oracle: partial last chunks, several rows, grouped q/k heads, state in/out.
+@pytest.mark.parametrize("prep", ["tcgen05", "warp"])
+@pytest.mark.parametrize("B,T,H,Hk,with_h0,with_dhT", [(1, 64, 1, 1, False, False),
+                                                       (2, 100, 3, 3, True, True),
+                                                       (1, 300, 4, 2, True, False),
+                                                       (3, 129, 2, 1, False, True)])
+def test_backward_preparation_forms_against_oracle(cuda, prep, B, T, H, Hk, with_h0, with_dhT):
+    from gated_deltanet_jax_b200 import _lib
+    dk = dv = 128
+    (q, k, v, g, b, h0), host = device_inputs(B, T, H, dk, dv, seed=T + H, dtype="bf16", dev=cuda,
+                                              h0_std=0.05 if with_h0 else None)
+    rep = H // Hk
+    if rep > 1:   # q/k with Hk heads; the oracle sees them repeated
+        q, k = q[:, :, ::rep].contiguous(), k[:, :, ::rep].contiguous()
+        host = list(host)
+        host[0] = f64(q.float().repeat_interleave(rep, 2))
+        host[1] = f64(k.float().repeat_interleave(rep, 2))
+    gen = torch.Generator(device=cuda).manual_seed(T)
+    do = torch.randn(B, T, H, dv, device=cuda, generator=gen).bfloat16()
+    dhT = torch.randn(B, H, dk, dv, device=cuda, generator=gen) if with_dhT else None
+    with _lib.kernel_env("GDN_BWD_PREP", "warp" if prep == "warp" else None):
+        got = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
+    ref = orc.chunk_exact_backward(*host[:5], host[5], f64(do), None if dhT is None else f64(dhT),
+                                   64)
+    if rep > 1:   # the gradients of the shared q/k heads sum over each group
+        ref = list(ref)
+        for idx in (0, 1):
+            r = ref[idx]
+            ref[idx] = r.reshape(B, T, Hk, rep, dk).sum(3)
+    _check(got, ref, "bf16", with_h0=with_h0)
+    assert _lib.load().gdn_device_error(1) == 0
+
+
+def test_backward_preparation_forms_agree_at_size(cuda):
+    """B=2 T=2048 H=8 dk=dv=128 bf16: the tcgen05 preparation's gradients
+    against the warp-level one's (tf32 operands), within the bf16 bar; and
+    repeated calls of the tcgen05 form are bit-identical."""
+    from gated_deltanet_jax_b200 import _lib
+    B, T, H, dk, dv = 2, 2048, 8, 128, 128
+    (q, k, v, g, b, h0), _ = device_inputs(B, T, H, dk, dv, seed=21, dtype="bf16", dev=cuda,
+                                           h0_std=0.05)
+    gen = torch.Generator(device=cuda).manual_seed(22)
+    do = torch.randn(B, T, H, dv, device=cuda, generator=gen).bfloat16()
+    dhT = torch.randn(B, H, dk, dv, device=cuda, generator=gen)
+    tc = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
+    tc2 = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
+    with _lib.kernel_env("GDN_BWD_PREP", "warp"):
+        wp = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
+    for n, a, a2, r in zip(["dq", "dk", "dv", "dg", "dbeta", "dh0"], tc, tc2, wp):
+        assert torch.equal(a, a2), n
+        err = orc.rel_err(f64(a), f64(r))
+        assert err <= TOL["bf16"], f"{n}: rel error {err:.2e}"
