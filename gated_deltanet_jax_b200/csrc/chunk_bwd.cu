@@ -84,6 +84,8 @@ struct BwdParams {
   // The forward on these kernels (dO == NULL): the final state (or NULL) and o.
   float* hTout = nullptr;
   void* o = nullptr;
+  // The state kernel's reverse direction only (the forward pass ran elsewhere).
+  int rev_only = 0;
 };
 
 // Tokens and chunks of sequence s.
@@ -569,7 +571,7 @@ __global__ void __launch_bounds__(NT, DKP == 256 ? 1 : 2) bwd_states_kernel(cons
   const Tin* dO = static_cast<const Tin*>(p.dO);
   const int c0 = blockIdx.x * VT, bh = blockIdx.y, sq = bh / p.H, h = bh - sq * p.H;
   const int hq = h * p.Hk / p.H, tid = threadIdx.x, w = tid >> 5;
-  const bool rev = blockIdx.z != 0;
+  const bool rev = blockIdx.z != 0 || p.rev_only;
   const SeqSpan sp = seq_span(p, sq);
   const size_t bT = sp.tok0;
   const int Tn = sp.len;
@@ -1133,7 +1135,7 @@ __global__ void __launch_bounds__(1024) bwd_chunk_offsets_kernel(const int* cu, 
 
 // Workspace: offsets in floats, each array on a 256-byte boundary.
 struct WsLayout {
-  size_t W, Z, UV, YX, hs, dhs, dqk, coff, total;
+  size_t W, Z, UV, YX, hs, dhs, dqk, coff, tiles, total;
 };
 
 int padded_dk(int dk) { return dk <= 32 ? 32 : dk <= 64 ? 64 : dk <= 128 ? 128 : 256; }
@@ -1152,6 +1154,9 @@ WsLayout ws_layout(size_t NC, size_t tokens, int H, int dk, int dv, int n_seqs) 
   L.dhs = take(NC * H * dk * dv);
   L.dqk = take(2 * tokens * H * dk);
   L.coff = take(n_seqs ? (size_t)n_seqs + 1 : 0);
+  // dense bf16 dk = dv = 128: the [T | Z] tiles of the forward pass on the scan
+  // kernel (24 KB per chunk and head; reserved whatever the input type)
+  L.tiles = take(!n_seqs && dk == 128 && dv == 128 ? NC * H * (24576 / sizeof(float)) : 0);
   L.total = o;
   return L;
 }
@@ -1189,16 +1194,37 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   if (e == cudaSuccess) e = ensure_smem(bwd_grads_kernel<Tin>, grads_bytes, set_grads);
   if (e != cudaSuccess) return e;
   if (packed) bwd_chunk_offsets_kernel<<<1, 1024, 0, st>>>(a.cu_seqlens, a.B, a.T, NC, coff);
-  if (sizeof(Tin) == 2 && bwd_prep_tc_supported(a.dtype, a.dk, a.dv) &&
-      !kernel_overrides().bwd_prep_warp) {
-    // bf16, dk = dv = 128: the per-chunk preparation on tcgen05
-    e = launch_bwd_prep_tc(a.q, a.k, a.v, a.dO, a.g, a.beta, p.W, p.Z, p.UV, p.YX, a.cu_seqlens,
+  const KernelOverrides ov = kernel_overrides();
+  // bf16, dk = dv = 128: the per-chunk preparation on tcgen05; on dense rows
+  // also the forward pass (every chunk's entering state and V') on the scan
+  // kernel, so that the state kernel runs the reverse direction alone
+  const bool tc_prep = sizeof(Tin) == 2 && bwd_prep_tc_supported(a.dtype, a.dk, a.dv) &&
+                       !ov.bwd_prep_warp;
+  const bool tc_fwd = tc_prep && !packed && L.tiles != L.total && !ov.bwd_fwdpass_warp;
+  unsigned char* tiles = reinterpret_cast<unsigned char*>(ws + L.tiles);
+  if (tc_prep) {
+    e = launch_bwd_prep_tc(a.q, a.k, a.v, a.dO, a.g, a.beta, tc_fwd ? nullptr : p.W, p.Z,
+                           tc_fwd ? nullptr : p.UV, p.YX, tc_fwd ? tiles : nullptr, a.cu_seqlens,
                            coff, packed ? a.B : 0, NC, a.B, a.T, a.H, a.Hk, st);
     if (e != cudaSuccess) return e;
   } else {
     bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);
   }
-  bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 2), NT, states_bytes, st>>>(p);
+  if (tc_fwd) {
+    ChunkArgs fa{};
+    fa.q = a.q; fa.k = a.k; fa.v = a.v; fa.g = a.g; fa.beta = a.beta; fa.h0 = a.h0;
+    fa.B = a.B; fa.T = a.T; fa.H = a.H; fa.Hk = a.Hk; fa.dk = a.dk; fa.dv = a.dv;
+    fa.chunk = C; fa.dtype = a.dtype; fa.semantics = kExact;
+    fa.workspace = tiles;
+    fa.ws_bytes = (L.total - L.tiles) * sizeof(float);
+    e = launch_chunk_scan_bwd(fa, p.hs, p.UV, st);
+    if (e != cudaSuccess) return e;
+    BwdParams pr = p;
+    pr.rev_only = 1;
+    bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 1), NT, states_bytes, st>>>(pr);
+  } else {
+    bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 2), NT, states_bytes, st>>>(p);
+  }
   bwd_grads_kernel<Tin><<<dim3(NC, a.H), NT, grads_bytes, st>>>(p);
   if (a.Hk != a.H) {
     const size_t total = (size_t)p.B * a.T * a.Hk * a.dk;

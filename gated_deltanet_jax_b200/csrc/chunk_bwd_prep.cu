@@ -96,7 +96,8 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                    const float* __restrict__ g, const float* __restrict__ beta,
                    float* __restrict__ Wg, float* __restrict__ Zg, float* __restrict__ Ug,
-                   float* __restrict__ Yg, const int* __restrict__ cu,
+                   float* __restrict__ Yg, unsigned char* __restrict__ tiles,
+                   const int* __restrict__ cu,
                    const int* __restrict__ coff, int n_seqs, int B, int T, int H, int Hk,
                    int N) {
   using L = BpLay;
@@ -108,6 +109,7 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   VecBuf* vecs = reinterpret_cast<VecBuf*>(sm + L::SM_VEC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool wu = Wg != nullptr;   // W and U wanted (the warp-level forward pass reads them)
   // Items w = blockIdx.x + j gridDim.x: value head h = w % H of global chunk
   // gc = w / H, whose workspace rows are (gc H + h) C ...  Dense: chunk n of
   // row b is gc = b N + n.  Packed (n_seqs > 0): B = 1 row of T tokens, and
@@ -222,16 +224,19 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint64_t a = umma_desc(st + L::ST_KQ + k * 2048, 16384, 1024, SW128);
-          mma_bf16(tmem + BT_W, a, umma_desc(sbase + L::SM_TBE + k * 32, 16, 1024, SW128),
-                   IDESC_MK, k > 0);
+          if (wu)
+            mma_bf16(tmem + BT_W, a, umma_desc(sbase + L::SM_TBE + k * 32, 16, 1024, SW128),
+                     IDESC_MK, k > 0);
           mma_bf16(tmem + BT_Z, a, umma_desc(sbase + L::SM_TD + k * 2048, 8192, 1024, SW128),
                    IDESC_MM, k > 0);
         }
         // U^T = V^T (T diag(beta))^T: A = V^T, M = dv in two blocks 8 KB apart
+        if (wu) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + BT_U, umma_desc(st + L::ST_V + k * 2048, 8192, 1024, SW128),
-                   umma_desc(sbase + L::SM_TB + k * 32, 16, 1024, SW128), IDESC_MK, k > 0);
+          for (int k = 0; k < 4; ++k)
+            mma_bf16(tmem + BT_U, umma_desc(st + L::ST_V + k * 2048, 8192, 1024, SW128),
+                     umma_desc(sbase + L::SM_TB + k * 32, 16, 1024, SW128), IDESC_MK, k > 0);
+        }
         mma_commit(&bars[B_MMA1]);
         // the next item's first product (its buffer's last reader, this
         // item's A/P pass, finished before B_TP)
@@ -405,16 +410,35 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
       // 32 ch .. 32 ch + 31: one 128-byte row segment per store of the warp
       {
         float x[32];
-        tmem_ld32(tmem + BT_W + (uint32_t)ch * 32 + lane_off, x);
+        if (wu) {
+          tmem_ld32(tmem + BT_W + (uint32_t)ch * 32 + lane_off, x);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) Wg[(row0 + 32 * ch + e) * BP_DK + p] = x[e];
+          for (int e = 0; e < 32; ++e) Wg[(row0 + 32 * ch + e) * BP_DK + p] = x[e];
+        }
         tmem_ld32(tmem + BT_Z + (uint32_t)ch * 32 + lane_off, x);
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          Zg[(row0 + 32 * ch + e) * BP_DK + p] = 32 * ch + e < it.len ? x[e] : 0.f;
-        tmem_ld32(tmem + BT_U + (uint32_t)ch * 32 + lane_off, x);
+        for (int e = 0; e < 32; ++e) {
+          if (32 * ch + e >= it.len) x[e] = 0.f;
+          Zg[(row0 + 32 * ch + e) * BP_DK + p] = x[e];
+        }
+        if (tiles) {
+          // the scan's tile of (head, chunk): T (rows 0-63 of [T; P], as
+          // stored) then Z^T = K^T diag(d) T (row = key dimension p), bf16,
+          // 128-byte swizzled
+          unsigned char* tile =
+              tiles + ((size_t)(it.b * H + it.h) * N + (it.gc - it.b * N)) * 24576;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) Ug[(row0 + 32 * ch + e) * BP_DV + p] = x[e];
+          for (int c8 = 0; c8 < 4; ++c8)
+            *reinterpret_cast<uint4*>(tile + 8192 + sw128(p, 4 * ch + c8)) =
+                pack_bf16x8(x + 8 * c8);
+          for (int e = pi; e < 512; e += 256)
+            reinterpret_cast<uint4*>(tile)[e] = reinterpret_cast<const uint4*>(tpt)[e];
+        }
+        if (wu) {
+          tmem_ld32(tmem + BT_U + (uint32_t)ch * 32 + lane_off, x);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) Ug[(row0 + 32 * ch + e) * BP_DV + p] = x[e];
+        }
         ok = mbar_wait(&bars[B_MMA2], (uint32_t)j & 1u) && ok;
         tc_fence_after();
         tmem_ld32(tmem + BT_Y + (uint32_t)ch * 32 + lane_off, x);
@@ -443,8 +467,9 @@ bool bwd_prep_tc_supported(int dtype, int dk, int dv) {
 
 cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, const void* dO,
                                const float* g, const float* beta, float* W, float* Z, float* U,
-                               float* Y, const int* cu, const int* coff, int n_seqs, int NC,
-                               int B, int T, int H, int Hk, cudaStream_t st) {
+                               float* Y, unsigned char* tiles, const int* cu, const int* coff,
+                               int n_seqs, int NC, int B, int T, int H, int Hk, cudaStream_t st) {
+  if ((W == nullptr) != (U == nullptr) || (tiles && n_seqs)) return cudaErrorInvalidValue;
   const int rows = n_seqs ? 1 : B;
   if ((long long)rows * H == 0 || T == 0 || NC == 0) return cudaSuccess;
   CUtensorMap mk, mq, mv, mo;
@@ -460,7 +485,8 @@ cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, cons
   const long long items = (long long)NC * H;
   const int ctas = (int)(items < device_sm_count() ? items : device_sm_count());
   bwd_prep_tc_kernel<<<ctas, kBpThreads, BpLay::SMEM_BYTES, st>>>(
-      mk, mq, mv, mo, g, beta, W, Z, U, Y, cu, coff, n_seqs, rows, T, H, Hk, (T + C - 1) / C);
+      mk, mq, mv, mo, g, beta, W, Z, U, Y, tiles, cu, coff, n_seqs, rows, T, H, Hk,
+      (T + C - 1) / C);
   return cudaGetLastError();
 }
 

@@ -445,12 +445,19 @@ constexpr uint32_t ST_D3 = 128;
 constexpr uint32_t ST_D2 = 192;
 constexpr uint32_t ST_COLS = 256;
 
+// kBwd: the forward pass of the backward (chunk_bwd.cu) instead of the forward
+// itself.  Its tiles are [T (64 rows) | Z (128 rows)], bf16, 24 KB, from the
+// backward's preparation; D2 = [T; Z rows 0-63] X gives V' = T X in rows 0-63;
+// Q is not loaded and no output is formed.  Every chunk's entering state goes
+// to hs [(b N + n) H + h][dk][dv] and V' to vp [((b N + n) H + h) C + i][dv]
+// (fp32), the layouts of the backward's workspace.
+template <bool kBwd>
 __global__ void __launch_bounds__(kScanThreads, 1)
 chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                   const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
                   const float* __restrict__ beta, const unsigned char* __restrict__ ws,
                   const float* h0, __nv_bfloat16* __restrict__ o, float* hT, int T, int H,
-                  int Hk, int dv, int ds) {
+                  int Hk, int dv, int ds, float* __restrict__ hs, float* __restrict__ vp) {
   // (h0 and hT may be the same array: each CTA reads its tile of h0 before it
   // writes the same tile of hT)
   // The state has ds columns: dv of them follow v (and give o); with ds = dv +
@@ -524,10 +531,10 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         if (n >= NS && !mbar_wait(&bars[S_EMPTY + s], (uint32_t)((n / NS) - 1) & 1u)) break;
         unsigned char* kq = sm + L::SM_KQ + s * 32768;
         uint64_t* fb = &bars[S_FULL + s];
-        mbar_arrive_expect_tx(fb, 32768 + (trans ? 0 : 8192));
+        mbar_arrive_expect_tx(fb, (kBwd ? 16384 : 32768) + (trans ? 0 : 8192));
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_4d(kq + kb * 16384, &tmK, 64 * kb, hq, n * C, b, fb);
-          tma_load_4d(kq + kb * 16384 + 8192, &tmQ, 64 * kb, hq, n * C, b, fb);
+          if (!kBwd) tma_load_4d(kq + kb * 16384 + 8192, &tmQ, 64 * kb, hq, n * C, b, fb);
         }
         if (!trans) tma_load_4d(sm + L::SM_V + s * 8192, &tmV, c0, h, n * C, b, fb);
         issued = n + 1;
@@ -563,17 +570,19 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         if (!ok) break;
         tc_fence_after();
         // D3 = Z X, the state increment (K-dim = tokens: 4 steps)
+        constexpr uint32_t kZ = kBwd ? 8192u : 0u, kD2 = kBwd ? 0u : 8192u;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t a = umma_desc(rt + k * 32, 16, 1024, SW128);
+          const uint64_t a = umma_desc(rt + kZ + k * 32, 16, 1024, SW128);
           const uint64_t bd = umma_desc(sbase + L::SM_X + k * 2048, 8192, 1024, SW128);
           mma_bf16(tmem + ST_D3, a, bd, IDESC_KM, k > 0);
         }
         mma_commit(&bars[S_D3]);
-        // D2 = [Z rows 64-127; PT] X: rows 64-127 are P T X
+        // D2 = [Z rows 64-127; PT] X: rows 64-127 are P T X (kBwd: [T; Z rows
+        // 0-63] X, rows 0-63 are V' = T X)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t a = umma_desc(rt + 8192 + k * 32, 16, 1024, SW128);
+          const uint64_t a = umma_desc(rt + kD2 + k * 32, 16, 1024, SW128);
           const uint64_t bd = umma_desc(sbase + L::SM_X + k * 2048, 8192, 1024, SW128);
           mma_bf16(tmem + ST_D2, a, bd, IDESC_KM, k > 0);
         }
@@ -659,6 +668,15 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       const int s = n % NS, v = n % NV, buf = n & 1;
       const ScanVec& vb = vecs[v];
       const uint32_t d1 = tmem + ST_D1 + (uint32_t)buf * 64 + (uint32_t)cb + lane_off;
+      // workspace slot of (chunk n, head) in the backward's layout
+      const size_t slot = ((size_t)b * N + n) * H + h;
+      if constexpr (kBwd) {
+        // the state entering chunk n, row r, this thread's 32 columns
+        float* dst = hs + (slot * DK + r) * dv + c0 + cb;
+#pragma unroll
+        for (int c = 0; c < 32; c += 4)
+          *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+      }
       ok = mbar_wait(&bars[S_VFULL + v], (uint32_t)(n / NV) & 1u);
       if (!ok) break;
       if (wq < 2) {
@@ -711,7 +729,30 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[S_S]);
       }
-      if (wq >= 2) {
+      if constexpr (kBwd) {
+        if (wq < 2) {
+          // ---- V' = T X (rows 0-63 of D2), token row r, into vp ----
+          ok = mbar_wait(&bars[S_D2], (uint32_t)n & 1u);
+          if (!ok) break;
+          tc_fence_after();
+          float x[32];
+          tmem_ld32(tmem + ST_D2 + (uint32_t)cb + lane_off, x);
+          if (n * C + r < T) {
+            float* dst = vp + (slot * C + r) * dv + c0 + cb;
+#pragma unroll
+            for (int c = 0; c < 32; c += 4)
+              *reinterpret_cast<float4*>(dst + c) =
+                  make_float4(x[c], x[c + 1], x[c + 2], x[c + 3]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[S_D2FREE]);
+        } else {
+          // no output: the D1 buffer's Q rows are not read
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[S_D1FREE + buf]);
+        }
+      } else if (wq >= 2) {
         // ---- output: O = e^G (Q S) + P T X, token row r - 64 ----
         ok = mbar_wait(&bars[S_D2], (uint32_t)n & 1u);
         if (!ok) break;
@@ -763,7 +804,7 @@ GDN_DEVICE_ERROR_ACCESSOR(device_error_chunk_scan)
 
 int chunk_scan_binary_version() {
   cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, chunk_scan_kernel) != cudaSuccess) return -1;
+  if (cudaFuncGetAttributes(&fa, chunk_scan_kernel<false>) != cudaSuccess) return -1;
   return fa.binaryVersion;
 }
 
@@ -821,7 +862,7 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
   if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv))
     return cudaErrorInvalidValue;
   static std::atomic<int> scan_slot[kMaxDevices] = {};
-  cudaError_t e = ensure_smem(chunk_scan_kernel, ScanLay::SMEM_BYTES, scan_slot);
+  cudaError_t e = ensure_smem(chunk_scan_kernel<false>, ScanLay::SMEM_BYTES, scan_slot);
   if (e != cudaSuccess) return e;
   const int ds = a.dv + (transition ? DK : 0);
   // Launched with programmatic stream serialization: when the preparation runs
@@ -838,10 +879,27 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, chunk_scan_kernel, mk, mq, mv, a.g, a.beta,
+  e = cudaLaunchKernelEx(&cfg, chunk_scan_kernel<false>, mk, mq, mv, a.g, a.beta,
                          static_cast<const unsigned char*>(a.workspace), a.h0,
-                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv, ds);
+                         static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv, ds,
+                         static_cast<float*>(nullptr), static_cast<float*>(nullptr));
   if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cudaStream_t st) {
+  if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !hs || !vp)
+    return cudaErrorInvalidValue;
+  CUtensorMap mk, mq, mv;
+  if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv))
+    return cudaErrorInvalidValue;
+  static std::atomic<int> slot[kMaxDevices] = {};
+  cudaError_t e = ensure_smem(chunk_scan_kernel<true>, ScanLay::SMEM_BYTES, slot);
+  if (e != cudaSuccess) return e;
+  chunk_scan_kernel<true><<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, ScanLay::SMEM_BYTES, st>>>(
+      mk, mq, mv, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), a.h0, nullptr,
+      nullptr, a.T, a.H, a.Hk, a.dv, a.dv, hs, vp);
   return cudaGetLastError();
 }
 

@@ -29,13 +29,16 @@ KernelOverrides read_overrides() {
   k.decode_pdl = !(pdl && pdl[0] == '0');
   const char* bprep = getenv("GDN_BWD_PREP");
   k.bwd_prep_warp = bprep && strcmp(bprep, "warp") == 0;
+  const char* bfwd = getenv("GDN_BWD_FWDPASS");
+  k.bwd_fwdpass_warp = bfwd && strcmp(bfwd, "warp") == 0;
   return k;
 }
 
 // The current choices, packed into one word so that a reload is atomic.
 int pack(const KernelOverrides& k) {
   return (k.chunk_simt ? 1 : 0) | (k.chunk_fused ? 2 : 0) | ((k.tc_pair + 1) << 2) |
-         (k.recurrent_token ? 16 : 0) | (k.decode_pdl ? 32 : 0) | (k.bwd_prep_warp ? 64 : 0);
+         (k.recurrent_token ? 16 : 0) | (k.decode_pdl ? 32 : 0) | (k.bwd_prep_warp ? 64 : 0) |
+         (k.bwd_fwdpass_warp ? 128 : 0);
 }
 
 std::atomic<int>& override_word() {
@@ -54,6 +57,7 @@ KernelOverrides kernel_overrides() {
   k.recurrent_token = (w & 16) != 0;
   k.decode_pdl = (w & 32) != 0;
   k.bwd_prep_warp = (w & 64) != 0;
+  k.bwd_fwdpass_warp = (w & 128) != 0;
   return k;
 }
 

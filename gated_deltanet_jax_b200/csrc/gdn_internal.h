@@ -58,6 +58,7 @@ inline int device_sm_count() {
 //   GDN_RECURRENT_KERNEL=token  the token loop for whole sequences
 //   GDN_DECODE_PDL=0         decode steps without programmatic dependent launch
 //   GDN_BWD_PREP=warp        the backward's warp-level per-chunk preparation
+//   GDN_BWD_FWDPASS=warp     the backward's forward pass on its warp-level state kernel
 struct KernelOverrides {
   bool chunk_simt = false;
   bool chunk_fused = false;
@@ -65,6 +66,7 @@ struct KernelOverrides {
   bool recurrent_token = false;
   bool decode_pdl = true;
   bool bwd_prep_warp = false;
+  bool bwd_fwdpass_warp = false;
 };
 KernelOverrides kernel_overrides();
 
@@ -191,21 +193,27 @@ cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st);   // both la
 // from the identity with v = 0, and a.h0 must be NULL).
 cudaError_t launch_chunk_prepare(const ChunkArgs& a, cudaStream_t st);
 cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cudaStream_t st);
+// The forward pass of the backward on the scan kernel (bf16, dk = dv = 128, dense rows):
+// a.workspace holds [T | Z] tiles per (head, chunk) from launch_bwd_prep_tc; every chunk's
+// entering state goes to hs and V' = T X to vp, in the backward's workspace layouts.
+cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cudaStream_t st);
 int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
 int chunk_scan_binary_version();
 
 // The backward's per-chunk preparation on tcgen05 (chunk_bwd_prep.cu): W, Z, U, Y
 // of every (chunk, head) into the backward's fp32 workspace (rows (gc H + h) C of
-// global chunk gc, strides dk and dv).  bf16, dk = dv = 128.  Dense: n_seqs = 0,
-// B rows of T tokens, NC = B ceil(T / 64).  Packed: n_seqs sequences in one row
-// of T tokens (cu, n_seqs + 1 device offsets), coff their chunk offsets on the
-// device, NC an upper bound of the chunks.
+// global chunk gc, strides dk and dv; W and U skipped when NULL).  bf16, dk = dv =
+// 128.  Dense: n_seqs = 0, B rows of T tokens, NC = B ceil(T / 64); with tiles,
+// also the [T | Z^T] bf16 tiles (24 KB, at (b H + h) ceil(T / 64) + n) that the
+// scan's backward mode reads.  Packed: n_seqs sequences in one row of T tokens
+// (cu, n_seqs + 1 device offsets), coff their chunk offsets on the device, NC an
+// upper bound of the chunks, tiles NULL.
 bool bwd_prep_tc_supported(int dtype, int dk, int dv);
 cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, const void* dO,
                                const float* g, const float* beta, float* W, float* Z, float* U,
-                               float* Y, const int* cu, const int* coff, int n_seqs, int NC,
-                               int B, int T, int H, int Hk, cudaStream_t st);
+                               float* Y, unsigned char* tiles, const int* cu, const int* coff,
+                               int n_seqs, int NC, int B, int T, int H, int Hk, cudaStream_t st);
 int device_error_bwd_prep(bool clear);
 
 // The layer's elementwise work (layer_ops.cu).  Short convolution + SiLU

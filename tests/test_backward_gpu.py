@@ -154,18 +154,30 @@ PACKED = [
 
 @pytest.mark.parametrize("lengths,H,Hk,dk,dv,dtype", PACKED)
 def test_packed_backward_equals_each_sequence_alone(cuda, lengths, H, Hk, dk, dv, dtype):
-    """Every packed sequence gets, bit for bit, what the dense backward gives it alone."""
+    """Every packed sequence gets, bit for bit, what the dense backward gives it
+    alone on the same kernels.  Dense rows at bf16 dk = dv = 128 run their
+    forward pass on the tensor-core scan, packed rows on the warp-level state
+    kernel: the dense call is made on the latter too (GDN_BWD_FWDPASS=warp) for
+    the bit comparison, and on its default path within the bf16 bar."""
+    from gated_deltanet_jax_b200 import _lib
     q, k, v, g, b, h0, do, dhT, cu = _packed_problem(lengths, H, Hk, dk, dv, dtype, cuda,
                                                      seed=len(lengths) + dk)
     got = ops._chunk_backward(q, k, v, g, b, h0, do, dhT, cu)
     for s in range(len(lengths)):
         a0, a1 = int(cu[s]), int(cu[s + 1])
         sl = slice(a0, a1)
-        one = ops._chunk_backward(q[:, sl], k[:, sl], v[:, sl], g[:, sl], b[:, sl],
-                                  h0[s:s + 1], do[:, sl], dhT[s:s + 1])
+        args = (q[:, sl], k[:, sl], v[:, sl], g[:, sl], b[:, sl], h0[s:s + 1], do[:, sl],
+                dhT[s:s + 1])
+        with _lib.kernel_env("GDN_BWD_FWDPASS", "warp"):
+            one = ops._chunk_backward(*args)
         for name, a, r in zip(("dq", "dk", "dv", "dg", "dbeta"), got[:5], one[:5]):
             assert torch.equal(a[:, sl], r), f"sequence {s}: {name}"
         assert torch.equal(got[5][s:s + 1], one[5]), f"sequence {s}: dh0"
+        if a1 > a0:
+            dflt = ops._chunk_backward(*args)
+            for name, a, r in zip(("dq", "dk", "dv", "dg", "dbeta", "dh0"), one, dflt):
+                err = orc.rel_err(f64(a), f64(r))
+                assert err <= TOL[dtype], f"sequence {s} {name}: rel error {err:.2e}"
 
 
 @pytest.mark.parametrize("lengths,H,Hk,dk,dv,dtype", PACKED[:2] + PACKED[3:])
@@ -213,7 +225,7 @@ def test_autograd_through_packed_chunk_op(cuda):
 # tcgen05 kernel (bf16 operands, fp32 accumulation); GDN_BWD_PREP=warp keeps
 # the warp-level one (tf32 operands) for cross-checks.  Both against the
 # oracle: partial last chunks, several rows, grouped q/k heads, state in/out.
-@pytest.mark.parametrize("prep", ["tcgen05", "warp"])
+@pytest.mark.parametrize("prep", ["tcgen05", "tcgen05-warp-fwdpass", "warp"])
 @pytest.mark.parametrize("B,T,H,Hk,with_h0,with_dhT", [(1, 64, 1, 1, False, False),
                                                        (2, 100, 3, 3, True, True),
                                                        (1, 300, 4, 2, True, False),
@@ -232,7 +244,8 @@ def test_backward_preparation_forms_against_oracle(cuda, prep, B, T, H, Hk, with
     gen = torch.Generator(device=cuda).manual_seed(T)
     do = torch.randn(B, T, H, dv, device=cuda, generator=gen).bfloat16()
     dhT = torch.randn(B, H, dk, dv, device=cuda, generator=gen) if with_dhT else None
-    with _lib.kernel_env("GDN_BWD_PREP", "warp" if prep == "warp" else None):
+    with _lib.kernel_env("GDN_BWD_PREP", "warp" if prep == "warp" else None), \
+            _lib.kernel_env("GDN_BWD_FWDPASS", "warp" if prep.endswith("fwdpass") else None):
         got = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
     ref = orc.chunk_exact_backward(*host[:5], host[5], f64(do), None if dhT is None else f64(dhT),
                                    64)
