@@ -1219,9 +1219,14 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
     fa.ws_bytes = (L.total - L.tiles) * sizeof(float);
     e = launch_chunk_scan_bwd(fa, p.hs, p.UV, st);
     if (e != cudaSuccess) return e;
-    BwdParams pr = p;
-    pr.rev_only = 1;
-    bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 1), NT, states_bytes, st>>>(pr);
+    if (!ov.bwd_revpass_warp) {
+      e = launch_chunk_scan_rev(fa, a.dO, a.dhT, a.dh0, p.YX, p.dhs, st);
+      if (e != cudaSuccess) return e;
+    } else {
+      BwdParams pr = p;
+      pr.rev_only = 1;
+      bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 1), NT, states_bytes, st>>>(pr);
+    }
   } else {
     bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 2), NT, states_bytes, st>>>(p);
   }

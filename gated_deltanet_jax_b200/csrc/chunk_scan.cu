@@ -670,8 +670,8 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       const uint32_t d1 = tmem + ST_D1 + (uint32_t)buf * 64 + (uint32_t)cb + lane_off;
       // workspace slot of (chunk n, head) in the backward's layout
       const size_t slot = ((size_t)b * N + n) * H + h;
-      if constexpr (kBwd) {
-        // the state entering chunk n, row r, this thread's 32 columns
+      if (kBwd && n == 0) {
+        // the state entering chunk 0 (later ones are stored as they are formed)
         float* dst = hs + (slot * DK + r) * dv + c0 + cb;
 #pragma unroll
         for (int c = 0; c < 32; c += 4)
@@ -728,6 +728,15 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[S_S]);
+        if (kBwd && n + 1 < N) {
+          // the state entering chunk n + 1, stored after the arrival (whose
+          // release would otherwise wait for these global stores)
+          float* dst = hs + ((slot + H) * DK + r) * dv + c0 + cb;
+#pragma unroll
+          for (int c = 0; c < 32; c += 4)
+            *reinterpret_cast<float4*>(dst + c) =
+                make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+        }
       }
       if constexpr (kBwd) {
         if (wq < 2) {
@@ -737,6 +746,10 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
           tc_fence_after();
           float x[32];
           tmem_ld32(tmem + ST_D2 + (uint32_t)cb + lane_off, x);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[S_D2FREE]);
+          // stored after the arrival, which gates the next chunk's products
           if (n * C + r < T) {
             float* dst = vp + (slot * C + r) * dv + c0 + cb;
 #pragma unroll
@@ -744,9 +757,6 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
               *reinterpret_cast<float4*>(dst + c) =
                   make_float4(x[c], x[c + 1], x[c + 2], x[c + 3]);
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[S_D2FREE]);
         } else {
           // no output: the D1 buffer's Q rows are not read
           __syncwarp();
@@ -788,6 +798,369 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 #pragma unroll
       for (int c = 0; c < 32; c += 4)
         *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ST_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// reverse scan: the backward's reverse state pass
+// ---------------------------------------------------------------------------
+
+// The backward's reverse pass (chunk_bwd.cu) walks the chunks from the last
+// to the first with the gradient R of the state leaving the chunk (starting
+// from dhT), per (b, h, 64 state columns), with Z = T^T diag(d) K and
+// Y = T^T P^T dO from the backward's preparation:
+//   D1 = Z R                      (tcgen05: A = Z^T tile as stored, MN-major)
+//   dX = Y + D1                   -> stored over Y (fp32)
+//   X  = -beta e dX               -> bf16 tile
+//   D3 = Q^T (e dO) + K^T X       (tcgen05, K-dim 128: the dO half is issued
+//                                  before X is known)
+//   R <- e^{G_C} R + D3           -> every chunk's leaving gradient to dhs
+// the reverse of the warp-level bwd_states_kernel's second direction, on the
+// same two-round-trip chain as the forward scan.  Loads per chunk: K, Q (TMA),
+// dO (TMA, this CTA's 64 columns) and the 16 KB Z^T half of the [T | Z^T]
+// tile.  The epilogue warps on TMEM lanes 64-127 form e dO for the products.
+constexpr int kRevTile = 16384;   // Z^T [128 keys][64 tokens] bf16, the tile's second part
+
+struct RevLay {
+  static constexpr int SM_KQ = 0;                          // NS x [2 key blocks][K | Q]
+  static constexpr int SM_DO = SM_KQ + NS * 32768;         // NS x dO [64 tokens][128 B]
+  static constexpr int SM_Z = SM_DO + NS * 8192;           // NR x Z^T [128][128 B]
+  static constexpr int SM_S = SM_Z + NR * kRevTile;        // bf16 gradient tile [128][128 B]
+  static constexpr int SM_X = SM_S + 16384;                // bf16 -beta e dX [64][128 B]
+  static constexpr int SM_E = SM_X + 8192;                 // bf16 e dO [64][128 B]
+  static constexpr int SM_VEC = SM_E + 8192;               // NV x ScanVec
+  static constexpr int SM_BAR = SM_VEC + NV * (int)sizeof(ScanVec);
+  static constexpr int SM_TMEM = SM_BAR + 32 * 8;
+  static constexpr int SMEM_BYTES = SM_TMEM + 16 + 1024;
+  static_assert(SM_Z % 1024 == 0 && SM_S % 1024 == 0 && SM_X % 1024 == 0 && SM_E % 1024 == 0,
+                "swizzled tiles");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
+
+enum {
+  R_FULL = 0,                 // [NS] K, Q, dO of a chunk loaded
+  R_EMPTY = R_FULL + NS,      // [NS] its products done, its dO read
+  R_ZFULL = R_EMPTY + NS,     // [NR] Z^T tile loaded
+  R_ZEMPTY = R_ZFULL + NR,    // [NR] Z^T tile read
+  R_VFULL = R_ZEMPTY + NR,    // [NV] gate vectors ready
+  R_VEMPTY = R_VFULL + NV,    // [NV] gate vectors read (8 warps)
+  R_D1 = R_VEMPTY + NV,       // D1 in TMEM
+  R_X,                        // X tile written (4 warps)
+  R_E,                        // e dO tile written (4 warps)
+  R_D3,                       // D3 in TMEM
+  R_S,                        // gradient tile written (8 warps)
+  R_D1FREE,                   // [2] a D1 buffer read (4 warps)
+  R_DONE = R_D1FREE + 2,
+  R_NBAR,
+};
+static_assert(R_NBAR <= 32, "barrier space");
+
+__global__ void __launch_bounds__(kScanThreads, 1)
+chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmQ,
+                      const __grid_constant__ CUtensorMap tmO, const float* __restrict__ g,
+                      const float* __restrict__ beta, const unsigned char* __restrict__ tiles,
+                      const float* __restrict__ dhT, float* __restrict__ dh0,
+                      float* __restrict__ yx, float* __restrict__ dhs, int T, int H, int Hk,
+                      int dv) {
+  using L = RevLay;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::SM_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::SM_TMEM);
+  ScanVec* vecs = reinterpret_cast<ScanVec*>(sm + L::SM_VEC);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - b * H;
+  const int hq = h * Hk / H;
+  const int c0 = blockIdx.x * DVT;
+  const int N = (T + C - 1) / C;
+  // iteration it handles chunk N - 1 - it
+
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&bars[R_FULL + i], 1);
+      mbar_init(&bars[R_EMPTY + i], 1);
+    }
+    for (int i = 0; i < NR; ++i) {
+      mbar_init(&bars[R_ZFULL + i], 1);
+      mbar_init(&bars[R_ZEMPTY + i], 1);
+    }
+    for (int i = 0; i < NV; ++i) {
+      mbar_init(&bars[R_VFULL + i], 1);
+      mbar_init(&bars[R_VEMPTY + i], 8);
+    }
+    mbar_init(&bars[R_D1], 1);
+    mbar_init(&bars[R_X], 4);
+    mbar_init(&bars[R_E], 4);
+    mbar_init(&bars[R_D3], 1);
+    mbar_init(&bars[R_S], 8);
+    mbar_init(&bars[R_D1FREE + 0], 4);
+    mbar_init(&bars[R_D1FREE + 1], 4);
+    mbar_init(&bars[R_DONE], 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, ST_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) {
+    // ---- K, Q and this CTA's dO columns of each chunk (TMA) ----
+    if (elect_one()) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmO);
+      int issued = 0;
+      for (int it = 0; it < N; ++it) {
+        const int n = N - 1 - it, s = it % NS;
+        if (it >= NS && !mbar_wait(&bars[R_EMPTY + s], (uint32_t)((it / NS) - 1) & 1u)) break;
+        unsigned char* kq = sm + L::SM_KQ + s * 32768;
+        uint64_t* fb = &bars[R_FULL + s];
+        mbar_arrive_expect_tx(fb, 32768 + 8192);
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_load_4d(kq + kb * 16384, &tmK, 64 * kb, hq, n * C, b, fb);
+          tma_load_4d(kq + kb * 16384 + 8192, &tmQ, 64 * kb, hq, n * C, b, fb);
+        }
+        tma_load_4d(sm + L::SM_DO + s * 8192, &tmO, c0, h, n * C, b, fb);
+        issued = it + 1;
+      }
+      for (int it = issued > NS ? issued - NS : 0; it < issued; ++it)
+        mbar_wait(&bars[R_FULL + it % NS], (uint32_t)(it / NS) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (elect_one()) {
+      bool ok = true;
+      for (int it = 0; it < N && ok; ++it) {
+        const int s = it % NS, r = it % NR, buf = it & 1;
+        const uint32_t kq = sbase + L::SM_KQ + s * 32768;
+        const uint32_t zt = sbase + L::SM_Z + r * kRevTile;
+        ok = mbar_wait(&bars[R_ZFULL + r], (uint32_t)(it / NR) & 1u) &&
+             mbar_wait(&bars[R_S], (uint32_t)it & 1u) &&
+             (it < 2 || mbar_wait(&bars[R_D1FREE + buf], (uint32_t)((it - 2) >> 1) & 1u));
+        if (!ok) break;
+        tc_fence_after();
+        // D1 = Z R: A = Z (M = tokens) read MN-major from the Z^T tile [key][token]
+        // (its second 64-row M block, LBO ahead, is not used: rows 64-127 of D1
+        // are ignored), B = the gradient tile, K-dim = dk in 8 steps
+#pragma unroll
+        for (int k = 0; k < DK / 16; ++k) {
+          const uint64_t a = umma_desc(zt + k * 2048, kRevTile, 1024, SW128);
+          const uint64_t bd = umma_desc(sbase + L::SM_S + k * 2048, 16384, 1024, SW128);
+          mma_bf16(tmem + ST_D1 + (uint32_t)buf * 64, a, bd, IDESC_MM, k > 0);
+        }
+        mma_commit(&bars[R_D1]);
+        // D3 = Q^T (e dO) first (A = Q^T, MN-major, M = dk in two 64-wide
+        // blocks 16 KB apart), then + K^T X once X is formed
+        ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / NS) & 1u) &&
+             mbar_wait(&bars[R_E], (uint32_t)it & 1u);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t a = umma_desc(kq + 8192 + k * 2048, 16384, 1024, SW128);
+          const uint64_t bd = umma_desc(sbase + L::SM_E + k * 2048, 8192, 1024, SW128);
+          mma_bf16(tmem + ST_D3, a, bd, IDESC_MM, k > 0);
+        }
+        ok = mbar_wait(&bars[R_X], (uint32_t)it & 1u);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t a = umma_desc(kq + k * 2048, 16384, 1024, SW128);
+          const uint64_t bd = umma_desc(sbase + L::SM_X + k * 2048, 8192, 1024, SW128);
+          mma_bf16(tmem + ST_D3, a, bd, IDESC_MM, 1u);
+        }
+        mma_commit(&bars[R_D3]);
+        mma_commit(&bars[R_EMPTY + s]);
+        mma_commit(&bars[R_ZEMPTY + r]);
+      }
+      mma_commit(&bars[R_DONE]);
+      mbar_wait(&bars[R_DONE], 0);
+    }
+  } else if (warp == 2) {
+    // ---- gate warp: beta, e^G and e^{G_C} of each chunk, NV - 1 chunks ahead ----
+    const size_t gb = (size_t)b * T * H + h;
+    for (int it = 0; it < N; ++it) {
+      const int n = N - 1 - it, v = it % NV;
+      const int t = n * C + 2 * lane;
+      const float g0 = t < T ? ldg_f32(g + gb + (size_t)t * H) : 0.f;
+      const float g1 = t + 1 < T ? ldg_f32(g + gb + (size_t)(t + 1) * H) : 0.f;
+      const float b0 = t < T ? ldg_f32(beta + gb + (size_t)t * H) : 0.f;
+      const float b1 = t + 1 < T ? ldg_f32(beta + gb + (size_t)(t + 1) * H) : 0.f;
+      if (it >= NV && !mbar_wait(&bars[R_VEMPTY + v], (uint32_t)((it / NV) - 1) & 1u)) break;
+      ScanVec& vb = vecs[v];
+      const float pair = g0 + g1;
+      float incl = pair;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      vb.beta[2 * lane] = b0;
+      vb.beta[2 * lane + 1] = b1;
+      vb.eG[2 * lane] = gate_exp(incl - pair + g0);
+      vb.eG[2 * lane + 1] = gate_exp(incl);
+      if (lane == 31) vb.eGC = gate_exp(incl);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[R_VFULL + v]);
+    }
+  } else if (warp == 3) {
+    // ---- Z^T tiles (bulk copies of the second 16 KB of each [T | Z^T] tile) ----
+    if (elect_one()) {
+      const unsigned char* src = tiles + (size_t)bh * N * kTileBytes + (kTileBytes - kRevTile);
+      int issued = 0;
+      for (int it = 0; it < N; ++it) {
+        const int n = N - 1 - it, r = it % NR;
+        if (it >= NR && !mbar_wait(&bars[R_ZEMPTY + r], (uint32_t)((it / NR) - 1) & 1u)) break;
+        mbar_arrive_expect_tx(&bars[R_ZFULL + r], kRevTile);
+        bulk_g2s(sm + L::SM_Z + r * kRevTile, src + (size_t)n * kTileBytes, kRevTile,
+                 &bars[R_ZFULL + r]);
+        issued = it + 1;
+      }
+      for (int it = issued > NR ? issued - NR : 0; it < issued; ++it)
+        mbar_wait(&bars[R_ZFULL + it % NR], (uint32_t)(it / NR) & 1u);
+    }
+  } else {
+    // ---- epilogue warps: quarter wq of the TMEM lanes, 32 of the 64 columns ----
+    const int wq = warp & 3;
+    const int cb = 32 * ((warp - 4) >> 2);  // column offset within the tile
+    const int r = wq * 32 + lane;           // TMEM lane: key row, or token row
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    unsigned char* Stile = sm + L::SM_S;
+    float R[32];
+    {
+      const float* src = dhT ? dhT + ((size_t)bh * DK + r) * dv + c0 + cb : nullptr;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4) {
+        const float4 x = src ? *reinterpret_cast<const float4*>(src + c)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        R[c] = x.x; R[c + 1] = x.y; R[c + 2] = x.z; R[c + 3] = x.w;
+      }
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8)
+        *reinterpret_cast<uint4*>(Stile + sw128(r, cb / 8 + c8)) = pack_bf16x8(R + 8 * c8);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[R_S]);
+      // the gradient leaving the last chunk
+      float* dst = dhs + ((((size_t)b * N + N - 1) * H + h) * DK + r) * dv + c0 + cb;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4)
+        *reinterpret_cast<float4*>(dst + c) = make_float4(R[c], R[c + 1], R[c + 2], R[c + 3]);
+    }
+    bool ok = true;
+    for (int it = 0; it < N && ok; ++it) {
+      const int n = N - 1 - it, s = it % NS, v = it % NV, buf = it & 1;
+      const ScanVec& vb = vecs[v];
+      const size_t slot = ((size_t)b * N + n) * H + h;   // workspace slot of (chunk, head)
+      ok = mbar_wait(&bars[R_VFULL + v], (uint32_t)(it / NV) & 1u);
+      if (!ok) break;
+      if (wq < 2) {
+        // ---- dX = Y + Z R, token row r; X = -beta e dX ----
+        const bool in = n * C + r < T;
+        float* yrow = yx + (slot * C + r) * dv + c0 + cb;
+        float y[32];
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          const float4 x = in ? *reinterpret_cast<const float4*>(yrow + c)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+          y[c] = x.x; y[c + 1] = x.y; y[c + 2] = x.z; y[c + 3] = x.w;
+        }
+        const float sc = -vb.beta[r] * vb.eG[r];
+        ok = mbar_wait(&bars[R_D1], (uint32_t)it & 1u);
+        if (!ok) break;
+        tc_fence_after();
+        float zr[32];
+        tmem_ld32(tmem + ST_D1 + (uint32_t)buf * 64 + (uint32_t)cb + lane_off, zr);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[R_D1FREE + buf]);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) y[e] += zr[e];
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = sc * y[8 * c8 + e];
+          *reinterpret_cast<uint4*>(sm + L::SM_X + sw128(r, cb / 8 + c8)) = pack_bf16x8(x);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[R_X]);
+        // dX over Y, after the arrival (which gates the chain)
+        if (in) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 4)
+            *reinterpret_cast<float4*>(yrow + c) = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
+        }
+      } else {
+        // ---- e dO, token row r - 64, the B operand of Q^T (e dO) ----
+        ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / NS) & 1u);
+        if (!ok) break;
+        const int i = r - 64;
+        const float ei = vb.eG[i];
+        const unsigned char* dOt = sm + L::SM_DO + s * 8192;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float x[8];
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(dOt + sw128(i, cb / 8 + c8)), x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] *= ei;
+          *reinterpret_cast<uint4*>(sm + L::SM_E + sw128(i, cb / 8 + c8)) = pack_bf16x8(x);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[R_E]);
+      }
+      // ---- R <- e^{G_C} R + D3, key row r ----
+      ok = mbar_wait(&bars[R_D3], (uint32_t)it & 1u);
+      if (!ok) break;
+      tc_fence_after();
+      {
+        float d3[32];
+        tmem_ld32(tmem + ST_D3 + (uint32_t)cb + lane_off, d3);
+        const float egc = vb.eGC;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) R[e] = fmaf(egc, R[e], d3[e]);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8)
+          *reinterpret_cast<uint4*>(Stile + sw128(r, cb / 8 + c8)) = pack_bf16x8(R + 8 * c8);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[R_S]);
+        if (n > 0) {
+          // the gradient leaving chunk n - 1
+          float* dst = dhs + ((slot - H) * DK + r) * dv + c0 + cb;
+#pragma unroll
+          for (int c = 0; c < 32; c += 4)
+            *reinterpret_cast<float4*>(dst + c) = make_float4(R[c], R[c + 1], R[c + 2], R[c + 3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[R_VEMPTY + v]);
+    }
+    if (ok && dh0) {
+      float* dst = dh0 + ((size_t)bh * DK + r) * dv + c0 + cb;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4)
+        *reinterpret_cast<float4*>(dst + c) = make_float4(R[c], R[c + 1], R[c + 2], R[c + 3]);
     }
   }
   tc_fence_before();
@@ -900,6 +1273,23 @@ cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cuda
   chunk_scan_kernel<true><<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, ScanLay::SMEM_BYTES, st>>>(
       mk, mq, mv, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), a.h0, nullptr,
       nullptr, a.T, a.H, a.Hk, a.dv, a.dv, hs, vp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const float* dhT,
+                                  float* dh0, float* yx, float* dhs, cudaStream_t st) {
+  if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !dO || !yx || !dhs)
+    return cudaErrorInvalidValue;
+  CUtensorMap mk, mq, mo;
+  if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mo, dO, a.B, a.T, a.H, a.dv))
+    return cudaErrorInvalidValue;
+  static std::atomic<int> slot[kMaxDevices] = {};
+  cudaError_t e = ensure_smem(chunk_scan_rev_kernel, RevLay::SMEM_BYTES, slot);
+  if (e != cudaSuccess) return e;
+  chunk_scan_rev_kernel<<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, RevLay::SMEM_BYTES, st>>>(
+      mk, mq, mo, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), dhT, dh0, yx,
+      dhs, a.T, a.H, a.Hk, a.dv);
   return cudaGetLastError();
 }
 

@@ -31,6 +31,8 @@ KernelOverrides read_overrides() {
   k.bwd_prep_warp = bprep && strcmp(bprep, "warp") == 0;
   const char* bfwd = getenv("GDN_BWD_FWDPASS");
   k.bwd_fwdpass_warp = bfwd && strcmp(bfwd, "warp") == 0;
+  const char* brev = getenv("GDN_BWD_REVPASS");
+  k.bwd_revpass_warp = brev && strcmp(brev, "warp") == 0;
   return k;
 }
 
@@ -38,7 +40,7 @@ KernelOverrides read_overrides() {
 int pack(const KernelOverrides& k) {
   return (k.chunk_simt ? 1 : 0) | (k.chunk_fused ? 2 : 0) | ((k.tc_pair + 1) << 2) |
          (k.recurrent_token ? 16 : 0) | (k.decode_pdl ? 32 : 0) | (k.bwd_prep_warp ? 64 : 0) |
-         (k.bwd_fwdpass_warp ? 128 : 0);
+         (k.bwd_fwdpass_warp ? 128 : 0) | (k.bwd_revpass_warp ? 256 : 0);
 }
 
 std::atomic<int>& override_word() {
@@ -58,6 +60,7 @@ KernelOverrides kernel_overrides() {
   k.decode_pdl = (w & 32) != 0;
   k.bwd_prep_warp = (w & 64) != 0;
   k.bwd_fwdpass_warp = (w & 128) != 0;
+  k.bwd_revpass_warp = (w & 256) != 0;
   return k;
 }
 

@@ -59,6 +59,7 @@ inline int device_sm_count() {
 //   GDN_DECODE_PDL=0         decode steps without programmatic dependent launch
 //   GDN_BWD_PREP=warp        the backward's warp-level per-chunk preparation
 //   GDN_BWD_FWDPASS=warp     the backward's forward pass on its warp-level state kernel
+//   GDN_BWD_REVPASS=warp     the backward's reverse pass on its warp-level state kernel
 struct KernelOverrides {
   bool chunk_simt = false;
   bool chunk_fused = false;
@@ -67,6 +68,7 @@ struct KernelOverrides {
   bool decode_pdl = true;
   bool bwd_prep_warp = false;
   bool bwd_fwdpass_warp = false;
+  bool bwd_revpass_warp = false;
 };
 KernelOverrides kernel_overrides();
 
@@ -197,6 +199,11 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
 // a.workspace holds [T | Z] tiles per (head, chunk) from launch_bwd_prep_tc; every chunk's
 // entering state goes to hs and V' = T X to vp, in the backward's workspace layouts.
 cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cudaStream_t st);
+// The backward's reverse pass on the scan kernels (same shapes and tiles): dX = Y + Z dh over
+// Y in yx, every chunk's leaving state gradient to dhs, the initial state's gradient to dh0
+// (NULL: not wanted), from dO and dhT (NULL: zero).
+cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const float* dhT,
+                                  float* dh0, float* yx, float* dhs, cudaStream_t st);
 int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
 int chunk_scan_binary_version();
