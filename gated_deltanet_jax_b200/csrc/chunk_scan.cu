@@ -450,14 +450,18 @@ constexpr uint32_t ST_COLS = 256;
 // backward's preparation; D2 = [T; Z rows 0-63] X gives V' = T X in rows 0-63;
 // Q is not loaded and no output is formed.  Every chunk's entering state goes
 // to hs [(b N + n) H + h][dk][dv] and V' to vp [((b N + n) H + h) C + i][dv]
-// (fp32), the layouts of the backward's workspace.
+// (fp32), the layouts of the backward's workspace, through the TMA maps tmHS
+// and tmVP: each epilogue warp stages its 32 x 32 block in the Q slots (not
+// loaded here) and stores it with one tensor store, instead of 32 separate
+// row segments per store instruction.
 template <bool kBwd>
 __global__ void __launch_bounds__(kScanThreads, 1)
 chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                   const __grid_constant__ CUtensorMap tmV, const float* __restrict__ g,
                   const float* __restrict__ beta, const unsigned char* __restrict__ ws,
                   const float* h0, __nv_bfloat16* __restrict__ o, float* hT, int T, int H,
-                  int Hk, int dv, int ds, float* __restrict__ hs, float* __restrict__ vp) {
+                  int Hk, int dv, int ds, const __grid_constant__ CUtensorMap tmHS,
+                  const __grid_constant__ CUtensorMap tmVP) {
   // (h0 and hT may be the same array: each CTA reads its tile of h0 before it
   // writes the same tile of hT)
   // The state has ds columns: dv of them follow v (and give o); with ds = dv +
@@ -643,6 +647,33 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     const int r = wq * 32 + lane;           // TMEM lane: state row, or token row
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     unsigned char* Stile = sm + L::SM_S;
+    // kBwd staging (4 KB per warp) in the six 8 KB Q slots, which are not loaded:
+    // slot p = stage p / 2, key block p % 2.  Epilogue warp e stages its state
+    // block in slot e / 2; the four warps on lanes 0-63 their V' block in slots 4-5.
+    const int ew = warp - 4;
+    auto qslot = [&](int p, int half) {
+      return sm + L::SM_KQ + (p >> 1) * 32768 + (p & 1) * 16384 + 8192 + half * 4096;
+    };
+    unsigned char* stg_s = qslot(ew >> 1, ew & 1);
+    const int xw = wq + 2 * (cb >> 5);
+    unsigned char* stg_v = qslot(4 + (xw >> 1), xw & 1);
+    // this warp's 32 x 32 fp32 block (lane = row) through its staging to a
+    // tensor store at (x, y); the staging's previous store has read it first
+    auto stage_store = [&](unsigned char* stg, const float (&vals)[32], const CUtensorMap* map,
+                           int x, int y) {
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<float4*>(stg + sw128(lane, c8)) =
+            make_float4(vals[4 * c8], vals[4 * c8 + 1], vals[4 * c8 + 2], vals[4 * c8 + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(map, x, y, stg);
+        bulk_commit();
+      }
+    };
     float S[32];
     {
       const float* src = h0 && !trans ? h0 + ((size_t)bh * DK + r) * ds + c0 + cb : nullptr;
@@ -672,10 +703,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       const size_t slot = ((size_t)b * N + n) * H + h;
       if (kBwd && n == 0) {
         // the state entering chunk 0 (later ones are stored as they are formed)
-        float* dst = hs + (slot * DK + r) * dv + c0 + cb;
-#pragma unroll
-        for (int c = 0; c < 32; c += 4)
-          *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+        stage_store(stg_s, S, &tmHS, c0 + cb, (int)(slot * DK) + wq * 32);
       }
       ok = mbar_wait(&bars[S_VFULL + v], (uint32_t)(n / NV) & 1u);
       if (!ok) break;
@@ -729,13 +757,8 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[S_S]);
         if (kBwd && n + 1 < N) {
-          // the state entering chunk n + 1, stored after the arrival (whose
-          // release would otherwise wait for these global stores)
-          float* dst = hs + ((slot + H) * DK + r) * dv + c0 + cb;
-#pragma unroll
-          for (int c = 0; c < 32; c += 4)
-            *reinterpret_cast<float4*>(dst + c) =
-                make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+          // the state entering chunk n + 1, after the arrival
+          stage_store(stg_s, S, &tmHS, c0 + cb, (int)((slot + H) * DK) + wq * 32);
         }
       }
       if constexpr (kBwd) {
@@ -750,13 +773,8 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars[S_D2FREE]);
           // stored after the arrival, which gates the next chunk's products
-          if (n * C + r < T) {
-            float* dst = vp + (slot * C + r) * dv + c0 + cb;
-#pragma unroll
-            for (int c = 0; c < 32; c += 4)
-              *reinterpret_cast<float4*>(dst + c) =
-                  make_float4(x[c], x[c + 1], x[c + 2], x[c + 3]);
-          }
+          // (rows past T hold V' = 0: their X is zero)
+          stage_store(stg_v, x, &tmVP, c0 + cb, (int)(slot * C) + wq * 32);
         } else {
           // no output: the D1 buffer's Q rows are not read
           __syncwarp();
@@ -799,6 +817,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       for (int c = 0; c < 32; c += 4)
         *reinterpret_cast<float4*>(dst + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
     }
+    if (kBwd && lane == 0) bulk_wait<0>();   // every tensor store done before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -1255,7 +1274,7 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
   e = cudaLaunchKernelEx(&cfg, chunk_scan_kernel<false>, mk, mq, mv, a.g, a.beta,
                          static_cast<const unsigned char*>(a.workspace), a.h0,
                          static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv, ds,
-                         static_cast<float*>(nullptr), static_cast<float*>(nullptr));
+                         mk, mk);   // (the state maps are read in the backward mode only)
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -1264,15 +1283,17 @@ cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cuda
   if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !hs || !vp)
     return cudaErrorInvalidValue;
-  CUtensorMap mk, mq, mv;
-  if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv))
+  CUtensorMap mk, mq, mv, mhs, mvp;
+  const long long slots = (long long)a.B * ((a.T + C - 1) / C) * a.H;
+  if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv) ||
+      !make_f32_map_2d(&mhs, hs, slots * DK, a.dv) || !make_f32_map_2d(&mvp, vp, slots * C, a.dv))
     return cudaErrorInvalidValue;
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(chunk_scan_kernel<true>, ScanLay::SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
   chunk_scan_kernel<true><<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, ScanLay::SMEM_BYTES, st>>>(
       mk, mq, mv, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), a.h0, nullptr,
-      nullptr, a.T, a.H, a.Hk, a.dv, a.dv, hs, vp);
+      nullptr, a.T, a.H, a.Hk, a.dv, a.dv, mhs, mvp);
   return cudaGetLastError();
 }
 

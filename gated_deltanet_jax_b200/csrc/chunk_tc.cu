@@ -862,6 +862,21 @@ bool make_bf16_map_4d(CUtensorMap* m, const void* base, int B, int T, int H, int
   return r == CUDA_SUCCESS;
 }
 
+// [rows, D] fp32 row-major as a 2-D TMA map (D, rows), boxes of 32 x 32 with
+// 128-byte swizzle (a box row is 128 bytes).
+bool make_f32_map_2d(CUtensorMap* m, const void* base, long long rows, int D) {
+  auto fn = encode_fn();
+  if (!fn || rows <= 0 || D % 32 != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 GDN_DEVICE_ERROR_ACCESSOR(device_error_chunk_tc)
 
 // Exact semantics compute the recurrence whatever the chunk length, so this

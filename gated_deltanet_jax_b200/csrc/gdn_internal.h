@@ -169,6 +169,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 // [B, T, H, D] bf16 as a 4-D TMA map (D, H, T, B), boxes of 64 x 1 x 64 x 1
 // with 128-byte swizzle; tokens past T read as zero.
 bool make_bf16_map_4d(CUtensorMap* m, const void* base, int B, int T, int H, int D);
+// [rows, D] fp32 as a 2-D TMA map, boxes of 32 x 32 with 128-byte swizzle (D % 32 == 0).
+bool make_f32_map_2d(CUtensorMap* m, const void* base, long long rows, int D);
 
 // Tensor-core chunk kernel: bf16, dk = 128 or 256, dv % 64 == 0, chunk = 64, exact.
 bool chunk_tc_supported(const ChunkArgs& a);

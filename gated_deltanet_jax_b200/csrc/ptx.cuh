@@ -312,6 +312,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0,
       : "memory");
 }
 
+// TMA tensor store, 2-D tile from this CTA's shared memory (coordinates >= 0,
+// x times the element size a multiple of 16 bytes), tracked by the issuing
+// thread's bulk groups.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, int c0, int c1, const void* src) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap),
+      "r"(c0), "r"(c1), "r"(smem_u32(src))
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
