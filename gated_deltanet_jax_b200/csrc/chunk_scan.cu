@@ -842,31 +842,36 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 //                                  before X is known)
 //   R <- e^{G_C} R + D3           -> every chunk's leaving gradient to dhs
 // the reverse of the warp-level bwd_states_kernel's second direction, on the
-// same two-round-trip chain as the forward scan.  Loads per chunk: K, Q (TMA),
+// same two-round-trip chain as the forward scan.  dX (over Y, rows of yx) and
+// the leaving gradients (rows of dhs) go out by TMA tensor stores (tmYX,
+// tmDHS), each epilogue warp staging its 32 x 32 block.  Loads per chunk: K, Q (TMA),
 // dO (TMA, this CTA's 64 columns) and the 16 KB Z^T half of the [T | Z^T]
 // tile.  The epilogue warps on TMEM lanes 64-127 form e dO for the products.
 constexpr int kRevTile = 16384;   // Z^T [128 keys][64 tokens] bf16, the tile's second part
+constexpr int kRevNS = 2;         // K/Q/dO stages (the rest of shared memory stages the stores)
 
 struct RevLay {
-  static constexpr int SM_KQ = 0;                          // NS x [2 key blocks][K | Q]
-  static constexpr int SM_DO = SM_KQ + NS * 32768;         // NS x dO [64 tokens][128 B]
-  static constexpr int SM_Z = SM_DO + NS * 8192;           // NR x Z^T [128][128 B]
+  static constexpr int SM_KQ = 0;                          // kRevNS x [2 key blocks][K | Q]
+  static constexpr int SM_DO = SM_KQ + kRevNS * 32768;     // kRevNS x dO [64 tokens][128 B]
+  static constexpr int SM_Z = SM_DO + kRevNS * 8192;           // NR x Z^T [128][128 B]
   static constexpr int SM_S = SM_Z + NR * kRevTile;        // bf16 gradient tile [128][128 B]
   static constexpr int SM_X = SM_S + 16384;                // bf16 -beta e dX [64][128 B]
   static constexpr int SM_E = SM_X + 8192;                 // bf16 e dO [64][128 B]
-  static constexpr int SM_VEC = SM_E + 8192;               // NV x ScanVec
+  static constexpr int SM_STG = SM_E + 8192;               // 12 x 4 KB store staging
+  static constexpr int SM_VEC = SM_STG + 12 * 4096;        // NV x ScanVec
   static constexpr int SM_BAR = SM_VEC + NV * (int)sizeof(ScanVec);
   static constexpr int SM_TMEM = SM_BAR + 32 * 8;
   static constexpr int SMEM_BYTES = SM_TMEM + 16 + 1024;
-  static_assert(SM_Z % 1024 == 0 && SM_S % 1024 == 0 && SM_X % 1024 == 0 && SM_E % 1024 == 0,
+  static_assert(SM_Z % 1024 == 0 && SM_S % 1024 == 0 && SM_X % 1024 == 0 && SM_E % 1024 == 0 &&
+                    SM_STG % 1024 == 0,
                 "swizzled tiles");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 
 enum {
-  R_FULL = 0,                 // [NS] K, Q, dO of a chunk loaded
-  R_EMPTY = R_FULL + NS,      // [NS] its products done, its dO read
-  R_ZFULL = R_EMPTY + NS,     // [NR] Z^T tile loaded
+  R_FULL = 0,                 // [kRevNS] K, Q, dO of a chunk loaded
+  R_EMPTY = R_FULL + kRevNS,  // [kRevNS] its products done, its dO read
+  R_ZFULL = R_EMPTY + kRevNS,     // [NR] Z^T tile loaded
   R_ZEMPTY = R_ZFULL + NR,    // [NR] Z^T tile read
   R_VFULL = R_ZEMPTY + NR,    // [NV] gate vectors ready
   R_VEMPTY = R_VFULL + NV,    // [NV] gate vectors read (8 warps)
@@ -887,8 +892,8 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmO, const float* __restrict__ g,
                       const float* __restrict__ beta, const unsigned char* __restrict__ tiles,
                       const float* __restrict__ dhT, float* __restrict__ dh0,
-                      float* __restrict__ yx, float* __restrict__ dhs, int T, int H, int Hk,
-                      int dv) {
+                      const float* __restrict__ yx, const __grid_constant__ CUtensorMap tmYX,
+                      const __grid_constant__ CUtensorMap tmDHS, int T, int H, int Hk, int dv) {
   using L = RevLay;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -906,7 +911,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
   // iteration it handles chunk N - 1 - it
 
   if (tid == 0) {
-    for (int i = 0; i < NS; ++i) {
+    for (int i = 0; i < kRevNS; ++i) {
       mbar_init(&bars[R_FULL + i], 1);
       mbar_init(&bars[R_EMPTY + i], 1);
     }
@@ -946,8 +951,9 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       prefetch_tmap(&tmO);
       int issued = 0;
       for (int it = 0; it < N; ++it) {
-        const int n = N - 1 - it, s = it % NS;
-        if (it >= NS && !mbar_wait(&bars[R_EMPTY + s], (uint32_t)((it / NS) - 1) & 1u)) break;
+        const int n = N - 1 - it, s = it % kRevNS;
+        if (it >= kRevNS && !mbar_wait(&bars[R_EMPTY + s], (uint32_t)((it / kRevNS) - 1) & 1u))
+          break;
         unsigned char* kq = sm + L::SM_KQ + s * 32768;
         uint64_t* fb = &bars[R_FULL + s];
         mbar_arrive_expect_tx(fb, 32768 + 8192);
@@ -958,15 +964,15 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         tma_load_4d(sm + L::SM_DO + s * 8192, &tmO, c0, h, n * C, b, fb);
         issued = it + 1;
       }
-      for (int it = issued > NS ? issued - NS : 0; it < issued; ++it)
-        mbar_wait(&bars[R_FULL + it % NS], (uint32_t)(it / NS) & 1u);
+      for (int it = issued > kRevNS ? issued - kRevNS : 0; it < issued; ++it)
+        mbar_wait(&bars[R_FULL + it % kRevNS], (uint32_t)(it / kRevNS) & 1u);
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----
     if (elect_one()) {
       bool ok = true;
       for (int it = 0; it < N && ok; ++it) {
-        const int s = it % NS, r = it % NR, buf = it & 1;
+        const int s = it % kRevNS, r = it % NR, buf = it & 1;
         const uint32_t kq = sbase + L::SM_KQ + s * 32768;
         const uint32_t zt = sbase + L::SM_Z + r * kRevTile;
         ok = mbar_wait(&bars[R_ZFULL + r], (uint32_t)(it / NR) & 1u) &&
@@ -986,7 +992,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         mma_commit(&bars[R_D1]);
         // D3 = Q^T (e dO) first (A = Q^T, MN-major, M = dk in two 64-wide
         // blocks 16 KB apart), then + K^T X once X is formed
-        ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / NS) & 1u) &&
+        ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / kRevNS) & 1u) &&
              mbar_wait(&bars[R_E], (uint32_t)it & 1u);
         if (!ok) break;
         tc_fence_after();
@@ -1062,6 +1068,26 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
     const int r = wq * 32 + lane;           // TMEM lane: key row, or token row
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     unsigned char* Stile = sm + L::SM_S;
+    // store staging, 4 KB per block: the gradient block of epilogue warp e at
+    // slot e, the dX block of the warps on lanes 0-63 at slots 8-11
+    const int ew = warp - 4, xw = wq + 2 * (cb >> 5);
+    unsigned char* stg_r = sm + L::SM_STG + ew * 4096;
+    unsigned char* stg_x = sm + L::SM_STG + (8 + xw) * 4096;
+    auto stage_store = [&](unsigned char* stg, const float (&vals)[32], const CUtensorMap* map,
+                           int x, int y) {
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<float4*>(stg + sw128(lane, c8)) =
+            make_float4(vals[4 * c8], vals[4 * c8 + 1], vals[4 * c8 + 2], vals[4 * c8 + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(map, x, y, stg);
+        bulk_commit();
+      }
+    };
     float R[32];
     {
       const float* src = dhT ? dhT + ((size_t)bh * DK + r) * dv + c0 + cb : nullptr;
@@ -1078,14 +1104,11 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[R_S]);
       // the gradient leaving the last chunk
-      float* dst = dhs + ((((size_t)b * N + N - 1) * H + h) * DK + r) * dv + c0 + cb;
-#pragma unroll
-      for (int c = 0; c < 32; c += 4)
-        *reinterpret_cast<float4*>(dst + c) = make_float4(R[c], R[c + 1], R[c + 2], R[c + 3]);
+      stage_store(stg_r, R, &tmDHS, c0 + cb, (int)((((size_t)b * N + N - 1) * H + h) * DK) + wq * 32);
     }
     bool ok = true;
     for (int it = 0; it < N && ok; ++it) {
-      const int n = N - 1 - it, s = it % NS, v = it % NV, buf = it & 1;
+      const int n = N - 1 - it, s = it % kRevNS, v = it % NV, buf = it & 1;
       const ScanVec& vb = vecs[v];
       const size_t slot = ((size_t)b * N + n) * H + h;   // workspace slot of (chunk, head)
       ok = mbar_wait(&bars[R_VFULL + v], (uint32_t)(it / NV) & 1u);
@@ -1093,7 +1116,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       if (wq < 2) {
         // ---- dX = Y + Z R, token row r; X = -beta e dX ----
         const bool in = n * C + r < T;
-        float* yrow = yx + (slot * C + r) * dv + c0 + cb;
+        const float* yrow = yx + (slot * C + r) * dv + c0 + cb;
         float y[32];
 #pragma unroll
         for (int c = 0; c < 32; c += 4) {
@@ -1122,15 +1145,12 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[R_X]);
-        // dX over Y, after the arrival (which gates the chain)
-        if (in) {
-#pragma unroll
-          for (int c = 0; c < 32; c += 4)
-            *reinterpret_cast<float4*>(yrow + c) = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
-        }
+        // dX over Y, after the arrival (which gates the chain); rows past T
+        // hold dX = 0 (their Y and their rows of Z are zero)
+        stage_store(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32);
       } else {
         // ---- e dO, token row r - 64, the B operand of Q^T (e dO) ----
-        ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / NS) & 1u);
+        ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / kRevNS) & 1u);
         if (!ok) break;
         const int i = r - 64;
         const float ei = vb.eG[i];
@@ -1164,13 +1184,8 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[R_S]);
-        if (n > 0) {
-          // the gradient leaving chunk n - 1
-          float* dst = dhs + ((slot - H) * DK + r) * dv + c0 + cb;
-#pragma unroll
-          for (int c = 0; c < 32; c += 4)
-            *reinterpret_cast<float4*>(dst + c) = make_float4(R[c], R[c + 1], R[c + 2], R[c + 3]);
-        }
+        if (n > 0)   // the gradient leaving chunk n - 1
+          stage_store(stg_r, R, &tmDHS, c0 + cb, (int)((slot - H) * DK) + wq * 32);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[R_VEMPTY + v]);
@@ -1181,6 +1196,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       for (int c = 0; c < 32; c += 4)
         *reinterpret_cast<float4*>(dst + c) = make_float4(R[c], R[c + 1], R[c + 2], R[c + 3]);
     }
+    if (lane == 0) bulk_wait<0>();   // every tensor store done before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -1302,15 +1318,17 @@ cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const floa
   if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !dO || !yx || !dhs)
     return cudaErrorInvalidValue;
-  CUtensorMap mk, mq, mo;
-  if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mo, dO, a.B, a.T, a.H, a.dv))
+  CUtensorMap mk, mq, mo, myx, mdhs;
+  const long long slots = (long long)a.B * ((a.T + C - 1) / C) * a.H;
+  if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mo, dO, a.B, a.T, a.H, a.dv) ||
+      !make_f32_map_2d(&myx, yx, slots * C, a.dv) || !make_f32_map_2d(&mdhs, dhs, slots * DK, a.dv))
     return cudaErrorInvalidValue;
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(chunk_scan_rev_kernel, RevLay::SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
   chunk_scan_rev_kernel<<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, RevLay::SMEM_BYTES, st>>>(
       mk, mq, mo, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), dhT, dh0, yx,
-      dhs, a.T, a.H, a.Hk, a.dv);
+      myx, mdhs, a.T, a.H, a.Hk, a.dv);
   return cudaGetLastError();
 }
 
