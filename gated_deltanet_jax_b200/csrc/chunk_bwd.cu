@@ -1203,9 +1203,13 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   const bool tc_fwd = tc_prep && !packed && L.tiles != L.total && !ov.bwd_fwdpass_warp;
   unsigned char* tiles = reinterpret_cast<unsigned char*>(ws + L.tiles);
   if (tc_prep) {
-    e = launch_bwd_prep_tc(a.q, a.k, a.v, a.dO, a.g, a.beta, tc_fwd ? nullptr : p.W, p.Z,
-                           tc_fwd ? nullptr : p.UV, p.YX, tc_fwd ? tiles : nullptr, a.cu_seqlens,
-                           coff, packed ? a.B : 0, NC, a.B, a.T, a.H, a.Hk, st);
+    // (on the tcgen05 passes the reverse scan reads Z from the tiles, and no
+    // kernel reads W, U)
+    const bool tc_rev = tc_fwd && !ov.bwd_revpass_warp;
+    e = launch_bwd_prep_tc(a.q, a.k, a.v, a.dO, a.g, a.beta, tc_fwd ? nullptr : p.W,
+                           tc_rev ? nullptr : p.Z, tc_fwd ? nullptr : p.UV, p.YX,
+                           tc_fwd ? tiles : nullptr, a.cu_seqlens, coff, packed ? a.B : 0, NC,
+                           a.B, a.T, a.H, a.Hk, st);
     if (e != cudaSuccess) return e;
   } else {
     bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(kBpThreads, 1)
 bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                    const float* __restrict__ g, const float* __restrict__ beta,
-                   float* __restrict__ Wg, float* __restrict__ Zg, float* __restrict__ Ug,
+                   float* __restrict__ Wg, float* Zg, float* __restrict__ Ug,
                    float* __restrict__ Yg, unsigned char* __restrict__ tiles,
                    const int* __restrict__ cu,
                    const int* __restrict__ coff, int n_seqs, int B, int T, int H, int Hk,
@@ -419,7 +419,7 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           if (32 * ch + e >= it.len) x[e] = 0.f;
-          Zg[(row0 + 32 * ch + e) * BP_DK + p] = x[e];
+          if (Zg) Zg[(row0 + 32 * ch + e) * BP_DK + p] = x[e];
         }
         if (tiles) {
           // the scan's tile of (head, chunk): T (rows 0-63 of [T; P], as
@@ -469,7 +469,9 @@ cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, cons
                                const float* g, const float* beta, float* W, float* Z, float* U,
                                float* Y, unsigned char* tiles, const int* cu, const int* coff,
                                int n_seqs, int NC, int B, int T, int H, int Hk, cudaStream_t st) {
-  if ((W == nullptr) != (U == nullptr) || (tiles && n_seqs)) return cudaErrorInvalidValue;
+  // W, U: both or neither; Z may be skipped only when the tiles carry it
+  if ((W == nullptr) != (U == nullptr) || (tiles && n_seqs) || (!Z && !tiles))
+    return cudaErrorInvalidValue;
   const int rows = n_seqs ? 1 : B;
   if ((long long)rows * H == 0 || T == 0 || NC == 0) return cudaSuccess;
   CUtensorMap mk, mq, mv, mo;
