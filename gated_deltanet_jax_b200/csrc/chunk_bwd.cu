@@ -1234,7 +1234,15 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   } else {
     bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 2), NT, states_bytes, st>>>(p);
   }
-  bwd_grads_kernel<Tin><<<dim3(NC, a.H), NT, grads_bytes, st>>>(p);
+  if (tc_prep && bwd_grads_tc_supported(a.dtype, a.dk, a.dv) && !ov.bwd_grads_warp) {
+    BwdGradsArgs ga{a.q, a.k, a.v, a.dO, a.g, a.beta, p.UV, p.YX, p.hs, p.dhs,
+                    a.dq, a.dk_out, a.dv_out, a.dg, a.dbeta, a.Hk != a.H ? p.dqk : nullptr,
+                    a.cu_seqlens, coff, packed ? a.B : 0, NC, a.B, a.T, a.H, a.Hk};
+    e = launch_bwd_grads_tc(ga, st);
+    if (e != cudaSuccess) return e;
+  } else {
+    bwd_grads_kernel<Tin><<<dim3(NC, a.H), NT, grads_bytes, st>>>(p);
+  }
   if (a.Hk != a.H) {
     const size_t total = (size_t)p.B * a.T * a.Hk * a.dk;
     const size_t want = (total + 255) / 256, cap = (size_t)8 * device_sm_count();

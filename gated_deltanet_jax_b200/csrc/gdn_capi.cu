@@ -33,6 +33,8 @@ KernelOverrides read_overrides() {
   k.bwd_fwdpass_warp = bfwd && strcmp(bfwd, "warp") == 0;
   const char* brev = getenv("GDN_BWD_REVPASS");
   k.bwd_revpass_warp = brev && strcmp(brev, "warp") == 0;
+  const char* bgr = getenv("GDN_BWD_GRADS");
+  k.bwd_grads_warp = bgr && strcmp(bgr, "warp") == 0;
   return k;
 }
 
@@ -40,7 +42,8 @@ KernelOverrides read_overrides() {
 int pack(const KernelOverrides& k) {
   return (k.chunk_simt ? 1 : 0) | (k.chunk_fused ? 2 : 0) | ((k.tc_pair + 1) << 2) |
          (k.recurrent_token ? 16 : 0) | (k.decode_pdl ? 32 : 0) | (k.bwd_prep_warp ? 64 : 0) |
-         (k.bwd_fwdpass_warp ? 128 : 0) | (k.bwd_revpass_warp ? 256 : 0);
+         (k.bwd_fwdpass_warp ? 128 : 0) | (k.bwd_revpass_warp ? 256 : 0) |
+         (k.bwd_grads_warp ? 512 : 0);
 }
 
 std::atomic<int>& override_word() {
@@ -61,6 +64,7 @@ KernelOverrides kernel_overrides() {
   k.bwd_prep_warp = (w & 64) != 0;
   k.bwd_fwdpass_warp = (w & 128) != 0;
   k.bwd_revpass_warp = (w & 256) != 0;
+  k.bwd_grads_warp = (w & 512) != 0;
   return k;
 }
 
@@ -621,7 +625,8 @@ int gdn_device_error(int clear) {
   const int b = gdn::device_error_chunk_tc(clear != 0);
   const int c = gdn::device_error_chunk_scan(clear != 0);
   const int d = gdn::device_error_bwd_prep(clear != 0);
-  return a ? a : (b ? b : (c ? c : d));
+  const int e = gdn::device_error_bwd_grads(clear != 0);
+  return a ? a : (b ? b : (c ? c : (d ? d : e)));
 }
 
 int gdn_abi_version(void) { return (1 << 16) | 9; }

@@ -60,6 +60,7 @@ inline int device_sm_count() {
 //   GDN_BWD_PREP=warp        the backward's warp-level per-chunk preparation
 //   GDN_BWD_FWDPASS=warp     the backward's forward pass on its warp-level state kernel
 //   GDN_BWD_REVPASS=warp     the backward's reverse pass on its warp-level state kernel
+//   GDN_BWD_GRADS=warp       the backward's warp-level per-chunk gradients
 struct KernelOverrides {
   bool chunk_simt = false;
   bool chunk_fused = false;
@@ -69,6 +70,7 @@ struct KernelOverrides {
   bool bwd_prep_warp = false;
   bool bwd_fwdpass_warp = false;
   bool bwd_revpass_warp = false;
+  bool bwd_grads_warp = false;
 };
 KernelOverrides kernel_overrides();
 
@@ -224,6 +226,24 @@ cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, cons
                                float* Y, unsigned char* tiles, const int* cu, const int* coff,
                                int n_seqs, int NC, int B, int T, int H, int Hk, cudaStream_t st);
 int device_error_bwd_prep(bool clear);
+
+// The backward's per-chunk gradients on tcgen05 (chunk_bwd_grads.cu): from q, k, v, dO,
+// g, beta and the workspace's V' (UV), dX (YX), entering states (hs) and leaving state
+// gradients (dhs), the gradients of q, k, v, g, beta (dq, dk straight into the outputs,
+// or per value head into dqk [2][rows T][H][dk] fp32 when dqk is not NULL).  bf16,
+// dk = dv = 128; dense (n_seqs = 0, B rows) or packed (n_seqs sequences in one row,
+// cu / coff on the device); NC the chunks of every row (an upper bound when packed).
+struct BwdGradsArgs {
+  const void* q; const void* k; const void* v; const void* dO;
+  const float* g; const float* beta;
+  const float* UV; const float* YX; const float* hs; const float* dhs;
+  void* dq; void* dk; void* dv; float* dg; float* dbeta; float* dqk;
+  const int* cu; const int* coff;
+  int n_seqs, NC, B, T, H, Hk;
+};
+bool bwd_grads_tc_supported(int dtype, int dk, int dv);
+cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st);
+int device_error_bwd_grads(bool clear);
 
 // The layer's elementwise work (layer_ops.cu).  Short convolution + SiLU
 // (model.py:15-40): x, y [B,T,C], w [K,C] fp32, states [B,K-1,C] in x's dtype;

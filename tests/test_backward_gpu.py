@@ -226,7 +226,7 @@ def test_autograd_through_packed_chunk_op(cuda):
 # the warp-level one (tf32 operands) for cross-checks.  Both against the
 # oracle: partial last chunks, several rows, grouped q/k heads, state in/out.
 @pytest.mark.parametrize("prep", ["tcgen05", "tcgen05-warp-fwdpass", "tcgen05-warp-revpass",
-                                  "warp"])
+                                  "tcgen05-warp-grads", "warp"])
 @pytest.mark.parametrize("B,T,H,Hk,with_h0,with_dhT", [(1, 64, 1, 1, False, False),
                                                        (2, 100, 3, 3, True, True),
                                                        (1, 300, 4, 2, True, False),
@@ -247,7 +247,8 @@ def test_backward_preparation_forms_against_oracle(cuda, prep, B, T, H, Hk, with
     dhT = torch.randn(B, H, dk, dv, device=cuda, generator=gen) if with_dhT else None
     with _lib.kernel_env("GDN_BWD_PREP", "warp" if prep == "warp" else None), \
             _lib.kernel_env("GDN_BWD_FWDPASS", "warp" if prep.endswith("fwdpass") else None), \
-            _lib.kernel_env("GDN_BWD_REVPASS", "warp" if prep.endswith("revpass") else None):
+            _lib.kernel_env("GDN_BWD_REVPASS", "warp" if prep.endswith("revpass") else None), \
+            _lib.kernel_env("GDN_BWD_GRADS", "warp" if prep.endswith("grads") else None):
         got = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
     ref = orc.chunk_exact_backward(*host[:5], host[5], f64(do), None if dhT is None else f64(dhT),
                                    64)
@@ -273,7 +274,7 @@ def test_backward_preparation_forms_agree_at_size(cuda):
     dhT = torch.randn(B, H, dk, dv, device=cuda, generator=gen)
     tc = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
     tc2 = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
-    with _lib.kernel_env("GDN_BWD_PREP", "warp"):
+    with _lib.kernel_env("GDN_BWD_PREP", "warp"), _lib.kernel_env("GDN_BWD_GRADS", "warp"):
         wp = ops._chunk_backward(q, k, v, g, b, h0, do, dhT)
     for n, a, a2, r in zip(["dq", "dk", "dv", "dg", "dbeta", "dh0"], tc, tc2, wp):
         assert torch.equal(a, a2), n
