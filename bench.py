@@ -904,14 +904,17 @@ def backward_leg(d, a, lib):
     ms, _ = _timed(d, step, steps)
     flops = B * T * H * rl.flops_chunk_bwd_per_token_head(dk, dv, C)
     return {"metric": "chunk backward tokens/s", "value": d.world * B * T / (ms / 1e3),
-            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "launches": 3 * steps,
+            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "launches": 4 * steps,
             "config": {"workload": "gradients of q, k, v, g, beta for B=4 T=4096 H=16 "
                                    "dk=dv=128, bf16 in, from a bf16 dO, no initial state",
                        "l2": f"inputs and {ws_bytes / 1e9:.2f} GB of workspace, larger than L2",
-                       "path": "gdn_chunk_bwd: prep, state passes, gradients (3 launches)"},
+                       "path": "gdn_chunk_bwd: per-chunk preparation, forward state pass "
+                               "(scan), reverse state pass (reverse scan), per-chunk gradients "
+                               "(4 launches)"},
             "algorithmic_flops_per_step": flops,
             "achieved_tflops": flops / (ms / 1e3) / 1e12,
-            "compute": "tensor cores, warp-level mma.sync with tf32 operands, fp32 accumulation"}
+            "compute": "tcgen05 tensor cores (bf16 operands staged by TMA, fp32 accumulation "
+                       "in TMEM) in all four kernels"}
 
 
 def long_context_leg(d, a):
