@@ -435,6 +435,23 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[G_CONV]);
 
+      // the next item's rows of dX, V', v, h, dh into L2 (this thread's own
+      // conversion reads), so that its conversion does not wait on DRAM
+      if (j + 1 < cnt) {
+        const Item nx = item(j + 1);
+        const size_t ns = (size_t)nx.gc * H + nx.h;
+        const int m = pi >> 2, c0 = (pi & 3) * 32, r = pi >> 1, cb = pi & 1;
+        prefetch_l2(YX + (ns * C + m) * GR_D + c0);
+        prefetch_l2(UV + (ns * C + m) * GR_D + c0);
+        if (m < nx.len) prefetch_l2(v + (((size_t)nx.b * T + nx.tok + m) * H + nx.h) * GR_D + c0);
+        const float* hr = hs + (ns * GR_D + r) * GR_D + cb * 64;
+        const float* dr = dhs + (ns * GR_D + r) * GR_D + cb * 64;
+        prefetch_l2(hr);
+        prefetch_l2(hr + 32);
+        prefetch_l2(dr);
+        prefetch_l2(dr + 32);
+      }
+
       // ---- first epilogue: dAE (lanes 0-63) and dPE (lanes 64-127), row i,
       //      columns 32 ch ..; their row and column sums against K K^T / Q K^T ----
       ok = mbar_wait(&bars[G_M12], (uint32_t)j & 1u) && ok;

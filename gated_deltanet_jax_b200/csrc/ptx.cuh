@@ -47,6 +47,11 @@ __device__ __forceinline__ uint4 ldg_u4(const void* p) {
   return v;
 }
 
+// Bring the 128-byte line holding `p` into L2 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
