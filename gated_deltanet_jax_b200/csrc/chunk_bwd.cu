@@ -1214,6 +1214,10 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   } else {
     bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);
   }
+  // the tcgen05 scans hand h and dh to the tcgen05 gradients as bf16 tiles
+  const bool tc_grads = tc_prep && bwd_grads_tc_supported(a.dtype, a.dk, a.dv) &&
+                        !ov.bwd_grads_warp;
+  const bool tiles_hd = tc_fwd && !ov.bwd_revpass_warp && tc_grads;
   if (tc_fwd) {
     ChunkArgs fa{};
     fa.q = a.q; fa.k = a.k; fa.v = a.v; fa.g = a.g; fa.beta = a.beta; fa.h0 = a.h0;
@@ -1221,10 +1225,10 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
     fa.chunk = C; fa.dtype = a.dtype; fa.semantics = kExact;
     fa.workspace = tiles;
     fa.ws_bytes = (L.total - L.tiles) * sizeof(float);
-    e = launch_chunk_scan_bwd(fa, p.hs, p.UV, st);
+    e = launch_chunk_scan_bwd(fa, p.hs, p.UV, tiles_hd, st);
     if (e != cudaSuccess) return e;
     if (!ov.bwd_revpass_warp) {
-      e = launch_chunk_scan_rev(fa, a.dO, a.dhT, a.dh0, p.YX, p.dhs, st);
+      e = launch_chunk_scan_rev(fa, a.dO, a.dhT, a.dh0, p.YX, p.dhs, tiles_hd, st);
       if (e != cudaSuccess) return e;
     } else {
       BwdParams pr = p;
@@ -1234,10 +1238,14 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   } else {
     bwd_states_kernel<Tin, DKP><<<dim3(a.dv / VT, a.B * a.H, 2), NT, states_bytes, st>>>(p);
   }
-  if (tc_prep && bwd_grads_tc_supported(a.dtype, a.dk, a.dv) && !ov.bwd_grads_warp) {
+  if (tc_grads) {
     BwdGradsArgs ga{a.q, a.k, a.v, a.dO, a.g, a.beta, p.UV, p.YX, p.hs, p.dhs,
                     a.dq, a.dk_out, a.dv_out, a.dg, a.dbeta, a.Hk != a.H ? p.dqk : nullptr,
                     a.cu_seqlens, coff, packed ? a.B : 0, NC, a.B, a.T, a.H, a.Hk};
+    if (tiles_hd) {
+      ga.hb = reinterpret_cast<const unsigned char*>(p.hs);
+      ga.dhb = reinterpret_cast<const unsigned char*>(p.dhs);
+    }
     e = launch_bwd_grads_tc(ga, st);
     if (e != cudaSuccess) return e;
   } else {

@@ -130,7 +130,11 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
                     __nv_bfloat16* __restrict__ dvo, float* __restrict__ dg,
                     float* __restrict__ dbeta, float* __restrict__ dqk,
                     const int* __restrict__ cu, const int* __restrict__ coff, int n_seqs, int B,
-                    int T, int H, int Hk, int N) {
+                    int T, int H, int Hk, int N, const unsigned char* __restrict__ hb,
+                    const unsigned char* __restrict__ dhb) {
+  // hb / dhb (both or neither): h and dh of every (chunk, head) as the bf16
+  // tiles the scan kernels wrote (64 KB slots, [column tile][128 key rows][128 B],
+  // 128-byte swizzled), loaded by bulk copies instead of converted from hs / dhs.
   using L = GrLay;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -206,7 +210,12 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       prefetch_tmap(&tmO);
       auto load = [&](int j) {
         const Item it = item(j);
-        mbar_arrive_expect_tx(&bars[G_FULL], 49152);
+        mbar_arrive_expect_tx(&bars[G_FULL], hb ? 49152 + 65536 : 49152);
+        if (hb) {
+          const size_t slot = ((size_t)it.gc * H + it.h) * 65536;
+          bulk_g2s(sm + L::SM_H, hb + slot, 32768, &bars[G_FULL]);
+          bulk_g2s(sm + L::SM_DH, dhb + slot, 32768, &bars[G_FULL]);
+        }
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_4d(sm + L::SM_KQ + kb * 16384, &tmK, 64 * kb, it.hq, it.tok, it.b, &bars[G_FULL]);
           tma_load_4d(sm + L::SM_KQ + kb * 16384 + 8192, &tmQ, 64 * kb, it.hq, it.tok, it.b,
@@ -384,7 +393,7 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         xv += __shfl_xor_sync(0xffffffffu, xv, 2);
         if ((pi & 3) == 0) red[RD_XV * 64 + m] = xv;
       }
-      {
+      if (!hb) {
         // h and dh: key row r, 64 columns of block cb, in two halves of 32
         const int r = pi >> 1, cb = pi & 1;
         const float* hr = hs + (slot * GR_D + r) * GR_D + cb * 64;
@@ -417,6 +426,24 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       {
         // beta K (rows scaled), once K has landed: row m, 32 key columns
         ok = mbar_wait(&bars[G_FULL], (uint32_t)j & 1u) && ok;
+        if (hb) {
+          // <h, dh> from the bf16 tiles: key row pi / 2, column tile pi % 2
+          const int r = pi >> 1, cb = pi & 1;
+          float hd = 0.f;
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            float a8[8], d8[8];
+            unpack_bf16x8(
+                *reinterpret_cast<const uint4*>(sm + L::SM_H + cb * 16384 + sw128(r, c8)), a8);
+            unpack_bf16x8(
+                *reinterpret_cast<const uint4*>(sm + L::SM_DH + cb * 16384 + sw128(r, c8)), d8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) hd = fmaf(a8[e], d8[e], hd);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) hd += __shfl_xor_sync(0xffffffffu, hd, o);
+          if (lane == 0) red[RD_HD * 64 + pw] = hd;
+        }
         const int m = pi >> 2, kb = (pi & 3) >> 1, k8 = (pi & 1) * 4;
         const float bm = vb.beta[m];
 #pragma unroll
@@ -444,12 +471,14 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         prefetch_l2(YX + (ns * C + m) * GR_D + c0);
         prefetch_l2(UV + (ns * C + m) * GR_D + c0);
         if (m < nx.len) prefetch_l2(v + (((size_t)nx.b * T + nx.tok + m) * H + nx.h) * GR_D + c0);
-        const float* hr = hs + (ns * GR_D + r) * GR_D + cb * 64;
-        const float* dr = dhs + (ns * GR_D + r) * GR_D + cb * 64;
-        prefetch_l2(hr);
-        prefetch_l2(hr + 32);
-        prefetch_l2(dr);
-        prefetch_l2(dr + 32);
+        if (!hb) {
+          const float* hr = hs + (ns * GR_D + r) * GR_D + cb * 64;
+          const float* dr = dhs + (ns * GR_D + r) * GR_D + cb * 64;
+          prefetch_l2(hr);
+          prefetch_l2(hr + 32);
+          prefetch_l2(dr);
+          prefetch_l2(dr + 32);
+        }
       }
 
       // ---- first epilogue: dAE (lanes 0-63) and dPE (lanes 64-127), row i,
@@ -640,7 +669,7 @@ cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st) {
       mk, mq, mo, static_cast<const __nv_bfloat16*>(a.v), a.g, a.beta, a.UV, a.YX, a.hs, a.dhs,
       static_cast<__nv_bfloat16*>(a.dq), static_cast<__nv_bfloat16*>(a.dk),
       static_cast<__nv_bfloat16*>(a.dv), a.dg, a.dbeta, a.dqk, a.cu, a.coff, a.n_seqs, rows, a.T,
-      a.H, a.Hk, (a.T + C - 1) / C);
+      a.H, a.Hk, (a.T + C - 1) / C, a.hb, a.dhb);
   return cudaGetLastError();
 }
 

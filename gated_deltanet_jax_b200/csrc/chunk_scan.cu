@@ -453,7 +453,11 @@ constexpr uint32_t ST_COLS = 256;
 // (fp32), the layouts of the backward's workspace, through the TMA maps tmHS
 // and tmVP: each epilogue warp stages its 32 x 32 block in the Q slots (not
 // loaded here) and stores it with one tensor store, instead of 32 separate
-// row segments per store instruction.
+// row segments per store instruction.  With hsb, the entering states go out
+// instead as the bf16 state tile the chain already holds in shared memory
+// (16 KB per chunk and CTA, [dk rows][64 columns], 128-byte swizzled) at
+// hsb + ((b N + n) H + h) 64 KB + 16 KB x (column tile): one bulk copy per
+// chunk, the layout the tcgen05 gradients kernel loads.
 template <bool kBwd>
 __global__ void __launch_bounds__(kScanThreads, 1)
 chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
@@ -461,7 +465,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                   const float* __restrict__ beta, const unsigned char* __restrict__ ws,
                   const float* h0, __nv_bfloat16* __restrict__ o, float* hT, int T, int H,
                   int Hk, int dv, int ds, const __grid_constant__ CUtensorMap tmHS,
-                  const __grid_constant__ CUtensorMap tmVP) {
+                  const __grid_constant__ CUtensorMap tmVP, unsigned char* __restrict__ hsb) {
   // (h0 and hT may be the same array: each CTA reads its tile of h0 before it
   // writes the same tile of hT)
   // The state has ds columns: dv of them follow v (and give o); with ds = dv +
@@ -568,10 +572,18 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
           mma_bf16(tmem + ST_D1 + (uint32_t)buf * 64, a, bd, IDESC_KM, k > 0);
         }
         mma_commit(&bars[S_D1]);
+        if (kBwd && hsb) {
+          // the bf16 state entering chunk n, as the tile D1 just read
+          bulk_s2g(hsb + (((size_t)b * N + n) * H + h) * 65536 + blockIdx.x * 16384,
+                   sm + L::SM_S, 16384);
+          bulk_commit();
+        }
         ok = mbar_wait(&bars[S_X], (uint32_t)n & 1u) &&
              mbar_wait(&bars[S_RFULL + r], (uint32_t)(n / NR) & 1u) &&
              (n < 1 || mbar_wait(&bars[S_D2FREE], (uint32_t)(n - 1) & 1u));
         if (!ok) break;
+        // the state tile is rewritten once D3 completes: its copy has read it
+        if (kBwd && hsb) bulk_wait_read<0>();
         tc_fence_after();
         // D3 = Z X, the state increment (K-dim = tokens: 4 steps)
         constexpr uint32_t kZ = kBwd ? 8192u : 0u, kD2 = kBwd ? 0u : 8192u;
@@ -596,6 +608,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       }
       mma_commit(&bars[S_DONE]);
       mbar_wait(&bars[S_DONE], 0);
+      if (kBwd && hsb) bulk_wait<0>();
     }
   } else if (warp == 2) {
     // ---- gate warp: beta, e^G and e^{G_C} of each chunk, NV - 1 chunks ahead ----
@@ -701,7 +714,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
       const uint32_t d1 = tmem + ST_D1 + (uint32_t)buf * 64 + (uint32_t)cb + lane_off;
       // workspace slot of (chunk n, head) in the backward's layout
       const size_t slot = ((size_t)b * N + n) * H + h;
-      if (kBwd && n == 0) {
+      if (kBwd && !hsb && n == 0) {
         // the state entering chunk 0 (later ones are stored as they are formed)
         stage_store(stg_s, S, &tmHS, c0 + cb, (int)(slot * DK) + wq * 32);
       }
@@ -756,7 +769,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[S_S]);
-        if (kBwd && n + 1 < N) {
+        if (kBwd && !hsb && n + 1 < N) {
           // the state entering chunk n + 1, after the arrival
           stage_store(stg_s, S, &tmHS, c0 + cb, (int)((slot + H) * DK) + wq * 32);
         }
@@ -844,7 +857,9 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 // the reverse of the warp-level bwd_states_kernel's second direction, on the
 // same two-round-trip chain as the forward scan.  dX (over Y, rows of yx) and
 // the leaving gradients (rows of dhs) go out by TMA tensor stores (tmYX,
-// tmDHS), each epilogue warp staging its 32 x 32 block.  Loads per chunk: K, Q (TMA),
+// tmDHS), each epilogue warp staging its 32 x 32 block; with dhsb the
+// gradients go out instead as the bf16 tile the chain holds (one bulk copy
+// per chunk, the layout of the forward scan's hsb).  Loads per chunk: K, Q (TMA),
 // dO (TMA, this CTA's 64 columns) and the 16 KB Z^T half of the [T | Z^T]
 // tile.  The epilogue warps on TMEM lanes 64-127 form e dO for the products.
 constexpr int kRevTile = 16384;   // Z^T [128 keys][64 tokens] bf16, the tile's second part
@@ -893,7 +908,8 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
                       const float* __restrict__ beta, const unsigned char* __restrict__ tiles,
                       const float* __restrict__ dhT, float* __restrict__ dh0,
                       const float* __restrict__ yx, const __grid_constant__ CUtensorMap tmYX,
-                      const __grid_constant__ CUtensorMap tmDHS, int T, int H, int Hk, int dv) {
+                      const __grid_constant__ CUtensorMap tmDHS, unsigned char* __restrict__ dhsb,
+                      int T, int H, int Hk, int dv) {
   using L = RevLay;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -990,6 +1006,12 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
           mma_bf16(tmem + ST_D1 + (uint32_t)buf * 64, a, bd, IDESC_MM, k > 0);
         }
         mma_commit(&bars[R_D1]);
+        if (dhsb) {
+          // the bf16 gradient leaving chunk N - 1 - it, as the tile D1 just read
+          bulk_s2g(dhsb + (((size_t)b * N + (N - 1 - it)) * H + h) * 65536 + blockIdx.x * 16384,
+                   sm + L::SM_S, 16384);
+          bulk_commit();
+        }
         // D3 = Q^T (e dO) first (A = Q^T, MN-major, M = dk in two 64-wide
         // blocks 16 KB apart), then + K^T X once X is formed
         ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / kRevNS) & 1u) &&
@@ -1004,6 +1026,8 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         }
         ok = mbar_wait(&bars[R_X], (uint32_t)it & 1u);
         if (!ok) break;
+        // the gradient tile is rewritten once D3 completes: its copy has read it
+        if (dhsb) bulk_wait_read<0>();
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -1017,6 +1041,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       }
       mma_commit(&bars[R_DONE]);
       mbar_wait(&bars[R_DONE], 0);
+      if (dhsb) bulk_wait<0>();
     }
   } else if (warp == 2) {
     // ---- gate warp: beta, e^G and e^{G_C} of each chunk, NV - 1 chunks ahead ----
@@ -1104,7 +1129,9 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[R_S]);
       // the gradient leaving the last chunk
-      stage_store(stg_r, R, &tmDHS, c0 + cb, (int)((((size_t)b * N + N - 1) * H + h) * DK) + wq * 32);
+      if (!dhsb)
+        stage_store(stg_r, R, &tmDHS, c0 + cb,
+                    (int)((((size_t)b * N + N - 1) * H + h) * DK) + wq * 32);
     }
     bool ok = true;
     for (int it = 0; it < N && ok; ++it) {
@@ -1184,7 +1211,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[R_S]);
-        if (n > 0)   // the gradient leaving chunk n - 1
+        if (!dhsb && n > 0)   // the gradient leaving chunk n - 1
           stage_store(stg_r, R, &tmDHS, c0 + cb, (int)((slot - H) * DK) + wq * 32);
       }
       __syncwarp();
@@ -1290,12 +1317,14 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
   e = cudaLaunchKernelEx(&cfg, chunk_scan_kernel<false>, mk, mq, mv, a.g, a.beta,
                          static_cast<const unsigned char*>(a.workspace), a.h0,
                          static_cast<__nv_bfloat16*>(a.o), a.hT, a.T, a.H, a.Hk, a.dv, ds,
-                         mk, mk);   // (the state maps are read in the backward mode only)
+                         mk, mk,   // (the state maps are read in the backward mode only)
+                         static_cast<unsigned char*>(nullptr));
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
-cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cudaStream_t st) {
+cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool hs_tiles,
+                                  cudaStream_t st) {
   if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !hs || !vp)
     return cudaErrorInvalidValue;
@@ -1309,12 +1338,14 @@ cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cuda
   if (e != cudaSuccess) return e;
   chunk_scan_kernel<true><<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, ScanLay::SMEM_BYTES, st>>>(
       mk, mq, mv, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), a.h0, nullptr,
-      nullptr, a.T, a.H, a.Hk, a.dv, a.dv, mhs, mvp);
+      nullptr, a.T, a.H, a.Hk, a.dv, a.dv, mhs, mvp,
+      hs_tiles ? reinterpret_cast<unsigned char*>(hs) : nullptr);
   return cudaGetLastError();
 }
 
 cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const float* dhT,
-                                  float* dh0, float* yx, float* dhs, cudaStream_t st) {
+                                  float* dh0, float* yx, float* dhs, bool dhs_tiles,
+                                  cudaStream_t st) {
   if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
   if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !dO || !yx || !dhs)
     return cudaErrorInvalidValue;
@@ -1328,7 +1359,8 @@ cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const floa
   if (e != cudaSuccess) return e;
   chunk_scan_rev_kernel<<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, RevLay::SMEM_BYTES, st>>>(
       mk, mq, mo, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), dhT, dh0, yx,
-      myx, mdhs, a.T, a.H, a.Hk, a.dv);
+      myx, mdhs, dhs_tiles ? reinterpret_cast<unsigned char*>(dhs) : nullptr, a.T, a.H, a.Hk,
+      a.dv);
   return cudaGetLastError();
 }
 

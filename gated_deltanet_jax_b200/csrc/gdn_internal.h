@@ -202,12 +202,16 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
 // The forward pass of the backward on the scan kernel (bf16, dk = dv = 128, dense rows):
 // a.workspace holds [T | Z] tiles per (head, chunk) from launch_bwd_prep_tc; every chunk's
 // entering state goes to hs and V' = T X to vp, in the backward's workspace layouts.
-cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, cudaStream_t st);
+// With hs_tiles, the entering states go to hs as bf16 [dk][64]-column tiles, 128-byte
+// swizzled (64 KB slot per (chunk, head), 16 KB per column tile), for the tcgen05 gradients.
+cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool hs_tiles,
+                                  cudaStream_t st);
 // The backward's reverse pass on the scan kernels (same shapes and tiles): dX = Y + Z dh over
 // Y in yx, every chunk's leaving state gradient to dhs, the initial state's gradient to dh0
 // (NULL: not wanted), from dO and dhT (NULL: zero).
 cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const float* dhT,
-                                  float* dh0, float* yx, float* dhs, cudaStream_t st);
+                                  float* dh0, float* yx, float* dhs, bool dhs_tiles,
+                                  cudaStream_t st);
 int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
 int chunk_scan_binary_version();
@@ -240,6 +244,9 @@ struct BwdGradsArgs {
   void* dq; void* dk; void* dv; float* dg; float* dbeta; float* dqk;
   const int* cu; const int* coff;
   int n_seqs, NC, B, T, H, Hk;
+  // h and dh as the scans' bf16 tiles (in the hs / dhs regions), or NULL: fp32 hs / dhs
+  const unsigned char* hb = nullptr;
+  const unsigned char* dhb = nullptr;
 };
 bool bwd_grads_tc_supported(int dtype, int dk, int dv);
 cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st);
