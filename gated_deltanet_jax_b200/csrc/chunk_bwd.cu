@@ -1136,6 +1136,7 @@ __global__ void __launch_bounds__(1024) bwd_chunk_offsets_kernel(const int* cu, 
 // Workspace: offsets in floats, each array on a 256-byte boundary.
 struct WsLayout {
   size_t W, Z, UV, YX, hs, dhs, dqk, coff, tiles, total;
+  bool has_tiles;
 };
 
 int padded_dk(int dk) { return dk <= 32 ? 32 : dk <= 64 ? 64 : dk <= 128 ? 128 : 256; }
@@ -1154,9 +1155,11 @@ WsLayout ws_layout(size_t NC, size_t tokens, int H, int dk, int dv, int n_seqs) 
   L.dhs = take(NC * H * dk * dv);
   L.dqk = take(2 * tokens * H * dk);
   L.coff = take(n_seqs ? (size_t)n_seqs + 1 : 0);
-  // dense bf16 dk = dv = 128: the [T | Z] tiles of the forward pass on the scan
-  // kernel (24 KB per chunk and head; reserved whatever the input type)
-  L.tiles = take(!n_seqs && dk == 128 && dv == 128 ? NC * H * (24576 / sizeof(float)) : 0);
+  // dense dk = dv = 128: the preparation's [Z | PT | T] slots for the scan
+  // kernels (32 KB per chunk and head) share W's region, which only the
+  // warp-level forward pass reads (the two never run in one call)
+  L.has_tiles = !n_seqs && dk == 128 && dv == 128;
+  L.tiles = L.W;
   L.total = o;
   return L;
 }
@@ -1196,39 +1199,45 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   if (packed) bwd_chunk_offsets_kernel<<<1, 1024, 0, st>>>(a.cu_seqlens, a.B, a.T, NC, coff);
   const KernelOverrides ov = kernel_overrides();
   // bf16, dk = dv = 128: the per-chunk preparation on tcgen05; on dense rows
-  // also the forward pass (every chunk's entering state and V') on the scan
-  // kernel, so that the state kernel runs the reverse direction alone
+  // the two state passes on the scan kernels, fed by the forward's preparation
+  // (its [Z | PT | T] slots), with no fp32 W, U, Z, Y at all
   const bool tc_prep = sizeof(Tin) == 2 && bwd_prep_tc_supported(a.dtype, a.dk, a.dv) &&
                        !ov.bwd_prep_warp;
-  const bool tc_fwd = tc_prep && !packed && L.tiles != L.total && !ov.bwd_fwdpass_warp;
+  const bool tc_fwd = tc_prep && !packed && L.has_tiles && !ov.bwd_fwdpass_warp;
+  const bool tc_rev = tc_fwd && !ov.bwd_revpass_warp;
   unsigned char* tiles = reinterpret_cast<unsigned char*>(ws + L.tiles);
-  if (tc_prep) {
-    // (on the tcgen05 passes the reverse scan reads Z from the tiles, and no
-    // kernel reads W, U)
-    const bool tc_rev = tc_fwd && !ov.bwd_revpass_warp;
-    e = launch_bwd_prep_tc(a.q, a.k, a.v, a.dO, a.g, a.beta, tc_fwd ? nullptr : p.W,
-                           tc_rev ? nullptr : p.Z, tc_fwd ? nullptr : p.UV, p.YX,
-                           tc_fwd ? tiles : nullptr, a.cu_seqlens, coff, packed ? a.B : 0, NC,
-                           a.B, a.T, a.H, a.Hk, st);
+  ChunkArgs fa{};
+  fa.q = a.q; fa.k = a.k; fa.v = a.v; fa.g = a.g; fa.beta = a.beta; fa.h0 = a.h0;
+  fa.B = a.B; fa.T = a.T; fa.H = a.H; fa.Hk = a.Hk; fa.dk = a.dk; fa.dv = a.dv;
+  fa.chunk = C; fa.dtype = a.dtype; fa.semantics = kExact;
+  fa.workspace = tiles;
+  fa.ws_bytes = (size_t)NC * a.H * C * DKP * sizeof(float);   // W's region
+  if (tc_fwd) {
+    e = launch_chunk_prepare_bwd(fa, st);
     if (e != cudaSuccess) return e;
-  } else {
+  }
+  if (tc_prep && !tc_rev) {
+    // the warp-level passes' operands: W, U for the forward direction, Z, Y
+    // for the reverse
+    e = launch_bwd_prep_tc(a.q, a.k, a.v, a.dO, a.g, a.beta, tc_fwd ? nullptr : p.W, p.Z,
+                           tc_fwd ? nullptr : p.UV, p.YX, a.cu_seqlens, coff,
+                           packed ? a.B : 0, NC, a.B, a.T, a.H, a.Hk, st);
+    if (e != cudaSuccess) return e;
+  } else if (!tc_prep) {
     bwd_prep_kernel<Tin><<<dim3(NC, a.H), NT, prep_bytes, st>>>(p);
   }
   // the tcgen05 scans hand h and dh to the tcgen05 gradients as bf16 tiles
   const bool tc_grads = tc_prep && bwd_grads_tc_supported(a.dtype, a.dk, a.dv) &&
                         !ov.bwd_grads_warp;
-  const bool tiles_hd = tc_fwd && !ov.bwd_revpass_warp && tc_grads;
+  const bool tiles_hd = tc_rev && tc_grads;
+  // the hand-off's bf16 V' and dX rows share the UV region: V' first, then dX
+  void* dx_bf16 = reinterpret_cast<__nv_bfloat16*>(p.UV) + (size_t)NC * a.H * C * a.dv;
   if (tc_fwd) {
-    ChunkArgs fa{};
-    fa.q = a.q; fa.k = a.k; fa.v = a.v; fa.g = a.g; fa.beta = a.beta; fa.h0 = a.h0;
-    fa.B = a.B; fa.T = a.T; fa.H = a.H; fa.Hk = a.Hk; fa.dk = a.dk; fa.dv = a.dv;
-    fa.chunk = C; fa.dtype = a.dtype; fa.semantics = kExact;
-    fa.workspace = tiles;
-    fa.ws_bytes = (L.total - L.tiles) * sizeof(float);
     e = launch_chunk_scan_bwd(fa, p.hs, p.UV, tiles_hd, st);
     if (e != cudaSuccess) return e;
-    if (!ov.bwd_revpass_warp) {
-      e = launch_chunk_scan_rev(fa, a.dO, a.dhT, a.dh0, p.YX, p.dhs, tiles_hd, st);
+    if (tc_rev) {
+      e = launch_chunk_scan_rev(fa, a.dO, a.dhT, a.dh0, p.YX, p.dhs,
+                                tiles_hd ? dx_bf16 : nullptr, a.dv_out, st);
       if (e != cudaSuccess) return e;
     } else {
       BwdParams pr = p;
@@ -1245,6 +1254,8 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
     if (tiles_hd) {
       ga.hb = reinterpret_cast<const unsigned char*>(p.hs);
       ga.dhb = reinterpret_cast<const unsigned char*>(p.dhs);
+      ga.vpb = p.UV;
+      ga.dxb = dx_bf16;
     }
     e = launch_bwd_grads_tc(ga, st);
     if (e != cudaSuccess) return e;

@@ -19,7 +19,8 @@
 // Persistent, one CTA per SM, one (chunk, head) item at a time.  Warp 0 loads
 // q, k and dO by TMA and issues the products; warp 1 forms the gate vectors one
 // item ahead; eight warps convert dX, V', h, dh to bf16 tiles and run the
-// epilogues.  Products (tcgen05.mma kind::f16, M = 128, fp32 in TMEM), stacked
+// epilogues.  After the tcgen05 scans (dense rows), those four arrive as bf16
+// (the hand-off) and warp 0 loads them with the item's q, k, dO, one item ahead.  Products (tcgen05.mma kind::f16, M = 128, fp32 in TMEM), stacked
 // so that everything dK needs sits on TMEM lanes 0-63 and everything dQ needs
 // on lanes 64-127:
 //   P1 = [dX; dO] V'^T     P2 = [K; Q] K^T          (64 columns each)
@@ -82,6 +83,7 @@ enum {
   RD_QG = 17,     // [2] dG from the dQ side
   RD_HD = 19,     // <h, dh> partials of the eight math warps
   RD_N = 20,
+  RD_XVP = 20,    // [4] (hand-off) rowsum(dX o v) by 32-column block, [64 tokens][4], loaded
 };
 
 enum {
@@ -131,10 +133,15 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
                     float* __restrict__ dbeta, float* __restrict__ dqk,
                     const int* __restrict__ cu, const int* __restrict__ coff, int n_seqs, int B,
                     int T, int H, int Hk, int N, const unsigned char* __restrict__ hb,
-                    const unsigned char* __restrict__ dhb) {
-  // hb / dhb (both or neither): h and dh of every (chunk, head) as the bf16
-  // tiles the scan kernels wrote (64 KB slots, [column tile][128 key rows][128 B],
-  // 128-byte swizzled), loaded by bulk copies instead of converted from hs / dhs.
+                    const unsigned char* __restrict__ dhb,
+                    const __grid_constant__ CUtensorMap tmVP,
+                    const __grid_constant__ CUtensorMap tmDX) {
+  // hb / dhb (the scans' hand-off; dense rows only): h and dh of every (chunk,
+  // head) as the bf16 tiles the scan kernels wrote (64 KB slots, [column
+  // tile][128 key rows][128 B], 128-byte swizzled), loaded by bulk copies with
+  // the rowsum(dX o v) partials (each dhs slot + 32 KB); V' and dX loaded by
+  // TMA (tmVP, tmDX: bf16 rows [slots C][dv], 64 x 64 boxes, 128-byte swizzle).
+  // Nothing is converted and dV is not formed here (the reverse scan wrote it).
   using L = GrLay;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -210,11 +217,16 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       prefetch_tmap(&tmO);
       auto load = [&](int j) {
         const Item it = item(j);
-        mbar_arrive_expect_tx(&bars[G_FULL], hb ? 49152 + 65536 : 49152);
+        mbar_arrive_expect_tx(&bars[G_FULL], hb ? 49152 + 65536 + 32768 + 1024 : 49152);
         if (hb) {
-          const size_t slot = ((size_t)it.gc * H + it.h) * 65536;
-          bulk_g2s(sm + L::SM_H, hb + slot, 32768, &bars[G_FULL]);
-          bulk_g2s(sm + L::SM_DH, dhb + slot, 32768, &bars[G_FULL]);
+          const size_t ws = (size_t)it.gc * H + it.h;
+          bulk_g2s(sm + L::SM_H, hb + ws * 65536, 32768, &bars[G_FULL]);
+          bulk_g2s(sm + L::SM_DH, dhb + ws * 65536, 32768, &bars[G_FULL]);
+          bulk_g2s(sm + L::SM_RED + RD_XVP * 256, dhb + ws * 65536 + 32768, 1024, &bars[G_FULL]);
+          for (int cb = 0; cb < 2; ++cb) {
+            tma_load_2d(sm + L::SM_VP + cb * 8192, &tmVP, 64 * cb, (int)(ws * C), &bars[G_FULL]);
+            tma_load_2d(sm + L::SM_XO + cb * 16384, &tmDX, 64 * cb, (int)(ws * C), &bars[G_FULL]);
+          }
         }
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_4d(sm + L::SM_KQ + kb * 16384, &tmK, 64 * kb, it.hq, it.tok, it.b, &bars[G_FULL]);
@@ -232,7 +244,9 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       for (int j = 0; j < cnt; ++j) {
         bool ok = mbar_wait(&bars[G_FULL], (uint32_t)j & 1u);
         pend = -1;
-        ok = ok && mbar_wait(&bars[G_CONV], (uint32_t)j & 1u);
+        // with the hand-off, P1 .. P4 read only loaded tiles; beta K (P6) was
+        // written before the G_AP arrivals that P6 waits for
+        ok = ok && (hb || mbar_wait(&bars[G_CONV], (uint32_t)j & 1u));
         if (!ok) break;
         tc_fence_after();
         // P2 = [K;Q] K^T and P1 = [dX;dO] V'^T (K-dim 128 in 8 steps of 16)
@@ -351,8 +365,9 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       ok = mbar_wait(&bars[G_VFULL + s], (uint32_t)(j >> 1) & 1u) && ok;
 
       // ---- bf16 tiles: dX (over the [dX; dO] blocks), V', h, dh, beta K;
-      //      dV = beta dX; rowsum(dX o V); <h, dh> ----
-      {
+      //      dV = beta dX; rowsum(dX o V); <h, dh> (with the hand-off: beta K,
+      //      <h, dh> and the sum of the rowsum partials) ----
+      if (!hb) {
         const int m = pi >> 2, c0 = (pi & 3) * 32, cb = c0 >> 6, k8 = (c0 & 63) >> 3;
         const bool valid = m < it.len;
         const size_t trow = ((size_t)it.b * T + it.tok + m) * H + it.h;   // token row (valid)
@@ -443,6 +458,10 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) hd += __shfl_xor_sync(0xffffffffu, hd, o);
           if (lane == 0) red[RD_HD * 64 + pw] = hd;
+          if (pi < 64) {
+            const float* xp = red + RD_XVP * 64 + pi * 4;
+            red[RD_XV * 64 + pi] = (xp[0] + xp[1]) + (xp[2] + xp[3]);
+          }
         }
         const int m = pi >> 2, kb = (pi & 3) >> 1, k8 = (pi & 1) * 4;
         const float bm = vb.beta[m];
@@ -463,22 +482,21 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       if (lane == 0) mbar_arrive(&bars[G_CONV]);
 
       // the next item's rows of dX, V', v, h, dh into L2 (this thread's own
-      // conversion reads), so that its conversion does not wait on DRAM
-      if (j + 1 < cnt) {
+      // conversion reads), so that its conversion does not wait on DRAM (with
+      // the hand-off, the next item's tiles are already being loaded)
+      if (j + 1 < cnt && !hb) {
         const Item nx = item(j + 1);
         const size_t ns = (size_t)nx.gc * H + nx.h;
         const int m = pi >> 2, c0 = (pi & 3) * 32, r = pi >> 1, cb = pi & 1;
         prefetch_l2(YX + (ns * C + m) * GR_D + c0);
         prefetch_l2(UV + (ns * C + m) * GR_D + c0);
         if (m < nx.len) prefetch_l2(v + (((size_t)nx.b * T + nx.tok + m) * H + nx.h) * GR_D + c0);
-        if (!hb) {
-          const float* hr = hs + (ns * GR_D + r) * GR_D + cb * 64;
-          const float* dr = dhs + (ns * GR_D + r) * GR_D + cb * 64;
-          prefetch_l2(hr);
-          prefetch_l2(hr + 32);
-          prefetch_l2(dr);
-          prefetch_l2(dr + 32);
-        }
+        const float* hr = hs + (ns * GR_D + r) * GR_D + cb * 64;
+        const float* dr = dhs + (ns * GR_D + r) * GR_D + cb * 64;
+        prefetch_l2(hr);
+        prefetch_l2(hr + 32);
+        prefetch_l2(dr);
+        prefetch_l2(dr + 32);
       }
 
       // ---- first epilogue: dAE (lanes 0-63) and dPE (lanes 64-127), row i,
@@ -655,11 +673,17 @@ bool bwd_grads_tc_supported(int dtype, int dk, int dv) {
 cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st) {
   const int rows = a.n_seqs ? 1 : a.B;
   if ((long long)rows * a.H == 0 || a.T == 0 || a.NC == 0) return cudaSuccess;
-  CUtensorMap mk, mq, mo;
+  const bool hand = a.hb != nullptr;
+  if (hand && (a.n_seqs || !a.dhb || !a.vpb || !a.dxb)) return cudaErrorInvalidValue;
+  CUtensorMap mk, mq, mo, mvp, mdx;
+  const long long slot_rows = (long long)a.NC * a.H * C;
   if (!make_bf16_map_4d(&mk, a.k, rows, a.T, a.Hk, GR_D) ||
       !make_bf16_map_4d(&mq, a.q, rows, a.T, a.Hk, GR_D) ||
-      !make_bf16_map_4d(&mo, a.dO, rows, a.T, a.H, GR_D))
+      !make_bf16_map_4d(&mo, a.dO, rows, a.T, a.H, GR_D) ||
+      (hand && (!make_bf16_map_2d(&mvp, a.vpb, slot_rows, GR_D, true) ||
+                !make_bf16_map_2d(&mdx, a.dxb, slot_rows, GR_D, true))))
     return cudaErrorInvalidValue;
+  if (!hand) mvp = mdx = mo;   // (not read)
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(bwd_grads_tc_kernel, GrLay::SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
@@ -669,7 +693,7 @@ cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st) {
       mk, mq, mo, static_cast<const __nv_bfloat16*>(a.v), a.g, a.beta, a.UV, a.YX, a.hs, a.dhs,
       static_cast<__nv_bfloat16*>(a.dq), static_cast<__nv_bfloat16*>(a.dk),
       static_cast<__nv_bfloat16*>(a.dv), a.dg, a.dbeta, a.dqk, a.cu, a.coff, a.n_seqs, rows, a.T,
-      a.H, a.Hk, (a.T + C - 1) / C, a.hb, a.dhb);
+      a.H, a.Hk, (a.T + C - 1) / C, a.hb, a.dhb, mvp, mdx);
   return cudaGetLastError();
 }
 

@@ -96,8 +96,7 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                    const float* __restrict__ g, const float* __restrict__ beta,
                    float* __restrict__ Wg, float* Zg, float* __restrict__ Ug,
-                   float* __restrict__ Yg, unsigned char* __restrict__ tiles,
-                   const int* __restrict__ cu,
+                   float* __restrict__ Yg, const int* __restrict__ cu,
                    const int* __restrict__ coff, int n_seqs, int B, int T, int H, int Hk,
                    int N) {
   using L = BpLay;
@@ -419,20 +418,7 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           if (32 * ch + e >= it.len) x[e] = 0.f;
-          if (Zg) Zg[(row0 + 32 * ch + e) * BP_DK + p] = x[e];
-        }
-        if (tiles) {
-          // the scan's tile of (head, chunk): T (rows 0-63 of [T; P], as
-          // stored) then Z^T = K^T diag(d) T (row = key dimension p), bf16,
-          // 128-byte swizzled
-          unsigned char* tile =
-              tiles + ((size_t)(it.b * H + it.h) * N + (it.gc - it.b * N)) * 24576;
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8)
-            *reinterpret_cast<uint4*>(tile + 8192 + sw128(p, 4 * ch + c8)) =
-                pack_bf16x8(x + 8 * c8);
-          for (int e = pi; e < 512; e += 256)
-            reinterpret_cast<uint4*>(tile)[e] = reinterpret_cast<const uint4*>(tpt)[e];
+          Zg[(row0 + 32 * ch + e) * BP_DK + p] = x[e];
         }
         if (wu) {
           tmem_ld32(tmem + BT_U + (uint32_t)ch * 32 + lane_off, x);
@@ -467,11 +453,10 @@ bool bwd_prep_tc_supported(int dtype, int dk, int dv) {
 
 cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, const void* dO,
                                const float* g, const float* beta, float* W, float* Z, float* U,
-                               float* Y, unsigned char* tiles, const int* cu, const int* coff,
-                               int n_seqs, int NC, int B, int T, int H, int Hk, cudaStream_t st) {
-  // W, U: both or neither; Z may be skipped only when the tiles carry it
-  if ((W == nullptr) != (U == nullptr) || (tiles && n_seqs) || (!Z && !tiles))
-    return cudaErrorInvalidValue;
+                               float* Y, const int* cu, const int* coff, int n_seqs, int NC,
+                               int B, int T, int H, int Hk, cudaStream_t st) {
+  // W, U: both or neither
+  if ((W == nullptr) != (U == nullptr) || !Z || !Y) return cudaErrorInvalidValue;
   const int rows = n_seqs ? 1 : B;
   if ((long long)rows * H == 0 || T == 0 || NC == 0) return cudaSuccess;
   CUtensorMap mk, mq, mv, mo;
@@ -487,7 +472,7 @@ cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, cons
   const long long items = (long long)NC * H;
   const int ctas = (int)(items < device_sm_count() ? items : device_sm_count());
   bwd_prep_tc_kernel<<<ctas, kBpThreads, BpLay::SMEM_BYTES, st>>>(
-      mk, mq, mv, mo, g, beta, W, Z, U, Y, tiles, cu, coff, n_seqs, rows, T, H, Hk,
+      mk, mq, mv, mo, g, beta, W, Z, U, Y, cu, coff, n_seqs, rows, T, H, Hk,
       (T + C - 1) / C);
   return cudaGetLastError();
 }

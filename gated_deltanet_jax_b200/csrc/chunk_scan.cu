@@ -48,6 +48,8 @@ namespace {
 constexpr int DK = 128;
 constexpr int DVT = 64;
 constexpr int kTileBytes = 24576;  // workspace per chunk-head: Z [128][64] | PT [64][64], bf16
+// The backward's tiles: the same, then T [64][64] (bf16, rows as the solve left them)
+constexpr int kTileBytesBwd = 32768;
 
 // ---------------------------------------------------------------------------
 // preparation kernel
@@ -98,6 +100,9 @@ enum {
 // TMEM columns of a preparation CTA (256 allocated: two CTAs fit one SM)
 constexpr uint32_t PT_PRE = 0, PT_PT = 128, PT_Z = 192, PT_COLS = 256;
 
+// kT: the backward's tiles, [Z | PT | T] in 32 KB slots (T copied out of the
+// [T; P] operand tile by a second bulk copy of the same group).
+template <bool kT>
 __global__ void __launch_bounds__(kPrepThreads, 2)
 chunk_prep_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                   const float* __restrict__ g, const float* __restrict__ beta,
@@ -230,7 +235,12 @@ chunk_prep_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
         ok = mbar_wait(&bars[P_OUT], (uint32_t)j & 1u);
         if (!ok) break;
-        bulk_s2g(ws + ((size_t)bh * N + n) * kTileBytes, sm + L::SM_OUT, kTileBytes);
+        constexpr size_t kStride = kT ? kTileBytesBwd : kTileBytes;
+        unsigned char* dst = ws + ((size_t)bh * N + n) * kStride;
+        bulk_s2g(dst, sm + L::SM_OUT, kTileBytes);
+        // (T, rows 0-63 of [T; P]: the next item's solve rewrites them only
+        // after the arrival below)
+        if (kT) bulk_s2g(dst + kTileBytes, sm + L::SM_TP, 8192);
         bulk_commit();
         bulk_wait_read<0>();
         mbar_arrive(&bars[P_OFREE]);
@@ -445,10 +455,38 @@ constexpr uint32_t ST_D3 = 128;
 constexpr uint32_t ST_D2 = 192;
 constexpr uint32_t ST_COLS = 256;
 
+// One warp's 32 x 32 fp32 block (lane = row) as bf16 through its staging (32
+// rows of 64 bytes, unswizzled) to a tensor store at (x, y) with a 32 x 32 bf16
+// map; the staging's previous store has read it first.  Lane l writes its four
+// 16-byte pieces in an order rotated by l / 2, so that the eight lanes of each
+// store phase hit distinct banks.
+__device__ __forceinline__ void stage_store_bf16(unsigned char* stg, const float (&vals)[32],
+                                                 const CUtensorMap* map, int x, int y, int lane) {
+  if (lane == 0) bulk_wait_read<0>();
+  __syncwarp();
+  uint4 p[4];
+#pragma unroll
+  for (int c8 = 0; c8 < 4; ++c8) p[c8] = pack_bf16x8(vals + 8 * c8);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int j = (c + (lane >> 1)) & 3;
+    const uint4 w = j == 0 ? p[0] : j == 1 ? p[1] : j == 2 ? p[2] : p[3];
+    *reinterpret_cast<uint4*>(stg + lane * 64 + j * 16) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, x, y, stg);
+    bulk_commit();
+  }
+}
+
 // kBwd: the forward pass of the backward (chunk_bwd.cu) instead of the forward
-// itself.  Its tiles are [T (64 rows) | Z (128 rows)], bf16, 24 KB, from the
-// backward's preparation; D2 = [T; Z rows 0-63] X gives V' = T X in rows 0-63;
-// Q is not loaded and no output is formed.  Every chunk's entering state goes
+// itself.  Its tiles are the preparation's 32 KB [Z | PT | T] slots
+// (chunk_prep_kernel<true>), of which Z and T are loaded, T where the forward
+// has PT: D2 = [Z rows 64-127; T] X gives V' = T X in rows 64-127, which the
+// epilogue warps on those TMEM lanes store; Q is not loaded and no output is
+// formed.  Every chunk's entering state goes
 // to hs [(b N + n) H + h][dk][dv] and V' to vp [((b N + n) H + h) C + i][dv]
 // (fp32), the layouts of the backward's workspace, through the TMA maps tmHS
 // and tmVP: each epilogue warp stages its 32 x 32 block in the Q slots (not
@@ -457,7 +495,9 @@ constexpr uint32_t ST_COLS = 256;
 // instead as the bf16 state tile the chain already holds in shared memory
 // (16 KB per chunk and CTA, [dk rows][64 columns], 128-byte swizzled) at
 // hsb + ((b N + n) H + h) 64 KB + 16 KB x (column tile): one bulk copy per
-// chunk, the layout the tcgen05 gradients kernel loads.
+// chunk, the layout the tcgen05 gradients kernel loads; and V' goes to vp as
+// bf16 rows ([((b N + n) H + h) C + i][dv], tmVP a 32 x 32 bf16 map), the
+// operand the gradients take, rounded once.
 template <bool kBwd>
 __global__ void __launch_bounds__(kScanThreads, 1)
 chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
@@ -586,19 +626,18 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         if (kBwd && hsb) bulk_wait_read<0>();
         tc_fence_after();
         // D3 = Z X, the state increment (K-dim = tokens: 4 steps)
-        constexpr uint32_t kZ = kBwd ? 8192u : 0u, kD2 = kBwd ? 0u : 8192u;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t a = umma_desc(rt + kZ + k * 32, 16, 1024, SW128);
+          const uint64_t a = umma_desc(rt + k * 32, 16, 1024, SW128);
           const uint64_t bd = umma_desc(sbase + L::SM_X + k * 2048, 8192, 1024, SW128);
           mma_bf16(tmem + ST_D3, a, bd, IDESC_KM, k > 0);
         }
         mma_commit(&bars[S_D3]);
-        // D2 = [Z rows 64-127; PT] X: rows 64-127 are P T X (kBwd: [T; Z rows
-        // 0-63] X, rows 0-63 are V' = T X)
+        // D2 = [Z rows 64-127; PT] X: rows 64-127 are P T X (kBwd: [Z rows
+        // 64-127; T] X, rows 64-127 are V' = T X)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t a = umma_desc(rt + kD2 + k * 32, 16, 1024, SW128);
+          const uint64_t a = umma_desc(rt + 8192 + k * 32, 16, 1024, SW128);
           const uint64_t bd = umma_desc(sbase + L::SM_X + k * 2048, 8192, 1024, SW128);
           mma_bf16(tmem + ST_D2, a, bd, IDESC_KM, k > 0);
         }
@@ -640,14 +679,23 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
   } else if (warp == 3) {
     // ---- preparation tiles (bulk copies from the workspace) ----
     if (elect_one()) {
-      const unsigned char* src = ws + (size_t)bh * N * kTileBytes;
+      constexpr size_t kStride = kBwd ? kTileBytesBwd : kTileBytes;
+      const unsigned char* src = ws + (size_t)bh * N * kStride;
       int issued = 0;
       for (int n = 0; n < N; ++n) {
         const int r = n % NR;
         if (n >= NR && !mbar_wait(&bars[S_REMPTY + r], (uint32_t)((n / NR) - 1) & 1u)) break;
         mbar_arrive_expect_tx(&bars[S_RFULL + r], kTileBytes);
-        bulk_g2s(sm + L::SM_R + r * kTileBytes, src + (size_t)n * kTileBytes, kTileBytes,
-                 &bars[S_RFULL + r]);
+        if (kBwd) {
+          // Z, then T in place of PT
+          bulk_g2s(sm + L::SM_R + r * kTileBytes, src + (size_t)n * kStride, 16384,
+                   &bars[S_RFULL + r]);
+          bulk_g2s(sm + L::SM_R + r * kTileBytes + 16384, src + (size_t)n * kStride + kTileBytes,
+                   8192, &bars[S_RFULL + r]);
+        } else {
+          bulk_g2s(sm + L::SM_R + r * kTileBytes, src + (size_t)n * kStride, kTileBytes,
+                   &bars[S_RFULL + r]);
+        }
         issued = n + 1;
       }
       for (int n = issued > NR ? issued - NR : 0; n < issued; ++n)
@@ -662,13 +710,13 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     unsigned char* Stile = sm + L::SM_S;
     // kBwd staging (4 KB per warp) in the six 8 KB Q slots, which are not loaded:
     // slot p = stage p / 2, key block p % 2.  Epilogue warp e stages its state
-    // block in slot e / 2; the four warps on lanes 0-63 their V' block in slots 4-5.
+    // block in slot e / 2; the four warps on lanes 64-127 their V' block in slots 4-5.
     const int ew = warp - 4;
     auto qslot = [&](int p, int half) {
       return sm + L::SM_KQ + (p >> 1) * 32768 + (p & 1) * 16384 + 8192 + half * 4096;
     };
     unsigned char* stg_s = qslot(ew >> 1, ew & 1);
-    const int xw = wq + 2 * (cb >> 5);
+    const int xw = (wq & 1) + 2 * (cb >> 5);
     unsigned char* stg_v = qslot(4 + (xw >> 1), xw & 1);
     // this warp's 32 x 32 fp32 block (lane = row) through its staging to a
     // tensor store at (x, y); the staging's previous store has read it first
@@ -775,8 +823,8 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
       }
       if constexpr (kBwd) {
-        if (wq < 2) {
-          // ---- V' = T X (rows 0-63 of D2), token row r, into vp ----
+        if (wq >= 2) {
+          // ---- V' = T X (rows 64-127 of D2), token row r - 64, into vp ----
           ok = mbar_wait(&bars[S_D2], (uint32_t)n & 1u);
           if (!ok) break;
           tc_fence_after();
@@ -784,14 +832,18 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
           tmem_ld32(tmem + ST_D2 + (uint32_t)cb + lane_off, x);
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[S_D2FREE]);
+          // (no output: the D1 buffer's Q rows are not read)
+          if (lane == 0) {
+            mbar_arrive(&bars[S_D2FREE]);
+            mbar_arrive(&bars[S_D1FREE + buf]);
+          }
           // stored after the arrival, which gates the next chunk's products
           // (rows past T hold V' = 0: their X is zero)
-          stage_store(stg_v, x, &tmVP, c0 + cb, (int)(slot * C) + wq * 32);
-        } else {
-          // no output: the D1 buffer's Q rows are not read
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[S_D1FREE + buf]);
+          const int row = (int)(slot * C) + (wq - 2) * 32;
+          if (hsb)
+            stage_store_bf16(stg_v, x, &tmVP, c0 + cb, row, lane);
+          else
+            stage_store(stg_v, x, &tmVP, c0 + cb, row);
         }
       } else if (wq >= 2) {
         // ---- output: O = e^G (Q S) + P T X, token row r - 64 ----
@@ -846,33 +898,42 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 
 // The backward's reverse pass (chunk_bwd.cu) walks the chunks from the last
 // to the first with the gradient R of the state leaving the chunk (starting
-// from dhT), per (b, h, 64 state columns), with Z = T^T diag(d) K and
-// Y = T^T P^T dO from the backward's preparation:
-//   D1 = Z R                      (tcgen05: A = Z^T tile as stored, MN-major)
-//   dX = Y + D1                   -> stored over Y (fp32)
+// from dhT), per (b, h, 64 state columns), with Z = T^T diag(d) K and PT = P T
+// from the preparation's [Z | PT | T] slots (chunk_prep_kernel<true>):
+//   D1 = PT^T dO + Z R            (tcgen05: A = PT^T and Z read MN-major from
+//                                  the tiles as stored; the dO product, which
+//                                  does not depend on R, is issued first)
+//   dX = D1                       -> yx (fp32)
 //   X  = -beta e dX               -> bf16 tile
 //   D3 = Q^T (e dO) + K^T X       (tcgen05, K-dim 128: the dO half is issued
 //                                  before X is known)
 //   R <- e^{G_C} R + D3           -> every chunk's leaving gradient to dhs
 // the reverse of the warp-level bwd_states_kernel's second direction, on the
-// same two-round-trip chain as the forward scan.  dX (over Y, rows of yx) and
+// same two-round-trip chain as the forward scan.  dX (rows of yx) and
 // the leaving gradients (rows of dhs) go out by TMA tensor stores (tmYX,
 // tmDHS), each epilogue warp staging its 32 x 32 block; with dhsb the
 // gradients go out instead as the bf16 tile the chain holds (one bulk copy
 // per chunk, the layout of the forward scan's hsb).  Loads per chunk: K, Q (TMA),
-// dO (TMA, this CTA's 64 columns) and the 16 KB Z^T half of the [T | Z^T]
-// tile.  The epilogue warps on TMEM lanes 64-127 form e dO for the products.
-constexpr int kRevTile = 16384;   // Z^T [128 keys][64 tokens] bf16, the tile's second part
+// dO (TMA, this CTA's 64 columns) and the first 24 KB ([Z | PT]) of the
+// preparation's slot.  The epilogue warps on TMEM lanes 64-127 form e dO for the products.
+// With dhsb (the hand-off to the tcgen05 gradients) the CTA also loads its 64
+// columns of v and, from each token row's fp32 dX, writes dV = beta dX (dvo),
+// the row's partial sum of dX o v over its 32 columns (fp32, at dhsb + 64 KB
+// slot + 32 KB, [64 tokens][4 column blocks]), and dX as bf16 rows through
+// tmYX (a 32 x 32 bf16 map) instead of fp32.
+constexpr int kRevTile = 24576;   // Z [128 keys][64 tokens] | PT [64][64], bf16
+constexpr int kRevNR = 2;         // ring of [Z | PT] tiles
 constexpr int kRevNS = 2;         // K/Q/dO stages (the rest of shared memory stages the stores)
 
 struct RevLay {
   static constexpr int SM_KQ = 0;                          // kRevNS x [2 key blocks][K | Q]
   static constexpr int SM_DO = SM_KQ + kRevNS * 32768;     // kRevNS x dO [64 tokens][128 B]
-  static constexpr int SM_Z = SM_DO + kRevNS * 8192;           // NR x Z^T [128][128 B]
-  static constexpr int SM_S = SM_Z + NR * kRevTile;        // bf16 gradient tile [128][128 B]
+  static constexpr int SM_Z = SM_DO + kRevNS * 8192;       // kRevNR x [Z | PT]
+  static constexpr int SM_S = SM_Z + kRevNR * kRevTile;    // bf16 gradient tile [128][128 B]
   static constexpr int SM_X = SM_S + 16384;                // bf16 -beta e dX [64][128 B]
   static constexpr int SM_E = SM_X + 8192;                 // bf16 e dO [64][128 B]
   static constexpr int SM_STG = SM_E + 8192;               // 12 x 4 KB store staging
+  static constexpr int SM_V = SM_STG;   // with dhsb: kRevNS x v [64 tokens][128 B] (slots 0-3)
   static constexpr int SM_VEC = SM_STG + 12 * 4096;        // NV x ScanVec
   static constexpr int SM_BAR = SM_VEC + NV * (int)sizeof(ScanVec);
   static constexpr int SM_TMEM = SM_BAR + 32 * 8;
@@ -886,9 +947,9 @@ struct RevLay {
 enum {
   R_FULL = 0,                 // [kRevNS] K, Q, dO of a chunk loaded
   R_EMPTY = R_FULL + kRevNS,  // [kRevNS] its products done, its dO read
-  R_ZFULL = R_EMPTY + kRevNS,     // [NR] Z^T tile loaded
-  R_ZEMPTY = R_ZFULL + NR,    // [NR] Z^T tile read
-  R_VFULL = R_ZEMPTY + NR,    // [NV] gate vectors ready
+  R_ZFULL = R_EMPTY + kRevNS,     // [kRevNR] Z | PT tile loaded
+  R_ZEMPTY = R_ZFULL + kRevNR,    // [kRevNR] Z | PT tile read
+  R_VFULL = R_ZEMPTY + kRevNR,    // [NV] gate vectors ready
   R_VEMPTY = R_VFULL + NV,    // [NV] gate vectors read (8 warps)
   R_D1 = R_VEMPTY + NV,       // D1 in TMEM
   R_X,                        // X tile written (4 warps)
@@ -907,8 +968,9 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmO, const float* __restrict__ g,
                       const float* __restrict__ beta, const unsigned char* __restrict__ tiles,
                       const float* __restrict__ dhT, float* __restrict__ dh0,
-                      const float* __restrict__ yx, const __grid_constant__ CUtensorMap tmYX,
+                      const __grid_constant__ CUtensorMap tmYX,
                       const __grid_constant__ CUtensorMap tmDHS, unsigned char* __restrict__ dhsb,
+                      const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ dvo,
                       int T, int H, int Hk, int dv) {
   using L = RevLay;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -931,7 +993,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       mbar_init(&bars[R_FULL + i], 1);
       mbar_init(&bars[R_EMPTY + i], 1);
     }
-    for (int i = 0; i < NR; ++i) {
+    for (int i = 0; i < kRevNR; ++i) {
       mbar_init(&bars[R_ZFULL + i], 1);
       mbar_init(&bars[R_ZEMPTY + i], 1);
     }
@@ -965,6 +1027,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmO);
+      if (dhsb) prefetch_tmap(&tmV);
       int issued = 0;
       for (int it = 0; it < N; ++it) {
         const int n = N - 1 - it, s = it % kRevNS;
@@ -972,12 +1035,13 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
           break;
         unsigned char* kq = sm + L::SM_KQ + s * 32768;
         uint64_t* fb = &bars[R_FULL + s];
-        mbar_arrive_expect_tx(fb, 32768 + 8192);
+        mbar_arrive_expect_tx(fb, dhsb ? 32768 + 16384 : 32768 + 8192);
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_4d(kq + kb * 16384, &tmK, 64 * kb, hq, n * C, b, fb);
           tma_load_4d(kq + kb * 16384 + 8192, &tmQ, 64 * kb, hq, n * C, b, fb);
         }
         tma_load_4d(sm + L::SM_DO + s * 8192, &tmO, c0, h, n * C, b, fb);
+        if (dhsb) tma_load_4d(sm + L::SM_V + s * 8192, &tmV, c0, h, n * C, b, fb);
         issued = it + 1;
       }
       for (int it = issued > kRevNS ? issued - kRevNS : 0; it < issued; ++it)
@@ -988,22 +1052,35 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
     if (elect_one()) {
       bool ok = true;
       for (int it = 0; it < N && ok; ++it) {
-        const int s = it % kRevNS, r = it % NR, buf = it & 1;
+        const int s = it % kRevNS, r = it % kRevNR, buf = it & 1;
         const uint32_t kq = sbase + L::SM_KQ + s * 32768;
         const uint32_t zt = sbase + L::SM_Z + r * kRevTile;
-        ok = mbar_wait(&bars[R_ZFULL + r], (uint32_t)(it / NR) & 1u) &&
-             mbar_wait(&bars[R_S], (uint32_t)it & 1u) &&
+        ok = mbar_wait(&bars[R_ZFULL + r], (uint32_t)(it / kRevNR) & 1u) &&
+             mbar_wait(&bars[R_FULL + s], (uint32_t)(it / kRevNS) & 1u) &&
              (it < 2 || mbar_wait(&bars[R_D1FREE + buf], (uint32_t)((it - 2) >> 1) & 1u));
         if (!ok) break;
         tc_fence_after();
-        // D1 = Z R: A = Z (M = tokens) read MN-major from the Z^T tile [key][token]
-        // (its second 64-row M block, LBO ahead, is not used: rows 64-127 of D1
-        // are ignored), B = the gradient tile, K-dim = dk in 8 steps
+        // D1 = PT^T dO first (Y, independent of R): A = PT^T (M = tokens i) read
+        // MN-major from the PT rows [j][i]; B = dO [j][64 columns], MN-major;
+        // K-dim = the chunk's 64 tokens j.  The second 64-row M block of every
+        // A here (LBO ahead, in shared memory) only feeds rows 64-127 of D1,
+        // which are not read.
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t a = umma_desc(zt + 16384 + k * 2048, 8192, 1024, SW128);
+          const uint64_t bd = umma_desc(sbase + L::SM_DO + s * 8192 + k * 2048, 8192, 1024, SW128);
+          mma_bf16(tmem + ST_D1 + (uint32_t)buf * 64, a, bd, IDESC_MM, k > 0);
+        }
+        ok = mbar_wait(&bars[R_S], (uint32_t)it & 1u);
+        if (!ok) break;
+        tc_fence_after();
+        // D1 += Z R: A = Z (M = tokens) read MN-major from the Z tile [key][token],
+        // B = the gradient tile, K-dim = dk in 8 steps
 #pragma unroll
         for (int k = 0; k < DK / 16; ++k) {
-          const uint64_t a = umma_desc(zt + k * 2048, kRevTile, 1024, SW128);
+          const uint64_t a = umma_desc(zt + k * 2048, 8192, 1024, SW128);
           const uint64_t bd = umma_desc(sbase + L::SM_S + k * 2048, 16384, 1024, SW128);
-          mma_bf16(tmem + ST_D1 + (uint32_t)buf * 64, a, bd, IDESC_MM, k > 0);
+          mma_bf16(tmem + ST_D1 + (uint32_t)buf * 64, a, bd, IDESC_MM, 1u);
         }
         mma_commit(&bars[R_D1]);
         if (dhsb) {
@@ -1014,8 +1091,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         }
         // D3 = Q^T (e dO) first (A = Q^T, MN-major, M = dk in two 64-wide
         // blocks 16 KB apart), then + K^T X once X is formed
-        ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / kRevNS) & 1u) &&
-             mbar_wait(&bars[R_E], (uint32_t)it & 1u);
+        ok = mbar_wait(&bars[R_E], (uint32_t)it & 1u);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
@@ -1071,20 +1147,21 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       if (lane == 0) mbar_arrive(&bars[R_VFULL + v]);
     }
   } else if (warp == 3) {
-    // ---- Z^T tiles (bulk copies of the second 16 KB of each [T | Z^T] tile) ----
+    // ---- [Z | PT] tiles (bulk copies of the first 24 KB of each slot) ----
     if (elect_one()) {
-      const unsigned char* src = tiles + (size_t)bh * N * kTileBytes + (kTileBytes - kRevTile);
+      const unsigned char* src = tiles + (size_t)bh * N * kTileBytesBwd;
       int issued = 0;
       for (int it = 0; it < N; ++it) {
-        const int n = N - 1 - it, r = it % NR;
-        if (it >= NR && !mbar_wait(&bars[R_ZEMPTY + r], (uint32_t)((it / NR) - 1) & 1u)) break;
+        const int n = N - 1 - it, r = it % kRevNR;
+        if (it >= kRevNR && !mbar_wait(&bars[R_ZEMPTY + r], (uint32_t)((it / kRevNR) - 1) & 1u))
+          break;
         mbar_arrive_expect_tx(&bars[R_ZFULL + r], kRevTile);
-        bulk_g2s(sm + L::SM_Z + r * kRevTile, src + (size_t)n * kTileBytes, kRevTile,
+        bulk_g2s(sm + L::SM_Z + r * kRevTile, src + (size_t)n * kTileBytesBwd, kRevTile,
                  &bars[R_ZFULL + r]);
         issued = it + 1;
       }
-      for (int it = issued > NR ? issued - NR : 0; it < issued; ++it)
-        mbar_wait(&bars[R_ZFULL + it % NR], (uint32_t)(it / NR) & 1u);
+      for (int it = issued > kRevNR ? issued - kRevNR : 0; it < issued; ++it)
+        mbar_wait(&bars[R_ZFULL + it % kRevNR], (uint32_t)(it / kRevNR) & 1u);
     }
   } else {
     // ---- epilogue warps: quarter wq of the TMEM lanes, 32 of the 64 columns ----
@@ -1141,27 +1218,26 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
       ok = mbar_wait(&bars[R_VFULL + v], (uint32_t)(it / NV) & 1u);
       if (!ok) break;
       if (wq < 2) {
-        // ---- dX = Y + Z R, token row r; X = -beta e dX ----
+        // ---- dX = D1 = PT^T dO + Z R, token row r; X = -beta e dX ----
         const bool in = n * C + r < T;
-        const float* yrow = yx + (slot * C + r) * dv + c0 + cb;
-        float y[32];
+        uint4 vrow[4];   // (hand-off) this row's 32 columns of v, read ahead of D1
+        if (dhsb) {
+          ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / kRevNS) & 1u);
+          if (!ok) break;
+          const unsigned char* Vt = sm + L::SM_V + s * 8192;
 #pragma unroll
-        for (int c = 0; c < 32; c += 4) {
-          const float4 x = in ? *reinterpret_cast<const float4*>(yrow + c)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-          y[c] = x.x; y[c + 1] = x.y; y[c + 2] = x.z; y[c + 3] = x.w;
+          for (int c8 = 0; c8 < 4; ++c8)
+            vrow[c8] = *reinterpret_cast<const uint4*>(Vt + sw128(r, cb / 8 + c8));
         }
         const float sc = -vb.beta[r] * vb.eG[r];
         ok = mbar_wait(&bars[R_D1], (uint32_t)it & 1u);
         if (!ok) break;
         tc_fence_after();
-        float zr[32];
-        tmem_ld32(tmem + ST_D1 + (uint32_t)buf * 64 + (uint32_t)cb + lane_off, zr);
+        float y[32];
+        tmem_ld32(tmem + ST_D1 + (uint32_t)buf * 64 + (uint32_t)cb + lane_off, y);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[R_D1FREE + buf]);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) y[e] += zr[e];
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
           float x[8];
@@ -1172,9 +1248,29 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[R_X]);
-        // dX over Y, after the arrival (which gates the chain); rows past T
-        // hold dX = 0 (their Y and their rows of Z are zero)
-        stage_store(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32);
+        // dX, after the arrival (which gates the chain); rows past T hold
+        // dX = 0 (their columns of PT and their rows of Z are zero)
+        if (dhsb) {
+          // dV = beta dX, the row's partial rowsum(dX o v), dX as bf16
+          const float bi = vb.beta[r];
+          float xv = 0.f;
+          __nv_bfloat16* dst = dvo + (((size_t)b * T + (size_t)n * C + r) * H + h) * dv + c0 + cb;
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            float vv[8], o8[8];
+            unpack_bf16x8(vrow[c8], vv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              xv = fmaf(y[8 * c8 + e], vv[e], xv);
+              o8[e] = bi * y[8 * c8 + e];
+            }
+            if (in) *reinterpret_cast<uint4*>(dst + 8 * c8) = pack_bf16x8(o8);
+          }
+          reinterpret_cast<float*>(dhsb + slot * 65536 + 32768)[r * 4 + (c0 + cb) / 32] = xv;
+          stage_store_bf16(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32, lane);
+        } else {
+          stage_store(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32);
+        }
       } else {
         // ---- e dO, token row r - 64, the B operand of Q^T (e dO) ----
         ok = mbar_wait(&bars[R_FULL + s], (uint32_t)(it / kRevNS) & 1u);
@@ -1258,6 +1354,12 @@ size_t chunk_scan_workspace_bytes(int B, int T, int H) {
   return (size_t)B * H * N * kTileBytes;
 }
 
+size_t chunk_scan_bwd_tiles_bytes(int B, int T, int H) {
+  if (B <= 0 || T <= 0 || H <= 0) return 0;
+  const size_t N = ((size_t)T + C - 1) / C;
+  return (size_t)B * H * N * kTileBytesBwd;
+}
+
 namespace {
 
 // TMA maps of q and k (dk = 128) over the dense rows.
@@ -1273,21 +1375,35 @@ bool workspace_ok(const ChunkArgs& a) {
 
 }  // namespace
 
-cudaError_t launch_chunk_prepare(const ChunkArgs& a, cudaStream_t st) {
-  if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
-  if (!chunk_scan_supported(a) || !workspace_ok(a)) return cudaErrorInvalidValue;
+template <bool kT>
+cudaError_t launch_prepare_t(const ChunkArgs& a, cudaStream_t st) {
   CUtensorMap mk, mq;
   if (!qk_maps(a, &mk, &mq)) return cudaErrorInvalidValue;
   static std::atomic<int> prep_slot[kMaxDevices] = {};
-  cudaError_t e = ensure_smem(chunk_prep_kernel, PrepLay::SMEM_BYTES, prep_slot);
+  cudaError_t e = ensure_smem(chunk_prep_kernel<kT>, PrepLay::SMEM_BYTES, prep_slot);
   if (e != cudaSuccess) return e;
   const int N = (a.T + C - 1) / C;
   const long long items = (long long)a.B * a.H * N;
   const int prep_ctas = (int)(items < 2LL * device_sm_count() ? items : 2LL * device_sm_count());
-  chunk_prep_kernel<<<prep_ctas, kPrepThreads, PrepLay::SMEM_BYTES, st>>>(
+  chunk_prep_kernel<kT><<<prep_ctas, kPrepThreads, PrepLay::SMEM_BYTES, st>>>(
       mk, mq, a.g, a.beta, static_cast<unsigned char*>(a.workspace), a.T, a.H, a.Hk,
       a.B * a.H, N);
   return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_prepare(const ChunkArgs& a, cudaStream_t st) {
+  if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_scan_supported(a) || !workspace_ok(a)) return cudaErrorInvalidValue;
+  return launch_prepare_t<false>(a, st);
+}
+
+cudaError_t launch_chunk_prepare_bwd(const ChunkArgs& a, cudaStream_t st) {
+  if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
+  if (!chunk_scan_supported(a) || !a.workspace ||
+      a.ws_bytes < chunk_scan_bwd_tiles_bytes(a.B, a.T, a.H) ||
+      (reinterpret_cast<uintptr_t>(a.workspace) & 15u) != 0)
+    return cudaErrorInvalidValue;
+  return launch_prepare_t<true>(a, st);
 }
 
 cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cudaStream_t st) {
@@ -1326,12 +1442,15 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
 cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool hs_tiles,
                                   cudaStream_t st) {
   if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
-  if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !hs || !vp)
+  if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !hs || !vp ||
+      a.ws_bytes < chunk_scan_bwd_tiles_bytes(a.B, a.T, a.H))
     return cudaErrorInvalidValue;
   CUtensorMap mk, mq, mv, mhs, mvp;
   const long long slots = (long long)a.B * ((a.T + C - 1) / C) * a.H;
   if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv) ||
-      !make_f32_map_2d(&mhs, hs, slots * DK, a.dv) || !make_f32_map_2d(&mvp, vp, slots * C, a.dv))
+      !make_f32_map_2d(&mhs, hs, slots * DK, a.dv) ||
+      !(hs_tiles ? make_bf16_map_2d(&mvp, vp, slots * C, a.dv, false)
+                 : make_f32_map_2d(&mvp, vp, slots * C, a.dv)))
     return cudaErrorInvalidValue;
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(chunk_scan_kernel<true>, ScanLay::SMEM_BYTES, slot);
@@ -1344,23 +1463,29 @@ cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool
 }
 
 cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const float* dhT,
-                                  float* dh0, float* yx, float* dhs, bool dhs_tiles,
+                                  float* dh0, float* yx, float* dhs, void* dxb, void* dvo,
                                   cudaStream_t st) {
   if ((long long)a.B * a.H == 0 || a.T == 0) return cudaSuccess;
-  if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !dO || !yx || !dhs)
+  const bool hand = dxb != nullptr;
+  if (!chunk_scan_supported(a) || a.dv != 128 || !a.workspace || !dO || !yx || !dhs ||
+      a.ws_bytes < chunk_scan_bwd_tiles_bytes(a.B, a.T, a.H) || (hand && (!dvo || !a.v)))
     return cudaErrorInvalidValue;
-  CUtensorMap mk, mq, mo, myx, mdhs;
+  CUtensorMap mk, mq, mo, myx, mdhs, mv;
   const long long slots = (long long)a.B * ((a.T + C - 1) / C) * a.H;
   if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mo, dO, a.B, a.T, a.H, a.dv) ||
-      !make_f32_map_2d(&myx, yx, slots * C, a.dv) || !make_f32_map_2d(&mdhs, dhs, slots * DK, a.dv))
+      !make_f32_map_2d(&mdhs, dhs, slots * DK, a.dv) ||
+      !(hand ? make_bf16_map_2d(&myx, dxb, slots * C, a.dv, false) &&
+                   make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv)
+             : make_f32_map_2d(&myx, yx, slots * C, a.dv)))
     return cudaErrorInvalidValue;
+  if (!hand) mv = mo;   // (not read)
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(chunk_scan_rev_kernel, RevLay::SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
   chunk_scan_rev_kernel<<<dim3(a.dv / DVT, a.B * a.H), kScanThreads, RevLay::SMEM_BYTES, st>>>(
-      mk, mq, mo, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), dhT, dh0, yx,
-      myx, mdhs, dhs_tiles ? reinterpret_cast<unsigned char*>(dhs) : nullptr, a.T, a.H, a.Hk,
-      a.dv);
+      mk, mq, mo, a.g, a.beta, static_cast<const unsigned char*>(a.workspace), dhT, dh0, myx,
+      mdhs, hand ? reinterpret_cast<unsigned char*>(dhs) : nullptr, mv,
+      static_cast<__nv_bfloat16*>(dvo), a.T, a.H, a.Hk, a.dv);
   return cudaGetLastError();
 }
 

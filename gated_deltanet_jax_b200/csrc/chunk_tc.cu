@@ -877,6 +877,23 @@ bool make_f32_map_2d(CUtensorMap* m, const void* base, long long rows, int D) {
   return r == CUDA_SUCCESS;
 }
 
+// [rows, D] bf16 row-major as a 2-D TMA map (D, rows) with boxes of bx x by:
+// 64 x 64 with 128-byte swizzle (swizzled = true; tile loads), or 32 x 32
+// unswizzled (64-byte box rows; tile stores from row-major staging).
+bool make_bf16_map_2d(CUtensorMap* m, const void* base, long long rows, int D, bool swizzled) {
+  auto fn = encode_fn();
+  if (!fn || rows <= 0 || D % 64 != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  cuuint32_t box[2] = {swizzled ? 64u : 32u, swizzled ? 64u : 32u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzled ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 GDN_DEVICE_ERROR_ACCESSOR(device_error_chunk_tc)
 
 // Exact semantics compute the recurrence whatever the chunk length, so this

@@ -173,6 +173,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn();
 bool make_bf16_map_4d(CUtensorMap* m, const void* base, int B, int T, int H, int D);
 // [rows, D] fp32 as a 2-D TMA map, boxes of 32 x 32 with 128-byte swizzle (D % 32 == 0).
 bool make_f32_map_2d(CUtensorMap* m, const void* base, long long rows, int D);
+// [rows, D] bf16 as a 2-D TMA map: boxes of 64 x 64 with 128-byte swizzle
+// (swizzled), or 32 x 32 unswizzled (D % 64 == 0).
+bool make_bf16_map_2d(CUtensorMap* m, const void* base, long long rows, int D, bool swizzled);
 
 // Tensor-core chunk kernel: bf16, dk = 128 or 256, dv % 64 == 0, chunk = 64, exact.
 bool chunk_tc_supported(const ChunkArgs& a);
@@ -198,19 +201,28 @@ cudaError_t launch_chunk_scan(const ChunkArgs& a, cudaStream_t st);   // both la
 // transition, the state -- a.hT, [B,H,dk,dv+dk] -- gains dk columns that start
 // from the identity with v = 0, and a.h0 must be NULL).
 cudaError_t launch_chunk_prepare(const ChunkArgs& a, cudaStream_t st);
+// The same preparation for the backward's scans: 32 KB slots [Z | PT | T] (T = (I + A)^{-1}
+// as bf16 rows), a.ws_bytes >= chunk_scan_bwd_tiles_bytes.
+cudaError_t launch_chunk_prepare_bwd(const ChunkArgs& a, cudaStream_t st);
+size_t chunk_scan_bwd_tiles_bytes(int B, int T, int H);
 cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cudaStream_t st);
 // The forward pass of the backward on the scan kernel (bf16, dk = dv = 128, dense rows):
-// a.workspace holds [T | Z] tiles per (head, chunk) from launch_bwd_prep_tc; every chunk's
+// a.workspace holds the [Z | PT | T] slots of launch_chunk_prepare_bwd; every chunk's
 // entering state goes to hs and V' = T X to vp, in the backward's workspace layouts.
-// With hs_tiles, the entering states go to hs as bf16 [dk][64]-column tiles, 128-byte
-// swizzled (64 KB slot per (chunk, head), 16 KB per column tile), for the tcgen05 gradients.
+// With hs_tiles (the hand-off to the tcgen05 gradients), the entering states go to hs as
+// bf16 [dk][64]-column tiles, 128-byte swizzled (64 KB slot per (chunk, head), 16 KB per
+// column tile), and V' to vp as bf16 rows [slots C][dv].
 cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool hs_tiles,
                                   cudaStream_t st);
-// The backward's reverse pass on the scan kernels (same shapes and tiles): dX = Y + Z dh over
-// Y in yx, every chunk's leaving state gradient to dhs, the initial state's gradient to dh0
-// (NULL: not wanted), from dO and dhT (NULL: zero).
+// The backward's reverse pass on the scan kernels (same shapes and slots): dX = PT^T dO + Z dh
+// to yx (fp32), every chunk's leaving state gradient to dhs, the initial state's gradient to
+// dh0 (NULL: not wanted), from dO and dhT (NULL: zero).  With dxb (the hand-off to the tcgen05
+// gradients; dvo and a.v then required): the leaving gradients go to dhs as bf16 tiles
+// (the layout of hs_tiles), dX to dxb as bf16 rows [slots C][dv], dV = beta dX to dvo
+// ([B,T,H,dv] bf16), and each token row's rowsum(dX o v) by 32-column block to the dhs
+// slot + 32 KB ([64][4] fp32).
 cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const float* dhT,
-                                  float* dh0, float* yx, float* dhs, bool dhs_tiles,
+                                  float* dh0, float* yx, float* dhs, void* dxb, void* dvo,
                                   cudaStream_t st);
 int device_error_chunk_scan(bool clear);
 // Compute capability the scan kernel was compiled for (major * 10 + minor), -1 if unknown.
@@ -219,16 +231,14 @@ int chunk_scan_binary_version();
 // The backward's per-chunk preparation on tcgen05 (chunk_bwd_prep.cu): W, Z, U, Y
 // of every (chunk, head) into the backward's fp32 workspace (rows (gc H + h) C of
 // global chunk gc, strides dk and dv; W and U skipped when NULL).  bf16, dk = dv =
-// 128.  Dense: n_seqs = 0, B rows of T tokens, NC = B ceil(T / 64); with tiles,
-// also the [T | Z^T] bf16 tiles (24 KB, at (b H + h) ceil(T / 64) + n) that the
-// scan's backward mode reads.  Packed: n_seqs sequences in one row of T tokens
-// (cu, n_seqs + 1 device offsets), coff their chunk offsets on the device, NC an
-// upper bound of the chunks, tiles NULL.
+// 128.  Dense: n_seqs = 0, B rows of T tokens, NC = B ceil(T / 64).  Packed:
+// n_seqs sequences in one row of T tokens (cu, n_seqs + 1 device offsets), coff
+// their chunk offsets on the device, NC an upper bound of the chunks.
 bool bwd_prep_tc_supported(int dtype, int dk, int dv);
 cudaError_t launch_bwd_prep_tc(const void* q, const void* k, const void* v, const void* dO,
                                const float* g, const float* beta, float* W, float* Z, float* U,
-                               float* Y, unsigned char* tiles, const int* cu, const int* coff,
-                               int n_seqs, int NC, int B, int T, int H, int Hk, cudaStream_t st);
+                               float* Y, const int* cu, const int* coff, int n_seqs, int NC,
+                               int B, int T, int H, int Hk, cudaStream_t st);
 int device_error_bwd_prep(bool clear);
 
 // The backward's per-chunk gradients on tcgen05 (chunk_bwd_grads.cu): from q, k, v, dO,
@@ -244,9 +254,13 @@ struct BwdGradsArgs {
   void* dq; void* dk; void* dv; float* dg; float* dbeta; float* dqk;
   const int* cu; const int* coff;
   int n_seqs, NC, B, T, H, Hk;
-  // h and dh as the scans' bf16 tiles (in the hs / dhs regions), or NULL: fp32 hs / dhs
+  // The scans' bf16 hand-off, or NULL (then UV, YX, hs, dhs are read as fp32 and dV is
+  // formed here): h and dh tiles (hs / dhs regions, with the rowsum(dX o v) partials at
+  // each dhs slot + 32 KB), V' and dX rows; dV was written by the reverse scan.
   const unsigned char* hb = nullptr;
   const unsigned char* dhb = nullptr;
+  const void* vpb = nullptr;
+  const void* dxb = nullptr;
 };
 bool bwd_grads_tc_supported(int dtype, int dk, int dv);
 cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st);

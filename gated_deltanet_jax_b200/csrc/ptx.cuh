@@ -317,6 +317,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0,
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // TMA tensor store, 2-D tile from this CTA's shared memory (coordinates >= 0,
 // x times the element size a multiple of 16 bytes), tracked by the issuing
 // thread's bulk groups.
