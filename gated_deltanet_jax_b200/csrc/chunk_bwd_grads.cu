@@ -52,7 +52,7 @@ struct GrLay {
   static constexpr int SM_H = 81920;       // [cb][h: 128 key rows, 16 KB]
   static constexpr int SM_DH = 114688;     // [cb][dh: 128 key rows, 16 KB]
   static constexpr int SM_AP = 147456;     // [dAE rows 0-63 | dPE rows 64-127], 16 KB
-  static constexpr int SM_BK = 163840;     // [kb][beta K 8 KB]
+  static constexpr int SM_QST = 163840;    // [kb][dQ rows 8 KB]: staging of its tensor stores
   static constexpr int SM_VEC = 180224;    // 2 x GrVec
   static constexpr int SM_RED = SM_VEC + 2 * 1536;   // per-token partial sums
   static constexpr int SM_BAR = SM_RED + 24 * 64 * 4;
@@ -95,6 +95,8 @@ enum {
   G_AP = 7,       // dAE / dPE tile written
   G_M3456 = 8,    // P3 .. P6 in TMEM: every product of the item complete
   G_KQFREE = 9,   // the last epilogue's reads of K and Q done (8 warps)
+  G_FULL2 = 10,   // dO (and the hand-off's V', dX, h, dh, rowsum partials) landed
+  G_HFREE = 11,   // (hand-off) h, dh and the rowsum partials read (8 warps)
 };
 
 // TMEM columns (the CTA has the SM to itself)
@@ -135,7 +137,13 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
                     int T, int H, int Hk, int N, const unsigned char* __restrict__ hb,
                     const unsigned char* __restrict__ dhb,
                     const __grid_constant__ CUtensorMap tmVP,
-                    const __grid_constant__ CUtensorMap tmDX) {
+                    const __grid_constant__ CUtensorMap tmDX,
+                    const __grid_constant__ CUtensorMap tmDQ,
+                    const __grid_constant__ CUtensorMap tmDK, int tma_out) {
+  // tma_out (dense rows, dq and dk written directly): each item's dK and dQ
+  // rows are staged as bf16 tiles (dK over the dAE / dPE tile, which P5 and P6
+  // no longer read, dQ in SM_QST) and written by four tensor stores, instead
+  // of 16-byte stores scattered over 64 rows 4 KB apart
   // hb / dhb (the scans' hand-off; dense rows only): h and dh of every (chunk,
   // head) as the bf16 tiles the scan kernels wrote (64 KB slots, [column
   // tile][128 key rows][128 B], 128-byte swizzled), loaded by bulk copies with
@@ -197,6 +205,8 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
     mbar_init(&bars[G_AP], 8);
     mbar_init(&bars[G_M3456], 1);
     mbar_init(&bars[G_KQFREE], 8);
+    mbar_init(&bars[G_FULL2], 1);
+    mbar_init(&bars[G_HFREE], 8);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -210,44 +220,75 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
   const uint32_t sbase = smem_u32(sm);
 
   if (warp == 0) {
-    // ---- q, k, dO (TMA) and the products ----
+    // ---- loads (TMA, bulk copies) and the products ----
     if (lane == 0 && cnt > 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmO);
-      auto load = [&](int j) {
+      // G_FULL2: everything the products P1 .. P4 read (dO; with the hand-off
+      // also V', dX, h, dh and the rowsum partials), loaded once P1 .. P6 of
+      // the previous item completed; G_FULL: K and Q, which the last epilogue
+      // also reads, loaded once it has
+      auto load_a = [&](int j) {
         const Item it = item(j);
-        mbar_arrive_expect_tx(&bars[G_FULL], hb ? 49152 + 65536 + 32768 + 1024 : 49152);
+        mbar_arrive_expect_tx(&bars[G_FULL2], hb ? 16384 + 65536 + 32768 + 1024 : 16384);
         if (hb) {
           const size_t ws = (size_t)it.gc * H + it.h;
-          bulk_g2s(sm + L::SM_H, hb + ws * 65536, 32768, &bars[G_FULL]);
-          bulk_g2s(sm + L::SM_DH, dhb + ws * 65536, 32768, &bars[G_FULL]);
-          bulk_g2s(sm + L::SM_RED + RD_XVP * 256, dhb + ws * 65536 + 32768, 1024, &bars[G_FULL]);
+          bulk_g2s(sm + L::SM_H, hb + ws * 65536, 32768, &bars[G_FULL2]);
+          bulk_g2s(sm + L::SM_DH, dhb + ws * 65536, 32768, &bars[G_FULL2]);
+          bulk_g2s(sm + L::SM_RED + RD_XVP * 256, dhb + ws * 65536 + 32768, 1024, &bars[G_FULL2]);
           for (int cb = 0; cb < 2; ++cb) {
-            tma_load_2d(sm + L::SM_VP + cb * 8192, &tmVP, 64 * cb, (int)(ws * C), &bars[G_FULL]);
-            tma_load_2d(sm + L::SM_XO + cb * 16384, &tmDX, 64 * cb, (int)(ws * C), &bars[G_FULL]);
+            tma_load_2d(sm + L::SM_VP + cb * 8192, &tmVP, 64 * cb, (int)(ws * C), &bars[G_FULL2]);
+            tma_load_2d(sm + L::SM_XO + cb * 16384, &tmDX, 64 * cb, (int)(ws * C),
+                        &bars[G_FULL2]);
           }
         }
+        for (int kb = 0; kb < 2; ++kb)
+          tma_load_4d(sm + L::SM_XO + kb * 16384 + 8192, &tmO, 64 * kb, it.h, it.tok, it.b,
+                      &bars[G_FULL2]);
+      };
+      auto load_b = [&](int j) {
+        const Item it = item(j);
+        mbar_arrive_expect_tx(&bars[G_FULL], 32768);
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_4d(sm + L::SM_KQ + kb * 16384, &tmK, 64 * kb, it.hq, it.tok, it.b, &bars[G_FULL]);
           tma_load_4d(sm + L::SM_KQ + kb * 16384 + 8192, &tmQ, 64 * kb, it.hq, it.tok, it.b,
                       &bars[G_FULL]);
-          tma_load_4d(sm + L::SM_XO + kb * 16384 + 8192, &tmO, 64 * kb, it.h, it.tok, it.b,
-                      &bars[G_FULL]);
+        }
+      };
+      // item j's inputs into L2 an item before their loads (no completion to
+      // wait for: a prefetch only warms the cache)
+      auto prefetch = [&](int j) {
+        const Item it = item(j);
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_prefetch_4d(&tmK, 64 * kb, it.hq, it.tok, it.b);
+          tma_prefetch_4d(&tmQ, 64 * kb, it.hq, it.tok, it.b);
+          tma_prefetch_4d(&tmO, 64 * kb, it.h, it.tok, it.b);
+        }
+        if (hb) {
+          const size_t ws = (size_t)it.gc * H + it.h;
+          bulk_prefetch_l2(hb + ws * 65536, 32768);
+          bulk_prefetch_l2(dhb + ws * 65536, 32768 + 1024);
+          for (int cb = 0; cb < 2; ++cb) {
+            tma_prefetch_2d(&tmVP, 64 * cb, (int)(ws * C));
+            tma_prefetch_2d(&tmDX, 64 * cb, (int)(ws * C));
+          }
         }
       };
       const uint32_t kq = sbase + L::SM_KQ, xo = sbase + L::SM_XO, vp = sbase + L::SM_VP;
       const uint32_t hh = sbase + L::SM_H, dh = sbase + L::SM_DH, ap = sbase + L::SM_AP;
-      const uint32_t bk = sbase + L::SM_BK;
-      load(0);
-      int pend = 0;   // the item whose load was issued and not yet seen to land (-1: none)
+      load_a(0);
+      load_b(0);
+      if (cnt > 1) prefetch(1);
+      int pend_a = 0, pend_b = 0;   // items whose loads were issued and not yet seen (-1: none)
       for (int j = 0; j < cnt; ++j) {
-        bool ok = mbar_wait(&bars[G_FULL], (uint32_t)j & 1u);
-        pend = -1;
-        // with the hand-off, P1 .. P4 read only loaded tiles; beta K (P6) was
-        // written before the G_AP arrivals that P6 waits for
+        bool ok = mbar_wait(&bars[G_FULL2], (uint32_t)j & 1u) &&
+                  mbar_wait(&bars[G_FULL], (uint32_t)j & 1u);
+        pend_a = pend_b = -1;
+        // with the hand-off, P1 .. P4 read only loaded tiles
         ok = ok && (hb || mbar_wait(&bars[G_CONV], (uint32_t)j & 1u));
         if (!ok) break;
+        if (j + 2 < cnt) prefetch(j + 2);
         tc_fence_after();
         // P2 = [K;Q] K^T and P1 = [dX;dO] V'^T (K-dim 128 in 8 steps of 16)
 #pragma unroll
@@ -276,15 +317,15 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         ok = mbar_wait(&bars[G_AP], (uint32_t)j & 1u);
         if (!ok) break;
         tc_fence_after();
-        // P5 = [dAE; dPE] K: A K-major over the chunk's tokens; B = K, MN-major
-        // (N = dk in two 64-wide blocks 16 KB apart)
+        // P5 = [beta dAE; dPE] K: A K-major over the chunk's tokens; B = K,
+        // MN-major (N = dk in two 64-wide blocks 16 KB apart)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + GT_P5, umma_desc(ap + k * 32, 16, 1024, SW128),
                    umma_desc(kq + k * 2048, 16384, 1024, SW128), IDESC_N128_KM, k > 0);
-        // P6 = dPE^T Q + dAE^T (beta K): A = dPE^T / dAE^T read MN-major from
-        // the rows of dPE / dAE (M = 64 tokens; the second M block, 8 KB on, is
-        // not used: rows 64-127 of P6 are ignored)
+        // P6 = dPE^T Q + (beta dAE)^T K: A = dPE^T / (beta dAE)^T read MN-major
+        // from the rows of the tile (M = 64 tokens; the second M block, 8 KB
+        // on, is not used: rows 64-127 of P6 are ignored)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + GT_P6, umma_desc(ap + 8192 + k * 2048, 8192, 1024, SW128),
@@ -292,19 +333,25 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + GT_P6, umma_desc(ap + k * 2048, 8192, 1024, SW128),
-                   umma_desc(bk + k * 2048, 8192, 1024, SW128), IDESC_N128_MM, 1u);
+                   umma_desc(kq + k * 2048, 16384, 1024, SW128), IDESC_N128_MM, 1u);
         mma_commit(&bars[G_M3456]);
-        // every product has read q, k, dO, and the last epilogue has read its
-        // rows of K and Q: load the next item's
         if (j + 1 < cnt) {
+          // every product has read dO, V', dX, h, dh (and the epilogues their
+          // h, dh, partials): the next item's
           if (!mbar_wait(&bars[G_M3456], (uint32_t)j & 1u) ||
-              !mbar_wait(&bars[G_KQFREE], (uint32_t)j & 1u))
+              (hb && !mbar_wait(&bars[G_HFREE], (uint32_t)j & 1u)))
             break;
-          load(j + 1);
-          pend = j + 1;
+          load_a(j + 1);
+          pend_a = j + 1;
+          // and the last epilogue has read its rows of K and Q
+          if (!mbar_wait(&bars[G_KQFREE], (uint32_t)j & 1u)) break;
+          load_b(j + 1);
+          pend_b = j + 1;
         }
       }
-      if (pend >= 0) mbar_wait(&bars[G_FULL], (uint32_t)pend & 1u);   // before the CTA exits
+      // (before the CTA exits)
+      if (pend_a >= 0) mbar_wait(&bars[G_FULL2], (uint32_t)pend_a & 1u);
+      if (pend_b >= 0) mbar_wait(&bars[G_FULL], (uint32_t)pend_b & 1u);
     }
   } else if (warp == 1) {
     // ---- gate vectors, one item ahead ----
@@ -364,9 +411,8 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       const GrVec& vb = vecs[s];
       ok = mbar_wait(&bars[G_VFULL + s], (uint32_t)(j >> 1) & 1u) && ok;
 
-      // ---- bf16 tiles: dX (over the [dX; dO] blocks), V', h, dh, beta K;
-      //      dV = beta dX; rowsum(dX o V); <h, dh> (with the hand-off: beta K,
-      //      <h, dh> and the sum of the rowsum partials) ----
+      // ---- without the hand-off: bf16 tiles of dX (over the [dX; dO]
+      //      blocks), V', h, dh; dV = beta dX; rowsum(dX o V); <h, dh> ----
       if (!hb) {
         const int m = pi >> 2, c0 = (pi & 3) * 32, cb = c0 >> 6, k8 = (c0 & 63) >> 3;
         const bool valid = m < it.len;
@@ -438,65 +484,28 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         for (int o = 16; o > 0; o >>= 1) hd += __shfl_xor_sync(0xffffffffu, hd, o);
         if (lane == 0) red[RD_HD * 64 + pw] = hd;
       }
-      {
-        // beta K (rows scaled), once K has landed: row m, 32 key columns
-        ok = mbar_wait(&bars[G_FULL], (uint32_t)j & 1u) && ok;
-        if (hb) {
-          // <h, dh> from the bf16 tiles: key row pi / 2, column tile pi % 2
-          const int r = pi >> 1, cb = pi & 1;
-          float hd = 0.f;
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            float a8[8], d8[8];
-            unpack_bf16x8(
-                *reinterpret_cast<const uint4*>(sm + L::SM_H + cb * 16384 + sw128(r, c8)), a8);
-            unpack_bf16x8(
-                *reinterpret_cast<const uint4*>(sm + L::SM_DH + cb * 16384 + sw128(r, c8)), d8);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) hd = fmaf(a8[e], d8[e], hd);
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) hd += __shfl_xor_sync(0xffffffffu, hd, o);
-          if (lane == 0) red[RD_HD * 64 + pw] = hd;
-          if (pi < 64) {
-            const float* xp = red + RD_XVP * 64 + pi * 4;
-            red[RD_XV * 64 + pi] = (xp[0] + xp[1]) + (xp[2] + xp[3]);
-          }
+      if (!hb) {
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[G_CONV]);
+        // the next item's rows of dX, V', v, h, dh into L2 (this thread's own
+        // conversion reads), so that its conversion does not wait on DRAM
+        if (j + 1 < cnt) {
+          const Item nx = item(j + 1);
+          const size_t ns = (size_t)nx.gc * H + nx.h;
+          const int m = pi >> 2, c0 = (pi & 3) * 32, r = pi >> 1, cb = pi & 1;
+          prefetch_l2(YX + (ns * C + m) * GR_D + c0);
+          prefetch_l2(UV + (ns * C + m) * GR_D + c0);
+          if (m < nx.len)
+            prefetch_l2(v + (((size_t)nx.b * T + nx.tok + m) * H + nx.h) * GR_D + c0);
+          const float* hr = hs + (ns * GR_D + r) * GR_D + cb * 64;
+          const float* dr = dhs + (ns * GR_D + r) * GR_D + cb * 64;
+          prefetch_l2(hr);
+          prefetch_l2(hr + 32);
+          prefetch_l2(dr);
+          prefetch_l2(dr + 32);
         }
-        const int m = pi >> 2, kb = (pi & 3) >> 1, k8 = (pi & 1) * 4;
-        const float bm = vb.beta[m];
-#pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          float kk[8];
-          unpack_bf16x8(
-              *reinterpret_cast<const uint4*>(sm + L::SM_KQ + kb * 16384 + sw128(m, k8 + c8)), kk);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) kk[e] *= bm;
-          *reinterpret_cast<uint4*>(sm + L::SM_BK + kb * 8192 + sw128(m, k8 + c8)) =
-              pack_bf16x8(kk);
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[G_CONV]);
-
-      // the next item's rows of dX, V', v, h, dh into L2 (this thread's own
-      // conversion reads), so that its conversion does not wait on DRAM (with
-      // the hand-off, the next item's tiles are already being loaded)
-      if (j + 1 < cnt && !hb) {
-        const Item nx = item(j + 1);
-        const size_t ns = (size_t)nx.gc * H + nx.h;
-        const int m = pi >> 2, c0 = (pi & 3) * 32, r = pi >> 1, cb = pi & 1;
-        prefetch_l2(YX + (ns * C + m) * GR_D + c0);
-        prefetch_l2(UV + (ns * C + m) * GR_D + c0);
-        if (m < nx.len) prefetch_l2(v + (((size_t)nx.b * T + nx.tok + m) * H + nx.h) * GR_D + c0);
-        const float* hr = hs + (ns * GR_D + r) * GR_D + cb * 64;
-        const float* dr = dhs + (ns * GR_D + r) * GR_D + cb * 64;
-        prefetch_l2(hr);
-        prefetch_l2(hr + 32);
-        prefetch_l2(dr);
-        prefetch_l2(dr + 32);
       }
 
       // ---- first epilogue: dAE (lanes 0-63) and dPE (lanes 64-127), row i,
@@ -522,7 +531,7 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
           if (!side) rb = fmaf(val, kk[e], rb);
           rg += xx;
           col[e] = xx;
-          a[e] = val;
+          a[e] = side ? val : val * bi;   // the tile holds beta dAE
         }
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8)
@@ -537,15 +546,43 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[G_AP]);
 
+      if (hb) {
+        // ---- while P5, P6 run: <h, dh> from the bf16 tiles (key row pi / 2,
+        //      column tile pi % 2) and the sum of the rowsum(dX o v) partials ----
+        ok = mbar_wait(&bars[G_FULL2], (uint32_t)j & 1u) && ok;
+        const int r = pi >> 1, cb = pi & 1;
+        float hd = 0.f;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float a8[8], d8[8];
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::SM_H + cb * 16384 + sw128(r, c8)),
+                        a8);
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::SM_DH + cb * 16384 + sw128(r, c8)),
+                        d8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hd = fmaf(a8[e], d8[e], hd);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) hd += __shfl_xor_sync(0xffffffffu, hd, o);
+        if (lane == 0) red[RD_HD * 64 + pw] = hd;
+        if (pi < 64) {
+          const float* xp = red + RD_XVP * 64 + pi * 4;
+          red[RD_XV * 64 + pi] = (xp[0] + xp[1]) + (xp[2] + xp[3]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[G_HFREE]);
+      }
+
       // ---- last epilogue: dK on lanes 0-63, dQ on lanes 64-127, token row m,
       //      key columns 64 ch .. 64 ch + 63 in four steps of 16 ----
       ok = mbar_wait(&bars[G_M3456], (uint32_t)j & 1u) && ok;
+      ok = mbar_wait(&bars[G_FULL], (uint32_t)j & 1u) && ok;   // (K, Q rows read below)
       tc_fence_after();
       {
         const int side = p >> 6, m = p & 63;
         const bool valid = m < it.len;
         const size_t trow = ((size_t)it.b * T + it.tok + m);
-        const float em = vb.e[m], dm = vb.d[m], bm = vb.beta[m], bem = vb.be[m];
+        const float em = vb.e[m], dm = vb.d[m], bem = vb.be[m];
         float r1 = 0.f, r2 = 0.f;   // dK side: rowsum(K o Kd), rowsum(K o M); dQ side: rowsum(Q o Q0)
 #pragma unroll 1
         for (int sub = 0; sub < 4; ++sub) {
@@ -564,7 +601,7 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
             tmem_ld16(tmem + GT_P6 + (uint32_t)c + lane_off, ak);
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              out[e] = dm * Kd[e] - bem * Mv[e] + ak[e] + bm * AK[e];
+              out[e] = dm * Kd[e] - bem * Mv[e] + ak[e] + AK[e];
               r1 = fmaf(kr[e], Kd[e], r1);
               r2 = fmaf(kr[e], Mv[e], r2);
             }
@@ -578,7 +615,13 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
               r1 = fmaf(kr[e], Q0[e], r1);
             }
           }
-          if (valid) {
+          if (tma_out) {
+            // staged for the item's tensor stores (rows past the end of T are
+            // clipped by the store): dK over the dAE / dPE tile, dQ in SM_QST
+            unsigned char* stg = sm + (side ? L::SM_QST : L::SM_AP) + kb * 8192;
+            *reinterpret_cast<uint4*>(stg + sw128(m, k8)) = pack_bf16x8(out);
+            *reinterpret_cast<uint4*>(stg + sw128(m, k8 + 1)) = pack_bf16x8(out + 8);
+          } else if (valid) {
             if (dqk) {   // grouped q/k heads: per value head, summed afterwards
               float* dst = dqk + (side ? 0 : plane) + (trow * H + it.h) * GR_D + c;
 #pragma unroll
@@ -602,8 +645,17 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
           red[(RD_QG + ch) * 64 + m] = em * r1;
         }
       }
+      if (tma_out) fence_proxy_async_smem();
       tc_fence_before();
       named_sync(1, 256);
+      if (tma_out && pi == 32) {
+        // the item's dK and dQ rows: four tensor stores of 64 x 64 tiles
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_store_4d(&tmDK, 64 * kb, it.hq, it.tok, it.b, sm + L::SM_AP + kb * 8192);
+          tma_store_4d(&tmDQ, 64 * kb, it.hq, it.tok, it.b, sm + L::SM_QST + kb * 8192);
+        }
+        bulk_commit();
+      }
       // ---- per token: dG, dbeta; dG_C; dg = reverse in-chunk cumsum of dG ----
       if (pi < 32) {
         const int l = pi;
@@ -650,9 +702,12 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         }
         if (l == 0) mbar_arrive(&bars[G_VEMPTY + s]);
       }
-      // the partial sums are read; the next item may overwrite them
+      // the partial sums are read, and the stores have read their staging:
+      // the next item may overwrite both
+      if (tma_out && pi == 32) bulk_wait_read<0>();
       if (!named_sync_and(1, 256, ok)) break;
     }
+    if (tma_out && pi == 32) bulk_wait<0>();
   }
   tc_fence_before();
   __syncthreads();
@@ -675,15 +730,19 @@ cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st) {
   if ((long long)rows * a.H == 0 || a.T == 0 || a.NC == 0) return cudaSuccess;
   const bool hand = a.hb != nullptr;
   if (hand && (a.n_seqs || !a.dhb || !a.vpb || !a.dxb)) return cudaErrorInvalidValue;
-  CUtensorMap mk, mq, mo, mvp, mdx;
+  const bool tma_out = !a.n_seqs && !a.dqk;
+  CUtensorMap mk, mq, mo, mvp, mdx, mdq, mdk;
   const long long slot_rows = (long long)a.NC * a.H * C;
   if (!make_bf16_map_4d(&mk, a.k, rows, a.T, a.Hk, GR_D) ||
       !make_bf16_map_4d(&mq, a.q, rows, a.T, a.Hk, GR_D) ||
       !make_bf16_map_4d(&mo, a.dO, rows, a.T, a.H, GR_D) ||
       (hand && (!make_bf16_map_2d(&mvp, a.vpb, slot_rows, GR_D, true) ||
-                !make_bf16_map_2d(&mdx, a.dxb, slot_rows, GR_D, true))))
+                !make_bf16_map_2d(&mdx, a.dxb, slot_rows, GR_D, true))) ||
+      (tma_out && (!make_bf16_map_4d(&mdq, a.dq, rows, a.T, a.Hk, GR_D) ||
+                   !make_bf16_map_4d(&mdk, a.dk, rows, a.T, a.Hk, GR_D))))
     return cudaErrorInvalidValue;
   if (!hand) mvp = mdx = mo;   // (not read)
+  if (!tma_out) mdq = mdk = mo;
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(bwd_grads_tc_kernel, GrLay::SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
@@ -693,7 +752,7 @@ cudaError_t launch_bwd_grads_tc(const BwdGradsArgs& a, cudaStream_t st) {
       mk, mq, mo, static_cast<const __nv_bfloat16*>(a.v), a.g, a.beta, a.UV, a.YX, a.hs, a.dhs,
       static_cast<__nv_bfloat16*>(a.dq), static_cast<__nv_bfloat16*>(a.dk),
       static_cast<__nv_bfloat16*>(a.dv), a.dg, a.dbeta, a.dqk, a.cu, a.coff, a.n_seqs, rows, a.T,
-      a.H, a.Hk, (a.T + C - 1) / C, a.hb, a.dhb, mvp, mdx);
+      a.H, a.Hk, (a.T + C - 1) / C, a.hb, a.dhb, mvp, mdx, mdq, mdk, tma_out ? 1 : 0);
   return cudaGetLastError();
 }
 
