@@ -97,6 +97,7 @@ enum {
   G_KQFREE = 9,   // the last epilogue's reads of K and Q done (8 warps)
   G_FULL2 = 10,   // dO (and the hand-off's V', dX, h, dh, rowsum partials) landed
   G_HFREE = 11,   // (hand-off) h, dh and the rowsum partials read (8 warps)
+  G_M1234 = 12,   // P1 .. P4 complete: dO, V', dX, h, dh no longer read
 };
 
 // TMEM columns (the CTA has the SM to itself)
@@ -207,6 +208,7 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
     mbar_init(&bars[G_KQFREE], 8);
     mbar_init(&bars[G_FULL2], 1);
     mbar_init(&bars[G_HFREE], 8);
+    mbar_init(&bars[G_M1234], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -226,9 +228,10 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmO);
       // G_FULL2: everything the products P1 .. P4 read (dO; with the hand-off
-      // also V', dX, h, dh and the rowsum partials), loaded once P1 .. P6 of
-      // the previous item completed; G_FULL: K and Q, which the last epilogue
-      // also reads, loaded once it has
+      // also V', dX, h, dh and the rowsum partials), loaded once P1 .. P4 of
+      // the previous item completed (its epilogues still running); G_FULL: K
+      // and Q, which P5, P6 and the last epilogue also read, loaded once those
+      // have
       auto load_a = [&](int j) {
         const Item it = item(j);
         mbar_arrive_expect_tx(&bars[G_FULL2], hb ? 16384 + 65536 + 32768 + 1024 : 16384);
@@ -314,6 +317,16 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
           mma_bf16(tmem + GT_P4, umma_desc(vp + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024, SW128),
                    umma_desc(dh + off, 16, 1024, SW128), IDESC_N128_KK, k > 0);
         }
+        mma_commit(&bars[G_M1234]);
+        if (j + 1 < cnt) {
+          // P1 .. P4 have read dO, V', dX, h, dh (and the epilogues their h,
+          // dh, partials): the next item's, while this item's epilogues run
+          if (!mbar_wait(&bars[G_M1234], (uint32_t)j & 1u) ||
+              (hb && !mbar_wait(&bars[G_HFREE], (uint32_t)j & 1u)))
+            break;
+          load_a(j + 1);
+          pend_a = j + 1;
+        }
         ok = mbar_wait(&bars[G_AP], (uint32_t)j & 1u);
         if (!ok) break;
         tc_fence_after();
@@ -336,15 +349,10 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
                    umma_desc(kq + k * 2048, 16384, 1024, SW128), IDESC_N128_MM, 1u);
         mma_commit(&bars[G_M3456]);
         if (j + 1 < cnt) {
-          // every product has read dO, V', dX, h, dh (and the epilogues their
-          // h, dh, partials): the next item's
+          // every product and the last epilogue have read K and Q: the next item's
           if (!mbar_wait(&bars[G_M3456], (uint32_t)j & 1u) ||
-              (hb && !mbar_wait(&bars[G_HFREE], (uint32_t)j & 1u)))
+              !mbar_wait(&bars[G_KQFREE], (uint32_t)j & 1u))
             break;
-          load_a(j + 1);
-          pend_a = j + 1;
-          // and the last epilogue has read its rows of K and Q
-          if (!mbar_wait(&bars[G_KQFREE], (uint32_t)j & 1u)) break;
           load_b(j + 1);
           pend_b = j + 1;
         }
@@ -508,6 +516,33 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         }
       }
 
+      if (hb) {
+        // ---- while P1, P2 run: <h, dh> from the bf16 tiles (key row pi / 2,
+        //      column tile pi % 2) and the sum of the rowsum(dX o v) partials ----
+        ok = mbar_wait(&bars[G_FULL2], (uint32_t)j & 1u) && ok;
+        const int r = pi >> 1, cb = pi & 1;
+        float hd = 0.f;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float a8[8], d8[8];
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::SM_H + cb * 16384 + sw128(r, c8)),
+                        a8);
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::SM_DH + cb * 16384 + sw128(r, c8)),
+                        d8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hd = fmaf(a8[e], d8[e], hd);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) hd += __shfl_xor_sync(0xffffffffu, hd, o);
+        if (lane == 0) red[RD_HD * 64 + pw] = hd;
+        if (pi < 64) {
+          const float* xp = red + RD_XVP * 64 + pi * 4;
+          red[RD_XV * 64 + pi] = (xp[0] + xp[1]) + (xp[2] + xp[3]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[G_HFREE]);
+      }
+
       // ---- first epilogue: dAE (lanes 0-63) and dPE (lanes 64-127), row i,
       //      columns 32 ch ..; their row and column sums against K K^T / Q K^T ----
       ok = mbar_wait(&bars[G_M12], (uint32_t)j & 1u) && ok;
@@ -546,32 +581,6 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[G_AP]);
 
-      if (hb) {
-        // ---- while P5, P6 run: <h, dh> from the bf16 tiles (key row pi / 2,
-        //      column tile pi % 2) and the sum of the rowsum(dX o v) partials ----
-        ok = mbar_wait(&bars[G_FULL2], (uint32_t)j & 1u) && ok;
-        const int r = pi >> 1, cb = pi & 1;
-        float hd = 0.f;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          float a8[8], d8[8];
-          unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::SM_H + cb * 16384 + sw128(r, c8)),
-                        a8);
-          unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + L::SM_DH + cb * 16384 + sw128(r, c8)),
-                        d8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) hd = fmaf(a8[e], d8[e], hd);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) hd += __shfl_xor_sync(0xffffffffu, hd, o);
-        if (lane == 0) red[RD_HD * 64 + pw] = hd;
-        if (pi < 64) {
-          const float* xp = red + RD_XVP * 64 + pi * 4;
-          red[RD_XV * 64 + pi] = (xp[0] + xp[1]) + (xp[2] + xp[3]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[G_HFREE]);
-      }
 
       // ---- last epilogue: dK on lanes 0-63, dQ on lanes 64-127, token row m,
       //      key columns 64 ch .. 64 ch + 63 in four steps of 16 ----
