@@ -248,7 +248,7 @@ size_t gdn_chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, in
  * fixed array of GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES (64 MiB) in this
  * library's own device memory; sizes whose gdn_chunk_bwd_workspace_bytes()
  * is larger are rejected with GDN_ERR_UNSUPPORTED (e.g. B*H = 16 heads at
- * dk = dv = 128 fit up to T = 736 tokens).  The call itself allocates
+ * dk = dv = 128 fit up to T = 768 tokens).  The call itself allocates
  * nothing: no cudaMalloc, cudaFree or allocating library routine.
  *
  * - The array is reserved on a GPU when the driver loads the module that
