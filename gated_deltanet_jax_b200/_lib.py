@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "gdn_chunk_bwd",
     "gdn_chunk_bwd_noalloc",
     "gdn_chunk_bwd_workspace_bytes",
+    "gdn_chunk_bwd_workspace_bytes_for",
     "gdn_chunk_bwd_varlen",
     "gdn_chunk_bwd_varlen_workspace_bytes",
     "gdn_chunk_workspace_bytes",
@@ -100,6 +101,8 @@ def _declare(lib):
     lib.gdn_chunk_bwd_noalloc.restype = _i
     lib.gdn_chunk_bwd_workspace_bytes.argtypes = [_i] * 5
     lib.gdn_chunk_bwd_workspace_bytes.restype = _sz
+    lib.gdn_chunk_bwd_workspace_bytes_for.argtypes = [_i] * 7
+    lib.gdn_chunk_bwd_workspace_bytes_for.restype = _sz
     lib.gdn_chunk_bwd_varlen.argtypes = [_vp] * 15 + [_i] * 7 + [_vp, _sz, _vp]
     lib.gdn_chunk_bwd_varlen.restype = _i
     lib.gdn_chunk_bwd_varlen_workspace_bytes.argtypes = [_i] * 5

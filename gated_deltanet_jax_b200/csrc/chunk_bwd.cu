@@ -1141,7 +1141,9 @@ struct WsLayout {
 
 int padded_dk(int dk) { return dk <= 32 ? 32 : dk <= 64 ? 64 : dk <= 128 ? 128 : 256; }
 
-// NC chunks per head, tokens in all, n_seqs chunk offsets (0: dense).
+// NC chunks per head, tokens in all, n_seqs chunk offsets (0: dense).  The
+// layout every path fits (fp32 W, Z, U/V', Y/dX, entering states, leaving
+// state gradients).
 WsLayout ws_layout(size_t NC, size_t tokens, int H, int dk, int dv, int n_seqs) {
   const size_t ldw = (size_t)padded_dk(dk);
   WsLayout L{};
@@ -1164,15 +1166,50 @@ WsLayout ws_layout(size_t NC, size_t tokens, int H, int dk, int dv, int n_seqs) 
   return L;
 }
 
+// The layout of the tcgen05 path's bf16 hand-off (dense, dk = dv = 128), in
+// floats: the preparation's [Z | PT | T] slots (32 KB per chunk and head), V'
+// and dX as bf16 rows (UV), the entering states as bf16 tiles (hs, 32 KB
+// slots), the leaving gradients as bf16 tiles with the dX.v row partials (dhs,
+// 36 KB slots), and per value head dq, dk for grouped heads.  Z and YX are
+// not used there; they alias W and UV.
+WsLayout ws_layout_handoff(size_t NC, size_t tokens, int H, bool grouped) {
+  WsLayout L{};
+  size_t o = 0;
+  auto take = [&](size_t n) { const size_t r = o; o += (n + 63) & ~size_t(63); return r; };
+  L.W = take(NC * H * (kTileBytesBwdSlot / sizeof(float)));
+  L.Z = L.W;
+  L.UV = take(NC * H * C * 128);
+  L.YX = L.UV;
+  L.hs = take(NC * H * (kHandoffHSlot / sizeof(float)));
+  L.dhs = take(NC * H * (kHandoffDhSlot / sizeof(float)));
+  L.dqk = take(grouped ? 2 * tokens * H * 128 : 0);
+  L.coff = take(0);
+  L.has_tiles = true;
+  L.tiles = L.W;
+  L.total = o;
+  return L;
+}
+
 // Chunks (an upper bound for packed sequences: sum of ceil(len / C) <= T / C + n_seqs).
 size_t chunk_count(const ChunkBwdArgs& a) {
   return a.cu_seqlens ? (size_t)(a.T / C) + (size_t)a.B
                       : (size_t)a.B * (size_t)((a.T + C - 1) / C);
 }
 
+// Whether the call takes the tcgen05 path with the bf16 hand-off: bf16, dense,
+// dk = dv = 128, none of the backward's kernel overrides set.
+bool bwd_handoff(const ChunkBwdArgs& a) {
+  const KernelOverrides ov = kernel_overrides();
+  return a.dtype == kBF16 && !a.cu_seqlens && a.dk == 128 && a.dv == 128 &&
+         bwd_prep_tc_supported(a.dtype, a.dk, a.dv) &&
+         bwd_grads_tc_supported(a.dtype, a.dk, a.dv) && !ov.bwd_prep_warp &&
+         !ov.bwd_fwdpass_warp && !ov.bwd_revpass_warp && !ov.bwd_grads_warp;
+}
+
 WsLayout ws_layout(const ChunkBwdArgs& a) {
-  return ws_layout(chunk_count(a), a.cu_seqlens ? (size_t)a.T : (size_t)a.B * a.T, a.H, a.dk,
-                   a.dv, a.cu_seqlens ? a.B : 0);
+  const size_t tokens = a.cu_seqlens ? (size_t)a.T : (size_t)a.B * a.T;
+  if (bwd_handoff(a)) return ws_layout_handoff(chunk_count(a), tokens, a.H, a.Hk != a.H);
+  return ws_layout(chunk_count(a), tokens, a.H, a.dk, a.dv, a.cu_seqlens ? a.B : 0);
 }
 
 template <typename Tin, int DKP>
@@ -1204,6 +1241,7 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   const bool tc_prep = sizeof(Tin) == 2 && bwd_prep_tc_supported(a.dtype, a.dk, a.dv) &&
                        !ov.bwd_prep_warp;
   const bool tc_fwd = tc_prep && !packed && L.has_tiles && !ov.bwd_fwdpass_warp;
+  const bool hand = bwd_handoff(a);   // (the layout above is then the compact one)
   const bool tc_rev = tc_fwd && !ov.bwd_revpass_warp;
   unsigned char* tiles = reinterpret_cast<unsigned char*>(ws + L.tiles);
   ChunkArgs fa{};
@@ -1229,7 +1267,7 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   // the tcgen05 scans hand h and dh to the tcgen05 gradients as bf16 tiles
   const bool tc_grads = tc_prep && bwd_grads_tc_supported(a.dtype, a.dk, a.dv) &&
                         !ov.bwd_grads_warp;
-  const bool tiles_hd = tc_rev && tc_grads;
+  const bool tiles_hd = hand;
   // the hand-off's bf16 V' and dX rows share the UV region: V' first, then dX
   void* dx_bf16 = reinterpret_cast<__nv_bfloat16*>(p.UV) + (size_t)NC * a.H * C * a.dv;
   if (tc_fwd) {
@@ -1342,8 +1380,12 @@ cudaError_t launch_fwd_dtype(const ChunkArgs& a, cudaStream_t st) {
 }  // namespace
 
 size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv) {
-  ChunkBwdArgs a{};
-  a.B = B; a.T = T; a.H = H; a.dk = dk; a.dv = dv;
+  ChunkBwdArgs a{};   // (fp32: the layout that fits every path)
+  a.B = B; a.T = T; a.H = H; a.Hk = H; a.dk = dk; a.dv = dv; a.dtype = kFP32;
+  return sizeof(float) * ws_layout(a).total;
+}
+
+size_t chunk_bwd_workspace_bytes_for(const ChunkBwdArgs& a) {
   return sizeof(float) * ws_layout(a).total;
 }
 
@@ -1351,7 +1393,7 @@ size_t chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv
   ChunkBwdArgs a{};
   static const int kPacked = 0;   // any non-NULL pointer: the layout of packed sequences
   a.cu_seqlens = &kPacked;
-  a.B = n_seqs; a.T = T; a.H = H; a.dk = dk; a.dv = dv;
+  a.B = n_seqs; a.T = T; a.H = H; a.Hk = H; a.dk = dk; a.dv = dv; a.dtype = kFP32;
   return sizeof(float) * ws_layout(a).total;
 }
 

@@ -146,7 +146,7 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
   // no longer read, dQ in SM_QST) and written by four tensor stores, instead
   // of 16-byte stores scattered over 64 rows 4 KB apart
   // hb / dhb (the scans' hand-off; dense rows only): h and dh of every (chunk,
-  // head) as the bf16 tiles the scan kernels wrote (64 KB slots, [column
+  // head) as the bf16 tiles the scan kernels wrote (32 and 36 KB slots, [column
   // tile][128 key rows][128 B], 128-byte swizzled), loaded by bulk copies with
   // the rowsum(dX o v) partials (each dhs slot + 32 KB); V' and dX loaded by
   // TMA (tmVP, tmDX: bf16 rows [slots C][dv], 64 x 64 boxes, 128-byte swizzle).
@@ -237,9 +237,10 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         mbar_arrive_expect_tx(&bars[G_FULL2], hb ? 16384 + 65536 + 32768 + 1024 : 16384);
         if (hb) {
           const size_t ws = (size_t)it.gc * H + it.h;
-          bulk_g2s(sm + L::SM_H, hb + ws * 65536, 32768, &bars[G_FULL2]);
-          bulk_g2s(sm + L::SM_DH, dhb + ws * 65536, 32768, &bars[G_FULL2]);
-          bulk_g2s(sm + L::SM_RED + RD_XVP * 256, dhb + ws * 65536 + 32768, 1024, &bars[G_FULL2]);
+          bulk_g2s(sm + L::SM_H, hb + ws * kHandoffHSlot, 32768, &bars[G_FULL2]);
+          bulk_g2s(sm + L::SM_DH, dhb + ws * kHandoffDhSlot, 32768, &bars[G_FULL2]);
+          bulk_g2s(sm + L::SM_RED + RD_XVP * 256, dhb + ws * kHandoffDhSlot + 32768, 1024,
+                   &bars[G_FULL2]);
           for (int cb = 0; cb < 2; ++cb) {
             tma_load_2d(sm + L::SM_VP + cb * 8192, &tmVP, 64 * cb, (int)(ws * C), &bars[G_FULL2]);
             tma_load_2d(sm + L::SM_XO + cb * 16384, &tmDX, 64 * cb, (int)(ws * C),
@@ -270,8 +271,8 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         }
         if (hb) {
           const size_t ws = (size_t)it.gc * H + it.h;
-          bulk_prefetch_l2(hb + ws * 65536, 32768);
-          bulk_prefetch_l2(dhb + ws * 65536, 32768 + 1024);
+          bulk_prefetch_l2(hb + ws * kHandoffHSlot, 32768);
+          bulk_prefetch_l2(dhb + ws * kHandoffDhSlot, 32768 + 1024);
           for (int cb = 0; cb < 2; ++cb) {
             tma_prefetch_2d(&tmVP, 64 * cb, (int)(ws * C));
             tma_prefetch_2d(&tmDX, 64 * cb, (int)(ws * C));

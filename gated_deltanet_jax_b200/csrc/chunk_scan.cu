@@ -494,7 +494,7 @@ __device__ __forceinline__ void stage_store_bf16(unsigned char* stg, const float
 // row segments per store instruction.  With hsb, the entering states go out
 // instead as the bf16 state tile the chain already holds in shared memory
 // (16 KB per chunk and CTA, [dk rows][64 columns], 128-byte swizzled) at
-// hsb + ((b N + n) H + h) 64 KB + 16 KB x (column tile): one bulk copy per
+// hsb + ((b N + n) H + h) 32 KB + 16 KB x (column tile): one bulk copy per
 // chunk, the layout the tcgen05 gradients kernel loads; and V' goes to vp as
 // bf16 rows ([((b N + n) H + h) C + i][dv], tmVP a 32 x 32 bf16 map), the
 // operand the gradients take, rounded once.
@@ -614,7 +614,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         mma_commit(&bars[S_D1]);
         if (kBwd && hsb) {
           // the bf16 state entering chunk n, as the tile D1 just read
-          bulk_s2g(hsb + (((size_t)b * N + n) * H + h) * 65536 + blockIdx.x * 16384,
+          bulk_s2g(hsb + (((size_t)b * N + n) * H + h) * kHandoffHSlot + blockIdx.x * 16384,
                    sm + L::SM_S, 16384);
           bulk_commit();
         }
@@ -918,7 +918,7 @@ chunk_scan_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 // preparation's slot.  The epilogue warps on TMEM lanes 64-127 form e dO for the products.
 // With dhsb (the hand-off to the tcgen05 gradients) the CTA also loads its 64
 // columns of v and, from each token row's fp32 dX, writes dV = beta dX (dvo),
-// the row's partial sum of dX o v over its 32 columns (fp32, at dhsb + 64 KB
+// the row's partial sum of dX o v over its 32 columns (fp32, at dhsb + 36 KB x
 // slot + 32 KB, [64 tokens][4 column blocks]), and dX as bf16 rows through
 // tmYX (a 32 x 32 bf16 map) instead of fp32.
 constexpr int kRevTile = 24576;   // Z [128 keys][64 tokens] | PT [64][64], bf16
@@ -1085,7 +1085,8 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         mma_commit(&bars[R_D1]);
         if (dhsb) {
           // the bf16 gradient leaving chunk N - 1 - it, as the tile D1 just read
-          bulk_s2g(dhsb + (((size_t)b * N + (N - 1 - it)) * H + h) * 65536 + blockIdx.x * 16384,
+          bulk_s2g(dhsb + (((size_t)b * N + (N - 1 - it)) * H + h) * kHandoffDhSlot +
+                       blockIdx.x * 16384,
                    sm + L::SM_S, 16384);
           bulk_commit();
         }
@@ -1266,7 +1267,7 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
             }
             if (in) *reinterpret_cast<uint4*>(dst + 8 * c8) = pack_bf16x8(o8);
           }
-          reinterpret_cast<float*>(dhsb + slot * 65536 + 32768)[r * 4 + (c0 + cb) / 32] = xv;
+          reinterpret_cast<float*>(dhsb + slot * kHandoffDhSlot + 32768)[r * 4 + (c0 + cb) / 32] = xv;
           stage_store_bf16(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32, lane);
         } else {
           stage_store(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32);

@@ -419,8 +419,9 @@ int chunk_bwd(const void* q, const void* k, const void* v, const float* g, const
   if (!gdn::chunk_bwd_supported(a))
     return fail(GDN_ERR_UNSUPPORTED, "backward supports dk <= 256, dv a multiple of 32 and "
                 "sequences x heads <= 65535 (dk=%d dv=%d)", dk, dv);
-  const size_t need = cu_seqlens ? gdn_chunk_bwd_varlen_workspace_bytes(B, T, H, dk, dv)
-                                 : gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv);
+  // this call's layout (the compact one of the bf16 hand-off when it applies);
+  // the dtype-blind queries give at least as much
+  const size_t need = (long long)rows * T * H > 0 ? gdn::chunk_bwd_workspace_bytes_for(a) : 0;
   if (ws_bytes < need || (need && !workspace))
     return fail(GDN_ERR_INVALID, "workspace of %zu bytes needed, %zu given", need, ws_bytes);
   if (need && !aligned16(workspace)) return fail(GDN_ERR_INVALID, "workspace is not 16-byte aligned");
@@ -507,6 +508,16 @@ int gdn_chunk_bwd(const void* q, const void* k, const void* v, const float* g,
                    T, H, Hk, dk, dv, dtype, workspace, ws_bytes, stream, "gdn_chunk_bwd");
 }
 
+size_t gdn_chunk_bwd_workspace_bytes_for(int B, int T, int H, int Hk, int dk, int dv,
+                                         int dtype) {
+  if (B <= 0 || T <= 0 || H <= 0 || Hk <= 0 || dk <= 0 || dv <= 0 ||
+      (dtype != GDN_DTYPE_FP32 && dtype != GDN_DTYPE_BF16))
+    return 0;
+  gdn::ChunkBwdArgs a{};
+  a.B = B; a.T = T; a.H = H; a.Hk = Hk; a.dk = dk; a.dv = dv; a.dtype = dtype;
+  return gdn::chunk_bwd_workspace_bytes_for(a);
+}
+
 size_t gdn_chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv) {
   if (n_seqs <= 0 || T <= 0 || H <= 0 || dk <= 0 || dv <= 0) return 0;
   return gdn::chunk_bwd_varlen_workspace_bytes(n_seqs, T, H, dk, dv);
@@ -537,7 +548,7 @@ int gdn_chunk_bwd_noalloc(const void* q, const void* k, const void* v, const flo
   // The size check comes first and touches no device; gdn_chunk_bwd then
   // checks everything else and zeroes the accumulators it uses.
   g_err[0] = '\0';
-  const size_t need = gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv);
+  const size_t need = gdn_chunk_bwd_workspace_bytes_for(B, T, H, Hk, dk, dv, dtype);
   if (need > GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES)
     return fail(GDN_ERR_UNSUPPORTED,
                 "these sizes need %zu bytes of backward scratch; the allocation-free entry "
@@ -629,7 +640,7 @@ int gdn_device_error(int clear) {
   return a ? a : (b ? b : (c ? c : (d ? d : e)));
 }
 
-int gdn_abi_version(void) { return (1 << 16) | 9; }
+int gdn_abi_version(void) { return (1 << 16) | 10; }
 
 int gdn_binary_version(void) { return gdn::chunk_scan_binary_version(); }
 

@@ -131,7 +131,8 @@ struct ChunkBwdArgs {
   const int* cu_seqlens = nullptr;
 };
 
-size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
+size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);   // every path's
+size_t chunk_bwd_workspace_bytes_for(const ChunkBwdArgs& a);              // this call's
 size_t chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, int dv);
 bool chunk_bwd_supported(const ChunkBwdArgs& a);
 cudaError_t launch_chunk_bwd(const ChunkBwdArgs& a, cudaStream_t st);
@@ -210,7 +211,7 @@ cudaError_t launch_chunk_scan_prepared(const ChunkArgs& a, bool transition, cuda
 // a.workspace holds the [Z | PT | T] slots of launch_chunk_prepare_bwd; every chunk's
 // entering state goes to hs and V' = T X to vp, in the backward's workspace layouts.
 // With hs_tiles (the hand-off to the tcgen05 gradients), the entering states go to hs as
-// bf16 [dk][64]-column tiles, 128-byte swizzled (64 KB slot per (chunk, head), 16 KB per
+// bf16 [dk][64]-column tiles, 128-byte swizzled (kHandoffHSlot per (chunk, head), 16 KB per
 // column tile), and V' to vp as bf16 rows [slots C][dv].
 cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool hs_tiles,
                                   cudaStream_t st);
@@ -218,9 +219,9 @@ cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool
 // to yx (fp32), every chunk's leaving state gradient to dhs, the initial state's gradient to
 // dh0 (NULL: not wanted), from dO and dhT (NULL: zero).  With dxb (the hand-off to the tcgen05
 // gradients; dvo and a.v then required): the leaving gradients go to dhs as bf16 tiles
-// (the layout of hs_tiles), dX to dxb as bf16 rows [slots C][dv], dV = beta dX to dvo
-// ([B,T,H,dv] bf16), and each token row's rowsum(dX o v) by 32-column block to the dhs
-// slot + 32 KB ([64][4] fp32).
+// (kHandoffDhSlot per (chunk, head)), dX to dxb as bf16 rows [slots C][dv], dV = beta dX
+// to dvo ([B,T,H,dv] bf16), and each token row's rowsum(dX o v) by 32-column block to the
+// dhs slot + 32 KB ([64][4] fp32).
 cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const float* dhT,
                                   float* dh0, float* yx, float* dhs, void* dxb, void* dvo,
                                   cudaStream_t st);
@@ -247,6 +248,14 @@ int device_error_bwd_prep(bool clear);
 // or per value head into dqk [2][rows T][H][dk] fp32 when dqk is not NULL).  bf16,
 // dk = dv = 128; dense (n_seqs = 0, B rows) or packed (n_seqs sequences in one row,
 // cu / coff on the device); NC the chunks of every row (an upper bound when packed).
+// Slots of the backward's bf16 hand-off (bytes per (chunk, head)): the
+// preparation's [Z | PT | T]; the entering state h as a bf16 tile [2 column
+// tiles][128 key rows][128 B]; the leaving state gradient dh as the same tile,
+// then the rows' dX.v partials ([64 tokens][4] fp32) at + 32 KB.
+constexpr int kTileBytesBwdSlot = 32768;
+constexpr int kHandoffHSlot = 32768;
+constexpr int kHandoffDhSlot = 36864;
+
 struct BwdGradsArgs {
   const void* q; const void* k; const void* v; const void* dO;
   const float* g; const float* beta;

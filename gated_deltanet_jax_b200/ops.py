@@ -182,7 +182,8 @@ def _chunk_backward(q, k, v, g, beta, h0, do, dhT, cu_seqlens=None):
         args = (_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(h0c), _ptr(do),
                 _ptr(dhT_c), _ptr(dq), _ptr(dk_), _ptr(dv_), _ptr(dg), _ptr(db), _ptr(dh0))
         if n_seqs is None:
-            ws_bytes = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv)
+            ws_bytes = lib.gdn_chunk_bwd_workspace_bytes_for(B, T, H, Hk, dk, dv,
+                                                             _DTYPES[q.dtype])
             ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
             rc = lib.gdn_chunk_bwd(*args, B, T, H, Hk, dk, dv, _DTYPES[q.dtype], _ptr(ws),
                                    ws_bytes, stream)

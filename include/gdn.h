@@ -198,9 +198,10 @@ int gdn_chunk_fwd_varlen(const void* q, const void* k, const void* v,
  * (ops.py:170-184 with a state carry).  Layouts as the forward's: dq, dk
  * [B,T,Hk,dk] and dv [B,T,H,dv] in the input dtype, dg, dbeta [B,T,H] and dh0
  * [B,H,dk,dv] fp32 (dh0 NULL: not wanted).  Needs dk <= 256 and dv a multiple
- * of 32, and a device workspace of gdn_chunk_bwd_workspace_bytes() (fp32
- * per-chunk intermediates: the state entering and the state gradient leaving
- * every chunk, and four [T, dk | dv] products per head).  Deterministic: the
+ * of 32, and a device workspace of gdn_chunk_bwd_workspace_bytes_for() or
+ * gdn_chunk_bwd_workspace_bytes() (per-chunk intermediates: the state entering
+ * and the state gradient leaving every chunk, and [T, dk | dv] products per
+ * head).  Deterministic: the
  * same inputs give the same bits on every run.
  */
 int gdn_chunk_bwd(const void* q, const void* k, const void* v,
@@ -210,8 +211,19 @@ int gdn_chunk_bwd(const void* q, const void* k, const void* v,
                   int B, int T, int H, int Hk, int dk_dim, int dv_dim, int dtype,
                   void* workspace, size_t ws_bytes, void* stream);
 
-/* Device workspace bytes gdn_chunk_bwd needs for these sizes. */
+/* Device workspace bytes gdn_chunk_bwd needs for these sizes, whatever the
+ * dtype and kernels (enough for every path). */
 size_t gdn_chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);
+
+/*
+ * Device workspace bytes gdn_chunk_bwd needs for exactly this call's sizes,
+ * grouped heads and dtype (0 for invalid arguments): at bf16, dk = dv = 128 the
+ * tensor-core path hands bf16 tiles between its launches and needs about 40 %
+ * of gdn_chunk_bwd_workspace_bytes() (0.55 against 1.34 GB at B=4 T=4096
+ * H=16).  Either size is accepted.
+ */
+size_t gdn_chunk_bwd_workspace_bytes_for(int B, int T, int H, int Hk, int dk, int dv,
+                                         int dtype);
 
 /*
  * The backward of gdn_chunk_fwd_varlen: n_seqs sequences packed back to back
@@ -246,9 +258,9 @@ size_t gdn_chunk_bwd_varlen_workspace_bytes(int n_seqs, int T, int H, int dk, in
  * Arguments and results are gdn_chunk_bwd's, without the workspace: the
  * caller still passes every input and output.  The scratch is instead a
  * fixed array of GDN_CHUNK_BWD_NOALLOC_SCRATCH_BYTES (64 MiB) in this
- * library's own device memory; sizes whose gdn_chunk_bwd_workspace_bytes()
+ * library's own device memory; sizes whose gdn_chunk_bwd_workspace_bytes_for()
  * is larger are rejected with GDN_ERR_UNSUPPORTED (e.g. B*H = 16 heads at
- * dk = dv = 128 fit up to T = 768 tokens).  The call itself allocates
+ * dk = dv = 128 fit up to T = 1984 tokens in bf16, T = 768 in fp32).  The call itself allocates
  * nothing: no cudaMalloc, cudaFree or allocating library routine.
  *
  * - The array is reserved on a GPU when the driver loads the module that
@@ -382,7 +394,7 @@ int gdn_gated_rmsnorm_fwd(const void* o, const void* gate, const float* weight, 
  * gdn_fold_states,
  * gdn_reload_kernel_overrides, gdn_binary_version; 1.9: the layer forms at
  * the other tensor-core shapes and the general recurrent shapes,
- * gdn_short_conv_fwd, gdn_gated_rmsnorm_fwd). */
+ * gdn_short_conv_fwd, gdn_gated_rmsnorm_fwd; 1.10: gdn_chunk_bwd_workspace_bytes_for). */
 int gdn_abi_version(void);
 
 /*

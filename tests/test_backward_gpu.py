@@ -113,6 +113,26 @@ def test_backward_is_deterministic(cuda, Hk):
             assert torch.equal(a, r)
 
 
+def test_handoff_workspace_is_compact(cuda):
+    """The tensor-core path's workspace (bf16, dk = dv = 128, dense) holds only
+    its bf16 hand-off: per (chunk, head) the 32 KB [Z | PT | T] slot, 32 KB of
+    bf16 V' and dX rows, the 32 KB h tile and the 36 KB dh tile with the row
+    partials; grouped heads add the per value head dq, dk."""
+    from gated_deltanet_jax_b200 import _lib
+    lib = _lib.load()
+    B, T, H = 4, 4096, 16
+    items = B * (T // 64) * H
+    for_ = lib.gdn_chunk_bwd_workspace_bytes_for
+    exact = for_(B, T, H, H, 128, 128, _lib.GDN_DTYPE_BF16)
+    assert exact == items * (32768 + 32768 + 32768 + 36864)
+    assert exact < 0.45 * lib.gdn_chunk_bwd_workspace_bytes(B, T, H, 128, 128)
+    assert for_(B, T, H, 4, 128, 128, _lib.GDN_DTYPE_BF16) == exact + 2 * B * T * H * 128 * 4
+    # a call given exactly that workspace (the op allocates this call's size),
+    # against the oracle
+    got, ref = _grads("bf16", 2, 200, 3, 128, 128, seed=21, dev=cuda)
+    _check(got, ref, "bf16")
+
+
 def test_backward_rejects_unsupported(cuda):
     q = torch.zeros(1, 8, 1, 16, device=cuda, requires_grad=True)
     g = torch.zeros(1, 8, 1, device=cuda)

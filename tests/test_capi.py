@@ -153,13 +153,18 @@ def test_backward_rejects_bad_arguments(lib):
 def test_backward_workspace_queries(lib):
     dense = lib.gdn_chunk_bwd_workspace_bytes(4, 4096, 16, 128, 128)
     assert dense > 1 << 30
-    # dense rows at dk = dv = 128 also hold the scan's [T | Z] tiles (24 KB per
-    # chunk and head) for the forward pass on the tensor-core scan
     dense64 = lib.gdn_chunk_bwd_workspace_bytes(4, 4096, 16, 64, 64)
-    assert dense - lib.gdn_chunk_bwd_varlen_workspace_bytes(4, 4 * 4096, 16, 128, 128) < \
-        4 * 64 * 16 * 24576
     # packed: an upper bound over any split of the tokens into n_seqs sequences
+    assert lib.gdn_chunk_bwd_varlen_workspace_bytes(4, 4 * 4096, 16, 128, 128) >= dense
     assert lib.gdn_chunk_bwd_varlen_workspace_bytes(4, 4 * 4096, 16, 64, 64) >= dense64
+    # the exact size of one call: fp32 takes the layout that fits every path, bf16
+    # no more (less where the tensor-core hand-off runs: a GPU test checks that)
+    for_ = lib.gdn_chunk_bwd_workspace_bytes_for
+    assert for_(4, 4096, 16, 16, 128, 128, _lib.GDN_DTYPE_FP32) == dense
+    assert for_(4, 4096, 16, 16, 128, 128, _lib.GDN_DTYPE_BF16) <= dense
+    assert for_(4, 4096, 16, 16, 64, 64, _lib.GDN_DTYPE_BF16) == dense64
+    for bad in ((0, 64, 2, 2, 16, 32, 1), (1, 64, 2, 0, 16, 32, 1), (1, 64, 2, 2, 16, 32, 7)):
+        assert for_(*bad) == 0
     assert lib.gdn_chunk_bwd_varlen_workspace_bytes(4, 4 * 4096, 16, 128, 128) > \
         lib.gdn_chunk_bwd_varlen_workspace_bytes(1, 4 * 4096, 16, 128, 128)
     for args in ((0, 64, 2, 16, 32), (1, 0, 2, 16, 32), (1, 64, -1, 16, 32)):

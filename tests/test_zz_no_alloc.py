@@ -69,15 +69,16 @@ def _call(lib, pr, no_alloc):
     return outs
 
 
-def _largest_T(lib, B, H, dk, dv):
-    """Longest sequence whose backward scratch fits the fixed array (the
-    scratch size grows with T)."""
+def _largest_T(lib, B, H, Hk, dk, dv, dtype):
+    """Longest sequence whose backward scratch (this call's exact size) fits
+    the fixed array (the scratch size grows with T)."""
+    need = lambda T: lib.gdn_chunk_bwd_workspace_bytes_for(B, T, H, Hk, dk, dv, dtype)  # noqa: E731
     lo, hi = 1, 1
-    while lib.gdn_chunk_bwd_workspace_bytes(B, hi, H, dk, dv) <= SCRATCH_BYTES:
+    while need(hi) <= SCRATCH_BYTES:
         lo, hi = hi, hi * 2
     while hi - lo > 1:
         mid = (lo + hi) // 2
-        if lib.gdn_chunk_bwd_workspace_bytes(B, mid, H, dk, dv) <= SCRATCH_BYTES:
+        if need(mid) <= SCRATCH_BYTES:
             lo = mid
         else:
             hi = mid
@@ -86,7 +87,7 @@ def _largest_T(lib, B, H, dk, dv):
 
 def test_no_alloc_matches_workspace_entry_on_consecutive_calls(cuda):
     lib = _lib.load()
-    T_max = _largest_T(lib, 1, 16, 128, 128)
+    T_max = _largest_T(lib, 1, 16, 8, 128, 128, _lib.GDN_DTYPE_BF16)
     largest = _problem(1, T_max, 16, 8, 128, 128, "bf16", seed=11, dev=cuda, with_state=True)
     smaller = _problem(2, 100, 3, 3, 64, 64, "fp32", seed=12, dev=cuda, with_state=False)
     names = ("dq", "dk", "dv", "dg", "dbeta", "dh0")
@@ -106,8 +107,9 @@ def test_no_alloc_rejects_sizes_beyond_its_scratch(cuda):
     """One token more than the largest size above needs more than the fixed
     array: refused before any pointer is read or anything is launched."""
     lib = _lib.load()
-    T = _largest_T(lib, 1, 16, 128, 128) + 1
-    assert lib.gdn_chunk_bwd_workspace_bytes(1, T, 16, 128, 128) > SCRATCH_BYTES
+    T = _largest_T(lib, 1, 16, 16, 128, 128, _lib.GDN_DTYPE_BF16) + 1
+    assert lib.gdn_chunk_bwd_workspace_bytes_for(1, T, 16, 16, 128, 128,
+                                                 _lib.GDN_DTYPE_BF16) > SCRATCH_BYTES
     rc = lib.gdn_chunk_bwd_noalloc(*([None] * 14), 1, T, 16, 16, 128, 128,
                                    _lib.GDN_DTYPE_BF16, None)
     assert rc == _lib.GDN_ERR_UNSUPPORTED
