@@ -1268,7 +1268,20 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
             if (in) *reinterpret_cast<uint4*>(dst + 8 * c8) = pack_bf16x8(o8);
           }
           reinterpret_cast<float*>(dhsb + slot * kHandoffDhSlot + 32768)[r * 4 + (c0 + cb) / 32] = xv;
-          stage_store_bf16(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32, lane);
+          // dX as bf16 into this warp's staging; the proxy fence that the
+          // gradient tile's epilogue below issues anyway covers it, and the
+          // tensor store goes out after that epilogue's arrival
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+          uint4 pk[4];
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) pk[c8] = pack_bf16x8(y + 8 * c8);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int jc = (c + (lane >> 1)) & 3;   // bank-spread order (as stage_store_bf16)
+            const uint4 w = jc == 0 ? pk[0] : jc == 1 ? pk[1] : jc == 2 ? pk[2] : pk[3];
+            *reinterpret_cast<uint4*>(stg_x + lane * 64 + jc * 16) = w;
+          }
         } else {
           stage_store(stg_x, y, &tmYX, c0 + cb, (int)(slot * C) + wq * 32);
         }
@@ -1310,6 +1323,10 @@ chunk_scan_rev_kernel(const __grid_constant__ CUtensorMap tmK,
         if (lane == 0) mbar_arrive(&bars[R_S]);
         if (!dhsb && n > 0)   // the gradient leaving chunk n - 1
           stage_store(stg_r, R, &tmDHS, c0 + cb, (int)((slot - H) * DK) + wq * 32);
+        if (dhsb && wq < 2 && lane == 0) {   // this chunk's dX rows, staged above
+          tma_store_2d(&tmYX, c0 + cb, (int)(slot * C) + wq * 32, stg_x);
+          bulk_commit();
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[R_VEMPTY + v]);
