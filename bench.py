@@ -886,7 +886,7 @@ def backward_leg(d, a, lib):
     do = torch.randn(B, T, H, dv, device=d.dev, generator=gen).bfloat16()
     dq, dk_, dv_ = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dg, db = torch.empty_like(g), torch.empty_like(beta)
-    ws_bytes = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, dk, dv)
+    ws_bytes = lib.gdn_chunk_bwd_workspace_bytes_for(B, T, H, H, dk, dv, _lib.GDN_DTYPE_BF16)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=d.dev)
     ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
@@ -908,9 +908,9 @@ def backward_leg(d, a, lib):
             "config": {"workload": "gradients of q, k, v, g, beta for B=4 T=4096 H=16 "
                                    "dk=dv=128, bf16 in, from a bf16 dO, no initial state",
                        "l2": f"inputs and {ws_bytes / 1e9:.2f} GB of workspace, larger than L2",
-                       "path": "gdn_chunk_bwd: per-chunk preparation, forward state pass "
-                               "(scan), reverse state pass (reverse scan), per-chunk gradients "
-                               "(4 launches)"},
+                       "path": "gdn_chunk_bwd: per-chunk preparation (with T), forward "
+                               "state pass (scan), reverse state pass (reverse scan), per-chunk "
+                               "gradients (4 launches, bf16 hand-off in the workspace)"},
             "algorithmic_flops_per_step": flops,
             "achieved_tflops": flops / (ms / 1e3) / 1e12,
             "compute": "tcgen05 tensor cores (bf16 operands staged by TMA, fp32 accumulation "
