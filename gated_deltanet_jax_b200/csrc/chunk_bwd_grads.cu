@@ -170,11 +170,20 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
   struct Item {
     int gc, h, hq, b, tok, len;   // tok: first token of the chunk in row b; len: its tokens
   };
+  // (32-bit division where the item count allows: the 64-bit one is a long
+  // software sequence, and every warp decodes every item)
+  const bool small = total < (1LL << 31);
   auto item = [&](int j) {
     const long long w = blockIdx.x + (long long)j * gridDim.x;
     Item it;
-    it.h = (int)(w % H);
-    it.gc = (int)(w / H);
+    if (small) {
+      const unsigned w32 = (unsigned)w;
+      it.gc = (int)(w32 / (unsigned)H);
+      it.h = (int)(w32 - (unsigned)it.gc * (unsigned)H);
+    } else {
+      it.h = (int)(w % H);
+      it.gc = (int)(w / H);
+    }
     it.hq = it.h * Hk / H;
     if (!n_seqs) {
       it.b = it.gc / N;

@@ -119,11 +119,18 @@ bwd_prep_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
   struct Item {
     int gc, h, hq, b, tok, len;   // tok: first token of the chunk in row b; len: its tokens
   };
+  const bool small = total < (1LL << 31);
   auto item = [&](int j) {
     const long long w = blockIdx.x + (long long)j * gridDim.x;
     Item it;
-    it.h = (int)(w % H);
-    it.gc = (int)(w / H);
+    if (small) {   // (32-bit division: the 64-bit one is a long software sequence)
+      const unsigned w32 = (unsigned)w;
+      it.gc = (int)(w32 / (unsigned)H);
+      it.h = (int)(w32 - (unsigned)it.gc * (unsigned)H);
+    } else {
+      it.h = (int)(w % H);
+      it.gc = (int)(w / H);
+    }
     it.hq = it.h * Hk / H;
     if (!n_seqs) {
       it.b = it.gc / N;

@@ -121,10 +121,20 @@ chunk_prep_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
   const long long total = (long long)BH * N;
   const int cnt = blockIdx.x < total
                       ? (int)((total - 1 - blockIdx.x) / gridDim.x) + 1 : 0;
+  // (32-bit division where the item count allows: the 64-bit one is a long
+  // software sequence)
+  const bool small = total < (1LL << 31);
   auto item = [&](int j, int& n, int& b, int& h, int& hq) {
     const long long w = blockIdx.x + (long long)j * gridDim.x;
-    const int bh = (int)(w % BH);
-    n = N - 1 - (int)(w / BH);
+    int bh;
+    if (small) {
+      const unsigned w32 = (unsigned)w, q = w32 / (unsigned)BH;
+      bh = (int)(w32 - q * (unsigned)BH);
+      n = N - 1 - (int)q;
+    } else {
+      bh = (int)(w % BH);
+      n = N - 1 - (int)(w / BH);
+    }
     b = bh / H;
     h = bh - b * H;
     hq = h * Hk / H;
