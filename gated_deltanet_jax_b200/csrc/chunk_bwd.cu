@@ -1199,7 +1199,7 @@ size_t chunk_count(const ChunkBwdArgs& a) {
 // Whether the call takes the tcgen05 path with the bf16 hand-off: bf16, dense,
 // dk = dv = 128, none of the backward's kernel overrides set.
 bool bwd_handoff(const ChunkBwdArgs& a) {
-  const KernelOverrides ov = kernel_overrides();
+  const KernelOverrides& ov = a.ov;
   return a.dtype == kBF16 && !a.cu_seqlens && a.dk == 128 && a.dv == 128 &&
          bwd_prep_tc_supported(a.dtype, a.dk, a.dv) &&
          bwd_grads_tc_supported(a.dtype, a.dk, a.dv) && !ov.bwd_prep_warp &&
@@ -1234,7 +1234,7 @@ cudaError_t launch_bwd_t(const ChunkBwdArgs& a, cudaStream_t st) {
   if (e == cudaSuccess) e = ensure_smem(bwd_grads_kernel<Tin>, grads_bytes, set_grads);
   if (e != cudaSuccess) return e;
   if (packed) bwd_chunk_offsets_kernel<<<1, 1024, 0, st>>>(a.cu_seqlens, a.B, a.T, NC, coff);
-  const KernelOverrides ov = kernel_overrides();
+  const KernelOverrides& ov = a.ov;
   // bf16, dk = dv = 128: the per-chunk preparation on tcgen05; on dense rows
   // the two state passes on the scan kernels, fed by the forward's preparation
   // (its [Z | PT | T] slots), with no fp32 W, U, Z, Y at all

@@ -129,6 +129,9 @@ struct ChunkBwdArgs {
   // Packed sequences: B = n_seqs sequences in one row of T tokens,
   // sequence s = tokens [cu_seqlens[s], cu_seqlens[s + 1]).
   const int* cu_seqlens = nullptr;
+  // The kernel overrides this call runs under: one snapshot, taken before its
+  // workspace is checked, so that the layout checked is the layout launched.
+  KernelOverrides ov = kernel_overrides();
 };
 
 size_t chunk_bwd_workspace_bytes(int B, int T, int H, int dk, int dv);   // every path's
