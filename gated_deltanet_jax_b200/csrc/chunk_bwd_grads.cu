@@ -269,30 +269,10 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
                       &bars[G_FULL]);
         }
       };
-      // item j's inputs into L2 an item before their loads (no completion to
-      // wait for: a prefetch only warms the cache)
-      auto prefetch = [&](int j) {
-        const Item it = item(j);
-        for (int kb = 0; kb < 2; ++kb) {
-          tma_prefetch_4d(&tmK, 64 * kb, it.hq, it.tok, it.b);
-          tma_prefetch_4d(&tmQ, 64 * kb, it.hq, it.tok, it.b);
-          tma_prefetch_4d(&tmO, 64 * kb, it.h, it.tok, it.b);
-        }
-        if (hb) {
-          const size_t ws = (size_t)it.gc * H + it.h;
-          bulk_prefetch_l2(hb + ws * kHandoffHSlot, 32768);
-          bulk_prefetch_l2(dhb + ws * kHandoffDhSlot, 32768 + 1024);
-          for (int cb = 0; cb < 2; ++cb) {
-            tma_prefetch_2d(&tmVP, 64 * cb, (int)(ws * C));
-            tma_prefetch_2d(&tmDX, 64 * cb, (int)(ws * C));
-          }
-        }
-      };
       const uint32_t kq = sbase + L::SM_KQ, xo = sbase + L::SM_XO, vp = sbase + L::SM_VP;
       const uint32_t hh = sbase + L::SM_H, dh = sbase + L::SM_DH, ap = sbase + L::SM_AP;
       load_a(0);
       load_b(0);
-      if (cnt > 1) prefetch(1);
       int pend_a = 0, pend_b = 0;   // items whose loads were issued and not yet seen (-1: none)
       for (int j = 0; j < cnt; ++j) {
         bool ok = mbar_wait(&bars[G_FULL2], (uint32_t)j & 1u) &&
@@ -301,7 +281,6 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
         // with the hand-off, P1 .. P4 read only loaded tiles
         ok = ok && (hb || mbar_wait(&bars[G_CONV], (uint32_t)j & 1u));
         if (!ok) break;
-        if (j + 2 < cnt) prefetch(j + 2);
         tc_fence_after();
         // P2 = [K;Q] K^T and P1 = [dX;dO] V'^T (K-dim 128 in 8 steps of 16)
 #pragma unroll
