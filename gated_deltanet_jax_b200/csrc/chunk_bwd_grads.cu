@@ -94,7 +94,7 @@ enum {
   G_M12 = 6,      // P1, P2 in TMEM
   G_AP = 7,       // dAE / dPE tile written
   G_M3456 = 8,    // P3 .. P6 in TMEM: every product of the item complete
-  G_KQFREE = 9,   // the last epilogue's reads of K and Q done (8 warps)
+  G_KQFREE = 9,   // the last epilogue's reads of K, Q and of P3 .. P6 done (8 warps)
   G_FULL2 = 10,   // dO (and the hand-off's V', dX, h, dh, rowsum partials) landed
   G_HFREE = 11,   // (hand-off) h, dh and the rowsum partials read (8 warps)
   G_M1234 = 12,   // P1 .. P4 complete: dO, V', dX, h, dh no longer read
@@ -633,8 +633,11 @@ bwd_grads_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_consta
             }
           }
         }
+        // (the reads of K, Q and of the TMEM that the next item's products
+        // overwrite are done)
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[G_KQFREE]);   // (the reads of K, Q above are done)
+        if (lane == 0) mbar_arrive(&bars[G_KQFREE]);
         if (!side) {
           red[(RD_KG + ch) * 64 + m] = -dm * r1 - bem * r2;
           red[(RD_KB + ch) * 64 + m] = -em * r2;

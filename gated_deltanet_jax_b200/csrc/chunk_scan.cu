@@ -1475,11 +1475,14 @@ cudaError_t launch_chunk_scan_bwd(const ChunkArgs& a, float* hs, float* vp, bool
     return cudaErrorInvalidValue;
   CUtensorMap mk, mq, mv, mhs, mvp;
   const long long slots = (long long)a.B * ((a.T + C - 1) / C) * a.H;
+  // (with hs_tiles the states go out by bulk copies: no fp32 map over hs, whose
+  // region then holds only the bf16 tiles)
   if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv) ||
-      !make_f32_map_2d(&mhs, hs, slots * DK, a.dv) ||
+      !(hs_tiles || make_f32_map_2d(&mhs, hs, slots * DK, a.dv)) ||
       !(hs_tiles ? make_bf16_map_2d(&mvp, vp, slots * C, a.dv, false)
                  : make_f32_map_2d(&mvp, vp, slots * C, a.dv)))
     return cudaErrorInvalidValue;
+  if (hs_tiles) mhs = mvp;   // (not read)
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(chunk_scan_kernel<true>, ScanLay::SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
@@ -1500,13 +1503,16 @@ cudaError_t launch_chunk_scan_rev(const ChunkArgs& a, const void* dO, const floa
     return cudaErrorInvalidValue;
   CUtensorMap mk, mq, mo, myx, mdhs, mv;
   const long long slots = (long long)a.B * ((a.T + C - 1) / C) * a.H;
+  // (with the hand-off the gradients go out by bulk copies: no fp32 map over
+  // dhs, whose region then holds only the bf16 tiles and row partials)
   if (!qk_maps(a, &mk, &mq) || !make_bf16_map_4d(&mo, dO, a.B, a.T, a.H, a.dv) ||
-      !make_f32_map_2d(&mdhs, dhs, slots * DK, a.dv) ||
+      !(hand || make_f32_map_2d(&mdhs, dhs, slots * DK, a.dv)) ||
       !(hand ? make_bf16_map_2d(&myx, dxb, slots * C, a.dv, false) &&
                    make_bf16_map_4d(&mv, a.v, a.B, a.T, a.H, a.dv)
              : make_f32_map_2d(&myx, yx, slots * C, a.dv)))
     return cudaErrorInvalidValue;
-  if (!hand) mv = mo;   // (not read)
+  if (hand) mdhs = mo;   // (not read)
+  else mv = mo;
   static std::atomic<int> slot[kMaxDevices] = {};
   cudaError_t e = ensure_smem(chunk_scan_rev_kernel, RevLay::SMEM_BYTES, slot);
   if (e != cudaSuccess) return e;
