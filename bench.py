@@ -7,7 +7,9 @@ updated in place (512 kernel launches, replayed as one CUDA graph).  The
 ``prefill`` object in the same line reports chunked prefill tokens/s on B=4,
 T=4096, H=16, dk=dv=128, chunk=64, bf16 in / fp32 state (two launches per step:
 the per-chunk preparation, then the scan, each also timed alone);
-``long_context`` B=1 T=65536; ``backward`` the gradients on the prefill workload.
+``long_context`` B=1 T=65536; ``backward`` the gradients on the prefill workload;
+``model_forward`` the full GatedDeltaNetModel forward at the reference's model
+configuration (24 layers, B=8 T=2048).
 
 Multi-GPU (torchrun, one rank per GPU): batch x head work is independent, so
 every rank runs its own full workload (weak scaling, no collective on the
@@ -828,8 +830,7 @@ def model_core_leg(d, a):
     """The delta-rule core of the reference's default model configuration
     (head_dim 256, expand_v 2: dk=256, dv=512; 6 heads; B=8 T=2048 as the
     full-model configuration quotes): the chunked forward in bf16 and in
-    fp32, and the bf16 backward, per layer call.  The full model (projections,
-    MLPs, 24 layers) is outside the operator path."""
+    fp32, and the bf16 backward, per layer call (the full model: model_forward_leg)."""
     import torch
     from gated_deltanet_jax_b200 import ops
     from gated_deltanet_jax_b200 import roofline as rl
@@ -867,6 +868,54 @@ def model_core_leg(d, a):
             "launches": steps * (1 + 3 + 3),
             "path": "bf16 forward: tcgen05 kernel (dk=256 form); fp32 forward: warp-level "
                     "tensor-core kernels (three-term tf32); backward: gdn_chunk_bwd"}
+
+
+def model_forward_leg(d, a):
+    """The full GatedDeltaNetModel forward at the reference's model configuration
+    (hidden 2048, 24 layers, 6 heads, head_dim 256, expand_v 2, short convolution
+    4, SiLU output gate, RMSNorm, vocab 32000) on B=8 T=2048 token ids: the
+    embedding, 24 blocks and the final norm, random init at Flax's default
+    scales, bf16.  Projections and MLPs are cuBLAS GEMMs; the short convolutions
+    and each layer's gates + chunked delta rule + gated RMSNorm run on this
+    library's kernels.  Like the reference (no q/k normalisation in its layer),
+    the recurrence overflows at these statistics: a throughput configuration;
+    the line reports the fraction of finite outputs."""
+    import torch
+    from gated_deltanet_jax_b200 import GatedDeltaNetConfig
+    from gated_deltanet_jax_b200.model import GatedDeltaNetModel
+    B, T = 8, 2048
+    cfg = GatedDeltaNetConfig(hidden_size=2048, num_hidden_layers=24, num_heads=6, head_dim=256,
+                              expand_v=2.0, conv_size=4, vocab_size=32000, attn_mode="chunk")
+    torch.manual_seed(31 + d.rank)
+    with torch.device(d.dev):
+        model = GatedDeltaNetModel(cfg).to(torch.bfloat16).eval()
+    gen = torch.Generator(device=d.dev)
+    gen.manual_seed(37 + d.rank)
+    ids = torch.randint(0, cfg.vocab_size, (B, T), device=d.dev, generator=gen)
+    out = {}
+
+    def step():
+        out["x"] = model(ids)
+
+    steps = max(1, min(a.steps, 3))
+    with torch.no_grad():
+        for _ in range(max(1, min(a.warmup, 2))):
+            step()
+        ms, _ = _timed(d, step, steps)
+    finite = float(torch.isfinite(out["x"]).float().mean())
+    nparam = sum(p.numel() for p in model.parameters())
+    del model, out
+    torch.cuda.empty_cache()
+    return {"metric": "full-model forward tokens/s", "value": d.world * B * T / (ms / 1e3),
+            "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "config": {"workload": "GatedDeltaNetModel forward, hidden 2048, 24 layers, 6 heads, "
+                                   "head_dim 256 (dk=256 dv=512), short conv 4, gated RMSNorm, "
+                                   "vocab 32000; B=8 T=2048 token ids, bf16, random init",
+                       "parameters": nparam},
+            "finite_fraction": finite,
+            "path": "torch embedding/RMSNorm/GEMMs (cuBLAS); per layer: short convolutions "
+                    "(gdn_short_conv_fwd) and gdn_chunk_fwd_layer (gates, tcgen05 dk=256 "
+                    "chunk kernel, gated RMSNorm)"}
 
 
 def backward_leg(d, a, lib):
@@ -1102,6 +1151,7 @@ def main():
     play = None if (a.no_layer or a.no_prefill) else prefill_layer_leg(d, a)
     pdef = None if (a.no_layer or a.no_prefill) else prefill_layer_default_leg(d, a)
     mcore = None if a.no_prefill else model_core_leg(d, a)
+    mfwd = None if (a.no_layer or a.no_prefill) else model_forward_leg(d, a)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not a.no_cpu:
@@ -1180,6 +1230,8 @@ def main():
             line["prefill_layer_default_dims"] = pdef
         if mcore:
             line["model_config_core"] = mcore
+        if mfwd:
+            line["model_forward"] = mfwd
         if bwd:
             if pre:
                 bwd["fwd_plus_bwd_tokens_per_s"] = (d.world * PRE["B"] * PRE["T"]
