@@ -102,6 +102,8 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x):
+        if x.is_cuda and hasattr(F, "rms_norm"):   # one fused pass (fp32 accumulation)
+            return F.rms_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.eps)
         xf = x.float()
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight.float()
         return y.to(x.dtype)
