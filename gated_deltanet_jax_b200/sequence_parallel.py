@@ -154,16 +154,39 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
         S, M = segment_summary(qs, ks, vs, gs, bs, fn)                  # [B*parts, H, ...]
     mark("pass1")
     packed = torch.cat([S, M], dim=-1).view(B, parts, H, dk, dv + dk).contiguous()
-    allp = torch.cat(gather(packed), dim=1).transpose(0, 1)             # [world*parts, B, H, dk, dv+dk]
-    mark("exchange")
-    if ws is not None and dk == 128 and dv % 32 == 0:
-        # one launch walks every segment: out[p + 1] = M_p out[p] + S_p
-        states = ops._fold_states(allp, initial_state, dv)               # [world*parts + 1, ...]
-    else:
+    use_kernel = ws is not None and dk == 128 and dv % 32 == 0
+
+    def fold(pairs, h0):
+        # [P, B, H, dk, dv + dk] summaries -> [P + 1, B, H, dk, dv]: the state
+        # entering each segment, then the state after the last one
+        if use_kernel:   # one launch walks every segment: out[p + 1] = M_p out[p] + S_p
+            return ops._fold_states(pairs, h0, dv)
         h0 = (torch.zeros(B, H, dk, dv, dtype=S.dtype, device=v.device)
-              if initial_state is None else initial_state.to(S.dtype))
-        states = fold_states_scan(h0, allp[..., :dv], allp[..., dv:])  # [world*parts + 1, ...]
-    mine = states[rank * parts:(rank + 1) * parts]
+              if h0 is None else h0.to(S.dtype))
+        return fold_states_scan(h0, pairs[..., :dv], pairs[..., dv:])
+
+    if world > 1 and parts > 1:
+        # This rank's segments composed into one map before the exchange,
+        # (M_b, S_b) o (M_a, S_a) = (M_b M_a, M_b S_a + S_b): the all-gather then
+        # moves one summary per rank, and the fold over the ranks takes `world`
+        # steps instead of world x parts; each rank then walks its own segments
+        # from the state entering it.
+        loc = packed.transpose(0, 1).contiguous()                       # [parts, B, H, dk, dv+dk]
+        acc = loc[0]
+        for p in range(1, parts):
+            acc = torch.matmul(loc[p, ..., dv:], acc)
+            acc[..., :dv] += loc[p, ..., :dv]
+        allr = torch.stack(gather(acc.contiguous()), dim=0)             # [world, B, H, dk, dv+dk]
+        mark("exchange")
+        ranks = fold(allr, initial_state)                               # [world + 1, ...]
+        mine = fold(loc, ranks[rank])[:parts]
+        final = ranks[world]
+    else:
+        allp = torch.cat(gather(packed), dim=1).transpose(0, 1)         # [world*parts, B, H, dk, dv+dk]
+        mark("exchange")
+        states = fold(allp, initial_state)                              # [world*parts + 1, ...]
+        mine = states[rank * parts:(rank + 1) * parts]
+        final = states[world * parts]
     s_in = mine.transpose(0, 1).reshape(B * parts, H, dk, dv).contiguous()
     mark("fold")
     if ws is not None:
@@ -172,7 +195,7 @@ def _two_pass(q, k, v, g, beta, initial_state, output_final_state, chunk_size, p
         o, _ = fn(qs, ks, vs, gs, bs, s_in)
     mark("pass2")
     o = o.reshape(B, Tp, H, dv)[:, :T]
-    return (o, states[world * parts]) if output_final_state else (o, None)
+    return (o, final) if output_final_state else (o, None)
 
 
 def chunk_gated_delta_rule_sp(q, k, v, g, beta, initial_state=None, output_final_state=False,

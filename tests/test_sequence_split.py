@@ -70,7 +70,7 @@ def _sp_worker(rank, world, port, T, results, local_parts=1, seg=None, auto_by_l
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,local_parts", [(2, 1), (3, 1), (2, 3)])
+@pytest.mark.parametrize("world,local_parts", [(2, 1), (3, 1), (2, 3), (3, 2)])
 def test_split_across_gloo_ranks_matches_oracle(world, local_parts):
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
